@@ -1,0 +1,684 @@
+// pb_oracle.cpp — CPU restatement of the FlashMoE reference arithmetic (Jc2k/pb,
+// src/inference/flashmoe) that the CUDA path in pb_b200/ replaces.
+//
+// THIS IS TEST INFRASTRUCTURE. Only tests/, __graft_entry__.smoke() and the
+// cpu_baseline / --impl reference legs of bench.py may load it, and only as the
+// checker or as the timed CPU baseline. The product path (libpbmoe.so) never
+// links or calls it.
+//
+// The reference is Rust and cannot be built in this image (no cargo/rustc), so
+// every function below restates one Rust function in C++ with the same loop
+// order and the same rounding points. Compile with -ffp-contract=off: an FMA
+// appears only where the Rust source calls `mul_add` (or the Metal shader calls
+// `fma`), through std::fma. Rust's f32::exp/sin/cos lower to the platform libm
+// on Linux, so glibc's expf/sin/cos reproduce Rust-on-Linux.
+//
+// Parity is pinned by the reference's own unit tests (their literal inputs and
+// expected outputs are transcribed in tests/golden/reference_kats.json, each
+// with its file:line) and checked by tests/test_oracle_kats.py.
+//
+// All entry points are extern "C", take plain pointers and sizes, return 0 on
+// success and a negative value on invalid arguments (mirroring the Rust
+// `bail!` paths, which the tests exercise).
+
+#include <cmath>
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <limits>
+#include <vector>
+
+#include <algorithm>
+#include <atomic>
+#include <thread>
+
+namespace {
+
+constexpr int kOk = 0;
+constexpr int kInvalid = -1;
+
+inline size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
+
+// Static split of [0, n) over `threads` std::threads (the multi-core CPU
+// baseline). Each index's arithmetic is the same as in the serial loop.
+template <class F>
+void parallel_for(size_t n, int threads, F&& body) {
+    if (threads <= 1 || n <= 1) {
+        for (size_t i = 0; i < n; ++i) body(i);
+        return;
+    }
+    size_t t = std::min<size_t>(static_cast<size_t>(threads), n);
+    std::vector<std::thread> pool;
+    pool.reserve(t);
+    for (size_t w = 0; w < t; ++w) {
+        size_t lo = n * w / t, hi = n * (w + 1) / t;
+        pool.emplace_back([lo, hi, &body] {
+            for (size_t i = lo; i < hi; ++i) body(i);
+        });
+    }
+    for (auto& th : pool) th.join();
+}
+
+// experts/mod.rs:917-934 (read_bf16_vec_le): bf16 bits << 16 reinterpreted.
+inline float bf16_to_f32(uint16_t bits) {
+    uint32_t w = static_cast<uint32_t>(bits) << 16;
+    float f;
+    std::memcpy(&f, &w, 4);
+    return f;
+}
+
+// experts/slots.rs:1165-1169 (f32_to_bf16_bits): round to nearest even by
+// adding 0x7fff + lsb, wrapping.
+inline uint16_t f32_to_bf16(float value) {
+    uint32_t bits;
+    std::memcpy(&bits, &value, 4);
+    uint32_t lsb = (bits >> 16) & 1u;
+    return static_cast<uint16_t>((bits + (0x7fffu + lsb)) >> 16);
+}
+
+inline float nibble_at(const uint8_t* packed_row, size_t col) {
+    uint8_t byte = packed_row[col / 2];
+    return static_cast<float>((col & 1) == 0 ? (byte & 0x0f) : (byte >> 4));
+}
+
+// math.rs:861-911 (q4_fma_matvec_with_group_size), one row.
+inline float q4_fma_row(const uint8_t* packed, const float* input, const float* scales,
+                        const float* biases, size_t row, size_t cols, size_t group_size) {
+    size_t groups_per_row = div_ceil(cols, group_size);
+    size_t packed_stride = div_ceil(cols, 2);
+    const uint8_t* packed_row = packed + row * packed_stride;
+    float acc = 0.0f;
+    for (size_t group = 0; group < groups_per_row; ++group) {
+        size_t idx = row * groups_per_row + group;
+        float scale = scales[idx];
+        float bias = biases[idx];
+        size_t start = group * group_size;
+        size_t end = start + group_size < cols ? start + group_size : cols;
+        for (size_t col = start; col < end; ++col) {
+            float x = input[col];
+            float scale_x = scale * x;
+            float bias_x = bias * x;
+            float q = nibble_at(packed_row, col);
+            acc += std::fma(q, scale_x, bias_x);
+        }
+    }
+    return acc;
+}
+
+// Same row with bf16 scale/bias decoded per group (FixedQ4ExpertSlot::project_cpu,
+// experts/slots.rs:629-670, decodes bf16 to f32 and calls the function above).
+inline float q4_fma_row_bf16(const uint8_t* packed, const float* input, const uint16_t* scales,
+                             const uint16_t* biases, size_t row, size_t cols, size_t group_size) {
+    size_t groups_per_row = div_ceil(cols, group_size);
+    size_t packed_stride = div_ceil(cols, 2);
+    const uint8_t* packed_row = packed + row * packed_stride;
+    float acc = 0.0f;
+    for (size_t group = 0; group < groups_per_row; ++group) {
+        size_t idx = row * groups_per_row + group;
+        float scale = bf16_to_f32(scales[idx]);
+        float bias = bf16_to_f32(biases[idx]);
+        size_t start = group * group_size;
+        size_t end = start + group_size < cols ? start + group_size : cols;
+        for (size_t col = start; col < end; ++col) {
+            float x = input[col];
+            float scale_x = scale * x;
+            float bias_x = bias * x;
+            float q = nibble_at(packed_row, col);
+            acc += std::fma(q, scale_x, bias_x);
+        }
+    }
+    return acc;
+}
+
+// Whole-expert slot (QwenMoeQ4ExpertLayout, model_family.rs:839-1010): nine
+// components gate{W,S,B}, up{W,S,B}, down{W,S,B} at byte offsets within one
+// slot; gate/up are [I x H], down is [H x I]; S/B are bf16 [rows x cols/G].
+// `offsets` holds the nine component offsets in that order.
+struct SlotView {
+    const uint8_t* gate_w; const uint16_t* gate_s; const uint16_t* gate_b;
+    const uint8_t* up_w; const uint16_t* up_s; const uint16_t* up_b;
+    const uint8_t* down_w; const uint16_t* down_s; const uint16_t* down_b;
+};
+
+inline SlotView slot_view(const uint8_t* slot, const uint64_t* offsets) {
+    SlotView v;
+    v.gate_w = slot + offsets[0];
+    v.gate_s = reinterpret_cast<const uint16_t*>(slot + offsets[1]);
+    v.gate_b = reinterpret_cast<const uint16_t*>(slot + offsets[2]);
+    v.up_w = slot + offsets[3];
+    v.up_s = reinterpret_cast<const uint16_t*>(slot + offsets[4]);
+    v.up_b = reinterpret_cast<const uint16_t*>(slot + offsets[5]);
+    v.down_w = slot + offsets[6];
+    v.down_s = reinterpret_cast<const uint16_t*>(slot + offsets[7]);
+    v.down_b = reinterpret_cast<const uint16_t*>(slot + offsets[8]);
+    return v;
+}
+
+// tests/scheduler.rs:327-336 (reference_q4_swiglu) with the production projection
+// arithmetic of FixedQ4ExpertSlot::project_cpu (experts/slots.rs:629-670).
+void expert_swiglu(const SlotView& v, size_t hidden, size_t inter, size_t group,
+                   const float* x, float* out, float* scratch_inter) {
+    for (size_t r = 0; r < inter; ++r) {
+        float g = q4_fma_row_bf16(v.gate_w, x, v.gate_s, v.gate_b, r, hidden, group);
+        float u = q4_fma_row_bf16(v.up_w, x, v.up_s, v.up_b, r, hidden, group);
+        scratch_inter[r] = g / (1.0f + std::exp(-g)) * u;
+    }
+    for (size_t r = 0; r < hidden; ++r) {
+        out[r] = q4_fma_row_bf16(v.down_w, scratch_inter, v.down_s, v.down_b, r, inter, group);
+    }
+}
+
+// math.rs:746-765 (routing_top_k_iter): K replacement slots initialised to
+// (0, -inf); each score replaces the first minimum slot when strictly greater.
+size_t routing_top_k_iter(const float* scores, size_t n, size_t k, uint32_t* ids, float* vals) {
+    k = k < n ? k : n;
+    for (size_t s = 0; s < k; ++s) {
+        ids[s] = 0;
+        vals[s] = -std::numeric_limits<float>::infinity();
+    }
+    for (size_t expert = 0; expert < n; ++expert) {
+        float score = scores[expert];
+        size_t minimum = 0;
+        for (size_t c = 1; c < k; ++c) {
+            if (vals[c] < vals[minimum]) minimum = c;
+        }
+        if (k > 0 && score > vals[minimum]) {
+            ids[minimum] = static_cast<uint32_t>(expert);
+            vals[minimum] = score;
+        }
+    }
+    return k;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint16_t oracle_f32_to_bf16(float value) { return f32_to_bf16(value); }
+float oracle_bf16_to_f32(uint16_t bits) { return bf16_to_f32(bits); }
+
+// math.rs:861-911.
+int oracle_q4_fma_matvec(const uint8_t* packed, const float* input, const float* scales,
+                         const float* biases, size_t rows, size_t cols, size_t group_size,
+                         float* out) {
+    if (group_size == 0) return kInvalid;
+    for (size_t r = 0; r < rows; ++r) {
+        out[r] = q4_fma_row(packed, input, scales, biases, r, cols, group_size);
+    }
+    return kOk;
+}
+
+// math.rs:861-911 with bf16 scale/bias (experts/slots.rs:629-670). `threads` > 1
+// splits rows over OpenMP threads (the multi-core CPU baseline); each row's
+// arithmetic is unchanged.
+int oracle_q4_fma_matvec_bf16(const uint8_t* packed, const float* input, const uint16_t* scales,
+                              const uint16_t* biases, size_t rows, size_t cols, size_t group_size,
+                              float* out, int threads) {
+    if (group_size == 0) return kInvalid;
+    parallel_for(rows, threads, [&](size_t r) {
+        out[r] = q4_fma_row_bf16(packed, input, scales, biases, r, cols, group_size);
+    });
+    return kOk;
+}
+
+// tests/scheduler.rs:308-325 (reference_q4_matvec): (q*s + b) * x, no FMA, bf16 S/B.
+int oracle_reference_q4_matvec(const uint8_t* packed, const float* input, const uint16_t* scales,
+                               const uint16_t* biases, size_t rows, size_t cols, size_t group_size,
+                               float* out) {
+    if (group_size == 0) return kInvalid;
+    size_t row_bytes = div_ceil(cols, 2);
+    size_t groups_per_row = div_ceil(cols, group_size);
+    for (size_t row = 0; row < rows; ++row) {
+        float sum = 0.0f;
+        for (size_t col = 0; col < cols; ++col) {
+            uint8_t byte = packed[row * row_bytes + col / 2];
+            uint8_t quantized = col % 2 == 0 ? (byte & 0x0f) : (byte >> 4);
+            size_t group = row * groups_per_row + col / group_size;
+            float scale = bf16_to_f32(scales[group]);
+            float bias = bf16_to_f32(biases[group]);
+            float w = static_cast<float>(quantized) * scale;
+            w = w + bias;
+            sum += w * input[col];
+        }
+        out[row] = sum;
+    }
+    return kOk;
+}
+
+// math.rs:913-954 (q4_dequantize_rows_with_group_size): q.mul_add(scale, bias).
+int oracle_q4_dequantize_rows(const uint8_t* packed, const float* scales, const float* biases,
+                              size_t rows, size_t cols, size_t group_size, float* out) {
+    if (group_size == 0) return kInvalid;
+    size_t groups_per_row = div_ceil(cols, group_size);
+    size_t packed_stride = div_ceil(cols, 2);
+    for (size_t row = 0; row < rows; ++row) {
+        const uint8_t* packed_row = packed + row * packed_stride;
+        for (size_t group = 0; group < groups_per_row; ++group) {
+            size_t idx = row * groups_per_row + group;
+            size_t start = group * group_size;
+            size_t end = start + group_size < cols ? start + group_size : cols;
+            for (size_t col = start; col < end; ++col) {
+                out[row * cols + col] = std::fma(nibble_at(packed_row, col), scales[idx], biases[idx]);
+            }
+        }
+    }
+    return kOk;
+}
+
+// Unpacked nibble values (the integer half of the format: element c is the low
+// nibble of byte c/2 when c is even, math.rs:903-904).
+int oracle_q4_unpack_nibbles(const uint8_t* packed, size_t rows, size_t cols, uint8_t* out) {
+    size_t packed_stride = div_ceil(cols, 2);
+    for (size_t row = 0; row < rows; ++row) {
+        for (size_t col = 0; col < cols; ++col) {
+            uint8_t byte = packed[row * packed_stride + col / 2];
+            out[row * cols + col] = (col & 1) == 0 ? (byte & 0x0f) : (byte >> 4);
+        }
+    }
+    return kOk;
+}
+
+// math.rs:728-744 (softmax_in_place).
+void oracle_softmax_in_place(float* values, size_t n) {
+    if (n == 0) return;
+    float max = -std::numeric_limits<float>::infinity();
+    for (size_t i = 0; i < n; ++i) max = std::fmax(max, values[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        values[i] = std::exp(values[i] - max);
+        sum += values[i];
+    }
+    if (sum > 0.0f && std::isfinite(sum)) {
+        float inverse_sum = 1.0f / sum;
+        for (size_t i = 0; i < n; ++i) values[i] *= inverse_sum;
+    }
+}
+
+// math.rs:767-769 (routing_top_k). Returns the number of slots written.
+size_t oracle_routing_top_k(const float* scores, size_t n, size_t k, uint32_t* ids, float* vals) {
+    return routing_top_k_iter(scores, n, k, ids, vals);
+}
+
+// math.rs:771-783 (routing_softmax_top_k): slot order of routing_top_k; each
+// selected score becomes exp(s - max) * (1/sum) over ALL n scores.
+size_t oracle_routing_softmax_top_k(const float* scores, size_t n, size_t k, uint32_t* ids,
+                                    float* weights) {
+    float max = -std::numeric_limits<float>::infinity();
+    for (size_t i = 0; i < n; ++i) max = std::fmax(max, scores[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; ++i) sum += std::exp(scores[i] - max);
+    size_t kk = routing_top_k_iter(scores, n, k, ids, weights);
+    bool have_inverse = sum > 0.0f && std::isfinite(sum);
+    float inverse_sum = have_inverse ? 1.0f / sum : 0.0f;
+    for (size_t s = 0; s < kk; ++s) {
+        weights[s] = std::exp(weights[s] - max);
+        if (have_inverse) weights[s] *= inverse_sum;
+    }
+    return kk;
+}
+
+// math.rs:788-819 (routing_sigmoid_noaux_top_k): selection on sigmoid(s)+bias,
+// returned weights are the unbiased sigmoid.
+size_t oracle_routing_sigmoid_noaux_top_k(const float* logits, const float* correction_bias,
+                                          size_t n, size_t k, uint32_t* ids, float* weights) {
+    std::vector<float> biased(n);
+    for (size_t e = 0; e < n; ++e) {
+        float raw = 1.0f / (1.0f + std::exp(-logits[e]));
+        biased[e] = raw + correction_bias[e];
+    }
+    size_t kk = routing_top_k_iter(biased.data(), n, k, ids, weights);
+    for (size_t s = 0; s < kk; ++s) {
+        float score = logits[ids[s]];
+        weights[s] = 1.0f / (1.0f + std::exp(-score));
+    }
+    return kk;
+}
+
+// scheduler/expert_access.rs:80-133 (ScheduledExpertRoutes::from_routes_with_policy).
+// policy 0 = RenormalizeSelected, 1 = DeepSeekRenormalizeSelectedWithFloor,
+// 2 = PreserveFullSoftmax (unsupported, an error as in the reference).
+int oracle_renormalize_routes(const float* scores, size_t k, int policy, float routed_expert_scale,
+                              float* weights) {
+    if (!(std::isfinite(routed_expert_scale) && routed_expert_scale > 0.0f)) return kInvalid;
+    for (size_t i = 0; i < k; ++i) weights[i] = scores[i];
+    float sum = 0.0f;
+    for (size_t i = 0; i < k; ++i) sum += weights[i];
+    float inverse_sum;
+    if (policy == 0) {
+        if (!(std::isfinite(sum) && sum > 0.0f)) return kInvalid;
+        inverse_sum = 1.0f / sum;
+    } else if (policy == 1) {
+        const float floor = 6.103515625e-5f;
+        if (!(std::isfinite(sum) && sum >= 0.0f)) return kInvalid;
+        inverse_sum = 1.0f / (sum > floor ? sum : floor);
+    } else {
+        return -2;
+    }
+    for (size_t i = 0; i < k; ++i) {
+        if (weights[i] < 0.0f) return kInvalid;
+        weights[i] *= inverse_sum;
+    }
+    for (size_t i = 0; i < k; ++i) weights[i] *= routed_expert_scale;
+    return kOk;
+}
+
+// metal/mod.rs:3197-3233 (qwen_layer_major_group_plan). route_slots[n] maps each
+// route (row*active + k) to its unique-expert slot. Outputs: source_rows[n],
+// output_indices[n], groups[2*unique] as (start, count) pairs.
+int oracle_layer_major_group_plan(const uint32_t* route_slots, size_t n, size_t unique_experts,
+                                  size_t active_experts, uint32_t* source_rows,
+                                  uint32_t* output_indices, uint32_t* groups) {
+    if (n == 0 || unique_experts == 0 || active_experts == 0) return kInvalid;
+    std::vector<std::vector<size_t>> routes_by_slot(unique_experts);
+    for (size_t route = 0; route < n; ++route) {
+        uint32_t slot = route_slots[route];
+        if (slot >= unique_experts) return kInvalid;
+        routes_by_slot[slot].push_back(route);
+    }
+    for (auto& v : routes_by_slot)
+        if (v.empty()) return kInvalid;
+    size_t written = 0;
+    for (size_t s = 0; s < unique_experts; ++s) {
+        size_t start = written;
+        for (size_t route : routes_by_slot[s]) {
+            source_rows[written] = static_cast<uint32_t>(route / active_experts);
+            output_indices[route] = static_cast<uint32_t>(written);
+            ++written;
+        }
+        groups[2 * s] = static_cast<uint32_t>(start);
+        groups[2 * s + 1] = static_cast<uint32_t>(routes_by_slot[s].size());
+    }
+    return kOk;
+}
+
+// math.rs:151-167 (rms_norm_with_weight_and_epsilon_in_place); weight may be NULL.
+void oracle_rms_norm(float* values, size_t n, const float* weight, float epsilon) {
+    float mean_square = 0.0f;
+    for (size_t i = 0; i < n; ++i) mean_square += values[i] * values[i];
+    mean_square = mean_square / static_cast<float>(n > 0 ? n : 1);
+    float scale = 1.0f / std::sqrt(mean_square + epsilon);
+    for (size_t i = 0; i < n; ++i) {
+        values[i] *= scale;
+        if (weight) values[i] *= weight[i];
+    }
+}
+
+// math.rs:822-846 (apply_rotary_interleaved_to_split_half): f64 angles.
+int oracle_rope_interleaved_to_split_half(float* values, size_t n, size_t position,
+                                          size_t rotary_dim, double theta) {
+    if (rotary_dim == 0 || rotary_dim % 2 != 0 || n < rotary_dim) return kInvalid;
+    std::vector<float> input(values, values + rotary_dim);
+    size_t half = rotary_dim / 2;
+    for (size_t pair = 0; pair < half; ++pair) {
+        double frequency = std::pow(theta, -static_cast<double>(2 * pair) / static_cast<double>(rotary_dim));
+        double angle = static_cast<double>(position) * frequency;
+        double s = std::sin(angle), c = std::cos(angle);
+        float a = input[2 * pair];
+        float b = input[2 * pair + 1];
+        values[pair] = a * static_cast<float>(c) - b * static_cast<float>(s);
+        values[half + pair] = b * static_cast<float>(c) + a * static_cast<float>(s);
+    }
+    return kOk;
+}
+
+// runtime/mod.rs:2825-2836: cos/sin tables for one position, computed in f64 and
+// stored as f32 (what the Metal path feeds glm_mla_prepare_query_kv).
+int oracle_rope_tables(size_t position, size_t rotary_dim, double theta, float* cos_out,
+                       float* sin_out) {
+    if (rotary_dim == 0 || rotary_dim % 2 != 0) return kInvalid;
+    for (size_t pair = 0; pair < rotary_dim / 2; ++pair) {
+        double frequency = std::pow(theta, -static_cast<double>(2 * pair) / static_cast<double>(rotary_dim));
+        double angle = static_cast<double>(position) * frequency;
+        cos_out[pair] = static_cast<float>(std::cos(angle));
+        sin_out[pair] = static_cast<float>(std::sin(angle));
+    }
+    return kOk;
+}
+
+// shaders.metal:1059-1075 (dense_mmap_fma_matvec_bf16): acc = fma(w, x, acc) in
+// column order. The router and shared-expert gate are dense bf16 rows.
+int oracle_dense_bf16_matvec(const uint16_t* weight, const float* input, size_t rows, size_t cols,
+                             float* out) {
+    for (size_t r = 0; r < rows; ++r) {
+        float acc = 0.0f;
+        for (size_t c = 0; c < cols; ++c) acc = std::fma(bf16_to_f32(weight[r * cols + c]), input[c], acc);
+        out[r] = acc;
+    }
+    return kOk;
+}
+
+// QwenMoeQ4ExpertLayout::fixed_bf16 (model_family.rs:954-1010): component
+// offsets (9) and the slot size. Returns 0, or -1 when hidden/inter are not
+// multiples of the group (the reference's bail!).
+int oracle_fixed_q4_layout(size_t hidden, size_t inter, size_t group, uint64_t* offsets,
+                           uint64_t* expert_bytes) {
+    if (hidden == 0 || inter == 0 || group == 0 || hidden % group != 0 || inter % group != 0)
+        return kInvalid;
+    uint64_t gw = inter * hidden / 2, gsb = inter * (hidden / group) * 2;
+    uint64_t dw = hidden * inter / 2, dsb = hidden * (inter / group) * 2;
+    uint64_t sizes[9] = {gw, gsb, gsb, gw, gsb, gsb, dw, dsb, dsb};
+    uint64_t off = 0;
+    for (int i = 0; i < 9; ++i) {
+        offsets[i] = off;
+        off += sizes[i];
+    }
+    *expert_bytes = off;
+    return kOk;
+}
+
+// One SwiGLU expert on a whole-expert slot (tests/scheduler.rs:327-336).
+int oracle_expert_swiglu(const uint8_t* slot, const uint64_t* offsets, size_t hidden,
+                         size_t inter, size_t group, const float* x, float* out) {
+    if (group == 0) return kInvalid;
+    std::vector<float> tmp(inter);
+    expert_swiglu(slot_view(slot, offsets), hidden, inter, group, x, out, tmp.data());
+    return kOk;
+}
+
+// qwen_layer_major_combine (shaders.metal:1756-1786) for tokens whose routed
+// expert outputs are already computed, routes in slot order:
+//   moe = sum_k weights[t,k] * expert_out[t,k,:]   (k ascending)
+//   hidden = residual + moe + shared_weight[t] * shared[t,:]
+// residual, shared and shared_weight are nullable (0, 0, and 1 respectively).
+int oracle_combine(const float* residual, const float* expert_out, const float* weights,
+                   const float* shared, const float* shared_weight, size_t tokens, size_t top_k,
+                   size_t hidden, float* out) {
+    for (size_t t = 0; t < tokens; ++t) {
+        for (size_t c = 0; c < hidden; ++c) {
+            float moe = 0.0f;
+            for (size_t k = 0; k < top_k; ++k)
+                moe += weights[t * top_k + k] * expert_out[(t * top_k + k) * hidden + c];
+            float sw = shared_weight ? shared_weight[t] : 1.0f;
+            float sh = shared ? shared[t * hidden + c] : 0.0f;
+            float r = residual ? residual[t * hidden + c] : 0.0f;
+            out[t * hidden + c] = r + moe + sw * sh;
+        }
+    }
+    return kOk;
+}
+
+// One MoE FFN decode layer per token, as the reference decode path runs it:
+//   router logits (dense bf16, shaders.metal:1059-1075)
+//   -> routing_softmax_top_k (math.rs:771-783)
+//   -> RenormalizeSelected x routed_scale (scheduler/expert_access.rs:80-133)
+//   -> per route SwiGLU expert (tests/scheduler.rs:327-336)
+//   -> hidden = residual + sum_k w_k y_k + sigmoid(shared_gate . x) * shared(x)
+//      (combine_expert_phase / qwen_layer_major_combine, shaders.metal:1723-1786).
+// x, residual (nullable) and out are f32 [tokens x hidden]. Expert e's slot
+// starts at expert_table + e * slot_stride and uses the nine component
+// `offsets`; the shared expert (nullable) uses the same offsets. A NULL
+// shared_gate gives the shared expert weight 1. ids/weights/logits outputs are
+// nullable. threads > 1 parallelises over tokens only.
+int oracle_moe_layer(const float* x, const float* residual, size_t tokens, size_t hidden,
+                     size_t num_experts, size_t top_k, size_t inter, size_t group,
+                     float routed_scale, const uint16_t* router_weight,
+                     const uint16_t* shared_gate, const uint8_t* expert_table,
+                     const uint64_t* offsets, size_t slot_stride, const uint8_t* shared_slot,
+                     float* out, uint32_t* ids_out, float* weights_out, float* logits_out,
+                     int threads) {
+    if (group == 0 || top_k == 0 || top_k > num_experts) return kInvalid;
+    auto one_token = [&](size_t t) -> int {
+        const float* xt = x + t * hidden;
+        std::vector<float> logits(num_experts);
+        oracle_dense_bf16_matvec(router_weight, xt, num_experts, hidden, logits.data());
+        if (logits_out) std::memcpy(logits_out + t * num_experts, logits.data(), num_experts * 4);
+        std::vector<uint32_t> ids(top_k);
+        std::vector<float> probs(top_k), weights(top_k);
+        oracle_routing_softmax_top_k(logits.data(), num_experts, top_k, ids.data(), probs.data());
+        if (oracle_renormalize_routes(probs.data(), top_k, 0, routed_scale, weights.data()) != kOk)
+            return kInvalid;
+        if (ids_out) std::memcpy(ids_out + t * top_k, ids.data(), top_k * 4);
+        if (weights_out) std::memcpy(weights_out + t * top_k, weights.data(), top_k * 4);
+        std::vector<float> y(top_k * hidden), tmp(inter), shared(hidden, 0.0f);
+        for (size_t k = 0; k < top_k; ++k) {
+            const uint8_t* slot = expert_table + static_cast<size_t>(ids[k]) * slot_stride;
+            expert_swiglu(slot_view(slot, offsets), hidden, inter, group, xt, y.data() + k * hidden,
+                          tmp.data());
+        }
+        float shared_weight = 0.0f;
+        if (shared_slot) {
+            expert_swiglu(slot_view(shared_slot, offsets), hidden, inter, group, xt, shared.data(),
+                          tmp.data());
+            if (shared_gate) {
+                float route;
+                oracle_dense_bf16_matvec(shared_gate, xt, 1, hidden, &route);
+                shared_weight = 1.0f / (1.0f + std::exp(-route));
+            } else {
+                shared_weight = 1.0f;
+            }
+        }
+        oracle_combine(residual ? residual + t * hidden : nullptr, y.data(), weights.data(),
+                       shared.data(), &shared_weight, 1, top_k, hidden, out + t * hidden);
+        return kOk;
+    };
+    std::atomic<int> failed{0};
+    parallel_for(tokens, threads, [&](size_t t) {
+        if (one_token(t) != kOk) failed.store(1);
+    });
+    return failed.load() ? kInvalid : kOk;
+}
+
+// weights/store.rs:1179-1327 (DenseStore::mla_absorbed_attention), FusedKvB
+// arm, with the absorbed weights given as dense bf16 instead of Q4 rows:
+//   w_uk [heads x nope x latent]  (kv_b rows head*(nope+v) + d, first nope rows)
+//   w_uv [heads x v x latent]     (kv_b rows head*(nope+v) + nope + d)
+// query is [heads x (nope + rope)] with the rope part ALREADY rotated (the
+// runtime rotates it before the call, runtime/mod.rs:2891-2899); records are
+// `sequence` rows of latent[latent] and rotary[rope] (already rotated at write).
+// out is [heads x v].
+//   absorbed[c] += q_nope[d] * w_uk[d][c]   (q4_row_add_scaled order, d outer)
+//   s_t = (sum absorbed*latent + sum q_rope*rotary) * (1/sqrt(qk_head_dim))
+//   p = softmax_in_place(s)                 (math.rs:728-744)
+//   ctx[c] += p_t * latent_t[c]             (t outer)
+//   out[d] = sum_c ctx[c] * w_uv[d][c]      (q4_row_dot: sum += input * w)
+int oracle_mla_absorbed_attention(const float* query, const float* latents, const float* rotary,
+                                  size_t sequence, const uint16_t* w_uk, const uint16_t* w_uv,
+                                  size_t heads, size_t nope, size_t rope, size_t latent,
+                                  size_t v_dim, float* out) {
+    if (sequence == 0) return kInvalid;
+    size_t qk_head_dim = nope + rope;
+    float scale = 1.0f / std::sqrt(static_cast<float>(qk_head_dim));
+    std::vector<float> absorbed(latent), scores(sequence), context(latent);
+    for (size_t h = 0; h < heads; ++h) {
+        const float* qh = query + h * qk_head_dim;
+        const float* q_nope = qh;
+        const float* q_rope = qh + nope;
+        std::fill(absorbed.begin(), absorbed.end(), 0.0f);
+        for (size_t d = 0; d < nope; ++d) {
+            float coefficient = q_nope[d];
+            const uint16_t* wrow = w_uk + (h * nope + d) * latent;
+            for (size_t c = 0; c < latent; ++c) absorbed[c] += coefficient * bf16_to_f32(wrow[c]);
+        }
+        for (size_t t = 0; t < sequence; ++t) {
+            const float* lat = latents + t * latent;
+            const float* rot = rotary + t * rope;
+            float latent_score = 0.0f;
+            for (size_t c = 0; c < latent; ++c) latent_score += absorbed[c] * lat[c];
+            float rotary_score = 0.0f;
+            for (size_t c = 0; c < rope; ++c) rotary_score += q_rope[c] * rot[c];
+            scores[t] = (latent_score + rotary_score) * scale;
+        }
+        oracle_softmax_in_place(scores.data(), sequence);
+        std::fill(context.begin(), context.end(), 0.0f);
+        for (size_t t = 0; t < sequence; ++t) {
+            float w = scores[t];
+            const float* lat = latents + t * latent;
+            for (size_t c = 0; c < latent; ++c) context[c] += w * lat[c];
+        }
+        for (size_t d = 0; d < v_dim; ++d) {
+            const uint16_t* wrow = w_uv + (h * v_dim + d) * latent;
+            float sum = 0.0f;
+            for (size_t c = 0; c < latent; ++c) sum += context[c] * bf16_to_f32(wrow[c]);
+            out[h * v_dim + d] = sum;
+        }
+    }
+    return kOk;
+}
+
+// weights/store.rs:1179-1327, AbsorbedMultiLinear arm with Q4 embed_q /
+// unembed_out (q4_row_dot, store.rs:1129-1177: sum += x * q.mul_add(s, b)).
+// embed_q: [heads*latent rows x nope cols]; unembed_out: [heads*v rows x latent cols];
+// both with bf16 S/B and `group` columns per group. Used to pin the oracle to
+// the closed-form test at tests/metal.rs:1872-2028.
+int oracle_mla_absorbed_attention_q4(const float* query, const float* latents, const float* rotary,
+                                     size_t sequence, const uint8_t* eq_packed,
+                                     const uint16_t* eq_s, const uint16_t* eq_b, size_t eq_group,
+                                     const uint8_t* uo_packed, const uint16_t* uo_s,
+                                     const uint16_t* uo_b, size_t uo_group, size_t heads,
+                                     size_t nope, size_t rope, size_t latent, size_t v_dim,
+                                     float* out) {
+    if (sequence == 0 || eq_group == 0 || uo_group == 0) return kInvalid;
+    size_t qk_head_dim = nope + rope;
+    float scale = 1.0f / std::sqrt(static_cast<float>(qk_head_dim));
+    auto row_dot = [](const uint8_t* packed, const uint16_t* s, const uint16_t* b, size_t group,
+                      size_t row, size_t cols, const float* input) {
+        size_t gpr = div_ceil(cols, group);
+        const uint8_t* pr = packed + row * div_ceil(cols, 2);
+        float sum = 0.0f;
+        for (size_t g = 0; g < gpr; ++g) {
+            float sc = bf16_to_f32(s[row * gpr + g]);
+            float bi = bf16_to_f32(b[row * gpr + g]);
+            size_t start = g * group, end = start + group < cols ? start + group : cols;
+            for (size_t c = start; c < end; ++c) sum += input[c] * std::fma(nibble_at(pr, c), sc, bi);
+        }
+        return sum;
+    };
+    std::vector<float> absorbed(latent), scores(sequence), context(latent);
+    for (size_t h = 0; h < heads; ++h) {
+        const float* qh = query + h * qk_head_dim;
+        for (size_t c = 0; c < latent; ++c)
+            absorbed[c] = row_dot(eq_packed, eq_s, eq_b, eq_group, h * latent + c, nope, qh);
+        for (size_t t = 0; t < sequence; ++t) {
+            float ls = 0.0f;
+            for (size_t c = 0; c < latent; ++c) ls += absorbed[c] * latents[t * latent + c];
+            float rs = 0.0f;
+            for (size_t c = 0; c < rope; ++c) rs += qh[nope + c] * rotary[t * rope + c];
+            scores[t] = (ls + rs) * scale;
+        }
+        oracle_softmax_in_place(scores.data(), sequence);
+        std::fill(context.begin(), context.end(), 0.0f);
+        for (size_t t = 0; t < sequence; ++t)
+            for (size_t c = 0; c < latent; ++c) context[c] += scores[t] * latents[t * latent + c];
+        for (size_t d = 0; d < v_dim; ++d)
+            out[h * v_dim + d] = row_dot(uo_packed, uo_s, uo_b, uo_group, h * v_dim + d, latent,
+                                         context.data());
+    }
+    return kOk;
+}
+
+// Dense Q4 x bf16 GEMM restated from the batched Metal matrix path
+// (q4_mmap_fma_matvec_batch_bf16_scale_bias, shaders.metal:973-1057): every
+// output element is the q4_fma row dot of math.rs:861-911 for one input row.
+// x [m x k] f32, out [m x n] f32 for weight [n x k]. threads > 1 splits rows.
+int oracle_q4_gemm(const float* x, size_t m, const uint8_t* packed, const uint16_t* scales,
+                   const uint16_t* biases, size_t n, size_t k, size_t group, float* out,
+                   int threads) {
+    if (group == 0) return kInvalid;
+    parallel_for(m, threads, [&](size_t i) {
+        for (size_t r = 0; r < n; ++r)
+            out[i * n + r] = q4_fma_row_bf16(packed, x + i * k, scales, biases, r, k, group);
+    });
+    return kOk;
+}
+
+}  // extern "C"
