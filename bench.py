@@ -1,0 +1,434 @@
+#!/usr/bin/env python3
+"""Benchmark of the FlashMoE hot path on B200.
+
+Workload: one MoE FFN decode layer per step — hidden
+2048, 512 routed experts top-10 (softmax, renormalised), 1 shared expert with
+a sigmoid gate, expert intermediate 512, 4-bit group-64 affine weights, bf16
+activations ~N(0,1) — on `--batch` tokens. Consecutive steps cycle through
+`--layers` (default 48) independently seeded layers (43.5 GB of expert
+weights) and distinct inputs, so every step's weights come from HBM rather
+than L2 (126 MB): the per-layer router + shared expert alone are 182 MB over
+48 layers.
+
+Reported (one JSON line on rank 0):
+  value     tokens/s of the whole job, device-timed (CUDA events, max over
+            ranks) over exactly --steps graph-replayed steps, inputs resident.
+  e2e       the same metric through the public C-ABI call per step with host
+            buffers: pinned H2D of the step's tokens, pbmoe_moe_layer, D2H of
+            its output, all inside the timed region.
+  roofline  dominant kernel's algorithmic bytes / its event-timed duration vs
+            the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the C++ oracle (restatement of the reference's Rust CPU path)
+            on this host's cores, bounded sample.
+`--impl reference` times the oracle alone (the reference cannot be built:
+Rust toolchain absent; its GPU path is Metal).
+
+Multi-GPU (torchrun, N>1): every rank runs its own replica of the layer stack
+on its own tokens ("weak" scaling); expert-parallel sharding is not wired into
+this bench yet.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, EXPERTS, TOPK, INTER, GROUP = 2048, 512, 10, 512, 64
+SLOT_BYTES = 1_769_472
+GATE_UP_BYTES = 2 * (524_288 + 2 * 32_768)  # gate + up: nibbles + bf16 S + B
+DOWN_BYTES = 524_288 + 2 * 32_768
+ROUTER_BYTES = EXPERTS * HIDDEN * 2
+SHARED_GATE_BYTES = HIDDEN * 2
+METRIC = "MoE decode tok/s (config 1: one MoE FFN decode layer per step)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--layers", type=int, default=48)
+    p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ CPU arm
+def host_layer(seed: int):
+    """One config-1 layer generated on the host (torch CPU generator)."""
+    import numpy as np
+    import torch
+
+    from oracle import pb_oracle
+
+    g = torch.Generator().manual_seed(seed)
+    offs, nbytes = pb_oracle.fixed_q4_layout(HIDDEN, INTER, GROUP)
+
+    def sb(rows, groups, n):
+        s = torch.empty(n, rows, groups).uniform_(0.004, 0.02, generator=g).to(torch.bfloat16)
+        b = (-8.0 * s.float() + torch.randn(n, rows, groups, generator=g) * 1e-3).to(torch.bfloat16)
+        return s.view(torch.int16).numpy().view(np.uint8).reshape(n, -1), \
+            b.view(torch.int16).numpy().view(np.uint8).reshape(n, -1)
+
+    def table(n):
+        t = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, generator=g).numpy()
+        for p, (rows, cols) in enumerate([(INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER)]):
+            s, b = sb(rows, cols // GROUP, n)
+            so, bo = int(offs[3 * p + 1]), int(offs[3 * p + 2])
+            t[:, so:so + s.shape[1]] = s
+            t[:, bo:bo + b.shape[1]] = b
+        return t
+
+    router = (torch.randn(EXPERTS, HIDDEN, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16).numpy()
+    experts = table(EXPERTS)
+    shared = table(1)[0]
+    gate = (torch.randn(HIDDEN, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16).numpy()
+    return dict(router=router.view(np.uint16), experts=experts, shared=shared, gate=gate.view(np.uint16), offs=offs,
+                nbytes=nbytes)
+
+
+def cpu_oracle_rate(batch: int, target_s: float, steps: int | None = None):
+    """Tokens/s of the oracle MoE layer on this host's cores (bounded sample)."""
+    import numpy as np
+    import torch
+
+    from oracle import pb_oracle
+
+    threads = os.cpu_count() or 1
+    L = host_layer(99)
+    g = torch.Generator().manual_seed(5)
+
+    def run(tokens):
+        x = torch.randn(tokens, HIDDEN, generator=g).to(torch.bfloat16).float().numpy()
+        t0 = time.perf_counter()
+        pb_oracle.moe_layer(x, L["router"], L["experts"], L["offs"], L["nbytes"], EXPERTS, TOPK, INTER, GROUP,
+                            shared_slot=L["shared"], shared_gate_bits=L["gate"], threads=threads)
+        return time.perf_counter() - t0
+
+    run(min(batch, threads))  # warm the page cache / code
+    probe = run(batch)
+    if steps is None:
+        reps = max(1, int(target_s / max(probe, 1e-3)))
+    else:
+        reps = steps
+    times = [run(batch) for _ in range(reps)]
+    total = sum(times)
+    return dict(value=batch * reps / total, unit="tok/s", cores=threads, kind="port",
+                sample=f"{reps} steps x {batch} tokens through one config-1 layer (C++ oracle, {threads} threads)",
+                seconds=total, per_step_s=total / reps)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    # Each step is one config-1 layer over --batch tokens on all host threads;
+    # warm-up steps are run and discarded.
+    import numpy as np  # noqa: F401
+
+    from oracle import pb_oracle
+
+    pb_oracle.build()
+    res = cpu_oracle_rate(args.batch, target_s=0, steps=max(1, args.warmup))
+    res = cpu_oracle_rate(args.batch, target_s=0, steps=args.steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["per_step_s"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, config-1 distributions)",
+        "config": {"workload": "config1 MoE FFN decode layer", "batch": args.batch, "hidden": HIDDEN,
+                   "experts": EXPERTS, "top_k": TOPK, "intermediate": INTER, "group": GROUP},
+        "cpu_baseline": {"value": res["value"], "unit": "tok/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference = C++ restatement of pb's Rust CPU path (Rust toolchain absent; Metal GPU path "
+                "unavailable on this box)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ CUDA arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import numpy as np
+    import torch
+
+    from pb_b200 import capi, synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    B, NL = args.batch, args.layers
+    ctx = capi.Context(local)
+    layers = [synth.MoeLayerWeights(dev, seed=1000 * rank + i) for i in range(NL)]
+    cfg = capi.moe_config(layers[0].layout, EXPERTS, TOPK)
+    ctx.reserve(B, cfg)
+    NIN = 2 * NL  # distinct inputs: step j uses layer j % NL and input j % NIN
+    g = synth.gen(dev, 7 + rank)
+    xs = [synth.normal_bf16((B, HIDDEN), 1.0, g, dev) for _ in range(NIN)]
+    outs = [torch.empty(B, HIDDEN, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    weights = [lw.c_weights() for lw in layers]
+    stream = torch.cuda.Stream(dev)
+
+    def step(j, s=None, debug=None):
+        ctx.moe_layer(cfg, weights[j % NL], xs[j % NIN], outs[j % 2], B, debug=debug, stream=s)
+
+    # -- unique experts per (layer, input) combination, from the routes themselves
+    ids = torch.empty(B, TOPK, dtype=torch.int32, device=dev)
+    uniq = []
+    with torch.cuda.stream(stream):
+        for j in range(NIN):
+            step(j, stream, capi.MoeDebug(None, ids.data_ptr(), None, None, None))
+            stream.synchronize()
+            uniq.append(int(torch.unique(ids).numel()))
+    assert ctx.device_status(stream=stream) == 0
+
+    # -- CUDA graphs: one per step slot, plus one holding a whole cycle of NIN
+    #    slots so that the host launches one graph per NIN steps
+    graphs = []
+    with torch.cuda.stream(stream):
+        for j in range(NIN):
+            step(j, stream)  # warm the launch path for this slot
+        stream.synchronize()
+        for j in range(NIN):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step(j, stream)
+            graphs.append(gr)
+        cycle = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cycle, stream=stream):
+            for j in range(NIN):
+                step(j, stream)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def replay_steps(first, count):
+        """Replay exactly `count` steps starting at slot `first` (mod NIN)."""
+        slot, left = first % NIN, count
+        while left and slot != 0:
+            graphs[slot].replay()
+            slot, left = (slot + 1) % NIN, left - 1
+        while left >= NIN:
+            cycle.replay()
+            left -= NIN
+        for j in range(left):
+            graphs[j].replay()
+
+    W, K = max(3, args.warmup), args.steps
+    with torch.cuda.stream(stream):
+        replay_steps(0, W)
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            replay_steps(W, K)
+            ev1.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clock_summary = clocks.summary()
+    assert ctx.device_status(stream=stream) == 0
+    value = K * B * world / (ms / 1e3)
+    steps_u = [uniq[(W + i) % NIN] for i in range(K)]
+    mean_u = float(np.mean(steps_u))
+    layer_bytes = ROUTER_BYTES + SHARED_GATE_BYTES + SLOT_BYTES * (1 + mean_u) + 2 * B * HIDDEN * 2
+
+    # -- per-kernel durations (events between the four kernels; serialised, no PDL overlap)
+    NPH = min(K, NIN)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(NPH)]
+    for row in evs:  # torch creates the CUDA event lazily, on first record
+        for e in row:
+            e.record(stream)
+    stream.synchronize()
+    handles = [(C_void_p_array(e)) for e in evs]
+    with torch.cuda.stream(stream):
+        for i in range(NPH):
+            step(W + i, stream, capi.MoeDebug(None, None, None, None, handles[i][0]))
+    stream.synchronize()
+    names = ["router+topk", "expert_gate_up", "expert_down", "combine"]
+    dur = {n: [] for n in names}
+    for e in evs:
+        for k, n in enumerate(names):
+            dur[n].append(e[k].elapsed_time(e[k + 1]))
+    mean_dur = {n: float(np.mean(v)) for n, v in dur.items()}
+    u_ph = [uniq[(W + i) % NIN] for i in range(NPH)]
+    kbytes = {
+        "router+topk": ROUTER_BYTES + SHARED_GATE_BYTES + B * HIDDEN * 2,
+        "expert_gate_up": float(np.mean([(u + 1) * GATE_UP_BYTES for u in u_ph])) + B * HIDDEN * 2,
+        "expert_down": float(np.mean([(u + 1) * DOWN_BYTES for u in u_ph])),
+        "combine": B * HIDDEN * 2 * 2 + B * (TOPK + 1) * HIDDEN * 4,
+    }
+    dominant = max(mean_dur, key=lambda n: mean_dur[n])
+    peak, peak_kind = measured_peaks()
+    achieved = kbytes[dominant] / (mean_dur[dominant] / 1e3) / 1e9
+    serial_ms = sum(mean_dur.values())
+
+    # -- end to end through the public C-ABI call with host buffers
+    h_in = torch.empty(B, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    h_out = torch.empty(B, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    h_in.copy_(xs[0].cpu())
+    d_in = torch.empty(B, HIDDEN, device=dev, dtype=torch.bfloat16)
+    KE = min(K, 4 * NIN)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(KE):
+            d_in.copy_(h_in, non_blocking=True)
+            ctx.moe_layer(cfg, weights[i % NL], d_in, outs[0], B, stream=stream)
+            h_out.copy_(outs[0], non_blocking=True)
+        e1.record(stream)
+    stream.synchronize()
+    ems = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ems], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = KE * B * world / (ems / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            from oracle import pb_oracle
+
+            pb_oracle.build()
+            cpu = cpu_oracle_rate(B, target_s=12.0)
+            cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {exc}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded; config-1 shapes and distributions)",
+            "config": {"workload": "config1 MoE FFN decode layer", "batch": B, "hidden": HIDDEN,
+                       "experts": EXPERTS, "top_k": TOPK, "intermediate": INTER, "group": GROUP,
+                       "shared_expert": True, "layers_cycled": NL,
+                       "l2": f"inputs larger than L2: {NL} distinct layers cycled ({NL * SLOT_BYTES * EXPERTS / 1e9:.1f} GB experts)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "graph": f"CUDA graphs of {NIN} steps replayed back to back"},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": B * HIDDEN * 2,
+                    "d2h_bytes_per_step": B * HIDDEN * 2, "steps": KE},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": None, "algorithmic_bytes_per_launch": kbytes[dominant],
+                         "launch_ms": mean_dur[dominant]},
+            "layer": {"unique_experts_mean": mean_u, "algorithmic_bytes": layer_bytes,
+                      "achieved_gbs": layer_bytes / (ms / K / 1e3) / 1e9,
+                      "frac_of_peak": layer_bytes / (ms / K / 1e3) / 1e9 / peak,
+                      "kernel_ms": mean_dur, "kernel_ms_serial_sum": serial_ms},
+            "gpu_launches": 4 * K,
+            "clocks": clock_summary,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def C_void_p_array(events):
+    """Host array of cudaEvent_t handles for pbmoe_moe_debug.phase_events."""
+    import ctypes
+
+    arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+    return ctypes.cast(arr, ctypes.c_void_p).value, arr
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/*
+ * pbmoe_cuda.h — C ABI of the B200 (sm_100a) FlashMoE hot path.
+ *
+ * This is the drop-in boundary that replaces the Metal execution backend of
+ * Jc2k/pb's FlashMoE runtime (src/inference/flashmoe/metal/, driven through
+ * MetalExecutionFacade, runtime/mod.rs:648-1416). The runtime's host code keeps
+ * its model/scheduler API and calls these entry points instead of encoding
+ * Metal command buffers; INTEGRATION.md shows the Rust `extern "C"` block and
+ * build.rs a maintainer would add.
+ *
+ * Conventions
+ *  - Plain C: pointers, sizes, enums. No CUDA or torch types; a stream is a
+ *    `void*` holding a cudaStream_t (NULL = the legacy default stream).
+ *  - Every data pointer is a DEVICE pointer unless the comment says host.
+ *  - Every call validates its geometry on the host before launching and
+ *    returns a pbmoe_status; the text of the last failure is kept per context
+ *    (pbmoe_last_error). Nothing falls back to a CPU path: an unsupported shape
+ *    is PBMOE_ERR_UNSUPPORTED, mirroring the reference's
+ *    `bail!("FlashMoe unsupported ...")` (docs/flashmoe-architecture-parity-plan.md:22-29).
+ *  - Calls are stream-ordered and asynchronous. Errors detected by a kernel
+ *    (invalid routing weights, bounded-wait timeouts) are latched in a device
+ *    status word that pbmoe_device_status() reads back.
+ *  - A context is not thread-safe; use one per engine, as the reference keeps
+ *    one FlashMoeEngine per request (`&mut self`).
+ *
+ * Quantised weight format (shared by every entry point)
+ *  - Q4 nibbles, row-major, ceil(cols/2) bytes per row; column c is the low
+ *    nibble of byte c/2 when c is even, the high nibble when odd
+ *    (math.rs:903-904; equivalently 8 nibbles per little-endian u32,
+ *    shaders.metal:58-65).
+ *  - Scales and biases: bf16 bits, [rows x ceil(cols/group_size)] row-major
+ *    (experts/mod.rs:917-934).
+ *  - w = q * scale + bias (math.rs:949).
+ */
+#ifndef PBMOE_CUDA_H
+#define PBMOE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PBMOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PBMOE_API __attribute__((visibility("default")))
+#else
+#define PBMOE_API
+#endif
+
+typedef enum pbmoe_status {
+    PBMOE_OK = 0,
+    PBMOE_ERR_INVALID_ARGUMENT = -1, /* bad pointer / size / geometry             */
+    PBMOE_ERR_UNSUPPORTED = -2,      /* valid in the reference, not built here     */
+    PBMOE_ERR_CUDA = -3,             /* a CUDA runtime call failed                 */
+    PBMOE_ERR_TIMEOUT = -4,          /* a bounded device or host wait expired      */
+    PBMOE_ERR_PEER = -5,             /* an expert-parallel peer failed / is absent */
+    PBMOE_ERR_NO_WORKSPACE = -6,     /* pbmoe_reserve was not called or too small  */
+    PBMOE_ERR_DEVICE_STATUS = -7     /* a kernel latched an error word             */
+} pbmoe_status;
+
+/* Device status bits latched by kernels (pbmoe_device_status). */
+#define PBMOE_DEV_ERR_ROUTE_WEIGHTS 0x1u /* selected probabilities not positive-finite */
+#define PBMOE_DEV_ERR_EXPERT_ID 0x2u     /* route expert id out of range               */
+#define PBMOE_DEV_ERR_PEER_TIMEOUT 0x4u  /* expert-parallel combine wait expired       */
+
+typedef enum pbmoe_dtype {
+    PBMOE_F32 = 0,
+    PBMOE_BF16 = 1
+} pbmoe_dtype;
+
+typedef struct pbmoe_ctx pbmoe_ctx;
+
+/* One Q4 affine matrix [rows x cols]. Replaces Q4MatvecPayload
+ * (experts/slots.rs:1172-1199) once its bytes are resident on the device. */
+typedef struct pbmoe_q4_tensor {
+    const void* packed;      /* rows * ceil(cols/2) bytes                      */
+    const uint16_t* scales;  /* rows * ceil(cols/group_size) bf16              */
+    const uint16_t* biases;  /* rows * ceil(cols/group_size) bf16              */
+    uint32_t rows;
+    uint32_t cols;
+    uint32_t group_size;
+} pbmoe_q4_tensor;
+
+/* Whole-expert slot layout. Replaces QwenMoeQ4ExpertLayout
+ * (model_family.rs:839-1010): nine components in the order gate{W,S,B},
+ * up{W,S,B}, down{W,S,B}; gate/up are [intermediate x hidden], down is
+ * [hidden x intermediate]. */
+typedef struct pbmoe_expert_layout {
+    uint64_t component_offsets[9];
+    uint64_t expert_bytes; /* slot stride in the expert table */
+    uint32_t hidden;
+    uint32_t intermediate;
+    uint32_t group_size;
+} pbmoe_expert_layout;
+
+/* Routing weight normalisation (QwenMoeRoutingWeightNormalization,
+ * model_family.rs:111-115; applied in scheduler/expert_access.rs:80-133). */
+typedef enum pbmoe_route_norm {
+    PBMOE_ROUTE_RENORMALIZE_SELECTED = 0,
+    PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR = 1
+} pbmoe_route_norm;
+
+/* Shapes and policy of one MoE FFN layer (QwenModelConfig fields,
+ * model_family.rs:180-470). */
+typedef struct pbmoe_moe_config {
+    pbmoe_expert_layout layout;
+    uint32_t num_experts;        /* experts per layer (E)                    */
+    uint32_t top_k;              /* routed experts per token (K), 1..32       */
+    uint32_t normalization;      /* pbmoe_route_norm                          */
+    float routed_scaling_factor; /* multiplies the normalised weights (1.0)   */
+    float norm_epsilon;          /* next-layer RMSNorm epsilon (1e-6)         */
+} pbmoe_moe_config;
+
+/* Device-resident weights of one MoE layer. */
+typedef struct pbmoe_moe_weights {
+    const uint16_t* router_weight;      /* bf16 [E x hidden]                          */
+    const uint8_t* experts;             /* E slots, layout.expert_bytes apart          */
+    const uint8_t* shared_expert;       /* one slot in the same layout, or NULL        */
+    const uint16_t* shared_expert_gate; /* bf16 [hidden] sigmoid gate, or NULL (= 1.0)  */
+} pbmoe_moe_weights;
+
+/* Optional outputs of pbmoe_moe_layer for inspection and parity checks. Any
+ * member may be NULL. */
+typedef struct pbmoe_moe_debug {
+    float* router_logits;   /* f32 [tokens x E]                        */
+    uint32_t* route_ids;    /* u32 [tokens x K], replacement-slot order */
+    float* route_weights;   /* f32 [tokens x K], normalised and scaled  */
+    float* shared_logit;    /* f32 [tokens]                             */
+    /* Host array of 5 cudaEvent_t (as void*), or NULL. When given, event 0 is
+     * recorded before the router kernel and event i after kernel i (router,
+     * expert gate/up, expert down, combine), the CUDA counterpart of the
+     * reference's per-phase timing buckets (FlashMoeTimingBuckets,
+     * types.rs:600-640). Recording serialises the four kernels. */
+    void* const* phase_events;
+} pbmoe_moe_debug;
+
+/* ---------------------------------------------------------------- context */
+
+/* Create a context on CUDA device `device`. Allocates nothing on the device
+ * beyond a status word; call pbmoe_reserve before pbmoe_moe_layer. */
+PBMOE_API int pbmoe_init(int device, pbmoe_ctx** out);
+PBMOE_API int pbmoe_destroy(pbmoe_ctx* ctx);
+/* Text of the last failure on this context (empty when none). Valid until the
+ * next call on the context. */
+PBMOE_API const char* pbmoe_last_error(const pbmoe_ctx* ctx);
+PBMOE_API int pbmoe_abi_version(void);
+
+/* Size the context's device workspace for MoE layers of up to `max_tokens`
+ * tokens with this config. Allocation happens here, never on the hot path
+ * (the reference recycles pooled Metal buffers, metal/mod.rs:3270-3330). */
+PBMOE_API int pbmoe_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, const pbmoe_moe_config* config);
+/* Workspace bytes pbmoe_reserve would allocate (host-only arithmetic). */
+PBMOE_API size_t pbmoe_moe_workspace_bytes(uint32_t max_tokens, const pbmoe_moe_config* config);
+
+/* Read (and clear when `clear` != 0) the device status word after
+ * synchronising `stream`. *out receives PBMOE_DEV_ERR_* bits. */
+PBMOE_API int pbmoe_device_status(pbmoe_ctx* ctx, void* stream, uint32_t* out, int clear);
+
+/* Fill *out with the reference's fixed whole-expert layout
+ * (QwenMoeQ4ExpertLayout::fixed_bf16, model_family.rs:954-1010). Host-only. */
+PBMOE_API int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group_size,
+                          pbmoe_expert_layout* out);
+
+/* ---------------------------------------------------------------- kernels */
+
+/* y[b, r] = sum_c (q[r,c] * scale + bias) * x[b, c] for b < batch.
+ * x: [batch x cols] in x_dtype; y: [batch x rows] in y_dtype; fp32 accumulate.
+ * Replaces q4_fma_matvec_bf16_scale_bias (shaders.metal:164-199, encoded by
+ * MetalScheduledCmd3Builder::encode_q4_matvec, metal/mod.rs:4871-4916) and the
+ * batched resident form (MetalExecutionFacade::resident_mmap_matvec_batch,
+ * runtime/mod.rs:1184). */
+PBMOE_API int pbmoe_q4_matvec(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype,
+                    void* y, pbmoe_dtype y_dtype, uint32_t batch, void* stream);
+
+/* Routing on given logits: logits f32 [tokens x E] -> route_ids u32 [tokens x K]
+ * (replacement-slot order of routing_top_k_iter, math.rs:746-765) and
+ * route_weights f32 [tokens x K] (routing_softmax_top_k, math.rs:771-783, then
+ * the config's normalisation x routed_scaling_factor,
+ * scheduler/expert_access.rs:80-133). Replaces the CPU RoutingSoftmaxTopK stage
+ * (capabilities.rs:21-31) that follows the router read-back
+ * (metal/qwen_execution.rs:1036-1050). */
+PBMOE_API int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint32_t num_experts,
+                     uint32_t top_k, uint32_t normalization, float routed_scaling_factor,
+                     uint32_t* route_ids, float* route_weights, void* stream);
+
+/* One MoE FFN decode layer for `tokens` tokens (1..max_tokens of pbmoe_reserve):
+ *   router logits -> top-k routing -> per-route SwiGLU expert on Q4 weights
+ *   -> out = residual + sum_k w_k * expert_k(x) + sigmoid(shared_gate . x) * shared(x)
+ * and, when next_norm_weight != NULL, next_normed = RMSNorm(out) * weight.
+ * x: [tokens x hidden] in x_dtype; residual (nullable), out and next_normed in
+ * out_dtype. Replaces MetalExecutionFacade::submit_scheduled_expert_command
+ * (runtime/mod.rs:922-961 -> MetalScheduledCmd3Builder::encode_and_submit,
+ * metal/mod.rs:4289-4470) together with the router projection and CPU top-k
+ * that precede it (runtime/mod.rs:1065, math.rs:771). */
+PBMOE_API int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
+                    const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
+                    pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
+                    void* next_normed, const pbmoe_moe_debug* debug, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* PBMOE_CUDA_H */

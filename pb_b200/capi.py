@@ -1,0 +1,189 @@
+"""ctypes binding of include/pbmoe_cuda.h (libpbmoe.so).
+
+This is plumbing for tests and the benchmark: it passes device pointers (from
+torch tensors) straight to the C ABI, so every call here exercises exactly the
+entry point a Rust host would bind. There is no fallback: if the library is
+missing or the device is absent, loading raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_build", "libpbmoe.so")
+
+PBMOE_OK = 0
+PBMOE_ERR_INVALID_ARGUMENT = -1
+PBMOE_ERR_UNSUPPORTED = -2
+PBMOE_ERR_CUDA = -3
+PBMOE_ERR_TIMEOUT = -4
+PBMOE_ERR_PEER = -5
+PBMOE_ERR_NO_WORKSPACE = -6
+PBMOE_ERR_DEVICE_STATUS = -7
+
+PBMOE_DEV_ERR_ROUTE_WEIGHTS = 0x1
+PBMOE_DEV_ERR_EXPERT_ID = 0x2
+PBMOE_DEV_ERR_PEER_TIMEOUT = 0x4
+
+PBMOE_F32 = 0
+PBMOE_BF16 = 1
+
+ROUTE_RENORMALIZE_SELECTED = 0
+ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR = 1
+
+# Every symbol the header declares (checked by tests/test_capi_symbols.py).
+EXPORTED = [
+    "pbmoe_init", "pbmoe_destroy", "pbmoe_last_error", "pbmoe_abi_version", "pbmoe_reserve",
+    "pbmoe_moe_workspace_bytes", "pbmoe_device_status", "pbmoe_fixed_q4_layout", "pbmoe_q4_matvec",
+    "pbmoe_route_topk", "pbmoe_moe_layer",
+]
+
+
+class Q4Tensor(C.Structure):
+    _fields_ = [("packed", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p),
+                ("rows", C.c_uint32), ("cols", C.c_uint32), ("group_size", C.c_uint32)]
+
+
+class ExpertLayout(C.Structure):
+    _fields_ = [("component_offsets", C.c_uint64 * 9), ("expert_bytes", C.c_uint64),
+                ("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("group_size", C.c_uint32)]
+
+
+class MoeConfig(C.Structure):
+    _fields_ = [("layout", ExpertLayout), ("num_experts", C.c_uint32), ("top_k", C.c_uint32),
+                ("normalization", C.c_uint32), ("routed_scaling_factor", C.c_float), ("norm_epsilon", C.c_float)]
+
+
+class MoeWeights(C.Structure):
+    _fields_ = [("router_weight", C.c_void_p), ("experts", C.c_void_p), ("shared_expert", C.c_void_p),
+                ("shared_expert_gate", C.c_void_p)]
+
+
+class MoeDebug(C.Structure):
+    _fields_ = [("router_logits", C.c_void_p), ("route_ids", C.c_void_p), ("route_weights", C.c_void_p),
+                ("shared_logit", C.c_void_p), ("phase_events", C.c_void_p)]
+
+
+class PbmoeError(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__(f"pbmoe status {code}: {message}")
+        self.code = code
+
+
+_lib = None
+
+
+def load():
+    """Load libpbmoe.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m pb_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        vp, u32, i32 = C.c_void_p, C.c_uint32, C.c_int
+        L.pbmoe_init.argtypes = [i32, C.POINTER(vp)]
+        L.pbmoe_destroy.argtypes = [vp]
+        L.pbmoe_last_error.restype = C.c_char_p
+        L.pbmoe_last_error.argtypes = [vp]
+        L.pbmoe_abi_version.restype = i32
+        L.pbmoe_reserve.argtypes = [vp, u32, C.POINTER(MoeConfig)]
+        L.pbmoe_moe_workspace_bytes.restype = C.c_size_t
+        L.pbmoe_moe_workspace_bytes.argtypes = [u32, C.POINTER(MoeConfig)]
+        L.pbmoe_device_status.argtypes = [vp, vp, C.POINTER(u32), i32]
+        L.pbmoe_fixed_q4_layout.argtypes = [u32, u32, u32, C.POINTER(ExpertLayout)]
+        L.pbmoe_q4_matvec.argtypes = [vp, C.POINTER(Q4Tensor), vp, i32, vp, i32, u32, vp]
+        L.pbmoe_route_topk.argtypes = [vp, vp, u32, u32, u32, u32, C.c_float, vp, vp, vp]
+        L.pbmoe_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32, u32,
+                                      vp, vp, C.POINTER(MoeDebug), vp]
+        _lib = L
+    return _lib
+
+
+def fixed_q4_layout(hidden, intermediate, group):
+    lay = ExpertLayout()
+    rc = load().pbmoe_fixed_q4_layout(hidden, intermediate, group, C.byref(lay))
+    if rc != PBMOE_OK:
+        raise PbmoeError(rc, "invalid fixed-Q4 layout")
+    return lay
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dtype_code(t):
+    import torch
+
+    if t.dtype == torch.float32:
+        return PBMOE_F32
+    if t.dtype == torch.bfloat16:
+        return PBMOE_BF16
+    raise TypeError(f"unsupported activation dtype {t.dtype}")
+
+
+class Context:
+    """One pbmoe_ctx on one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        self.device = device
+        h = C.c_void_p()
+        rc = self.lib.pbmoe_init(device, C.byref(h))
+        if rc != PBMOE_OK:
+            raise PbmoeError(rc, f"pbmoe_init({device}) failed")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.pbmoe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self) -> str:
+        return self.lib.pbmoe_last_error(self.h).decode()
+
+    def check(self, rc):
+        if rc != PBMOE_OK:
+            raise PbmoeError(rc, self.last_error())
+
+    def stream_ptr(self, stream=None):
+        import torch
+
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return C.c_void_p(s.cuda_stream)
+
+    # -------------------------------------------------------------- entry points
+    def q4_matvec(self, packed, scales, biases, rows, cols, group, x, y, batch=1, stream=None):
+        t = Q4Tensor(packed.data_ptr(), scales.data_ptr(), biases.data_ptr(), rows, cols, group)
+        self.check(self.lib.pbmoe_q4_matvec(self.h, C.byref(t), _ptr(x), _dtype_code(x), _ptr(y), _dtype_code(y),
+                                            batch, self.stream_ptr(stream)))
+
+    def route_topk(self, logits, tokens, num_experts, top_k, ids, weights, normalization=0, scale=1.0, stream=None):
+        self.check(self.lib.pbmoe_route_topk(self.h, _ptr(logits), tokens, num_experts, top_k, normalization, scale,
+                                             _ptr(ids), _ptr(weights), self.stream_ptr(stream)))
+
+    def reserve(self, max_tokens, config: MoeConfig):
+        self.check(self.lib.pbmoe_reserve(self.h, max_tokens, C.byref(config)))
+
+    def moe_layer(self, config, weights: MoeWeights, x, out, tokens, residual=None, next_norm_weight=None,
+                  next_normed=None, debug: MoeDebug | None = None, stream=None):
+        self.check(self.lib.pbmoe_moe_layer(
+            self.h, C.byref(config), C.byref(weights), _ptr(x), _dtype_code(x), _ptr(residual), _ptr(out),
+            _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed),
+            C.byref(debug) if debug is not None else None, self.stream_ptr(stream)))
+
+    def device_status(self, clear=True, stream=None) -> int:
+        v = C.c_uint32()
+        self.check(self.lib.pbmoe_device_status(self.h, self.stream_ptr(stream), C.byref(v), 1 if clear else 0))
+        return v.value
+
+
+def moe_config(layout: ExpertLayout, num_experts, top_k, normalization=0, routed_scale=1.0, eps=1e-6) -> MoeConfig:
+    return MoeConfig(layout, num_experts, top_k, normalization, routed_scale, eps)

@@ -1,0 +1,400 @@
+// capi.cu — the extern "C" boundary (include/pbmoe_cuda.h): context, argument
+// validation, workspace ownership and launches. Every entry point validates
+// geometry on the host first and never falls back to a CPU path.
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "kernels.h"
+#include "q4_rows.cuh"
+
+struct pbmoe_ctx {
+    int device = 0;
+    uint32_t* status = nullptr;  // device status word
+    void* ws_base = nullptr;     // MoE workspace
+    size_t ws_bytes = 0;
+    uint32_t ws_tokens = 0, ws_E = 0, ws_K = 0, ws_H = 0, ws_I = 0;
+    std::string last_error;
+};
+
+namespace {
+
+int fail(pbmoe_ctx* ctx, int code, const char* fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        ctx->last_error = buf;
+    }
+    return code;
+}
+
+int cuda_fail(pbmoe_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, PBMOE_ERR_CUDA, "FlashMoe CUDA %s failed: %s", what, cudaGetErrorString(e));
+}
+
+// Make `ctx->device` current for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool aligned(const void* p, size_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Validates an expert layout for the MoE fast path. Returns 0 or a status.
+int check_layout(pbmoe_ctx* ctx, const pbmoe_expert_layout& L) {
+    const uint32_t H = L.hidden, I = L.intermediate, G = L.group_size;
+    if (H == 0 || I == 0 || G == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "expert layout has a zero dimension");
+    if (H % G != 0 || I % G != 0)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
+                    "fixed-Q4 expert dimensions hidden=%u intermediate=%u must be divisible by group_size=%u", H, I,
+                    G);
+    const bool pow2 = G >= 32 && (G & (G - 1)) == 0;
+    if (!pow2 || H % 32 != 0 || I % 32 != 0 || H > 16384 || I > 16384)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported expert geometry on CUDA: needs group_size a power of two >= 32 and "
+                    "hidden, intermediate multiples of 32 up to 16384 (got hidden=%u intermediate=%u group=%u)",
+                    H, I, G);
+    const uint64_t gate_w = uint64_t(I) * H / 2, gate_sb = uint64_t(I) * (H / G) * 2;
+    const uint64_t down_w = uint64_t(H) * I / 2, down_sb = uint64_t(H) * (I / G) * 2;
+    const uint64_t sizes[9] = {gate_w, gate_sb, gate_sb, gate_w, gate_sb, gate_sb, down_w, down_sb, down_sb};
+    for (int i = 0; i < 9; ++i) {
+        const uint64_t o = L.component_offsets[i];
+        if (o + sizes[i] > L.expert_bytes)
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "expert component %d [%llu, +%llu) exceeds slot bytes %llu",
+                        i, (unsigned long long)o, (unsigned long long)sizes[i], (unsigned long long)L.expert_bytes);
+        const uint64_t need = (i % 3 == 0) ? 16 : 2;
+        if (o % need != 0)
+            return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert component %d offset %llu is not %llu-byte aligned", i,
+                        (unsigned long long)o, (unsigned long long)need);
+    }
+    if (L.expert_bytes % 16 != 0)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert slot stride %llu is not a multiple of 16",
+                    (unsigned long long)L.expert_bytes);
+    return PBMOE_OK;
+}
+
+int check_moe_config(pbmoe_ctx* ctx, const pbmoe_moe_config* c) {
+    if (!c) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "null MoE config");
+    int rc = check_layout(ctx, c->layout);
+    if (rc) return rc;
+    if (c->num_experts == 0 || c->num_experts > 4096)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "num_experts %u outside 1..4096", c->num_experts);
+    if (c->top_k == 0 || c->top_k > 32 || c->top_k > c->num_experts)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "top_k %u outside 1..min(32, num_experts)", c->top_k);
+    if (c->normalization > PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported routing weights: normalisation %u is not implemented on CUDA",
+                    c->normalization);
+    if (!(c->routed_scaling_factor > 0.f) || !std::isfinite(c->routed_scaling_factor))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "routed expert scale must be positive and finite");
+    return PBMOE_OK;
+}
+
+}  // namespace
+
+namespace pbmoe {
+
+MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
+    MoeWsSizes s{};
+    const size_t R = size_t(T) * K + T;
+    const size_t gmax = size_t(T) * K + 1;
+    size_t* b = s.bytes;
+    b[0] = 0;                    // status lives in the context
+    b[1] = 4;                    // ticket
+    b[2] = size_t(T) * E * 4;    // logits
+    b[3] = size_t(T) * 4;        // shared_logit
+    b[4] = size_t(T) * K * 4;    // route_ids
+    b[5] = size_t(T) * K * 4;    // route_w
+    b[6] = 4;                    // num_groups
+    b[7] = gmax * 4;             // group_expert
+    b[8] = gmax * 4;             // group_start
+    b[9] = gmax * 4;             // group_count
+    b[10] = R * 4;               // group_routes
+    b[11] = R * 4;               // group_tokens
+    b[12] = R * I * 4;           // h
+    b[13] = R * H * 4;           // y
+    b[14] = size_t(T) * H * 4;   // y_tmp
+    s.total = 0;
+    for (int i = 0; i < 15; ++i) s.total += align_up(b[i], 256);
+    return s;
+}
+
+MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
+    MoeWsSizes s = moe_ws_sizes(T, E, K, H, I);
+    char* p = static_cast<char*>(base);
+    void* ptr[15];
+    for (int i = 0; i < 15; ++i) {
+        ptr[i] = p;
+        p += align_up(s.bytes[i], 256);
+    }
+    MoeWs w;
+    w.status = status;
+    w.ticket = static_cast<uint32_t*>(ptr[1]);
+    w.logits = static_cast<float*>(ptr[2]);
+    w.shared_logit = static_cast<float*>(ptr[3]);
+    w.route_ids = static_cast<uint32_t*>(ptr[4]);
+    w.route_w = static_cast<float*>(ptr[5]);
+    w.num_groups = static_cast<uint32_t*>(ptr[6]);
+    w.group_expert = static_cast<uint32_t*>(ptr[7]);
+    w.group_start = static_cast<uint32_t*>(ptr[8]);
+    w.group_count = static_cast<uint32_t*>(ptr[9]);
+    w.group_routes = static_cast<uint32_t*>(ptr[10]);
+    w.group_tokens = static_cast<uint32_t*>(ptr[11]);
+    w.h = static_cast<float*>(ptr[12]);
+    w.y = static_cast<float*>(ptr[13]);
+    w.y_tmp = static_cast<float*>(ptr[14]);
+    return w;
+}
+
+}  // namespace pbmoe
+
+using namespace pbmoe;
+
+extern "C" {
+
+int pbmoe_abi_version(void) { return PBMOE_ABI_VERSION; }
+
+const char* pbmoe_last_error(const pbmoe_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+int pbmoe_init(int device, pbmoe_ctx** out) {
+    if (!out) return PBMOE_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return PBMOE_ERR_CUDA;
+    auto* ctx = new pbmoe_ctx();
+    ctx->device = device;
+    DeviceGuard g(device);
+    if (!g.ok) {
+        delete ctx;
+        return PBMOE_ERR_CUDA;
+    }
+    if (cudaMalloc(&ctx->status, sizeof(uint32_t)) != cudaSuccess) {
+        delete ctx;
+        return PBMOE_ERR_CUDA;
+    }
+    if (cudaMemset(ctx->status, 0, sizeof(uint32_t)) != cudaSuccess) {
+        cudaFree(ctx->status);
+        delete ctx;
+        return PBMOE_ERR_CUDA;
+    }
+    *out = ctx;
+    return PBMOE_OK;
+}
+
+int pbmoe_destroy(pbmoe_ctx* ctx) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    {
+        DeviceGuard g(ctx->device);
+        if (ctx->ws_base) cudaFree(ctx->ws_base);
+        if (ctx->status) cudaFree(ctx->status);
+    }
+    delete ctx;
+    return PBMOE_OK;
+}
+
+int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group, pbmoe_expert_layout* out) {
+    if (!out || hidden == 0 || intermediate == 0 || group == 0 || hidden % group || intermediate % group)
+        return PBMOE_ERR_INVALID_ARGUMENT;
+    const uint64_t gw = uint64_t(intermediate) * hidden / 2, gsb = uint64_t(intermediate) * (hidden / group) * 2;
+    const uint64_t dw = uint64_t(hidden) * intermediate / 2, dsb = uint64_t(hidden) * (intermediate / group) * 2;
+    const uint64_t sizes[9] = {gw, gsb, gsb, gw, gsb, gsb, dw, dsb, dsb};
+    uint64_t off = 0;
+    for (int i = 0; i < 9; ++i) {
+        out->component_offsets[i] = off;
+        off += sizes[i];
+    }
+    out->expert_bytes = off;
+    out->hidden = hidden;
+    out->intermediate = intermediate;
+    out->group_size = group;
+    return PBMOE_OK;
+}
+
+size_t pbmoe_moe_workspace_bytes(uint32_t max_tokens, const pbmoe_moe_config* c) {
+    if (!c || max_tokens == 0) return 0;
+    return moe_ws_sizes(max_tokens, c->num_experts, c->top_k, c->layout.hidden, c->layout.intermediate).total;
+}
+
+int pbmoe_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, const pbmoe_moe_config* c) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    int rc = check_moe_config(ctx, c);
+    if (rc) return rc;
+    if (max_tokens == 0 || max_tokens > 4096)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "max_tokens %u outside 1..4096", max_tokens);
+    const uint32_t E = c->num_experts, K = c->top_k, H = c->layout.hidden, I = c->layout.intermediate;
+    if (moe_router_smem(max_tokens, H, E, K) > 200 * 1024)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "router staging for %u tokens exceeds shared memory", max_tokens);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    const size_t need = moe_ws_sizes(max_tokens, E, K, H, I).total;
+    if (ctx->ws_base && ctx->ws_bytes >= need && ctx->ws_E == E && ctx->ws_K == K && ctx->ws_H == H &&
+        ctx->ws_I == I && ctx->ws_tokens >= max_tokens)
+        return PBMOE_OK;
+    if (ctx->ws_base) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before workspace resize");
+        cudaFree(ctx->ws_base);
+        ctx->ws_base = nullptr;
+        ctx->ws_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->ws_base, need);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "workspace allocation");
+    e = cudaMemset(ctx->ws_base, 0, need);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "workspace clear");
+    ctx->ws_bytes = need;
+    ctx->ws_tokens = max_tokens;
+    ctx->ws_E = E;
+    ctx->ws_K = K;
+    ctx->ws_H = H;
+    ctx->ws_I = I;
+    return PBMOE_OK;
+}
+
+int pbmoe_device_status(pbmoe_ctx* ctx, void* stream, uint32_t* out, int clear) {
+    if (!ctx || !out) return PBMOE_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(out, ctx->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "status read-back");
+    if (clear) {
+        e = cudaMemsetAsync(ctx->status, 0, sizeof(uint32_t), s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "status clear");
+    }
+    return PBMOE_OK;
+}
+
+int pbmoe_q4_matvec(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype, void* y,
+                    pbmoe_dtype y_dtype, uint32_t batch, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!w || !w->packed || !w->scales || !w->biases || !x || !y)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec: null pointer");
+    if (w->group_size == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "group_size must be positive");
+    if (w->rows == 0 || w->cols == 0 || batch == 0) return PBMOE_OK;
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (!aligned(x, x_dtype == PBMOE_F32 ? 4 : 2) || !aligned(y, y_dtype == PBMOE_F32 ? 4 : 2) ||
+        !aligned(w->scales, 2) || !aligned(w->biases, 2))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec: misaligned pointer");
+    DeviceGuard g(ctx->device);
+    Q4MatvecArgs a{static_cast<const uint8_t*>(w->packed), w->scales, w->biases, w->rows, w->cols, w->group_size,
+                   x, x_dtype, y, y_dtype, batch};
+    cudaError_t e = q4_matvec_launch(a, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorNotSupported)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported q4 matvec: cols=%u needs too much shared memory",
+                    w->cols);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 matvec launch");
+    return PBMOE_OK;
+}
+
+int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint32_t E, uint32_t K,
+                     uint32_t normalization, float routed_scale, uint32_t* ids, float* weights, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!logits || !ids || !weights) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "route top-k: null pointer");
+    if (E == 0 || K == 0 || K > 32 || K > E)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "route top-k: K=%u over E=%u outside 1..min(32, E)", K, E);
+    if (normalization > PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported routing weights: normalisation %u is not implemented on CUDA", normalization);
+    if (!(routed_scale > 0.f) || !std::isfinite(routed_scale))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "routed expert scale must be positive and finite");
+    if (tokens == 0) return PBMOE_OK;
+    DeviceGuard g(ctx->device);
+    cudaError_t e = route_topk_launch(logits, tokens, E, K, normalization, routed_scale, ids, weights, ctx->status,
+                                      static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "route top-k launch");
+    return PBMOE_OK;
+}
+
+int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w, const void* x,
+                    pbmoe_dtype x_dtype, const void* residual, void* out, pbmoe_dtype out_dtype, uint32_t tokens,
+                    const float* next_norm_weight, void* next_normed, const pbmoe_moe_debug* debug, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    int rc = check_moe_config(ctx, c);
+    if (rc) return rc;
+    if (!w || !w->router_weight || !w->experts || !x || !out)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "moe layer: null pointer");
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (out_dtype != PBMOE_F32 && out_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if ((next_norm_weight == nullptr) != (next_normed == nullptr))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "next_norm_weight and next_normed must be given together");
+    if (w->shared_expert_gate && !w->shared_expert)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "shared expert gate given without a shared expert");
+    if (!aligned(w->experts, 16) || (w->shared_expert && !aligned(w->shared_expert, 16)) ||
+        !aligned(w->router_weight, 16) || (w->shared_expert_gate && !aligned(w->shared_expert_gate, 16)))
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert table, shared expert and router weights must be 16-byte aligned");
+    if (tokens == 0) return PBMOE_OK;
+    const uint32_t E = c->num_experts, K = c->top_k, H = c->layout.hidden, I = c->layout.intermediate;
+    if (!ctx->ws_base || tokens > ctx->ws_tokens || ctx->ws_E != E || ctx->ws_K != K || ctx->ws_H != H ||
+        ctx->ws_I != I)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE,
+                    "moe layer: workspace reserved for tokens<=%u E=%u K=%u H=%u I=%u, call needs tokens=%u E=%u K=%u "
+                    "H=%u I=%u (call pbmoe_reserve)",
+                    ctx->ws_tokens, ctx->ws_E, ctx->ws_K, ctx->ws_H, ctx->ws_I, tokens, E, K, H, I);
+    DeviceGuard g(ctx->device);
+    MoeLaunch a{};
+    a.ws = moe_ws_carve(ctx->ws_base, ctx->status, ctx->ws_tokens, E, K, H, I);
+    const pbmoe_expert_layout& L = c->layout;
+    for (int i = 0; i < 9; ++i) a.layout.off[i] = L.component_offsets[i];
+    a.layout.expert_bytes = L.expert_bytes;
+    a.layout.hidden = H;
+    a.layout.inter = I;
+    a.layout.group = L.group_size;
+    a.layout.cpg_shift_h = ilog2_u32(L.group_size / 32);
+    a.layout.cpg_shift_i = ilog2_u32(L.group_size / 32);
+    a.tokens = tokens;
+    a.num_experts = E;
+    a.top_k = K;
+    a.normalization = c->normalization;
+    a.routed_scale = c->routed_scaling_factor;
+    a.eps = c->norm_epsilon;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.residual = residual;
+    a.out = out;
+    a.out_dtype = out_dtype;
+    a.next_norm_w = next_norm_weight;
+    a.next_normed = next_normed;
+    a.router_w = w->router_weight;
+    a.shared_gate = w->shared_expert_gate;
+    a.experts = w->experts;
+    a.shared_slot = w->shared_expert;
+    a.pdl = true;
+    a.phase_events = debug ? debug->phase_events : nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = moe_layer_launch(a, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer launch");
+    if (debug) {
+        if (debug->router_logits)
+            e = cudaMemcpyAsync(debug->router_logits, a.ws.logits, size_t(tokens) * E * 4, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && debug->route_ids)
+            e = cudaMemcpyAsync(debug->route_ids, a.ws.route_ids, size_t(tokens) * K * 4, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && debug->route_weights)
+            e = cudaMemcpyAsync(debug->route_weights, a.ws.route_w, size_t(tokens) * K * 4, cudaMemcpyDeviceToDevice,
+                                s);
+        if (e == cudaSuccess && debug->shared_logit)
+            e = cudaMemcpyAsync(debug->shared_logit, a.ws.shared_logit, size_t(tokens) * 4, cudaMemcpyDeviceToDevice,
+                                s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "moe debug copy");
+    }
+    return PBMOE_OK;
+}
+
+}  // extern "C"

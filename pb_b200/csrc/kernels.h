@@ -1,0 +1,94 @@
+// kernels.h — host-visible launch interfaces between the C-ABI layer
+// (capi.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "pbmoe_cuda.h"
+
+namespace pbmoe {
+
+// Device workspace of one MoE layer launch (carved out of one allocation by
+// capi.cu, sized for the reserved maximum token count). Route index r is
+// t*K + k for routed routes and T*K + t for token t's shared-expert route.
+struct MoeWs {
+    uint32_t* status;        // device status word (PBMOE_DEV_ERR_*)
+    uint32_t* ticket;        // last-CTA counter of the router kernel, kept at 0 between launches
+    float* logits;           // [T x E]
+    float* shared_logit;     // [T]
+    uint32_t* route_ids;     // [T x K]
+    float* route_w;          // [T x K]
+    uint32_t* num_groups;    // [1]
+    uint32_t* group_expert;  // [gmax]  expert id, E = shared expert
+    uint32_t* group_start;   // [gmax]  first grouped position
+    uint32_t* group_count;   // [gmax]
+    uint32_t* group_routes;  // [T*K + T] route index per grouped position
+    uint32_t* group_tokens;  // [T*K + T] token index per grouped position
+    float* h;                // [(T*K + T) x I] SwiGLU activations per route
+    float* y;                // [(T*K + T) x H] expert outputs per route
+    float* y_tmp;            // [T x H] combined hidden (f32) for the next-layer norm
+};
+
+// Expert slot geometry as the kernels use it.
+struct MoeLayoutDev {
+    uint64_t off[9];
+    uint64_t expert_bytes;
+    uint32_t hidden;
+    uint32_t inter;
+    uint32_t group;
+    uint32_t cpg_shift_h;  // log2(group/32) for rows of length hidden
+    uint32_t cpg_shift_i;  // same for rows of length inter
+};
+
+struct MoeLaunch {
+    MoeWs ws;
+    MoeLayoutDev layout;
+    uint32_t tokens, num_experts, top_k, normalization;
+    float routed_scale, eps;
+    const void* x;
+    pbmoe_dtype x_dtype;
+    const void* residual;
+    void* out;
+    pbmoe_dtype out_dtype;
+    const float* next_norm_w;
+    void* next_normed;
+    const uint16_t* router_w;
+    const uint16_t* shared_gate;
+    const uint8_t* experts;
+    const uint8_t* shared_slot;
+    bool pdl;  // launch the router kernel with programmatic dependent launch
+    void* const* phase_events;  // NULL, or 5 cudaEvent_t recorded around the kernels
+};
+
+// Per-launch bytes of each workspace array, in MoeWs order (host arithmetic).
+struct MoeWsSizes {
+    size_t bytes[15];
+    size_t total;
+};
+MoeWsSizes moe_ws_sizes(uint32_t max_tokens, uint32_t E, uint32_t K, uint32_t H, uint32_t I);
+MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t max_tokens, uint32_t E, uint32_t K, uint32_t H,
+                   uint32_t I);
+
+cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s);
+size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K);
+cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
+                              float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s);
+
+struct Q4MatvecArgs {
+    const uint8_t* packed;
+    const uint16_t* scales;
+    const uint16_t* biases;
+    uint32_t rows, cols, group;
+    const void* x;
+    pbmoe_dtype x_dtype;
+    void* y;
+    pbmoe_dtype y_dtype;
+    uint32_t batch;
+};
+// Returns cudaErrorNotSupported when the shape needs more shared memory than
+// a CTA has.
+cudaError_t q4_matvec_launch(const Q4MatvecArgs& a, cudaStream_t s);
+
+}  // namespace pbmoe

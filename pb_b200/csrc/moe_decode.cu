@@ -1,0 +1,512 @@
+// moe_decode.cu — one MoE FFN decode layer on sm_100a, four stream-ordered
+// kernels:
+//
+//   1. moe_router_kernel   router GEMV (bf16 [E x H]) + shared-expert gate
+//                          logit; the last CTA to finish routes every token
+//                          (route_token_warp) and builds the layer-major group
+//                          plan (unique experts in ascending id order, routes
+//                          in route order inside each group, shared expert as
+//                          group 0 with every token).
+//   2. moe_expert_up_kernel   gate and up rows of one group's expert for the
+//                          group's tokens, SwiGLU fused: h = silu(g) * u.
+//   3. moe_expert_down_kernel down rows of the group's expert on h -> y.
+//   4. moe_combine_kernel  out = residual + sum_k w_k y_k + sigma(gate.x) y_shared,
+//                          optional next-layer RMSNorm.
+//
+// Reference counterparts: the router projection and CPU top-k
+// (runtime/mod.rs:1065, math.rs:771-783), the grouping plan
+// (metal/mod.rs:3197-3233), the per-expert CMD3 dispatches
+// (metal/mod.rs:4289-4470: q4 gate :4365, up :4375, silu_product :4389,
+// down :4396), the shared phase (metal/mod.rs:4609-4716) and the combine
+// (shaders.metal:1723-1786) with the next-layer rms_norm_reduced
+// (shaders.metal:1176-1213).
+//
+// Kernels 2-4 are launched with programmatic dependent launch: each waits on
+// griddepcontrol.wait before touching its predecessor's outputs.
+
+#include "kernels.h"
+#include "q4_rows.cuh"
+#include "routing.cuh"
+
+namespace pbmoe {
+
+// ---------------------------------------------------------------- kernel 1
+constexpr int kRouterThreads = 128;
+constexpr int kRouterRowsPerWarp = 1;
+constexpr int kRouterTokPass = 8;
+constexpr int kRouterVec = 8;  // 16-byte weight vectors per lane loaded before use
+
+template <typename XT>
+__global__ void __launch_bounds__(kRouterThreads)
+moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
+                  uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
+                  const uint16_t* __restrict__ shared_gate_w, int has_shared, MoeWs ws) {
+    extern __shared__ __align__(16) float smem[];
+    float* xs = smem;  // [kRouterTokPass][H]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t nrows = E + (shared_gate_w ? 1u : 0u);
+    const uint32_t row0 = (blockIdx.x * (kRouterThreads / 32) + warp) * kRouterRowsPerWarp;
+    const uint32_t vec_per_row = H / 8;  // 16-byte vectors of 8 bf16
+
+    pdl_wait();
+    for (uint32_t t0 = 0; t0 < T; t0 += kRouterTokPass) {
+        const uint32_t nt = min(T - t0, static_cast<uint32_t>(kRouterTokPass));
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < nt * H; i += blockDim.x) {
+            const uint32_t t = i / H, c = i - t * H;
+            xs[t * H + c] = load_act<XT>(x, static_cast<size_t>(t0 + t) * H + c);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int rr = 0; rr < kRouterRowsPerWarp; ++rr) {
+            const uint32_t row = row0 + rr;
+            if (row >= nrows) break;
+            const uint16_t* wrow = row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w;
+            float acc[kRouterTokPass];
+#pragma unroll
+            for (int t = 0; t < kRouterTokPass; ++t) acc[t] = 0.f;
+            for (uint32_t vb = 0; vb < vec_per_row; vb += 32 * kRouterVec) {
+                uint4 w4[kRouterVec];
+#pragma unroll
+                for (int i = 0; i < kRouterVec; ++i) {
+                    const uint32_t v = vb + i * 32 + lane;
+                    w4[i] = v < vec_per_row ? ld_stream_u4(wrow + static_cast<size_t>(v) * 8) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int i = 0; i < kRouterVec; ++i) {
+                    const uint32_t v = vb + i * 32 + lane;
+                    if (v >= vec_per_row) break;
+                    const uint32_t wv[4] = {w4[i].x, w4[i].y, w4[i].z, w4[i].w};
+                    float wf[8];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        wf[2 * q] = __uint_as_float(wv[q] << 16);
+                        wf[2 * q + 1] = __uint_as_float(wv[q] & 0xffff0000u);
+                    }
+#pragma unroll
+                    for (int t = 0; t < kRouterTokPass; ++t) {
+                        if (static_cast<uint32_t>(t) < nt) {
+                            const float4* xp = reinterpret_cast<const float4*>(xs + t * H + v * 8);
+                            const float4 a = xp[0], b = xp[1];
+                            acc[t] = fmaf(wf[0], a.x, acc[t]);
+                            acc[t] = fmaf(wf[1], a.y, acc[t]);
+                            acc[t] = fmaf(wf[2], a.z, acc[t]);
+                            acc[t] = fmaf(wf[3], a.w, acc[t]);
+                            acc[t] = fmaf(wf[4], b.x, acc[t]);
+                            acc[t] = fmaf(wf[5], b.y, acc[t]);
+                            acc[t] = fmaf(wf[6], b.z, acc[t]);
+                            acc[t] = fmaf(wf[7], b.w, acc[t]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < kRouterTokPass; ++t) {
+                if (static_cast<uint32_t>(t) < nt) {
+                    const float s = warp_sum(acc[t]);
+                    if (lane == 0) {
+                        if (row < E)
+                            ws.logits[static_cast<size_t>(t0 + t) * E + row] = s;
+                        else
+                            ws.shared_logit[t0 + t] = s;
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- last CTA: routing + group plan
+    __shared__ uint32_t is_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t prev = atomicAdd(ws.ticket, 1u);
+        is_last = (prev == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+
+    for (uint32_t t = warp; t < T; t += blockDim.x / 32)
+        route_token_warp(ws.logits + static_cast<size_t>(t) * E, E, K, normalization, routed_scale,
+                         ws.route_ids + static_cast<size_t>(t) * K, ws.route_w + static_cast<size_t>(t) * K,
+                         ws.status);
+    __syncthreads();
+
+    // group plan; shared memory reuses the activation staging area
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(smem);  // [E] counts -> starts
+    uint32_t* gidx = cnt + E;                           // [E] used flags -> group index
+    uint32_t* ids = gidx + E;                           // [T*K]
+    uint32_t* tmp = ids + T * K;                        // [32]
+    const uint32_t R = T * K;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
+        const uint32_t e = __ldcg(ws.route_ids + r);
+        ids[r] = e;
+        atomicAdd(&cnt[e], 1u);
+    }
+    __syncthreads();
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) gidx[e] = cnt[e] ? 1u : 0u;
+    __syncthreads();
+    const uint32_t U = block_exclusive_scan(gidx, E, tmp);
+    block_exclusive_scan(cnt, E, tmp);  // cnt[e] = start of expert e among routed positions
+    const uint32_t shared_groups = has_shared ? 1u : 0u;
+    const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared group
+    for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
+        const uint32_t e = ids[r];
+        uint32_t rank = 0;
+        for (uint32_t q = 0; q < r; ++q) rank += (ids[q] == e) ? 1u : 0u;
+        const uint32_t pos = routed_base + cnt[e] + rank;
+        ws.group_routes[pos] = r;
+        ws.group_tokens[pos] = r / K;
+        if (rank == 0) {
+            // exclusive-scan property: the group's size is the next start minus this one
+            const uint32_t g = shared_groups + gidx[e];
+            ws.group_expert[g] = e;
+            ws.group_start[g] = routed_base + cnt[e];
+            ws.group_count[g] = (e + 1 < E ? cnt[e + 1] : R) - cnt[e];
+        }
+    }
+    if (has_shared) {
+        for (uint32_t t = threadIdx.x; t < T; t += blockDim.x) {
+            ws.group_routes[t] = R + t;
+            ws.group_tokens[t] = t;
+        }
+        if (threadIdx.x == 0) {
+            ws.group_expert[0] = E;
+            ws.group_start[0] = 0;
+            ws.group_count[0] = T;
+        }
+    }
+    if (threadIdx.x == 0) {
+        *ws.num_groups = U + shared_groups;
+        *ws.ticket = 0;  // ready for the next launch
+    }
+}
+
+// ---------------------------------------------------------------- kernel 2
+constexpr int kUpThreads = 128;
+constexpr int kUpRowsPerWarp = 4;  // intermediate indices per warp (gate+up = 8 rows)
+constexpr int kUpRowsPerCta = kUpRowsPerWarp * (kUpThreads / 32);
+
+template <typename XT, int NT>
+__global__ void __launch_bounds__(kUpThreads)
+moe_expert_up_kernel(const XT* __restrict__ x, uint32_t E, const uint8_t* __restrict__ experts,
+                     const uint8_t* __restrict__ shared_slot, MoeLayoutDev L, MoeWs ws) {
+    extern __shared__ __align__(16) float smem[];
+    const uint32_t g = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    pdl_wait();
+    if (g >= *ws.num_groups) return;
+    const uint32_t e = ws.group_expert[g];
+    const uint32_t start = ws.group_start[g], n = ws.group_count[g];
+    const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * L.expert_bytes;
+    const uint32_t H = L.hidden, I = L.inter;
+    const uint32_t chunks = H >> 5;
+    float* xs = smem;
+    float* xe = xs + NT * H;
+    float* xo = xe + NT * chunks;
+
+    const Q4Geom geom{I, H, (H + L.group - 1) / L.group, chunks, L.cpg_shift_h};
+    const uint32_t i0 = blockIdx.x * kUpRowsPerCta + warp * kUpRowsPerWarp;
+    const uint8_t* pk[2 * kUpRowsPerWarp];
+    const uint16_t* ps[2 * kUpRowsPerWarp];
+    const uint16_t* pb[2 * kUpRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kUpRowsPerWarp; ++r) {
+        const uint32_t i = i0 + r;
+        const bool ok = i < I;
+        const size_t prow = static_cast<size_t>(i) * (H / 2);
+        const size_t srow = static_cast<size_t>(i) * geom.gpr;
+        pk[r] = ok ? slot + L.off[0] + prow : nullptr;
+        ps[r] = reinterpret_cast<const uint16_t*>(slot + L.off[1]) + srow;
+        pb[r] = reinterpret_cast<const uint16_t*>(slot + L.off[2]) + srow;
+        pk[kUpRowsPerWarp + r] = ok ? slot + L.off[3] + prow : nullptr;
+        ps[kUpRowsPerWarp + r] = reinterpret_cast<const uint16_t*>(slot + L.off[4]) + srow;
+        pb[kUpRowsPerWarp + r] = reinterpret_cast<const uint16_t*>(slot + L.off[5]) + srow;
+    }
+    for (uint32_t p0 = 0; p0 < n; p0 += NT) {
+        const int nt = static_cast<int>(min(n - p0, static_cast<uint32_t>(NT)));
+        __syncthreads();
+        stage_x_fast<XT>(x, H, ws.group_tokens + start + p0, nt, H, xs, xe, xo);
+        __syncthreads();
+        float acc[2 * kUpRowsPerWarp][NT];
+        q4_rows_partial<32, 2 * kUpRowsPerWarp, 2, NT>(pk, ps, pb, geom, xs, xe, xo, nt, acc);
+#pragma unroll
+        for (int r = 0; r < kUpRowsPerWarp; ++r) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float gs = warp_sum(acc[r][t]);
+                const float us = warp_sum(acc[kUpRowsPerWarp + r][t]);
+                if (lane == 0 && t < nt && i0 + r < I) {
+                    const uint32_t route = ws.group_routes[start + p0 + t];
+                    ws.h[static_cast<size_t>(route) * I + i0 + r] = gs / (1.0f + expf(-gs)) * us;
+                }
+            }
+        }
+    }
+    pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------- kernel 3
+constexpr int kDownThreads = 128;
+constexpr int kDownRowsPerGroup = 8;  // rows per lane group
+
+template <int LPR, int NT>
+__global__ void __launch_bounds__(kDownThreads)
+moe_expert_down_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint8_t* __restrict__ shared_slot,
+                       MoeLayoutDev L, MoeWs ws) {
+    extern __shared__ __align__(16) float smem[];
+    constexpr int kGroups = 32 / LPR;
+    constexpr int kRowsPerCta = kDownRowsPerGroup * kGroups * (kDownThreads / 32);
+    const uint32_t g = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int sub = lane / LPR;
+    const uint32_t H = L.hidden, I = L.inter;
+    const uint32_t chunks = I >> 5;
+    const Q4Geom geom{H, I, (I + L.group - 1) / L.group, chunks, L.cpg_shift_i};
+
+    // The group plan was written by the router kernel, which completed before
+    // the up kernel could start; weights do not depend on the up kernel.
+    const uint32_t ng = *ws.num_groups;
+    if (g >= ng) {
+        pdl_wait();
+        return;
+    }
+    const uint32_t e = ws.group_expert[g];
+    const uint32_t start = ws.group_start[g], n = ws.group_count[g];
+    const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * L.expert_bytes;
+    float* xs = smem;
+    float* xe = xs + NT * I;
+    float* xo = xe + NT * chunks;
+    const uint32_t r0 = blockIdx.x * kRowsPerCta + (warp * kGroups + sub) * kDownRowsPerGroup;
+    const uint8_t* pk[kDownRowsPerGroup];
+    const uint16_t* ps[kDownRowsPerGroup];
+    const uint16_t* pb[kDownRowsPerGroup];
+#pragma unroll
+    for (int r = 0; r < kDownRowsPerGroup; ++r) {
+        const uint32_t row = r0 + r;
+        pk[r] = row < H ? slot + L.off[6] + static_cast<size_t>(row) * (I / 2) : nullptr;
+        ps[r] = reinterpret_cast<const uint16_t*>(slot + L.off[7]) + static_cast<size_t>(row) * geom.gpr;
+        pb[r] = reinterpret_cast<const uint16_t*>(slot + L.off[8]) + static_cast<size_t>(row) * geom.gpr;
+    }
+    pdl_wait();
+    for (uint32_t p0 = 0; p0 < n; p0 += NT) {
+        const int nt = static_cast<int>(min(n - p0, static_cast<uint32_t>(NT)));
+        __syncthreads();
+        stage_x_fast<float>(ws.h, I, ws.group_routes + start + p0, nt, I, xs, xe, xo);
+        __syncthreads();
+        float acc[kDownRowsPerGroup][NT];
+        q4_rows_partial<LPR, kDownRowsPerGroup, 1, NT>(pk, ps, pb, geom, xs, xe, xo, nt, acc);
+#pragma unroll
+        for (int r = 0; r < kDownRowsPerGroup; ++r) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float s = group_sum<LPR>(acc[r][t]);
+                if ((lane & (LPR - 1)) == 0 && t < nt && r0 + r < H) {
+                    const uint32_t route = ws.group_routes[start + p0 + t];
+                    ws.y[static_cast<size_t>(route) * H + r0 + r] = s;
+                }
+            }
+        }
+    }
+    pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------- kernel 4
+constexpr int kCombineThreads = 256;
+
+template <typename OT>
+__global__ void __launch_bounds__(kCombineThreads)
+moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_gate, const OT* __restrict__ residual,
+                   OT* __restrict__ out, const float* __restrict__ norm_w, OT* __restrict__ next_normed, float eps,
+                   MoeWs ws) {
+    __shared__ float red[32];
+    const uint32_t t = blockIdx.x;
+    pdl_wait();
+    float sw = 0.f;
+    if (has_shared) sw = has_gate ? 1.0f / (1.0f + expf(-ws.shared_logit[t])) : 1.0f;
+    const float* wk = ws.route_w + static_cast<size_t>(t) * K;
+    float ss = 0.f;
+    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+        float moe = 0.f;
+        for (uint32_t k = 0; k < K; ++k) moe += wk[k] * ws.y[(static_cast<size_t>(t) * K + k) * H + c];
+        const float sh = has_shared ? ws.y[(static_cast<size_t>(T) * K + t) * H + c] : 0.f;
+        const float r = residual ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
+        const float v = r + moe + sw * sh;
+        store_act<OT>(out, static_cast<size_t>(t) * H + c, v);
+        ss += v * v;
+        if (norm_w) ws.y_tmp[static_cast<size_t>(t) * H + c] = v;
+    }
+    if (!norm_w) return;
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(red[0] / static_cast<float>(H) + eps);
+    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+        const float v = ws.y_tmp[static_cast<size_t>(t) * H + c];
+        store_act<OT>(next_normed, static_cast<size_t>(t) * H + c, v * scale * norm_w[c]);
+    }
+}
+
+// ---------------------------------------------------------------- routing only
+__global__ void route_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E, uint32_t K,
+                                  uint32_t normalization, float routed_scale, uint32_t* ids, float* w,
+                                  uint32_t* status) {
+    const uint32_t t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    route_token_warp(logits + static_cast<size_t>(t) * E, E, K, normalization, routed_scale,
+                     ids + static_cast<size_t>(t) * K, w + static_cast<size_t>(t) * K, status);
+}
+
+// ---------------------------------------------------------------- host side
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args,
+                              bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K) {
+    const size_t stage = static_cast<size_t>(kRouterTokPass) * H * sizeof(float);
+    const size_t plan = (2ull * E + static_cast<size_t>(T) * K + 32) * sizeof(uint32_t);
+    return stage > plan ? stage : plan;
+}
+
+template <typename F>
+static cudaError_t set_smem(F* fn, size_t bytes) {
+    return cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(bytes));
+}
+
+template <typename XT, typename OT>
+static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
+    cudaError_t err;
+    const uint32_t T = a.tokens, H = a.layout.hidden, I = a.layout.inter, E = a.num_experts, K = a.top_k;
+    const int has_shared = a.shared_slot != nullptr;
+    const int has_gate = a.shared_gate != nullptr;
+    MoeWs ws = a.ws;
+    auto mark = [&](int i) -> cudaError_t {
+        return a.phase_events ? cudaEventRecord(static_cast<cudaEvent_t>(a.phase_events[i]), s) : cudaSuccess;
+    };
+    const bool pdl = a.phase_events == nullptr;
+    if ((err = mark(0)) != cudaSuccess) return err;
+    // 1. router + routing + plan
+    {
+        const uint32_t nrows = E + (has_gate ? 1u : 0u);
+        const uint32_t rows_per_cta = (kRouterThreads / 32) * kRouterRowsPerWarp;
+        dim3 grid((nrows + rows_per_cta - 1) / rows_per_cta);
+        const size_t smem = moe_router_smem(T, H, E, K);
+        auto fn = moe_router_kernel<XT>;
+        if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
+        const XT* x = static_cast<const XT*>(a.x);
+        uint32_t norm = a.normalization;
+        float scale = a.routed_scale;
+        const uint16_t* rw = a.router_w;
+        const uint16_t* sg = a.shared_gate;
+        void* args[] = {(void*)&x, (void*)&T, (void*)&H, (void*)&E, (void*)&K, (void*)&norm, (void*)&scale,
+                        (void*)&rw, (void*)&sg, (void*)&has_shared, (void*)&ws};
+        if ((err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRouterThreads), smem, s, args,
+                              a.pdl && pdl)) != cudaSuccess)
+            return err;
+    }
+    if ((err = mark(1)) != cudaSuccess) return err;
+    const uint32_t gmax = (T * K < E ? T * K : E) + (has_shared ? 1u : 0u);
+    MoeLayoutDev L = a.layout;
+    const uint8_t* experts = a.experts;
+    const uint8_t* shared = a.shared_slot;
+    // 2. gate/up/SwiGLU
+    {
+        const uint32_t chunks = H >> 5;
+        dim3 grid((I + kUpRowsPerCta - 1) / kUpRowsPerCta, gmax);
+        const XT* x = static_cast<const XT*>(a.x);
+        void* args[] = {(void*)&x, (void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
+        if (T == 1) {
+            const size_t smem = (1ull * H + 2ull * chunks) * sizeof(float);
+            auto fn = moe_expert_up_kernel<XT, 1>;
+            if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
+            err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
+        } else {
+            const size_t smem = 4ull * (H + 2ull * chunks) * sizeof(float);
+            auto fn = moe_expert_up_kernel<XT, 4>;
+            if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
+            err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
+        }
+        if (err != cudaSuccess) return err;
+    }
+    if ((err = mark(2)) != cudaSuccess) return err;
+    // 3. down
+    {
+        const uint32_t chunks = I >> 5;
+        void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
+        const int lpr = chunks >= 32 ? 32 : (chunks >= 16 ? 16 : 8);
+        const int groups = 32 / lpr;
+        const uint32_t rows_per_cta = kDownRowsPerGroup * groups * (kDownThreads / 32);
+        dim3 grid((H + rows_per_cta - 1) / rows_per_cta, gmax);
+        const int nt = T == 1 ? 1 : 4;
+        const size_t smem = static_cast<size_t>(nt) * (I + 2ull * chunks) * sizeof(float);
+        const void* fn = nullptr;
+        if (lpr == 32)
+            fn = nt == 1 ? reinterpret_cast<const void*>(moe_expert_down_kernel<32, 1>)
+                         : reinterpret_cast<const void*>(moe_expert_down_kernel<32, 4>);
+        else if (lpr == 16)
+            fn = nt == 1 ? reinterpret_cast<const void*>(moe_expert_down_kernel<16, 1>)
+                         : reinterpret_cast<const void*>(moe_expert_down_kernel<16, 4>);
+        else
+            fn = nt == 1 ? reinterpret_cast<const void*>(moe_expert_down_kernel<8, 1>)
+                         : reinterpret_cast<const void*>(moe_expert_down_kernel<8, 4>);
+        if ((err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) !=
+            cudaSuccess)
+            return err;
+        if ((err = launch_pdl(fn, grid, dim3(kDownThreads), smem, s, args, pdl)) != cudaSuccess) return err;
+    }
+    if ((err = mark(3)) != cudaSuccess) return err;
+    // 4. combine (+ next-layer norm)
+    {
+        const OT* res = static_cast<const OT*>(a.residual);
+        OT* out = static_cast<OT*>(a.out);
+        OT* nn = static_cast<OT*>(a.next_normed);
+        const float* nw = a.next_norm_w;
+        float eps = a.eps;
+        void* args[] = {(void*)&T, (void*)&H, (void*)&K, (void*)&has_shared, (void*)&has_gate, (void*)&res,
+                        (void*)&out, (void*)&nw, (void*)&nn, (void*)&eps, (void*)&ws};
+        auto fn = moe_combine_kernel<OT>;
+        if ((err = launch_pdl(reinterpret_cast<const void*>(fn), dim3(T), dim3(kCombineThreads), 0, s, args,
+                              pdl)) != cudaSuccess)
+            return err;
+    }
+    return mark(4);
+}
+
+cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s) {
+    if (a.x_dtype == PBMOE_BF16) {
+        return a.out_dtype == PBMOE_BF16 ? moe_layer_launch_t<uint16_t, uint16_t>(a, s)
+                                         : moe_layer_launch_t<uint16_t, float>(a, s);
+    }
+    return a.out_dtype == PBMOE_BF16 ? moe_layer_launch_t<float, uint16_t>(a, s) : moe_layer_launch_t<float, float>(a, s);
+}
+
+cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
+                              float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s) {
+    const int warps = 4;
+    route_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>(logits, T, E, K, normalization, routed_scale,
+                                                                       ids, w, status);
+    return cudaGetLastError();
+}
+
+}  // namespace pbmoe

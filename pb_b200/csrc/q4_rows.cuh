@@ -1,0 +1,159 @@
+// q4_rows.cuh — warp-level Q4 row-dot building blocks shared by the decode
+// kernels (pbmoe_q4_matvec, the MoE expert kernels).
+#pragma once
+
+#include "common.cuh"
+
+namespace pbmoe {
+
+// Geometry of one Q4 matrix as the fast path sees it.
+struct Q4Geom {
+    uint32_t rows;
+    uint32_t cols;
+    uint32_t gpr;        // groups per row = ceil(cols / group)
+    uint32_t chunks;     // cols / 32
+    uint32_t cpg_shift;  // log2(group / 32): chunk j lives in group j >> cpg_shift
+};
+
+// Fast path: cols % 32 == 0, group a power of two >= 32, packed rows 16-byte
+// aligned (cols/2 % 16 == 0 and a 16-byte aligned base).
+__host__ __device__ inline bool q4_fast_ok(uint32_t cols, uint32_t group, const void* packed) {
+    bool pow2 = group >= 32 && (group & (group - 1)) == 0;
+    return cols % 32 == 0 && pow2 && (reinterpret_cast<uintptr_t>(packed) % 16 == 0);
+}
+
+__host__ __device__ inline uint32_t ilog2_u32(uint32_t v) {
+    uint32_t r = 0;
+    while (v > 1) {
+        v >>= 1;
+        ++r;
+    }
+    return r;
+}
+
+// Stage `ntok` activation rows (row stride `x_stride` elements) into shared
+// memory as f32, plus each 32-column chunk's even/odd sums. Layout per token:
+// xs[t * cols + xs_index(j, c)], xe[t * chunks + j], xo[t * chunks + j].
+// Needs cols % 32 == 0.
+// `rows_idx` maps local token t to the source row (NULL = identity).
+template <typename XT>
+__device__ void stage_x_fast(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx,
+                             int ntok, uint32_t cols, float* xs, float* xe, float* xo) {
+    const uint32_t chunks = cols >> 5;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    for (int t = 0; t < ntok; ++t) {
+        const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
+        const XT* xr = x + src * x_stride;
+        for (uint32_t j = warp; j < chunks; j += nwarps) {
+            float v = load_act<XT>(xr, (static_cast<size_t>(j) << 5) + lane);
+            xs[static_cast<size_t>(t) * cols + xs_index(j, lane)] = v;
+            float e = (lane & 1) ? 0.f : v;
+            float o = (lane & 1) ? v : 0.f;
+            e = warp_sum(e);
+            o = warp_sum(o);
+            if (lane == 0) {
+                xe[t * chunks + j] = e;
+                xo[t * chunks + j] = o;
+            }
+        }
+    }
+}
+
+// Generic staging (any cols): f32 copy only.
+template <typename XT>
+__device__ void stage_x_generic(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx,
+                                int ntok, uint32_t cols, float* xs) {
+    for (int t = 0; t < ntok; ++t) {
+        const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
+        for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x)
+            xs[static_cast<size_t>(t) * cols + c] = load_act<XT>(x, src * x_stride + c);
+    }
+}
+
+// Fast-path partial dot products of NR rows with NT staged tokens.
+//
+// The warp is split into 32/LPR lane groups; a lane group owns one row at a
+// time and its LPR lanes stride over the row's 16-byte chunks (chunk j goes to
+// lane j % LPR), so every warp-wide load instruction reads 16*32 contiguous
+// bytes per row group. All NR rows' first CPL chunks are loaded before any
+// arithmetic so that NR*CPL*16 bytes per lane are in flight.
+//
+// row_packed[r] / row_scale[r] / row_bias[r] are this lane group's row r
+// (NULL = absent row, contributes 0). acc[r][t] receives the lane's partial
+// sum_c (q*s+b)*x_t[c]; reduce across the LPR lanes afterwards.
+template <int LPR, int NR, int CPL, int NT>
+__device__ __forceinline__ void q4_rows_partial(const uint8_t* const (&row_packed)[NR],
+                                                const uint16_t* const (&row_scale)[NR],
+                                                const uint16_t* const (&row_bias)[NR], const Q4Geom& g,
+                                                const float* xs, const float* xe, const float* xo,
+                                                int ntok, float (&acc)[NR][NT]) {
+    const int li = threadIdx.x & (LPR - 1);
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+
+    for (uint32_t jb = 0; jb < g.chunks; jb += LPR * CPL) {
+        uint4 w[NR][CPL];
+        float sc[NR][CPL], bi[NR][CPL];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) {
+                const uint32_t j = jb + c * LPR + li;
+                if (row_packed[r] != nullptr && j < g.chunks) {
+                    w[r][c] = ld_stream_u4(row_packed[r] + (static_cast<size_t>(j) << 4));
+                    const uint32_t gi = j >> g.cpg_shift;
+                    sc[r][c] = bf16_bits_to_f32(ld_nc_u16(row_scale[r] + gi));
+                    bi[r][c] = bf16_bits_to_f32(ld_nc_u16(row_bias[r] + gi));
+                } else {
+                    w[r][c] = make_uint4(0, 0, 0, 0);
+                    sc[r][c] = 0.f;
+                    bi[r][c] = 0.f;
+                }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const uint32_t j = jb + c * LPR + li;
+            if (j >= g.chunks) continue;
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                ChunkF f;
+                decode_chunk(w[r][c], f);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t < ntok) {
+                        const float e = xe[t * g.chunks + j];
+                        const float o = xo[t * g.chunks + j];
+                        const float qd =
+                            chunk_qdot(f, xs + static_cast<size_t>(t) * g.cols + (j << 5), j & 7u, e, o);
+                        acc[r][t] = fmaf(sc[r][c], qd, fmaf(bi[r][c], e + o, acc[r][t]));
+                    }
+                }
+            }
+        }
+    }
+}
+
+// Generic partial dot of one row (any cols / group): lanes stride over
+// columns and accumulate fma(q, s*x, b*x) as math.rs:861-911 does per element.
+__device__ __forceinline__ float q4_row_partial_generic(const uint8_t* packed_row, const uint16_t* s_row,
+                                                        const uint16_t* b_row, uint32_t cols, uint32_t group,
+                                                        const float* xs, int lane, int nl) {
+    float acc = 0.f;
+    for (uint32_t c = lane; c < cols; c += nl) {
+        const uint8_t byte = packed_row[c >> 1];
+        const float q = static_cast<float>((c & 1) ? (byte >> 4) : (byte & 0x0f));
+        const uint32_t gi = c / group;
+        const float s = bf16_bits_to_f32(s_row[gi]);
+        const float b = bf16_bits_to_f32(b_row[gi]);
+        const float x = xs[c];
+        acc += fmaf(q, s * x, b * x);
+    }
+    return acc;
+}
+
+}  // namespace pbmoe

@@ -1,0 +1,155 @@
+// routing.cuh — on-device routing softmax/top-K with the reference's exact
+// selection semantics, and the layer-major group plan.
+#pragma once
+
+#include "common.cuh"
+
+namespace pbmoe {
+
+// Order-preserving map of a non-NaN float to u32 (IEEE order; -0.0 and +0.0
+// map to the same key because they compare equal in the reference's `<`).
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) == 0) u = 0;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr uint32_t kMaxTopK = 32;
+
+// One warp routes one token.
+//
+// Selection reproduces routing_top_k_iter (math.rs:746-765) exactly: K slots
+// start as (expert 0, -inf); experts are visited in index order and an expert
+// replaces the FIRST slot holding the minimum value when its score is strictly
+// greater. Slots live in lanes 0..K-1. Experts are examined 32 at a time; only
+// lanes whose score beats the current minimum are candidates, and candidates
+// are replayed one by one in ascending expert order, recomputing the minimum
+// slot (lowest slot index on ties) before each, so the final slot contents and
+// order equal the sequential algorithm's. Experts that could not have been
+// inserted (score <= current minimum) are skipped, which the sequential
+// algorithm would also have done.
+//
+// Weights follow routing_softmax_top_k (math.rs:771-783): p_k = exp(s_k - max)
+// * (1/sum_e exp(s_e - max)); then the configured normalisation over the K
+// selected p_k (summed in slot order, scheduler/expert_access.rs:80-133) and
+// the routed scaling factor. Invalid sums latch PBMOE_DEV_ERR_ROUTE_WEIGHTS
+// (where the reference bails) and write zero weights.
+__device__ void route_token_warp(const float* __restrict__ logits, uint32_t E, uint32_t K,
+                                 uint32_t normalization, float routed_scale, uint32_t* ids_out,
+                                 float* w_out, uint32_t* status) {
+    const int lane = threadIdx.x & 31;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+
+    // max and sum of exp over all experts
+    float m = NEG_INF;
+    for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, __ldcg(logits + e));
+    m = warp_max(m);
+    float sum = 0.f;
+    for (uint32_t e = lane; e < E; e += 32) sum += expf(__ldcg(logits + e) - m);
+    sum = warp_sum(sum);
+
+    float sval = NEG_INF;
+    uint32_t sid = 0;
+    const bool is_slot = static_cast<uint32_t>(lane) < K;
+    for (uint32_t base = 0; base < E; base += 32) {
+        const uint32_t e = base + lane;
+        const float v = e < E ? __ldcg(logits + e) : NEG_INF;
+        // current minimum slot value (lower bound for pruning)
+        uint32_t key = is_slot ? float_order_key(sval) : 0xffffffffu;
+        uint32_t mk = __reduce_min_sync(kFull, key);
+        int mslot = __ffs(__ballot_sync(kFull, key == mk)) - 1;
+        float mv = __shfl_sync(kFull, sval, mslot);
+        uint32_t cand = __ballot_sync(kFull, v > mv);
+        while (cand) {
+            const int src = __ffs(cand) - 1;
+            const float ve = __shfl_sync(kFull, v, src);
+            cand &= cand - 1;
+            if (ve > mv) {  // warp-uniform: mv is the exact current minimum
+                if (lane == mslot) {
+                    sval = ve;
+                    sid = base + static_cast<uint32_t>(src);
+                }
+                key = is_slot ? float_order_key(sval) : 0xffffffffu;
+                mk = __reduce_min_sync(kFull, key);
+                mslot = __ffs(__ballot_sync(kFull, key == mk)) - 1;
+                mv = __shfl_sync(kFull, sval, mslot);
+                cand &= __ballot_sync(kFull, v > mv);
+            }
+        }
+    }
+
+    // softmax probability of each selected slot
+    const bool have_inverse = sum > 0.f && isfinite(sum);
+    const float inverse_sum = have_inverse ? 1.0f / sum : 0.f;
+    float p = 0.f;
+    if (is_slot) {
+        p = expf(sval - m);
+        if (have_inverse) p *= inverse_sum;
+    }
+    // normalisation over the K selected, summed in slot order
+    float ssum = 0.f;
+    for (uint32_t k = 0; k < K; ++k) ssum += __shfl_sync(kFull, p, k);
+    bool ok;
+    float inv;
+    if (normalization == PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR) {
+        const float floor_v = 6.103515625e-5f;
+        ok = isfinite(ssum) && ssum >= 0.f;
+        inv = 1.0f / fmaxf(ssum, floor_v);
+    } else {
+        ok = isfinite(ssum) && ssum > 0.f;
+        inv = 1.0f / ssum;
+    }
+    float w = p * inv;
+    ok = ok && __all_sync(kFull, !is_slot || p >= 0.f);
+    w *= routed_scale;
+    if (!ok) {
+        w = 0.f;
+        if (lane == 0) latch_status(status, PBMOE_DEV_ERR_ROUTE_WEIGHTS);
+    }
+    if (is_slot) {
+        ids_out[lane] = sid;
+        w_out[lane] = w;
+    }
+}
+
+// Block-wide exclusive scan of n <= 4096 u32 values in shared memory, in
+// place; returns the total. Uses `tmp` (>= 32 words of shared memory).
+__device__ uint32_t block_exclusive_scan(uint32_t* a, uint32_t n, uint32_t* tmp) {
+    const uint32_t tid = threadIdx.x, nt = blockDim.x;
+    const uint32_t per = (n + nt - 1) / nt;
+    const uint32_t lo = tid * per, hi = min(lo + per, n);
+    uint32_t local = 0;
+    for (uint32_t i = lo; i < hi; ++i) local += a[i];
+    // warp inclusive scan of local
+    const int lane = tid & 31, warp = tid >> 5;
+    uint32_t incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) tmp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t nw = nt >> 5;
+        uint32_t v = lane < static_cast<int>(nw) ? tmp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t u = __shfl_up_sync(kFull, v, o);
+            if (lane >= o) v += u;
+        }
+        if (lane < static_cast<int>(nw)) tmp[lane] = v;  // inclusive per warp
+    }
+    __syncthreads();
+    uint32_t run = (warp > 0 ? tmp[warp - 1] : 0) + incl - local;
+    const uint32_t total = tmp[(nt >> 5) - 1];
+    for (uint32_t i = lo; i < hi; ++i) {
+        uint32_t v = a[i];
+        a[i] = run;
+        run += v;
+    }
+    __syncthreads();
+    return total;
+}
+
+}  // namespace pbmoe

@@ -1,0 +1,268 @@
+"""pbmoe_moe_layer and pbmoe_route_topk against the CPU oracle.
+
+Routing is integer work: route ids must match bit-exactly. The GPU router
+GEMV sums in a different order than the reference's sequential fma loop
+(shaders.metal:1059-1075), so end-to-end id equality is asserted for tokens
+whose K-th and (K+1)-th logits are separated by more than the accumulated
+rounding bound; the selection function itself is checked bit-exactly on
+identical logits (GPU logits fed to the oracle's routing_softmax_top_k).
+"""
+
+import numpy as np
+import pytest
+
+from parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    import torch
+
+    from pb_b200 import capi
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    c = capi.Context(0)
+    yield c
+    c.close()
+
+
+def _host_u16(t):
+    from pb_b200.synth import bf16_bits
+
+    return bf16_bits(t).cpu().numpy().view(np.uint16)
+
+
+def _run_layer(ctx, w, x, tokens, top_k, residual=None, norm_w=None, out_dtype=None, routed_scale=1.0,
+               normalization=0):
+    import torch
+
+    from pb_b200 import capi
+
+    cfg = capi.moe_config(w.layout, w.num_experts, top_k, normalization=normalization, routed_scale=routed_scale)
+    ctx.reserve(max(tokens, 1), cfg)
+    od = out_dtype or x.dtype
+    out = torch.empty(tokens, w.hidden, device="cuda", dtype=od)
+    nn = torch.empty_like(out) if norm_w is not None else None
+    logits = torch.empty(tokens, w.num_experts, device="cuda")
+    ids = torch.empty(tokens, top_k, device="cuda", dtype=torch.int32)
+    rw = torch.empty(tokens, top_k, device="cuda")
+    sl = torch.empty(tokens, device="cuda")
+    dbg = capi.MoeDebug(logits.data_ptr(), ids.data_ptr(), rw.data_ptr(), sl.data_ptr())
+    ctx.moe_layer(cfg, w.c_weights(), x, out, tokens, residual=residual, next_norm_weight=norm_w, next_normed=nn,
+                  debug=dbg)
+    torch.cuda.synchronize()
+    status = ctx.device_status()
+    return out, nn, logits, ids, rw, sl, status
+
+
+def _oracle_layer(oracle, w, x, top_k, residual=None, routed_scale=1.0):
+    offs = np.array(list(w.layout.component_offsets), np.uint64)
+    return oracle.moe_layer(
+        x.float().cpu().numpy(), _host_u16(w.router), w.experts.cpu().numpy(), offs, int(w.layout.expert_bytes),
+        w.num_experts, top_k, w.intermediate, w.group,
+        shared_slot=None if w.shared is None else w.shared.cpu().numpy(),
+        shared_gate_bits=None if w.shared_gate is None else _host_u16(w.shared_gate),
+        residual=None if residual is None else residual.float().cpu().numpy(), routed_scale=routed_scale, threads=8)
+
+
+def _safe_tokens(logits_ref, k, hidden, x):
+    """Tokens whose routing cannot flip under GPU-vs-CPU summation order:
+    the gap between the K-th and (K+1)-th largest logit exceeds a generous
+    bound on the two dot products' rounding difference."""
+    srt = -np.sort(-logits_ref, axis=1)
+    gap = srt[:, k - 1] - srt[:, k]
+    bound = 64 * np.finfo(np.float32).eps * np.sqrt(hidden) * (np.abs(x).max(axis=1) * 0.1 + 1)
+    return gap > bound
+
+
+def _check_layer(ctx, oracle, w, tokens, top_k, seed, residual=False, norm=False, out_dtype=None):
+    import torch
+
+    from pb_b200 import synth
+
+    g = synth.gen("cuda", seed)
+    x = synth.normal_bf16((tokens, w.hidden), 1.0, g, "cuda")
+    res = synth.normal_bf16((tokens, w.hidden), 1.0, g, "cuda") if residual else None
+    norm_w = torch.rand(w.hidden, device="cuda", generator=g) + 0.5 if norm else None
+    out, nn, logits, ids, rw, sl, status = _run_layer(ctx, w, x, tokens, top_k, residual=res, norm_w=norm_w,
+                                                      out_dtype=out_dtype)
+    assert status == 0
+    ref_out, ref_ids, ref_w, ref_logits = _oracle_layer(oracle, w, x, top_k, residual=res)
+    lg = logits.cpu().numpy()
+    assert_close(lg, ref_logits, what="router logits")
+    # selection function bit-exact on identical logits
+    gids = ids.cpu().numpy().view(np.uint32)
+    for t in range(tokens):
+        oid, _ = oracle.routing_softmax_top_k(lg[t], top_k)
+        assert gids[t].tolist() == oid.tolist(), f"token {t}: selection differs on identical logits"
+    # end-to-end ids where the routing margin is safe
+    safe = _safe_tokens(ref_logits, top_k, w.hidden, x.float().cpu().numpy())
+    assert safe.mean() > 0.5
+    for t in np.nonzero(safe)[0]:
+        assert gids[t].tolist() == ref_ids[t].tolist(), f"token {t}: routed experts differ"
+    assert_close(rw.cpu().numpy()[safe], ref_w[safe], what="route weights")
+    if safe.all():
+        assert_close(out.float().cpu().numpy(), ref_out, what="layer output")
+    else:
+        assert_close(out.float().cpu().numpy()[safe], ref_out[safe], what="layer output (safe tokens)")
+    if norm:
+        ref_nn = np.stack([oracle.rms_norm(ref_out[t], norm_w.cpu().numpy()) for t in range(tokens)])
+        assert_close(nn.float().cpu().numpy()[safe], ref_nn[safe], what="next-layer norm")
+    return safe
+
+
+@pytest.fixture(scope="module")
+def small_layer():
+    from pb_b200 import synth
+
+    return synth.MoeLayerWeights("cuda", seed=11, hidden=512, num_experts=64, intermediate=256, group=64)
+
+
+@pytest.mark.parametrize("tokens", [1, 3, 8, 33])
+def test_small_layer(ctx, oracle, small_layer, tokens):
+    _check_layer(ctx, oracle, small_layer, tokens, top_k=6, seed=100 + tokens, residual=True, norm=True)
+
+
+def test_small_layer_f32_activations(ctx, oracle, small_layer):
+    import torch
+
+    _check_layer(ctx, oracle, small_layer, 4, top_k=4, seed=7, out_dtype=torch.float32)
+
+
+def test_no_shared_expert(ctx, oracle):
+    from pb_b200 import synth
+
+    w = synth.MoeLayerWeights("cuda", seed=5, hidden=256, num_experts=32, intermediate=128, group=32, shared=False)
+    _check_layer(ctx, oracle, w, 5, top_k=4, seed=9)
+
+
+def test_shared_expert_without_gate(ctx, oracle):
+    from pb_b200 import synth
+
+    w = synth.MoeLayerWeights("cuda", seed=6, hidden=256, num_experts=16, intermediate=96, group=32,
+                              shared_gate=False)
+    _check_layer(ctx, oracle, w, 2, top_k=2, seed=3)
+
+
+@pytest.fixture(scope="module")
+def config1_layer():
+    from pb_b200 import synth
+
+    return synth.MoeLayerWeights("cuda", seed=2024)
+
+
+@pytest.mark.parametrize("tokens", [1, 8, 32])
+def test_config1_layer(ctx, oracle, config1_layer, tokens):
+    """Config 1: hidden 2048, 512 experts top-10, I=512, group 64, shared expert."""
+    _check_layer(ctx, oracle, config1_layer, tokens, top_k=10, seed=77 + tokens)
+
+
+# ---------------------------------------------------------------- routing only
+def _route(ctx, logits_np, k, normalization=0, scale=1.0):
+    import torch
+
+    T, E = logits_np.shape
+    lg = torch.tensor(logits_np, device="cuda")
+    ids = torch.empty(T, k, device="cuda", dtype=torch.int32)
+    w = torch.empty(T, k, device="cuda")
+    ctx.route_topk(lg, T, E, k, ids, w, normalization=normalization, scale=scale)
+    torch.cuda.synchronize()
+    return ids.cpu().numpy().view(np.uint32), w.cpu().numpy(), ctx.device_status()
+
+
+def _oracle_route(oracle, logits_np, k, scale=1.0):
+    ids, ws = [], []
+    for row in logits_np:
+        i, p = oracle.routing_softmax_top_k(row, k)
+        ids.append(i)
+        ws.append(oracle.renormalize_routes(p, scale))
+    return np.stack(ids), np.stack(ws)
+
+
+def test_route_reference_slot_order(ctx, oracle):
+    """math.rs:1257-1279: slot order [5, 1, 8, 3]."""
+    ids, w, st = _route(ctx, np.array([[0.1, 2.0, -1.0, 3.0, 0.5, 2.5, -0.2, 1.5, 4.0]], np.float32), 4)
+    assert ids[0].tolist() == [5, 1, 8, 3]
+    assert st == 0
+    assert np.max(np.abs(w[0] - np.array([0.12925005, 0.07839412, 0.57925856, 0.2130973]))) <= 1e-6
+
+
+def test_route_huge_negative(ctx):
+    """math.rs:1292-1305."""
+    ids, w, st = _route(ctx, np.array([[-2.0e30, -3.0e30, -4.0e30]], np.float32), 2)
+    assert ids[0].tolist() == [0, 1]
+    assert abs(float(w[0].sum()) - 1.0) < 1e-6 and st == 0
+
+
+@pytest.mark.parametrize("E,k", [(512, 10), (64, 8), (33, 32), (128, 1), (1000, 7)])
+def test_route_random_bit_exact(ctx, oracle, E, k):
+    rng = np.random.default_rng(E * 31 + k)
+    lg = rng.standard_normal((64, E)).astype(np.float32)
+    ids, w, st = _route(ctx, lg, k)
+    rid, rw = _oracle_route(oracle, lg, k)
+    assert st == 0
+    assert np.array_equal(ids, rid)
+    assert_close(w, rw, tol=1e-5, what="weights")
+
+
+def test_route_ties_and_specials(ctx, oracle):
+    """Ties (earlier expert wins, first minimum slot replaced), -inf and NaN
+    scores, signed zeros."""
+    rows = [
+        np.zeros(40, np.float32),
+        np.array([1.0, 1.0, 1.0, 2.0, 2.0, 0.5, 2.0, 1.0] * 5, np.float32),
+        np.concatenate([np.full(20, -np.inf, np.float32), np.arange(20, dtype=np.float32)]),
+        np.where(np.arange(40) % 3 == 0, np.nan, np.arange(40, dtype=np.float32)).astype(np.float32),
+        np.array([-0.0, 0.0] * 20, np.float32),
+        np.round(np.random.default_rng(3).standard_normal(40) * 2).astype(np.float32),
+    ]
+    lg = np.stack(rows)
+    ids, w, st = _route(ctx, lg, 6)
+    rid, rw = _oracle_route(oracle, lg, 6)
+    assert np.array_equal(ids, rid)
+    assert_close(w, rw, tol=1e-5, what="weights")
+    assert st == 0
+
+
+def test_route_all_neg_inf_latches_error(ctx):
+    """All -inf logits: the reference bails on the selected-probability sum;
+    the kernel latches PBMOE_DEV_ERR_ROUTE_WEIGHTS."""
+    from pb_b200 import capi
+
+    _, _, st = _route(ctx, np.full((1, 16), -np.inf, np.float32), 4)
+    assert st & capi.PBMOE_DEV_ERR_ROUTE_WEIGHTS
+
+
+def test_route_routed_scale_and_floor(ctx, oracle):
+    rng = np.random.default_rng(12)
+    lg = rng.standard_normal((8, 96)).astype(np.float32)
+    ids, w, st = _route(ctx, lg, 8, scale=2.5)
+    rid, rw = _oracle_route(oracle, lg, 8, scale=2.5)
+    assert np.array_equal(ids, rid) and st == 0
+    assert_close(w, rw, tol=1e-5, what="scaled weights")
+    ids, w, st = _route(ctx, lg, 8, normalization=1)
+    ref = []
+    for row in lg:
+        _, p = oracle.routing_softmax_top_k(row, 8)
+        ref.append(oracle.renormalize_routes(p, 1.0, policy=1))
+    assert_close(w, np.stack(ref), tol=1e-5, what="floor weights")
+
+
+def test_moe_layer_rejects_bad_calls(ctx, small_layer):
+    import torch
+
+    from pb_b200 import capi
+
+    cfg = capi.moe_config(small_layer.layout, small_layer.num_experts, 6)
+    ctx.reserve(2, cfg)
+    x = torch.zeros(4, small_layer.hidden, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    with pytest.raises(capi.PbmoeError) as e:  # more tokens than reserved
+        ctx.moe_layer(cfg, small_layer.c_weights(), x, out, 4)
+    assert e.value.code == capi.PBMOE_ERR_NO_WORKSPACE
+    bad = capi.moe_config(small_layer.layout, small_layer.num_experts, 40)
+    with pytest.raises(capi.PbmoeError) as e:
+        ctx.moe_layer(bad, small_layer.c_weights(), x, out, 1)
+    assert e.value.code == capi.PBMOE_ERR_UNSUPPORTED
