@@ -200,6 +200,30 @@ PBMOE_API int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config, co
                     pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
                     void* next_normed, const pbmoe_moe_debug* debug, void* stream);
 
+/* pbmoe_moe_layer without any device allocation. No counterpart in the
+ * reference: it exists for hosts that cannot call cudaMalloc at run time (an
+ * engine whose own arena owns all device memory, code running under CUDA
+ * graph capture, loops that must not risk the synchronisation an allocation
+ * can cause) and therefore cannot create a pbmoe_ctx either.
+ *
+ * Same arithmetic and arguments as pbmoe_moe_layer, with no context. Its
+ * scratch is a fixed PBMOE_STATIC_SCRATCH_BYTES device array inside the
+ * library, present on every GPU where the library's kernels are loaded until
+ * the process exits; calls whose workspace does not fit (more than 34 tokens at
+ * hidden 2048 / 512 experts / top-10 / intermediate 512) return
+ * PBMOE_ERR_UNSUPPORTED. The array's device address is looked up on the first
+ * call on each device (the calling thread's current device): make that first
+ * call before any stream capture. All calls share the array: calls that may
+ * overlap on the GPU race and must be serialised by the caller.
+ * device_status (nullable, device u32) receives PBMOE_DEV_ERR_* bits; the
+ * message of a failed call goes to error_buf (nullable). */
+#define PBMOE_STATIC_SCRATCH_BYTES (4u << 20)
+PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
+                                     const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
+                                     pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
+                                     void* next_normed, uint32_t* device_status, char* error_buf,
+                                     size_t error_len, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -37,7 +37,7 @@ ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR = 1
 EXPORTED = [
     "pbmoe_init", "pbmoe_destroy", "pbmoe_last_error", "pbmoe_abi_version", "pbmoe_reserve",
     "pbmoe_moe_workspace_bytes", "pbmoe_device_status", "pbmoe_fixed_q4_layout", "pbmoe_q4_matvec",
-    "pbmoe_route_topk", "pbmoe_moe_layer",
+    "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static",
 ]
 
 
@@ -97,6 +97,8 @@ def load():
         L.pbmoe_route_topk.argtypes = [vp, vp, u32, u32, u32, u32, C.c_float, vp, vp, vp]
         L.pbmoe_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32, u32,
                                       vp, vp, C.POINTER(MoeDebug), vp]
+        L.pbmoe_moe_layer_static.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
+                                             u32, vp, vp, vp, C.c_char_p, C.c_size_t, vp]
         _lib = L
     return _lib
 
