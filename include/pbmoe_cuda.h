@@ -65,6 +65,7 @@ typedef enum pbmoe_status {
 #define PBMOE_DEV_ERR_ROUTE_WEIGHTS 0x1u /* selected probabilities not positive-finite */
 #define PBMOE_DEV_ERR_EXPERT_ID 0x2u     /* route expert id out of range               */
 #define PBMOE_DEV_ERR_PEER_TIMEOUT 0x4u  /* expert-parallel combine wait expired       */
+#define PBMOE_DEV_ERR_PIPE_TIMEOUT 0x8u  /* an asynchronous copy wait expired          */
 
 typedef enum pbmoe_dtype {
     PBMOE_F32 = 0,

@@ -130,16 +130,17 @@ MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t
     b[12] = R * I * 4;           // h
     b[13] = R * H * 4;           // y
     b[14] = size_t(T) * H * 4;   // y_tmp
+    b[15] = R * hperm_stride(I); // h_perm
     s.total = 0;
-    for (int i = 0; i < 15; ++i) s.total += align_up(b[i], 256);
+    for (int i = 0; i < 16; ++i) s.total += align_up(b[i], 256);
     return s;
 }
 
 MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
     MoeWsSizes s = moe_ws_sizes(T, E, K, H, I);
     char* p = static_cast<char*>(base);
-    void* ptr[15];
-    for (int i = 0; i < 15; ++i) {
+    void* ptr[16];
+    for (int i = 0; i < 16; ++i) {
         ptr[i] = p;
         p += align_up(s.bytes[i], 256);
     }
@@ -159,6 +160,7 @@ MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_
     w.h = static_cast<float*>(ptr[12]);
     w.y = static_cast<float*>(ptr[13]);
     w.y_tmp = static_cast<float*>(ptr[14]);
+    w.h_perm = static_cast<uint8_t*>(ptr[15]);
     return w;
 }
 
@@ -337,6 +339,8 @@ int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_w
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "next_norm_weight and next_normed must be given together");
     if (w->shared_expert_gate && !w->shared_expert)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "shared expert gate given without a shared expert");
+    if (!aligned(x, 16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "moe layer: x must be 16-byte aligned (rows are read as 16-byte vectors)");
     if (!aligned(w->experts, 16) || (w->shared_expert && !aligned(w->shared_expert, 16)) ||
         !aligned(w->router_weight, 16) || (w->shared_expert_gate && !aligned(w->shared_expert_gate, 16)))
         return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert table, shared expert and router weights must be 16-byte aligned");

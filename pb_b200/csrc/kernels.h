@@ -29,7 +29,15 @@ struct MoeWs {
     float* h;                // [(T*K + T) x I] SwiGLU activations per route
     float* y;                // [(T*K + T) x H] expert outputs per route
     float* y_tmp;            // [T x H] combined hidden (f32) for the next-layer norm
+    uint8_t* h_perm;         // [(T*K + T) x hperm_stride] SwiGLU activations as bf16 hi/lo pair
+                             // slots + per-8 partial sums (input layout of the pipelined down kernel)
 };
+
+// Bytes per route of MoeWs::h_perm for intermediate size I: hi slots, lo
+// slots (I/8 x 16 B each) and I/8 f32 partial sums, rounded to 16.
+__host__ __device__ inline size_t hperm_stride(uint32_t I) {
+    return ((size_t(I / 8) * 16 * 2 + size_t(I / 8) * 4) + 15) / 16 * 16;
+}
 
 // Expert slot geometry as the kernels use it.
 struct MoeLayoutDev {
@@ -64,7 +72,7 @@ struct MoeLaunch {
 
 // Per-launch bytes of each workspace array, in MoeWs order (host arithmetic).
 struct MoeWsSizes {
-    size_t bytes[15];
+    size_t bytes[16];
     size_t total;
 };
 MoeWsSizes moe_ws_sizes(uint32_t max_tokens, uint32_t E, uint32_t K, uint32_t H, uint32_t I);
@@ -72,6 +80,15 @@ MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t max_tokens, uint32_t E
                    uint32_t I);
 
 cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s);
+// Tensor-core expert kernels (group-64 layouts, moe_mma.cu).
+bool moe_mma_supported(const MoeLayoutDev& L);
+cudaError_t moe_up_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
+cudaError_t moe_down_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
+// Persistent, bulk-copy pipelined expert kernels (moe_pipe.cu) for decode
+// batches of at most 8 tokens on moe_mma_supported layouts.
+bool moe_pipe_supported(const MoeLaunch& a);
+cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
+cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
 size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K);
 cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
                               float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s);

@@ -3,7 +3,7 @@
 //
 //   1. moe_router_kernel   router GEMV (bf16 [E x H]) + shared-expert gate
 //                          logit; the last CTA to finish routes every token
-//                          (route_token_warp) and builds the layer-major group
+//                          (route_token_smem) and builds the layer-major group
 //                          plan (unique experts in ascending id order, routes
 //                          in route order inside each group, shared expert as
 //                          group 0 with every token).
@@ -31,7 +31,7 @@
 namespace pbmoe {
 
 // ---------------------------------------------------------------- kernel 1
-constexpr int kRouterThreads = 128;
+constexpr int kRouterThreads = 256;
 constexpr int kRouterRowsPerWarp = 1;
 constexpr int kRouterTokPass = 8;
 constexpr int kRouterVec = 8;  // 16-byte weight vectors per lane loaded before use
@@ -48,30 +48,62 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     const uint32_t row0 = (blockIdx.x * (kRouterThreads / 32) + warp) * kRouterRowsPerWarp;
     const uint32_t vec_per_row = H / 8;  // 16-byte vectors of 8 bf16
 
+    // The router row does not depend on earlier kernels: start its loads
+    // before waiting for the previous kernel (programmatic dependent launch).
+    const uint32_t row = row0;
+    const bool has_row = row < nrows;
+    const uint16_t* wrow = !has_row ? nullptr : (row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w);
+    uint4 w4[kRouterVec];
+    auto load_block = [&](uint32_t vb) {
+#pragma unroll
+        for (int i = 0; i < kRouterVec; ++i) {
+            const uint32_t v = vb + i * 32 + lane;
+            w4[i] = (has_row && v < vec_per_row) ? ld_stream_u4(wrow + static_cast<size_t>(v) * 8)
+                                                 : make_uint4(0, 0, 0, 0);
+        }
+    };
+    load_block(0);
     pdl_wait();
     for (uint32_t t0 = 0; t0 < T; t0 += kRouterTokPass) {
         const uint32_t nt = min(T - t0, static_cast<uint32_t>(kRouterTokPass));
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < nt * H; i += blockDim.x) {
-            const uint32_t t = i / H, c = i - t * H;
-            xs[t * H + c] = load_act<XT>(x, static_cast<size_t>(t0 + t) * H + c);
+        {  // stage x: every 16-byte load issued before any store
+            constexpr uint32_t kPerVec = 16 / sizeof(XT);
+            const uint32_t vpr = H / kPerVec, total = nt * vpr;
+            for (uint32_t base = 0; base < total; base += 8 * blockDim.x) {
+                uint4 v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+                    if (idx < total)
+                        v[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0) * H +
+                                                               static_cast<size_t>(idx) * kPerVec);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+                    if (idx < total) {
+                        float4* d = reinterpret_cast<float4*>(xs + static_cast<size_t>(idx) * kPerVec);
+                        if constexpr (sizeof(XT) == 2) {
+                            d[0] = make_float4(__uint_as_float(v[i].x << 16), __uint_as_float(v[i].x & 0xffff0000u),
+                                               __uint_as_float(v[i].y << 16), __uint_as_float(v[i].y & 0xffff0000u));
+                            d[1] = make_float4(__uint_as_float(v[i].z << 16), __uint_as_float(v[i].z & 0xffff0000u),
+                                               __uint_as_float(v[i].w << 16), __uint_as_float(v[i].w & 0xffff0000u));
+                        } else {
+                            d[0] = make_float4(__uint_as_float(v[i].x), __uint_as_float(v[i].y),
+                                               __uint_as_float(v[i].z), __uint_as_float(v[i].w));
+                        }
+                    }
+                }
+            }
         }
         __syncthreads();
-#pragma unroll
-        for (int rr = 0; rr < kRouterRowsPerWarp; ++rr) {
-            const uint32_t row = row0 + rr;
-            if (row >= nrows) break;
-            const uint16_t* wrow = row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w;
+        if (has_row) {
             float acc[kRouterTokPass];
 #pragma unroll
             for (int t = 0; t < kRouterTokPass; ++t) acc[t] = 0.f;
             for (uint32_t vb = 0; vb < vec_per_row; vb += 32 * kRouterVec) {
-                uint4 w4[kRouterVec];
-#pragma unroll
-                for (int i = 0; i < kRouterVec; ++i) {
-                    const uint32_t v = vb + i * 32 + lane;
-                    w4[i] = v < vec_per_row ? ld_stream_u4(wrow + static_cast<size_t>(v) * 8) : make_uint4(0, 0, 0, 0);
-                }
+                if (vb > 0 || t0 > 0) load_block(vb);
 #pragma unroll
                 for (int i = 0; i < kRouterVec; ++i) {
                     const uint32_t v = vb + i * 32 + lane;
@@ -103,12 +135,12 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
 #pragma unroll
             for (int t = 0; t < kRouterTokPass; ++t) {
                 if (static_cast<uint32_t>(t) < nt) {
-                    const float s = warp_sum(acc[t]);
+                    const float sum = warp_sum(acc[t]);
                     if (lane == 0) {
                         if (row < E)
-                            ws.logits[static_cast<size_t>(t0 + t) * E + row] = s;
+                            ws.logits[static_cast<size_t>(t0 + t) * E + row] = sum;
                         else
-                            ws.shared_logit[t0 + t] = s;
+                            ws.shared_logit[t0 + t] = sum;
                     }
                 }
             }
@@ -127,10 +159,15 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     if (!is_last) return;
     __threadfence();
 
-    for (uint32_t t = warp; t < T; t += blockDim.x / 32)
-        route_token_warp(ws.logits + static_cast<size_t>(t) * E, E, K, normalization, routed_scale,
-                         ws.route_ids + static_cast<size_t>(t) * K, ws.route_w + static_cast<size_t>(t) * K,
-                         ws.status);
+    {
+        const uint32_t Ep = (E + 3) & ~3u;
+        float* s = smem + warp * Ep;  // the x staging area is free now
+        for (uint32_t t = warp; t < T; t += blockDim.x / 32) {
+            stage_logits_warp(ws.logits + static_cast<size_t>(t) * E, E, s);
+            route_token_smem(s, E, K, normalization, routed_scale, ws.route_ids + static_cast<size_t>(t) * K,
+                             ws.route_w + static_cast<size_t>(t) * K, ws.status);
+        }
+    }
     __syncthreads();
 
     // group plan; shared memory reuses the activation staging area
@@ -187,11 +224,11 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
 
 // ---------------------------------------------------------------- kernel 2
 constexpr int kUpThreads = 128;
-constexpr int kUpRowsPerWarp = 4;  // intermediate indices per warp (gate+up = 8 rows)
+constexpr int kUpRowsPerWarp = 2;  // intermediate indices per warp (gate+up = 4 rows)
 constexpr int kUpRowsPerCta = kUpRowsPerWarp * (kUpThreads / 32);
 
 template <typename XT, int NT>
-__global__ void __launch_bounds__(kUpThreads)
+__global__ void __launch_bounds__(kUpThreads, 3)
 moe_expert_up_kernel(const XT* __restrict__ x, uint32_t E, const uint8_t* __restrict__ experts,
                      const uint8_t* __restrict__ shared_slot, MoeLayoutDev L, MoeWs ws) {
     extern __shared__ __align__(16) float smem[];
@@ -226,13 +263,14 @@ moe_expert_up_kernel(const XT* __restrict__ x, uint32_t E, const uint8_t* __rest
         ps[kUpRowsPerWarp + r] = reinterpret_cast<const uint16_t*>(slot + L.off[4]) + srow;
         pb[kUpRowsPerWarp + r] = reinterpret_cast<const uint16_t*>(slot + L.off[5]) + srow;
     }
+    Q4RowFrag<32, 2 * kUpRowsPerWarp, 2> frag;
     for (uint32_t p0 = 0; p0 < n; p0 += NT) {
         const int nt = static_cast<int>(min(n - p0, static_cast<uint32_t>(NT)));
+        frag.load(pk, ps, pb, geom, 0);  // weights in flight while x is staged
         __syncthreads();
         stage_x_fast<XT>(x, H, ws.group_tokens + start + p0, nt, H, xs, xe, xo);
-        __syncthreads();
         float acc[2 * kUpRowsPerWarp][NT];
-        q4_rows_partial<32, 2 * kUpRowsPerWarp, 2, NT>(pk, ps, pb, geom, xs, xe, xo, nt, acc);
+        q4_rows_finish<32, 2 * kUpRowsPerWarp, 2, NT>(frag, pk, ps, pb, geom, xs, xe, xo, nt, acc);
 #pragma unroll
         for (int r = 0; r < kUpRowsPerWarp; ++r) {
 #pragma unroll
@@ -251,10 +289,10 @@ moe_expert_up_kernel(const XT* __restrict__ x, uint32_t E, const uint8_t* __rest
 
 // ---------------------------------------------------------------- kernel 3
 constexpr int kDownThreads = 128;
-constexpr int kDownRowsPerGroup = 8;  // rows per lane group
+constexpr int kDownRowsPerGroup = 4;  // rows per lane group
 
 template <int LPR, int NT>
-__global__ void __launch_bounds__(kDownThreads)
+__global__ void __launch_bounds__(kDownThreads, 4)
 moe_expert_down_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint8_t* __restrict__ shared_slot,
                        MoeLayoutDev L, MoeWs ws) {
     extern __shared__ __align__(16) float smem[];
@@ -291,14 +329,16 @@ moe_expert_down_kernel(uint32_t E, const uint8_t* __restrict__ experts, const ui
         ps[r] = reinterpret_cast<const uint16_t*>(slot + L.off[7]) + static_cast<size_t>(row) * geom.gpr;
         pb[r] = reinterpret_cast<const uint16_t*>(slot + L.off[8]) + static_cast<size_t>(row) * geom.gpr;
     }
+    Q4RowFrag<LPR, kDownRowsPerGroup, 1> frag;
+    frag.load(pk, ps, pb, geom, 0);  // down weights do not depend on the up kernel
     pdl_wait();
     for (uint32_t p0 = 0; p0 < n; p0 += NT) {
         const int nt = static_cast<int>(min(n - p0, static_cast<uint32_t>(NT)));
+        if (p0 > 0) frag.load(pk, ps, pb, geom, 0);
         __syncthreads();
         stage_x_fast<float>(ws.h, I, ws.group_routes + start + p0, nt, I, xs, xe, xo);
-        __syncthreads();
         float acc[kDownRowsPerGroup][NT];
-        q4_rows_partial<LPR, kDownRowsPerGroup, 1, NT>(pk, ps, pb, geom, xs, xe, xo, nt, acc);
+        q4_rows_finish<LPR, kDownRowsPerGroup, 1, NT>(frag, pk, ps, pb, geom, xs, xe, xo, nt, acc);
 #pragma unroll
         for (int r = 0; r < kDownRowsPerGroup; ++r) {
 #pragma unroll
@@ -315,29 +355,57 @@ moe_expert_down_kernel(uint32_t E, const uint8_t* __restrict__ experts, const ui
 }
 
 // ---------------------------------------------------------------- kernel 4
-constexpr int kCombineThreads = 256;
+constexpr int kCombineThreads = 512;
+constexpr int kCombineEpt = 4;  // elements per thread per pass (H <= 2048 in one pass)
 
-template <typename OT>
+// One CTA per token. The K routed outputs, the shared output and the
+// residual of a thread's elements are all requested before any arithmetic
+// (K <= KMAX, unrolled), then summed in slot order as the reference does.
+template <typename OT, int KMAX>
 __global__ void __launch_bounds__(kCombineThreads)
 moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_gate, const OT* __restrict__ residual,
                    OT* __restrict__ out, const float* __restrict__ norm_w, OT* __restrict__ next_normed, float eps,
                    MoeWs ws) {
     __shared__ float red[32];
+    __shared__ float wsh[KMAX];
     const uint32_t t = blockIdx.x;
     pdl_wait();
+    if (threadIdx.x < K) wsh[threadIdx.x] = __ldcg(ws.route_w + static_cast<size_t>(t) * K + threadIdx.x);
     float sw = 0.f;
-    if (has_shared) sw = has_gate ? 1.0f / (1.0f + expf(-ws.shared_logit[t])) : 1.0f;
-    const float* wk = ws.route_w + static_cast<size_t>(t) * K;
+    if (has_shared) sw = has_gate ? 1.0f / (1.0f + expf(-__ldcg(ws.shared_logit + t))) : 1.0f;
+    __syncthreads();
+    const float* yt = ws.y + static_cast<size_t>(t) * K * H;
+    const float* ysh = ws.y + (static_cast<size_t>(T) * K + t) * H;
     float ss = 0.f;
-    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
-        float moe = 0.f;
-        for (uint32_t k = 0; k < K; ++k) moe += wk[k] * ws.y[(static_cast<size_t>(t) * K + k) * H + c];
-        const float sh = has_shared ? ws.y[(static_cast<size_t>(T) * K + t) * H + c] : 0.f;
-        const float r = residual ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
-        const float v = r + moe + sw * sh;
-        store_act<OT>(out, static_cast<size_t>(t) * H + c, v);
-        ss += v * v;
-        if (norm_w) ws.y_tmp[static_cast<size_t>(t) * H + c] = v;
+    float keep[kCombineEpt];
+    for (uint32_t c0 = threadIdx.x; c0 < H; c0 += kCombineEpt * blockDim.x) {
+        float yv[KMAX][kCombineEpt];
+        float sh[kCombineEpt], rv[kCombineEpt];
+#pragma unroll
+        for (int i = 0; i < kCombineEpt; ++i) {
+            const uint32_t c = c0 + i * blockDim.x;
+            const bool in = c < H;
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k)
+                yv[k][i] = (in && static_cast<uint32_t>(k) < K) ? __ldcg(yt + static_cast<size_t>(k) * H + c) : 0.f;
+            sh[i] = (in && has_shared) ? __ldcg(ysh + c) : 0.f;
+            rv[i] = (in && residual) ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kCombineEpt; ++i) {
+            const uint32_t c = c0 + i * blockDim.x;
+            float moe = 0.f;
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k)
+                if (static_cast<uint32_t>(k) < K) moe += wsh[k] * yv[k][i];
+            const float v = rv[i] + moe + sw * sh[i];
+            keep[i] = v;
+            if (c < H) {
+                store_act<OT>(out, static_cast<size_t>(t) * H + c, v);
+                ss += v * v;
+                if (norm_w) ws.y_tmp[static_cast<size_t>(t) * H + c] = v;
+            }
+        }
     }
     if (!norm_w) return;
     ss = warp_sum(ss);
@@ -350,9 +418,18 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     }
     __syncthreads();
     const float scale = 1.0f / sqrtf(red[0] / static_cast<float>(H) + eps);
-    for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
-        const float v = ws.y_tmp[static_cast<size_t>(t) * H + c];
-        store_act<OT>(next_normed, static_cast<size_t>(t) * H + c, v * scale * norm_w[c]);
+    if (H <= kCombineEpt * blockDim.x) {
+        // one pass: the values are still in registers
+#pragma unroll
+        for (int i = 0; i < kCombineEpt; ++i) {
+            const uint32_t c = threadIdx.x + i * blockDim.x;
+            if (c < H) store_act<OT>(next_normed, static_cast<size_t>(t) * H + c, keep[i] * scale * norm_w[c]);
+        }
+    } else {
+        for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
+            const float v = ws.y_tmp[static_cast<size_t>(t) * H + c];
+            store_act<OT>(next_normed, static_cast<size_t>(t) * H + c, v * scale * norm_w[c]);
+        }
     }
 }
 
@@ -360,10 +437,15 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
 __global__ void route_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E, uint32_t K,
                                   uint32_t normalization, float routed_scale, uint32_t* ids, float* w,
                                   uint32_t* status) {
-    const uint32_t t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    extern __shared__ __align__(16) float rsm[];  // per warp: E logits (padded to 4)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t t = blockIdx.x * (blockDim.x / 32) + warp;
     if (t >= T) return;
-    route_token_warp(logits + static_cast<size_t>(t) * E, E, K, normalization, routed_scale,
-                     ids + static_cast<size_t>(t) * K, w + static_cast<size_t>(t) * K, status);
+    const uint32_t Ep = (E + 3) & ~3u;
+    float* s = rsm + warp * Ep;
+    stage_logits_warp(logits + static_cast<size_t>(t) * E, E, s);
+    route_token_smem(s, E, K, normalization, routed_scale, ids + static_cast<size_t>(t) * K,
+                     w + static_cast<size_t>(t) * K, status);
 }
 
 // ---------------------------------------------------------------- host side
@@ -385,7 +467,9 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
 size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K) {
     const size_t stage = static_cast<size_t>(kRouterTokPass) * H * sizeof(float);
     const size_t plan = (2ull * E + static_cast<size_t>(T) * K + 32) * sizeof(uint32_t);
-    return stage > plan ? stage : plan;
+    const size_t route = static_cast<size_t>(kRouterThreads / 32) * ((E + 3) & ~3u) * sizeof(float);
+    size_t m = stage > plan ? stage : plan;
+    return m > route ? m : route;
 }
 
 template <typename F>
@@ -430,8 +514,14 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     MoeLayoutDev L = a.layout;
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
+    const bool mma = moe_mma_supported(a.layout);
+    const bool pipe = moe_pipe_supported(a);
     // 2. gate/up/SwiGLU
-    {
+    if (pipe) {
+        if ((err = moe_up_pipe_launch(a, s, pdl)) != cudaSuccess) return err;
+    } else if (mma) {
+        if ((err = moe_up_mma_launch(a, gmax, s, pdl)) != cudaSuccess) return err;
+    } else {
         const uint32_t chunks = H >> 5;
         dim3 grid((I + kUpRowsPerCta - 1) / kUpRowsPerCta, gmax);
         const XT* x = static_cast<const XT*>(a.x);
@@ -451,7 +541,11 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     }
     if ((err = mark(2)) != cudaSuccess) return err;
     // 3. down
-    {
+    if (pipe) {
+        if ((err = moe_down_pipe_launch(a, s, pdl)) != cudaSuccess) return err;
+    } else if (mma) {
+        if ((err = moe_down_mma_launch(a, gmax, s, pdl)) != cudaSuccess) return err;
+    } else {
         const uint32_t chunks = I >> 5;
         void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
         const int lpr = chunks >= 32 ? 32 : (chunks >= 16 ? 16 : 8);
@@ -485,10 +579,10 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         float eps = a.eps;
         void* args[] = {(void*)&T, (void*)&H, (void*)&K, (void*)&has_shared, (void*)&has_gate, (void*)&res,
                         (void*)&out, (void*)&nw, (void*)&nn, (void*)&eps, (void*)&ws};
-        auto fn = moe_combine_kernel<OT>;
-        if ((err = launch_pdl(reinterpret_cast<const void*>(fn), dim3(T), dim3(kCombineThreads), 0, s, args,
-                              pdl)) != cudaSuccess)
-            return err;
+        const void* fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8>)
+                         : K <= 16 ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 16>)
+                                   : reinterpret_cast<const void*>(moe_combine_kernel<OT, 32>);
+        if ((err = launch_pdl(fn, dim3(T), dim3(kCombineThreads), 0, s, args, pdl)) != cudaSuccess) return err;
     }
     return mark(4);
 }
@@ -504,8 +598,12 @@ cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s) {
 cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
                               float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s) {
     const int warps = 4;
-    route_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>(logits, T, E, K, normalization, routed_scale,
-                                                                       ids, w, status);
+    const size_t smem = warps * ((E + 3) & ~3u) * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(route_topk_kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    route_topk_kernel<<<(T + warps - 1) / warps, warps * 32, smem, s>>>(logits, T, E, K, normalization,
+                                                                          routed_scale, ids, w, status);
     return cudaGetLastError();
 }
 

@@ -108,6 +108,12 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
         return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
     if ((next_norm_weight == nullptr) != (next_normed == nullptr) || (w->shared_expert_gate && !w->shared_expert))
         return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT, "inconsistent optional arguments");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w->experts) % 16 ||
+        reinterpret_cast<uintptr_t>(w->router_weight) % 16 ||
+        (w->shared_expert && reinterpret_cast<uintptr_t>(w->shared_expert) % 16) ||
+        (w->shared_expert_gate && reinterpret_cast<uintptr_t>(w->shared_expert_gate) % 16))
+        return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT,
+                      "moe layer (static): x, experts, router and shared weights must be 16-byte aligned");
     if (tokens == 0) return PBMOE_OK;
     const size_t need = kStatusBytes + moe_ws_sizes(tokens, E, K, H, I).total;
     if (need > kStaticScratchBytes)

@@ -11,6 +11,7 @@
 // reference's own per-element arithmetic.
 
 #include "kernels.h"
+#include "q4_mma.cuh"
 #include "q4_rows.cuh"
 
 namespace pbmoe {
@@ -19,7 +20,7 @@ constexpr int kMvThreads = 128;
 constexpr int kMvRows = 4;  // rows per lane group per pass
 
 template <typename XT, typename YT, int LPR, int CPL, int NT>
-__global__ void __launch_bounds__(kMvThreads)
+__global__ void __launch_bounds__(kMvThreads, 3)
 q4_matvec_fast_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
                       const uint16_t* __restrict__ biases, Q4Geom g, const XT* __restrict__ x,
                       YT* __restrict__ y, uint32_t batch) {
@@ -42,13 +43,14 @@ q4_matvec_fast_kernel(const uint8_t* __restrict__ packed, const uint16_t* __rest
         ps[r] = scales + static_cast<size_t>(row) * g.gpr;
         pb[r] = biases + static_cast<size_t>(row) * g.gpr;
     }
+    Q4RowFrag<LPR, kMvRows, CPL> frag;
     for (uint32_t b0 = 0; b0 < batch; b0 += NT) {
         const int nt = static_cast<int>(min(batch - b0, static_cast<uint32_t>(NT)));
+        frag.load(pk, ps, pb, g, 0);  // weights in flight while x is staged
         __syncthreads();
         stage_x_fast<XT>(x + static_cast<size_t>(b0) * g.cols, g.cols, nullptr, nt, g.cols, xs, xe, xo);
-        __syncthreads();
         float acc[kMvRows][NT];
-        q4_rows_partial<LPR, kMvRows, CPL, NT>(pk, ps, pb, g, xs, xe, xo, nt, acc);
+        q4_rows_finish<LPR, kMvRows, CPL, NT>(frag, pk, ps, pb, g, xs, xe, xo, nt, acc);
 #pragma unroll
         for (int r = 0; r < kMvRows; ++r) {
 #pragma unroll
@@ -85,6 +87,107 @@ q4_matvec_generic_kernel(const uint8_t* __restrict__ packed, const uint16_t* __r
     }
 }
 
+// Tensor-core matvec for group-64 weights (q4_mma.cuh): CTA = 8 warps =
+// (8/KS) tiles of 8 rows x KS K-slices; slices are summed in shared memory.
+// kTok16: bf16 activations, up to 16 tokens per pass; f32 activations use
+// hi/lo rows (8 tokens per pass).
+template <typename XT, typename YT, int KS, bool kTok16>
+__global__ void __launch_bounds__(256, 2)
+q4_matvec_mma_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
+                     const uint16_t* __restrict__ biases, uint32_t rows, uint32_t cols, const XT* __restrict__ x,
+                     YT* __restrict__ y, uint32_t batch) {
+    constexpr bool kLo = sizeof(XT) == 4;
+    constexpr bool kRows16 = kLo || kTok16;
+    constexpr int kPass = kTok16 ? 16 : 8;
+    constexpr int kTiles = 8 / KS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t trows = kRows16 ? 16 : 8;
+    const ActTile tile = act_tile_at(smem_raw, cols, trows);
+    float* red = reinterpret_cast<float*>(smem_raw + act_tile_bytes(cols, trows));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int tl = warp / KS, ks = warp % KS;
+    const uint32_t gpr = cols / kMmaGroup;
+    const uint32_t gps = gpr / KS;
+    const uint32_t r0 = blockIdx.x * (8 * kTiles) + tl * 8;
+    // rows past the end read the last row and are never stored
+    const uint32_t rg = min(r0 + g, rows - 1), ra = min(r0 + 2 * t, rows - 1), rb = min(r0 + 2 * t + 1, rows - 1);
+    const uint8_t* wrow = packed + static_cast<size_t>(rg) * (cols / 2);
+    const uint32_t grp0 = ks * gps;
+    Q4MmaFrag4 f;
+    // scale rows ra and rb = ra + 1 unless clamped; load them through the
+    // (row 2t, row 2t+1) pair when both exist, else clamp both to ra
+    const uint16_t* sa = scales + static_cast<size_t>(ra) * gpr;
+    const uint16_t* ba = biases + static_cast<size_t>(ra) * gpr;
+    const uint32_t pair_gpr = (rb == ra + 1) ? gpr : 0;
+    f.load(wrow, sa, ba, pair_gpr, grp0, t);
+    for (uint32_t b0 = 0; b0 < batch; b0 += kPass) {
+        const int nt = static_cast<int>(min(batch - b0, static_cast<uint32_t>(kPass)));
+        __syncthreads();
+        if constexpr (kRows16)
+            stage_act_mma<XT>(x + static_cast<size_t>(b0) * cols, cols, nullptr, nt, cols, tile);
+        else
+            stage_act_rows8_tok<XT>(x + static_cast<size_t>(b0) * cols, cols, nt, cols, tile);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (uint32_t b = 0; b < gps; b += 4) {
+            if (b > 0) f.load(wrow, sa, ba, pair_gpr, grp0 + b, t);
+            f.compute<kLo, kTok16>(tile, grp0 + b, g, t, acc);
+        }
+        if (gps > 4) f.load(wrow, sa, ba, pair_gpr, grp0, t);  // block 0 again for the next pass
+        float* rw = red + warp * (16 * 8);
+        rw[g * 8 + 2 * t] = acc[0];
+        rw[g * 8 + 2 * t + 1] = acc[1];
+        if (kTok16) {
+            rw[(g + 8) * 8 + 2 * t] = acc[2];
+            rw[(g + 8) * 8 + 2 * t + 1] = acc[3];
+        }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < kTiles * 16 * 8; i += blockDim.x) {
+            const uint32_t tile_i = i / 128, tok = (i / 8) % 16, r = i % 8;
+            const uint32_t row = blockIdx.x * (8 * kTiles) + tile_i * 8 + r;
+            if (tok < static_cast<uint32_t>(nt) && row < rows) {
+                float sum = 0.f;
+#pragma unroll
+                for (int k = 0; k < KS; ++k) sum += red[(tile_i * KS + k) * 128 + tok * 8 + r];
+                store_act<YT>(y, static_cast<size_t>(b0 + tok) * rows + row, sum);
+            }
+        }
+    }
+}
+
+template <typename XT, typename YT, int KS>
+static cudaError_t launch_mma_ks(const Q4MatvecArgs& a, cudaStream_t s) {
+    constexpr int kTiles = 8 / KS;
+    const bool lo = sizeof(XT) == 4;
+    const bool tok16 = !lo && a.batch > 8;
+    const size_t trows = (lo || tok16) ? 16 : 8;
+    const size_t smem = act_tile_bytes(a.cols, static_cast<uint32_t>(trows)) + 8 * 16 * 8 * 4;
+    if (smem > 200 * 1024) return cudaErrorNotSupported;
+    const void* fn = tok16 ? reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, true>)
+                           : reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, false>);
+    cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    const dim3 grid((a.rows + 8 * kTiles - 1) / (8 * kTiles));
+    const uint8_t* p = a.packed;
+    const uint16_t* sc = a.scales;
+    const uint16_t* bi = a.biases;
+    uint32_t rows = a.rows, cols = a.cols, batch = a.batch;
+    const XT* x = static_cast<const XT*>(a.x);
+    YT* y = static_cast<YT*>(a.y);
+    void* args[] = {(void*)&p, (void*)&sc, (void*)&bi, (void*)&rows, (void*)&cols, (void*)&x, (void*)&y, (void*)&batch};
+    return cudaLaunchKernel(fn, grid, dim3(256), args, smem, s);
+}
+
+// Group-64 weights whose row length is a multiple of 256 columns.
+template <typename XT, typename YT>
+static cudaError_t launch_mma(const Q4MatvecArgs& a, cudaStream_t s) {
+    const uint32_t blocks = a.cols / 256;  // 4-group blocks per row
+    if (blocks % 8 == 0) return launch_mma_ks<XT, YT, 8>(a, s);
+    if (blocks % 4 == 0) return launch_mma_ks<XT, YT, 4>(a, s);
+    if (blocks % 2 == 0) return launch_mma_ks<XT, YT, 2>(a, s);
+    return launch_mma_ks<XT, YT, 1>(a, s);
+}
+
 template <typename XT, typename YT, int LPR, int CPL, int NT>
 static cudaError_t launch_fast(const Q4MatvecArgs& a, const Q4Geom& g, cudaStream_t s) {
     constexpr int kGroups = 32 / LPR;
@@ -103,7 +206,15 @@ static cudaError_t launch_fast(const Q4MatvecArgs& a, const Q4Geom& g, cudaStrea
 template <typename XT, typename YT>
 static cudaError_t q4_matvec_launch_t(const Q4MatvecArgs& a, cudaStream_t s) {
     constexpr size_t kSmemLimit = 200 * 1024;
-    if (q4_fast_ok(a.cols, a.group, a.packed)) {
+    const size_t xelem = a.x_dtype == PBMOE_BF16 ? 2 : 4;
+    if (a.group == kMmaGroup && a.cols % 256 == 0 && reinterpret_cast<uintptr_t>(a.packed) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(a.scales) % 8 == 0 && reinterpret_cast<uintptr_t>(a.biases) % 8 == 0 &&
+        reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
+        cudaError_t e = launch_mma<XT, YT>(a, s);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    if (q4_fast_ok(a.cols, a.group, a.packed) && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
+        (a.cols * xelem) % 16 == 0) {
         Q4Geom g{a.rows, a.cols, (a.cols + a.group - 1) / a.group, a.cols / 32, ilog2_u32(a.group / 32)};
         const size_t per_tok = (g.cols + 2ull * g.chunks) * sizeof(float);
         const bool multi = a.batch > 1 && 4 * per_tok <= kSmemLimit;

@@ -1,0 +1,332 @@
+// q4_mma.cuh — decode-GEMV building blocks on the tensor cores (mma.sync
+// m16n8k16, bf16 inputs, f32 accumulate) for group-64 Q4 weights.
+//
+// Why tensor cores for a matvec: the decode path is HBM-bound, and at B200
+// bandwidth the SM has ~2.8 instruction issues per weight nibble to spend.
+// Dequantising on the CUDA cores costs ~3.3 (shift, mask, convert, FMA per
+// nibble) and leaves the kernel issue-bound. Here a nibble costs one mask-OR
+// (two nibbles per instruction) plus a quarter of an mma.
+//
+// Exact nibble → bf16: OR-ing a nibble into the mantissa of 128.0 (0x4300)
+// gives the bf16 value 128 + q exactly, so one LOP3 turns a shifted u32 word
+// into a bf16x2 pair (128 + q_a, 128 + q_b). The mma then accumulates
+//     D = sum_c (128 + q_c) x_c = 128 * X + sum_c q_c x_c,   X = sum_c x_c
+// in fp32 over one quantisation group (products are exact; the 128*X offset
+// costs ~2^-17 relative), and each group is finished on the CUDA cores as
+//     y += s * D + (b - 128 s) * X
+// which equals sum_c (q_c s + b) x_c (math.rs:861-911 up to summation order).
+//
+// Fragment mapping (PTX ISA m16n8k16 .row.col): lane = 4*g + t.
+//   A (16x16 activations): row g = token g, row g+8 = token g+8 (or the low
+//     part of token g when activations are f32, see stage_act_mma);
+//     a0/a2 hold k = {2t,2t+1} / {2t+8,2t+9} of row g, a1/a3 of row g+8.
+//   B (16x8 weights, k x n): column n = weight row r0+n, supplied by lanes
+//     with g = n; b0/b1 hold k = {2t,2t+1} / {2t+8,2t+9}.
+//   D: d0/d1 = token g x weight rows r0+2t / r0+2t+1; d2/d3 = token g+8.
+// The contraction index k is a free permutation of the group's 64 columns:
+// for word step m in {0,1} lane t contributes packed word w = 2t+m of the
+// group (columns 8w..8w+7). mma "P" takes nibble pairs (0,4) and (1,5), mma
+// "Q" takes (2,6) and (3,7); the activations are staged in shared memory in
+// the same pair order, so one 16-byte load yields all four A registers.
+#pragma once
+
+#include "common.cuh"
+
+namespace pbmoe {
+
+constexpr uint32_t kMmaGroup = 64;       // the fast path's quantisation group
+constexpr uint32_t kBf16Offset = 0x43004300u;  // bf16x2 (128.0, 128.0)
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+
+// Shared-memory activation tile for the mma path:
+//   act  : [rows][K/8 + 1 slots] of uint4, slot = 8 activations of one packed
+//          word in pair order (x0,x4),(x1,x5),(x2,x6),(x3,x7) as bf16x2; the
+//          extra slot pads each row so that lanes reading the same word of
+//          consecutive rows hit different banks (rows can then also be filled
+//          by contiguous bulk copies)
+//   gsum : [rows][K/64] f32 group sums of the (full precision) activations
+// Rows >= the token count are zero. With LO (f32 inputs), row t+8 holds the
+// bf16 rounding residue of token t, so hi + lo carries ~16 mantissa bits.
+struct ActTile {
+    uint4* act;
+    float* gsum;
+    uint32_t slots;   // K / 8
+    uint32_t groups;  // row stride of gsum in floats (K / 64 + 1: padded against bank conflicts)
+    uint32_t stride;  // slots per row including the pad (K / 8 + 1)
+};
+
+__host__ __device__ inline uint32_t act_stride(uint32_t K) { return K / 8 + 1; }
+
+__host__ __device__ inline size_t act_tile_bytes(uint32_t K, uint32_t rows) {
+    return size_t(rows) * act_stride(K) * 16 + (size_t(rows) * (K / 64 + 1) * 4 + 15) / 16 * 16;
+}
+
+__host__ __device__ inline ActTile act_tile_at(void* base, uint32_t K, uint32_t rows) {
+    ActTile t;
+    t.act = reinterpret_cast<uint4*>(base);
+    t.gsum = reinterpret_cast<float*>(reinterpret_cast<char*>(base) + size_t(rows) * act_stride(K) * 16);
+    t.slots = K / 8;
+    t.groups = K / 64 + 1;
+    t.stride = act_stride(K);
+    return t;
+}
+
+__device__ __forceinline__ uint32_t pack_pairs_lo(uint32_t a, uint32_t b) {  // (a.lo, b.lo)
+    return __byte_perm(a, b, 0x5410);
+}
+__device__ __forceinline__ uint32_t pack_pairs_hi(uint32_t a, uint32_t b) {  // (a.hi, b.hi)
+    return __byte_perm(a, b, 0x7632);
+}
+
+// Round two floats to a bf16x2 (round to nearest even), low half = a.
+__device__ __forceinline__ uint32_t f2_to_bf16x2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+
+// Stage `ntok` activation rows (<= 16 for bf16, <= 8 for f32) into `tile`.
+// x rows are `x_stride` elements apart; rows_idx maps local token t to its
+// source row (NULL = identity). All global loads of a thread are issued before
+// its shared stores. Ends with __syncthreads.
+template <typename XT>
+__device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx, int ntok,
+                              uint32_t K, const ActTile& tile) {
+    constexpr bool kLo = sizeof(XT) == 4;
+    const uint32_t slots = K / 8;
+    const uint32_t nrows = 16;
+    // zero the unused rows (and, for bf16, rows ntok..15; for f32, rows ntok..7 and 8+ntok..15)
+    for (uint32_t i = threadIdx.x; i < nrows * slots; i += blockDim.x) {
+        const uint32_t row = i / slots;
+        const uint32_t tok = kLo ? (row & 7u) : row;
+        if (tok >= static_cast<uint32_t>(ntok)) tile.act[(i / slots) * tile.stride + (i % slots)] = make_uint4(0, 0, 0, 0);
+    }
+    for (uint32_t i = threadIdx.x; i < nrows * tile.groups; i += blockDim.x) {
+        const uint32_t row = i / tile.groups;
+        const uint32_t tok = kLo ? (row & 7u) : row;
+        if (tok >= static_cast<uint32_t>(ntok) || (kLo && row >= 8)) tile.gsum[i] = 0.f;
+    }
+    // one thread per (token, word): 8 activations
+    const uint32_t total = static_cast<uint32_t>(ntok) * slots;
+    constexpr int kBatch = kLo ? 1 : 4;
+    for (uint32_t base = 0; base < total; base += kBatch * blockDim.x) {
+        uint4 v[kBatch][kLo ? 2 : 1];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            if (idx < total) {
+                const uint32_t t = idx / slots, w = idx - t * slots;
+                const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
+                const uint4* p = reinterpret_cast<const uint4*>(x + src * x_stride + static_cast<size_t>(w) * 8);
+                v[i][0] = p[0];
+                if constexpr (kLo) v[i][1] = p[1];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            float sum = 0.f;
+            uint32_t t = 0, w = 0;
+            const bool ok = idx < total;
+            if (ok) {
+                t = idx / slots;
+                w = idx - t * slots;
+                if constexpr (!kLo) {
+                    const uint4 r = v[i][0];  // (x0,x1) (x2,x3) (x4,x5) (x6,x7)
+                    tile.act[t * tile.stride + w] =
+                        make_uint4(pack_pairs_lo(r.x, r.z), pack_pairs_hi(r.x, r.z), pack_pairs_lo(r.y, r.w),
+                                   pack_pairs_hi(r.y, r.w));
+                    const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) sum += __uint_as_float(rr[q] << 16) + __uint_as_float(rr[q] & 0xffff0000u);
+                } else {
+                    float f[8] = {__uint_as_float(v[i][0].x), __uint_as_float(v[i][0].y), __uint_as_float(v[i][0].z),
+                                  __uint_as_float(v[i][0].w), __uint_as_float(v[i][1].x), __uint_as_float(v[i][1].y),
+                                  __uint_as_float(v[i][1].z), __uint_as_float(v[i][1].w)};
+                    uint32_t hi[4], lo[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        // pair order (x_q, x_{q+4})
+                        const uint32_t h = f2_to_bf16x2(f[q], f[q + 4]);
+                        const float h0 = __uint_as_float(h << 16), h1 = __uint_as_float(h & 0xffff0000u);
+                        hi[q] = h;
+                        lo[q] = f2_to_bf16x2(f[q] - h0, f[q + 4] - h1);
+                        sum += f[q] + f[q + 4];
+                    }
+                    tile.act[t * tile.stride + w] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    tile.act[(t + 8) * tile.stride + w] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                }
+            }
+            // group sums: the 8 words of a group are 8 consecutive threads
+            // when slots % 8 == 0 (always: K % 64 == 0)
+            sum += __shfl_xor_sync(kFull, sum, 1);
+            sum += __shfl_xor_sync(kFull, sum, 2);
+            sum += __shfl_xor_sync(kFull, sum, 4);
+            if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
+        }
+    }
+    __syncthreads();
+}
+
+// stage_act_mma for bf16 tiles with only 8 token rows (tokens <= 8) and
+// contiguous token rows.
+template <typename XT>
+__device__ void stage_act_rows8_tok(const XT* __restrict__ x, size_t x_stride, int ntok, uint32_t K,
+                                    const ActTile& tile) {
+    static_assert(sizeof(XT) == 2, "8-row tiles hold bf16 activations");
+    const uint32_t slots = K / 8;
+    for (uint32_t i = threadIdx.x; i < 8 * slots; i += blockDim.x)
+        if (i / slots >= static_cast<uint32_t>(ntok)) tile.act[(i / slots) * tile.stride + (i % slots)] = make_uint4(0, 0, 0, 0);
+    for (uint32_t i = threadIdx.x; i < 8 * tile.groups; i += blockDim.x)
+        if (i / tile.groups >= static_cast<uint32_t>(ntok)) tile.gsum[i] = 0.f;
+    const uint32_t total = static_cast<uint32_t>(ntok) * slots;
+    constexpr int kBatch = 4;
+    for (uint32_t base = 0; base < total; base += kBatch * blockDim.x) {
+        uint4 v[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            if (idx < total) {
+                const uint32_t t = idx / slots, w = idx - t * slots;
+                v[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * x_stride + static_cast<size_t>(w) * 8);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            float sum = 0.f;
+            uint32_t t = 0, w = 0;
+            const bool ok = idx < total;
+            if (ok) {
+                t = idx / slots;
+                w = idx - t * slots;
+                const uint4 r = v[i];
+                tile.act[t * tile.stride + w] = make_uint4(pack_pairs_lo(r.x, r.z), pack_pairs_hi(r.x, r.z),
+                                                                  pack_pairs_lo(r.y, r.w), pack_pairs_hi(r.y, r.w));
+                const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) sum += __uint_as_float(rr[q] << 16) + __uint_as_float(rr[q] & 0xffff0000u);
+            }
+            sum += __shfl_xor_sync(kFull, sum, 1);
+            sum += __shfl_xor_sync(kFull, sum, 2);
+            sum += __shfl_xor_sync(kFull, sum, 4);
+            if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
+        }
+    }
+    __syncthreads();
+}
+
+// Register fragment of one 8-row tile over a block of 4 consecutive groups:
+// lane (g,t) holds words 2t, 2t+1 of row r0+g for each group, and the bf16
+// scales/biases of rows r0+2t and r0+2t+1 for the four groups (8 bytes each).
+// load() only issues global loads, so it can run before activation staging
+// or before a programmatic-dependent-launch wait.
+struct Q4MmaFrag4 {
+    uint2 w[4];
+    uint2 sa, sb, ba, bb;  // 4 bf16 each: scale/bias of row 2t (a) and 2t+1 (b)
+
+    __device__ __forceinline__ void load(const uint8_t* row_g, const uint16_t* s_row_2t, const uint16_t* b_row_2t,
+                                         uint32_t gpr, uint32_t grp0, int t) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w[j] = *reinterpret_cast<const uint2*>(row_g + (grp0 + j) * (kMmaGroup / 2) + 8 * t);
+        sa = *reinterpret_cast<const uint2*>(s_row_2t + grp0);
+        sb = *reinterpret_cast<const uint2*>(s_row_2t + gpr + grp0);
+        ba = *reinterpret_cast<const uint2*>(b_row_2t + grp0);
+        bb = *reinterpret_cast<const uint2*>(b_row_2t + gpr + grp0);
+    }
+
+    // Same fragment from a shared-memory copy of the tile: row_g is row r0+g,
+    // s_row_2t / b_row_2t are rows r0+2t of the scale / bias blocks, and
+    // `sstride` elements separate consecutive scale rows.
+    __device__ __forceinline__ void load_smem(const uint8_t* row_g, const uint16_t* s_row_2t, const uint16_t* b_row_2t,
+                                              uint32_t sstride, uint32_t grp0, int t) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w[j] = *reinterpret_cast<const uint2*>(row_g + (grp0 + j) * (kMmaGroup / 2) + 8 * t);
+        sa = *reinterpret_cast<const uint2*>(s_row_2t + grp0);
+        sb = *reinterpret_cast<const uint2*>(s_row_2t + sstride + grp0);
+        ba = *reinterpret_cast<const uint2*>(b_row_2t + grp0);
+        bb = *reinterpret_cast<const uint2*>(b_row_2t + sstride + grp0);
+    }
+
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = make_uint2(0, 0);
+        sa = sb = ba = bb = make_uint2(0, 0);
+    }
+
+    static __device__ __forceinline__ float pick(const uint2& v, int j) {
+        const uint32_t word = (j < 2) ? v.x : v.y;
+        return (j & 1) ? __uint_as_float(word & 0xffff0000u) : __uint_as_float(word << 16);
+    }
+
+    // acc[0..1]: token g x rows 2t / 2t+1; acc[2..3]: token g+8 (kTok16).
+    // With kLo the residue rows g+8 are folded into acc[0..1].
+    template <bool kLo, bool kTok16>
+    __device__ __forceinline__ void compute(const ActTile& tile, uint32_t grp0, int g, int t, float (&acc)[4]) const {
+        float X[4], X2[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            X[j] = tile.gsum[g * tile.groups + grp0 + j];
+            X2[j] = kTok16 ? tile.gsum[(g + 8) * tile.groups + grp0 + j] : 0.f;
+        }
+        compute_x<kLo, kTok16>(tile, grp0, g, t, X, X2, acc);
+    }
+
+    // Same with the activation group sums supplied by the caller (X: token g,
+    // X2: token g+8).
+    template <bool kLo, bool kTok16>
+    __device__ __forceinline__ void compute_x(const ActTile& tile, uint32_t grp0, int g, int t, const float (&X)[4],
+                                              const float (&X2)[4], float (&acc)[4]) const {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t wd = (grp0 + j) * 8 + 2 * t;
+            const uint4 xa0 = tile.act[g * tile.stride + wd];
+            const uint4 xa1 = tile.act[g * tile.stride + wd + 1];
+            uint4 xb0 = make_uint4(0, 0, 0, 0), xb1 = make_uint4(0, 0, 0, 0);
+            if (kLo || kTok16) {
+                xb0 = tile.act[(g + 8) * tile.stride + wd];
+                xb1 = tile.act[(g + 8) * tile.stride + wd + 1];
+            }
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t words[2] = {w[j].x, w[j].y};
+            const uint4 xa[2] = {xa0, xa1}, xb[2] = {xb0, xb1};
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const uint32_t q = words[m];
+                const uint32_t b0p = (q & 0x000F000Fu) | kBf16Offset;
+                const uint32_t b1p = ((q >> 4) & 0x000F000Fu) | kBf16Offset;
+                const uint32_t b0q = ((q >> 8) & 0x000F000Fu) | kBf16Offset;
+                const uint32_t b1q = ((q >> 12) & 0x000F000Fu) | kBf16Offset;
+                mma_bf16_16816(d, xa[m].x, xb[m].x, xa[m].y, xb[m].y, b0p, b1p);
+                mma_bf16_16816(d, xa[m].z, xb[m].z, xa[m].w, xb[m].w, b0q, b1q);
+            }
+            const float s0 = pick(sa, j), s1 = pick(sb, j);
+            const float c0 = fmaf(-128.f, s0, pick(ba, j));
+            const float c1 = fmaf(-128.f, s1, pick(bb, j));
+            if (kLo) {
+                acc[0] = fmaf(s0, d[0] + d[2], fmaf(c0, X[j], acc[0]));
+                acc[1] = fmaf(s1, d[1] + d[3], fmaf(c1, X[j], acc[1]));
+            } else {
+                acc[0] = fmaf(s0, d[0], fmaf(c0, X[j], acc[0]));
+                acc[1] = fmaf(s1, d[1], fmaf(c1, X[j], acc[1]));
+                if (kTok16) {
+                    acc[2] = fmaf(s0, d[2], fmaf(c0, X2[j], acc[2]));
+                    acc[3] = fmaf(s1, d[3], fmaf(c1, X2[j], acc[3]));
+                }
+            }
+        }
+    }
+};
+
+}  // namespace pbmoe

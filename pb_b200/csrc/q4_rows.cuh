@@ -34,31 +34,72 @@ __host__ __device__ inline uint32_t ilog2_u32(uint32_t v) {
 // Stage `ntok` activation rows (row stride `x_stride` elements) into shared
 // memory as f32, plus each 32-column chunk's even/odd sums. Layout per token:
 // xs[t * cols + xs_index(j, c)], xe[t * chunks + j], xo[t * chunks + j].
-// Needs cols % 32 == 0.
-// `rows_idx` maps local token t to the source row (NULL = identity).
+// Needs cols % 32 == 0 and 16-byte aligned rows. `rows_idx` maps local token t
+// to the source row (NULL = identity).
+//
+// Phase 1 issues every 16-byte load of the thread before storing any of them
+// (one memory round trip for the whole staging); phase 2 forms the chunk sums
+// from shared memory. Ends with __syncthreads.
 template <typename XT>
 __device__ void stage_x_fast(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx,
                              int ntok, uint32_t cols, float* xs, float* xe, float* xo) {
+    constexpr uint32_t kPerVec = 16 / sizeof(XT);  // elements per 16-byte vector
+    constexpr int kBatch = 8;                       // vectors in flight per thread
     const uint32_t chunks = cols >> 5;
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int nwarps = blockDim.x >> 5;
-    for (int t = 0; t < ntok; ++t) {
-        const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
-        const XT* xr = x + src * x_stride;
-        for (uint32_t j = warp; j < chunks; j += nwarps) {
-            float v = load_act<XT>(xr, (static_cast<size_t>(j) << 5) + lane);
-            xs[static_cast<size_t>(t) * cols + xs_index(j, lane)] = v;
-            float e = (lane & 1) ? 0.f : v;
-            float o = (lane & 1) ? v : 0.f;
-            e = warp_sum(e);
-            o = warp_sum(o);
-            if (lane == 0) {
-                xe[t * chunks + j] = e;
-                xo[t * chunks + j] = o;
+    const uint32_t vec_per_row = cols / kPerVec;
+    const uint32_t total = static_cast<uint32_t>(ntok) * vec_per_row;
+    for (uint32_t base = 0; base < total; base += kBatch * blockDim.x) {
+        uint4 v[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            if (idx < total) {
+                const uint32_t t = idx / vec_per_row, q = idx - t * vec_per_row;
+                const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
+                v[i] = *reinterpret_cast<const uint4*>(x + src * x_stride + static_cast<size_t>(q) * kPerVec);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            if (idx < total) {
+                const uint32_t t = idx / vec_per_row, q = idx - t * vec_per_row;
+                const uint32_t c0 = q * kPerVec;
+                float* dst = xs + static_cast<size_t>(t) * cols;
+                const uint32_t j = c0 >> 5;
+                if constexpr (sizeof(XT) == 2) {
+                    // eight bf16 columns = two swizzled float4
+                    *reinterpret_cast<float4*>(dst + xs_index(j, c0 & 31u)) =
+                        make_float4(__uint_as_float(v[i].x << 16), __uint_as_float(v[i].x & 0xffff0000u),
+                                    __uint_as_float(v[i].y << 16), __uint_as_float(v[i].y & 0xffff0000u));
+                    *reinterpret_cast<float4*>(dst + xs_index(j, (c0 & 31u) + 4)) =
+                        make_float4(__uint_as_float(v[i].z << 16), __uint_as_float(v[i].z & 0xffff0000u),
+                                    __uint_as_float(v[i].w << 16), __uint_as_float(v[i].w & 0xffff0000u));
+                } else {
+                    // four consecutive f32 columns = one swizzled float4
+                    *reinterpret_cast<float4*>(dst + xs_index(j, c0 & 31u)) =
+                        make_float4(__uint_as_float(v[i].x), __uint_as_float(v[i].y), __uint_as_float(v[i].z),
+                                    __uint_as_float(v[i].w));
+                }
             }
         }
     }
+    __syncthreads();
+    const uint32_t nsum = static_cast<uint32_t>(ntok) * chunks;
+    for (uint32_t i = threadIdx.x; i < nsum; i += blockDim.x) {
+        const uint32_t t = i / chunks, j = i - t * chunks;
+        const float4* c4 = reinterpret_cast<const float4*>(xs + static_cast<size_t>(t) * cols + (j << 5));
+        float e = 0.f, o = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 f = c4[k];
+            e += f.x + f.z;
+            o += f.y + f.w;
+        }
+        xe[i] = e;
+        xo[i] = o;
+    }
+    __syncthreads();
 }
 
 // Generic staging (any cols): f32 copy only.
@@ -77,27 +118,22 @@ __device__ void stage_x_generic(const XT* __restrict__ x, size_t x_stride, const
 // The warp is split into 32/LPR lane groups; a lane group owns one row at a
 // time and its LPR lanes stride over the row's 16-byte chunks (chunk j goes to
 // lane j % LPR), so every warp-wide load instruction reads 16*32 contiguous
-// bytes per row group. All NR rows' first CPL chunks are loaded before any
-// arithmetic so that NR*CPL*16 bytes per lane are in flight.
+// bytes per row group. A fragment holds one block of LPR*CPL chunks of NR rows
+// in registers: load() issues all of the block's loads at once, accumulate()
+// consumes them, so a kernel can start the weight loads before it stages the
+// activations.
 //
 // row_packed[r] / row_scale[r] / row_bias[r] are this lane group's row r
-// (NULL = absent row, contributes 0). acc[r][t] receives the lane's partial
-// sum_c (q*s+b)*x_t[c]; reduce across the LPR lanes afterwards.
-template <int LPR, int NR, int CPL, int NT>
-__device__ __forceinline__ void q4_rows_partial(const uint8_t* const (&row_packed)[NR],
-                                                const uint16_t* const (&row_scale)[NR],
-                                                const uint16_t* const (&row_bias)[NR], const Q4Geom& g,
-                                                const float* xs, const float* xe, const float* xo,
-                                                int ntok, float (&acc)[NR][NT]) {
-    const int li = threadIdx.x & (LPR - 1);
-#pragma unroll
-    for (int r = 0; r < NR; ++r)
-#pragma unroll
-        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+// (NULL packed = absent row, contributes 0). acc[r][t] receives the lane's
+// partial sum_c (q*s+b)*x_t[c]; reduce across the LPR lanes afterwards.
+template <int LPR, int NR, int CPL>
+struct Q4RowFrag {
+    uint4 w[NR][CPL];
+    float sc[NR][CPL], bi[NR][CPL];
 
-    for (uint32_t jb = 0; jb < g.chunks; jb += LPR * CPL) {
-        uint4 w[NR][CPL];
-        float sc[NR][CPL], bi[NR][CPL];
+    __device__ __forceinline__ void load(const uint8_t* const (&row_packed)[NR], const uint16_t* const (&row_scale)[NR],
+                                         const uint16_t* const (&row_bias)[NR], const Q4Geom& g, uint32_t jb) {
+        const int li = threadIdx.x & (LPR - 1);
 #pragma unroll
         for (int r = 0; r < NR; ++r) {
 #pragma unroll
@@ -115,6 +151,12 @@ __device__ __forceinline__ void q4_rows_partial(const uint8_t* const (&row_packe
                 }
             }
         }
+    }
+
+    template <int NT>
+    __device__ __forceinline__ void accumulate(const Q4Geom& g, uint32_t jb, const float* xs, const float* xe,
+                                               const float* xo, int ntok, float (&acc)[NR][NT]) const {
+        const int li = threadIdx.x & (LPR - 1);
 #pragma unroll
         for (int c = 0; c < CPL; ++c) {
             const uint32_t j = jb + c * LPR + li;
@@ -135,6 +177,24 @@ __device__ __forceinline__ void q4_rows_partial(const uint8_t* const (&row_packe
                 }
             }
         }
+    }
+};
+
+// Runs the fragment over all chunk blocks of the rows; `frag` must already
+// hold block 0 (frag.load(..., 0)).
+template <int LPR, int NR, int CPL, int NT>
+__device__ __forceinline__ void q4_rows_finish(Q4RowFrag<LPR, NR, CPL>& frag, const uint8_t* const (&row_packed)[NR],
+                                               const uint16_t* const (&row_scale)[NR],
+                                               const uint16_t* const (&row_bias)[NR], const Q4Geom& g,
+                                               const float* xs, const float* xe, const float* xo, int ntok,
+                                               float (&acc)[NR][NT]) {
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+    for (uint32_t jb = 0; jb < g.chunks; jb += LPR * CPL) {
+        if (jb > 0) frag.load(row_packed, row_scale, row_bias, g, jb);
+        frag.template accumulate<NT>(g, jb, xs, xe, xo, ntok, acc);
     }
 }
 

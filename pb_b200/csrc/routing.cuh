@@ -16,61 +16,96 @@ __device__ __forceinline__ uint32_t float_order_key(float f) {
 
 constexpr uint32_t kMaxTopK = 32;
 
-// One warp routes one token.
+// Copy one token's E logits from global memory (written by an earlier kernel
+// or CTA: read through L2) into shared memory, with every load of the lane in
+// flight at once. `s` must be 16-byte aligned; ends with __syncwarp.
+__device__ __forceinline__ void stage_logits_warp(const float* __restrict__ lg, uint32_t E, float* s) {
+    const int lane = threadIdx.x & 31;
+    if ((reinterpret_cast<uintptr_t>(lg) & 15u) == 0) {
+        const uint32_t n4 = E >> 2;
+        constexpr int kMax = 8;  // 8 x 128 floats per pass
+        for (uint32_t base = 0; base < n4; base += 32 * kMax) {
+            float4 v[kMax];
+#pragma unroll
+            for (int i = 0; i < kMax; ++i) {
+                const uint32_t q = base + i * 32 + lane;
+                if (q < n4) v[i] = __ldcg(reinterpret_cast<const float4*>(lg) + q);
+            }
+#pragma unroll
+            for (int i = 0; i < kMax; ++i) {
+                const uint32_t q = base + i * 32 + lane;
+                if (q < n4) reinterpret_cast<float4*>(s)[q] = v[i];
+            }
+        }
+        for (uint32_t e = (n4 << 2) + lane; e < E; e += 32) s[e] = __ldcg(lg + e);
+    } else {
+        for (uint32_t base = 0; base < E; base += 32 * 16) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t e = base + i * 32 + lane;
+                if (e < E) v[i] = __ldcg(lg + e);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t e = base + i * 32 + lane;
+                if (e < E) s[e] = v[i];
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// One warp routes one token whose E logits are in shared memory `s` (K <= 32).
 //
 // Selection reproduces routing_top_k_iter (math.rs:746-765) exactly: K slots
 // start as (expert 0, -inf); experts are visited in index order and an expert
 // replaces the FIRST slot holding the minimum value when its score is strictly
-// greater. Slots live in lanes 0..K-1. Experts are examined 32 at a time; only
-// lanes whose score beats the current minimum are candidates, and candidates
-// are replayed one by one in ascending expert order, recomputing the minimum
-// slot (lowest slot index on ties) before each, so the final slot contents and
-// order equal the sequential algorithm's. Experts that could not have been
-// inserted (score <= current minimum) are skipped, which the sequential
-// algorithm would also have done.
+// greater. Slots live in lanes 0..K-1 (slot index = lane). Experts are examined
+// 32 at a time: only lanes whose score beats the current minimum are
+// candidates, and they are replayed one by one in ascending expert order; after
+// each replacement the minimum slot is found again (__reduce_min_sync on an
+// order-preserving key, lowest slot on ties) and the remaining candidates are
+// pruned against it. Experts that could not have been inserted (score <= the
+// current minimum) are skipped, as the sequential loop would have skipped them.
 //
 // Weights follow routing_softmax_top_k (math.rs:771-783): p_k = exp(s_k - max)
 // * (1/sum_e exp(s_e - max)); then the configured normalisation over the K
 // selected p_k (summed in slot order, scheduler/expert_access.rs:80-133) and
 // the routed scaling factor. Invalid sums latch PBMOE_DEV_ERR_ROUTE_WEIGHTS
 // (where the reference bails) and write zero weights.
-__device__ void route_token_warp(const float* __restrict__ logits, uint32_t E, uint32_t K,
-                                 uint32_t normalization, float routed_scale, uint32_t* ids_out,
-                                 float* w_out, uint32_t* status) {
+__device__ void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
+                                 float routed_scale, uint32_t* ids_out, float* w_out, uint32_t* status) {
     const int lane = threadIdx.x & 31;
     const float NEG_INF = -__int_as_float(0x7f800000);
-
-    // max and sum of exp over all experts
     float m = NEG_INF;
-    for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, __ldcg(logits + e));
+    for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, s[e]);
     m = warp_max(m);
     float sum = 0.f;
-    for (uint32_t e = lane; e < E; e += 32) sum += expf(__ldcg(logits + e) - m);
+    for (uint32_t e = lane; e < E; e += 32) sum += expf(s[e] - m);
     sum = warp_sum(sum);
 
+    const bool is_slot = static_cast<uint32_t>(lane) < K;
     float sval = NEG_INF;
     uint32_t sid = 0;
-    const bool is_slot = static_cast<uint32_t>(lane) < K;
+    // current minimum slot (value mv, index mslot); all slots start at -inf
+    float mv = NEG_INF;
+    int mslot = 0;
     for (uint32_t base = 0; base < E; base += 32) {
         const uint32_t e = base + lane;
-        const float v = e < E ? __ldcg(logits + e) : NEG_INF;
-        // current minimum slot value (lower bound for pruning)
-        uint32_t key = is_slot ? float_order_key(sval) : 0xffffffffu;
-        uint32_t mk = __reduce_min_sync(kFull, key);
-        int mslot = __ffs(__ballot_sync(kFull, key == mk)) - 1;
-        float mv = __shfl_sync(kFull, sval, mslot);
+        const float v = e < E ? s[e] : NEG_INF;
         uint32_t cand = __ballot_sync(kFull, v > mv);
         while (cand) {
             const int src = __ffs(cand) - 1;
-            const float ve = __shfl_sync(kFull, v, src);
             cand &= cand - 1;
+            const float ve = __shfl_sync(kFull, v, src);
             if (ve > mv) {  // warp-uniform: mv is the exact current minimum
                 if (lane == mslot) {
                     sval = ve;
                     sid = base + static_cast<uint32_t>(src);
                 }
-                key = is_slot ? float_order_key(sval) : 0xffffffffu;
-                mk = __reduce_min_sync(kFull, key);
+                const uint32_t key = is_slot ? float_order_key(sval) : 0xffffffffu;
+                const uint32_t mk = __reduce_min_sync(kFull, key);
                 mslot = __ffs(__ballot_sync(kFull, key == mk)) - 1;
                 mv = __shfl_sync(kFull, sval, mslot);
                 cand &= __ballot_sync(kFull, v > mv);
@@ -92,9 +127,8 @@ __device__ void route_token_warp(const float* __restrict__ logits, uint32_t E, u
     bool ok;
     float inv;
     if (normalization == PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR) {
-        const float floor_v = 6.103515625e-5f;
         ok = isfinite(ssum) && ssum >= 0.f;
-        inv = 1.0f / fmaxf(ssum, floor_v);
+        inv = 1.0f / fmaxf(ssum, 6.103515625e-5f);
     } else {
         ok = isfinite(ssum) && ssum > 0.f;
         inv = 1.0f / ssum;
@@ -110,6 +144,7 @@ __device__ void route_token_warp(const float* __restrict__ logits, uint32_t E, u
         ids_out[lane] = sid;
         w_out[lane] = w;
     }
+    __syncwarp();
 }
 
 // Block-wide exclusive scan of n <= 4096 u32 values in shared memory, in

@@ -146,6 +146,29 @@ def test_shared_expert_without_gate(ctx, oracle):
     _check_layer(ctx, oracle, w, 2, top_k=2, seed=3)
 
 
+@pytest.mark.parametrize("tokens,x_f32", [(3, True), (12, False), (9, True)])
+def test_tensor_core_path_i256(ctx, oracle, tokens, x_f32):
+    """Hidden 2048 / group 64 selects the tensor-core expert kernels; this
+    covers intermediate 256, f32 activations (hi/lo rows) and bf16 passes of
+    up to 16 tokens."""
+    import torch
+
+    from pb_b200 import synth
+
+    w = synth.MoeLayerWeights("cuda", seed=21, hidden=2048, num_experts=48, intermediate=256, group=64)
+    if x_f32:
+        g = synth.gen("cuda", 5)
+        x = synth.normal_bf16((tokens, w.hidden), 1.0, g, "cuda").float() * 1.37
+        out, nn, logits, ids, rw, sl, status = _run_layer(ctx, w, x, tokens, 8, out_dtype=torch.float32)
+        assert status == 0
+        ref_out, ref_ids, ref_w, ref_logits = _oracle_layer(oracle, w, x, 8)
+        safe = _safe_tokens(ref_logits, 8, w.hidden, x.cpu().numpy())
+        assert_close(out.cpu().numpy()[safe], ref_out[safe], what="f32 layer output")
+        assert np.array_equal(ids.cpu().numpy().view(np.uint32)[safe], ref_ids[safe])
+    else:
+        _check_layer(ctx, oracle, w, tokens, top_k=8, seed=13)
+
+
 @pytest.fixture(scope="module")
 def config1_layer():
     from pb_b200 import synth
