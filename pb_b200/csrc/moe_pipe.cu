@@ -1,27 +1,29 @@
 // moe_pipe.cu — persistent, asynchronously pipelined MoE expert kernels for
 // decode batches of at most 8 tokens (group-64 Q4 experts).
 //
-// One CTA per SM walks a strided list of work items. The weight bytes of each
-// item are moved by the SM's TMA engine (1-D cp.async.bulk, no multicast) into
-// one of several shared-memory stages, completing on that stage's mbarrier;
-// warp 0 refills a stage as soon as every warp has finished reading it, so
-// several items' bytes are always in flight per SM while the tensor cores
-// (mma.sync, q4_mma.cuh) consume the current one. Rows land in padded shared
-// rows so fragment loads are bank-conflict free.
+// Each CTA (8 warps) walks a strided list of work items. The bytes of each
+// item are moved into one of several shared-memory stages by 16-byte
+// cp.async copies that every thread of the CTA issues a share of, and each
+// thread's completion is counted on the stage's mbarrier; after the item's
+// compute the CTA synchronises once, refills the stage it just released with
+// the item `stages` ahead, and runs the item's epilogue. Several items' bytes
+// are therefore always in flight per SM while the tensor cores (mma.sync,
+// q4_mma.cuh) consume the current one. Rows land in padded shared rows so
+// fragment loads are bank-conflict free.
 //
 //   moe_up_pipe_kernel    item = (group, 8 intermediate rows): gate and up
 //       rows + their scales/biases; the batch's tokens stay resident in shared
 //       memory for the whole kernel. 8 warps = 8 K-slices, summed in shared
 //       memory; SwiGLU (silu(g)*u, shaders.metal:1699-1708) is written as bf16
 //       hi/lo pair slots + per-8 partial sums (MoeWs::h_perm), the down
-//       kernel's input layout.
+//       kernel's input layout, by one warp per routed token of the group.
 //   moe_down_pipe_kernel  item = (group, 64 down rows): rows, scales, and the
-//       group's routes' h_perm rows. Weights of the first stages are requested
-//       before the programmatic-dependent-launch wait (they do not depend on
-//       the up kernel).
+//       group's routes' h_perm rows; warp w owns rows 8w..8w+7. Weights of the
+//       first stages are requested before the programmatic-dependent-launch
+//       wait (they do not depend on the up kernel).
 //
 // Every mbarrier wait is bounded (kPipeWaitNs); on expiry the kernel latches
-// PBMOE_DEV_ERR_PIPE_TIMEOUT, waits (bounded) for its own copies, and returns.
+// PBMOE_DEV_ERR_PIPE_TIMEOUT, waits for its own copies, and returns.
 
 #include "kernels.h"
 #include "pipe.cuh"
@@ -29,7 +31,7 @@
 
 namespace pbmoe {
 
-// Stage counts: bf16 activations run two CTAs per SM (3 stages each, 18 warps
+// Stage counts: bf16 activations run two CTAs per SM (3 stages each, 16 warps
 // per SM); f32 activations keep a 16-row token tile and run one CTA per SM.
 constexpr int kUpStagesBf16 = 3;
 constexpr int kUpStagesF32 = 5;
@@ -52,12 +54,45 @@ static int device_sm_count() {
     return cached[dev];
 }
 
+// The layer-major group plan (written by the router kernel) copied into
+// shared memory once per CTA, so that per-item lookups are shared-memory
+// loads instead of dependent L2 round trips. `cap_g` groups and `cap_r`
+// grouped positions fit (host-checked: T*K + 1 and T*K + T).
+struct PlanSmem {
+    uint32_t* expert;  // [cap_g]
+    uint32_t* start;   // [cap_g]
+    uint32_t* count;   // [cap_g]
+    uint32_t* token;   // [cap_r]
+    uint32_t* route;   // [cap_r]
+};
+
+__host__ __device__ inline size_t plan_smem_bytes(uint32_t cap_g, uint32_t cap_r) {
+    return (size_t(3) * cap_g + size_t(2) * cap_r) * 4;
+}
+
+__device__ inline PlanSmem plan_at(void* base, uint32_t cap_g, uint32_t cap_r) {
+    uint32_t* p = reinterpret_cast<uint32_t*>(base);
+    return {p, p + cap_g, p + 2 * cap_g, p + 3 * cap_g, p + 3 * cap_g + cap_r};
+}
+
+// All threads: copy the plan (ng groups, positions 0..npos) through L2.
+__device__ inline void load_plan(const MoeWs& ws, uint32_t ng, uint32_t npos, const PlanSmem& pl) {
+    for (uint32_t i = threadIdx.x; i < ng; i += blockDim.x) {
+        pl.expert[i] = __ldcg(ws.group_expert + i);
+        pl.start[i] = __ldcg(ws.group_start + i);
+        pl.count[i] = __ldcg(ws.group_count + i);
+    }
+    for (uint32_t i = threadIdx.x; i < npos; i += blockDim.x) {
+        pl.token[i] = __ldcg(ws.group_tokens + i);
+        pl.route[i] = __ldcg(ws.group_routes + i);
+    }
+}
+
 // ---------------------------------------------------------------- layouts
 struct UpStage {
     uint32_t rs;     // padded row stride (bytes) = H/2 + 32
     uint32_t gate, up, gs, gb, us, ub;
     uint32_t bytes;  // stage size, multiple of 128
-    uint32_t tx;     // bytes delivered per item
 };
 
 __host__ __device__ inline UpStage up_stage(uint32_t H) {
@@ -71,15 +106,15 @@ __host__ __device__ inline UpStage up_stage(uint32_t H) {
     L.us = L.gb + sb;
     L.ub = L.us + sb;
     L.bytes = (L.ub + sb + 127) / 128 * 128;
-    L.tx = 16 * (H / 2) + 4 * sb;
     return L;
 }
 
-__host__ __device__ inline size_t up_pipe_smem(uint32_t H, bool lo) {
+__host__ __device__ inline size_t up_pipe_smem(uint32_t H, bool lo, uint32_t cap_g, uint32_t cap_r) {
     const UpStage L = up_stage(H);
     const int stages = lo ? kUpStagesF32 : kUpStagesBf16;
-    // stages, token tile, 2 x 8 warps x 128 partial sums, 64-entry h buffer, flags, mbarriers
-    return size_t(stages) * L.bytes + act_tile_bytes(H, lo ? 16 : 8) + 2 * 8 * 128 * 4 + 64 * 4 + 16 + stages * 8;
+    // stages, token tile, 2 x 8 warps x 128 partial sums, flags, mbarriers, plan
+    return size_t(stages) * L.bytes + act_tile_bytes(H, lo ? 16 : 8) + 2 * 8 * 128 * 4 + 16 + stages * 8 +
+           plan_smem_bytes(cap_g, cap_r);
 }
 
 struct DownStage {
@@ -87,8 +122,6 @@ struct DownStage {
     uint32_t w, s, b, act, part;
     uint32_t part_stride;  // padded stride of the per-route partial-sum rows
     uint32_t bytes;
-    uint32_t tx_w;     // weight + scale bytes per item
-    uint32_t tx_route; // h bytes per route
 };
 
 __host__ __device__ inline DownStage down_stage(uint32_t I) {
@@ -103,37 +136,22 @@ __host__ __device__ inline DownStage down_stage(uint32_t I) {
     L.part = (L.part + 15) / 16 * 16;
     L.part_stride = (I / 8) * 4 + 32;
     L.bytes = (L.part + 8 * L.part_stride + 127) / 128 * 128;
-    L.tx_w = 64 * (I / 2) + 2 * sb;
-    L.tx_route = 2 * (I / 8) * 16 + (I / 8) * 4;
     return L;
 }
 
-__host__ __device__ inline size_t down_pipe_smem(uint32_t I) {
-    return size_t(kDownStages) * down_stage(I).bytes + 16 + kDownStages * 8;
+__host__ __device__ inline size_t down_pipe_smem(uint32_t I, uint32_t cap_g, uint32_t cap_r) {
+    return size_t(kDownStages) * down_stage(I).bytes + 16 + kDownStages * 8 + plan_smem_bytes(cap_g, cap_r);
 }
 
-// Bounded drain of every stage's outstanding phase after a failure.
-__device__ void drain_stages(uint64_t* bar, int stages, const uint32_t* pending_parity, const bool* pending) {
-    for (int s = 0; s < stages; ++s)
-        if (pending[s]) mbar_wait_bounded(&bar[s], pending_parity[s], 100000000ull);
-}
-
-// Warp roles: warps 0..7 compute, warp 8 ("PE") produces copies and runs
-// the epilogue. Compute warps never wait on a CTA-wide barrier: they wait on
-// the stage's mbarrier (data), arrive on named barrier READY(s) once they have
-// finished reading stage s (and, for the up kernel, written their partial
-// sums), and - up kernel only - sync on FREE(p) before overwriting the
-// double-buffered partial-sum area p that the PE warp reads.
-constexpr int kComputeWarps = 8;
-constexpr int kPipeCtaThreads = (kComputeWarps + 1) * 32;
-__device__ __forceinline__ int bar_ready(int s) { return 1 + s; }   // ids 1..stages (<= 6)
-__device__ __forceinline__ int bar_free(int p) { return 7 + p; }    // ids 7, 8
+constexpr int kWarps = 8;
+constexpr int kPipeThreads = kWarps * 32;
 
 // ---------------------------------------------------------------- up
 template <typename XT>
-__global__ void __launch_bounds__(kPipeCtaThreads, UpCfg<XT>::kCtasPerSm)
+__global__ void __launch_bounds__(kPipeThreads, UpCfg<XT>::kCtasPerSm)
 moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8_t* __restrict__ experts,
-                   const uint8_t* __restrict__ shared_slot, MoeLayoutDev Ld, MoeWs ws) {
+                   const uint8_t* __restrict__ shared_slot, MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g,
+                   uint32_t cap_r) {
     constexpr bool kLo = sizeof(XT) == 4;
     constexpr int kUpStages = UpCfg<XT>::kStages;
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -141,314 +159,276 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     const UpStage SL = up_stage(H);
     unsigned char* stages = smem_raw;
     const ActTile tile = act_tile_at(stages + kUpStages * SL.bytes, H, kLo ? 16 : 8);
+    // partial sums: [2 buffers][8 warps][gate 64 | up 64], entry tok*8 + row
     float* red = reinterpret_cast<float*>(stages + kUpStages * SL.bytes + act_tile_bytes(H, kLo ? 16 : 8));
-    float* hbuf = red + 2 * kComputeWarps * 2 * 64;  // [8 routes][8 rows]
-    uint32_t* flags = reinterpret_cast<uint32_t*>(hbuf + 64);  // [0] error, [1] stop
+    uint32_t* flags = reinterpret_cast<uint32_t*>(red + 2 * kWarps * 128);  // [0] error
     uint64_t* bar = reinterpret_cast<uint64_t*>(flags + 4);
+    const PlanSmem pl = plan_at(bar + kUpStages, cap_g, cap_r);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t tiles = I / 8;
     const uint32_t gpr = H / kMmaGroup;
-    const uint32_t gps = gpr / kComputeWarps;  // groups per warp K-slice (multiple of 4)
+    const uint32_t gps = gpr / kWarps;  // groups per warp K-slice (multiple of 4)
     const size_t hps = hperm_stride(I);
 
     pdl_wait();
-    const uint32_t total = __ldcg(ws.num_groups) * tiles;
+    const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
+    const uint32_t total = ng * tiles;
     if (blockIdx.x >= total) return;
     const uint32_t my_items = (total - blockIdx.x + gridDim.x - 1) / gridDim.x;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kUpStages; ++s) mbar_init(&bar[s], 1);
+        for (int s = 0; s < kUpStages; ++s) mbar_init(&bar[s], kPipeThreads);  // one arrival per thread
         flags[0] = 0;
-        flags[1] = 0;
         fence_mbar_init();
     }
+    load_plan(ws, ng, cap_r, pl);
     __syncthreads();
 
-    auto slot_of = [&](uint32_t gi) -> const uint8_t* {
-        const uint32_t e = __ldcg(ws.group_expert + gi);
-        return e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
-    };
-    // PE warp: request item k into stage s
+    // Every thread: its share of item k's copies into stage s - warp w takes
+    // weight rows 2w, 2w+1 of the 16 (8 gate, 8 up), warps 0-3 one 8-row
+    // scale/bias block each - then its completion arrival on the stage.
     auto issue = [&](uint32_t k, int s) {
         const uint32_t gi = k / tiles, i0 = (k % tiles) * 8;
-        const uint8_t* slot = slot_of(gi);
+        const uint32_t e = pl.expert[gi];
+        const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
         unsigned char* st = stages + s * SL.bytes;
-        if (lane == 0) mbar_arrive_expect_tx(&bar[s], SL.tx);
-        __syncwarp();
-        if (lane < 8) {
-            bulk_g2s(st + SL.gate + lane * SL.rs, slot + Ld.off[0] + static_cast<size_t>(i0 + lane) * (H / 2), H / 2,
-                     &bar[s]);
-        } else if (lane < 16) {
-            const int r = lane - 8;
-            bulk_g2s(st + SL.up + r * SL.rs, slot + Ld.off[3] + static_cast<size_t>(i0 + r) * (H / 2), H / 2, &bar[s]);
-        } else if (lane < 20) {
-            const int c = lane - 16;  // gs, gb, us, ub
-            const uint32_t dst[4] = {SL.gs, SL.gb, SL.us, SL.ub};
-            const uint64_t off[4] = {Ld.off[1], Ld.off[2], Ld.off[4], Ld.off[5]};
-            bulk_g2s(st + dst[c], slot + off[c] + static_cast<size_t>(i0) * (H / 32), 8 * (H / 32), &bar[s]);
+        const uint32_t rb = H / 2;  // bytes of one weight row
+        const bool up_rows = warp >= 4;
+        const uint32_t r = 2 * (warp & 3);
+        const uint8_t* src = slot + Ld.off[up_rows ? 3 : 0] + static_cast<size_t>(i0 + r) * rb;
+        unsigned char* dst = st + (up_rows ? SL.up : SL.gate) + r * SL.rs;
+        for (uint32_t c = lane * 16; c < rb; c += 512) {
+            cp_async16(dst + c, src + c);
+            cp_async16(dst + SL.rs + c, src + rb + c);
         }
+        if (warp < 4) {
+            const uint32_t sb = 8 * (H / 32);  // one 8-row block of H/64 bf16 per row
+            const uint32_t dsts[4] = {SL.gs, SL.gb, SL.us, SL.ub};
+            const uint64_t offs[4] = {Ld.off[1], Ld.off[2], Ld.off[4], Ld.off[5]};
+            for (uint32_t c = lane * 16; c < sb; c += 512)
+                cp_async16(st + dsts[warp] + c, slot + offs[warp] + static_cast<size_t>(i0) * (H / 32) + c);
+        }
+        cp_async_arrive(&bar[s]);
     };
 
-    if (warp == kComputeWarps) {
-        for (int j = 0; j < kUpStages && static_cast<uint32_t>(j) < my_items; ++j) issue(blockIdx.x + j * gridDim.x, j);
-    }
-    // the batch's tokens stay resident for the whole kernel (all 288 threads stage them)
+    for (int j = 0; j < kUpStages && static_cast<uint32_t>(j) < my_items; ++j) issue(blockIdx.x + j * gridDim.x, j);
+    // the batch's tokens stay resident for the whole kernel
     if constexpr (kLo)
         stage_act_mma<XT>(x, H, nullptr, static_cast<int>(T), H, tile);
     else
         stage_act_rows8_tok<XT>(x, H, static_cast<int>(T), H, tile);
-    // Every CTA of this grid is resident (one per SM), so the down kernel may
-    // be scheduled now: its CTAs take SMs as these exit and prefetch weights
-    // while the rest of this grid finishes (it waits for all of it before
-    // reading h_perm).
+    // Every CTA of this grid is resident, so the down kernel may be scheduled
+    // now: its CTAs take SMs as these exit and prefetch weights while the
+    // rest of this grid finishes (it waits for all of it before reading h_perm).
     pdl_launch_dependents();
 
-    if (warp < kComputeWarps) {
-        const uint32_t grp0 = warp * gps;
-        for (uint32_t j = 0; j < my_items; ++j) {
-            const int s = static_cast<int>(j % kUpStages);
-            const int p = static_cast<int>(j & 1u);
-            if (j >= 2) {
-                named_sync(bar_free(p), kPipeCtaThreads);  // PE has consumed red[p] of item j-2
-                if (*reinterpret_cast<volatile uint32_t*>(&flags[1])) break;
+    const uint32_t grp0 = warp * gps;
+    for (uint32_t j = 0; j < my_items; ++j) {
+        const int s = static_cast<int>(j % kUpStages);
+        const int p = static_cast<int>(j & 1u);
+        const uint32_t k = blockIdx.x + j * gridDim.x;
+        const bool ok = mbar_wait_bounded(&bar[s], (j / kUpStages) & 1u, kPipeWaitNs);
+        float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+            const unsigned char* st = stages + s * SL.bytes;
+            const uint16_t* gs = reinterpret_cast<const uint16_t*>(st + SL.gs) + (2 * t) * gpr;
+            const uint16_t* gb = reinterpret_cast<const uint16_t*>(st + SL.gb) + (2 * t) * gpr;
+            const uint16_t* us = reinterpret_cast<const uint16_t*>(st + SL.us) + (2 * t) * gpr;
+            const uint16_t* ub = reinterpret_cast<const uint16_t*>(st + SL.ub) + (2 * t) * gpr;
+            for (uint32_t b = 0; b < gps; b += 4) {
+                Q4MmaFrag4 fg, fu;
+                fg.load_smem(st + SL.gate + g * SL.rs, gs, gb, gpr, grp0 + b, t);
+                fu.load_smem(st + SL.up + g * SL.rs, us, ub, gpr, grp0 + b, t);
+                q4_mma_pair<kLo>(fg, fu, tile, grp0 + b, g, t, ag, au);
             }
-            const bool ok = mbar_wait_bounded(&bar[s], (j / kUpStages) & 1u, kPipeWaitNs);
-            float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
-            if (ok) {
-                const unsigned char* st = stages + s * SL.bytes;
-                const uint16_t* gs = reinterpret_cast<const uint16_t*>(st + SL.gs) + (2 * t) * gpr;
-                const uint16_t* gb = reinterpret_cast<const uint16_t*>(st + SL.gb) + (2 * t) * gpr;
-                const uint16_t* us = reinterpret_cast<const uint16_t*>(st + SL.us) + (2 * t) * gpr;
-                const uint16_t* ub = reinterpret_cast<const uint16_t*>(st + SL.ub) + (2 * t) * gpr;
-                for (uint32_t b = 0; b < gps; b += 4) {
-                    Q4MmaFrag4 fg, fu;
-                    fg.load_smem(st + SL.gate + g * SL.rs, gs, gb, gpr, grp0 + b, t);
-                    fu.load_smem(st + SL.up + g * SL.rs, us, ub, gpr, grp0 + b, t);
-                    fg.compute<kLo, false>(tile, grp0 + b, g, t, ag);
-                    fu.compute<kLo, false>(tile, grp0 + b, g, t, au);
-                }
-            } else if (lane == 0) {
-                atomicOr(&flags[0], 1u);
-            }
-            float* rw = red + (p * kComputeWarps + warp) * 128;
-            rw[g * 8 + 2 * t] = ag[0];
-            rw[g * 8 + 2 * t + 1] = ag[1];
-            rw[64 + g * 8 + 2 * t] = au[0];
-            rw[64 + g * 8 + 2 * t + 1] = au[1];
-            named_arrive(bar_ready(s), kPipeCtaThreads);
+        } else if (lane == 0) {
+            atomicOr(&flags[0], 1u);
         }
-    } else {
-        // PE warp: refill + epilogue
-        for (uint32_t j = 0; j < my_items; ++j) {
-            const int s = static_cast<int>(j % kUpStages);
-            const int p = static_cast<int>(j & 1u);
-            named_sync(bar_ready(s), kPipeCtaThreads);  // stage s read, red[p] written by every compute warp
-            if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) {
-                if (lane == 0) {
-                    latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
-                    flags[1] = 1;
-                    uint32_t pp[kUpStages];
-                    bool pend[kUpStages];
-                    for (int q = 0; q < kUpStages; ++q) {
-                        const uint32_t jj = j + ((q - s + kUpStages) % kUpStages);
-                        pend[q] = jj < my_items && jj != j;
-                        pp[q] = (jj / kUpStages) & 1u;
-                    }
-                    drain_stages(bar, kUpStages, pp, pend);
-                }
-                __syncwarp();
-                if (j + 2 < my_items) named_arrive(bar_free(p), kPipeCtaThreads);
-                break;
-            }
-            const uint32_t k = blockIdx.x + j * gridDim.x;
-            if (j + kUpStages < my_items) issue(k + kUpStages * gridDim.x, s);
-            const uint32_t gi = k / tiles, ti = k % tiles;
-            const uint32_t start = __ldcg(ws.group_start + gi), n = __ldcg(ws.group_count + gi);
-            // lane (route q0 = lane/4, rows 2(lane%4), 2(lane%4)+1)
-            const uint32_t q0 = lane >> 2, rr = 2 * (lane & 3);
-            const float* rb = red + p * kComputeWarps * 128;
-            if (q0 < n) {
-                const uint32_t tok = __ldcg(ws.group_tokens + start + q0);
-                float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
-#pragma unroll
-                for (int w = 0; w < kComputeWarps; ++w) {
-                    g0 += rb[w * 128 + tok * 8 + rr];
-                    g1 += rb[w * 128 + tok * 8 + rr + 1];
-                    u0 += rb[w * 128 + 64 + tok * 8 + rr];
-                    u1 += rb[w * 128 + 64 + tok * 8 + rr + 1];
-                }
-                hbuf[q0 * 8 + rr] = g0 / (1.0f + expf(-g0)) * u0;
-                hbuf[q0 * 8 + rr + 1] = g1 / (1.0f + expf(-g1)) * u1;
-            }
-            __syncwarp();
-            // red[p] fully read: the compute warps may overwrite it (item j+2)
-            if (j + 2 < my_items) named_arrive(bar_free(p), kPipeCtaThreads);
-            if (q0 < n) {
-                // lane writes bf16 pair word c = lane%4: (h_c, h_{c+4}) as hi and lo
-                const uint32_t c = lane & 3;
-                const float a = hbuf[q0 * 8 + c], bv = hbuf[q0 * 8 + c + 4];
-                const uint32_t hi = f2_to_bf16x2(a, bv);
-                const uint32_t lo = f2_to_bf16x2(a - __uint_as_float(hi << 16), bv - __uint_as_float(hi & 0xffff0000u));
-                const uint32_t route = __ldcg(ws.group_routes + start + q0);
-                uint8_t* hr = ws.h_perm + static_cast<size_t>(route) * hps;
+        float* rw = red + (p * kWarps + warp) * 128;
+        *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(ag[0], ag[1]);
+        *reinterpret_cast<float2*>(rw + 64 + g * 8 + 2 * t) = make_float2(au[0], au[1]);
+        // Stage s is consumed, red[p] complete, the error flag visible. Item
+        // j+2 overwrites red[p] only after the next barrier, which every warp
+        // reaches after this item's epilogue.
+        __syncthreads();
+        if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) {
+            if (threadIdx.x == 0) latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+            break;
+        }
+        if (j + kUpStages < my_items) issue(k + kUpStages * gridDim.x, s);
+
+        // epilogue: warp q finishes the group's q-th route (token) of this tile
+        const uint32_t gi = k / tiles, ti = k % tiles;
+        const uint32_t n = pl.count[gi];
+        if (static_cast<uint32_t>(warp) < n) {
+            const uint32_t pos = pl.start[gi] + warp;
+            const uint32_t tok = pl.token[pos];
+            const float* rb = red + p * kWarps * 128;
+            // lane: row = lane/4 sums the partials of K-slices 2(lane%4), 2(lane%4)+1
+            const int row = lane >> 2, sl = lane & 3;
+            const float* r0 = rb + (2 * sl) * 128 + tok * 8 + row;
+            float gsum = r0[0] + r0[128];
+            float usum = r0[64] + r0[128 + 64];
+            gsum += __shfl_xor_sync(kFull, gsum, 1);
+            gsum += __shfl_xor_sync(kFull, gsum, 2);
+            usum += __shfl_xor_sync(kFull, usum, 1);
+            usum += __shfl_xor_sync(kFull, usum, 2);
+            const float h = gsum / (1.0f + expf(-gsum)) * usum;  // the four lanes of a row agree
+            // pair word c = (h_c, h_{c+4}) is formed in lane 4c from lane 4c+16
+            const float h4 = __shfl_down_sync(kFull, h, 16);
+            float part = h;
+            part += __shfl_xor_sync(kFull, part, 4);
+            part += __shfl_xor_sync(kFull, part, 8);
+            part += __shfl_xor_sync(kFull, part, 16);
+            uint8_t* hr = ws.h_perm + static_cast<size_t>(pl.route[pos]) * hps;
+            if (lane < 16 && sl == 0) {
+                const uint32_t c = lane >> 2;
+                const uint32_t hi = f2_to_bf16x2(h, h4);
+                const uint32_t lo = f2_to_bf16x2(h - __uint_as_float(hi << 16), h4 - __uint_as_float(hi & 0xffff0000u));
                 reinterpret_cast<uint32_t*>(hr)[ti * 4 + c] = hi;
                 reinterpret_cast<uint32_t*>(hr + tiles * 16)[ti * 4 + c] = lo;
-                if (c == 0) {
-                    float part = 0.f;
-#pragma unroll
-                    for (int r = 0; r < 8; ++r) part += hbuf[q0 * 8 + r];
-                    reinterpret_cast<float*>(hr + 2 * tiles * 16)[ti] = part;
-                }
             }
-            __syncwarp();
+            if (lane == 0) reinterpret_cast<float*>(hr + 2 * tiles * 16)[ti] = part;
         }
     }
+    cp_async_wait_all();  // no copy of this CTA outlives it
 }
 
 // ---------------------------------------------------------------- down
-__global__ void __launch_bounds__(kPipeCtaThreads, 2)
+__global__ void __launch_bounds__(kPipeThreads, 2)
 moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint8_t* __restrict__ shared_slot,
-                     MoeLayoutDev Ld, MoeWs ws) {
+                     MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g, uint32_t cap_r) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const uint32_t H = Ld.hidden, I = Ld.inter;
     const DownStage SL = down_stage(I);
     unsigned char* stages = smem_raw;
     uint32_t* flags = reinterpret_cast<uint32_t*>(stages + kDownStages * SL.bytes);
     uint64_t* bar = reinterpret_cast<uint64_t*>(flags + 4);
+    const PlanSmem pl = plan_at(bar + kDownStages, cap_g, cap_r);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t tiles = H / 64;
     const uint32_t gpr = I / kMmaGroup;  // 4 or 8
     const uint32_t wslots = I / 8;
     const size_t hps = hperm_stride(I);
+    const uint32_t rw0 = warp * 8;  // this warp's 8 rows within the 64-row tile
 
     // The group plan was written by the router kernel, which completed before
     // the up kernel passed its own wait; it is safe to read before this
     // kernel's wait (through L2).
-    const uint32_t total = __ldcg(ws.num_groups) * tiles;
+    const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
+    const uint32_t total = ng * tiles;
     if (blockIdx.x >= total) {
         pdl_wait();
         return;
     }
     const uint32_t my_items = (total - blockIdx.x + gridDim.x - 1) / gridDim.x;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kDownStages; ++s) mbar_init(&bar[s], 1);
+        for (int s = 0; s < kDownStages; ++s) mbar_init(&bar[s], kPipeThreads);  // one arrival per thread
         flags[0] = 0;
         fence_mbar_init();
     }
+    load_plan(ws, ng, cap_r, pl);
     __syncthreads();
 
-    auto slot_of = [&](uint32_t gi) -> const uint8_t* {
-        const uint32_t e = __ldcg(ws.group_expert + gi);
-        return e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
-    };
+    // Every thread: its share of item k's weight copies into stage s (warp w
+    // its own 8 rows; threads 0-127 the scale and bias blocks) ...
     auto issue_weights = [&](uint32_t k, int s) {
         const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
-        const uint32_t n = __ldcg(ws.group_count + gi);
-        const uint8_t* slot = slot_of(gi);
+        const uint32_t e = pl.expert[gi];
+        const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
         unsigned char* st = stages + s * SL.bytes;
-        if (lane == 0) mbar_arrive_expect_tx(&bar[s], SL.tx_w + n * SL.tx_route);
-        __syncwarp();
-        for (int r = lane; r < 64; r += 32)
-            bulk_g2s(st + SL.w + r * SL.rs, slot + Ld.off[6] + static_cast<size_t>(r0 + r) * (I / 2), I / 2, &bar[s]);
-        if (lane == 0) bulk_g2s(st + SL.s, slot + Ld.off[7] + static_cast<size_t>(r0) * (I / 32), 64 * (I / 32), &bar[s]);
-        if (lane == 1) bulk_g2s(st + SL.b, slot + Ld.off[8] + static_cast<size_t>(r0) * (I / 32), 64 * (I / 32), &bar[s]);
+        const uint32_t rb = I / 2;                     // bytes of one weight row
+        const uint32_t cpr_shift = __ffs(rb / 16) - 1;  // log2 of 16-byte chunks per row (I = 256 or 512)
+        const uint8_t* wsrc = slot + Ld.off[6] + static_cast<size_t>(r0 + rw0) * rb;
+        for (uint32_t c = lane; c < (8u << cpr_shift); c += 32) {
+            const uint32_t r = c >> cpr_shift, xo = c & ((1u << cpr_shift) - 1);
+            cp_async16(st + SL.w + (rw0 + r) * SL.rs + xo * 16, wsrc + static_cast<size_t>(c) * 16);
+        }
+        const uint32_t sb = 64 * (I / 32);
+        const size_t soff = static_cast<size_t>(r0) * (I / 32);
+        for (uint32_t c = threadIdx.x * 16; c < sb; c += kPipeThreads * 16) {
+            cp_async16(st + SL.s + c, slot + Ld.off[7] + soff + c);
+            cp_async16(st + SL.b + c, slot + Ld.off[8] + soff + c);
+        }
     };
+    // ... and of the group's routed activations: warp p copies route p's hi
+    // and lo bf16 rows of h (pair order) and its per-8 partial sums.
     auto issue_h = [&](uint32_t k, int s) {
         const uint32_t gi = k / tiles;
-        const uint32_t start = __ldcg(ws.group_start + gi), n = __ldcg(ws.group_count + gi);
+        const uint32_t n = pl.count[gi];
+        if (static_cast<uint32_t>(warp) >= n) return;
         unsigned char* st = stages + s * SL.bytes;
         const ActTile tile = act_tile_at(st + SL.act, I, 16);
-        for (uint32_t c = lane; c < 3 * n; c += 32) {
-            const uint32_t p = c / 3, part = c % 3;
-            const uint8_t* hr = ws.h_perm + static_cast<size_t>(__ldcg(ws.group_routes + start + p)) * hps;
-            if (part == 0)
-                bulk_g2s(tile.act + p * tile.stride, hr, wslots * 16, &bar[s]);
-            else if (part == 1)
-                bulk_g2s(tile.act + (p + 8) * tile.stride, hr + wslots * 16, wslots * 16, &bar[s]);
-            else
-                bulk_g2s(st + SL.part + p * SL.part_stride, hr + 2 * wslots * 16, wslots * 4, &bar[s]);
+        const uint32_t p = warp;
+        const uint8_t* hr = ws.h_perm + static_cast<size_t>(pl.route[pl.start[gi] + p]) * hps;
+        for (uint32_t c = lane; c < wslots; c += 32) {
+            cp_async16(tile.act + p * tile.stride + c, hr + c * 16);
+            cp_async16(tile.act + (p + 8) * tile.stride + c, hr + (wslots + c) * 16);
         }
+        for (uint32_t c = lane; c < wslots / 4; c += 32)
+            cp_async16(st + SL.part + p * SL.part_stride + c * 16, hr + 2 * wslots * 16 + c * 16);
     };
 
-    if (warp == kComputeWarps) {
-        for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j)
-            issue_weights(blockIdx.x + j * gridDim.x, j);
-    }
-    pdl_wait();  // h_perm comes from the up kernel
+    for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j)
+        issue_weights(blockIdx.x + j * gridDim.x, j);
+    pdl_wait();               // h_perm comes from the up kernel
     pdl_launch_dependents();  // the combine kernel waits for this whole grid
-    if (warp == kComputeWarps) {
-        for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j)
-            issue_h(blockIdx.x + j * gridDim.x, j);
+    for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j) {
+        issue_h(blockIdx.x + j * gridDim.x, j);
+        cp_async_arrive(&bar[j]);
     }
 
-    if (warp < kComputeWarps) {
-        const uint32_t rw0 = warp * 8;  // this warp's 8 rows within the 64-row tile
-        for (uint32_t j = 0; j < my_items; ++j) {
-            const int s = static_cast<int>(j % kDownStages);
-            const bool ok = mbar_wait_bounded(&bar[s], (j / kDownStages) & 1u, kPipeWaitNs);
-            if (ok) {
-                const uint32_t k = blockIdx.x + j * gridDim.x;
-                const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
-                const uint32_t start = __ldcg(ws.group_start + gi), n = __ldcg(ws.group_count + gi);
-                const unsigned char* st = stages + s * SL.bytes;
-                const ActTile tile = act_tile_at(const_cast<unsigned char*>(st) + SL.act, I, 16);
-                const uint16_t* ds = reinterpret_cast<const uint16_t*>(st + SL.s) + (rw0 + 2 * t) * gpr;
-                const uint16_t* db = reinterpret_cast<const uint16_t*>(st + SL.b) + (rw0 + 2 * t) * gpr;
-                const float* prow = reinterpret_cast<const float*>(st + SL.part + g * SL.part_stride);
-                float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                for (uint32_t b = 0; b < gpr; b += 4) {
-                    // route g's activation sums of groups b..b+3: each lane adds two of the
-                    // eight per-8 partials of a group, the quad finishes the sum
-                    float X[4], X2[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t j = 0; j < my_items; ++j) {
+        const int s = static_cast<int>(j % kDownStages);
+        const uint32_t k = blockIdx.x + j * gridDim.x;
+        const bool ok = mbar_wait_bounded(&bar[s], (j / kDownStages) & 1u, kPipeWaitNs);
+        if (ok) {
+            const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
+            const uint32_t start = pl.start[gi], n = pl.count[gi];
+            const unsigned char* st = stages + s * SL.bytes;
+            const ActTile tile = act_tile_at(const_cast<unsigned char*>(st) + SL.act, I, 16);
+            const uint16_t* ds = reinterpret_cast<const uint16_t*>(st + SL.s) + (rw0 + 2 * t) * gpr;
+            const uint16_t* db = reinterpret_cast<const uint16_t*>(st + SL.b) + (rw0 + 2 * t) * gpr;
+            const float* prow = reinterpret_cast<const float*>(st + SL.part + g * SL.part_stride);
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (uint32_t b = 0; b < gpr; b += 4) {
+                // route g's activation sums of groups b..b+3: each lane adds two of the
+                // eight per-8 partials of a group, the quad finishes the sum
+                float X[4], X2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const float2 pv = *reinterpret_cast<const float2*>(prow + (b + jj) * 8 + 2 * t);
-                        float v = pv.x + pv.y;
-                        v += __shfl_xor_sync(kFull, v, 1);
-                        v += __shfl_xor_sync(kFull, v, 2);
-                        X[jj] = v;
-                    }
-                    Q4MmaFrag4 f;
-                    f.load_smem(st + SL.w + (rw0 + g) * SL.rs, ds, db, gpr, b, t);
-                    f.compute_x<true, false>(tile, b, g, t, X, X2, acc);
+                for (int jj = 0; jj < 4; ++jj) {
+                    const float2 pv = *reinterpret_cast<const float2*>(prow + (b + jj) * 8 + 2 * t);
+                    float v = pv.x + pv.y;
+                    v += __shfl_xor_sync(kFull, v, 1);
+                    v += __shfl_xor_sync(kFull, v, 2);
+                    X[jj] = v;
                 }
-                if (static_cast<uint32_t>(g) < n) {
-                    const uint32_t route = __ldcg(ws.group_routes + start + g);
-                    *reinterpret_cast<float2*>(ws.y + static_cast<size_t>(route) * H + r0 + rw0 + 2 * t) =
-                        make_float2(acc[0], acc[1]);
-                }
-            } else if (lane == 0) {
-                atomicOr(&flags[0], 1u);
+                Q4MmaFrag4 f;
+                f.load_smem(st + SL.w + (rw0 + g) * SL.rs, ds, db, gpr, b, t);
+                f.compute_x<true, false>(tile, b, g, t, X, X2, acc);
             }
-            named_arrive(bar_ready(s), kPipeCtaThreads);
-            if (!ok) break;
+            if (static_cast<uint32_t>(g) < n) {
+                const uint32_t route = pl.route[start + g];
+                *reinterpret_cast<float2*>(ws.y + static_cast<size_t>(route) * H + r0 + rw0 + 2 * t) =
+                    make_float2(acc[0], acc[1]);
+            }
+        } else if (lane == 0) {
+            atomicOr(&flags[0], 1u);
         }
-    } else {
-        for (uint32_t j = 0; j < my_items; ++j) {
-            const int s = static_cast<int>(j % kDownStages);
-            named_sync(bar_ready(s), kPipeCtaThreads);  // stage s consumed by every compute warp
-            if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) {
-                if (lane == 0) {
-                    latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
-                    uint32_t pp[kDownStages];
-                    bool pend[kDownStages];
-                    for (int q = 0; q < kDownStages; ++q) {
-                        const uint32_t jj = j + ((q - s + kDownStages) % kDownStages);
-                        pend[q] = jj < my_items && jj != j;
-                        pp[q] = (jj / kDownStages) & 1u;
-                    }
-                    drain_stages(bar, kDownStages, pp, pend);
-                }
-                break;
-            }
-            if (j + kDownStages < my_items) {
-                const uint32_t kn = blockIdx.x + (j + kDownStages) * gridDim.x;
-                issue_weights(kn, s);
-                issue_h(kn, s);
-            }
+        __syncthreads();  // stage s consumed by every warp; error flag visible
+        if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) {
+            if (threadIdx.x == 0) latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+            break;
+        }
+        if (j + kDownStages < my_items) {
+            const uint32_t kn = k + kDownStages * gridDim.x;
+            issue_weights(kn, s);
+            issue_h(kn, s);
+            cp_async_arrive(&bar[s]);
         }
     }
+    cp_async_wait_all();  // no copy of this CTA outlives it
 }
 
 // ---------------------------------------------------------------- launch
@@ -457,7 +437,7 @@ static cudaError_t launch_pipe(const void* fn, dim3 grid, size_t smem, cudaStrea
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kPipeCtaThreads);
+    cfg.blockDim = dim3(kPipeThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -468,34 +448,47 @@ static cudaError_t launch_pipe(const void* fn, dim3 grid, size_t smem, cudaStrea
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+static void plan_caps(const MoeLaunch& a, uint32_t& cap_g, uint32_t& cap_r) {
+    const uint32_t routed = a.tokens * a.top_k;
+    cap_g = (routed < a.num_experts ? routed : a.num_experts) + 1;
+    cap_r = routed + a.tokens;
+}
+
 bool moe_pipe_supported(const MoeLaunch& a) {
     const MoeLayoutDev& L = a.layout;
     if (!moe_mma_supported(L) || a.tokens > 8) return false;
     for (int i = 0; i < 9; ++i)
         if (L.off[i] % 16) return false;
+    uint32_t cg, cr;
+    plan_caps(a, cg, cr);
     const bool lo = a.x_dtype == PBMOE_F32;
     // two CTAs per SM for the bf16 up kernel and the down kernel
-    return up_pipe_smem(L.hidden, lo) <= (lo ? 220u : 112u) * 1024 && down_pipe_smem(L.inter) <= 112u * 1024;
+    return up_pipe_smem(L.hidden, lo, cg, cr) <= (lo ? 220u : 112u) * 1024 &&
+           down_pipe_smem(L.inter, cg, cr) <= 112u * 1024;
 }
 
 cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     MoeLayoutDev L = a.layout;
     MoeWs ws = a.ws;
     uint32_t E = a.num_experts, T = a.tokens;
+    uint32_t cg, cr;
+    plan_caps(a, cg, cr);
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
     if (a.x_dtype == PBMOE_BF16) {
         const dim3 grid(device_sm_count() * UpCfg<uint16_t>::kCtasPerSm);
         const uint16_t* x = static_cast<const uint16_t*>(a.x);
-        void* args[] = {(void*)&x, (void*)&T, (void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
+        void* args[] = {(void*)&x,       (void*)&T,  (void*)&E,  (void*)&experts, (void*)&shared,
+                        (void*)&L,       (void*)&ws, (void*)&cg, (void*)&cr};
         return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<uint16_t>), grid,
-                           up_pipe_smem(L.hidden, false), s, args, pdl);
+                           up_pipe_smem(L.hidden, false, cg, cr), s, args, pdl);
     }
     const float* x = static_cast<const float*>(a.x);
     const dim3 grid(device_sm_count() * UpCfg<float>::kCtasPerSm);
-    void* args[] = {(void*)&x, (void*)&T, (void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
-    return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<float>), grid, up_pipe_smem(L.hidden, true),
-                       s, args, pdl);
+    void* args[] = {(void*)&x, (void*)&T, (void*)&E, (void*)&experts, (void*)&shared,
+                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr};
+    return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<float>), grid,
+                       up_pipe_smem(L.hidden, true, cg, cr), s, args, pdl);
 }
 
 cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
@@ -504,9 +497,11 @@ cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     uint32_t E = a.num_experts;
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
-    void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
+    uint32_t cg, cr;
+    plan_caps(a, cg, cr);
+    void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr};
     return launch_pipe(reinterpret_cast<const void*>(moe_down_pipe_kernel), dim3(2 * device_sm_count()),
-                       down_pipe_smem(L.inter), s, args, pdl);
+                       down_pipe_smem(L.inter, cg, cr), s, args, pdl);
 }
 
 }  // namespace pbmoe

@@ -41,13 +41,15 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Wait for phase `parity` of `bar` to complete, giving up after `limit_ns`
 // of wall time (returns false; the caller latches an error and winds down).
+// try_wait suspends the thread for a while on each poll; the wall clock is
+// read once every 32 polls so that a waiting warp issues almost nothing.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (global_ns() - t0 > limit_ns) return false;
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31u) == 0 && global_ns() - t0 > limit_ns) return false;
     }
-    return true;
 }
 
 // One bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
@@ -58,6 +60,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+
+// 16-byte asynchronous copy global -> shared through L2 (no L1 allocation).
+// Unlike a bulk copy, each is a plain LSU request, so thousands of small
+// row pieces per stage cost no per-copy TMA setup, and the destination may
+// be any padded layout.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+// The arrival is not added to the pending count: the barrier's expected
+// count must include one arrival per issuing thread and phase.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Wait until this thread's own cp.async copies have landed.
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Named CTA barriers (ids 1..15; 0 is __syncthreads) for warp-specialised
 // producer/consumer hand-offs. `count` is the number of participating threads

@@ -329,4 +329,53 @@ struct Q4MmaFrag4 {
     }
 };
 
+// Gate and up fragments of the same rows and groups on one activation tile:
+// the activation fragments and group sums are loaded once for both.
+template <bool kLo>
+__device__ __forceinline__ void q4_mma_pair(const Q4MmaFrag4& fa, const Q4MmaFrag4& fb, const ActTile& tile,
+                                            uint32_t grp0, int g, int t, float (&acc_a)[4], float (&acc_b)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t wd = (grp0 + j) * 8 + 2 * t;
+        const uint4 xa0 = tile.act[g * tile.stride + wd];
+        const uint4 xa1 = tile.act[g * tile.stride + wd + 1];
+        uint4 xb0 = make_uint4(0, 0, 0, 0), xb1 = make_uint4(0, 0, 0, 0);
+        if (kLo) {
+            xb0 = tile.act[(g + 8) * tile.stride + wd];
+            xb1 = tile.act[(g + 8) * tile.stride + wd + 1];
+        }
+        const float X = tile.gsum[g * tile.groups + grp0 + j];
+        const uint4 xa[2] = {xa0, xa1}, xb[2] = {xb0, xb1};
+        const Q4MmaFrag4* fr[2] = {&fa, &fb};
+        float (*ac[2])[4] = {&acc_a, &acc_b};
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {
+            const Q4MmaFrag4& F = *fr[f];
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t words[2] = {F.w[j].x, F.w[j].y};
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const uint32_t q = words[m];
+                const uint32_t b0p = (q & 0x000F000Fu) | kBf16Offset;
+                const uint32_t b1p = ((q >> 4) & 0x000F000Fu) | kBf16Offset;
+                const uint32_t b0q = ((q >> 8) & 0x000F000Fu) | kBf16Offset;
+                const uint32_t b1q = ((q >> 12) & 0x000F000Fu) | kBf16Offset;
+                mma_bf16_16816(d, xa[m].x, xb[m].x, xa[m].y, xb[m].y, b0p, b1p);
+                mma_bf16_16816(d, xa[m].z, xb[m].z, xa[m].w, xb[m].w, b0q, b1q);
+            }
+            const float s0 = Q4MmaFrag4::pick(F.sa, j), s1 = Q4MmaFrag4::pick(F.sb, j);
+            const float c0 = fmaf(-128.f, s0, Q4MmaFrag4::pick(F.ba, j));
+            const float c1 = fmaf(-128.f, s1, Q4MmaFrag4::pick(F.bb, j));
+            float(&acc)[4] = *ac[f];
+            if (kLo) {
+                acc[0] = fmaf(s0, d[0] + d[2], fmaf(c0, X, acc[0]));
+                acc[1] = fmaf(s1, d[1] + d[3], fmaf(c1, X, acc[1]));
+            } else {
+                acc[0] = fmaf(s0, d[0], fmaf(c0, X, acc[0]));
+                acc[1] = fmaf(s1, d[1], fmaf(c1, X, acc[1]));
+            }
+        }
+    }
+}
+
 }  // namespace pbmoe
