@@ -143,11 +143,24 @@ __host__ __device__ inline size_t down_pipe_smem(uint32_t I, uint32_t cap_g, uin
     return size_t(kDownStages) * down_stage(I).bytes + 16 + kDownStages * 8 + plan_smem_bytes(cap_g, cap_r);
 }
 
+// Warp roles: warps 0..7 compute; warp 8 ("producer") only issues copies.
+// A thread's cp.async may stall at issue until the SM's request queue has
+// room, so the producer spends most of its time blocked there, keeping the
+// queue full, while no compute warp ever waits behind a copy it issued.
+// Handshakes: stage s is full when its mbarrier has the producer's 32 lane
+// arrivals (cp.async completion); compute warps release it with
+// bar.arrive EMPTY(s), on which the producer bar.syncs before refilling. An
+// arrival is made only for items whose stage the producer refills, so the
+// two sides always match.
+constexpr uint32_t kPipeH = 2048, kPipeI = 512;
 constexpr int kWarps = 8;
-constexpr int kPipeThreads = kWarps * 32;
+constexpr int kPipeThreads = (kWarps + 1) * 32;
+constexpr int kComputeThreads = kWarps * 32;
+constexpr int kBarCompute = 1;                                        // compute warps only
+__device__ __forceinline__ int bar_empty(int s) { return 2 + s; }  // ids 2..6
 
 // ---------------------------------------------------------------- up
-template <typename XT>
+template <typename XT, uint32_t H, uint32_t I>
 __global__ void __launch_bounds__(kPipeThreads, UpCfg<XT>::kCtasPerSm)
 moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8_t* __restrict__ experts,
                    const uint8_t* __restrict__ shared_slot, MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g,
@@ -155,7 +168,6 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     constexpr bool kLo = sizeof(XT) == 4;
     constexpr int kUpStages = UpCfg<XT>::kStages;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    const uint32_t H = Ld.hidden, I = Ld.inter;
     const UpStage SL = up_stage(H);
     unsigned char* stages = smem_raw;
     const ActTile tile = act_tile_at(stages + kUpStages * SL.bytes, H, kLo ? 16 : 8);
@@ -166,57 +178,73 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     const PlanSmem pl = plan_at(bar + kUpStages, cap_g, cap_r);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t tiles = I / 8;
-    const uint32_t gpr = H / kMmaGroup;
-    const uint32_t gps = gpr / kWarps;  // groups per warp K-slice (multiple of 4)
+    constexpr uint32_t tiles = I / 8;
+    constexpr uint32_t gpr = H / kMmaGroup;
+    constexpr uint32_t gps = gpr / kWarps;  // groups per warp K-slice (multiple of 4)
     const size_t hps = hperm_stride(I);
 
     pdl_wait();
     const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
     const uint32_t total = ng * tiles;
-    if (blockIdx.x >= total) return;
-    const uint32_t my_items = (total - blockIdx.x + gridDim.x - 1) / gridDim.x;
+    // a contiguous run of items per CTA: consecutive tiles of one expert
+    const uint32_t k0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * total / gridDim.x);
+    const uint32_t k1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * total / gridDim.x);
+    if (k0 >= k1) return;
+    const uint32_t my_items = k1 - k0;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kUpStages; ++s) mbar_init(&bar[s], kPipeThreads);  // one arrival per thread
+        for (int s = 0; s < kUpStages; ++s) mbar_init(&bar[s], 32);  // the producer's lanes
         flags[0] = 0;
         fence_mbar_init();
     }
     load_plan(ws, ng, cap_r, pl);
     __syncthreads();
 
-    // Every thread: its share of item k's copies into stage s - warp w takes
-    // weight rows 2w, 2w+1 of the 16 (8 gate, 8 up), warps 0-3 one 8-row
-    // scale/bias block each - then its completion arrival on the stage.
-    auto issue = [&](uint32_t k, int s) {
-        const uint32_t gi = k / tiles, i0 = (k % tiles) * 8;
-        const uint32_t e = pl.expert[gi];
-        const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
-        unsigned char* st = stages + s * SL.bytes;
-        const uint32_t rb = H / 2;  // bytes of one weight row
-        const bool up_rows = warp >= 4;
-        const uint32_t r = 2 * (warp & 3);
-        const uint8_t* src = slot + Ld.off[up_rows ? 3 : 0] + static_cast<size_t>(i0 + r) * rb;
-        unsigned char* dst = st + (up_rows ? SL.up : SL.gate) + r * SL.rs;
-        for (uint32_t c = lane * 16; c < rb; c += 512) {
-            cp_async16(dst + c, src + c);
-            cp_async16(dst + SL.rs + c, src + rb + c);
+    if (warp == kWarps) {
+        // producer: 16-byte copies of the 8 gate rows, the 8 up rows and the
+        // four 8-row scale/bias blocks of item k into stage s, then each
+        // lane's completion arrival. The 8 rows of a matrix are contiguous in
+        // the slot; warp iteration i copies bytes 512i..512i+511 of them, so
+        // every copy address is a per-lane base plus a constant.
+        constexpr uint32_t kRowBytes = H / 2;
+        constexpr uint32_t kIters = 8 * kRowBytes / 512;
+        constexpr uint32_t kScaleBlock = 8 * (H / 32);  // one 8-row block of H/64 bf16 per row
+        static_assert(kRowBytes % 512 == 0 && kScaleBlock == 512, "row and block shapes");
+        auto issue = [&](uint32_t k, int s) {
+            const uint32_t gi = k / tiles, i0 = (k % tiles) * 8;
+            const uint32_t e = pl.expert[gi];
+            const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
+            unsigned char* st = stages + s * SL.bytes + lane * 16;
+            const uint8_t* gsrc = slot + Ld.off[0] + static_cast<size_t>(i0) * kRowBytes + lane * 16;
+            const uint8_t* usrc = slot + Ld.off[3] + static_cast<size_t>(i0) * kRowBytes + lane * 16;
+#pragma unroll
+            for (uint32_t i = 0; i < kIters; ++i) {
+                const uint32_t d = (i * 512) / kRowBytes * SL.rs + (i * 512) % kRowBytes;
+                cp_async16(st + SL.gate + d, gsrc + i * 512);
+                cp_async16(st + SL.up + d, usrc + i * 512);
+            }
+            const size_t so = static_cast<size_t>(i0) * (H / 32) + lane * 16;
+            cp_async16(st + SL.gs, slot + Ld.off[1] + so);
+            cp_async16(st + SL.gb, slot + Ld.off[2] + so);
+            cp_async16(st + SL.us, slot + Ld.off[4] + so);
+            cp_async16(st + SL.ub, slot + Ld.off[5] + so);
+            cp_async_arrive(&bar[s]);
+        };
+        for (int j = 0; j < kUpStages && static_cast<uint32_t>(j) < my_items; ++j) issue(k0 + j, j);
+        for (uint32_t j = 0; j + kUpStages < my_items; ++j) {
+            const int s = static_cast<int>(j % kUpStages);
+            named_sync(bar_empty(s), kPipeThreads);  // every compute warp has released item j's stage
+            if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) break;
+            issue(k0 + j + kUpStages, s);
         }
-        if (warp < 4) {
-            const uint32_t sb = 8 * (H / 32);  // one 8-row block of H/64 bf16 per row
-            const uint32_t dsts[4] = {SL.gs, SL.gb, SL.us, SL.ub};
-            const uint64_t offs[4] = {Ld.off[1], Ld.off[2], Ld.off[4], Ld.off[5]};
-            for (uint32_t c = lane * 16; c < sb; c += 512)
-                cp_async16(st + dsts[warp] + c, slot + offs[warp] + static_cast<size_t>(i0) * (H / 32) + c);
-        }
-        cp_async_arrive(&bar[s]);
-    };
+        cp_async_wait_all();  // no copy of this CTA outlives it
+        return;
+    }
 
-    for (int j = 0; j < kUpStages && static_cast<uint32_t>(j) < my_items; ++j) issue(blockIdx.x + j * gridDim.x, j);
-    // the batch's tokens stay resident for the whole kernel
+    // compute warps: the batch's tokens stay resident for the whole kernel
     if constexpr (kLo)
-        stage_act_mma<XT>(x, H, nullptr, static_cast<int>(T), H, tile);
+        stage_act_mma<XT>(x, H, nullptr, static_cast<int>(T), H, tile, kBarCompute, kComputeThreads);
     else
-        stage_act_rows8_tok<XT>(x, H, static_cast<int>(T), H, tile);
+        stage_act_rows8_tok<XT>(x, H, static_cast<int>(T), H, tile, kBarCompute, kComputeThreads);
     // Every CTA of this grid is resident, so the down kernel may be scheduled
     // now: its CTAs take SMs as these exit and prefetch weights while the
     // rest of this grid finishes (it waits for all of it before reading h_perm).
@@ -226,7 +254,7 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     for (uint32_t j = 0; j < my_items; ++j) {
         const int s = static_cast<int>(j % kUpStages);
         const int p = static_cast<int>(j & 1u);
-        const uint32_t k = blockIdx.x + j * gridDim.x;
+        const uint32_t k = k0 + j;
         const bool ok = mbar_wait_bounded(&bar[s], (j / kUpStages) & 1u, kPipeWaitNs);
         float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
         if (ok) {
@@ -244,24 +272,26 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
         } else if (lane == 0) {
             atomicOr(&flags[0], 1u);
         }
+        if (j + kUpStages < my_items) named_arrive(bar_empty(s), kPipeThreads);  // stage s released
         float* rw = red + (p * kWarps + warp) * 128;
         *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(ag[0], ag[1]);
         *reinterpret_cast<float2*>(rw + 64 + g * 8 + 2 * t) = make_float2(au[0], au[1]);
-        // Stage s is consumed, red[p] complete, the error flag visible. Item
-        // j+2 overwrites red[p] only after the next barrier, which every warp
-        // reaches after this item's epilogue.
-        __syncthreads();
+        // red[p] complete and the error flag visible. Item j+2 overwrites
+        // red[p] only after the next such barrier, which every warp reaches
+        // after this item's epilogue.
+        named_sync(kBarCompute, kComputeThreads);
         if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) {
             if (threadIdx.x == 0) latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
             break;
         }
-        if (j + kUpStages < my_items) issue(k + kUpStages * gridDim.x, s);
 
-        // epilogue: warp q finishes the group's q-th route (token) of this tile
+        // epilogue: the group's q-th route (token) of this tile is finished by
+        // warp (q + j) mod 8, so the work rotates over the warps
         const uint32_t gi = k / tiles, ti = k % tiles;
         const uint32_t n = pl.count[gi];
-        if (static_cast<uint32_t>(warp) < n) {
-            const uint32_t pos = pl.start[gi] + warp;
+        const uint32_t q = (static_cast<uint32_t>(warp) + kWarps - (j & (kWarps - 1))) & (kWarps - 1);
+        if (q < n) {
+            const uint32_t pos = pl.start[gi] + q;
             const uint32_t tok = pl.token[pos];
             const float* rb = red + p * kWarps * 128;
             // lane: row = lane/4 sums the partials of K-slices 2(lane%4), 2(lane%4)+1
@@ -291,15 +321,14 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
             if (lane == 0) reinterpret_cast<float*>(hr + 2 * tiles * 16)[ti] = part;
         }
     }
-    cp_async_wait_all();  // no copy of this CTA outlives it
 }
 
 // ---------------------------------------------------------------- down
+template <uint32_t H, uint32_t I>
 __global__ void __launch_bounds__(kPipeThreads, 2)
 moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint8_t* __restrict__ shared_slot,
                      MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g, uint32_t cap_r) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    const uint32_t H = Ld.hidden, I = Ld.inter;
     const DownStage SL = down_stage(I);
     unsigned char* stages = smem_raw;
     uint32_t* flags = reinterpret_cast<uint32_t*>(stages + kDownStages * SL.bytes);
@@ -307,81 +336,96 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
     const PlanSmem pl = plan_at(bar + kDownStages, cap_g, cap_r);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t tiles = H / 64;
-    const uint32_t gpr = I / kMmaGroup;  // 4 or 8
-    const uint32_t wslots = I / 8;
+    constexpr uint32_t tiles = H / 64;
+    constexpr uint32_t gpr = I / kMmaGroup;
+    constexpr uint32_t wslots = I / 8;
     const size_t hps = hperm_stride(I);
-    const uint32_t rw0 = warp * 8;  // this warp's 8 rows within the 64-row tile
 
     // The group plan was written by the router kernel, which completed before
     // the up kernel passed its own wait; it is safe to read before this
     // kernel's wait (through L2).
     const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
     const uint32_t total = ng * tiles;
-    if (blockIdx.x >= total) {
+    // a contiguous run of items per CTA (consecutive tiles of one expert)
+    const uint32_t k0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * total / gridDim.x);
+    const uint32_t k1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * total / gridDim.x);
+    if (k0 >= k1) {
         pdl_wait();
         return;
     }
-    const uint32_t my_items = (total - blockIdx.x + gridDim.x - 1) / gridDim.x;
+    const uint32_t my_items = k1 - k0;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kDownStages; ++s) mbar_init(&bar[s], kPipeThreads);  // one arrival per thread
+        for (int s = 0; s < kDownStages; ++s) mbar_init(&bar[s], 32);  // the producer's lanes
         flags[0] = 0;
         fence_mbar_init();
     }
     load_plan(ws, ng, cap_r, pl);
     __syncthreads();
 
-    // Every thread: its share of item k's weight copies into stage s (warp w
-    // its own 8 rows; threads 0-127 the scale and bias blocks) ...
-    auto issue_weights = [&](uint32_t k, int s) {
-        const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
-        const uint32_t e = pl.expert[gi];
-        const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
-        unsigned char* st = stages + s * SL.bytes;
-        const uint32_t rb = I / 2;                     // bytes of one weight row
-        const uint32_t cpr_shift = __ffs(rb / 16) - 1;  // log2 of 16-byte chunks per row (I = 256 or 512)
-        const uint8_t* wsrc = slot + Ld.off[6] + static_cast<size_t>(r0 + rw0) * rb;
-        for (uint32_t c = lane; c < (8u << cpr_shift); c += 32) {
-            const uint32_t r = c >> cpr_shift, xo = c & ((1u << cpr_shift) - 1);
-            cp_async16(st + SL.w + (rw0 + r) * SL.rs + xo * 16, wsrc + static_cast<size_t>(c) * 16);
+    if (warp == kWarps) {
+        // producer: item k's 64 weight rows (contiguous in the slot; warp
+        // iteration i copies rows 2i, 2i+1) and scale/bias blocks ...
+        constexpr uint32_t kRowBytes = I / 2;
+        static_assert(kRowBytes == 256, "two rows per 512-byte warp copy");
+        constexpr uint32_t kScaleBytes = 64 * (I / 32);
+        auto issue_weights = [&](uint32_t k, int s) {
+            const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
+            const uint32_t e = pl.expert[gi];
+            const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
+            unsigned char* st = stages + s * SL.bytes;
+            const uint8_t* wsrc = slot + Ld.off[6] + static_cast<size_t>(r0) * kRowBytes + lane * 16;
+            unsigned char* wdst = st + SL.w + (lane >> 4) * SL.rs + (lane & 15) * 16;
+#pragma unroll
+            for (uint32_t i = 0; i < 32; ++i) cp_async16(wdst + 2 * i * SL.rs, wsrc + i * 512);
+            const size_t so = static_cast<size_t>(r0) * (I / 32) + lane * 16;
+#pragma unroll
+            for (uint32_t c = 0; c < kScaleBytes; c += 512) {
+                cp_async16(st + SL.s + lane * 16 + c, slot + Ld.off[7] + so + c);
+                cp_async16(st + SL.b + lane * 16 + c, slot + Ld.off[8] + so + c);
+            }
+        };
+        // ... and the group's routed activations: hi and lo bf16 rows of h
+        // (pair order) and the per-8 partial sums of each route
+        auto issue_h = [&](uint32_t k, int s) {
+            const uint32_t gi = k / tiles;
+            const uint32_t start = pl.start[gi], n = pl.count[gi];
+            unsigned char* st = stages + s * SL.bytes;
+            const ActTile tile = act_tile_at(st + SL.act, I, 16);
+            for (uint32_t p = 0; p < n; ++p) {
+                const uint8_t* hr = ws.h_perm + static_cast<size_t>(pl.route[start + p]) * hps + lane * 16;
+#pragma unroll
+                for (uint32_t c = 0; c < wslots; c += 32) {
+                    cp_async16(tile.act + p * tile.stride + c + lane, hr + c * 16);
+                    cp_async16(tile.act + (p + 8) * tile.stride + c + lane, hr + (wslots + c) * 16);
+                }
+                if (lane < wslots / 4)
+                    cp_async16(st + SL.part + p * SL.part_stride + lane * 16, hr + 2 * wslots * 16);
+            }
+        };
+        for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j) issue_weights(k0 + j, j);
+        pdl_wait();  // h_perm comes from the up kernel
+        for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j) {
+            issue_h(k0 + j, j);
+            cp_async_arrive(&bar[j]);
         }
-        const uint32_t sb = 64 * (I / 32);
-        const size_t soff = static_cast<size_t>(r0) * (I / 32);
-        for (uint32_t c = threadIdx.x * 16; c < sb; c += kPipeThreads * 16) {
-            cp_async16(st + SL.s + c, slot + Ld.off[7] + soff + c);
-            cp_async16(st + SL.b + c, slot + Ld.off[8] + soff + c);
+        for (uint32_t j = 0; j + kDownStages < my_items; ++j) {
+            const int s = static_cast<int>(j % kDownStages);
+            named_sync(bar_empty(s), kPipeThreads);  // every compute warp has released item j's stage
+            if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) break;
+            issue_weights(k0 + j + kDownStages, s);
+            issue_h(k0 + j + kDownStages, s);
+            cp_async_arrive(&bar[s]);
         }
-    };
-    // ... and of the group's routed activations: warp p copies route p's hi
-    // and lo bf16 rows of h (pair order) and its per-8 partial sums.
-    auto issue_h = [&](uint32_t k, int s) {
-        const uint32_t gi = k / tiles;
-        const uint32_t n = pl.count[gi];
-        if (static_cast<uint32_t>(warp) >= n) return;
-        unsigned char* st = stages + s * SL.bytes;
-        const ActTile tile = act_tile_at(st + SL.act, I, 16);
-        const uint32_t p = warp;
-        const uint8_t* hr = ws.h_perm + static_cast<size_t>(pl.route[pl.start[gi] + p]) * hps;
-        for (uint32_t c = lane; c < wslots; c += 32) {
-            cp_async16(tile.act + p * tile.stride + c, hr + c * 16);
-            cp_async16(tile.act + (p + 8) * tile.stride + c, hr + (wslots + c) * 16);
-        }
-        for (uint32_t c = lane; c < wslots / 4; c += 32)
-            cp_async16(st + SL.part + p * SL.part_stride + c * 16, hr + 2 * wslots * 16 + c * 16);
-    };
-
-    for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j)
-        issue_weights(blockIdx.x + j * gridDim.x, j);
-    pdl_wait();               // h_perm comes from the up kernel
-    pdl_launch_dependents();  // the combine kernel waits for this whole grid
-    for (int j = 0; j < kDownStages && static_cast<uint32_t>(j) < my_items; ++j) {
-        issue_h(blockIdx.x + j * gridDim.x, j);
-        cp_async_arrive(&bar[j]);
+        cp_async_wait_all();  // no copy of this CTA outlives it
+        return;
     }
 
+    pdl_wait();
+    pdl_launch_dependents();  // the combine kernel waits for this whole grid
+    const uint32_t rw0 = warp * 8;  // this warp's 8 rows within the 64-row tile
     for (uint32_t j = 0; j < my_items; ++j) {
         const int s = static_cast<int>(j % kDownStages);
-        const uint32_t k = blockIdx.x + j * gridDim.x;
+        const uint32_t k = k0 + j;
         const bool ok = mbar_wait_bounded(&bar[s], (j / kDownStages) & 1u, kPipeWaitNs);
         if (ok) {
             const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
@@ -408,27 +452,23 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
                 f.load_smem(st + SL.w + (rw0 + g) * SL.rs, ds, db, gpr, b, t);
                 f.compute_x<true, false>(tile, b, g, t, X, X2, acc);
             }
+            if (j + kDownStages < my_items) named_arrive(bar_empty(s), kPipeThreads);  // stage s released
             if (static_cast<uint32_t>(g) < n) {
                 const uint32_t route = pl.route[start + g];
                 *reinterpret_cast<float2*>(ws.y + static_cast<size_t>(route) * H + r0 + rw0 + 2 * t) =
                     make_float2(acc[0], acc[1]);
             }
-        } else if (lane == 0) {
-            atomicOr(&flags[0], 1u);
-        }
-        __syncthreads();  // stage s consumed by every warp; error flag visible
-        if (*reinterpret_cast<volatile uint32_t*>(&flags[0])) {
-            if (threadIdx.x == 0) latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+        } else {
+            // the producer stops at this item (it reads the flag after the release)
+            if (lane == 0) {
+                atomicOr(&flags[0], 1u);
+                latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+            }
+            __syncwarp();
+            if (j + kDownStages < my_items) named_arrive(bar_empty(s), kPipeThreads);
             break;
         }
-        if (j + kDownStages < my_items) {
-            const uint32_t kn = k + kDownStages * gridDim.x;
-            issue_weights(kn, s);
-            issue_h(kn, s);
-            cp_async_arrive(&bar[s]);
-        }
     }
-    cp_async_wait_all();  // no copy of this CTA outlives it
 }
 
 // ---------------------------------------------------------------- launch
@@ -456,7 +496,9 @@ static void plan_caps(const MoeLaunch& a, uint32_t& cap_g, uint32_t& cap_r) {
 
 bool moe_pipe_supported(const MoeLaunch& a) {
     const MoeLayoutDev& L = a.layout;
-    if (!moe_mma_supported(L) || a.tokens > 8) return false;
+    // the pipelined kernels are specialised for the expert shape of every
+    // configuration the runtime ships (hidden 2048, intermediate 512)
+    if (!moe_mma_supported(L) || a.tokens > 8 || L.hidden != kPipeH || L.inter != kPipeI) return false;
     for (int i = 0; i < 9; ++i)
         if (L.off[i] % 16) return false;
     uint32_t cg, cr;
@@ -480,14 +522,14 @@ cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
         const uint16_t* x = static_cast<const uint16_t*>(a.x);
         void* args[] = {(void*)&x,       (void*)&T,  (void*)&E,  (void*)&experts, (void*)&shared,
                         (void*)&L,       (void*)&ws, (void*)&cg, (void*)&cr};
-        return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<uint16_t>), grid,
+        return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<uint16_t, kPipeH, kPipeI>), grid,
                            up_pipe_smem(L.hidden, false, cg, cr), s, args, pdl);
     }
     const float* x = static_cast<const float*>(a.x);
     const dim3 grid(device_sm_count() * UpCfg<float>::kCtasPerSm);
     void* args[] = {(void*)&x, (void*)&T, (void*)&E, (void*)&experts, (void*)&shared,
                     (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr};
-    return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<float>), grid,
+    return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<float, kPipeH, kPipeI>), grid,
                        up_pipe_smem(L.hidden, true, cg, cr), s, args, pdl);
 }
 
@@ -500,7 +542,7 @@ cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     uint32_t cg, cr;
     plan_caps(a, cg, cr);
     void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr};
-    return launch_pipe(reinterpret_cast<const void*>(moe_down_pipe_kernel), dim3(2 * device_sm_count()),
+    return launch_pipe(reinterpret_cast<const void*>(moe_down_pipe_kernel<kPipeH, kPipeI>), dim3(2 * device_sm_count()),
                        down_pipe_smem(L.inter, cg, cr), s, args, pdl);
 }
 

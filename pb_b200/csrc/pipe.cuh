@@ -33,6 +33,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` while the phase
+// is incomplete (it resumes as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -41,24 +53,15 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Wait for phase `parity` of `bar` to complete, giving up after `limit_ns`
 // of wall time (returns false; the caller latches an error and winds down).
-// try_wait suspends the thread for a while on each poll; the wall clock is
-// read once every 32 polls so that a waiting warp issues almost nothing.
+// Each poll suspends the thread in hardware for up to 20 us, so a waiting
+// warp issues a handful of instructions per wait instead of spinning.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 31u) == 0 && global_ns() - t0 > limit_ns) return false;
+    while (!mbar_try_wait_hint(bar, parity, 20000u)) {
+        if (global_ns() - t0 > limit_ns) return false;
     }
-}
-
-// One bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
-// from global memory into this CTA's shared memory, completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
+    return true;
 }
 
 // 16-byte asynchronous copy global -> shared through L2 (no L1 allocation).

@@ -94,23 +94,34 @@ __device__ __forceinline__ uint32_t f2_to_bf16x2(float a, float b) {
     return r;
 }
 
+// Barrier that ends a staging pass: the whole CTA (nthreads == 0) or the
+// `nthreads` threads of named barrier `bar_id`.
+__device__ __forceinline__ void tile_sync(int bar_id, uint32_t nthreads) {
+    if (nthreads == 0)
+        __syncthreads();
+    else
+        asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+}
+
 // Stage `ntok` activation rows (<= 16 for bf16, <= 8 for f32) into `tile`.
 // x rows are `x_stride` elements apart; rows_idx maps local token t to its
 // source row (NULL = identity). All global loads of a thread are issued before
-// its shared stores. Ends with __syncthreads.
+// its shared stores. Run by threads 0..nthreads-1 (the whole CTA when
+// nthreads == 0) and ends with their barrier (tile_sync).
 template <typename XT>
 __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx, int ntok,
-                              uint32_t K, const ActTile& tile) {
+                              uint32_t K, const ActTile& tile, int bar_id = 0, uint32_t nthreads = 0) {
     constexpr bool kLo = sizeof(XT) == 4;
+    const uint32_t nthr = nthreads ? nthreads : blockDim.x;
     const uint32_t slots = K / 8;
     const uint32_t nrows = 16;
     // zero the unused rows (and, for bf16, rows ntok..15; for f32, rows ntok..7 and 8+ntok..15)
-    for (uint32_t i = threadIdx.x; i < nrows * slots; i += blockDim.x) {
+    for (uint32_t i = threadIdx.x; i < nrows * slots; i += nthr) {
         const uint32_t row = i / slots;
         const uint32_t tok = kLo ? (row & 7u) : row;
         if (tok >= static_cast<uint32_t>(ntok)) tile.act[(i / slots) * tile.stride + (i % slots)] = make_uint4(0, 0, 0, 0);
     }
-    for (uint32_t i = threadIdx.x; i < nrows * tile.groups; i += blockDim.x) {
+    for (uint32_t i = threadIdx.x; i < nrows * tile.groups; i += nthr) {
         const uint32_t row = i / tile.groups;
         const uint32_t tok = kLo ? (row & 7u) : row;
         if (tok >= static_cast<uint32_t>(ntok) || (kLo && row >= 8)) tile.gsum[i] = 0.f;
@@ -118,11 +129,11 @@ __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const u
     // one thread per (token, word): 8 activations
     const uint32_t total = static_cast<uint32_t>(ntok) * slots;
     constexpr int kBatch = kLo ? 1 : 4;
-    for (uint32_t base = 0; base < total; base += kBatch * blockDim.x) {
+    for (uint32_t base = 0; base < total; base += kBatch * nthr) {
         uint4 v[kBatch][kLo ? 2 : 1];
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            const uint32_t idx = base + i * nthr + threadIdx.x;
             if (idx < total) {
                 const uint32_t t = idx / slots, w = idx - t * slots;
                 const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
@@ -133,7 +144,7 @@ __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const u
         }
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            const uint32_t idx = base + i * nthr + threadIdx.x;
             float sum = 0.f;
             uint32_t t = 0, w = 0;
             const bool ok = idx < total;
@@ -174,27 +185,28 @@ __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const u
             if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
         }
     }
-    __syncthreads();
+    tile_sync(bar_id, nthreads);
 }
 
 // stage_act_mma for bf16 tiles with only 8 token rows (tokens <= 8) and
 // contiguous token rows.
 template <typename XT>
 __device__ void stage_act_rows8_tok(const XT* __restrict__ x, size_t x_stride, int ntok, uint32_t K,
-                                    const ActTile& tile) {
+                                    const ActTile& tile, int bar_id = 0, uint32_t nthreads = 0) {
+    const uint32_t nthr = nthreads ? nthreads : blockDim.x;
     static_assert(sizeof(XT) == 2, "8-row tiles hold bf16 activations");
     const uint32_t slots = K / 8;
-    for (uint32_t i = threadIdx.x; i < 8 * slots; i += blockDim.x)
+    for (uint32_t i = threadIdx.x; i < 8 * slots; i += nthr)
         if (i / slots >= static_cast<uint32_t>(ntok)) tile.act[(i / slots) * tile.stride + (i % slots)] = make_uint4(0, 0, 0, 0);
-    for (uint32_t i = threadIdx.x; i < 8 * tile.groups; i += blockDim.x)
+    for (uint32_t i = threadIdx.x; i < 8 * tile.groups; i += nthr)
         if (i / tile.groups >= static_cast<uint32_t>(ntok)) tile.gsum[i] = 0.f;
     const uint32_t total = static_cast<uint32_t>(ntok) * slots;
     constexpr int kBatch = 4;
-    for (uint32_t base = 0; base < total; base += kBatch * blockDim.x) {
+    for (uint32_t base = 0; base < total; base += kBatch * nthr) {
         uint4 v[kBatch];
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            const uint32_t idx = base + i * nthr + threadIdx.x;
             if (idx < total) {
                 const uint32_t t = idx / slots, w = idx - t * slots;
                 v[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * x_stride + static_cast<size_t>(w) * 8);
@@ -202,7 +214,7 @@ __device__ void stage_act_rows8_tok(const XT* __restrict__ x, size_t x_stride, i
         }
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * blockDim.x + threadIdx.x;
+            const uint32_t idx = base + i * nthr + threadIdx.x;
             float sum = 0.f;
             uint32_t t = 0, w = 0;
             const bool ok = idx < total;
@@ -222,7 +234,7 @@ __device__ void stage_act_rows8_tok(const XT* __restrict__ x, size_t x_stride, i
             if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
         }
     }
-    __syncthreads();
+    tile_sync(bar_id, nthreads);
 }
 
 // Register fragment of one 8-row tile over a block of 4 consecutive groups:
