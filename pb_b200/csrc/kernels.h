@@ -84,7 +84,7 @@ cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s);
 bool moe_mma_supported(const MoeLayoutDev& L);
 cudaError_t moe_up_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
 cudaError_t moe_down_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
-// Persistent, bulk-copy pipelined expert kernels (moe_pipe.cu) for decode
+// Persistent, cp.async-pipelined expert kernels (moe_pipe.cu) for decode
 // batches of at most 8 tokens on moe_mma_supported layouts.
 bool moe_pipe_supported(const MoeLaunch& a);
 cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
