@@ -16,19 +16,22 @@
 // Handshakes: a stage is full when its mbarrier has the producer's 32 lane
 // arrivals (cp.async completion, no pending-count increment); compute warps
 // release it with bar.arrive EMPTY(s), on which the producer bar.syncs before
-// refilling it. Partial sums go through 4 rotating buffers (RED(p) arrive /
+// refilling it. Partial sums go through 2 rotating buffers (RED(p) arrive /
 // sync towards the epilogue warp, FREE(p) back). An arrival is made exactly
 // when the matching sync will be made, and no role leaves its item loop
 // early: after a failure (a bounded wait expired, PBMOE_DEV_ERR_PIPE_TIMEOUT
 // latched) the roles keep the handshakes but skip waits, copies and math, so
 // every named barrier completes and the kernel returns.
 //
-//   moe_up_pipe_kernel    item = (group, 8 intermediate rows): gate and up
-//       rows + scales/biases; the batch's tokens stay resident in shared
-//       memory (staged before the programmatic-dependent-launch wait, as they
-//       do not depend on the router). 8 compute warps = 8 K-slices; SwiGLU
-//       (silu(g)*u, shaders.metal:1699-1708) is written as bf16 hi/lo pair
-//       slots + per-8 partial sums (MoeWs::h_perm), the down kernel's input.
+//   moe_up_pipe_kernel    item = (group, 16 intermediate rows), fetched and
+//       computed as two steps of half the hidden dimension each: gate and up
+//       half-rows + their scales/biases. The 16 rows are the M operand of the
+//       mma and the batch's tokens the N operand (q4_mma_rows16); the tokens
+//       stay resident in shared memory (staged before the programmatic-
+//       dependent-launch wait, as they do not depend on the router). 8 compute
+//       warps = 8 K-slices of each step; SwiGLU (silu(g)*u,
+//       shaders.metal:1699-1708) is written as bf16 hi/lo pair slots +
+//       per-8 partial sums (MoeWs::h_perm), the down kernel's input.
 //   moe_down_pipe_kernel  item = (group, 64 down rows); warp w owns rows
 //       8w..8w+7. Weight stages hold only weights: the routed activations of
 //       the (at most two) groups of the CTA's run are copied once into their
@@ -47,7 +50,7 @@ constexpr int kComputeThreads = kWarps * 32;
 constexpr int kHandshake = kComputeThreads + 32;  // compute warps + producer (or + epilogue)
 constexpr int kUpThreads = (kWarps + 2) * 32;     // + producer + epilogue
 constexpr int kDownThreads = (kWarps + 1) * 32;   // + producer
-constexpr int kRedBufs = 4;
+constexpr int kRedBufs = 2;
 
 // Stage counts: bf16 activations run two CTAs per SM (3 stages each);
 // f32 activations keep a 16-row token tile and run one CTA per SM.
@@ -63,8 +66,8 @@ struct UpCfg {
 // Named barrier ids (0 is __syncthreads).
 constexpr int kBarStage = 1;                                        // compute warps only
 __device__ __forceinline__ int bar_empty(int s) { return 2 + s; }  // 2..6
-__device__ __forceinline__ int bar_red(int p) { return 7 + p; }    // 7..10
-__device__ __forceinline__ int bar_free(int p) { return 11 + p; }  // 11..14
+__device__ __forceinline__ int bar_red(int p) { return 7 + p; }    // 7, 8
+__device__ __forceinline__ int bar_free(int p) { return 9 + p; }   // 9, 10
 
 static int device_sm_count() {
     static int cached[64] = {0};
@@ -124,28 +127,25 @@ __device__ __forceinline__ bool pipe_failed(const uint32_t* flags) {
 }
 
 // ---------------------------------------------------------------- layouts
+// One up step: 16 rows x half of the hidden dimension of gate and of up
+// (padded rows), and the matching half of each row's scales/biases.
 struct UpStage {
-    uint32_t rs;     // padded row stride (bytes) = H/2 + 32
-    uint32_t gate, up, gs, gb, us, ub;
+    uint32_t rs;     // padded half-row stride (bytes) = H/4 + 32
+    uint32_t srs;    // padded scale-row stride (bytes): H/128 bf16 + pad, 48 for H = 2048
+    uint32_t gate, up, sc;  // sc: gs, gb, us, ub blocks of 16 rows each
     uint32_t bytes;  // stage size, multiple of 128
 };
 
 __host__ __device__ constexpr UpStage up_stage(uint32_t H) {
-    return {H / 2 + 32,
-            0,
-            8 * (H / 2 + 32),
-            16 * (H / 2 + 32),
-            16 * (H / 2 + 32) + 8 * (H / 32),
-            16 * (H / 2 + 32) + 16 * (H / 32),
-            16 * (H / 2 + 32) + 24 * (H / 32),
-            (16 * (H / 2 + 32) + 32 * (H / 32) + 127) / 128 * 128};
+    return {H / 4 + 32, H / 64 + 16, 0, 16 * (H / 4 + 32), 32 * (H / 4 + 32),
+            (32 * (H / 4 + 32) + 4 * 16 * (H / 64 + 16) + 127) / 128 * 128};
 }
 
 __host__ __device__ inline size_t up_pipe_smem(uint32_t H, bool lo, uint32_t cap_g, uint32_t cap_r) {
     const UpStage L = up_stage(H);
     const int stages = lo ? kUpStagesF32 : kUpStagesBf16;
     // stages, token tile, partial-sum buffers, flags, mbarriers, plan
-    return size_t(stages) * L.bytes + act_tile_bytes(H, lo ? 16 : 8) + size_t(kRedBufs) * kWarps * 128 * 4 + 16 +
+    return size_t(stages) * L.bytes + act_tile_bytes(H, lo ? 16 : 8) + size_t(kRedBufs) * kWarps * 256 * 4 + 16 +
            stages * 8 + plan_smem_bytes(cap_g, cap_r);
 }
 
@@ -187,15 +187,17 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     constexpr bool kLo = sizeof(XT) == 4;
     constexpr int S = UpCfg<XT>::kStages;
     constexpr UpStage SL = up_stage(H);
-    constexpr uint32_t tiles = I / 8;
-    constexpr uint32_t gpr = H / kMmaGroup;
-    constexpr uint32_t gps = gpr / kWarps;  // groups per warp K-slice (multiple of 4)
+    constexpr uint32_t kTiles = I / 16;          // 16-row tiles per expert
+    constexpr uint32_t kTiles8 = I / 8;          // 8-row tiles of the h_perm layout
+    constexpr uint32_t kHalfGroups = H / 128;    // scale groups per step
+    constexpr uint32_t kGpw = kHalfGroups / kWarps;  // groups per warp per step
+    static_assert(kGpw == 2, "two groups per warp per step");
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char* stages = smem_raw;
     const ActTile tile = act_tile_at(stages + S * SL.bytes, H, kLo ? 16 : 8);
-    // partial sums: [kRedBufs][8 warps][gate 64 | up 64], entry tok*8 + row
+    // partial sums: [kRedBufs][8 warps][gate | up][16 rows][8 tokens]
     float* red = reinterpret_cast<float*>(stages + S * SL.bytes + act_tile_bytes(H, kLo ? 16 : 8));
-    uint32_t* flags = reinterpret_cast<uint32_t*>(red + kRedBufs * kWarps * 128);  // [0] failure
+    uint32_t* flags = reinterpret_cast<uint32_t*>(red + kRedBufs * kWarps * 256);  // [0] failure
     uint64_t* bar = reinterpret_cast<uint64_t*>(flags + 4);
     const PlanSmem pl = plan_at(bar + S, cap_g, cap_r);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -217,9 +219,10 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     pdl_wait();
     const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
     uint32_t k0, k1;
-    item_run(ng * tiles, k0, k1);
+    item_run(ng * kTiles, k0, k1);
     if (k0 >= k1) return;
     const uint32_t my_items = k1 - k0;
+    const uint32_t steps = 2 * my_items;
     load_plan(ws, ng, cap_r, pl);
     __syncthreads();
     // Every CTA of this grid is resident, so the down kernel may be scheduled
@@ -228,39 +231,40 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     pdl_launch_dependents();
 
     if (warp == kWarps) {
-        // producer: 16-byte copies of the 8 gate rows, the 8 up rows and the
-        // four 8-row scale/bias blocks of item k into stage s, then each
-        // lane's completion arrival. The 8 rows of a matrix are contiguous in
-        // the slot; warp iteration i copies bytes 512i..512i+511 of them, so
-        // every copy address is a per-lane base plus a constant.
-        constexpr uint32_t kRowBytes = H / 2;
-        constexpr uint32_t kIters = 8 * kRowBytes / 512;
-        static_assert(kRowBytes % 512 == 0 && 8 * (H / 32) == 512, "row and scale-block shapes");
-        auto issue = [&](uint32_t k, int s) {
-            const uint32_t gi = k / tiles, i0 = (k % tiles) * 8;
+        // producer: step u = (item k0 + u/2, half u%2): 16 gate and 16 up
+        // half-rows (one 512-byte warp copy each) and the four 16-row
+        // scale/bias half-blocks (lane = row/2, 16-byte chunk), then each
+        // lane's completion arrival
+        constexpr uint32_t kRowBytes = H / 2, kHalfBytes = H / 4, kScaleRow = H / 32;
+        static_assert(kHalfBytes == 512 && kScaleRow / 2 == 32, "one warp copy per half-row, two chunks per scale half-row");
+        auto issue = [&](uint32_t u, int s) {
+            const uint32_t k = k0 + u / 2, half = u & 1u;
+            const uint32_t gi = k / kTiles, r0 = (k % kTiles) * 16;
             const uint32_t e = pl.expert[gi];
             const uint8_t* slot = e >= E ? shared_slot : experts + static_cast<size_t>(e) * Ld.expert_bytes;
-            unsigned char* st = stages + s * SL.bytes + lane * 16;
-            const uint8_t* gsrc = slot + Ld.off[0] + static_cast<size_t>(i0) * kRowBytes + lane * 16;
-            const uint8_t* usrc = slot + Ld.off[3] + static_cast<size_t>(i0) * kRowBytes + lane * 16;
+            unsigned char* st = stages + s * SL.bytes;
+            const size_t wo = static_cast<size_t>(r0) * kRowBytes + half * kHalfBytes + lane * 16;
+            const uint8_t* gsrc = slot + Ld.off[0] + wo;
+            const uint8_t* usrc = slot + Ld.off[3] + wo;
 #pragma unroll
-            for (uint32_t i = 0; i < kIters; ++i) {
-                const uint32_t d = (i * 512) / kRowBytes * SL.rs + (i * 512) % kRowBytes;
-                cp_async16(st + SL.gate + d, gsrc + i * 512);
-                cp_async16(st + SL.up + d, usrc + i * 512);
+            for (uint32_t r = 0; r < 16; ++r) {
+                cp_async16(st + SL.gate + r * SL.rs + lane * 16, gsrc + r * kRowBytes);
+                cp_async16(st + SL.up + r * SL.rs + lane * 16, usrc + r * kRowBytes);
             }
-            const size_t so = static_cast<size_t>(i0) * (H / 32) + lane * 16;
-            cp_async16(st + SL.gs, slot + Ld.off[1] + so);
-            cp_async16(st + SL.gb, slot + Ld.off[2] + so);
-            cp_async16(st + SL.us, slot + Ld.off[4] + so);
-            cp_async16(st + SL.ub, slot + Ld.off[5] + so);
+            const uint32_t row = lane >> 1, chunk = lane & 1;
+            const size_t so = static_cast<size_t>(r0 + row) * kScaleRow + half * (kScaleRow / 2) + chunk * 16;
+            unsigned char* sd = st + SL.sc + row * SL.srs + chunk * 16;
+            cp_async16(sd + 0 * 16 * SL.srs, slot + Ld.off[1] + so);
+            cp_async16(sd + 1 * 16 * SL.srs, slot + Ld.off[2] + so);
+            cp_async16(sd + 2 * 16 * SL.srs, slot + Ld.off[4] + so);
+            cp_async16(sd + 3 * 16 * SL.srs, slot + Ld.off[5] + so);
             cp_async_arrive(&bar[s]);
         };
-        for (int j = 0; j < S && static_cast<uint32_t>(j) < my_items; ++j) issue(k0 + j, j);
-        for (uint32_t j = 0; j + S < my_items; ++j) {
-            const int s = static_cast<int>(j % S);
-            named_sync(bar_empty(s), kHandshake);  // every compute warp has released item j's stage
-            if (!pipe_failed(flags)) issue(k0 + j + S, s);
+        for (int u = 0; u < S && static_cast<uint32_t>(u) < steps; ++u) issue(u, u);
+        for (uint32_t u = 0; u + S < steps; ++u) {
+            const int s = static_cast<int>(u % S);
+            named_sync(bar_empty(s), kHandshake);  // every compute warp has released step u's stage
+            if (!pipe_failed(flags)) issue(u + S, s);
         }
         cp_async_wait_all();  // no copy of this CTA outlives it
         return;
@@ -268,42 +272,55 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
 
     if (warp == kWarps + 1) {
         // epilogue: lane (q = lane/4, c = lane%4) finishes route q of the
-        // group (q < n <= 8) for rows c and c+4 of the tile: it sums the 8
-        // K-slice partials of both rows for gate and up, applies SwiGLU and
-        // writes pair word c = (h_c, h_{c+4}) as bf16 hi and lo; the quad sums
-        // the tile's per-8 partial.
+        // group (q < n <= 8) for rows c, c+4 (first 8-row tile of the item)
+        // and 8+c, 12+c (second): it sums the 8 K-slice partials of each row
+        // for gate and up, applies SwiGLU and writes pair word c of both
+        // 8-row tiles as bf16 hi and lo; the quad sums each tile's per-8 partial.
         const uint32_t q = static_cast<uint32_t>(lane >> 2), c = static_cast<uint32_t>(lane & 3);
         for (uint32_t j = 0; j < my_items; ++j) {
             const int p = static_cast<int>(j % kRedBufs);
             named_sync(bar_red(p), kHandshake);  // red[p] holds item j's partials
             if (!pipe_failed(flags)) {
                 const uint32_t k = k0 + j;
-                const uint32_t gi = k / tiles, ti = k % tiles;
+                const uint32_t gi = k / kTiles, ti = k % kTiles;
                 const uint32_t start = pl.start[gi], n = pl.count[gi];
                 const bool active = q < n;
                 const uint32_t tok = active ? pl.token[start + q] : 0u;
-                const float* rb = red + p * kWarps * 128 + tok * 8 + c;
-                float g0 = 0.f, g4 = 0.f, u0 = 0.f, u4 = 0.f;
+                const float* rb = red + p * kWarps * 256 + c * 8 + tok;
+                float gs[4] = {0.f, 0.f, 0.f, 0.f}, us[4] = {0.f, 0.f, 0.f, 0.f};  // rows c, c+4, c+8, c+12
 #pragma unroll
                 for (int w = 0; w < kWarps; ++w) {
-                    g0 += rb[w * 128];
-                    g4 += rb[w * 128 + 4];
-                    u0 += rb[w * 128 + 64];
-                    u4 += rb[w * 128 + 68];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        gs[r] += rb[w * 256 + r * 32];
+                        us[r] += rb[w * 256 + 128 + r * 32];
+                    }
                 }
-                const float h0 = g0 / (1.0f + expf(-g0)) * u0;
-                const float h4 = g4 / (1.0f + expf(-g4)) * u4;
-                float part = h0 + h4;
-                part += __shfl_xor_sync(kFull, part, 1);
-                part += __shfl_xor_sync(kFull, part, 2);
+                float h[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) h[r] = gs[r] / (1.0f + expf(-gs[r])) * us[r];
+                float part0 = h[0] + h[1], part1 = h[2] + h[3];
+                part0 += __shfl_xor_sync(kFull, part0, 1);
+                part0 += __shfl_xor_sync(kFull, part0, 2);
+                part1 += __shfl_xor_sync(kFull, part1, 1);
+                part1 += __shfl_xor_sync(kFull, part1, 2);
                 if (active) {
                     uint8_t* hr = ws.h_perm + static_cast<size_t>(pl.route[start + q]) * hps;
-                    const uint32_t hi = f2_to_bf16x2(h0, h4);
-                    const uint32_t lo =
-                        f2_to_bf16x2(h0 - __uint_as_float(hi << 16), h4 - __uint_as_float(hi & 0xffff0000u));
-                    reinterpret_cast<uint32_t*>(hr)[ti * 4 + c] = hi;
-                    reinterpret_cast<uint32_t*>(hr + tiles * 16)[ti * 4 + c] = lo;
-                    if (c == 0) reinterpret_cast<float*>(hr + 2 * tiles * 16)[ti] = part;
+                    uint32_t* hw = reinterpret_cast<uint32_t*>(hr);
+                    uint32_t* lw = reinterpret_cast<uint32_t*>(hr + kTiles8 * 16);
+#pragma unroll
+                    for (int bt = 0; bt < 2; ++bt) {
+                        const float a = h[2 * bt], bv = h[2 * bt + 1];
+                        const uint32_t hi = f2_to_bf16x2(a, bv);
+                        const uint32_t lo = f2_to_bf16x2(a - __uint_as_float(hi << 16), bv - __uint_as_float(hi & 0xffff0000u));
+                        hw[(2 * ti + bt) * 4 + c] = hi;
+                        lw[(2 * ti + bt) * 4 + c] = lo;
+                    }
+                    if (c == 0) {
+                        float* pp = reinterpret_cast<float*>(hr + 2 * kTiles8 * 16);
+                        pp[2 * ti] = part0;
+                        pp[2 * ti + 1] = part1;
+                    }
                 }
             }
             __syncwarp();
@@ -312,38 +329,69 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
         return;
     }
 
-    // compute warps
+    // compute warps: warp w takes groups 2w, 2w+1 of each half
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t grp0 = warp * gps;
-    for (uint32_t j = 0; j < my_items; ++j) {
-        const int s = static_cast<int>(j % S);
-        const int p = static_cast<int>(j % kRedBufs);
-        float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
-        if (!pipe_failed(flags)) {
-            if (mbar_wait_bounded(&bar[s], (j / S) & 1u, kPipeWaitNs)) {
-                const unsigned char* st = stages + s * SL.bytes;
-                const uint16_t* gs = reinterpret_cast<const uint16_t*>(st + SL.gs) + (2 * t) * gpr;
-                const uint16_t* gb = reinterpret_cast<const uint16_t*>(st + SL.gb) + (2 * t) * gpr;
-                const uint16_t* us = reinterpret_cast<const uint16_t*>(st + SL.us) + (2 * t) * gpr;
-                const uint16_t* ub = reinterpret_cast<const uint16_t*>(st + SL.ub) + (2 * t) * gpr;
+    float ag[4], au[4];
+    for (uint32_t u = 0; u < steps; ++u) {
+        const int s = static_cast<int>(u % S);
+        const uint32_t half = u & 1u, j = u >> 1;
+        if (half == 0) {
 #pragma unroll
-                for (uint32_t b = 0; b < gps; b += 4) {
-                    Q4MmaFrag4 fg, fu;
-                    fg.load_smem(st + SL.gate + g * SL.rs, gs, gb, gpr, grp0 + b, t);
-                    fu.load_smem(st + SL.up + g * SL.rs, us, ub, gpr, grp0 + b, t);
-                    q4_mma_pair<kLo>(fg, fu, tile, grp0 + b, g, t, ag, au);
+            for (int i = 0; i < 4; ++i) ag[i] = au[i] = 0.f;
+        }
+        if (!pipe_failed(flags)) {
+            if (mbar_wait_bounded(&bar[s], (u / S) & 1u, kPipeWaitNs)) {
+                const unsigned char* st = stages + s * SL.bytes;
+                const uint32_t gl0 = warp * kGpw;  // first group of this warp within the half
+                // scale / bias pairs of rows g and g+8 for groups gl0, gl0+1
+                const unsigned char* sc = st + SL.sc + gl0 * 2;
+                const uint32_t sgw = *reinterpret_cast<const uint32_t*>(sc + 0 * 16 * SL.srs + g * SL.srs);
+                const uint32_t shw = *reinterpret_cast<const uint32_t*>(sc + 0 * 16 * SL.srs + (g + 8) * SL.srs);
+                const uint32_t bgw = *reinterpret_cast<const uint32_t*>(sc + 1 * 16 * SL.srs + g * SL.srs);
+                const uint32_t bhw = *reinterpret_cast<const uint32_t*>(sc + 1 * 16 * SL.srs + (g + 8) * SL.srs);
+                const uint32_t sgu = *reinterpret_cast<const uint32_t*>(sc + 2 * 16 * SL.srs + g * SL.srs);
+                const uint32_t shu = *reinterpret_cast<const uint32_t*>(sc + 2 * 16 * SL.srs + (g + 8) * SL.srs);
+                const uint32_t bgu = *reinterpret_cast<const uint32_t*>(sc + 3 * 16 * SL.srs + g * SL.srs);
+                const uint32_t bhu = *reinterpret_cast<const uint32_t*>(sc + 3 * 16 * SL.srs + (g + 8) * SL.srs);
+#pragma unroll
+                for (uint32_t gl = 0; gl < kGpw; ++gl) {
+                    const uint32_t grp = half * kHalfGroups + gl0 + gl;  // group index along H
+                    const uint32_t wd = grp * 8 + 2 * t;
+                    const uint4 xb[2] = {tile.act[g * tile.stride + wd], tile.act[g * tile.stride + wd + 1]};
+                    uint4 xl[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                    if (kLo) {
+                        xl[0] = tile.act[(g + 8) * tile.stride + wd];
+                        xl[1] = tile.act[(g + 8) * tile.stride + wd + 1];
+                    }
+                    const float X0 = tile.gsum[(2 * t) * tile.groups + grp];
+                    const float X1 = tile.gsum[(2 * t + 1) * tile.groups + grp];
+                    const uint32_t wo = (gl0 + gl) * 32 + 8 * t;
+                    const uint2 gg = *reinterpret_cast<const uint2*>(st + SL.gate + g * SL.rs + wo);
+                    const uint2 gh = *reinterpret_cast<const uint2*>(st + SL.gate + (g + 8) * SL.rs + wo);
+                    const uint2 ug = *reinterpret_cast<const uint2*>(st + SL.up + g * SL.rs + wo);
+                    const uint2 uh = *reinterpret_cast<const uint2*>(st + SL.up + (g + 8) * SL.rs + wo);
+                    auto bf = [&](uint32_t wv) {
+                        return gl ? __uint_as_float(wv & 0xffff0000u) : __uint_as_float(wv << 16);
+                    };
+                    q4_mma_rows16<kLo>(gg, gh, xb, xl, bf(sgw), bf(shw), bf(bgw), bf(bhw), X0, X1, ag);
+                    q4_mma_rows16<kLo>(ug, uh, xb, xl, bf(sgu), bf(shu), bf(bgu), bf(bhu), X0, X1, au);
                 }
             } else if (lane == 0) {
                 atomicOr(&flags[0], 1u);
                 latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
             }
         }
-        if (j + S < my_items) named_arrive(bar_empty(s), kHandshake);  // stage s released
-        if (j >= kRedBufs) named_sync(bar_free(p), kHandshake);        // the epilogue is done with red[p]
-        float* rw = red + (p * kWarps + warp) * 128;
-        *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(ag[0], ag[1]);
-        *reinterpret_cast<float2*>(rw + 64 + g * 8 + 2 * t) = make_float2(au[0], au[1]);
-        named_arrive(bar_red(p), kHandshake);
+        if (u + S < steps) named_arrive(bar_empty(s), kHandshake);  // stage s released
+        if (half == 1) {
+            const int p = static_cast<int>(j % kRedBufs);
+            if (j >= kRedBufs) named_sync(bar_free(p), kHandshake);  // the epilogue is done with red[p]
+            float* rw = red + (p * kWarps + warp) * 256;
+            *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(ag[0], ag[1]);
+            *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(ag[2], ag[3]);
+            *reinterpret_cast<float2*>(rw + 128 + g * 8 + 2 * t) = make_float2(au[0], au[1]);
+            *reinterpret_cast<float2*>(rw + 128 + (g + 8) * 8 + 2 * t) = make_float2(au[2], au[3]);
+            named_arrive(bar_red(p), kHandshake);
+        }
     }
 }
 

@@ -390,4 +390,38 @@ __device__ __forceinline__ void q4_mma_pair(const Q4MmaFrag4& fa, const Q4MmaFra
     }
 }
 
+// Weight-stationary form for batches of at most 8 tokens: 16 weight rows are
+// the M operand (rows g and g+8 of lane (g,t)) and the tokens the N operand,
+// so every product of the m16n8k16 is useful. For one group the lane holds
+// words 2t, 2t+1 of both rows (wg, wh); xb[m] is token g's staged slot for
+// word 2t+m (xl[m]: its lo residue when activations are f32, folded into the
+// same accumulator). d = [row g | row g+8] x [token 2t | token 2t+1], finished
+// as acc += s * d + (b - 128 s) * X with the tokens' group sums X0, X1.
+template <bool kLo>
+__device__ __forceinline__ void q4_mma_rows16(uint2 wg, uint2 wh, const uint4 (&xb)[2], const uint4 (&xl)[2],
+                                              float s_g, float s_h, float b_g, float b_h, float X0, float X1,
+                                              float (&acc)[4]) {
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t wgs[2] = {wg.x, wg.y}, whs[2] = {wh.x, wh.y};
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+        const uint32_t q = wgs[m], r = whs[m];
+        const uint32_t qa = (q & 0x000F000Fu) | kBf16Offset, ra = (r & 0x000F000Fu) | kBf16Offset;
+        const uint32_t qb = ((q >> 4) & 0x000F000Fu) | kBf16Offset, rb = ((r >> 4) & 0x000F000Fu) | kBf16Offset;
+        const uint32_t qc = ((q >> 8) & 0x000F000Fu) | kBf16Offset, rc = ((r >> 8) & 0x000F000Fu) | kBf16Offset;
+        const uint32_t qd = ((q >> 12) & 0x000F000Fu) | kBf16Offset, rd = ((r >> 12) & 0x000F000Fu) | kBf16Offset;
+        mma_bf16_16816(d, qa, ra, qb, rb, xb[m].x, xb[m].y);
+        mma_bf16_16816(d, qc, rc, qd, rd, xb[m].z, xb[m].w);
+        if (kLo) {
+            mma_bf16_16816(d, qa, ra, qb, rb, xl[m].x, xl[m].y);
+            mma_bf16_16816(d, qc, rc, qd, rd, xl[m].z, xl[m].w);
+        }
+    }
+    const float c_g = fmaf(-128.f, s_g, b_g), c_h = fmaf(-128.f, s_h, b_h);
+    acc[0] = fmaf(s_g, d[0], fmaf(c_g, X0, acc[0]));
+    acc[1] = fmaf(s_g, d[1], fmaf(c_g, X1, acc[1]));
+    acc[2] = fmaf(s_h, d[2], fmaf(c_h, X0, acc[2]));
+    acc[3] = fmaf(s_h, d[3], fmaf(c_h, X1, acc[3]));
+}
+
 }  // namespace pbmoe
