@@ -397,25 +397,61 @@ __device__ __forceinline__ void q4_mma_pair(const Q4MmaFrag4& fa, const Q4MmaFra
 // word 2t+m (xl[m]: its lo residue when activations are f32, folded into the
 // same accumulator). d = [row g | row g+8] x [token 2t | token 2t+1], finished
 // as acc += s * d + (b - 128 s) * X with the tokens' group sums X0, X1.
+// One word pair (word m of rows g and g+8, 8 nibbles each) unpacked and
+// multiplied in a single asm block: the four unpacked bf16x2 registers of an
+// mma's A operand are produced in place, so no operand-marshalling moves are
+// needed between the unpack and the two (four with a lo residue) mma.sync.
+__device__ __forceinline__ void q4_rows16_word(float (&d)[4], uint32_t q, uint32_t r, uint4 xb) {
+    asm("{\n"
+        " .reg .b32 qa, qb, qc, qd, ra, rb, rc, rd, t;\n"
+        " lop3.b32 qa, %4, 0x000F000F, 0x43004300, 0xea;\n"
+        " lop3.b32 ra, %5, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %4, 4;\n lop3.b32 qb, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %5, 4;\n lop3.b32 rb, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %4, 8;\n lop3.b32 qc, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %5, 8;\n lop3.b32 rc, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %4, 12;\n lop3.b32 qd, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %5, 12;\n lop3.b32 rd, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {qa,ra,qb,rb}, {%6,%7}, {%0,%1,%2,%3};\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {qc,rc,qd,rd}, {%8,%9}, {%0,%1,%2,%3};\n"
+        "}\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(q), "r"(r), "r"(xb.x), "r"(xb.y), "r"(xb.z), "r"(xb.w));
+}
+
+// Same with the hi and lo parts of f32 activations accumulated together.
+__device__ __forceinline__ void q4_rows16_word_lo(float (&d)[4], uint32_t q, uint32_t r, uint4 xb, uint4 xl) {
+    asm("{\n"
+        " .reg .b32 qa, qb, qc, qd, ra, rb, rc, rd, t;\n"
+        " lop3.b32 qa, %4, 0x000F000F, 0x43004300, 0xea;\n"
+        " lop3.b32 ra, %5, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %4, 4;\n lop3.b32 qb, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %5, 4;\n lop3.b32 rb, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %4, 8;\n lop3.b32 qc, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %5, 8;\n lop3.b32 rc, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %4, 12;\n lop3.b32 qd, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " shr.b32 t, %5, 12;\n lop3.b32 rd, t, 0x000F000F, 0x43004300, 0xea;\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {qa,ra,qb,rb}, {%6,%7}, {%0,%1,%2,%3};\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {qc,rc,qd,rd}, {%8,%9}, {%0,%1,%2,%3};\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {qa,ra,qb,rb}, {%10,%11}, {%0,%1,%2,%3};\n"
+        " mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {qc,rc,qd,rd}, {%12,%13}, {%0,%1,%2,%3};\n"
+        "}\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(q), "r"(r), "r"(xb.x), "r"(xb.y), "r"(xb.z), "r"(xb.w), "r"(xl.x), "r"(xl.y), "r"(xl.z), "r"(xl.w));
+}
+
 template <bool kLo>
 __device__ __forceinline__ void q4_mma_rows16(uint2 wg, uint2 wh, const uint4 (&xb)[2], const uint4 (&xl)[2],
                                               float s_g, float s_h, float b_g, float b_h, float X0, float X1,
                                               float (&acc)[4]) {
+    static_assert(kBf16Offset == 0x43004300u, "unpack constant of q4_rows16_word");
     float d[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t wgs[2] = {wg.x, wg.y}, whs[2] = {wh.x, wh.y};
-#pragma unroll
-    for (int m = 0; m < 2; ++m) {
-        const uint32_t q = wgs[m], r = whs[m];
-        const uint32_t qa = (q & 0x000F000Fu) | kBf16Offset, ra = (r & 0x000F000Fu) | kBf16Offset;
-        const uint32_t qb = ((q >> 4) & 0x000F000Fu) | kBf16Offset, rb = ((r >> 4) & 0x000F000Fu) | kBf16Offset;
-        const uint32_t qc = ((q >> 8) & 0x000F000Fu) | kBf16Offset, rc = ((r >> 8) & 0x000F000Fu) | kBf16Offset;
-        const uint32_t qd = ((q >> 12) & 0x000F000Fu) | kBf16Offset, rd = ((r >> 12) & 0x000F000Fu) | kBf16Offset;
-        mma_bf16_16816(d, qa, ra, qb, rb, xb[m].x, xb[m].y);
-        mma_bf16_16816(d, qc, rc, qd, rd, xb[m].z, xb[m].w);
-        if (kLo) {
-            mma_bf16_16816(d, qa, ra, qb, rb, xl[m].x, xl[m].y);
-            mma_bf16_16816(d, qc, rc, qd, rd, xl[m].z, xl[m].w);
-        }
+    if (kLo) {
+        q4_rows16_word_lo(d, wg.x, wh.x, xb[0], xl[0]);
+        q4_rows16_word_lo(d, wg.y, wh.y, xb[1], xl[1]);
+    } else {
+        q4_rows16_word(d, wg.x, wh.x, xb[0]);
+        q4_rows16_word(d, wg.y, wh.y, xb[1]);
     }
     const float c_g = fmaf(-128.f, s_g, b_g), c_h = fmaf(-128.f, s_h, b_h);
     acc[0] = fmaf(s_g, d[0], fmaf(c_g, X0, acc[0]));
