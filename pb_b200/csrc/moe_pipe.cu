@@ -32,8 +32,10 @@
 //       warps = 8 K-slices of each step; SwiGLU (silu(g)*u,
 //       shaders.metal:1699-1708) is written as bf16 hi/lo pair slots +
 //       per-8 partial sums (MoeWs::h_perm), the down kernel's input.
-//   moe_down_pipe_kernel  item = (group, 64 down rows); warp w owns rows
-//       8w..8w+7. Weight stages hold only weights: the routed activations of
+//   moe_down_pipe_kernel  item = (group, 64 down rows): warp w takes the
+//       16-row block w%4 (the mma's M operand; the group's routes are N) over
+//       K-half w/4, and the two halves are summed through shared memory.
+//       Weight stages hold only weights: the routed activations of
 //       the (at most two) groups of the CTA's run are copied once into their
 //       own buffers after the programmatic-dependent-launch wait, while the
 //       first weight stages are requested before it.
@@ -66,8 +68,10 @@ struct UpCfg {
 // Named barrier ids (0 is __syncthreads).
 constexpr int kBarStage = 1;                                        // compute warps only
 __device__ __forceinline__ int bar_empty(int s) { return 2 + s; }  // 2..6
-__device__ __forceinline__ int bar_red(int p) { return 7 + p; }    // 7, 8
-__device__ __forceinline__ int bar_free(int p) { return 9 + p; }   // 9, 10
+__device__ __forceinline__ int bar_red(int p) { return 7 + p; }    // 7, 8 (up)
+__device__ __forceinline__ int bar_free(int p) { return 9 + p; }   // 9, 10 (up)
+__device__ __forceinline__ int bar_pair(int rb) { return 5 + rb; }       // 5..8 (down)
+__device__ __forceinline__ int bar_pair_free(int rb) { return 9 + rb; }  // 9..12 (down)
 
 static int device_sm_count() {
     static int cached[64] = {0};
@@ -173,9 +177,11 @@ __host__ __device__ inline DownAct down_act(uint32_t I) {
     return {0, part, ps, (part + 8 * ps + 127) / 128 * 128};
 }
 
+// stages, two activation buffers, K-half partial sums [4 row blocks][32 lanes][4], flags, mbarriers, plan
+constexpr uint32_t kDownRedBytes = 4 * 32 * 4 * 4;
 __host__ __device__ inline size_t down_pipe_smem(uint32_t I, uint32_t cap_g, uint32_t cap_r) {
-    return size_t(kDownStages) * down_stage(I).bytes + 2 * size_t(down_act(I).bytes) + 16 + (kDownStages + 2) * 8 +
-           plan_smem_bytes(cap_g, cap_r);
+    return size_t(kDownStages) * down_stage(I).bytes + 2 * size_t(down_act(I).bytes) + kDownRedBytes + 16 +
+           (kDownStages + 2) * 8 + plan_smem_bytes(cap_g, cap_r);
 }
 
 // ---------------------------------------------------------------- up
@@ -409,7 +415,8 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
     const DownAct AL = down_act(I);
     unsigned char* stages = smem_raw;
     unsigned char* abuf = stages + S * SL.bytes;  // [2][AL.bytes]
-    uint32_t* flags = reinterpret_cast<uint32_t*>(abuf + 2 * AL.bytes);
+    float4* kred = reinterpret_cast<float4*>(abuf + 2 * AL.bytes);  // [4 row blocks][32 lanes]
+    uint32_t* flags = reinterpret_cast<uint32_t*>(abuf + 2 * AL.bytes + kDownRedBytes);
     uint64_t* bar = reinterpret_cast<uint64_t*>(flags + 4);  // [S] weight stages, [2] activation buffers
     const PlanSmem pl = plan_at(bar + S + 2, cap_g, cap_r);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -490,10 +497,12 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
 
     pdl_launch_dependents();  // the combine kernel waits for this whole grid
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t rw0 = warp * 8;  // this warp's 8 rows within the 64-row tile
+    const int rb = warp & 3, kh = warp >> 2;  // 16-row block, K-half
+    constexpr uint32_t kHalfGroups = gpr / 2;
+    static_assert(kHalfGroups == 4, "four groups per K-half");
     uint32_t cur_group = 0xffffffffu;
     ActTile tile{};
-    float X[gpr];  // route g's activation sums of the I/64 groups, per current expert group
+    float X0[kHalfGroups], X1[kHalfGroups];  // activation sums of routes 2t, 2t+1 over this K-half's groups
     for (uint32_t j = 0; j < my_items; ++j) {
         const int s = static_cast<int>(j % S);
         const uint32_t k = k0 + j;
@@ -505,46 +514,69 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
             if (ok) {
                 unsigned char* ab = abuf + hb * AL.bytes;
                 tile = act_tile_at(ab + AL.act, I, 16);
-                const float* prow = reinterpret_cast<const float*>(ab + AL.part + g * AL.part_stride);
+                const float* p0 = reinterpret_cast<const float*>(ab + AL.part + (2 * t) * AL.part_stride);
+                const float* p1 = reinterpret_cast<const float*>(ab + AL.part + (2 * t + 1) * AL.part_stride);
 #pragma unroll
-                for (uint32_t q = 0; q < gpr; ++q) {
-                    // each lane adds two of the eight per-8 partials of a group, the quad finishes the sum
-                    const float2 pv = *reinterpret_cast<const float2*>(prow + q * 8 + 2 * t);
-                    float v = pv.x + pv.y;
-                    v += __shfl_xor_sync(kFull, v, 1);
-                    v += __shfl_xor_sync(kFull, v, 2);
-                    X[q] = v;
+                for (uint32_t i = 0; i < kHalfGroups; ++i) {
+                    const uint32_t o = (kh * kHalfGroups + i) * 8;
+                    const float4 a0 = *reinterpret_cast<const float4*>(p0 + o), a1 = *reinterpret_cast<const float4*>(p0 + o + 4);
+                    const float4 c0 = *reinterpret_cast<const float4*>(p1 + o), c1 = *reinterpret_cast<const float4*>(p1 + o + 4);
+                    X0[i] = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
+                    X1[i] = ((c0.x + c0.y) + (c0.z + c0.w)) + ((c1.x + c1.y) + (c1.z + c1.w));
                 }
                 cur_group = gi;
             }
         }
         if (ok) ok = mbar_wait_bounded(&bar[s], (j / S) & 1u, kPipeWaitNs);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows (g, g+8) x routes (2t, 2t+1)
         if (ok) {
-            const uint32_t start = pl.start[gi], n = pl.count[gi];
             const unsigned char* st = stages + s * SL.bytes;
-            const uint16_t* ds = reinterpret_cast<const uint16_t*>(st + SL.s) + (rw0 + 2 * t) * gpr;
-            const uint16_t* db = reinterpret_cast<const uint16_t*>(st + SL.b) + (rw0 + 2 * t) * gpr;
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t rg = rb * 16 + g;
+            // scale / bias of rows rg, rg+8 for the four groups of this K-half
+            const uint2 sg = *reinterpret_cast<const uint2*>(st + SL.s + rg * (gpr * 2) + kh * 8);
+            const uint2 sh = *reinterpret_cast<const uint2*>(st + SL.s + (rg + 8) * (gpr * 2) + kh * 8);
+            const uint2 bg = *reinterpret_cast<const uint2*>(st + SL.b + rg * (gpr * 2) + kh * 8);
+            const uint2 bh = *reinterpret_cast<const uint2*>(st + SL.b + (rg + 8) * (gpr * 2) + kh * 8);
 #pragma unroll
-            for (uint32_t b = 0; b < gpr; b += 4) {
-                const float Xb[4] = {X[b], X[b + 1], X[b + 2], X[b + 3]}, X2[4] = {0.f, 0.f, 0.f, 0.f};
-                Q4MmaFrag4 f;
-                f.load_smem(st + SL.w + (rw0 + g) * SL.rs, ds, db, gpr, b, t);
-                f.compute_x<true, false>(tile, b, g, t, Xb, X2, acc);
+            for (uint32_t i = 0; i < kHalfGroups; ++i) {
+                const uint32_t grp = kh * kHalfGroups + i;
+                const uint32_t wd = grp * 8 + 2 * t;
+                const uint4 xb[2] = {tile.act[g * tile.stride + wd], tile.act[g * tile.stride + wd + 1]};
+                const uint4 xl[2] = {tile.act[(g + 8) * tile.stride + wd], tile.act[(g + 8) * tile.stride + wd + 1]};
+                const uint32_t wo = grp * 32 + 8 * t;
+                const uint2 wg = *reinterpret_cast<const uint2*>(st + SL.w + rg * SL.rs + wo);
+                const uint2 wh = *reinterpret_cast<const uint2*>(st + SL.w + (rg + 8) * SL.rs + wo);
+                q4_mma_rows16<true>(wg, wh, xb, xl, Q4MmaFrag4::pick(sg, i), Q4MmaFrag4::pick(sh, i),
+                                    Q4MmaFrag4::pick(bg, i), Q4MmaFrag4::pick(bh, i), X0[i], X1[i], acc);
             }
-            if (j + S < my_items) named_arrive(bar_empty(s), kHandshake);  // stage s released
-            if (static_cast<uint32_t>(g) < n) {
-                const uint32_t route = pl.route[start + g];
-                *reinterpret_cast<float2*>(ws.y + static_cast<size_t>(route) * H + r0 + rw0 + 2 * t) =
-                    make_float2(acc[0], acc[1]);
-            }
+        } else if (lane == 0 && !pipe_failed(flags)) {
+            atomicOr(&flags[0], 1u);
+            latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+        }
+        if (j + S < my_items) named_arrive(bar_empty(s), kHandshake);  // stage s released
+        // the K-halves meet: half 1 hands its partials to half 0, which stores y
+        if (kh == 1) {
+            if (j > 0) named_sync(bar_pair_free(rb), 64);
+            kred[rb * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            named_arrive(bar_pair(rb), 64);
         } else {
-            if (lane == 0 && !pipe_failed(flags)) {
-                atomicOr(&flags[0], 1u);
-                latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+            named_sync(bar_pair(rb), 64);
+            const float4 o = kred[rb * 32 + lane];
+            if (j + 1 < my_items) named_arrive(bar_pair_free(rb), 64);
+            if (ok && !pipe_failed(flags)) {
+                const uint32_t start = pl.start[gi], n = pl.count[gi];
+                const uint32_t row = r0 + rb * 16 + g;
+                const float v[4] = {acc[0] + o.x, acc[1] + o.y, acc[2] + o.z, acc[3] + o.w};
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const uint32_t q = 2 * t + c;
+                    if (q < n) {
+                        float* yr = ws.y + static_cast<size_t>(pl.route[start + q]) * H;
+                        yr[row] = v[c];
+                        yr[row + 8] = v[2 + c];
+                    }
+                }
             }
-            __syncwarp();
-            if (j + S < my_items) named_arrive(bar_empty(s), kHandshake);
         }
     }
 }

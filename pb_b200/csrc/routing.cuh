@@ -74,45 +74,13 @@ __device__ __forceinline__ void stage_logits_warp(const float* __restrict__ lg, 
 // selected p_k (summed in slot order, scheduler/expert_access.rs:80-133) and
 // the routed scaling factor. Invalid sums latch PBMOE_DEV_ERR_ROUTE_WEIGHTS
 // (where the reference bails) and write zero weights.
-__device__ void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
-                                 float routed_scale, uint32_t* ids_out, float* w_out, uint32_t* status) {
+// Weights of the K selected slots (lane k = slot k holds its score `sval` and
+// expert `sid`), given the token's logit maximum m and softmax denominator sum.
+__device__ __forceinline__ void route_weights_lanes(float sval, uint32_t sid, float m, float sum, uint32_t K,
+                                                    uint32_t normalization, float routed_scale, uint32_t* ids_out,
+                                                    float* w_out, uint32_t* status) {
     const int lane = threadIdx.x & 31;
-    const float NEG_INF = -__int_as_float(0x7f800000);
-    float m = NEG_INF;
-    for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, s[e]);
-    m = warp_max(m);
-    float sum = 0.f;
-    for (uint32_t e = lane; e < E; e += 32) sum += expf(s[e] - m);
-    sum = warp_sum(sum);
-
     const bool is_slot = static_cast<uint32_t>(lane) < K;
-    float sval = NEG_INF;
-    uint32_t sid = 0;
-    // current minimum slot (value mv, index mslot); all slots start at -inf
-    float mv = NEG_INF;
-    int mslot = 0;
-    for (uint32_t base = 0; base < E; base += 32) {
-        const uint32_t e = base + lane;
-        const float v = e < E ? s[e] : NEG_INF;
-        uint32_t cand = __ballot_sync(kFull, v > mv);
-        while (cand) {
-            const int src = __ffs(cand) - 1;
-            cand &= cand - 1;
-            const float ve = __shfl_sync(kFull, v, src);
-            if (ve > mv) {  // warp-uniform: mv is the exact current minimum
-                if (lane == mslot) {
-                    sval = ve;
-                    sid = base + static_cast<uint32_t>(src);
-                }
-                const uint32_t key = is_slot ? float_order_key(sval) : 0xffffffffu;
-                const uint32_t mk = __reduce_min_sync(kFull, key);
-                mslot = __ffs(__ballot_sync(kFull, key == mk)) - 1;
-                mv = __shfl_sync(kFull, sval, mslot);
-                cand &= __ballot_sync(kFull, v > mv);
-            }
-        }
-    }
-
     // softmax probability of each selected slot
     const bool have_inverse = sum > 0.f && isfinite(sum);
     const float inverse_sum = have_inverse ? 1.0f / sum : 0.f;
@@ -145,6 +113,81 @@ __device__ void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_
         w_out[lane] = w;
     }
     __syncwarp();
+}
+
+// Inverse of float_order_key (the zero key maps back to +0.0, which compares
+// equal to -0.0 as the reference's comparisons do).
+__device__ __forceinline__ float float_from_order_key(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__device__ void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
+                                 float routed_scale, uint32_t* ids_out, float* w_out, uint32_t* status) {
+    const int lane = threadIdx.x & 31;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    // the lane's scores stay in registers for the max, the sum and the scan
+    constexpr int kRegChunks = 16;
+    const bool in_regs = E <= 32u * kRegChunks;
+    float v[kRegChunks];
+    float m = NEG_INF;
+    float sum = 0.f;
+    if (in_regs) {
+#pragma unroll
+        for (int c = 0; c < kRegChunks; ++c) {
+            const uint32_t e = c * 32 + lane;
+            v[c] = e < E ? s[e] : NEG_INF;
+        }
+#pragma unroll
+        for (int c = 0; c < kRegChunks; ++c) m = fmaxf(m, v[c]);
+        m = warp_max(m);
+#pragma unroll
+        for (int c = 0; c < kRegChunks; ++c)
+            if (static_cast<uint32_t>(c * 32 + lane) < E) sum += expf(v[c] - m);
+    } else {
+        for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, s[e]);
+        m = warp_max(m);
+        for (uint32_t e = lane; e < E; e += 32) sum += expf(s[e] - m);
+    }
+    sum = warp_sum(sum);
+
+    const bool is_slot = static_cast<uint32_t>(lane) < K;
+    float sval = NEG_INF;
+    uint32_t sid = 0;
+    uint32_t key = is_slot ? float_order_key(NEG_INF) : 0xffffffffu;
+    // current minimum slot (value mv, index mslot); all slots start at -inf
+    float mv = NEG_INF;
+    int mslot = 0;
+    // One dependent chain per replacement: select in the slot lane, min-reduce
+    // the slot keys, then (in parallel) the new minimum's value from its key
+    // and its first slot from a ballot. Candidates are tested against the
+    // exact current minimum; stale ones are simply rejected.
+    auto scan_chunk = [&](uint32_t base, float vc) {
+        uint32_t cand = __ballot_sync(kFull, vc > mv);
+        while (cand) {
+            const int src = __ffs(cand) - 1;
+            cand &= cand - 1;
+            const float ve = __shfl_sync(kFull, vc, src);
+            if (ve > mv) {  // warp-uniform
+                const uint32_t kn = float_order_key(ve);
+                if (lane == mslot) {
+                    sval = ve;
+                    sid = base + static_cast<uint32_t>(src);
+                    key = kn;
+                }
+                const uint32_t mk = __reduce_min_sync(kFull, key);
+                mslot = __ffs(__ballot_sync(kFull, key == mk)) - 1;
+                mv = float_from_order_key(mk);
+            }
+        }
+    };
+    if (in_regs) {
+#pragma unroll
+        for (int c = 0; c < kRegChunks; ++c)
+            if (static_cast<uint32_t>(c * 32) < E) scan_chunk(c * 32, v[c]);
+    } else {
+        for (uint32_t base = 0; base < E; base += 32) scan_chunk(base, base + lane < E ? s[base + lane] : NEG_INF);
+    }
+    route_weights_lanes(sval, sid, m, sum, K, normalization, routed_scale, ids_out, w_out, status);
 }
 
 // Block-wide exclusive scan of n <= 4096 u32 values in shared memory, in
