@@ -225,6 +225,54 @@ PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* config, const pbmoe
                                      void* next_normed, uint32_t* device_status, char* error_buf,
                                      size_t error_len, void* stream);
 
+/* ---------------------------------------------------------------- MLA decode */
+
+/* Shapes of MLA absorbed decode attention (MlaAttentionLayout,
+ * weights/mod.rs:651-664). The tensor-core kernels take heads 16, rope 64,
+ * latent 512 and v 128 (any nope dim); other shapes are PBMOE_ERR_UNSUPPORTED. */
+typedef struct pbmoe_mla_config {
+    uint32_t heads;
+    uint32_t nope_dim;
+    uint32_t rope_dim;
+    uint32_t latent_dim; /* kv_lora_rank */
+    uint32_t v_dim;
+    float softmax_scale; /* 0 = 1/sqrt(nope_dim + rope_dim) (weights/store.rs:1262) */
+} pbmoe_mla_config;
+
+/* One decode step of `batch` sequences, each attending over its own latent
+ * cache (KvCache::mla_records, state/kv_cache.rs:414-450). */
+typedef struct pbmoe_mla_args {
+    uint32_t batch;                 /* 1..32                                             */
+    const uint32_t* seq_lens;       /* HOST array [batch]: cache length of each sequence */
+    const void* query;              /* [batch x heads x (nope + rope)] in query_dtype;
+                                       the rope part already rotated                     */
+    pbmoe_dtype query_dtype;
+    const uint16_t* const* c_kv;    /* HOST array [batch] of device pointers:
+                                       bf16 [seq_len x latent], 16-byte aligned          */
+    const uint16_t* const* k_rope;  /* HOST array [batch] of device pointers:
+                                       bf16 [seq_len x rope], rotated at write,
+                                       16-byte aligned                                   */
+    const uint16_t* w_uk;           /* bf16 [heads x nope x latent] (absorbed into q)    */
+    const uint16_t* w_uv;           /* bf16 [heads x v x latent], 16-byte aligned        */
+    void* out;                      /* [batch x heads x v] in out_dtype                  */
+    pbmoe_dtype out_dtype;
+} pbmoe_mla_args;
+
+/* Size the context's MLA workspace for batches of up to `max_batch`
+ * sequences (any cache length). Allocation happens here, never in
+ * pbmoe_mla_decode. */
+PBMOE_API int pbmoe_mla_reserve(pbmoe_ctx* ctx, const pbmoe_mla_config* config, uint32_t max_batch);
+
+/* out[b, h, :] = W_UV[h] . sum_t softmax_t(s_t) c_kv_b[t] with
+ * s_t = ((W_UK[h]^T q_nope[b, h]) . c_kv_b[t] + q_rope[b, h] . k_rope_b[t]) * scale.
+ * Replaces MetalExecutionFacade::resident_glm_mla_absorbed_attention /
+ * resident_glm_mla_fused_attention (runtime/mod.rs:1327-1403, Metal kernels
+ * glm_mla_absorbed_scores / glm_mla_softmax / glm_mla_context,
+ * shaders.metal:1603-1682) and the CPU mla_absorbed_attention
+ * (weights/store.rs:1179-1327) with bf16 W_UK / W_UV. */
+PBMOE_API int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* config, const pbmoe_mla_args* args,
+                               void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -37,7 +37,7 @@ ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR = 1
 EXPORTED = [
     "pbmoe_init", "pbmoe_destroy", "pbmoe_last_error", "pbmoe_abi_version", "pbmoe_reserve",
     "pbmoe_moe_workspace_bytes", "pbmoe_device_status", "pbmoe_fixed_q4_layout", "pbmoe_q4_matvec",
-    "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static",
+    "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static", "pbmoe_mla_reserve", "pbmoe_mla_decode",
 ]
 
 
@@ -64,6 +64,17 @@ class MoeWeights(C.Structure):
 class MoeDebug(C.Structure):
     _fields_ = [("router_logits", C.c_void_p), ("route_ids", C.c_void_p), ("route_weights", C.c_void_p),
                 ("shared_logit", C.c_void_p), ("phase_events", C.c_void_p)]
+
+
+class MlaConfig(C.Structure):
+    _fields_ = [("heads", C.c_uint32), ("nope_dim", C.c_uint32), ("rope_dim", C.c_uint32),
+                ("latent_dim", C.c_uint32), ("v_dim", C.c_uint32), ("softmax_scale", C.c_float)]
+
+
+class MlaArgs(C.Structure):
+    _fields_ = [("batch", C.c_uint32), ("seq_lens", C.c_void_p), ("query", C.c_void_p), ("query_dtype", C.c_int),
+                ("c_kv", C.c_void_p), ("k_rope", C.c_void_p), ("w_uk", C.c_void_p), ("w_uv", C.c_void_p),
+                ("out", C.c_void_p), ("out_dtype", C.c_int)]
 
 
 class PbmoeError(RuntimeError):
@@ -97,6 +108,8 @@ def load():
         L.pbmoe_route_topk.argtypes = [vp, vp, u32, u32, u32, u32, C.c_float, vp, vp, vp]
         L.pbmoe_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32, u32,
                                       vp, vp, C.POINTER(MoeDebug), vp]
+        L.pbmoe_mla_reserve.argtypes = [vp, C.POINTER(MlaConfig), u32]
+        L.pbmoe_mla_decode.argtypes = [vp, C.POINTER(MlaConfig), C.POINTER(MlaArgs), vp]
         L.pbmoe_moe_layer_static.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
                                              u32, vp, vp, vp, C.c_char_p, C.c_size_t, vp]
         _lib = L
@@ -181,10 +194,27 @@ class Context:
             _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed),
             C.byref(debug) if debug is not None else None, self.stream_ptr(stream)))
 
+    def mla_reserve(self, config: MlaConfig, max_batch: int):
+        self.check(self.lib.pbmoe_mla_reserve(self.h, C.byref(config), max_batch))
+
+    def mla_decode(self, config: MlaConfig, query, c_kv, k_rope, w_uk, w_uv, out, stream=None):
+        """query [B, heads, nope+rope]; c_kv / k_rope: lists of B device tensors."""
+        b = len(c_kv)
+        lens = (C.c_uint32 * b)(*[int(t.shape[0]) for t in c_kv])
+        ckv = (C.c_void_p * b)(*[t.data_ptr() for t in c_kv])
+        kr = (C.c_void_p * b)(*[t.data_ptr() for t in k_rope])
+        args = MlaArgs(b, C.cast(lens, C.c_void_p), query.data_ptr(), _dtype_code(query), C.cast(ckv, C.c_void_p),
+                       C.cast(kr, C.c_void_p), w_uk.data_ptr(), w_uv.data_ptr(), out.data_ptr(), _dtype_code(out))
+        self.check(self.lib.pbmoe_mla_decode(self.h, C.byref(config), C.byref(args), self.stream_ptr(stream)))
+
     def device_status(self, clear=True, stream=None) -> int:
         v = C.c_uint32()
         self.check(self.lib.pbmoe_device_status(self.h, self.stream_ptr(stream), C.byref(v), 1 if clear else 0))
         return v.value
+
+
+def mla_config(heads=16, nope=128, rope=64, latent=512, v_dim=128, scale=0.0) -> MlaConfig:
+    return MlaConfig(heads, nope, rope, latent, v_dim, scale)
 
 
 def moe_config(layout: ExpertLayout, num_experts, top_k, normalization=0, routed_scale=1.0, eps=1e-6) -> MoeConfig:

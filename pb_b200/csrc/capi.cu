@@ -17,6 +17,10 @@ struct pbmoe_ctx {
     void* ws_base = nullptr;     // MoE workspace
     size_t ws_bytes = 0;
     uint32_t ws_tokens = 0, ws_E = 0, ws_K = 0, ws_H = 0, ws_I = 0;
+    void* mla_base = nullptr;  // MLA decode workspace
+    size_t mla_bytes = 0;
+    uint32_t mla_batch = 0;
+    int num_sms = 0;
     std::string last_error;
 };
 
@@ -204,6 +208,7 @@ int pbmoe_destroy(pbmoe_ctx* ctx) {
     {
         DeviceGuard g(ctx->device);
         if (ctx->ws_base) cudaFree(ctx->ws_base);
+        if (ctx->mla_base) cudaFree(ctx->mla_base);
         if (ctx->status) cudaFree(ctx->status);
     }
     delete ctx;
@@ -402,3 +407,121 @@ int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_w
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- MLA decode
+namespace {
+
+struct MlaWsSizes {
+    size_t qp, partial, ctx, total;
+};
+
+MlaWsSizes mla_ws_sizes(uint32_t max_batch, int num_sms) {
+    MlaWsSizes w{};
+    w.qp = align_up(size_t(max_batch) * 16 * 576 * 4, 256);
+    // batch x splits <= num_sms + batch (pbmoe::mla_plan_splits)
+    w.partial = align_up((size_t(num_sms) + 2 * max_batch) * 16 * 514 * 4, 256);
+    w.ctx = align_up(size_t(max_batch) * 16 * 512 * 4, 256);
+    w.total = w.qp + w.partial + w.ctx;
+    return w;
+}
+
+int check_mla_config(pbmoe_ctx* ctx, const pbmoe_mla_config* c) {
+    if (!c) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: null config");
+    if (c->heads == 0 || c->nope_dim == 0 || c->rope_dim == 0 || c->latent_dim == 0 || c->v_dim == 0)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: zero dimension");
+    if (!pbmoe::mla_shape_supported(c->heads, c->rope_dim, c->latent_dim, c->v_dim) || c->nope_dim > 1024)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported MLA shape on CUDA: heads=%u nope=%u rope=%u latent=%u v=%u (built for "
+                    "heads 16, rope 64, latent 512, v 128, nope <= 1024)",
+                    c->heads, c->nope_dim, c->rope_dim, c->latent_dim, c->v_dim);
+    if (!(c->softmax_scale >= 0.f) || !std::isfinite(c->softmax_scale))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: softmax_scale must be finite and >= 0");
+    return PBMOE_OK;
+}
+
+int sm_count(pbmoe_ctx* ctx) {
+    if (ctx->num_sms <= 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, ctx->device) != cudaSuccess || n <= 0) n = 148;
+        ctx->num_sms = n;
+    }
+    return ctx->num_sms;
+}
+
+}  // namespace
+
+int pbmoe_mla_reserve(pbmoe_ctx* ctx, const pbmoe_mla_config* c, uint32_t max_batch) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    int rc = check_mla_config(ctx, c);
+    if (rc) return rc;
+    if (max_batch == 0 || max_batch > pbmoe::kMlaMaxBatch)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: max_batch %u outside 1..%u", max_batch,
+                    pbmoe::kMlaMaxBatch);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    const size_t need = mla_ws_sizes(max_batch, sm_count(ctx)).total;
+    if (ctx->mla_base && ctx->mla_bytes >= need && ctx->mla_batch >= max_batch) return PBMOE_OK;
+    if (ctx->mla_base) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before MLA workspace resize");
+        cudaFree(ctx->mla_base);
+        ctx->mla_base = nullptr;
+        ctx->mla_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->mla_base, need);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "MLA workspace allocation");
+    ctx->mla_bytes = need;
+    ctx->mla_batch = max_batch;
+    return PBMOE_OK;
+}
+
+int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_args* a, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    int rc = check_mla_config(ctx, c);
+    if (rc) return rc;
+    if (!a || !a->seq_lens || !a->query || !a->c_kv || !a->k_rope || !a->w_uk || !a->w_uv || !a->out)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: null pointer");
+    if (a->batch == 0 || a->batch > pbmoe::kMlaMaxBatch)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: batch %u outside 1..%u", a->batch, pbmoe::kMlaMaxBatch);
+    if ((a->query_dtype != PBMOE_F32 && a->query_dtype != PBMOE_BF16) ||
+        (a->out_dtype != PBMOE_F32 && a->out_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: unknown dtype");
+    if (!ctx->mla_base || ctx->mla_batch < a->batch)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "mla: workspace reserved for batch<=%u, call needs %u "
+                    "(call pbmoe_mla_reserve)", ctx->mla_batch, a->batch);
+    if (!aligned(a->query, a->query_dtype == PBMOE_F32 ? 4 : 2) ||
+        !aligned(a->out, a->out_dtype == PBMOE_F32 ? 4 : 2) || !aligned(a->w_uk, 2) || !aligned(a->w_uv, 16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: misaligned query / out / W_UK / W_UV");
+    pbmoe::MlaLaunch L{};
+    L.batch = a->batch;
+    L.nope = c->nope_dim;
+    L.scale = c->softmax_scale > 0.f ? c->softmax_scale
+                                     : 1.0f / std::sqrt(static_cast<float>(c->nope_dim + c->rope_dim));
+    L.q = a->query;
+    L.q_dtype = a->query_dtype;
+    for (uint32_t b = 0; b < a->batch; ++b) {
+        if (a->seq_lens[b] == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: sequence %u is empty", b);
+        if (!a->c_kv[b] || !a->k_rope[b])
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: null cache pointer for sequence %u", b);
+        if (!aligned(a->c_kv[b], 16) || !aligned(a->k_rope[b], 16))
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: cache of sequence %u not 16-byte aligned", b);
+        L.seqs.c_kv[b] = a->c_kv[b];
+        L.seqs.k_rope[b] = a->k_rope[b];
+        L.seqs.len[b] = a->seq_lens[b];
+    }
+    L.w_uk = a->w_uk;
+    L.w_uv = a->w_uv;
+    L.out = a->out;
+    L.out_dtype = a->out_dtype;
+    const MlaWsSizes w = mla_ws_sizes(ctx->mla_batch, sm_count(ctx));
+    char* base = static_cast<char*>(ctx->mla_base);
+    L.qp = reinterpret_cast<float*>(base);
+    L.partial = reinterpret_cast<float*>(base + w.qp);
+    L.ctx = reinterpret_cast<float*>(base + w.qp + w.partial);
+    pbmoe::mla_plan_splits(L, sm_count(ctx), L.split_tokens, L.splits);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    cudaError_t e = pbmoe::mla_decode_launch(L, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "MLA decode launch");
+    return PBMOE_OK;
+}

@@ -108,4 +108,37 @@ struct Q4MatvecArgs {
 // a CTA has.
 cudaError_t q4_matvec_launch(const Q4MatvecArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- MLA decode (mla.cu)
+constexpr uint32_t kMlaMaxBatch = 32;
+
+// Per-sequence latent caches, passed by value to the attention kernel.
+struct MlaSeqs {
+    const uint16_t* c_kv[kMlaMaxBatch];    // bf16 [len x latent]
+    const uint16_t* k_rope[kMlaMaxBatch];  // bf16 [len x rope]
+    uint32_t len[kMlaMaxBatch];
+};
+
+struct MlaLaunch {
+    uint32_t batch, nope;
+    float scale;
+    const void* q;  // [batch x 16 x (nope + 64)], rope part rotated
+    pbmoe_dtype q_dtype;
+    MlaSeqs seqs;
+    const uint16_t* w_uk;  // bf16 [16 x nope x 512]
+    const uint16_t* w_uv;  // bf16 [16 x 128 x 512]
+    void* out;             // [batch x 16 x 128]
+    pbmoe_dtype out_dtype;
+    // workspace
+    float* qp;       // [batch x 16 x 576] scaled absorbed queries
+    float* partial;  // [batch x splits x 16 x 514] per-split (max, sum, O)
+    float* ctx;      // [batch x 16 x 512]
+    uint32_t split_tokens, splits;
+};
+
+bool mla_shape_supported(uint32_t heads, uint32_t rope, uint32_t latent, uint32_t v_dim);
+size_t mla_smem_bytes();
+void mla_plan_splits(const MlaLaunch& a, int num_sms, uint32_t& split_tokens, uint32_t& splits);
+uint32_t mla_max_splits(uint32_t max_batch, int num_sms);
+cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s);
+
 }  // namespace pbmoe

@@ -1,0 +1,472 @@
+// mla.cu — MLA absorbed decode attention (split-KV, tensor cores).
+//
+// Reference semantics (mla_absorbed_attention, weights/store.rs:1179-1327;
+// Metal glm_mla_absorbed_scores / glm_mla_softmax / glm_mla_context,
+// shaders.metal:1603-1682), per sequence and head h:
+//   q_lat[c] = sum_d q_nope[h,d] * W_UK[h,d,c]                 (absorb)
+//   s_t      = (q_lat . c_kv[t] + q_rope[h] . k_rope[t]) * scale
+//   p        = softmax_t(s)
+//   ctx[c]   = sum_t p_t * c_kv[t,c]
+//   out[h,d] = sum_c ctx[c] * W_UV[h,d,c]
+// with scale = 1/sqrt(nope + rope) (store.rs:1262) and k_rope already rotated
+// when the cache was written (runtime/mod.rs:2906-2913).
+//
+// Four launches:
+//   1. mla_absorb_kernel   q_lat for every (sequence, head), W_UK read once;
+//                          writes Q' = [q_lat | q_rope] * scale * log2(e) (f32).
+//   2. mla_attn_kernel     one CTA per (KV split, sequence): every 64-token
+//                          tile of the split's latent cache is read from HBM
+//                          once (cp.async, double-buffered) and serves all 16
+//                          heads. S = Q' K^T (16 heads = the mma's M; Q' as
+//                          bf16 hi + lo so scores keep ~16 mantissa bits),
+//                          online softmax in base 2, O += P C with P in bf16.
+//                          Writes the split's (max, sum, O[16 x 512]).
+//   3. mla_combine_kernel  merges the splits of each (sequence, head) -> ctx.
+//   4. mla_out_kernel      out = W_UV ctx, W_UV read once for the batch.
+// Shapes: 16 heads, latent 512, rope 64, v 128 (any nope), batch <= 32.
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pbmoe {
+
+constexpr uint32_t kMlaHeads = 16, kMlaLatent = 512, kMlaRope = 64, kMlaV = 128;
+constexpr uint32_t kMlaK = kMlaLatent + kMlaRope;  // 576: score dimension
+constexpr uint32_t kMlaTile = 64;                  // tokens per tile
+constexpr uint32_t kMlaWarps = 4;
+// shared-memory row strides (bytes), padded by 16 against ldmatrix bank conflicts
+constexpr uint32_t kQRow = kMlaK * 2 + 16;        // Q' hi / lo rows
+constexpr uint32_t kCRow = kMlaLatent * 2 + 16;   // c_kv rows
+constexpr uint32_t kRRow = kMlaRope * 2 + 16;     // k_rope rows
+constexpr uint32_t kPRow = kMlaTile * 2 + 16;     // P rows
+constexpr uint32_t kStageBytes = kMlaTile * (kCRow + kRRow);
+constexpr uint32_t kMlaPartialFloats = 2 + kMlaLatent;  // max, sum, O
+constexpr size_t kMlaSmem = 2 * size_t(kMlaHeads) * kQRow + 2 * size_t(kStageBytes) + kMlaHeads * kPRow +
+                            kMlaWarps * kMlaHeads * 4 * 2;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 16-byte global -> shared async copy; src_bytes = 0 zero-fills the chunk.
+__device__ __forceinline__ void cp16_zfill(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return static_cast<uint32_t>(f32_to_bf16_bits(lo)) | (static_cast<uint32_t>(f32_to_bf16_bits(hi)) << 16);
+}
+
+// ---------------------------------------------------------------- 1. absorb
+// grid (heads, latent/128, 1), 128 threads: thread = one latent column c of
+// head h for every sequence. Writes Q'[b][h][0..511] = q_lat * k and
+// Q'[b][h][512..575] = q_rope * k, k = scale * log2(e).
+template <typename QT>
+__global__ void __launch_bounds__(128) mla_absorb_kernel(const QT* __restrict__ q, uint32_t batch, uint32_t nope,
+                                                         const uint16_t* __restrict__ w_uk, float k,
+                                                         float* __restrict__ qp) {
+    extern __shared__ float qs[];  // [batch][nope]
+    const uint32_t h = blockIdx.x, c = blockIdx.y * 128 + threadIdx.x;
+    const uint32_t qdim = nope + kMlaRope;
+    for (uint32_t i = threadIdx.x; i < batch * nope; i += blockDim.x) {
+        const uint32_t b = i / nope, d = i % nope;
+        qs[i] = load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + d);
+    }
+    __syncthreads();
+    float acc[kMlaMaxBatch];
+#pragma unroll
+    for (uint32_t b = 0; b < kMlaMaxBatch; ++b) acc[b] = 0.f;
+    const uint16_t* wcol = w_uk + static_cast<size_t>(h) * nope * kMlaLatent + c;
+    for (uint32_t d = 0; d < nope; ++d) {
+        const float w = bf16_bits_to_f32(wcol[static_cast<size_t>(d) * kMlaLatent]);
+#pragma unroll
+        for (uint32_t b = 0; b < kMlaMaxBatch; ++b)
+            if (b < batch) acc[b] = fmaf(qs[b * nope + d], w, acc[b]);
+    }
+#pragma unroll
+    for (uint32_t b = 0; b < kMlaMaxBatch; ++b)
+        if (b < batch) qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + c] = acc[b] * k;
+    if (blockIdx.y == 0 && threadIdx.x < kMlaRope) {
+        for (uint32_t b = 0; b < batch; ++b)
+            qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + kMlaLatent + threadIdx.x] =
+                load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + nope + threadIdx.x) * k;
+    }
+}
+
+// ---------------------------------------------------------------- 2. attention
+// grid (splits, batch), 128 threads (4 warps). Warp w computes the scores of
+// tokens 16w..16w+15 of each tile (two n-tiles, all 576 dims) and owns the
+// context columns 128w..128w+127.
+__global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float* __restrict__ qp, MlaSeqs seqs,
+                                                                      uint32_t split_tokens, uint32_t splits,
+                                                                      float* __restrict__ partial) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* qhi = smem;
+    unsigned char* qlo = qhi + kMlaHeads * kQRow;
+    unsigned char* stage0 = qlo + kMlaHeads * kQRow;
+    unsigned char* pbuf = stage0 + 2 * kStageBytes;
+    float* wmax = reinterpret_cast<float*>(pbuf + kMlaHeads * kPRow);  // [warps][16]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t b = blockIdx.y, sp = blockIdx.x;
+    const uint32_t L = seqs.len[b];
+    const uint32_t t0 = sp * split_tokens, t1 = min(L, t0 + split_tokens);
+    float* out = partial + (static_cast<size_t>(b) * splits + sp) * kMlaHeads * kMlaPartialFloats;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    if (t0 >= t1) {  // empty split: contributes nothing
+        for (uint32_t i = threadIdx.x; i < kMlaHeads * kMlaPartialFloats; i += blockDim.x)
+            out[i] = (i % kMlaPartialFloats == 0) ? NEG_INF : 0.f;
+        return;
+    }
+    const uint16_t* ckv = seqs.c_kv[b];
+    const uint16_t* krope = seqs.k_rope[b];
+    const uint32_t ntiles = (t1 - t0 + kMlaTile - 1) / kMlaTile;
+
+    auto issue_tile = [&](uint32_t tile, int buf) {
+        unsigned char* st = stage0 + buf * kStageBytes;
+        const uint32_t tb = t0 + tile * kMlaTile;
+        // c_kv: 64 rows x 64 chunks; k_rope: 64 rows x 8 chunks
+        for (uint32_t i = threadIdx.x; i < kMlaTile * 64; i += blockDim.x) {
+            const uint32_t r = i >> 6, ch = i & 63;
+            const uint32_t tok = tb + r;
+            const bool ok = tok < t1;
+            cp16_zfill(st + r * kCRow + ch * 16, ckv + static_cast<size_t>(ok ? tok : t0) * kMlaLatent + ch * 8,
+                       ok ? 16u : 0u);
+        }
+        unsigned char* rt = st + kMlaTile * kCRow;
+        for (uint32_t i = threadIdx.x; i < kMlaTile * 8; i += blockDim.x) {
+            const uint32_t r = i >> 3, ch = i & 7;
+            const uint32_t tok = tb + r;
+            const bool ok = tok < t1;
+            cp16_zfill(rt + r * kRRow + ch * 16, krope + static_cast<size_t>(ok ? tok : t0) * kMlaRope + ch * 8,
+                       ok ? 16u : 0u);
+        }
+    };
+    issue_tile(0, 0);
+    cp_commit();
+
+    // Q' of this sequence as bf16 hi and lo (residue) rows
+    const float* q = qp + static_cast<size_t>(b) * kMlaHeads * kMlaK;
+    for (uint32_t i = threadIdx.x; i < kMlaHeads * kMlaK / 2; i += blockDim.x) {
+        const uint32_t h = i / (kMlaK / 2), c2 = i % (kMlaK / 2);
+        const float2 v = *reinterpret_cast<const float2*>(q + h * kMlaK + 2 * c2);
+        const uint32_t hi = pack_bf16x2(v.x, v.y);
+        const float rx = v.x - bf16_bits_to_f32(hi & 0xffffu), ry = v.y - bf16_bits_to_f32(hi >> 16);
+        *reinterpret_cast<uint32_t*>(qhi + h * kQRow + c2 * 4) = hi;
+        *reinterpret_cast<uint32_t*>(qlo + h * kQRow + c2 * 4) = pack_bf16x2(rx, ry);
+    }
+
+    // running state: heads g and g+8 (per lane), context columns of this warp
+    float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    // ldmatrix lane addressing: A (16 x 16 block): lane -> row (lane & 15), col half (lane >> 4)
+    const uint32_t a_row = lane & 15, a_col = (lane >> 4) * 8;
+    // B (n8 x k16) from [n][k] rows: lane -> row (lane & 7) + 8 * ((lane >> 4) & 1) for x4 over 2 n-tiles,
+    // k half ((lane >> 3) & 1)
+    const uint32_t b_row = (lane & 7) + ((lane >> 4) << 3), b_k = ((lane >> 3) & 1) * 8;
+
+    for (uint32_t tile = 0; tile < ntiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntiles) issue_tile(tile + 1, buf ^ 1);
+        cp_commit();
+        cp_wait<1>();
+        __syncthreads();  // tile `tile` landed (and, on the first pass, Q')
+        const unsigned char* st = stage0 + buf * kStageBytes;
+        const unsigned char* rt = st + kMlaTile * kCRow;
+
+        // ---- scores of tokens 16w .. 16w+15: two n-tiles, hi and lo accumulators
+        float sh[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        float sl[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const uint32_t tok0 = warp * 16;
+#pragma unroll 4
+        for (uint32_t kk = 0; kk < kMlaK / 16; ++kk) {
+            uint32_t ah[4], al[4], bb[4];
+            ldsm_x4(ah, qhi + a_row * kQRow + (kk * 16 + a_col) * 2);
+            ldsm_x4(al, qlo + a_row * kQRow + (kk * 16 + a_col) * 2);
+            const uint32_t kc = kk * 16 + b_k;
+            if (kk < kMlaLatent / 16)
+                ldsm_x4(bb, st + (tok0 + b_row) * kCRow + kc * 2);
+            else
+                ldsm_x4(bb, rt + (tok0 + b_row) * kRRow + (kc - kMlaLatent) * 2);
+            mma16816(sh[0], ah, bb[0], bb[1]);
+            mma16816(sl[0], al, bb[0], bb[1]);
+            mma16816(sh[1], ah, bb[2], bb[3]);
+            mma16816(sl[1], al, bb[2], bb[3]);
+        }
+        // s[n][i]: n-tile n, (head g | g+8) x (token 2t | 2t+1)
+        float s[2][4];
+        const uint32_t tbase = t0 + tile * kMlaTile + tok0;
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t tok = tbase + n * 8 + 2 * t + (i & 1);
+                s[n][i] = tok < t1 ? sh[n][i] + sl[n][i] : NEG_INF;
+            }
+        // per-head maximum over the tile: warp's 16 tokens, then across warps
+        float mx[2];
+        mx[0] = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+        mx[1] = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 2));
+        }
+        if (t == 0) {
+            wmax[warp * kMlaHeads + g] = mx[0];
+            wmax[warp * kMlaHeads + g + 8] = mx[1];
+        }
+        __syncthreads();
+        float alpha[2], m_new[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float m = m_run[r];
+#pragma unroll
+            for (int w = 0; w < kMlaWarps; ++w) m = fmaxf(m, wmax[w * kMlaHeads + g + 8 * r]);
+            m_new[r] = m;
+            alpha[r] = (m_run[r] == NEG_INF) ? 0.f : exp2f(m_run[r] - m);
+            m_run[r] = m;
+        }
+        // p = 2^(s - m) rounded to bf16; the row sums use the rounded values
+        float lsum[2] = {0.f, 0.f};
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            uint32_t pw[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const float p0 = (m_new[r] == NEG_INF) ? 0.f : exp2f(s[n][2 * r] - m_new[r]);
+                const float p1 = (m_new[r] == NEG_INF) ? 0.f : exp2f(s[n][2 * r + 1] - m_new[r]);
+                pw[r] = pack_bf16x2(p0, p1);
+                lsum[r] += bf16_bits_to_f32(pw[r] & 0xffffu) + bf16_bits_to_f32(pw[r] >> 16);
+            }
+            const uint32_t col = (tok0 + n * 8 + 2 * t) * 2;
+            *reinterpret_cast<uint32_t*>(pbuf + g * kPRow + col) = pw[0];
+            *reinterpret_cast<uint32_t*>(pbuf + (g + 8) * kPRow + col) = pw[1];
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            lsum[r] += __shfl_xor_sync(kFull, lsum[r], 1);
+            lsum[r] += __shfl_xor_sync(kFull, lsum[r], 2);
+            l_run[r] = l_run[r] * alpha[r] + lsum[r];  // this warp's tokens only; summed over warps at the end
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= alpha[0];
+            o[n][1] *= alpha[0];
+            o[n][2] *= alpha[1];
+            o[n][3] *= alpha[1];
+        }
+        __syncthreads();  // P complete
+        // ---- O[:, 128w .. 128w+127] += P (16 x 64) C (64 x 128)
+#pragma unroll
+        for (uint32_t kk = 0; kk < kMlaTile / 16; ++kk) {
+            uint32_t pa[4];
+            ldsm_x4(pa, pbuf + a_row * kPRow + (kk * 16 + a_col) * 2);
+            // trans loads: rows = tokens kk*16 + (lane & 15), columns 8-wide blocks
+            const unsigned char* crow = st + (kk * 16 + (lane & 15)) * kCRow;
+#pragma unroll
+            for (int n = 0; n < 16; n += 2) {
+                uint32_t bb[4];
+                ldsm_x4_t(bb, crow + (warp * 128 + n * 8 + (lane >> 4) * 8) * 2);
+                mma16816(o[n], pa, bb[0], bb[1]);
+                mma16816(o[n + 1], pa, bb[2], bb[3]);
+            }
+        }
+        __syncthreads();  // stage `buf` and P free for reuse
+    }
+    cp_wait<0>();
+
+    // split partial: max, sum over all warps' tokens, O
+    __syncthreads();
+    float* lsh = wmax;  // reuse: [warps][16] partial sums
+    if (t == 0) {
+        lsh[warp * kMlaHeads + g] = l_run[0];
+        lsh[warp * kMlaHeads + g + 8] = l_run[1];
+    }
+    __syncthreads();
+    if (threadIdx.x < kMlaHeads) {
+        float l = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMlaWarps; ++w) l += lsh[w * kMlaHeads + threadIdx.x];
+        out[threadIdx.x * kMlaPartialFloats + 1] = l;
+    }
+    if (warp == 0 && t == 0) {
+        out[g * kMlaPartialFloats] = m_run[0];
+        out[(g + 8) * kMlaPartialFloats] = m_run[1];
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+        const uint32_t col = warp * 128 + n * 8 + 2 * t;
+        *reinterpret_cast<float2*>(out + g * kMlaPartialFloats + 2 + col) = make_float2(o[n][0], o[n][1]);
+        *reinterpret_cast<float2*>(out + (g + 8) * kMlaPartialFloats + 2 + col) = make_float2(o[n][2], o[n][3]);
+    }
+}
+
+// ---------------------------------------------------------------- 3. combine
+// grid (heads, batch), 256 threads: ctx[b][h][c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s
+__global__ void __launch_bounds__(256) mla_combine_kernel(const float* __restrict__ partial, uint32_t splits,
+                                                           float* __restrict__ ctx) {
+    __shared__ float wsc[1024];
+    __shared__ float inv_total;
+    const uint32_t h = blockIdx.x, b = blockIdx.y;
+    const float* base = partial + static_cast<size_t>(b) * splits * kMlaHeads * kMlaPartialFloats +
+                        h * kMlaPartialFloats;
+    const size_t stride = static_cast<size_t>(kMlaHeads) * kMlaPartialFloats;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    if (threadIdx.x < 32) {
+        float M = NEG_INF;
+        for (uint32_t s = threadIdx.x; s < splits; s += 32) M = fmaxf(M, base[s * stride]);
+        M = warp_max(M);
+        float tot = 0.f;
+        for (uint32_t s = threadIdx.x; s < splits; s += 32) {
+            const float m = base[s * stride];
+            const float w = (m == NEG_INF) ? 0.f : exp2f(m - M);
+            wsc[s] = w;
+            tot += w * base[s * stride + 1];
+        }
+        tot = warp_sum(tot);
+        if (threadIdx.x == 0) inv_total = tot > 0.f ? 1.0f / tot : 0.f;
+    }
+    __syncthreads();
+    const float inv = inv_total;
+    for (uint32_t c = threadIdx.x; c < kMlaLatent; c += blockDim.x) {
+        float acc = 0.f;
+        for (uint32_t s = 0; s < splits; ++s) acc = fmaf(wsc[s], base[s * stride + 2 + c], acc);
+        ctx[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaLatent + c] = acc * inv;
+    }
+}
+
+// ---------------------------------------------------------------- 4. output
+// grid (heads, v/32), 256 threads: warp w -> rows d = blockIdx.y*32 + 4w .. +3;
+// W_UV rows are read once and dotted with every sequence's context.
+template <typename OT>
+__global__ void __launch_bounds__(256) mla_out_kernel(const float* __restrict__ ctx, uint32_t batch,
+                                                       const uint16_t* __restrict__ w_uv, OT* __restrict__ out) {
+    extern __shared__ __align__(16) float cs[];  // [batch][latent]
+    const uint32_t h = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (uint32_t i = threadIdx.x; i < batch * kMlaLatent; i += blockDim.x) {
+        const uint32_t bb = i / kMlaLatent, c = i % kMlaLatent;
+        cs[i] = ctx[(static_cast<size_t>(bb) * kMlaHeads + h) * kMlaLatent + c];
+    }
+    __syncthreads();
+    for (int r = 0; r < 4; ++r) {
+        const uint32_t d = blockIdx.y * 32 + warp * 4 + r;
+        const uint16_t* wrow = w_uv + (static_cast<size_t>(h) * kMlaV + d) * kMlaLatent;
+        // lane covers columns 16*lane .. 16*lane+15
+        const uint4 w0 = *reinterpret_cast<const uint4*>(wrow + lane * 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + lane * 16 + 8);
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float wf[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            wf[2 * i] = bf16_bits_to_f32(wv[i] & 0xffffu);
+            wf[2 * i + 1] = bf16_bits_to_f32(wv[i] >> 16);
+        }
+        for (uint32_t bb = 0; bb < batch; ++bb) {
+            const float* c = cs + bb * kMlaLatent + lane * 16;
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc = fmaf(wf[i], c[i], acc);
+            acc = warp_sum(acc);
+            if (lane == 0) store_act(out, (static_cast<size_t>(bb) * kMlaHeads + h) * kMlaV + d, acc);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- launch
+size_t mla_smem_bytes() { return kMlaSmem; }
+
+bool mla_shape_supported(uint32_t heads, uint32_t rope, uint32_t latent, uint32_t v_dim) {
+    return heads == kMlaHeads && rope == kMlaRope && latent == kMlaLatent && v_dim == kMlaV;
+}
+
+void mla_plan_splits(const MlaLaunch& a, int num_sms, uint32_t& split_tokens, uint32_t& splits) {
+    uint32_t lmax = 1;
+    for (uint32_t b = 0; b < a.batch; ++b) lmax = a.seqs.len[b] > lmax ? a.seqs.len[b] : lmax;
+    const uint64_t per_sm = (static_cast<uint64_t>(lmax) * a.batch + num_sms - 1) / num_sms;
+    uint64_t st = (per_sm + kMlaTile - 1) / kMlaTile * kMlaTile;
+    if (st < kMlaTile) st = kMlaTile;
+    split_tokens = static_cast<uint32_t>(st);
+    splits = static_cast<uint32_t>((lmax + st - 1) / st);
+}
+
+uint32_t mla_max_splits(uint32_t max_batch, int num_sms) {
+    // splits <= lmax / split_tokens + 1 <= num_sms / batch + 1 (split_tokens >= lmax * batch / num_sms)
+    return static_cast<uint32_t>(num_sms) / (max_batch ? max_batch : 1) + 2;
+}
+
+cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
+    const float k = a.scale * 1.4426950408889634f;  // scores in base 2
+    cudaError_t e;
+    {
+        const size_t sm = static_cast<size_t>(a.batch) * a.nope * sizeof(float);
+        const dim3 grid(kMlaHeads, kMlaLatent / 128);
+        if (a.q_dtype == PBMOE_F32) {
+            if ((e = cudaFuncSetAttribute(mla_absorb_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(sm))) != cudaSuccess)
+                return e;
+            mla_absorb_kernel<float><<<grid, 128, sm, s>>>(static_cast<const float*>(a.q), a.batch, a.nope, a.w_uk,
+                                                           k, a.qp);
+        } else {
+            if ((e = cudaFuncSetAttribute(mla_absorb_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(sm))) != cudaSuccess)
+                return e;
+            mla_absorb_kernel<uint16_t><<<grid, 128, sm, s>>>(static_cast<const uint16_t*>(a.q), a.batch, a.nope,
+                                                              a.w_uk, k, a.qp);
+        }
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    if ((e = cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kMlaSmem))) != cudaSuccess)
+        return e;
+    mla_attn_kernel<<<dim3(a.splits, a.batch), kMlaWarps * 32, kMlaSmem, s>>>(a.qp, a.seqs, a.split_tokens, a.splits,
+                                                                             a.partial);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    mla_combine_kernel<<<dim3(kMlaHeads, a.batch), 256, 0, s>>>(a.partial, a.splits, a.ctx);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t osm = static_cast<size_t>(a.batch) * kMlaLatent * sizeof(float);
+    if (a.out_dtype == PBMOE_F32) {
+        if ((e = cudaFuncSetAttribute(mla_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(osm))) != cudaSuccess)
+            return e;
+        mla_out_kernel<float><<<dim3(kMlaHeads, kMlaV / 32), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
+                                                                            static_cast<float*>(a.out));
+    } else {
+        if ((e = cudaFuncSetAttribute(mla_out_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(osm))) != cudaSuccess)
+            return e;
+        mla_out_kernel<uint16_t><<<dim3(kMlaHeads, kMlaV / 32), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
+                                                                               static_cast<uint16_t*>(a.out));
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace pbmoe
