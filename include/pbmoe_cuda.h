@@ -229,7 +229,7 @@ PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* config, const pbmoe
 
 /* Shapes of MLA absorbed decode attention (MlaAttentionLayout,
  * weights/mod.rs:651-664). The tensor-core kernels take heads 16, rope 64,
- * latent 512 and v 128 (any nope dim); other shapes are PBMOE_ERR_UNSUPPORTED. */
+ * latent 512, v 128 and nope <= 128; other shapes are PBMOE_ERR_UNSUPPORTED. */
 typedef struct pbmoe_mla_config {
     uint32_t heads;
     uint32_t nope_dim;

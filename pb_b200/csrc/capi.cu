@@ -429,10 +429,10 @@ int check_mla_config(pbmoe_ctx* ctx, const pbmoe_mla_config* c) {
     if (!c) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: null config");
     if (c->heads == 0 || c->nope_dim == 0 || c->rope_dim == 0 || c->latent_dim == 0 || c->v_dim == 0)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: zero dimension");
-    if (!pbmoe::mla_shape_supported(c->heads, c->rope_dim, c->latent_dim, c->v_dim) || c->nope_dim > 1024)
+    if (!pbmoe::mla_shape_supported(c->heads, c->rope_dim, c->latent_dim, c->v_dim) || c->nope_dim > 128)
         return fail(ctx, PBMOE_ERR_UNSUPPORTED,
                     "FlashMoe unsupported MLA shape on CUDA: heads=%u nope=%u rope=%u latent=%u v=%u (built for "
-                    "heads 16, rope 64, latent 512, v 128, nope <= 1024)",
+                    "heads 16, rope 64, latent 512, v 128, nope <= 128)",
                     c->heads, c->nope_dim, c->rope_dim, c->latent_dim, c->v_dim);
     if (!(c->softmax_scale >= 0.f) || !std::isfinite(c->softmax_scale))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: softmax_scale must be finite and >= 0");

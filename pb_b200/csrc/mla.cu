@@ -23,7 +23,7 @@
 //                          Writes the split's (max, sum, O[16 x 512]).
 //   3. mla_combine_kernel  merges the splits of each (sequence, head) -> ctx.
 //   4. mla_out_kernel      out = W_UV ctx, W_UV read once for the batch.
-// Shapes: 16 heads, latent 512, rope 64, v 128 (any nope), batch <= 32.
+// Shapes: 16 heads, latent 512, rope 64, v 128, nope <= 128, batch <= 32.
 
 #include "common.cuh"
 #include "kernels.h"
@@ -82,38 +82,60 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---------------------------------------------------------------- 1. absorb
-// grid (heads, latent/128, 1), 128 threads: thread = one latent column c of
-// head h for every sequence. Writes Q'[b][h][0..511] = q_lat * k and
-// Q'[b][h][512..575] = q_rope * k, k = scale * log2(e).
+// grid (heads, latent/64), 256 threads: thread (quarter = tid/64, column
+// c = 64*blockIdx.y + tid%64) sums a quarter of the nope dims for every
+// sequence, with all its W_UK loads in flight at once; the quarters meet in
+// shared memory. Writes Q'[b][h][0..511] = q_lat * k and Q'[b][h][512..575] =
+// q_rope * k, k = scale * log2(e). nope <= 128 (host-checked).
+constexpr uint32_t kAbsorbMaxNope = 128;
 template <typename QT>
-__global__ void __launch_bounds__(128) mla_absorb_kernel(const QT* __restrict__ q, uint32_t batch, uint32_t nope,
+__global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ q, uint32_t batch, uint32_t nope,
                                                          const uint16_t* __restrict__ w_uk, float k,
                                                          float* __restrict__ qp) {
-    extern __shared__ float qs[];  // [batch][nope]
-    const uint32_t h = blockIdx.x, c = blockIdx.y * 128 + threadIdx.x;
+    __shared__ float qs[kMlaMaxBatch * kAbsorbMaxNope];
+    __shared__ float red[4][8][64];
+    const uint32_t h = blockIdx.x, tid = threadIdx.x;
+    const uint32_t quarter = tid >> 6, cc = tid & 63, c = blockIdx.y * 64 + cc;
     const uint32_t qdim = nope + kMlaRope;
-    for (uint32_t i = threadIdx.x; i < batch * nope; i += blockDim.x) {
+    for (uint32_t i = tid; i < batch * nope; i += blockDim.x) {
         const uint32_t b = i / nope, d = i % nope;
         qs[i] = load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + d);
     }
-    __syncthreads();
-    float acc[kMlaMaxBatch];
-#pragma unroll
-    for (uint32_t b = 0; b < kMlaMaxBatch; ++b) acc[b] = 0.f;
+    const uint32_t dq = (nope + 3) / 4, d0 = quarter * dq;
+    float w[kAbsorbMaxNope / 4];
     const uint16_t* wcol = w_uk + static_cast<size_t>(h) * nope * kMlaLatent + c;
-    for (uint32_t d = 0; d < nope; ++d) {
-        const float w = bf16_bits_to_f32(wcol[static_cast<size_t>(d) * kMlaLatent]);
 #pragma unroll
-        for (uint32_t b = 0; b < kMlaMaxBatch; ++b)
-            if (b < batch) acc[b] = fmaf(qs[b * nope + d], w, acc[b]);
+    for (uint32_t i = 0; i < kAbsorbMaxNope / 4; ++i)
+        w[i] = (i < dq && d0 + i < nope) ? bf16_bits_to_f32(wcol[static_cast<size_t>(d0 + i) * kMlaLatent]) : 0.f;
+    __syncthreads();
+    for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            acc[j] = 0.f;
+            if (b0 + j < batch) {
+                const float* qb = qs + (b0 + j) * nope + d0;
+#pragma unroll
+                for (uint32_t i = 0; i < kAbsorbMaxNope / 4; ++i)
+                    if (i < dq && d0 + i < nope) acc[j] = fmaf(qb[i], w[i], acc[j]);
+            }
+            red[quarter][j][cc] = acc[j];
+        }
+        __syncthreads();
+        if (quarter == 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (b0 + j < batch) {
+                    const float v = red[0][j][cc] + red[1][j][cc] + red[2][j][cc] + red[3][j][cc];
+                    qp[(static_cast<size_t>(b0 + j) * kMlaHeads + h) * kMlaK + c] = v * k;
+                }
+        }
+        __syncthreads();
     }
-#pragma unroll
-    for (uint32_t b = 0; b < kMlaMaxBatch; ++b)
-        if (b < batch) qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + c] = acc[b] * k;
-    if (blockIdx.y == 0 && threadIdx.x < kMlaRope) {
+    if (blockIdx.y == 0 && tid < kMlaRope) {
         for (uint32_t b = 0; b < batch; ++b)
-            qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + kMlaLatent + threadIdx.x] =
-                load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + nope + threadIdx.x) * k;
+            qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + kMlaLatent + tid] =
+                load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + nope + tid) * k;
     }
 }
 
@@ -169,15 +191,26 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
     issue_tile(0, 0);
     cp_commit();
 
-    // Q' of this sequence as bf16 hi and lo (residue) rows
-    const float* q = qp + static_cast<size_t>(b) * kMlaHeads * kMlaK;
-    for (uint32_t i = threadIdx.x; i < kMlaHeads * kMlaK / 2; i += blockDim.x) {
-        const uint32_t h = i / (kMlaK / 2), c2 = i % (kMlaK / 2);
-        const float2 v = *reinterpret_cast<const float2*>(q + h * kMlaK + 2 * c2);
-        const uint32_t hi = pack_bf16x2(v.x, v.y);
-        const float rx = v.x - bf16_bits_to_f32(hi & 0xffffu), ry = v.y - bf16_bits_to_f32(hi >> 16);
-        *reinterpret_cast<uint32_t*>(qhi + h * kQRow + c2 * 4) = hi;
-        *reinterpret_cast<uint32_t*>(qlo + h * kQRow + c2 * 4) = pack_bf16x2(rx, ry);
+    // Q' of this sequence as bf16 hi and lo (residue) rows; every load of the
+    // thread is issued before any conversion
+    {
+        const float4* q4 = reinterpret_cast<const float4*>(qp + static_cast<size_t>(b) * kMlaHeads * kMlaK);
+        constexpr uint32_t kVec = kMlaHeads * kMlaK / 4;  // 2304 float4
+        constexpr uint32_t kPer = kVec / (kMlaWarps * 32);
+        static_assert(kVec % (kMlaWarps * 32) == 0, "whole float4 per thread");
+        float4 v[kPer];
+#pragma unroll
+        for (uint32_t j = 0; j < kPer; ++j) v[j] = __ldcg(q4 + j * kMlaWarps * 32 + threadIdx.x);
+#pragma unroll
+        for (uint32_t j = 0; j < kPer; ++j) {
+            const uint32_t i = j * kMlaWarps * 32 + threadIdx.x;
+            const uint32_t h = i / (kMlaK / 4), c4 = i % (kMlaK / 4);
+            const uint32_t h0 = pack_bf16x2(v[j].x, v[j].y), h1 = pack_bf16x2(v[j].z, v[j].w);
+            const uint32_t l0 = pack_bf16x2(v[j].x - bf16_bits_to_f32(h0 & 0xffffu), v[j].y - bf16_bits_to_f32(h0 >> 16));
+            const uint32_t l1 = pack_bf16x2(v[j].z - bf16_bits_to_f32(h1 & 0xffffu), v[j].w - bf16_bits_to_f32(h1 >> 16));
+            *reinterpret_cast<uint2*>(qhi + h * kQRow + c4 * 8) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2*>(qlo + h * kQRow + c4 * 8) = make_uint2(l0, l1);
+        }
     }
 
     // running state: heads g and g+8 (per lane), context columns of this warp
@@ -205,7 +238,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
         float sh[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         float sl[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         const uint32_t tok0 = warp * 16;
-#pragma unroll 4
+#pragma unroll
         for (uint32_t kk = 0; kk < kMlaK / 16; ++kk) {
             uint32_t ah[4], al[4], bb[4];
             ldsm_x4(ah, qhi + a_row * kQRow + (kk * 16 + a_col) * 2);
@@ -330,73 +363,100 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
 }
 
 // ---------------------------------------------------------------- 3. combine
-// grid (heads, batch), 256 threads: ctx[b][h][c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s
-__global__ void __launch_bounds__(256) mla_combine_kernel(const float* __restrict__ partial, uint32_t splits,
+// grid (heads, batch, latent/128), 128 threads = latent columns:
+// ctx[b][h][c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s
+__global__ void __launch_bounds__(128) mla_combine_kernel(const float* __restrict__ partial, uint32_t splits,
                                                            float* __restrict__ ctx) {
     __shared__ float wsc[1024];
-    __shared__ float inv_total;
-    const uint32_t h = blockIdx.x, b = blockIdx.y;
+    __shared__ float red[4];
+    const uint32_t h = blockIdx.x, b = blockIdx.y, c = blockIdx.z * 128 + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* base = partial + static_cast<size_t>(b) * splits * kMlaHeads * kMlaPartialFloats +
                         h * kMlaPartialFloats;
     const size_t stride = static_cast<size_t>(kMlaHeads) * kMlaPartialFloats;
     const float NEG_INF = -__int_as_float(0x7f800000);
-    if (threadIdx.x < 32) {
-        float M = NEG_INF;
-        for (uint32_t s = threadIdx.x; s < splits; s += 32) M = fmaxf(M, base[s * stride]);
-        M = warp_max(M);
-        float tot = 0.f;
-        for (uint32_t s = threadIdx.x; s < splits; s += 32) {
-            const float m = base[s * stride];
-            const float w = (m == NEG_INF) ? 0.f : exp2f(m - M);
-            wsc[s] = w;
-            tot += w * base[s * stride + 1];
-        }
-        tot = warp_sum(tot);
-        if (threadIdx.x == 0) inv_total = tot > 0.f ? 1.0f / tot : 0.f;
-    }
+    float M = NEG_INF;
+    for (uint32_t s = threadIdx.x; s < splits; s += blockDim.x) M = fmaxf(M, __ldcg(base + s * stride));
+    M = warp_max(M);
+    if (lane == 0) red[warp] = M;
     __syncthreads();
-    const float inv = inv_total;
-    for (uint32_t c = threadIdx.x; c < kMlaLatent; c += blockDim.x) {
-        float acc = 0.f;
-        for (uint32_t s = 0; s < splits; ++s) acc = fmaf(wsc[s], base[s * stride + 2 + c], acc);
-        ctx[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaLatent + c] = acc * inv;
+    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float tot = 0.f;
+    for (uint32_t s = threadIdx.x; s < splits; s += blockDim.x) {
+        const float m = __ldcg(base + s * stride);
+        const float w = (m == NEG_INF) ? 0.f : exp2f(m - M);
+        wsc[s] = w;
+        tot += w * __ldcg(base + s * stride + 1);
     }
+    tot = warp_sum(tot);
+    __syncthreads();
+    if (lane == 0) red[warp] = tot;
+    __syncthreads();
+    tot = red[0] + red[1] + red[2] + red[3];
+    const float inv = tot > 0.f ? 1.0f / tot : 0.f;
+    const float* oc = base + 2 + c;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t s = 0;
+    for (; s + 8 <= splits; s += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __ldcg(oc + (s + j) * stride);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j & 3] = fmaf(wsc[s + j], v[j], acc[j & 3]);
+    }
+    for (; s < splits; ++s) acc[0] = fmaf(wsc[s], __ldcg(oc + s * stride), acc[0]);
+    ctx[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaLatent + c] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * inv;
 }
 
 // ---------------------------------------------------------------- 4. output
-// grid (heads, v/32), 256 threads: warp w -> rows d = blockIdx.y*32 + 4w .. +3;
-// W_UV rows are read once and dotted with every sequence's context.
+// grid (heads, v/16), 256 threads: warp w -> rows d = 16*blockIdx.y + 2w, +1;
+// W_UV rows are read once (all loads in flight) and dotted with every
+// sequence's context.
 template <typename OT>
 __global__ void __launch_bounds__(256) mla_out_kernel(const float* __restrict__ ctx, uint32_t batch,
                                                        const uint16_t* __restrict__ w_uv, OT* __restrict__ out) {
     extern __shared__ __align__(16) float cs[];  // [batch][latent]
     const uint32_t h = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (uint32_t i = threadIdx.x; i < batch * kMlaLatent; i += blockDim.x) {
-        const uint32_t bb = i / kMlaLatent, c = i % kMlaLatent;
-        cs[i] = ctx[(static_cast<size_t>(bb) * kMlaHeads + h) * kMlaLatent + c];
-    }
-    __syncthreads();
-    for (int r = 0; r < 4; ++r) {
-        const uint32_t d = blockIdx.y * 32 + warp * 4 + r;
-        const uint16_t* wrow = w_uv + (static_cast<size_t>(h) * kMlaV + d) * kMlaLatent;
-        // lane covers columns 16*lane .. 16*lane+15
-        const uint4 w0 = *reinterpret_cast<const uint4*>(wrow + lane * 16);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + lane * 16 + 8);
+    float wf[2][16];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint32_t d = blockIdx.y * 16 + warp * 2 + r;
+        const uint16_t* wrow = w_uv + (static_cast<size_t>(h) * kMlaV + d) * kMlaLatent + lane * 16;
+        const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(wrow));
+        const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(wrow + 8));
         const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        float wf[16];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            wf[2 * i] = bf16_bits_to_f32(wv[i] & 0xffffu);
-            wf[2 * i + 1] = bf16_bits_to_f32(wv[i] >> 16);
+            wf[r][2 * i] = bf16_bits_to_f32(wv[i] & 0xffffu);
+            wf[r][2 * i + 1] = bf16_bits_to_f32(wv[i] >> 16);
         }
-        for (uint32_t bb = 0; bb < batch; ++bb) {
-            const float* c = cs + bb * kMlaLatent + lane * 16;
-            float acc = 0.f;
+    }
+    for (uint32_t i = threadIdx.x; i < batch * kMlaLatent / 4; i += blockDim.x) {
+        const uint32_t bb = i / (kMlaLatent / 4), c4 = i % (kMlaLatent / 4);
+        reinterpret_cast<float4*>(cs)[i] =
+            __ldcg(reinterpret_cast<const float4*>(ctx + (static_cast<size_t>(bb) * kMlaHeads + h) * kMlaLatent) + c4);
+    }
+    __syncthreads();
+    for (uint32_t bb = 0; bb < batch; ++bb) {
+        const float4* c4 = reinterpret_cast<const float4*>(cs + bb * kMlaLatent + lane * 16);
+        float acc[2] = {0.f, 0.f};
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc = fmaf(wf[i], c[i], acc);
-            acc = warp_sum(acc);
-            if (lane == 0) store_act(out, (static_cast<size_t>(bb) * kMlaHeads + h) * kMlaV + d, acc);
+        for (int i = 0; i < 4; ++i) {
+            const float4 v = c4[i];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                acc[r] = fmaf(wf[r][4 * i], v.x, acc[r]);
+                acc[r] = fmaf(wf[r][4 * i + 1], v.y, acc[r]);
+                acc[r] = fmaf(wf[r][4 * i + 2], v.z, acc[r]);
+                acc[r] = fmaf(wf[r][4 * i + 3], v.w, acc[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float v = warp_sum(acc[r]);
+            if (lane == 0)
+                store_act(out, (static_cast<size_t>(bb) * kMlaHeads + h) * kMlaV + blockIdx.y * 16 + warp * 2 + r, v);
         }
     }
 }
@@ -427,21 +487,13 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     const float k = a.scale * 1.4426950408889634f;  // scores in base 2
     cudaError_t e;
     {
-        const size_t sm = static_cast<size_t>(a.batch) * a.nope * sizeof(float);
-        const dim3 grid(kMlaHeads, kMlaLatent / 128);
-        if (a.q_dtype == PBMOE_F32) {
-            if ((e = cudaFuncSetAttribute(mla_absorb_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(sm))) != cudaSuccess)
-                return e;
-            mla_absorb_kernel<float><<<grid, 128, sm, s>>>(static_cast<const float*>(a.q), a.batch, a.nope, a.w_uk,
-                                                           k, a.qp);
-        } else {
-            if ((e = cudaFuncSetAttribute(mla_absorb_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(sm))) != cudaSuccess)
-                return e;
-            mla_absorb_kernel<uint16_t><<<grid, 128, sm, s>>>(static_cast<const uint16_t*>(a.q), a.batch, a.nope,
-                                                              a.w_uk, k, a.qp);
-        }
+        const dim3 grid(kMlaHeads, kMlaLatent / 64);
+        if (a.q_dtype == PBMOE_F32)
+            mla_absorb_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(a.q), a.batch, a.nope, a.w_uk,
+                                                          k, a.qp);
+        else
+            mla_absorb_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(a.q), a.batch, a.nope,
+                                                             a.w_uk, k, a.qp);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     if ((e = cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -450,20 +502,20 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     mla_attn_kernel<<<dim3(a.splits, a.batch), kMlaWarps * 32, kMlaSmem, s>>>(a.qp, a.seqs, a.split_tokens, a.splits,
                                                                              a.partial);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    mla_combine_kernel<<<dim3(kMlaHeads, a.batch), 256, 0, s>>>(a.partial, a.splits, a.ctx);
+    mla_combine_kernel<<<dim3(kMlaHeads, a.batch, kMlaLatent / 128), 128, 0, s>>>(a.partial, a.splits, a.ctx);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t osm = static_cast<size_t>(a.batch) * kMlaLatent * sizeof(float);
     if (a.out_dtype == PBMOE_F32) {
         if ((e = cudaFuncSetAttribute(mla_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(osm))) != cudaSuccess)
             return e;
-        mla_out_kernel<float><<<dim3(kMlaHeads, kMlaV / 32), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
+        mla_out_kernel<float><<<dim3(kMlaHeads, kMlaV / 16), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
                                                                             static_cast<float*>(a.out));
     } else {
         if ((e = cudaFuncSetAttribute(mla_out_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(osm))) != cudaSuccess)
             return e;
-        mla_out_kernel<uint16_t><<<dim3(kMlaHeads, kMlaV / 32), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
+        mla_out_kernel<uint16_t><<<dim3(kMlaHeads, kMlaV / 16), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
                                                                                static_cast<uint16_t*>(a.out));
     }
     return cudaGetLastError();
