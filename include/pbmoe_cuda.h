@@ -66,6 +66,7 @@ typedef enum pbmoe_status {
 #define PBMOE_DEV_ERR_EXPERT_ID 0x2u     /* route expert id out of range               */
 #define PBMOE_DEV_ERR_PEER_TIMEOUT 0x4u  /* expert-parallel combine wait expired       */
 #define PBMOE_DEV_ERR_PIPE_TIMEOUT 0x8u  /* an asynchronous copy wait expired          */
+#define PBMOE_DEV_ERR_F16_RANGE 0x10u    /* prefill GEMM input |x| >= 65536 or non-finite */
 
 typedef enum pbmoe_dtype {
     PBMOE_F32 = 0,
@@ -272,6 +273,62 @@ PBMOE_API int pbmoe_mla_reserve(pbmoe_ctx* ctx, const pbmoe_mla_config* config, 
  * (weights/store.rs:1179-1327) with bf16 W_UK / W_UV. */
 PBMOE_API int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* config, const pbmoe_mla_args* args,
                                void* stream);
+
+/* ---------------------------------------------------------------- prefill */
+
+/* Y[m, r] = sum_c X[m, c] * (q[r,c] * scale + bias) for a dense Q4 weight:
+ * X bf16 [m x cols] (16-byte aligned rows), Y [m x rows] in y_dtype, fp32
+ * accumulate. Operands are fp16: each weight is dequantised once (q * s + b,
+ * one fp16 rounding) and x converts exactly; an x entry of magnitude >= 65536
+ * or non-finite latches PBMOE_DEV_ERR_F16_RANGE (pbmoe_device_status).
+ * Replaces the batched prefill matvec q4_mmap_fma_matvec_batch_bf16_scale_bias
+ * (shaders.metal:973-1057, q4_mmap_fma_row_bf16_pair :768-866) as encoded by
+ * encode_layer_major_q4_matrix_from_buffer (metal/mod.rs:4201-4275) for one
+ * matrix. Needs group_size 64 and cols a multiple of 64; packed, scales,
+ * biases and x 16-byte aligned. */
+PBMOE_API int pbmoe_q4_gemm(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype,
+                            void* y, pbmoe_dtype y_dtype, uint32_t m, void* stream);
+
+/* Layer-major grouping of a prefill chunk's routes, on the device.
+ * route_ids: device u32 [rows x top_k] (each row's routed experts).
+ * Outputs (device): slot_experts [num_experts] = the selected experts in
+ * ascending id order (slot s = s-th selected expert), *unique_count = their
+ * number, route_slots [routes] (nullable) = the slot of each route,
+ * source_rows [routes] / output_indices [routes] / groups [num_experts x 2]
+ * as qwen_layer_major_group_plan (metal/mod.rs:3197-3233) returns them, slot
+ * order from ScheduledLayerMajorExperts (scheduler/mod.rs:720-765). An expert
+ * id >= num_experts latches PBMOE_DEV_ERR_EXPERT_ID and sets *unique_count
+ * to 0. num_experts <= 1024. */
+PBMOE_API int pbmoe_prefill_group_plan(pbmoe_ctx* ctx, const uint32_t* route_ids, uint32_t rows, uint32_t top_k,
+                                       uint32_t num_experts, uint32_t* slot_experts, uint32_t* unique_count,
+                                       uint32_t* route_slots, uint32_t* source_rows, uint32_t* output_indices,
+                                       uint32_t* groups, void* stream);
+
+/* One projection (gate, up or down) of every expert in an expert table. */
+typedef struct pbmoe_q4_expert_matrix {
+    const uint8_t* experts; /* slot table, expert_bytes apart (16-byte aligned) */
+    uint64_t expert_bytes;
+    uint64_t packed_offset; /* component offsets of this projection in a slot    */
+    uint64_t scales_offset;
+    uint64_t biases_offset;
+    uint32_t num_experts;
+    uint32_t rows, cols, group_size; /* per-expert matrix [rows x cols]         */
+} pbmoe_q4_expert_matrix;
+
+/* Grouped GEMM of the layer-major prefill: for every slot s with group
+ * (start, count) and every j < count,
+ *   y[start + j, :] = W_{slot_experts[s]} . x[source_rows[start + j], :].
+ * The row gather of qwen_layer_major_gather (shaders.metal:1743-1754) is
+ * fused into the activation loads; y stays in grouped order like the
+ * reference's per-group matrix outputs (encode_and_execute_layer_major,
+ * metal/mod.rs:3334-3600). Plan arrays are device memory, as written by
+ * pbmoe_prefill_group_plan; max_unique bounds *unique_count (the grid is
+ * sized from routes and max_unique, so no read-back is needed). x bf16
+ * [tokens x cols]; y [routes x rows] in y_dtype. */
+PBMOE_API int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const uint32_t* slot_experts,
+                                    const uint32_t* unique_count, const uint32_t* groups,
+                                    const uint32_t* source_rows, uint32_t routes, uint32_t max_unique,
+                                    const void* x, pbmoe_dtype x_dtype, void* y, pbmoe_dtype y_dtype, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

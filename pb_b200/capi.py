@@ -26,6 +26,8 @@ PBMOE_ERR_DEVICE_STATUS = -7
 PBMOE_DEV_ERR_ROUTE_WEIGHTS = 0x1
 PBMOE_DEV_ERR_EXPERT_ID = 0x2
 PBMOE_DEV_ERR_PEER_TIMEOUT = 0x4
+PBMOE_DEV_ERR_PIPE_TIMEOUT = 0x8
+PBMOE_DEV_ERR_F16_RANGE = 0x10
 
 PBMOE_F32 = 0
 PBMOE_BF16 = 1
@@ -38,6 +40,7 @@ EXPORTED = [
     "pbmoe_init", "pbmoe_destroy", "pbmoe_last_error", "pbmoe_abi_version", "pbmoe_reserve",
     "pbmoe_moe_workspace_bytes", "pbmoe_device_status", "pbmoe_fixed_q4_layout", "pbmoe_q4_matvec",
     "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static", "pbmoe_mla_reserve", "pbmoe_mla_decode",
+    "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
 ]
 
 
@@ -77,6 +80,12 @@ class MlaArgs(C.Structure):
                 ("out", C.c_void_p), ("out_dtype", C.c_int)]
 
 
+class Q4ExpertMatrix(C.Structure):
+    _fields_ = [("experts", C.c_void_p), ("expert_bytes", C.c_uint64), ("packed_offset", C.c_uint64),
+                ("scales_offset", C.c_uint64), ("biases_offset", C.c_uint64), ("num_experts", C.c_uint32),
+                ("rows", C.c_uint32), ("cols", C.c_uint32), ("group_size", C.c_uint32)]
+
+
 class PbmoeError(RuntimeError):
     def __init__(self, code, message):
         super().__init__(f"pbmoe status {code}: {message}")
@@ -112,6 +121,10 @@ def load():
         L.pbmoe_mla_decode.argtypes = [vp, C.POINTER(MlaConfig), C.POINTER(MlaArgs), vp]
         L.pbmoe_moe_layer_static.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
                                              u32, vp, vp, vp, C.c_char_p, C.c_size_t, vp]
+        L.pbmoe_q4_gemm.argtypes = [vp, C.POINTER(Q4Tensor), vp, i32, vp, i32, u32, vp]
+        L.pbmoe_prefill_group_plan.argtypes = [vp, vp, u32, u32, u32, vp, vp, vp, vp, vp, vp, vp]
+        L.pbmoe_q4_gemm_grouped.argtypes = [vp, C.POINTER(Q4ExpertMatrix), vp, vp, vp, vp, u32, u32, vp, i32, vp,
+                                            i32, vp]
         _lib = L
     return _lib
 
@@ -207,6 +220,24 @@ class Context:
                        C.cast(kr, C.c_void_p), w_uk.data_ptr(), w_uv.data_ptr(), out.data_ptr(), _dtype_code(out))
         self.check(self.lib.pbmoe_mla_decode(self.h, C.byref(config), C.byref(args), self.stream_ptr(stream)))
 
+    def q4_gemm(self, packed, scales, biases, rows, cols, group, x, y, stream=None):
+        """y [m, rows] = x [m, cols] . W^T for a dense Q4 weight."""
+        t = Q4Tensor(packed.data_ptr(), scales.data_ptr(), biases.data_ptr(), rows, cols, group)
+        self.check(self.lib.pbmoe_q4_gemm(self.h, C.byref(t), _ptr(x), _dtype_code(x), _ptr(y), _dtype_code(y),
+                                          int(x.shape[0]), self.stream_ptr(stream)))
+
+    def prefill_group_plan(self, route_ids, rows, top_k, num_experts, slot_experts, unique_count, source_rows,
+                           output_indices, groups, route_slots=None, stream=None):
+        self.check(self.lib.pbmoe_prefill_group_plan(
+            self.h, _ptr(route_ids), rows, top_k, num_experts, _ptr(slot_experts), _ptr(unique_count),
+            _ptr(route_slots), _ptr(source_rows), _ptr(output_indices), _ptr(groups), self.stream_ptr(stream)))
+
+    def q4_gemm_grouped(self, matrix: Q4ExpertMatrix, slot_experts, unique_count, groups, source_rows, routes,
+                        max_unique, x, y, stream=None):
+        self.check(self.lib.pbmoe_q4_gemm_grouped(
+            self.h, C.byref(matrix), _ptr(slot_experts), _ptr(unique_count), _ptr(groups), _ptr(source_rows),
+            routes, max_unique, _ptr(x), _dtype_code(x), _ptr(y), _dtype_code(y), self.stream_ptr(stream)))
+
     def device_status(self, clear=True, stream=None) -> int:
         v = C.c_uint32()
         self.check(self.lib.pbmoe_device_status(self.h, self.stream_ptr(stream), C.byref(v), 1 if clear else 0))
@@ -215,6 +246,16 @@ class Context:
 
 def mla_config(heads=16, nope=128, rope=64, latent=512, v_dim=128, scale=0.0) -> MlaConfig:
     return MlaConfig(heads, nope, rope, latent, v_dim, scale)
+
+
+def expert_matrix(experts, layout: ExpertLayout, num_experts, projection) -> Q4ExpertMatrix:
+    """One projection ("gate", "up" or "down") of an expert table laid out by `layout`."""
+    i = {"gate": 0, "up": 3, "down": 6}[projection]
+    rows, cols = ((layout.intermediate, layout.hidden) if projection != "down"
+                  else (layout.hidden, layout.intermediate))
+    off = layout.component_offsets
+    return Q4ExpertMatrix(experts.data_ptr(), layout.expert_bytes, off[i], off[i + 1], off[i + 2], num_experts,
+                          rows, cols, layout.group_size)
 
 
 def moe_config(layout: ExpertLayout, num_experts, top_k, normalization=0, routed_scale=1.0, eps=1e-6) -> MoeConfig:

@@ -525,3 +525,107 @@ int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_
     if (e != cudaSuccess) return cuda_fail(ctx, e, "MLA decode launch");
     return PBMOE_OK;
 }
+
+int pbmoe_q4_gemm(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype, void* y,
+                  pbmoe_dtype y_dtype, uint32_t m, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!w || !w->packed || !w->scales || !w->biases || !x || !y)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 gemm: null pointer");
+    if (w->group_size == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "group_size must be positive");
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (w->rows == 0 || w->cols == 0 || m == 0) return PBMOE_OK;
+    if (x_dtype != PBMOE_BF16 || !pbmoe::q4_gemm_supported(w->rows, w->cols, w->group_size))
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported q4 gemm: needs bf16 x, group_size 64 and cols a multiple of 64 "
+                    "(got x dtype %d, group %u, cols %u)", static_cast<int>(x_dtype), w->group_size, w->cols);
+    if (!aligned(w->packed, 16) || !aligned(w->scales, 16) || !aligned(w->biases, 16) || !aligned(x, 16) ||
+        !aligned(y, 16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 gemm: packed, scales, biases, x and y must be 16-byte aligned");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    pbmoe::Q4GemmArgs a{static_cast<const uint8_t*>(w->packed), w->scales, w->biases, w->rows, w->cols,
+                        w->group_size, x, m, y, y_dtype, ctx->status};
+    cudaError_t e = pbmoe::q4_gemm_launch(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 gemm launch");
+    return PBMOE_OK;
+}
+
+int pbmoe_prefill_group_plan(pbmoe_ctx* ctx, const uint32_t* route_ids, uint32_t rows, uint32_t top_k,
+                             uint32_t num_experts, uint32_t* slot_experts, uint32_t* unique_count,
+                             uint32_t* route_slots, uint32_t* source_rows, uint32_t* output_indices,
+                             uint32_t* groups, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!route_ids || !slot_experts || !unique_count || !source_rows || !output_indices || !groups)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "prefill group plan: null pointer");
+    // the reference rejects an empty plan (metal/mod.rs:3202-3204)
+    if (rows == 0 || top_k == 0 || num_experts == 0)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
+                    "Qwen layer-major group plan has invalid geometry routes=%u unique=%u active=%u", rows * top_k,
+                    num_experts, top_k);
+    if (num_experts > pbmoe::kPlanMaxExperts)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported prefill plan: %u experts (max %u)",
+                    num_experts, pbmoe::kPlanMaxExperts);
+    if (static_cast<uint64_t>(rows) * top_k > 0xffffffffull)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "prefill group plan: route count overflows u32");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    pbmoe::PrefillPlanArgs a{route_ids,   rows,        top_k,          num_experts, slot_experts, unique_count,
+                             route_slots, source_rows, output_indices, groups,      ctx->status};
+    cudaError_t e = pbmoe::prefill_plan_launch(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill group plan launch");
+    return PBMOE_OK;
+}
+
+int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const uint32_t* slot_experts,
+                          const uint32_t* unique_count, const uint32_t* groups, const uint32_t* source_rows,
+                          uint32_t routes, uint32_t max_unique, const void* x, pbmoe_dtype x_dtype, void* y,
+                          pbmoe_dtype y_dtype, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!w || !w->experts || !slot_experts || !unique_count || !groups || !source_rows || !x || !y)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 grouped gemm: null pointer");
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (w->group_size == 0 || w->rows == 0 || w->cols == 0 || w->num_experts == 0)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 grouped gemm: zero dimension");
+    if (routes == 0 || max_unique == 0) return PBMOE_OK;
+    if (x_dtype != PBMOE_BF16 || !pbmoe::q4_gemm_supported(w->rows, w->cols, w->group_size))
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported q4 grouped gemm: needs bf16 x, group_size 64 and cols a multiple of 64 "
+                    "(got x dtype %d, group %u, cols %u)", static_cast<int>(x_dtype), w->group_size, w->cols);
+    const uint64_t wbytes = uint64_t(w->rows) * w->cols / 2, sbytes = uint64_t(w->rows) * (w->cols / 64) * 2;
+    if (w->packed_offset + wbytes > w->expert_bytes || w->scales_offset + sbytes > w->expert_bytes ||
+        w->biases_offset + sbytes > w->expert_bytes)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 grouped gemm: projection does not fit in an expert slot");
+    if (!aligned(w->experts, 16) || w->expert_bytes % 16 || w->packed_offset % 16 || w->scales_offset % 16 ||
+        w->biases_offset % 16 || !aligned(x, 16) || !aligned(y, 16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
+                    "q4 grouped gemm: expert table, slot stride, component offsets, x and y must be 16-byte aligned");
+    if (static_cast<uint64_t>(pbmoe::q4_grouped_tile_bound(routes, max_unique)) > 65535u)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported q4 grouped gemm: %u routes over %u slots "
+                    "exceed one launch", routes, max_unique);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    pbmoe::Q4GroupedArgs a{};
+    a.experts = w->experts;
+    a.expert_bytes = w->expert_bytes;
+    a.packed_offset = w->packed_offset;
+    a.scales_offset = w->scales_offset;
+    a.biases_offset = w->biases_offset;
+    a.rows = w->rows;
+    a.cols = w->cols;
+    a.num_experts = w->num_experts;
+    a.slot_experts = slot_experts;
+    a.unique_count = unique_count;
+    a.max_unique = max_unique;
+    a.groups = groups;
+    a.source_rows = source_rows;
+    a.routes = routes;
+    a.x = x;
+    a.y = y;
+    a.y_dtype = y_dtype;
+    a.status = ctx->status;
+    cudaError_t e = pbmoe::q4_gemm_grouped_launch(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 grouped gemm launch");
+    return PBMOE_OK;
+}

@@ -141,4 +141,56 @@ void mla_plan_splits(const MlaLaunch& a, int num_sms, uint32_t& split_tokens, ui
 uint32_t mla_max_splits(uint32_t max_batch, int num_sms);
 cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- prefill Q4 GEMM (q4_gemm.cu)
+struct Q4GemmArgs {
+    const uint8_t* packed;
+    const uint16_t* scales;
+    const uint16_t* biases;
+    uint32_t rows, cols, group;  // W [rows x cols] (N x K)
+    const void* x;               // bf16 [m x cols]
+    uint32_t m;
+    void* y;  // [m x rows]
+    pbmoe_dtype y_dtype;
+    uint32_t* status;
+};
+bool q4_gemm_supported(uint32_t N, uint32_t K, uint32_t group);
+cudaError_t q4_gemm_launch(const Q4GemmArgs& a, cudaStream_t s);
+
+// One projection of every expert (gate, up or down) against routes grouped by
+// slot: y[first + i] = x[source_rows[first + i]] . W_{slot_experts[slot]}^T.
+struct Q4GroupedArgs {
+    const uint8_t* experts;
+    uint64_t expert_bytes;
+    uint64_t packed_offset, scales_offset, biases_offset;
+    uint32_t rows, cols, num_experts;
+    const uint32_t* slot_experts;  // [max_unique] expert id of each slot
+    const uint32_t* unique_count;  // device scalar
+    uint32_t max_unique;
+    const uint32_t* groups;       // [unique x 2] (start, count)
+    const uint32_t* source_rows;  // [routes]
+    uint32_t routes;
+    const void* x;  // bf16 [tokens x cols]
+    void* y;        // [routes x rows]
+    pbmoe_dtype y_dtype;
+    uint32_t* status;
+};
+uint32_t q4_grouped_tile_bound(uint32_t routes, uint32_t max_unique);
+cudaError_t q4_gemm_grouped_launch(const Q4GroupedArgs& a, cudaStream_t s);
+
+// ---------------------------------------------------------------- prefill group plan (prefill_plan.cu)
+constexpr uint32_t kPlanMaxExperts = 1024;
+struct PrefillPlanArgs {
+    const uint32_t* route_ids;  // [rows x top_k]
+    uint32_t rows, top_k, num_experts;
+    uint32_t* slot_experts;    // [num_experts]: selected ids, ascending
+    uint32_t* unique_count;    // device scalar
+    uint32_t* route_slots;     // [routes] or null
+    uint32_t* source_rows;     // [routes]
+    uint32_t* output_indices;  // [routes]
+    uint32_t* groups;          // [num_experts x 2]
+    uint32_t* status;
+};
+size_t prefill_plan_smem(uint32_t num_experts);
+cudaError_t prefill_plan_launch(const PrefillPlanArgs& a, cudaStream_t s);
+
 }  // namespace pbmoe

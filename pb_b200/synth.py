@@ -71,6 +71,13 @@ def normal_bf16(shape, std: float, g: torch.Generator, device) -> torch.Tensor:
     return (torch.randn(*shape, device=device, dtype=torch.float32, generator=g) * std).to(torch.bfloat16)
 
 
+def random_routes(tokens: int, num_experts: int, top_k: int, g: torch.Generator, device) -> torch.Tensor:
+    """u32-valued int32 [tokens, top_k]: each token's top_k distinct experts,
+    uniformly random (the seeded stand-in for a prefill chunk's routing)."""
+    keys = torch.rand(tokens, num_experts, device=device, generator=g)
+    return keys.topk(top_k, dim=1).indices.to(torch.int32).contiguous()
+
+
 class MoeLayerWeights:
     """Device-resident weights of one synthetic MoE FFN layer (config 1 shapes
     by default: hidden 2048, 512 experts, intermediate 512, group 64, one
