@@ -70,7 +70,8 @@ typedef enum pbmoe_status {
 
 typedef enum pbmoe_dtype {
     PBMOE_F32 = 0,
-    PBMOE_BF16 = 1
+    PBMOE_BF16 = 1,
+    PBMOE_F16 = 2 /* prefill GEMM activations only */
 } pbmoe_dtype;
 
 typedef struct pbmoe_ctx pbmoe_ctx;
@@ -276,16 +277,25 @@ PBMOE_API int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* config, c
 
 /* ---------------------------------------------------------------- prefill */
 
+/* Size the context's prefill workspace: the fp16 image of a bf16 activation
+ * matrix of up to max_rows x max_cols, which the tensor-core GEMMs read.
+ * Allocation happens here, never in pbmoe_q4_gemm / pbmoe_q4_gemm_grouped;
+ * fp16 activations need no workspace. */
+PBMOE_API int pbmoe_prefill_reserve(pbmoe_ctx* ctx, uint32_t max_rows, uint32_t max_cols);
+
 /* Y[m, r] = sum_c X[m, c] * (q[r,c] * scale + bias) for a dense Q4 weight:
- * X bf16 [m x cols] (16-byte aligned rows), Y [m x rows] in y_dtype, fp32
- * accumulate. Operands are fp16: each weight is dequantised once (q * s + b,
- * one fp16 rounding) and x converts exactly; an x entry of magnitude >= 65536
- * or non-finite latches PBMOE_DEV_ERR_F16_RANGE (pbmoe_device_status).
+ * X [m x cols] bf16 or fp16 (rows 16-byte aligned), Y [m x rows] in y_dtype
+ * (f32 or bf16), fp32 accumulation on the tensor cores (tcgen05). Operands are
+ * fp16: each weight is dequantised once (q * s + b, one fp16 rounding) and a
+ * bf16 x converts exactly into the context's workspace (pbmoe_prefill_reserve);
+ * an x entry of magnitude >= 65536 or non-finite latches
+ * PBMOE_DEV_ERR_F16_RANGE (pbmoe_device_status).
  * Replaces the batched prefill matvec q4_mmap_fma_matvec_batch_bf16_scale_bias
  * (shaders.metal:973-1057, q4_mmap_fma_row_bf16_pair :768-866) as encoded by
  * encode_layer_major_q4_matrix_from_buffer (metal/mod.rs:4201-4275) for one
- * matrix. Needs group_size 64 and cols a multiple of 64; packed, scales,
- * biases and x 16-byte aligned. */
+ * matrix. Needs group_size 64 and cols a multiple of 512 (whole 16-byte runs
+ * of eight group scales per row) up to 4096 (the per-tile scale buffers stay
+ * in shared memory); packed, scales, biases, x and y 16-byte aligned. */
 PBMOE_API int pbmoe_q4_gemm(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype,
                             void* y, pbmoe_dtype y_dtype, uint32_t m, void* stream);
 
@@ -323,12 +333,14 @@ typedef struct pbmoe_q4_expert_matrix {
  * reference's per-group matrix outputs (encode_and_execute_layer_major,
  * metal/mod.rs:3334-3600). Plan arrays are device memory, as written by
  * pbmoe_prefill_group_plan; max_unique bounds *unique_count (the grid is
- * sized from routes and max_unique, so no read-back is needed). x bf16
- * [tokens x cols]; y [routes x rows] in y_dtype. */
+ * sized from routes and max_unique, so no read-back is needed). x [x_rows x
+ * cols] bf16 (converted through the prefill workspace) or fp16; a source row
+ * >= x_rows latches PBMOE_DEV_ERR_EXPERT_ID. y [routes x rows] in y_dtype. */
 PBMOE_API int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const uint32_t* slot_experts,
                                     const uint32_t* unique_count, const uint32_t* groups,
                                     const uint32_t* source_rows, uint32_t routes, uint32_t max_unique,
-                                    const void* x, pbmoe_dtype x_dtype, void* y, pbmoe_dtype y_dtype, void* stream);
+                                    const void* x, pbmoe_dtype x_dtype, uint32_t x_rows, void* y,
+                                    pbmoe_dtype y_dtype, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -31,6 +31,7 @@ PBMOE_DEV_ERR_F16_RANGE = 0x10
 
 PBMOE_F32 = 0
 PBMOE_BF16 = 1
+PBMOE_F16 = 2
 
 ROUTE_RENORMALIZE_SELECTED = 0
 ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR = 1
@@ -40,7 +41,7 @@ EXPORTED = [
     "pbmoe_init", "pbmoe_destroy", "pbmoe_last_error", "pbmoe_abi_version", "pbmoe_reserve",
     "pbmoe_moe_workspace_bytes", "pbmoe_device_status", "pbmoe_fixed_q4_layout", "pbmoe_q4_matvec",
     "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static", "pbmoe_mla_reserve", "pbmoe_mla_decode",
-    "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
+    "pbmoe_prefill_reserve", "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
 ]
 
 
@@ -121,10 +122,11 @@ def load():
         L.pbmoe_mla_decode.argtypes = [vp, C.POINTER(MlaConfig), C.POINTER(MlaArgs), vp]
         L.pbmoe_moe_layer_static.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
                                              u32, vp, vp, vp, C.c_char_p, C.c_size_t, vp]
+        L.pbmoe_prefill_reserve.argtypes = [vp, u32, u32]
         L.pbmoe_q4_gemm.argtypes = [vp, C.POINTER(Q4Tensor), vp, i32, vp, i32, u32, vp]
         L.pbmoe_prefill_group_plan.argtypes = [vp, vp, u32, u32, u32, vp, vp, vp, vp, vp, vp, vp]
-        L.pbmoe_q4_gemm_grouped.argtypes = [vp, C.POINTER(Q4ExpertMatrix), vp, vp, vp, vp, u32, u32, vp, i32, vp,
-                                            i32, vp]
+        L.pbmoe_q4_gemm_grouped.argtypes = [vp, C.POINTER(Q4ExpertMatrix), vp, vp, vp, vp, u32, u32, vp, i32, u32,
+                                            vp, i32, vp]
         _lib = L
     return _lib
 
@@ -148,6 +150,8 @@ def _dtype_code(t):
         return PBMOE_F32
     if t.dtype == torch.bfloat16:
         return PBMOE_BF16
+    if t.dtype == torch.float16:
+        return PBMOE_F16
     raise TypeError(f"unsupported activation dtype {t.dtype}")
 
 
@@ -220,8 +224,11 @@ class Context:
                        C.cast(kr, C.c_void_p), w_uk.data_ptr(), w_uv.data_ptr(), out.data_ptr(), _dtype_code(out))
         self.check(self.lib.pbmoe_mla_decode(self.h, C.byref(config), C.byref(args), self.stream_ptr(stream)))
 
+    def prefill_reserve(self, max_rows, max_cols):
+        self.check(self.lib.pbmoe_prefill_reserve(self.h, max_rows, max_cols))
+
     def q4_gemm(self, packed, scales, biases, rows, cols, group, x, y, stream=None):
-        """y [m, rows] = x [m, cols] . W^T for a dense Q4 weight."""
+        """y [m, rows] = x [m, cols] . W^T for a dense Q4 weight (x bf16 needs prefill_reserve)."""
         t = Q4Tensor(packed.data_ptr(), scales.data_ptr(), biases.data_ptr(), rows, cols, group)
         self.check(self.lib.pbmoe_q4_gemm(self.h, C.byref(t), _ptr(x), _dtype_code(x), _ptr(y), _dtype_code(y),
                                           int(x.shape[0]), self.stream_ptr(stream)))
@@ -236,7 +243,8 @@ class Context:
                         max_unique, x, y, stream=None):
         self.check(self.lib.pbmoe_q4_gemm_grouped(
             self.h, C.byref(matrix), _ptr(slot_experts), _ptr(unique_count), _ptr(groups), _ptr(source_rows),
-            routes, max_unique, _ptr(x), _dtype_code(x), _ptr(y), _dtype_code(y), self.stream_ptr(stream)))
+            routes, max_unique, _ptr(x), _dtype_code(x), int(x.shape[0]), _ptr(y), _dtype_code(y),
+            self.stream_ptr(stream)))
 
     def device_status(self, clear=True, stream=None) -> int:
         v = C.c_uint32()

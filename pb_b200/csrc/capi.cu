@@ -20,6 +20,8 @@ struct pbmoe_ctx {
     void* mla_base = nullptr;  // MLA decode workspace
     size_t mla_bytes = 0;
     uint32_t mla_batch = 0;
+    void* x16_base = nullptr;  // prefill fp16 activation image
+    size_t x16_elems = 0;
     int num_sms = 0;
     std::string last_error;
 };
@@ -209,6 +211,7 @@ int pbmoe_destroy(pbmoe_ctx* ctx) {
         DeviceGuard g(ctx->device);
         if (ctx->ws_base) cudaFree(ctx->ws_base);
         if (ctx->mla_base) cudaFree(ctx->mla_base);
+        if (ctx->x16_base) cudaFree(ctx->x16_base);
         if (ctx->status) cudaFree(ctx->status);
     }
     delete ctx;
@@ -526,27 +529,76 @@ int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_
     return PBMOE_OK;
 }
 
+int pbmoe_prefill_reserve(pbmoe_ctx* ctx, uint32_t max_rows, uint32_t max_cols) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (max_rows == 0 || max_cols == 0 || max_cols % 64)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "prefill reserve: %u x %u (cols must be a positive multiple of 64)",
+                    max_rows, max_cols);
+    const size_t need = size_t(max_rows) * max_cols;
+    if (ctx->x16_base && ctx->x16_elems >= need) return PBMOE_OK;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    if (ctx->x16_base) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before prefill workspace resize");
+        cudaFree(ctx->x16_base);
+        ctx->x16_base = nullptr;
+        ctx->x16_elems = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->x16_base, need * 2);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill workspace allocation");
+    ctx->x16_elems = need;
+    return PBMOE_OK;
+}
+
+namespace {
+// fp16 activations for the tensor-core GEMMs: x itself, or its conversion
+// into the context workspace (queued on `stream` ahead of the GEMM).
+int prefill_x16(pbmoe_ctx* ctx, const void* x, pbmoe_dtype x_dtype, size_t elems, cudaStream_t stream,
+                const void** out) {
+    if (x_dtype == PBMOE_F16) {
+        *out = x;
+        return PBMOE_OK;
+    }
+    if (x_dtype != PBMOE_BF16)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported prefill GEMM activations: dtype %d "
+                    "(bf16 or fp16)", static_cast<int>(x_dtype));
+    if (!ctx->x16_base || ctx->x16_elems < elems)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "prefill GEMM: bf16 activations of %zu elements need "
+                    "pbmoe_prefill_reserve (workspace holds %zu)", elems, ctx->x16_elems);
+    cudaError_t e = pbmoe::x16_convert_launch(x, ctx->x16_base, elems, ctx->status, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "activation fp16 conversion launch");
+    *out = ctx->x16_base;
+    return PBMOE_OK;
+}
+}  // namespace
+
 int pbmoe_q4_gemm(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype, void* y,
                   pbmoe_dtype y_dtype, uint32_t m, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
     if (!w || !w->packed || !w->scales || !w->biases || !x || !y)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 gemm: null pointer");
     if (w->group_size == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "group_size must be positive");
-    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16 && x_dtype != PBMOE_F16) ||
+        (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
     if (w->rows == 0 || w->cols == 0 || m == 0) return PBMOE_OK;
-    if (x_dtype != PBMOE_BF16 || !pbmoe::q4_gemm_supported(w->rows, w->cols, w->group_size))
+    if (x_dtype == PBMOE_F32 || !pbmoe::q4_gemm_supported(w->rows, w->cols, w->group_size))
         return fail(ctx, PBMOE_ERR_UNSUPPORTED,
-                    "FlashMoe unsupported q4 gemm: needs bf16 x, group_size 64 and cols a multiple of 64 "
+                    "FlashMoe unsupported q4 gemm: needs bf16 or fp16 x, group_size 64 and cols a multiple of 512 "
                     "(got x dtype %d, group %u, cols %u)", static_cast<int>(x_dtype), w->group_size, w->cols);
     if (!aligned(w->packed, 16) || !aligned(w->scales, 16) || !aligned(w->biases, 16) || !aligned(x, 16) ||
         !aligned(y, 16))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 gemm: packed, scales, biases, x and y must be 16-byte aligned");
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const void* x16 = nullptr;
+    int rc = prefill_x16(ctx, x, x_dtype, size_t(m) * w->cols, s, &x16);
+    if (rc) return rc;
     pbmoe::Q4GemmArgs a{static_cast<const uint8_t*>(w->packed), w->scales, w->biases, w->rows, w->cols,
-                        w->group_size, x, m, y, y_dtype, ctx->status};
-    cudaError_t e = pbmoe::q4_gemm_launch(a, static_cast<cudaStream_t>(stream));
+                        w->group_size, x16, m, y, y_dtype, ctx->status};
+    cudaError_t e = pbmoe::q4_gemm_launch(a, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 gemm launch");
     return PBMOE_OK;
 }
@@ -579,20 +631,23 @@ int pbmoe_prefill_group_plan(pbmoe_ctx* ctx, const uint32_t* route_ids, uint32_t
 
 int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const uint32_t* slot_experts,
                           const uint32_t* unique_count, const uint32_t* groups, const uint32_t* source_rows,
-                          uint32_t routes, uint32_t max_unique, const void* x, pbmoe_dtype x_dtype, void* y,
-                          pbmoe_dtype y_dtype, void* stream) {
+                          uint32_t routes, uint32_t max_unique, const void* x, pbmoe_dtype x_dtype, uint32_t x_rows,
+                          void* y, pbmoe_dtype y_dtype, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
     if (!w || !w->experts || !slot_experts || !unique_count || !groups || !source_rows || !x || !y)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 grouped gemm: null pointer");
-    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16 && x_dtype != PBMOE_F16) ||
+        (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
     if (w->group_size == 0 || w->rows == 0 || w->cols == 0 || w->num_experts == 0)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 grouped gemm: zero dimension");
     if (routes == 0 || max_unique == 0) return PBMOE_OK;
-    if (x_dtype != PBMOE_BF16 || !pbmoe::q4_gemm_supported(w->rows, w->cols, w->group_size))
+    if (x_rows == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 grouped gemm: x has no rows");
+    if (x_dtype == PBMOE_F32 || !pbmoe::q4_grouped_supported(w->rows, w->cols, w->group_size, routes, max_unique))
         return fail(ctx, PBMOE_ERR_UNSUPPORTED,
-                    "FlashMoe unsupported q4 grouped gemm: needs bf16 x, group_size 64 and cols a multiple of 64 "
-                    "(got x dtype %d, group %u, cols %u)", static_cast<int>(x_dtype), w->group_size, w->cols);
+                    "FlashMoe unsupported q4 grouped gemm: needs bf16 or fp16 x, group_size 64, cols a multiple "
+                    "of 512 and a tile table that fits in shared memory (got x dtype %d, group %u, cols %u, "
+                    "%u routes over %u slots)", static_cast<int>(x_dtype), w->group_size, w->cols, routes, max_unique);
     const uint64_t wbytes = uint64_t(w->rows) * w->cols / 2, sbytes = uint64_t(w->rows) * (w->cols / 64) * 2;
     if (w->packed_offset + wbytes > w->expert_bytes || w->scales_offset + sbytes > w->expert_bytes ||
         w->biases_offset + sbytes > w->expert_bytes)
@@ -601,11 +656,12 @@ int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const
         w->biases_offset % 16 || !aligned(x, 16) || !aligned(y, 16))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
                     "q4 grouped gemm: expert table, slot stride, component offsets, x and y must be 16-byte aligned");
-    if (static_cast<uint64_t>(pbmoe::q4_grouped_tile_bound(routes, max_unique)) > 65535u)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported q4 grouped gemm: %u routes over %u slots "
-                    "exceed one launch", routes, max_unique);
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const void* x16 = nullptr;
+    int rc = prefill_x16(ctx, x, x_dtype, size_t(x_rows) * w->cols, s, &x16);
+    if (rc) return rc;
     pbmoe::Q4GroupedArgs a{};
     a.experts = w->experts;
     a.expert_bytes = w->expert_bytes;
@@ -621,11 +677,12 @@ int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const
     a.groups = groups;
     a.source_rows = source_rows;
     a.routes = routes;
-    a.x = x;
+    a.x16 = x16;
+    a.x_rows = x_rows;
     a.y = y;
     a.y_dtype = y_dtype;
     a.status = ctx->status;
-    cudaError_t e = pbmoe::q4_gemm_grouped_launch(a, static_cast<cudaStream_t>(stream));
+    cudaError_t e = pbmoe::q4_gemm_grouped_launch(a, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 grouped gemm launch");
     return PBMOE_OK;
 }

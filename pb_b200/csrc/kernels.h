@@ -147,7 +147,7 @@ struct Q4GemmArgs {
     const uint16_t* scales;
     const uint16_t* biases;
     uint32_t rows, cols, group;  // W [rows x cols] (N x K)
-    const void* x;               // bf16 [m x cols]
+    const void* x16;             // fp16 [m x cols]
     uint32_t m;
     void* y;  // [m x rows]
     pbmoe_dtype y_dtype;
@@ -155,9 +155,11 @@ struct Q4GemmArgs {
 };
 bool q4_gemm_supported(uint32_t N, uint32_t K, uint32_t group);
 cudaError_t q4_gemm_launch(const Q4GemmArgs& a, cudaStream_t s);
+// bf16 [elems] -> fp16 (elems a multiple of 8), latching PBMOE_DEV_ERR_F16_RANGE
+cudaError_t x16_convert_launch(const void* x, void* x16, size_t elems, uint32_t* status, cudaStream_t s);
 
 // One projection of every expert (gate, up or down) against routes grouped by
-// slot: y[first + i] = x[source_rows[first + i]] . W_{slot_experts[slot]}^T.
+// slot: y[first + i] = x16[source_rows[first + i]] . W_{slot_experts[slot]}^T.
 struct Q4GroupedArgs {
     const uint8_t* experts;
     uint64_t expert_bytes;
@@ -169,12 +171,14 @@ struct Q4GroupedArgs {
     const uint32_t* groups;       // [unique x 2] (start, count)
     const uint32_t* source_rows;  // [routes]
     uint32_t routes;
-    const void* x;  // bf16 [tokens x cols]
-    void* y;        // [routes x rows]
+    const void* x16;  // fp16 [x_rows x cols]
+    uint32_t x_rows;
+    void* y;  // [routes x rows]
     pbmoe_dtype y_dtype;
     uint32_t* status;
 };
 uint32_t q4_grouped_tile_bound(uint32_t routes, uint32_t max_unique);
+bool q4_grouped_supported(uint32_t N, uint32_t K, uint32_t group, uint32_t routes, uint32_t max_unique);
 cudaError_t q4_gemm_grouped_launch(const Q4GroupedArgs& a, cudaStream_t s);
 
 // ---------------------------------------------------------------- prefill group plan (prefill_plan.cu)

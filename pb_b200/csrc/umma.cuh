@@ -1,0 +1,108 @@
+// umma.cuh — 5th-generation tensor core (tcgen05) building blocks for sm_100a:
+// tensor-memory allocation, shared-memory matrix descriptors, the single-thread
+// MMA issue, commit-to-mbarrier and the TMEM -> register epilogue load.
+//
+// Conventions used by the kernels here: cta_group::1 (one SM per MMA), both
+// operands K-major in shared memory with the 128-byte swizzle (rows of 64
+// 16-bit elements, 8-row groups 1024 bytes apart, tile bases 1024-aligned),
+// fp32 accumulation in TMEM with accumulator row i in TMEM lane i.
+#pragma once
+
+#include "pipe.cuh"
+
+namespace pbmoe {
+
+// ---------------------------------------------------------------- TMEM
+// Allocate `ncols` (a power of two >= 32) TMEM columns; one full warp executes
+// it and the base address lands in shared memory at `dst`.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Order tcgen05 operations around thread synchronisation (barriers, mbarrier
+// waits) that hands TMEM or MMA results from one thread to another.
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Make this thread's generic-proxy shared-memory writes (st.shared, and
+// cp.async copies it has waited for) visible to the async proxy that
+// tcgen05.mma reads operands through.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- descriptors
+// Shared-memory matrix descriptor, K-major with the 128-byte swizzle: start
+// address (16-byte units, bits 0-13), leading byte offset 16 B (unused by a
+// swizzled K-major operand, bits 16-29), stride byte offset 1024 B between
+// 8-row groups (bits 32-45), descriptor version 1 (bits 46-47), swizzle mode
+// 2 = 128B (bits 61-63). Advancing K by 16 elements adds 32 bytes to the
+// start address inside the 128-byte swizzled row.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor of kind::f16 with fp16 A and B (both K-major), fp32
+// D, shape M x N: D format bits 4-5 (1 = f32), A/B formats bits 7-9 / 10-12
+// (0 = f16), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N) {
+    return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled
+// K-major tile (rows of 128 bytes, tile base 1024-aligned).
+__host__ __device__ constexpr uint32_t sw128_offset(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+
+// ---------------------------------------------------------------- MMA
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05.mma this thread issued so far has
+// completed (their shared-memory operands may then be overwritten).
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---------------------------------------------------------------- epilogue
+// 32 consecutive fp32 columns of this thread's TMEM lane (shape 32x32b: warp
+// w % 4 reads lanes 32*(w%4) .. +31). The wait is tied to the registers so no
+// use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]),
+                   "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]),
+                   "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+                 :
+                 : "memory");
+}
+
+}  // namespace pbmoe

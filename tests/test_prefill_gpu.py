@@ -24,6 +24,7 @@ def ctx():
 
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     c = capi.Context(0)
+    c.prefill_reserve(4096, 2048)
     yield c
     c.close()
 
@@ -44,12 +45,13 @@ def _gemm(ctx, packed, s, b, n, k, x, out_dtype):
 
 
 @pytest.mark.parametrize("m,n,k", [
-    (1, 128, 64), (5, 200, 192), (130, 257, 128), (128, 128, 2048), (300, 512, 512), (17, 1000, 320),
+    (1, 128, 512), (5, 200, 512), (130, 257, 1024), (128, 128, 2048), (300, 512, 512), (17, 1000, 1536),
+    (520, 384, 4096), (129, 5, 512),
 ])
 @pytest.mark.parametrize("out", ["bf16", "f32"])
 def test_dense_gemm_shapes(ctx, oracle, m, n, k, out):
-    """Ragged token counts, weight rows not a multiple of 128 (and of 8: the
-    scalar store path), group counts that are not a multiple of 8."""
+    """Ragged token counts (tiles of 128 tokens), weight rows not a multiple
+    of 128, K from one to eight 512-wide runs of groups."""
     import torch
 
     from pb_b200 import synth
@@ -60,6 +62,42 @@ def test_dense_gemm_shapes(ctx, oracle, m, n, k, out):
     y = _gemm(ctx, packed, s, b, n, k, x, torch.bfloat16 if out == "bf16" else torch.float32)
     ref = oracle.q4_gemm(x.float().cpu().numpy(), packed.cpu().numpy(), _u16(s), _u16(b), n, k, 64, threads=8)
     assert_close(y, ref, what=f"gemm {m}x{n}x{k}")
+
+
+def test_dense_gemm_f16_input(ctx, oracle):
+    """fp16 activations go straight to the tensor cores (no workspace)."""
+    import torch
+
+    from pb_b200 import synth
+
+    g = synth.gen("cuda", 77)
+    packed, s, b = synth.q4_matrix(384, 512, 64, g, "cuda")
+    x = synth.normal_bf16((70, 512), 1.0, g, "cuda")
+    y = _gemm(ctx, packed, s, b, 384, 512, x.half(), torch.float32)
+    ref = oracle.q4_gemm(x.float().cpu().numpy(), packed.cpu().numpy(), _u16(s), _u16(b), 384, 512, 64, threads=8)
+    assert_close(y, ref, what="f16 input")
+
+
+def test_dense_gemm_needs_workspace():
+    import torch
+
+    from pb_b200 import capi, synth
+
+    c = capi.Context(0)
+    try:
+        g = synth.gen("cuda", 8)
+        packed, s, b = synth.q4_matrix(128, 512, 64, g, "cuda")
+        x = synth.normal_bf16((4, 512), 1.0, g, "cuda")
+        y = torch.empty(4, 128, device="cuda", dtype=torch.float32)
+        with pytest.raises(capi.PbmoeError) as e:
+            c.q4_gemm(packed, s, b, 128, 512, 64, x, y)
+        assert e.value.code == capi.PBMOE_ERR_NO_WORKSPACE
+        c.prefill_reserve(4, 512)
+        c.q4_gemm(packed, s, b, 128, 512, 64, x, y)
+        torch.cuda.synchronize()
+        assert torch.isfinite(y).all()
+    finally:
+        c.close()
 
 
 def test_dense_gemm_config2(ctx, oracle):
@@ -91,9 +129,13 @@ def test_dense_gemm_rejects(ctx):
     with pytest.raises(capi.PbmoeError) as e:
         ctx.q4_gemm(packed, s, b, 64, 96, 32, x, y)
     assert e.value.code == capi.PBMOE_ERR_UNSUPPORTED
-    packed, s, b = synth.q4_matrix(64, 128, 64, g, "cuda")
+    packed, s, b = synth.q4_matrix(64, 512, 64, g, "cuda")
     with pytest.raises(capi.PbmoeError) as e:
-        ctx.q4_gemm(packed, s, b, 64, 128, 64, torch.zeros(4, 128, device="cuda"), y)  # f32 x
+        ctx.q4_gemm(packed, s, b, 64, 512, 64, torch.zeros(4, 512, device="cuda"), y)  # f32 x
+    assert e.value.code == capi.PBMOE_ERR_UNSUPPORTED
+    packed, s, b = synth.q4_matrix(64, 576, 64, g, "cuda")
+    with pytest.raises(capi.PbmoeError) as e:  # K not a multiple of 512
+        ctx.q4_gemm(packed, s, b, 64, 576, 64, synth.normal_bf16((4, 576), 1.0, g, "cuda"), y)
     assert e.value.code == capi.PBMOE_ERR_UNSUPPORTED
 
 
@@ -106,15 +148,15 @@ def test_dense_gemm_f16_range_latches(ctx):
     from pb_b200 import capi, synth
 
     g = synth.gen("cuda", 6)
-    packed, s, b = synth.q4_matrix(128, 128, 64, g, "cuda")
-    x = synth.normal_bf16((3, 128), 1.0, g, "cuda")
+    packed, s, b = synth.q4_matrix(128, 512, 64, g, "cuda")
+    x = synth.normal_bf16((3, 512), 1.0, g, "cuda")
     y = torch.empty(3, 128, device="cuda", dtype=torch.float32)
     ctx.device_status(clear=True)
     x[1, 5] = 65280.0
-    ctx.q4_gemm(packed, s, b, 128, 128, 64, x, y)
+    ctx.q4_gemm(packed, s, b, 128, 512, 64, x, y)
     assert ctx.device_status(clear=True) == 0
     x[2, 70] = -70000.0
-    ctx.q4_gemm(packed, s, b, 128, 128, 64, x, y)
+    ctx.q4_gemm(packed, s, b, 128, 512, 64, x, y)
     assert ctx.device_status(clear=True) & capi.PBMOE_DEV_ERR_F16_RANGE
 
 
@@ -245,19 +287,42 @@ def _grouped_case(ctx, oracle, tokens, E, k, H, I, projection, seed, check_slots
 
 @pytest.mark.parametrize("projection", ["gate", "up", "down"])
 def test_grouped_small(ctx, oracle, projection):
-    _grouped_case(ctx, oracle, tokens=37, E=16, k=3, H=256, I=192, projection=projection, seed=11)
+    _grouped_case(ctx, oracle, tokens=37, E=16, k=3, H=1024, I=512, projection=projection, seed=11)
 
 
 def test_grouped_big_group(ctx, oracle):
     """A slot with more than one 64-route tile (few experts, many tokens)."""
-    _grouped_case(ctx, oracle, tokens=300, E=4, k=2, H=128, I=320, projection="up", seed=12)
+    _grouped_case(ctx, oracle, tokens=300, E=4, k=2, H=512, I=512, projection="up", seed=12)
 
 
 def test_grouped_f32_out(ctx, oracle):
     import torch
 
-    _grouped_case(ctx, oracle, tokens=50, E=8, k=2, H=128, I=128, projection="gate", seed=13,
+    _grouped_case(ctx, oracle, tokens=50, E=8, k=2, H=512, I=512, projection="gate", seed=13,
                   out_dtype=torch.float32)
+
+
+def test_grouped_bad_source_row_latches(ctx):
+    """A source row outside x latches PBMOE_DEV_ERR_EXPERT_ID (the row is not read)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    g = synth.gen("cuda", 15)
+    layout = capi.fixed_q4_layout(512, 512, 64)
+    table = synth.expert_table(2, layout, g, "cuda")
+    x = synth.normal_bf16((4, 512), 1.0, g, "cuda")
+    i32 = dict(device="cuda", dtype=torch.int32)
+    slot_experts = torch.tensor([1], **i32)
+    unique = torch.tensor([1], **i32)
+    groups = torch.tensor([[0, 3]], **i32)
+    source_rows = torch.tensor([0, 9, 2], **i32)
+    y = torch.empty(3, 512, device="cuda", dtype=torch.float32)
+    ctx.device_status(clear=True)
+    ctx.q4_gemm_grouped(capi.expert_matrix(table, layout, 2, "gate"), slot_experts, unique, groups, source_rows, 3,
+                        1, x, y)
+    torch.cuda.synchronize()
+    assert ctx.device_status(clear=True) & capi.PBMOE_DEV_ERR_EXPERT_ID
 
 
 def test_grouped_config2(ctx, oracle):
