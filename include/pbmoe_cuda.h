@@ -277,10 +277,11 @@ PBMOE_API int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* config, c
 
 /* ---------------------------------------------------------------- prefill */
 
-/* Size the context's prefill workspace: the fp16 image of a bf16 activation
- * matrix of up to max_rows x max_cols, which the tensor-core GEMMs read.
- * Allocation happens here, never in pbmoe_q4_gemm / pbmoe_q4_gemm_grouped;
- * fp16 activations need no workspace. */
+/* Size the context's prefill workspace: fp16 token rows for the tensor-core
+ * GEMMs, max_rows x max_cols (pbmoe_q4_gemm with bf16 x: m rows;
+ * pbmoe_q4_gemm_grouped: routes rows, the gathered rows in grouped order).
+ * Allocation happens here, never in the GEMM calls; a dense GEMM on fp16 x
+ * needs no workspace. */
 PBMOE_API int pbmoe_prefill_reserve(pbmoe_ctx* ctx, uint32_t max_rows, uint32_t max_cols);
 
 /* Y[m, r] = sum_c X[m, c] * (q[r,c] * scale + bias) for a dense Q4 weight:
@@ -294,7 +295,7 @@ PBMOE_API int pbmoe_prefill_reserve(pbmoe_ctx* ctx, uint32_t max_rows, uint32_t 
  * (shaders.metal:973-1057, q4_mmap_fma_row_bf16_pair :768-866) as encoded by
  * encode_layer_major_q4_matrix_from_buffer (metal/mod.rs:4201-4275) for one
  * matrix. Needs group_size 64 and cols a multiple of 512 (whole 16-byte runs
- * of eight group scales per row) up to 4096 (the per-tile scale buffers stay
+ * of eight group scales per row) up to 3072 (the per-tile scale buffers stay
  * in shared memory); packed, scales, biases, x and y 16-byte aligned. */
 PBMOE_API int pbmoe_q4_gemm(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype,
                             void* y, pbmoe_dtype y_dtype, uint32_t m, void* stream);
@@ -329,13 +330,14 @@ typedef struct pbmoe_q4_expert_matrix {
  * (start, count) and every j < count,
  *   y[start + j, :] = W_{slot_experts[s]} . x[source_rows[start + j], :].
  * The row gather of qwen_layer_major_gather (shaders.metal:1743-1754) is
- * fused into the activation loads; y stays in grouped order like the
+ * fused with the fp16 conversion; y stays in grouped order like the
  * reference's per-group matrix outputs (encode_and_execute_layer_major,
  * metal/mod.rs:3334-3600). Plan arrays are device memory, as written by
  * pbmoe_prefill_group_plan; max_unique bounds *unique_count (the grid is
  * sized from routes and max_unique, so no read-back is needed). x [x_rows x
- * cols] bf16 (converted through the prefill workspace) or fp16; a source row
- * >= x_rows latches PBMOE_DEV_ERR_EXPERT_ID. y [routes x rows] in y_dtype. */
+ * cols] bf16 or fp16, gathered into grouped order in the prefill workspace
+ * (routes x cols fp16, pbmoe_prefill_reserve); a source row >= x_rows latches
+ * PBMOE_DEV_ERR_EXPERT_ID. y [routes x rows] in y_dtype. */
 PBMOE_API int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const uint32_t* slot_experts,
                                     const uint32_t* unique_count, const uint32_t* groups,
                                     const uint32_t* source_rows, uint32_t routes, uint32_t max_unique,

@@ -552,22 +552,25 @@ int pbmoe_prefill_reserve(pbmoe_ctx* ctx, uint32_t max_rows, uint32_t max_cols) 
 }
 
 namespace {
-// fp16 activations for the tensor-core GEMMs: x itself, or its conversion
-// into the context workspace (queued on `stream` ahead of the GEMM).
-int prefill_x16(pbmoe_ctx* ctx, const void* x, pbmoe_dtype x_dtype, size_t elems, cudaStream_t stream,
-                const void** out) {
-    if (x_dtype == PBMOE_F16) {
+// fp16 token rows for the tensor-core GEMMs: x itself (fp16, no gather), or
+// x[rows[j]] converted / gathered into the context workspace (queued on
+// `stream` ahead of the GEMM).
+int prefill_rows(pbmoe_ctx* ctx, const void* x, pbmoe_dtype x_dtype, const uint32_t* rows, uint32_t nrows,
+                 uint32_t x_rows, uint32_t K, cudaStream_t stream, const void** out) {
+    if (x_dtype != PBMOE_BF16 && x_dtype != PBMOE_F16)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported prefill GEMM activations: dtype %d "
+                    "(bf16 or fp16)", static_cast<int>(x_dtype));
+    if (x_dtype == PBMOE_F16 && !rows) {
         *out = x;
         return PBMOE_OK;
     }
-    if (x_dtype != PBMOE_BF16)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported prefill GEMM activations: dtype %d "
-                    "(bf16 or fp16)", static_cast<int>(x_dtype));
+    const size_t elems = size_t(nrows) * K;
     if (!ctx->x16_base || ctx->x16_elems < elems)
-        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "prefill GEMM: bf16 activations of %zu elements need "
-                    "pbmoe_prefill_reserve (workspace holds %zu)", elems, ctx->x16_elems);
-    cudaError_t e = pbmoe::x16_convert_launch(x, ctx->x16_base, elems, ctx->status, stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "activation fp16 conversion launch");
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "prefill GEMM: %u activation rows of %u need "
+                    "pbmoe_prefill_reserve (workspace holds %zu elements)", nrows, K, ctx->x16_elems);
+    cudaError_t e = pbmoe::x16_gather_launch(x, x_dtype == PBMOE_F16, rows, nrows, x_rows, K, ctx->x16_base,
+                                             ctx->status, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "activation fp16 gather launch");
     *out = ctx->x16_base;
     return PBMOE_OK;
 }
@@ -594,7 +597,7 @@ int pbmoe_q4_gemm(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const void* x16 = nullptr;
-    int rc = prefill_x16(ctx, x, x_dtype, size_t(m) * w->cols, s, &x16);
+    int rc = prefill_rows(ctx, x, x_dtype, nullptr, m, m, w->cols, s, &x16);
     if (rc) return rc;
     pbmoe::Q4GemmArgs a{static_cast<const uint8_t*>(w->packed), w->scales, w->biases, w->rows, w->cols,
                         w->group_size, x16, m, y, y_dtype, ctx->status};
@@ -659,8 +662,8 @@ int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const void* x16 = nullptr;
-    int rc = prefill_x16(ctx, x, x_dtype, size_t(x_rows) * w->cols, s, &x16);
+    const void* xg16 = nullptr;
+    int rc = prefill_rows(ctx, x, x_dtype, source_rows, routes, x_rows, w->cols, s, &xg16);
     if (rc) return rc;
     pbmoe::Q4GroupedArgs a{};
     a.experts = w->experts;
@@ -675,10 +678,8 @@ int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const
     a.unique_count = unique_count;
     a.max_unique = max_unique;
     a.groups = groups;
-    a.source_rows = source_rows;
     a.routes = routes;
-    a.x16 = x16;
-    a.x_rows = x_rows;
+    a.xg16 = xg16;
     a.y = y;
     a.y_dtype = y_dtype;
     a.status = ctx->status;

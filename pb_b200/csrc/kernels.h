@@ -155,11 +155,15 @@ struct Q4GemmArgs {
 };
 bool q4_gemm_supported(uint32_t N, uint32_t K, uint32_t group);
 cudaError_t q4_gemm_launch(const Q4GemmArgs& a, cudaStream_t s);
-// bf16 [elems] -> fp16 (elems a multiple of 8), latching PBMOE_DEV_ERR_F16_RANGE
-cudaError_t x16_convert_launch(const void* x, void* x16, size_t elems, uint32_t* status, cudaStream_t s);
+// fp16 rows for the tensor cores: out[j] = x[rows ? rows[j] : j] for j < nrows
+// (K elements per row, bf16 converted or fp16 copied); latches
+// PBMOE_DEV_ERR_F16_RANGE / PBMOE_DEV_ERR_EXPERT_ID.
+cudaError_t x16_gather_launch(const void* x, bool x_is_f16, const uint32_t* rows, uint32_t nrows, uint32_t x_rows,
+                              uint32_t K, void* out, uint32_t* status, cudaStream_t s);
 
 // One projection of every expert (gate, up or down) against routes grouped by
-// slot: y[first + i] = x16[source_rows[first + i]] . W_{slot_experts[slot]}^T.
+// slot: y[j] = xg16[j] . W_{slot_experts[slot of j]}^T, xg16 the fp16 token
+// rows already gathered into grouped order.
 struct Q4GroupedArgs {
     const uint8_t* experts;
     uint64_t expert_bytes;
@@ -168,12 +172,10 @@ struct Q4GroupedArgs {
     const uint32_t* slot_experts;  // [max_unique] expert id of each slot
     const uint32_t* unique_count;  // device scalar
     uint32_t max_unique;
-    const uint32_t* groups;       // [unique x 2] (start, count)
-    const uint32_t* source_rows;  // [routes]
+    const uint32_t* groups;  // [unique x 2] (start, count)
     uint32_t routes;
-    const void* x16;  // fp16 [x_rows x cols]
-    uint32_t x_rows;
-    void* y;  // [routes x rows]
+    const void* xg16;  // fp16 [routes x cols], grouped order
+    void* y;           // [routes x rows]
     pbmoe_dtype y_dtype;
     uint32_t* status;
 };

@@ -9,36 +9,38 @@
 // re-streams every weight row for each pair of input rows with no matrix
 // units.
 //
-// Here a persistent CTA per SM walks a static list of output tiles of 128
-// weight rows (the UMMA M dimension: one TMEM lane per row) x up to BN tokens
-// (N), K advancing one 64-wide quantisation group per step. Ten warps, each
-// role on its own ring of shared-memory buffers and mbarriers, so that no role
-// waits on another's latency:
+// A persistent CTA per SM walks a static list of output tiles of 128 weight
+// rows (the UMMA M dimension: one TMEM lane per row) x up to BN tokens (N), K
+// advancing two 64-wide quantisation groups per step. Fourteen warps, each
+// role on its own ring of buffers and mbarriers:
 //
-//   warp 0      loader: cp.async of each step's nibbles (128 rows x 32 B) into
-//               a deep W ring and of each tile's scales and biases (double-
-//               buffered); completion arrives asynchronously on wfull / sfull
-//               through cp.async.mbarrier.arrive.noinc, so it never waits on
-//               its own copies.
-//   warp 1      TMEM owner; lane 0 issues four tcgen05.mma (K = 16 each) per
-//               step when afull completes and commits them to aempty / bempty
-//               (frees the A and B stages) and, per tile, to tfull.
-//   warps 2-5   one weight row per thread: dequantise w = q*s + b to fp16 (one
-//               rounding) into the swizzled A tile; and, P steps ahead, copy
-//               the tokens' fp16 rows (gathered by row index) into the
-//               128B-swizzled K-major B ring. Each thread waits for its own
-//               B copies of the step (cp.async.wait_group P), fences its A
-//               stores and those copies to the async proxy the tensor core
-//               reads through (fence.proxy.async) and arrives on afull.
-//   warps 6-9   epilogue: tcgen05.ld of the finished accumulator (double-
+//   warp 0      loader (one thread): TMA loads of each step's nibbles (128
+//               rows x 64 B, 64-byte swizzle) into a W ring, of the step's
+//               fp16 token rows (two boxes of 64 k x BN rows, 128-byte
+//               swizzle, the UMMA K-major layout) into a B ring, and bulk
+//               copies of each tile's
+//               scales and biases; all complete as transaction bytes on the
+//               ring's mbarrier, so the loader never waits on its own copies.
+//   warp 1      TMEM owner; lane 0 issues eight tcgen05.mma (K = 16 each, A
+//               from TMEM, B from shared memory) per step when afull and bfull
+//               complete, commits them to aempty / bempty and per tile to tfull.
+//   warps 2-9   dequant, two warps per 32-row TMEM lane quarter, one per
+//               group of the step: each thread takes its row's 64 weights of
+//               that group, w = q*s + b to fp16 (one rounding), 32 packed
+//               columns written straight into the step's A slot in TMEM
+//               (tcgen05.st), then arrives on afull. A never touches shared
+//               memory, so no proxy fence is needed between the dequant and
+//               the MMA.
+//   warps 10-13 epilogue: tcgen05.ld of the finished accumulator (double-
 //               buffered in TMEM, so tile t+1's MMAs overlap tile t's stores),
 //               stores, arrive on tempty.
 //
 // Operands are fp16. bf16 weights would carry 2^-9 relative rounding per
 // weight (up to ~0.9% max-relative error against the f32 reference on
 // config-2 shapes); fp16 keeps 11 bits. bf16 activations convert to fp16
-// exactly (x16_convert_kernel); a magnitude >= 65536 or a non-finite value
-// has no fp16 image and latches PBMOE_DEV_ERR_F16_RANGE.
+// exactly (x16_gather_kernel, which also gathers the grouped rows into
+// grouped order); a magnitude >= 65536 or a non-finite value has no fp16
+// image and latches PBMOE_DEV_ERR_F16_RANGE.
 //
 // Nibble unpack: byte t of a packed word holds k = 2t (low nibble) and
 // 2t+1 (high nibble). prmt copies the byte into both halves, one lop3 keeps
@@ -50,7 +52,10 @@
 // and raises a CTA-wide abort flag on which all roles stop; the MMA thread
 // drains its issued MMAs and the loader its copies before TMEM is released.
 
+#include <cuda.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "kernels.h"
 #include "pipe.cuh"
@@ -58,31 +63,31 @@
 
 namespace pbmoe {
 
-constexpr int kUmThreads = 320;
+constexpr int kUmThreads = 448;  // loader, MMA, 8 dequant, 4 epilogue warps
+constexpr uint32_t kDequantThreads = 256;
 constexpr uint32_t kUmRows = 128;
 constexpr uint32_t kMagicPair = 0x54006400u;  // f16x2 (lo 1024.0, hi 64.0)
 constexpr uint32_t kNoSlot = 0xffffffffu;
 
-template <int BN_, int SA_, int SB_, int SW_, bool kGathered_>
+template <int BN_, int SB_, int SW_, bool kGathered_>
 struct UmmaCfg {
-    static constexpr int BN = BN_, SA = SA_, SB = SB_, SW = SW_;
-    static constexpr int P = SB - 2;  // B copies run P steps ahead of the dequant step
+    static constexpr int BN = BN_, SA = 3, SB = SB_, SW = SW_;
     static constexpr bool kGathered = kGathered_;
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "UMMA N per accumulator");
-    static_assert(SA >= 2 && SB >= 3, "rings");
-    static constexpr uint32_t kA = kUmRows * 128;  // fp16 [128 rows][64 k], swizzled
-    static constexpr uint32_t kB = BN * 128;       // fp16 [BN tokens][64 k], swizzled (multiple of 1024)
-    static constexpr uint32_t kW = kUmRows * 32;   // nibbles [128 rows][32 B]
-    static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
-    static constexpr int kBRows = BN / 16;         // token rows each dequant thread copies per step
+    static constexpr uint32_t kBox = BN * 128;    // fp16 [BN tokens][64 k], 128B-swizzled (multiple of 1024)
+    static constexpr uint32_t kB = 2 * kBox;      // one step: two k-boxes
+    static constexpr uint32_t kW = kUmRows * 64;  // nibbles [128 rows][64 B] (two groups), 64B-swizzled
+    static constexpr uint32_t kACols = 64;        // one step of A: 128 k as packed fp16 pairs
+    static constexpr uint32_t kAccCols = 2 * BN;  // two accumulators, then SA A slots
+    static constexpr uint32_t kTmemCols =
+        (kAccCols + SA * kACols) <= 256 ? 256 : 512;
     static constexpr size_t sbuf_bytes(uint32_t groups) { return size_t(kUmRows) * groups * 4; }  // scales + biases
     static constexpr size_t smem(uint32_t groups, uint32_t table) {
-        return 1024 + size_t(SA) * kA + size_t(SB) * kB + size_t(SW) * kW + 2 * sbuf_bytes(groups) +
-               size_t(table) * 4;
+        return 1024 + size_t(SB) * kB + size_t(SW) * kW + 2 * sbuf_bytes(groups) + size_t(table) * 4;
     }
 };
-using DenseCfg = UmmaCfg<128, 3, 6, 8, false>;
-using GroupedCfg = UmmaCfg<64, 3, 8, 12, true>;
+using DenseCfg = UmmaCfg<128, 4, 6, false>;
+using GroupedCfg = UmmaCfg<64, 6, 8, true>;
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -123,25 +128,15 @@ __device__ __forceinline__ bool wait_or_abort_lazy(uint64_t* bar, uint32_t parit
     }
 }
 
-__device__ __forceinline__ bool warp_wait_lazy(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
-                                               uint32_t* status) {
+// A wait decided by lane 0 and broadcast, so the warp stays converged for the
+// warp-collective operations that follow.
+template <bool kLazy>
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                          uint32_t* status) {
     bool ok = false;
-    if ((threadIdx.x & 31) == 0) ok = wait_or_abort_lazy(bar, parity, abort_flag, status);
+    if ((threadIdx.x & 31) == 0)
+        ok = kLazy ? wait_or_abort_lazy(bar, parity, abort_flag, status) : wait_or_abort(bar, parity, abort_flag, status);
     return __shfl_sync(kFull, ok ? 1u : 0u, 0) != 0u;
-}
-
-// wait_or_abort decided by lane 0 and broadcast, so the warp stays converged
-// for the warp-collective operations that follow.
-__device__ __forceinline__ bool warp_wait_or_abort(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
-                                                   uint32_t* status) {
-    bool ok = false;
-    if ((threadIdx.x & 31) == 0) ok = wait_or_abort(bar, parity, abort_flag, status);
-    return __shfl_sync(kFull, ok ? 1u : 0u, 0) != 0u;
-}
-
-__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes)
-                 : "memory");
 }
 
 // bf16 bits -> fp16 bits (round to nearest)
@@ -149,9 +144,8 @@ __device__ __forceinline__ uint32_t f16_of_bf16(uint32_t v16) {
     return __half_as_ushort(__float2half_rn(__uint_as_float(v16 << 16)));
 }
 
-// Eight fp16 weights (k = 8j .. 8j+7) from packed word w of one row.
-__device__ __forceinline__ uint4 dequant_word_f16(uint32_t w, uint32_t s2, uint32_t b2) {
-    uint32_t o[4];
+// Four packed fp16 pairs (k = 8j .. 8j+7 in order) from packed word w of one row.
+__device__ __forceinline__ void dequant_word_f16(uint32_t w, uint32_t s2, uint32_t b2, uint32_t* o) {
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         const uint32_t X = __byte_perm(w, 0u, 0x4040u + 0x0101u * t);  // (byte t, 0, byte t, 0)
@@ -160,29 +154,25 @@ __device__ __forceinline__ uint4 dequant_word_f16(uint32_t w, uint32_t s2, uint3
         asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q) : "r"(m), "r"(kMagicPair));
         asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[t]) : "r"(q), "r"(s2), "r"(b2));
     }
-    return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Kernel arguments. Dense: packed / scales / biases of one matrix. Grouped:
-// the expert table and the component offsets of one projection in a slot.
+// Kernel arguments. Dense: scales / biases of one matrix, the nibbles through
+// the W tensor map (a single "expert"). Grouped: the expert table and the
+// component offsets of one projection in a slot.
 struct UmmaParams {
-    const uint8_t* packed;
     const uint16_t* scales;
     const uint16_t* biases;
     const uint8_t* experts;
     uint64_t expert_bytes;
-    uint64_t packed_offset, scales_offset, biases_offset;
-    uint32_t N, K;                 // per-matrix rows x cols
+    uint64_t scales_offset, biases_offset;
+    uint32_t N, K;  // per-matrix rows x cols
     uint32_t num_experts;
-    const uint16_t* x16;  // fp16 activations [x_rows x K]
-    uint32_t x_rows;
     uint32_t M;  // dense: token rows
     // grouped
     const uint32_t* slot_experts;
     const uint32_t* unique_count;
     uint32_t max_unique;
     const uint32_t* groups;
-    const uint32_t* source_rows;
     uint32_t routes;
     uint32_t table_cap;  // grouped tile table capacity (entries)
     void* y;
@@ -191,12 +181,12 @@ struct UmmaParams {
 
 // One output tile as every role sees it.
 struct TileInfo {
-    const uint8_t* packed;  // this tile's matrix
-    const uint16_t* scales;
+    const uint16_t* scales;  // this tile's matrix
     const uint16_t* biases;
+    uint32_t expert;  // W tensor-map coordinate
     uint32_t n0, rows_here;
     uint32_t ntok;   // 0: skip
-    uint32_t first;  // dense: first token row; grouped: first grouped row
+    uint32_t first;  // first token row in the fp16 B matrix and the output
 };
 
 template <class Cfg>
@@ -207,15 +197,15 @@ __device__ __forceinline__ TileInfo tile_info(const UmmaParams& p, uint32_t t, u
     ti.n0 = rt * kUmRows;
     ti.rows_here = min(p.N - ti.n0, kUmRows);
     if constexpr (!Cfg::kGathered) {
-        ti.packed = p.packed;
         ti.scales = p.scales;
         ti.biases = p.biases;
+        ti.expert = 0;
         ti.first = jt * Cfg::BN;
         ti.ntok = min(p.M - ti.first, static_cast<uint32_t>(Cfg::BN));
     } else {
         const uint32_t e = table[jt];  // (slot << 8) | token-tile, or kNoSlot
-        ti.packed = nullptr;
         ti.scales = ti.biases = nullptr;
+        ti.expert = 0;
         if (e == kNoSlot) {
             ti.first = 0;
             ti.ntok = 0;
@@ -224,8 +214,8 @@ __device__ __forceinline__ TileInfo tile_info(const UmmaParams& p, uint32_t t, u
             const uint32_t start = p.groups[2 * slot], cnt = p.groups[2 * slot + 1];
             ti.first = start + tok0;
             ti.ntok = min(cnt - tok0, static_cast<uint32_t>(Cfg::BN));
-            const uint8_t* base = p.experts + static_cast<size_t>(p.slot_experts[slot]) * p.expert_bytes;
-            ti.packed = base + p.packed_offset;
+            ti.expert = p.slot_experts[slot];
+            const uint8_t* base = p.experts + static_cast<size_t>(ti.expert) * p.expert_bytes;
             ti.scales = reinterpret_cast<const uint16_t*>(base + p.scales_offset);
             ti.biases = reinterpret_cast<const uint16_t*>(base + p.biases_offset);
         }
@@ -234,19 +224,20 @@ __device__ __forceinline__ TileInfo tile_info(const UmmaParams& p, uint32_t t, u
 }
 
 template <class Cfg, typename YT>
-__global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams p) {
-    constexpr int BN = Cfg::BN, SA = Cfg::SA, SB = Cfg::SB, SW = Cfg::SW, P = Cfg::P;
+__global__ void __launch_bounds__(kUmThreads, 1)
+    q4_umma_kernel(const UmmaParams p, const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w) {
+    constexpr int BN = Cfg::BN, SA = Cfg::SA, SB = Cfg::SB, SW = Cfg::SW;
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t wfull[SW], wfree[SW], sfull[2], sfree[2], afull[SA], aempty[SA], bempty[SB],
-        tfull[2], tempty[2], drain;
+    __shared__ __align__(8) uint64_t wfull[SW], wfree[SW], sfull[2], sfree[2], afull[SA], aempty[SA], bfull[SB],
+        bempty[SB], tfull[2], tempty[2], drain;
     __shared__ uint32_t tmem_base_sh, abort_sh, num_tiles_sh, warp_tot[kUmThreads / 32];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t G = p.K / 64;
-    unsigned char* aring = smem;                      // SA x A tiles
-    unsigned char* bring = aring + SA * Cfg::kA;      // SB x B tiles
-    unsigned char* wring = bring + SB * Cfg::kB;      // SW x [128][32] nibbles
-    unsigned char* sbufs = wring + SW * Cfg::kW;      // 2 x [scales 128 x G | biases 128 x G] bf16
+    const uint32_t G = p.K / 64;       // quantisation groups per row
+    const uint32_t steps = G / 2;      // K steps of two groups
+    unsigned char* bring = smem;                  // SB x B tiles
+    unsigned char* wring = bring + SB * Cfg::kB;  // SW x [128][32] nibbles
+    unsigned char* sbufs = wring + SW * Cfg::kW;  // 2 x [scales 128 x G | biases 128 x G] bf16
     uint32_t* table = reinterpret_cast<uint32_t*>(sbufs + 2 * Cfg::sbuf_bytes(G));
     volatile uint32_t* abort_flag = &abort_sh;
     uint32_t* status = p.status;
@@ -255,20 +246,23 @@ __global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams
 
     if (tid == 0) {
         for (int i = 0; i < SW; ++i) {
-            mbar_init(&wfull[i], 32);  // one cp.async.mbarrier.arrive.noinc per loader lane
-            mbar_init(&wfree[i], 128);
+            mbar_init(&wfull[i], 1);
+            mbar_init(&wfree[i], kDequantThreads);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&sfull[i], 32);
-            mbar_init(&sfree[i], 128);
+            mbar_init(&sfull[i], 1);
+            mbar_init(&sfree[i], kDequantThreads);
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], 128);
         }
         for (int i = 0; i < SA; ++i) {
-            mbar_init(&afull[i], 128);
+            mbar_init(&afull[i], kDequantThreads);
             mbar_init(&aempty[i], 1);
         }
-        for (int i = 0; i < SB; ++i) mbar_init(&bempty[i], 1);
+        for (int i = 0; i < SB; ++i) {
+            mbar_init(&bfull[i], 1);
+            mbar_init(&bempty[i], 1);
+        }
         mbar_init(&drain, 1);
         abort_sh = 0;
         fence_mbar_init();
@@ -324,50 +318,56 @@ __global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams
     const uint32_t num_tiles = num_tiles_sh;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ loader: nibbles, scales
-        const size_t prow = p.K / 2;
-        uint32_t gs = 0, lt = 0;  // global step, local tile
-        bool ok = true;
-        for (uint32_t t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-            const TileInfo ti = tile_info<Cfg>(p, t, row_tiles, table);
-            if (ti.ntok == 0) continue;
-            const int sb = static_cast<int>(lt & 1);
-            if (lt >= 2 && !warp_wait_lazy(&sfree[sb], ((lt >> 1) - 1) & 1, abort_flag, status)) {
-                ok = false;
-                break;
-            }
-            {  // the tile rows' scales and biases (contiguous: rows x G each)
-                unsigned char* sdst = sbufs + sb * Cfg::sbuf_bytes(G);
-                const uint32_t chunks = kUmRows * G / 8, avail = ti.rows_here * G;
-                for (uint32_t q = lane; q < chunks; q += 32) {
-                    const bool in = q * 8 < avail;
-                    const size_t off = static_cast<size_t>(ti.n0) * G + (in ? q * 8 : 0);
-                    cp_async16_zfill(sdst + q * 16, ti.scales + off, in ? 16u : 0u);
-                    cp_async16_zfill(sdst + kUmRows * G * 2 + q * 16, ti.biases + off, in ? 16u : 0u);
-                }
-                cp_async_arrive(&sfull[sb]);
-            }
-            for (uint32_t i = 0; i < G; ++i, ++gs) {
-                const int w = static_cast<int>(gs % SW);
-                if (gs >= static_cast<uint32_t>(SW) &&
-                    !warp_wait_lazy(&wfree[w], ((gs / SW) - 1) & 1, abort_flag, status)) {
+        // ------------------------------------------------------------ loader (lane 0)
+        if (lane == 0) {
+            uint32_t gs = 0, lt = 0;  // global step, local tile
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+                const TileInfo ti = tile_info<Cfg>(p, t, row_tiles, table);
+                if (ti.ntok == 0) continue;
+                const int sb = static_cast<int>(lt & 1);
+                if (lt >= 2 && !wait_or_abort_lazy(&sfree[sb], ((lt >> 1) - 1) & 1, abort_flag, status)) {
                     ok = false;
                     break;
                 }
-                unsigned char* wdst = wring + w * Cfg::kW;
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {  // 128 rows x 2 chunks of nibbles
-                    const uint32_t q = jj * 32 + lane, r = q >> 1, cc = q & 1;
-                    const bool in = r < ti.rows_here;
-                    const uint8_t* src =
-                        ti.packed + (static_cast<size_t>(ti.n0 + (in ? r : 0)) * prow + i * 32 + cc * 16);
-                    cp_async16_zfill(wdst + r * 32 + ((cc ^ ((r >> 2) & 1)) << 4), src, in ? 16u : 0u);
+                {  // the tile rows' scales and biases (contiguous: rows x G each)
+                    unsigned char* sdst = sbufs + sb * Cfg::sbuf_bytes(G);
+                    const uint32_t bytes = ti.rows_here * G * 2;
+                    mbar_arrive_expect_tx(&sfull[sb], 2 * bytes);
+                    bulk_load(sdst, ti.scales + static_cast<size_t>(ti.n0) * G, bytes, &sfull[sb]);
+                    bulk_load(sdst + kUmRows * G * 2, ti.biases + static_cast<size_t>(ti.n0) * G, bytes, &sfull[sb]);
                 }
-                cp_async_arrive(&wfull[w]);
+                for (uint32_t i = 0; i < steps; ++i, ++gs) {
+                    const int w = static_cast<int>(gs % SW), s = static_cast<int>(gs % SB);
+                    if (gs >= static_cast<uint32_t>(SW) &&
+                        !wait_or_abort_lazy(&wfree[w], ((gs / SW) - 1) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&wfull[w], Cfg::kW);
+                    tma_load_3d(wring + w * Cfg::kW, &tm_w, static_cast<int32_t>(i * 64), static_cast<int32_t>(ti.n0),
+                                static_cast<int32_t>(ti.expert), &wfull[w]);
+                    if (gs >= static_cast<uint32_t>(SB) &&
+                        !wait_or_abort_lazy(&bempty[s], ((gs / SB) - 1) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&bfull[s], Cfg::kB);
+                    unsigned char* bdst = bring + s * Cfg::kB;
+                    tma_load_2d(bdst, &tm_x, static_cast<int32_t>(i * 128), static_cast<int32_t>(ti.first), &bfull[s]);
+                    tma_load_2d(bdst + Cfg::kBox, &tm_x, static_cast<int32_t>(i * 128 + 64),
+                                static_cast<int32_t>(ti.first), &bfull[s]);
+                }
+                ++lt;
             }
-            ++lt;
+            if (!ok) {
+                // aborted: give the loads in flight time to land before the
+                // CTA exits (each completes on its own; nothing waits on them)
+                const uint64_t t0 = global_ns();
+                while (global_ns() - t0 < 100000ull) __nanosleep(1000);
+            }
         }
-        cp_async_wait_all();  // no copy outlives the CTA
+        __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issue
         if (lane == 0) {
@@ -384,20 +384,21 @@ __global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams
                 tc_fence_after();
                 const uint32_t idesc = idesc_f16_f32(kUmRows, (ti.ntok + 15u) & ~15u);
                 const uint32_t d = tmem + acc * BN;
-                for (uint32_t i = 0; i < G; ++i, ++gs) {
-                    const int sa = static_cast<int>(gs % SA), sbi = static_cast<int>(gs % SB);
-                    if (!wait_or_abort(&afull[sa], (gs / SA) & 1, abort_flag, status)) {
+                for (uint32_t i = 0; i < steps; ++i, ++gs) {
+                    const int sa = static_cast<int>(gs % SA), s = static_cast<int>(gs % SB);
+                    if (!wait_or_abort(&afull[sa], (gs / SA) & 1, abort_flag, status) ||
+                        !wait_or_abort(&bfull[s], (gs / SB) & 1, abort_flag, status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(aring + sa * Cfg::kA), b0 = smem_u32(bring + sbi * Cfg::kB);
+                    const uint32_t a = tmem + Cfg::kAccCols + sa * Cfg::kACols, b0 = smem_u32(bring + s * Cfg::kB);
 #pragma unroll
-                    for (uint32_t kk = 0; kk < 4; ++kk)
-                        umma_f16(d, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), idesc,
-                                 (i | kk) != 0u);
+                    for (uint32_t kk = 0; kk < 8; ++kk)
+                        umma_f16_ts(d, a + kk * 8, sw128_kmajor_desc(b0 + (kk >> 2) * Cfg::kBox + (kk & 3) * 32),
+                                    idesc, (i | kk) != 0u);
                     umma_commit(&aempty[sa]);
-                    umma_commit(&bempty[sbi]);
+                    umma_commit(&bempty[s]);
                 }
                 if (!ok) break;
                 umma_commit(&tfull[acc]);
@@ -412,118 +413,63 @@ __global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams
             }
         }
         __syncwarp();
-    } else if (warp < 6) {
-        // ------------------------------------------------------------ dequant + token rows
-        const uint32_t dq = static_cast<uint32_t>(tid - 64);  // 0..127
-        const uint32_t r = 32u * (warp & 3) + lane;          // weight row of this thread
-        const uint32_t wsw = ((r >> 2) & 1) << 4;
-        const uint32_t bc = dq & 7, bj = dq >> 3;  // B copies: chunk bc of token rows bj + 16u
-        // B cursor: runs P steps ahead over the same tile sequence
-        uint32_t bt = blockIdx.x, bi = 0, bgs = 0;
-        TileInfo bti{};
-        uint32_t brows[Cfg::kBRows];
-        auto b_seek = [&]() {  // first tile with tokens at or after bt
-            for (; bt < num_tiles; bt += gridDim.x) {
-                bti = tile_info<Cfg>(p, bt, row_tiles, table);
-                if (bti.ntok) break;
-            }
-            if (bt >= num_tiles) return;
-#pragma unroll
-            for (int u = 0; u < Cfg::kBRows; ++u) {
-                const uint32_t j = bj + 16u * u;
-                uint32_t row = 0;
-                if (j < bti.ntok) {
-                    if constexpr (Cfg::kGathered) {
-                        row = __ldg(p.source_rows + bti.first + j);
-                        if (row >= p.x_rows) {
-                            if (status) atomicOr(status, PBMOE_DEV_ERR_EXPERT_ID);
-                            row = 0;
-                        }
-                    } else {
-                        row = bti.first + j;
-                    }
-                }
-                brows[u] = row;
-            }
-        };
-        bool ok = true;
-        auto b_issue = [&]() {  // token rows of global step bgs, then advance; always one commit group
-            if (ok && bt < num_tiles) {
-                const int slot = static_cast<int>(bgs % SB);
-                if (bgs >= static_cast<uint32_t>(SB) &&
-                    !warp_wait_or_abort(&bempty[slot], ((bgs / SB) - 1) & 1, abort_flag, status)) {
-                    ok = false;
-                } else {
-                    unsigned char* bdst = bring + slot * Cfg::kB;
-#pragma unroll
-                    for (int u = 0; u < Cfg::kBRows; ++u) {
-                        const uint32_t j = bj + 16u * u;
-                        if (j < bti.ntok)
-                            cp_async16(bdst + sw128_offset(j, bc),
-                                       p.x16 + static_cast<size_t>(brows[u]) * p.K + bi * 64 + bc * 8);
-                    }
-                    ++bgs;
-                    if (++bi == G) {
-                        bi = 0;
-                        bt += gridDim.x;
-                        b_seek();
-                    }
-                }
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-        };
-        b_seek();
-        for (int k = 0; k < P; ++k) b_issue();
-
+    } else if (warp < 10) {
+        // ------------------------------------------------------------ dequant into TMEM
+        const uint32_t q = warp & 3, r = 32u * q + lane;  // weight row = TMEM lane
+        const uint32_t h = static_cast<uint32_t>(warp - 2) >> 2;  // group of the step (0, 1)
+        // 64-byte swizzle of the nibble rows: 16-byte chunk c of row r at c ^ ((r >> 1) & 3)
+        const uint32_t wc0 = ((2 * h) ^ ((r >> 1) & 3)) << 4, wc1 = ((2 * h + 1) ^ ((r >> 1) & 3)) << 4;
+        const uint32_t a_lane = tmem + ((32u * q) << 16) + Cfg::kAccCols + 32 * h;
         uint32_t gs = 0, lt = 0;
+        bool ok = true;
         for (uint32_t t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
             const TileInfo ti = tile_info<Cfg>(p, t, row_tiles, table);
             if (ti.ntok == 0) continue;
             const int sbuf = static_cast<int>(lt & 1);
-            if (!warp_wait_or_abort(&sfull[sbuf], (lt >> 1) & 1, abort_flag, status)) {
+            if (!warp_wait<false>(&sfull[sbuf], (lt >> 1) & 1, abort_flag, status)) {
                 ok = false;
                 break;
             }
+            // rows beyond the matrix (ragged N) dequantise with scale and bias 0
+            const bool rok = r < ti.rows_here;
             const uint16_t* srow = reinterpret_cast<const uint16_t*>(sbufs + sbuf * Cfg::sbuf_bytes(G)) + r * G;
             const uint16_t* brow = srow + kUmRows * G;
             uint4 sq = make_uint4(0, 0, 0, 0), bq = sq;
-            for (uint32_t i = 0; i < G; ++i, ++gs) {
-                b_issue();  // step gs + P
-                asm volatile("cp.async.wait_group %0;" ::"n"(P) : "memory");  // this thread's rows of step gs
-                if ((i & 7) == 0) {
-                    sq = *reinterpret_cast<const uint4*>(srow + i);
-                    bq = *reinterpret_cast<const uint4*>(brow + i);
+            for (uint32_t i = 0; i < steps; ++i, ++gs) {
+                if ((i & 3) == 0 && rok) {  // groups 2i .. 2i+7
+                    sq = *reinterpret_cast<const uint4*>(srow + 2 * i);
+                    bq = *reinterpret_cast<const uint4*>(brow + 2 * i);
                 }
                 const int w = static_cast<int>(gs % SW), sa = static_cast<int>(gs % SA);
-                if (!ok || !warp_wait_or_abort(&wfull[w], (gs / SW) & 1, abort_flag, status) ||
+                if (!warp_wait<false>(&wfull[w], (gs / SW) & 1, abort_flag, status) ||
                     (gs >= static_cast<uint32_t>(SA) &&
-                     !warp_wait_or_abort(&aempty[sa], ((gs / SA) - 1) & 1, abort_flag, status))) {
+                     !warp_wait<false>(&aempty[sa], ((gs / SA) - 1) & 1, abort_flag, status))) {
                     ok = false;
                     break;
                 }
-                // this step's scale and bias: half (i & 1) of word (i & 7) / 2
-                const uint32_t sw = (i & 4) ? ((i & 2) ? sq.w : sq.z) : ((i & 2) ? sq.y : sq.x);
-                const uint32_t bw = (i & 4) ? ((i & 2) ? bq.w : bq.z) : ((i & 2) ? bq.y : bq.x);
-                const uint32_t s16 = f16_of_bf16((i & 1) ? (sw >> 16) : (sw & 0xffffu));
-                const uint32_t b16 = f16_of_bf16((i & 1) ? (bw >> 16) : (bw & 0xffffu));
+                // group 2i + h: half h of word i & 3 of the eight cached groups
+                const uint32_t sw = (i & 2) ? ((i & 1) ? sq.w : sq.z) : ((i & 1) ? sq.y : sq.x);
+                const uint32_t bw = (i & 2) ? ((i & 1) ? bq.w : bq.z) : ((i & 1) ? bq.y : bq.x);
+                const uint32_t s16 = f16_of_bf16(h ? (sw >> 16) : (sw & 0xffffu));
+                const uint32_t b16 = f16_of_bf16(h ? (bw >> 16) : (bw & 0xffffu));
                 const uint32_t s2 = s16 * 0x10001u, b2 = b16 * 0x10001u;
-                const unsigned char* wr = wring + w * Cfg::kW + r * 32;
-                const uint4 w0 = *reinterpret_cast<const uint4*>(wr + wsw);
-                const uint4 w1 = *reinterpret_cast<const uint4*>(wr + (16 ^ wsw));
+                const unsigned char* wr = wring + w * Cfg::kW + r * 64;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(wr + wc0);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(wr + wc1);
                 mbar_arrive(&wfree[w]);  // nibbles are in registers
-                unsigned char* arow = aring + sa * Cfg::kA;
                 const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                uint32_t v[32];
 #pragma unroll
-                for (uint32_t jj = 0; jj < 8; ++jj)
-                    *reinterpret_cast<uint4*>(arow + sw128_offset(r, jj)) = dequant_word_f16(words[jj], s2, b2);
-                fence_proxy_async_smem();  // A stores and the landed token rows, for the tensor core
+                for (int jj = 0; jj < 8; ++jj) dequant_word_f16(words[jj], s2, b2, v + 4 * jj);
+                tc_fence_after();  // after the aempty wait: the MMA reading this slot is done
+                tmem_st32_wait(a_lane + sa * Cfg::kACols, v);
+                tc_fence_before();
                 mbar_arrive(&afull[sa]);
             }
             if (!ok) break;
             mbar_arrive(&sfree[sbuf]);
             ++lt;
         }
-        cp_async_wait_all();  // no copy outlives the CTA
     } else {
         // ------------------------------------------------------------ epilogue
         const uint32_t q = warp & 3, r = 32u * q + lane;
@@ -533,7 +479,7 @@ __global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams
             const TileInfo ti = tile_info<Cfg>(p, t, row_tiles, table);
             if (ti.ntok == 0) continue;
             const int acc = static_cast<int>(lt & 1);
-            if (!warp_wait_lazy(&tfull[acc], (lt >> 1) & 1, abort_flag, status)) break;
+            if (!warp_wait<true>(&tfull[acc], (lt >> 1) & 1, abort_flag, status)) break;
             tc_fence_after();
             const uint32_t taddr = tmem + (acc * BN) + ((32u * q) << 16);
             const bool rok = r < ti.rows_here;
@@ -562,13 +508,31 @@ __global__ void __launch_bounds__(kUmThreads, 1) q4_umma_kernel(const UmmaParams
     }
 }
 
-// bf16 -> fp16, eight values per thread step; latches PBMOE_DEV_ERR_F16_RANGE
-// for a magnitude >= 65536 or a non-finite value.
-__global__ void __launch_bounds__(256) x16_convert_kernel(const uint4* __restrict__ x, uint4* __restrict__ x16,
-                                                          size_t n8, uint32_t* status) {
+// fp16 rows for the tensor cores: out[j] = x[rows ? rows[j] : j] (bf16 or fp16
+// in, K elements per row), eight values per thread step. A source row >= x_rows
+// latches PBMOE_DEV_ERR_EXPERT_ID (written as zeros); a bf16 value of magnitude
+// >= 65536 or non-finite latches PBMOE_DEV_ERR_F16_RANGE.
+__global__ void __launch_bounds__(256) x16_gather_kernel(const uint4* __restrict__ x, int x_is_f16,
+                                                         const uint32_t* __restrict__ rows, uint32_t nrows,
+                                                         uint32_t x_rows, uint32_t K, uint4* __restrict__ out,
+                                                         uint32_t* status) {
+    const uint32_t per_row = K / 8;
+    const size_t n8 = size_t(nrows) * per_row;
     uint32_t mx = 0;
+    bool bad = false;
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n8; i += size_t(gridDim.x) * blockDim.x) {
-        const uint4 v = __ldg(x + i);
+        const uint32_t j = static_cast<uint32_t>(i / per_row), c = static_cast<uint32_t>(i % per_row);
+        const uint32_t src = rows ? __ldg(rows + j) : j;
+        if (src >= x_rows) {
+            bad = true;
+            out[i] = make_uint4(0, 0, 0, 0);
+            continue;
+        }
+        const uint4 v = __ldg(x + size_t(src) * per_row + c);
+        if (x_is_f16) {
+            out[i] = v;
+            continue;
+        }
         mx = __vmaxu2(mx, __vmaxu2(__vmaxu2(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu),
                                    __vmaxu2(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu)));
         uint32_t o[4];
@@ -578,69 +542,93 @@ __global__ void __launch_bounds__(256) x16_convert_kernel(const uint4* __restric
             asm("cvt.rn.f16x2.f32 %0, %1, %2;"
                 : "=r"(o[k])
                 : "f"(__uint_as_float(in[k] & 0xffff0000u)), "f"(__uint_as_float(in[k] << 16)));
-        x16[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        out[i] = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    if (((mx & 0xffffu) >= 0x4780u || (mx >> 16) >= 0x4780u) && status) atomicOr(status, PBMOE_DEV_ERR_F16_RANGE);
-}
-
-static int g_num_sms = 0;
-
-static int num_sms() {
-    if (g_num_sms == 0) {
-        int dev = 0, n = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
-                                                      cudaSuccess)
-            g_num_sms = n;
-        else
-            g_num_sms = 148;
+    if (status) {
+        if ((mx & 0xffffu) >= 0x4780u || (mx >> 16) >= 0x4780u) atomicOr(status, PBMOE_DEV_ERR_F16_RANGE);
+        if (bad) atomicOr(status, PBMOE_DEV_ERR_EXPERT_ID);
     }
-    return g_num_sms;
 }
 
-bool q4_gemm_supported(uint32_t N, uint32_t K, uint32_t group) {
-    return group == 64 && K % 512 == 0 && N > 0 && DenseCfg::smem(K / 64, 0) <= 227 * 1024;
+// ---------------------------------------------------------------- host side
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
 }
 
-bool q4_grouped_supported(uint32_t N, uint32_t K, uint32_t group, uint32_t routes, uint32_t max_unique) {
-    return q4_gemm_supported(N, K, group) &&
-           GroupedCfg::smem(K / 64, q4_grouped_tile_bound(routes, max_unique)) <= 227 * 1024;
+// fp16 token matrix [rows x K], box 64 k x box_rows rows, 128-byte swizzle.
+cudaError_t make_x_map(CUtensorMap* m, const void* x16, uint32_t rows, uint32_t K, uint32_t box_rows) {
+    EncodeTiledFn f = encode_fn();
+    if (!f) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x16), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+               ? cudaSuccess
+               : cudaErrorInvalidValue;
+}
+
+// Nibble matrices [experts][N rows][K/2 bytes] (experts `stride` bytes apart),
+// box 64 bytes (two groups) x 128 rows x 1, 64-byte swizzle.
+cudaError_t make_w_map(CUtensorMap* m, const void* packed, uint32_t N, uint32_t K, uint32_t experts,
+                       uint64_t stride) {
+    EncodeTiledFn f = encode_fn();
+    if (!f) return cudaErrorNotSupported;
+    const cuuint64_t dims[3] = {K / 2, N, experts};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K / 2), experts > 1 ? stride : uint64_t(K / 2) * N};
+    const cuuint32_t box[3] = {64, kUmRows, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return f(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(packed), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+               ? cudaSuccess
+               : cudaErrorInvalidValue;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0, v = 0;
+        n = (cudaGetDevice(&dev) == cudaSuccess &&
+             cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+                ? v
+                : 148;
+    }
+    return n;
 }
 
 template <class Cfg, typename YT>
-static cudaError_t launch_umma(const UmmaParams& p, uint32_t tiles, size_t smem, cudaStream_t s) {
+cudaError_t launch_umma(const UmmaParams& p, const CUtensorMap& tx, const CUtensorMap& tw, uint32_t tiles,
+                        size_t smem, cudaStream_t s) {
     auto k = q4_umma_kernel<Cfg, YT>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const uint32_t grid = std::max<uint32_t>(1u, std::min<uint32_t>(tiles, static_cast<uint32_t>(num_sms())));
-    k<<<grid, kUmThreads, smem, s>>>(p);
+    k<<<grid, kUmThreads, smem, s>>>(p, tx, tw);
     return cudaGetLastError();
 }
 
-cudaError_t x16_convert_launch(const void* x, void* x16, size_t elems, uint32_t* status, cudaStream_t s) {
-    const size_t n8 = elems / 8;
-    if (n8 == 0) return cudaSuccess;
-    const unsigned grid = static_cast<unsigned>(std::min<size_t>((n8 + 255) / 256, 148 * 8));
-    x16_convert_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(x), static_cast<uint4*>(x16), n8, status);
-    return cudaGetLastError();
-}
+}  // namespace
 
-cudaError_t q4_gemm_launch(const Q4GemmArgs& a, cudaStream_t s) {
-    UmmaParams p{};
-    p.packed = a.packed;
-    p.scales = a.scales;
-    p.biases = a.biases;
-    p.N = a.rows;
-    p.K = a.cols;
-    p.num_experts = 1;
-    p.x16 = static_cast<const uint16_t*>(a.x16);
-    p.x_rows = a.m;
-    p.M = a.m;
-    p.y = a.y;
-    p.status = a.status;
-    const uint32_t tiles = ((a.rows + kUmRows - 1) / kUmRows) * ((a.m + DenseCfg::BN - 1) / DenseCfg::BN);
-    const size_t smem = DenseCfg::smem(a.cols / 64, 0);
-    return a.y_dtype == PBMOE_F32 ? launch_umma<DenseCfg, float>(p, tiles, smem, s)
-                                  : launch_umma<DenseCfg, uint16_t>(p, tiles, smem, s);
+bool q4_gemm_supported(uint32_t N, uint32_t K, uint32_t group) {
+    return group == 64 && K % 512 == 0 && N > 0 && DenseCfg::smem(K / 64, 0) <= 227 * 1024;
 }
 
 uint32_t q4_grouped_tile_bound(uint32_t routes, uint32_t max_unique) {
@@ -648,31 +636,68 @@ uint32_t q4_grouped_tile_bound(uint32_t routes, uint32_t max_unique) {
     return (routes + GroupedCfg::BN - 1) / GroupedCfg::BN + max_unique;
 }
 
+bool q4_grouped_supported(uint32_t N, uint32_t K, uint32_t group, uint32_t routes, uint32_t max_unique) {
+    return q4_gemm_supported(N, K, group) &&
+           GroupedCfg::smem(K / 64, q4_grouped_tile_bound(routes, max_unique)) <= 227 * 1024;
+}
+
+cudaError_t x16_gather_launch(const void* x, bool x_is_f16, const uint32_t* rows, uint32_t nrows, uint32_t x_rows,
+                              uint32_t K, void* out, uint32_t* status, cudaStream_t s) {
+    const size_t n8 = size_t(nrows) * (K / 8);
+    if (n8 == 0) return cudaSuccess;
+    const unsigned grid = static_cast<unsigned>(std::min<size_t>((n8 + 255) / 256, 148 * 8));
+    x16_gather_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(x), x_is_f16 ? 1 : 0, rows, nrows, x_rows, K,
+                                           static_cast<uint4*>(out), status);
+    return cudaGetLastError();
+}
+
+cudaError_t q4_gemm_launch(const Q4GemmArgs& a, cudaStream_t s) {
+    UmmaParams p{};
+    p.scales = a.scales;
+    p.biases = a.biases;
+    p.N = a.rows;
+    p.K = a.cols;
+    p.num_experts = 1;
+    p.M = a.m;
+    p.y = a.y;
+    p.status = a.status;
+    CUtensorMap tx, tw;
+    cudaError_t e;
+    if ((e = make_x_map(&tx, a.x16, a.m, a.cols, DenseCfg::BN)) != cudaSuccess) return e;
+    if ((e = make_w_map(&tw, a.packed, a.rows, a.cols, 1, 0)) != cudaSuccess) return e;
+    const uint32_t tiles = ((a.rows + kUmRows - 1) / kUmRows) * ((a.m + DenseCfg::BN - 1) / DenseCfg::BN);
+    const size_t smem = DenseCfg::smem(a.cols / 64, 0);
+    return a.y_dtype == PBMOE_F32 ? launch_umma<DenseCfg, float>(p, tx, tw, tiles, smem, s)
+                                  : launch_umma<DenseCfg, uint16_t>(p, tx, tw, tiles, smem, s);
+}
+
 cudaError_t q4_gemm_grouped_launch(const Q4GroupedArgs& a, cudaStream_t s) {
     UmmaParams p{};
     p.experts = a.experts;
     p.expert_bytes = a.expert_bytes;
-    p.packed_offset = a.packed_offset;
     p.scales_offset = a.scales_offset;
     p.biases_offset = a.biases_offset;
     p.N = a.rows;
     p.K = a.cols;
     p.num_experts = a.num_experts;
-    p.x16 = static_cast<const uint16_t*>(a.x16);
-    p.x_rows = a.x_rows;
     p.slot_experts = a.slot_experts;
     p.unique_count = a.unique_count;
     p.max_unique = a.max_unique;
     p.groups = a.groups;
-    p.source_rows = a.source_rows;
     p.routes = a.routes;
     p.table_cap = q4_grouped_tile_bound(a.routes, a.max_unique);
     p.y = a.y;
     p.status = a.status;
+    CUtensorMap tx, tw;
+    cudaError_t e;
+    if ((e = make_x_map(&tx, a.xg16, a.routes, a.cols, GroupedCfg::BN)) != cudaSuccess) return e;
+    if ((e = make_w_map(&tw, a.experts + a.packed_offset, a.rows, a.cols, a.num_experts, a.expert_bytes)) !=
+        cudaSuccess)
+        return e;
     const uint32_t tiles = ((a.rows + kUmRows - 1) / kUmRows) * p.table_cap;
     const size_t smem = GroupedCfg::smem(a.cols / 64, p.table_cap);
-    return a.y_dtype == PBMOE_F32 ? launch_umma<GroupedCfg, float>(p, tiles, smem, s)
-                                  : launch_umma<GroupedCfg, uint16_t>(p, tiles, smem, s);
+    return a.y_dtype == PBMOE_F32 ? launch_umma<GroupedCfg, float>(p, tx, tw, tiles, smem, s)
+                                  : launch_umma<GroupedCfg, uint16_t>(p, tx, tw, tiles, smem, s);
 }
 
 }  // namespace pbmoe

@@ -24,7 +24,7 @@ def ctx():
 
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     c = capi.Context(0)
-    c.prefill_reserve(4096, 2048)
+    c.prefill_reserve(20480, 2048)
     yield c
     c.close()
 
@@ -46,7 +46,7 @@ def _gemm(ctx, packed, s, b, n, k, x, out_dtype):
 
 @pytest.mark.parametrize("m,n,k", [
     (1, 128, 512), (5, 200, 512), (130, 257, 1024), (128, 128, 2048), (300, 512, 512), (17, 1000, 1536),
-    (520, 384, 4096), (129, 5, 512),
+    (520, 384, 3072), (129, 5, 512),
 ])
 @pytest.mark.parametrize("out", ["bf16", "f32"])
 def test_dense_gemm_shapes(ctx, oracle, m, n, k, out):
