@@ -28,7 +28,8 @@
 //               group of the step: each thread takes its row's 64 weights of
 //               that group, w = q*s + b to fp16 (one rounding), 32 packed
 //               columns written straight into the step's A slot in TMEM
-//               (tcgen05.st), then arrives on afull. A never touches shared
+//               (tcgen05.st); lane 0 arrives on afull for the warp (mbarrier
+//               arrivals are one per warp throughout). A never touches shared
 //               memory, so no proxy fence is needed between the dequant and
 //               the MMA.
 //   warps 10-13 epilogue: tcgen05.ld of the finished accumulator (double-
@@ -64,7 +65,8 @@
 namespace pbmoe {
 
 constexpr int kUmThreads = 448;  // loader, MMA, 8 dequant, 4 epilogue warps
-constexpr uint32_t kDequantThreads = 256;
+constexpr uint32_t kDequantWarps = 8;
+constexpr uint32_t kEpilogueWarps = 4;
 constexpr uint32_t kUmRows = 128;
 constexpr uint32_t kMagicPair = 0x54006400u;  // f16x2 (lo 1024.0, hi 64.0)
 constexpr uint32_t kNoSlot = 0xffffffffu;
@@ -247,16 +249,16 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     if (tid == 0) {
         for (int i = 0; i < SW; ++i) {
             mbar_init(&wfull[i], 1);
-            mbar_init(&wfree[i], kDequantThreads);
+            mbar_init(&wfree[i], kDequantWarps);  // one arrival per warp (lane 0 after __syncwarp)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sfull[i], 1);
-            mbar_init(&sfree[i], kDequantThreads);
+            mbar_init(&sfree[i], kDequantWarps);
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 128);
+            mbar_init(&tempty[i], kEpilogueWarps);
         }
         for (int i = 0; i < SA; ++i) {
-            mbar_init(&afull[i], kDequantThreads);
+            mbar_init(&afull[i], kDequantWarps);
             mbar_init(&aempty[i], 1);
         }
         for (int i = 0; i < SB; ++i) {
@@ -456,7 +458,8 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 const unsigned char* wr = wring + w * Cfg::kW + r * 64;
                 const uint4 w0 = *reinterpret_cast<const uint4*>(wr + wc0);
                 const uint4 w1 = *reinterpret_cast<const uint4*>(wr + wc1);
-                mbar_arrive(&wfree[w]);  // nibbles are in registers
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wfree[w]);  // the warp's nibbles are in registers
                 const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
                 uint32_t v[32];
 #pragma unroll
@@ -464,10 +467,12 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 tc_fence_after();  // after the aempty wait: the MMA reading this slot is done
                 tmem_st32_wait(a_lane + sa * Cfg::kACols, v);
                 tc_fence_before();
-                mbar_arrive(&afull[sa]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[sa]);
             }
             if (!ok) break;
-            mbar_arrive(&sfree[sbuf]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sfree[sbuf]);
             ++lt;
         }
     } else {
@@ -496,7 +501,8 @@ __global__ void __launch_bounds__(kUmThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
             ++lt;
         }
     }
