@@ -344,6 +344,59 @@ PBMOE_API int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix
                                     const void* x, pbmoe_dtype x_dtype, uint32_t x_rows, void* y,
                                     pbmoe_dtype y_dtype, void* stream);
 
+/* ---------------------------------------------------------------- expert parallelism */
+
+/* The reference runs on one device (no expert parallelism); this extends its
+ * decode layer (encode_expert_phase, metal/mod.rs:4289-4470, and the combine
+ * combine_expert_phase, shaders.metal:1723-1741) to experts sharded over
+ * `world` GPUs of one node. Activations, router and shared expert are
+ * replicated, so dispatch is local: every rank routes every token
+ * (deterministically, identically) and runs the routes of its own experts;
+ * the combine sums the ranks' partial outputs over NVLink peer memory in a
+ * one-shot exchange (no multicast, bounded waits). */
+
+/* Rank r of `world` owns experts [floor(r*E/world), floor((r+1)*E/world)).
+ * Host-only. */
+PBMOE_API int pbmoe_ep_expert_range(uint32_t num_experts, uint32_t rank, uint32_t world, uint32_t* begin,
+                                    uint32_t* count);
+
+#define PBMOE_EP_HANDLE_BYTES 64
+
+/* Allocate this rank's exchange buffer (receive slots of every rank's partial
+ * outputs for up to max_tokens tokens of `hidden` values, double-buffered,
+ * plus epoch flags), zeroed. world <= 8. */
+PBMOE_API int pbmoe_ep_reserve(pbmoe_ctx* ctx, uint32_t rank, uint32_t world, uint32_t max_tokens, uint32_t hidden);
+/* The exchange buffer's CUDA IPC handle (PBMOE_EP_HANDLE_BYTES bytes) for the
+ * other ranks' processes. */
+PBMOE_API int pbmoe_ep_ipc_handle(pbmoe_ctx* ctx, void* handle);
+/* Map every rank's exchange buffer: `handles` holds world handles in rank
+ * order (this rank's own entry is ignored). */
+PBMOE_API int pbmoe_ep_open_peers(pbmoe_ctx* ctx, const void* handles);
+/* Same, for ranks driven from one process: device pointers of every rank's
+ * exchange buffer in rank order (peer access already enabled by the caller;
+ * NULL entries are left unmapped). */
+PBMOE_API int pbmoe_ep_set_peers(pbmoe_ctx* ctx, void* const* buffers);
+/* This rank's exchange buffer (device pointer), for pbmoe_ep_set_peers. */
+PBMOE_API void* pbmoe_ep_buffer(pbmoe_ctx* ctx);
+
+typedef struct pbmoe_ep_shard {
+    uint32_t expert_begin; /* first expert id this rank owns                  */
+    uint32_t expert_count; /* experts owned (weights->experts holds exactly   */
+                           /* these slots, expert_begin first)                */
+    uint32_t timeout_us;   /* bound of the wait for peers (0 = 2 s)           */
+} pbmoe_ep_shard;
+
+/* One MoE decode layer, expert-parallel. Every rank calls it with the same
+ * inputs in the same order. weights->experts is this rank's shard;
+ * weights->shared_expert (and its gate) is given on exactly one rank. Output
+ * (and next_normed) is the full layer, identical on every rank. A peer that
+ * does not arrive within the timeout latches PBMOE_DEV_ERR_PEER_TIMEOUT
+ * (pbmoe_device_status) and its partial counts as zero. */
+PBMOE_API int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
+                                 const pbmoe_ep_shard* shard, const void* x, pbmoe_dtype x_dtype, const void* residual,
+                                 void* out, pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
+                                 void* next_normed, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -42,7 +42,11 @@ EXPORTED = [
     "pbmoe_moe_workspace_bytes", "pbmoe_device_status", "pbmoe_fixed_q4_layout", "pbmoe_q4_matvec",
     "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static", "pbmoe_mla_reserve", "pbmoe_mla_decode",
     "pbmoe_prefill_reserve", "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
+    "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
+    "pbmoe_ep_buffer", "pbmoe_ep_moe_layer",
 ]
+
+EP_HANDLE_BYTES = 64
 
 
 class Q4Tensor(C.Structure):
@@ -87,6 +91,10 @@ class Q4ExpertMatrix(C.Structure):
                 ("rows", C.c_uint32), ("cols", C.c_uint32), ("group_size", C.c_uint32)]
 
 
+class EpShard(C.Structure):
+    _fields_ = [("expert_begin", C.c_uint32), ("expert_count", C.c_uint32), ("timeout_us", C.c_uint32)]
+
+
 class PbmoeError(RuntimeError):
     def __init__(self, code, message):
         super().__init__(f"pbmoe status {code}: {message}")
@@ -127,6 +135,15 @@ def load():
         L.pbmoe_prefill_group_plan.argtypes = [vp, vp, u32, u32, u32, vp, vp, vp, vp, vp, vp, vp]
         L.pbmoe_q4_gemm_grouped.argtypes = [vp, C.POINTER(Q4ExpertMatrix), vp, vp, vp, vp, u32, u32, vp, i32, u32,
                                             vp, i32, vp]
+        L.pbmoe_ep_expert_range.argtypes = [u32, u32, u32, C.POINTER(u32), C.POINTER(u32)]
+        L.pbmoe_ep_reserve.argtypes = [vp, u32, u32, u32, u32]
+        L.pbmoe_ep_ipc_handle.argtypes = [vp, vp]
+        L.pbmoe_ep_open_peers.argtypes = [vp, vp]
+        L.pbmoe_ep_set_peers.argtypes = [vp, vp]
+        L.pbmoe_ep_buffer.restype = vp
+        L.pbmoe_ep_buffer.argtypes = [vp]
+        L.pbmoe_ep_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), C.POINTER(EpShard), vp, i32,
+                                         vp, vp, i32, u32, vp, vp, vp]
         _lib = L
     return _lib
 
@@ -141,6 +158,13 @@ def fixed_q4_layout(hidden, intermediate, group):
 
 def _ptr(t):
     return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _same_dtype(out, *others):
+    """residual / next_normed travel in the output's dtype (the C-ABI cannot see it)."""
+    for t in others:
+        if t is not None and t.dtype != out.dtype:
+            raise TypeError(f"expected {out.dtype} like the output, got {t.dtype}")
 
 
 def _dtype_code(t):
@@ -206,6 +230,7 @@ class Context:
 
     def moe_layer(self, config, weights: MoeWeights, x, out, tokens, residual=None, next_norm_weight=None,
                   next_normed=None, debug: MoeDebug | None = None, stream=None):
+        _same_dtype(out, residual, next_normed)
         self.check(self.lib.pbmoe_moe_layer(
             self.h, C.byref(config), C.byref(weights), _ptr(x), _dtype_code(x), _ptr(residual), _ptr(out),
             _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed),
@@ -246,6 +271,34 @@ class Context:
             routes, max_unique, _ptr(x), _dtype_code(x), int(x.shape[0]), _ptr(y), _dtype_code(y),
             self.stream_ptr(stream)))
 
+    # ---------------------------------------------------------- expert parallelism
+    def ep_reserve(self, rank, world, max_tokens, hidden):
+        self.check(self.lib.pbmoe_ep_reserve(self.h, rank, world, max_tokens, hidden))
+
+    def ep_ipc_handle(self) -> bytes:
+        buf = (C.c_char * EP_HANDLE_BYTES)()
+        self.check(self.lib.pbmoe_ep_ipc_handle(self.h, C.cast(buf, C.c_void_p)))
+        return bytes(buf)
+
+    def ep_open_peers(self, handles):
+        blob = b"".join(handles)
+        buf = (C.c_char * len(blob)).from_buffer_copy(blob)
+        self.check(self.lib.pbmoe_ep_open_peers(self.h, C.cast(buf, C.c_void_p)))
+
+    def ep_buffer(self) -> int:
+        return self.lib.pbmoe_ep_buffer(self.h) or 0
+
+    def ep_set_peers(self, pointers):
+        arr = (C.c_void_p * len(pointers))(*pointers)
+        self.check(self.lib.pbmoe_ep_set_peers(self.h, C.cast(arr, C.c_void_p)))
+
+    def ep_moe_layer(self, config, weights: MoeWeights, shard: EpShard, x, out, tokens, residual=None,
+                     next_norm_weight=None, next_normed=None, stream=None):
+        _same_dtype(out, residual, next_normed)
+        self.check(self.lib.pbmoe_ep_moe_layer(
+            self.h, C.byref(config), C.byref(weights), C.byref(shard), _ptr(x), _dtype_code(x), _ptr(residual),
+            _ptr(out), _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed), self.stream_ptr(stream)))
+
     def device_status(self, clear=True, stream=None) -> int:
         v = C.c_uint32()
         self.check(self.lib.pbmoe_device_status(self.h, self.stream_ptr(stream), C.byref(v), 1 if clear else 0))
@@ -268,3 +321,12 @@ def expert_matrix(experts, layout: ExpertLayout, num_experts, projection) -> Q4E
 
 def moe_config(layout: ExpertLayout, num_experts, top_k, normalization=0, routed_scale=1.0, eps=1e-6) -> MoeConfig:
     return MoeConfig(layout, num_experts, top_k, normalization, routed_scale, eps)
+
+
+def ep_expert_range(num_experts, rank, world):
+    """(begin, count) of the experts rank `rank` of `world` owns (host-only)."""
+    b, n = C.c_uint32(), C.c_uint32()
+    rc = load().pbmoe_ep_expert_range(num_experts, rank, world, C.byref(b), C.byref(n))
+    if rc != PBMOE_OK:
+        raise PbmoeError(rc, f"invalid expert partition E={num_experts} rank={rank} world={world}")
+    return b.value, n.value

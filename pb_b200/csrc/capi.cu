@@ -22,6 +22,11 @@ struct pbmoe_ctx {
     uint32_t mla_batch = 0;
     void* x16_base = nullptr;  // prefill fp16 activation image
     size_t x16_elems = 0;
+    void* ep_base = nullptr;  // expert-parallel exchange buffer
+    size_t ep_bytes = 0;
+    uint32_t ep_rank = 0, ep_world = 0, ep_max_tokens = 0, ep_hidden = 0, ep_epoch = 0;
+    void* ep_peer[pbmoe::kMaxEpRanks] = {};
+    bool ep_peer_ipc[pbmoe::kMaxEpRanks] = {};  // mapped through CUDA IPC (closed at destroy)
     int num_sms = 0;
     std::string last_error;
 };
@@ -212,6 +217,9 @@ int pbmoe_destroy(pbmoe_ctx* ctx) {
         if (ctx->ws_base) cudaFree(ctx->ws_base);
         if (ctx->mla_base) cudaFree(ctx->mla_base);
         if (ctx->x16_base) cudaFree(ctx->x16_base);
+        for (uint32_t r = 0; r < pbmoe::kMaxEpRanks; ++r)
+            if (ctx->ep_peer_ipc[r]) cudaIpcCloseMemHandle(ctx->ep_peer[r]);
+        if (ctx->ep_base) cudaFree(ctx->ep_base);
         if (ctx->status) cudaFree(ctx->status);
     }
     delete ctx;
@@ -333,9 +341,13 @@ int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint3
     return PBMOE_OK;
 }
 
-int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w, const void* x,
-                    pbmoe_dtype x_dtype, const void* residual, void* out, pbmoe_dtype out_dtype, uint32_t tokens,
-                    const float* next_norm_weight, void* next_normed, const pbmoe_moe_debug* debug, void* stream) {
+namespace {
+// One decode layer; with `ep` set, the experts of [e_lo, e_lo + e_count) only
+// and the expert-parallel combine.
+int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w, const void* x,
+                   pbmoe_dtype x_dtype, const void* residual, void* out, pbmoe_dtype out_dtype, uint32_t tokens,
+                   const float* next_norm_weight, void* next_normed, const pbmoe_moe_debug* debug, void* stream,
+                   uint32_t e_lo, uint32_t e_count, const pbmoe::EpPeers* ep) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
     int rc = check_moe_config(ctx, c);
     if (rc) return rc;
@@ -390,6 +402,9 @@ int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_w
     a.shared_slot = w->shared_expert;
     a.pdl = true;
     a.phase_events = debug ? debug->phase_events : nullptr;
+    a.expert_lo = e_lo;
+    a.expert_count = e_count;
+    a.ep = ep;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = moe_layer_launch(a, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer launch");
@@ -407,6 +422,14 @@ int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_w
         if (e != cudaSuccess) return cuda_fail(ctx, e, "moe debug copy");
     }
     return PBMOE_OK;
+}
+}  // namespace
+
+int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w, const void* x,
+                    pbmoe_dtype x_dtype, const void* residual, void* out, pbmoe_dtype out_dtype, uint32_t tokens,
+                    const float* next_norm_weight, void* next_normed, const pbmoe_moe_debug* debug, void* stream) {
+    return moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
+                          debug, stream, 0, 0, nullptr);
 }
 
 }  // extern "C"
@@ -686,4 +709,139 @@ int pbmoe_q4_gemm_grouped(pbmoe_ctx* ctx, const pbmoe_q4_expert_matrix* w, const
     cudaError_t e = pbmoe::q4_gemm_grouped_launch(a, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 grouped gemm launch");
     return PBMOE_OK;
+}
+
+// ---------------------------------------------------------------- expert parallelism
+int pbmoe_ep_expert_range(uint32_t E, uint32_t rank, uint32_t world, uint32_t* begin, uint32_t* count) {
+    if (!begin || !count || world == 0 || rank >= world || E < world) return PBMOE_ERR_INVALID_ARGUMENT;
+    const uint64_t b = uint64_t(rank) * E / world, e = uint64_t(rank + 1) * E / world;
+    *begin = static_cast<uint32_t>(b);
+    *count = static_cast<uint32_t>(e - b);
+    return PBMOE_OK;
+}
+
+namespace {
+void ep_unmap(pbmoe_ctx* ctx) {
+    for (uint32_t r = 0; r < pbmoe::kMaxEpRanks; ++r) {
+        if (ctx->ep_peer_ipc[r]) cudaIpcCloseMemHandle(ctx->ep_peer[r]);
+        ctx->ep_peer_ipc[r] = false;
+        ctx->ep_peer[r] = nullptr;
+    }
+}
+}  // namespace
+
+int pbmoe_ep_reserve(pbmoe_ctx* ctx, uint32_t rank, uint32_t world, uint32_t max_tokens, uint32_t hidden) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (world == 0 || world > pbmoe::kMaxEpRanks || rank >= world)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert parallelism: rank %u of world %u (world 1..%u)", rank, world,
+                    pbmoe::kMaxEpRanks);
+    if (max_tokens == 0 || hidden == 0 || hidden % 8)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "expert parallelism: max_tokens %u, hidden %u", max_tokens, hidden);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    const size_t need = pbmoe::ep_buffer_bytes(world, max_tokens, hidden);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before exchange-buffer setup");
+    ep_unmap(ctx);
+    if (ctx->ep_base && ctx->ep_bytes != need) {
+        cudaFree(ctx->ep_base);
+        ctx->ep_base = nullptr;
+    }
+    if (!ctx->ep_base && (e = cudaMalloc(&ctx->ep_base, need)) != cudaSuccess)
+        return cuda_fail(ctx, e, "exchange buffer allocation");
+    if ((e = cudaMemset(ctx->ep_base, 0, need)) != cudaSuccess) return cuda_fail(ctx, e, "exchange buffer clear");
+    ctx->ep_bytes = need;
+    ctx->ep_rank = rank;
+    ctx->ep_world = world;
+    ctx->ep_max_tokens = max_tokens;
+    ctx->ep_hidden = hidden;
+    ctx->ep_epoch = 0;
+    ctx->ep_peer[rank] = ctx->ep_base;
+    return PBMOE_OK;
+}
+
+void* pbmoe_ep_buffer(pbmoe_ctx* ctx) { return ctx ? ctx->ep_base : nullptr; }
+
+int pbmoe_ep_ipc_handle(pbmoe_ctx* ctx, void* handle) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!handle) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "ep ipc handle: null output");
+    if (!ctx->ep_base) return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "ep ipc handle: call pbmoe_ep_reserve first");
+    static_assert(sizeof(cudaIpcMemHandle_t) == PBMOE_EP_HANDLE_BYTES, "IPC handle size");
+    DeviceGuard g(ctx->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, ctx->ep_base);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange buffer IPC handle");
+    std::memcpy(handle, &h, sizeof h);
+    return PBMOE_OK;
+}
+
+int pbmoe_ep_open_peers(pbmoe_ctx* ctx, const void* handles) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!handles) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "ep open peers: null handles");
+    if (!ctx->ep_base) return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "ep open peers: call pbmoe_ep_reserve first");
+    DeviceGuard g(ctx->device);
+    ep_unmap(ctx);
+    ctx->ep_peer[ctx->ep_rank] = ctx->ep_base;
+    for (uint32_t r = 0; r < ctx->ep_world; ++r) {
+        if (r == ctx->ep_rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const char*>(handles) + size_t(r) * PBMOE_EP_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            ep_unmap(ctx);
+            ctx->ep_peer[ctx->ep_rank] = ctx->ep_base;
+            return fail(ctx, PBMOE_ERR_PEER, "ep open peers: mapping rank %u failed: %s", r, cudaGetErrorString(e));
+        }
+        ctx->ep_peer[r] = p;
+        ctx->ep_peer_ipc[r] = true;
+    }
+    return PBMOE_OK;
+}
+
+int pbmoe_ep_set_peers(pbmoe_ctx* ctx, void* const* buffers) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!buffers) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "ep set peers: null buffers");
+    if (!ctx->ep_base) return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "ep set peers: call pbmoe_ep_reserve first");
+    ep_unmap(ctx);
+    for (uint32_t r = 0; r < ctx->ep_world; ++r) ctx->ep_peer[r] = r == ctx->ep_rank ? ctx->ep_base : buffers[r];
+    return PBMOE_OK;
+}
+
+int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w,
+                       const pbmoe_ep_shard* shard, const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
+                       pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight, void* next_normed,
+                       void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    int rc = check_moe_config(ctx, c);
+    if (rc) return rc;
+    if (!shard) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "ep moe layer: null shard");
+    if (shard->expert_count == 0 || uint64_t(shard->expert_begin) + shard->expert_count > c->num_experts)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "ep moe layer: experts [%u, %u) outside 0..%u", shard->expert_begin,
+                    shard->expert_begin + shard->expert_count, c->num_experts);
+    if (!ctx->ep_base)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "ep moe layer: call pbmoe_ep_reserve first");
+    if (tokens > ctx->ep_max_tokens || c->layout.hidden != ctx->ep_hidden)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "ep moe layer: exchange buffer reserved for tokens<=%u hidden=%u, "
+                    "call needs tokens=%u hidden=%u", ctx->ep_max_tokens, ctx->ep_hidden, tokens, c->layout.hidden);
+    for (uint32_t r = 0; r < ctx->ep_world; ++r)
+        if (!ctx->ep_peer[r])
+            return fail(ctx, PBMOE_ERR_PEER, "ep moe layer: rank %u's exchange buffer is not mapped "
+                        "(pbmoe_ep_open_peers / pbmoe_ep_set_peers)", r);
+    if (tokens == 0) return PBMOE_OK;
+    pbmoe::EpPeers ep{};
+    const size_t recv_bytes = pbmoe::ep_recv_floats(ctx->ep_world, ctx->ep_max_tokens, ctx->ep_hidden) * 4;
+    for (uint32_t r = 0; r < ctx->ep_world; ++r) {
+        ep.recv[r] = static_cast<float*>(ctx->ep_peer[r]);
+        ep.flags[r] = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->ep_peer[r]) + recv_bytes);
+    }
+    ep.rank = ctx->ep_rank;
+    ep.world = ctx->ep_world;
+    ep.max_tokens = ctx->ep_max_tokens;
+    ep.epoch = ctx->ep_epoch + 1;
+    ep.timeout_ns = shard->timeout_us ? uint64_t(shard->timeout_us) * 1000ull : 2000000000ull;
+    rc = moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
+                        nullptr, stream, shard->expert_begin, shard->expert_count, &ep);
+    if (rc == PBMOE_OK) ctx->ep_epoch = ep.epoch;
+    return rc;
 }

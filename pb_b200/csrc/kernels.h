@@ -50,6 +50,23 @@ struct MoeLayoutDev {
     uint32_t cpg_shift_i;  // same for rows of length inter
 };
 
+// Expert-parallel combine: every rank's receive buffer ([2 parity][world]
+// [max_tokens][H] f32 partial outputs, then [world][max_tokens] u32 epoch
+// flags), addressed through peer pointers (this rank's own at index rank).
+constexpr uint32_t kMaxEpRanks = 8;
+struct EpPeers {
+    float* recv[kMaxEpRanks];
+    uint32_t* flags[kMaxEpRanks];
+    uint32_t rank, world, max_tokens, epoch;
+    uint64_t timeout_ns;
+};
+__host__ __device__ inline size_t ep_recv_floats(uint32_t world, uint32_t max_tokens, uint32_t H) {
+    return size_t(2) * world * max_tokens * H;
+}
+__host__ __device__ inline size_t ep_buffer_bytes(uint32_t world, uint32_t max_tokens, uint32_t H) {
+    return ep_recv_floats(world, max_tokens, H) * 4 + size_t(world) * max_tokens * 4;
+}
+
 struct MoeLaunch {
     MoeWs ws;
     MoeLayoutDev layout;
@@ -68,6 +85,11 @@ struct MoeLaunch {
     const uint8_t* shared_slot;
     bool pdl;  // launch the router kernel with programmatic dependent launch
     void* const* phase_events;  // NULL, or 5 cudaEvent_t recorded around the kernels
+    // expert parallelism: this rank runs experts [expert_lo, expert_lo +
+    // expert_count) (0 = all), `experts` holding exactly those slots; with
+    // `ep` set the combine sums the partials of every rank over peer memory
+    uint32_t expert_lo, expert_count;
+    const EpPeers* ep;
 };
 
 // Per-launch bytes of each workspace array, in MoeWs order (host arithmetic).

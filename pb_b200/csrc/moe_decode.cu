@@ -25,6 +25,7 @@
 // griddepcontrol.wait before touching its predecessor's outputs.
 
 #include "kernels.h"
+#include "pipe.cuh"
 #include "q4_rows.cuh"
 #include "routing.cuh"
 
@@ -40,7 +41,8 @@ template <typename XT>
 __global__ void __launch_bounds__(kRouterThreads)
 moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
                   uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
-                  const uint16_t* __restrict__ shared_gate_w, int has_shared, MoeWs ws) {
+                  const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
+                  MoeWs ws) {
     extern __shared__ __align__(16) float smem[];
     float* xs = smem;  // [kRouterTokPass][H]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -178,20 +180,23 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     const uint32_t R = T * K;
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
+    // only the experts of this rank's range [e_lo, e_hi) form groups (all of
+    // them on a single GPU); group_expert holds the slot index e - e_lo
     for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
         const uint32_t e = __ldcg(ws.route_ids + r);
         ids[r] = e;
-        atomicAdd(&cnt[e], 1u);
+        if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e], 1u);
     }
     __syncthreads();
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) gidx[e] = cnt[e] ? 1u : 0u;
     __syncthreads();
     const uint32_t U = block_exclusive_scan(gidx, E, tmp);
-    block_exclusive_scan(cnt, E, tmp);  // cnt[e] = start of expert e among routed positions
+    const uint32_t RL = block_exclusive_scan(cnt, E, tmp);  // cnt[e] = start of expert e; RL local routes
     const uint32_t shared_groups = has_shared ? 1u : 0u;
     const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared group
     for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
         const uint32_t e = ids[r];
+        if (e < e_lo || e >= e_hi) continue;
         uint32_t rank = 0;
         for (uint32_t q = 0; q < r; ++q) rank += (ids[q] == e) ? 1u : 0u;
         const uint32_t pos = routed_base + cnt[e] + rank;
@@ -200,9 +205,9 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
         if (rank == 0) {
             // exclusive-scan property: the group's size is the next start minus this one
             const uint32_t g = shared_groups + gidx[e];
-            ws.group_expert[g] = e;
+            ws.group_expert[g] = e - e_lo;
             ws.group_start[g] = routed_base + cnt[e];
-            ws.group_count[g] = (e + 1 < E ? cnt[e + 1] : R) - cnt[e];
+            ws.group_count[g] = (e + 1 < E ? cnt[e + 1] : RL) - cnt[e];
         }
     }
     if (has_shared) {
@@ -361,16 +366,45 @@ constexpr int kCombineEpt = 4;  // elements per thread per pass (H <= 2048 in on
 // One CTA per token. The K routed outputs, the shared output and the
 // residual of a thread's elements are all requested before any arithmetic
 // (K <= KMAX, unrolled), then summed in slot order as the reference does.
-template <typename OT, int KMAX>
+// Routes whose expert lies outside [e_lo, e_hi) belong to another rank and
+// are skipped (their y rows were not written).
+//
+// kEP: expert-parallel combine. The token's partial (local routes plus, on
+// the rank that holds it, the shared expert) goes to every rank's receive
+// buffer over peer memory (NVLink stores); after a CTA barrier thread 0
+// publishes it with a system-scope release of the epoch flag in each peer's
+// flag array. Threads 0..world-1 then wait, bounded, for every rank's flag
+// (acquire); the output is residual + the world partials summed in rank
+// order, identical on every rank. A wait that expires latches
+// PBMOE_DEV_ERR_PEER_TIMEOUT and the missing partial counts as zero.
+// Receive buffers alternate by epoch parity: a rank can run at most one layer
+// ahead of another (its next partial waits for everyone's flags), so the
+// parity a rank writes is never the one a slower rank is still reading.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <typename OT, int KMAX, bool kEP>
 __global__ void __launch_bounds__(kCombineThreads)
 moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_gate, const OT* __restrict__ residual,
                    OT* __restrict__ out, const float* __restrict__ norm_w, OT* __restrict__ next_normed, float eps,
-                   MoeWs ws) {
+                   uint32_t e_lo, uint32_t e_hi, MoeWs ws, EpPeers ep) {
     __shared__ float red[32];
     __shared__ float wsh[KMAX];
+    __shared__ uint32_t missing;
     const uint32_t t = blockIdx.x;
     pdl_wait();
-    if (threadIdx.x < K) wsh[threadIdx.x] = __ldcg(ws.route_w + static_cast<size_t>(t) * K + threadIdx.x);
+    if (threadIdx.x < K) {
+        const uint32_t e = __ldcg(ws.route_ids + static_cast<size_t>(t) * K + threadIdx.x);
+        wsh[threadIdx.x] = (e >= e_lo && e < e_hi) ? __ldcg(ws.route_w + static_cast<size_t>(t) * K + threadIdx.x)
+                                                   : 0.f;  // another rank's route
+    }
+    if (threadIdx.x == 0) missing = 0;
     float sw = 0.f;
     if (has_shared) sw = has_gate ? 1.0f / (1.0f + expf(-__ldcg(ws.shared_logit + t))) : 1.0f;
     __syncthreads();
@@ -378,27 +412,94 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     const float* ysh = ws.y + (static_cast<size_t>(T) * K + t) * H;
     float ss = 0.f;
     float keep[kCombineEpt];
+    const uint32_t par = ep.epoch & 1u;
+    auto recv_row = [&](uint32_t rank_buf, uint32_t src) {  // partial of `src` in rank `rank_buf`'s buffer
+        return ep.recv[rank_buf] + ((static_cast<size_t>(par) * ep.world + src) * ep.max_tokens + t) * H;
+    };
+    if constexpr (kEP) {
+        // 1. this rank's partial to every rank
+        for (uint32_t c0 = threadIdx.x; c0 < H; c0 += kCombineEpt * blockDim.x) {
+            float yv[KMAX][kCombineEpt], sh[kCombineEpt];
+#pragma unroll
+            for (int i = 0; i < kCombineEpt; ++i) {
+                const uint32_t c = c0 + i * blockDim.x;
+                const bool in = c < H;
+#pragma unroll
+                for (int k = 0; k < KMAX; ++k)
+                    yv[k][i] = (in && static_cast<uint32_t>(k) < K && wsh[k] != 0.f)
+                                   ? __ldcg(yt + static_cast<size_t>(k) * H + c)
+                                   : 0.f;
+                sh[i] = (in && has_shared) ? __ldcg(ysh + c) : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < kCombineEpt; ++i) {
+                const uint32_t c = c0 + i * blockDim.x;
+                float moe = 0.f;
+#pragma unroll
+                for (int k = 0; k < KMAX; ++k)
+                    if (static_cast<uint32_t>(k) < K) moe += wsh[k] * yv[k][i];
+                const float part = moe + sw * sh[i];
+                if (c < H)
+                    for (uint32_t d = 0; d < ep.world; ++d) recv_row(d, ep.rank)[c] = part;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            for (uint32_t d = 0; d < ep.world; ++d)
+                st_release_sys(ep.flags[d] + static_cast<size_t>(ep.rank) * ep.max_tokens + t, ep.epoch);
+        }
+        // 2. every rank's partial of this token has landed here
+        if (threadIdx.x < ep.world) {
+            const uint32_t* f = ep.flags[ep.rank] + static_cast<size_t>(threadIdx.x) * ep.max_tokens + t;
+            const uint64_t t0 = global_ns();
+            while (static_cast<int32_t>(ld_acquire_sys(f) - ep.epoch) < 0) {
+                if (global_ns() - t0 > ep.timeout_ns) {
+                    atomicOr(&missing, 1u << threadIdx.x);
+                    if (ws.status) atomicOr(ws.status, PBMOE_DEV_ERR_PEER_TIMEOUT);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __syncthreads();
+    }
     for (uint32_t c0 = threadIdx.x; c0 < H; c0 += kCombineEpt * blockDim.x) {
         float yv[KMAX][kCombineEpt];
         float sh[kCombineEpt], rv[kCombineEpt];
+        if constexpr (!kEP) {
+#pragma unroll
+            for (int i = 0; i < kCombineEpt; ++i) {
+                const uint32_t c = c0 + i * blockDim.x;
+                const bool in = c < H;
+#pragma unroll
+                for (int k = 0; k < KMAX; ++k)
+                    yv[k][i] = (in && static_cast<uint32_t>(k) < K && wsh[k] != 0.f)
+                                   ? __ldcg(yt + static_cast<size_t>(k) * H + c)
+                                   : 0.f;
+                sh[i] = (in && has_shared) ? __ldcg(ysh + c) : 0.f;
+            }
+        }
 #pragma unroll
         for (int i = 0; i < kCombineEpt; ++i) {
             const uint32_t c = c0 + i * blockDim.x;
-            const bool in = c < H;
-#pragma unroll
-            for (int k = 0; k < KMAX; ++k)
-                yv[k][i] = (in && static_cast<uint32_t>(k) < K) ? __ldcg(yt + static_cast<size_t>(k) * H + c) : 0.f;
-            sh[i] = (in && has_shared) ? __ldcg(ysh + c) : 0.f;
-            rv[i] = (in && residual) ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
+            rv[i] = (c < H && residual) ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
         }
 #pragma unroll
         for (int i = 0; i < kCombineEpt; ++i) {
             const uint32_t c = c0 + i * blockDim.x;
             float moe = 0.f;
+            if constexpr (kEP) {
+                // every rank's partial, in rank order (not cached: peers wrote it)
+                for (uint32_t src = 0; src < ep.world; ++src)
+                    if (c < H && !(missing & (1u << src))) moe += __ldcv(recv_row(ep.rank, src) + c);
+            } else {
 #pragma unroll
-            for (int k = 0; k < KMAX; ++k)
-                if (static_cast<uint32_t>(k) < K) moe += wsh[k] * yv[k][i];
-            const float v = rv[i] + moe + sw * sh[i];
+                for (int k = 0; k < KMAX; ++k)
+                    if (static_cast<uint32_t>(k) < K) moe += wsh[k] * yv[k][i];
+                moe += sw * sh[i];
+            }
+            const float v = rv[i] + moe;
             keep[i] = v;
             if (c < H) {
                 store_act<OT>(out, static_cast<size_t>(t) * H + c, v);
@@ -484,6 +585,8 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     const uint32_t T = a.tokens, H = a.layout.hidden, I = a.layout.inter, E = a.num_experts, K = a.top_k;
     const int has_shared = a.shared_slot != nullptr;
     const int has_gate = a.shared_gate != nullptr;
+    const uint32_t e_lo = a.expert_count ? a.expert_lo : 0u;
+    const uint32_t e_hi = a.expert_count ? a.expert_lo + a.expert_count : E;
     MoeWs ws = a.ws;
     auto mark = [&](int i) -> cudaError_t {
         return a.phase_events ? cudaEventRecord(static_cast<cudaEvent_t>(a.phase_events[i]), s) : cudaSuccess;
@@ -504,7 +607,7 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         const uint16_t* rw = a.router_w;
         const uint16_t* sg = a.shared_gate;
         void* args[] = {(void*)&x, (void*)&T, (void*)&H, (void*)&E, (void*)&K, (void*)&norm, (void*)&scale,
-                        (void*)&rw, (void*)&sg, (void*)&has_shared, (void*)&ws};
+                        (void*)&rw, (void*)&sg, (void*)&has_shared, (void*)&e_lo, (void*)&e_hi, (void*)&ws};
         if ((err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRouterThreads), smem, s, args,
                               a.pdl && pdl)) != cudaSuccess)
             return err;
@@ -577,11 +680,21 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         OT* nn = static_cast<OT*>(a.next_normed);
         const float* nw = a.next_norm_w;
         float eps = a.eps;
-        void* args[] = {(void*)&T, (void*)&H, (void*)&K, (void*)&has_shared, (void*)&has_gate, (void*)&res,
-                        (void*)&out, (void*)&nw, (void*)&nn, (void*)&eps, (void*)&ws};
-        const void* fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8>)
-                         : K <= 16 ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 16>)
-                                   : reinterpret_cast<const void*>(moe_combine_kernel<OT, 32>);
+        EpPeers ep{};
+        if (a.ep) ep = *a.ep;
+        uint32_t lo = e_lo, hi = e_hi;
+        void* args[] = {(void*)&T,   (void*)&H,   (void*)&K,   (void*)&has_shared, (void*)&has_gate,
+                        (void*)&res, (void*)&out, (void*)&nw,  (void*)&nn,         (void*)&eps,
+                        (void*)&lo,  (void*)&hi,  (void*)&ws,  (void*)&ep};
+        const void* fn;
+        if (a.ep)
+            fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8, true>)
+                 : K <= 16 ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 16, true>)
+                           : reinterpret_cast<const void*>(moe_combine_kernel<OT, 32, true>);
+        else
+            fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8, false>)
+                 : K <= 16 ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 16, false>)
+                           : reinterpret_cast<const void*>(moe_combine_kernel<OT, 32, false>);
         if ((err = launch_pdl(fn, dim3(T), dim3(kCombineThreads), 0, s, args, pdl)) != cudaSuccess) return err;
     }
     return mark(4);
