@@ -23,9 +23,12 @@ Reported (one JSON line on rank 0):
 `--impl reference` times the oracle alone (the reference cannot be built:
 Rust toolchain absent; its GPU path is Metal).
 
-Multi-GPU (torchrun, N>1): every rank runs its own replica of the layer stack
-on its own tokens ("weak" scaling); expert-parallel sharding is not wired into
-this bench yet.
+Multi-GPU (torchrun, N>1): expert parallelism. Rank r holds experts
+[r*512/N, (r+1)*512/N) of every cycled layer (router and shared expert
+replicated, the shared expert computed on rank 0); every rank routes the same
+tokens and runs its own experts' routes; the layer output is the one-shot
+NVLink peer-memory combine of the ranks' partials (pbmoe_ep_moe_layer). The
+job processes the same --batch tokens per step at every N ("strong" scaling).
 """
 
 from __future__ import annotations
@@ -156,15 +159,17 @@ def host_layer(seed: int):
                 nbytes=nbytes)
 
 
-def cpu_oracle_rate(batch: int, target_s: float, steps: int | None = None):
-    """Tokens/s of the oracle MoE layer on this host's cores (bounded sample)."""
-    import numpy as np
+def cpu_oracle_rate(batch: int, steps: int, warmup: int = 0, budget_s: float = 12.0, layer=None):
+    """Tokens/s of the oracle MoE layer on this host's cores over `steps` timed
+    steps (after `warmup`), each a bounded sample of the workload: the full
+    batch when warm-up + steps fit `budget_s`, else fewer tokens per step, and
+    if even one token per step does not fit, fewer steps (reported)."""
     import torch
 
     from oracle import pb_oracle
 
     threads = os.cpu_count() or 1
-    L = host_layer(99)
+    L = layer if layer is not None else host_layer(99)
     g = torch.Generator().manual_seed(5)
 
     def run(tokens):
@@ -175,38 +180,38 @@ def cpu_oracle_rate(batch: int, target_s: float, steps: int | None = None):
         return time.perf_counter() - t0
 
     run(min(batch, threads))  # warm the page cache / code
-    probe = run(batch)
-    if steps is None:
-        reps = max(1, int(target_s / max(probe, 1e-3)))
-    else:
-        reps = steps
-    times = [run(batch) for _ in range(reps)]
-    total = sum(times)
-    return dict(value=batch * reps / total, unit="tok/s", cores=threads, kind="port",
-                sample=f"{reps} steps x {batch} tokens through one config-1 layer (C++ oracle, {threads} threads)",
-                seconds=total, per_step_s=total / reps)
+    per_token = run(batch) / batch
+    total = max(1, steps + warmup)
+    tokens = max(1, min(batch, int(budget_s / (total * per_token))))
+    run_steps = steps if total * tokens * per_token <= 3 * budget_s else max(1, int(3 * budget_s / per_token) - warmup)
+    for _ in range(warmup if run_steps == steps else 0):
+        run(tokens)
+    times = [run(tokens) for _ in range(run_steps)]
+    secs = sum(times)
+    return dict(value=tokens * run_steps / secs, unit="tok/s", cores=threads, kind="port",
+                sample=(f"{run_steps} steps x {tokens} of the {batch} tokens through one config-1 layer "
+                        f"(C++ oracle, {threads} threads)"),
+                seconds=secs, per_step_s=secs / run_steps, steps_run=run_steps, tokens_per_step=tokens)
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    # Each step is one config-1 layer over --batch tokens on all host threads;
-    # warm-up steps are run and discarded.
-    import numpy as np  # noqa: F401
-
+    # the reference's CPU path on all host threads; the whole --steps/--warmup
+    # run is bounded to a few minutes by the per-step sample size
     from oracle import pb_oracle
 
     pb_oracle.build()
-    res = cpu_oracle_rate(args.batch, target_s=0, steps=max(1, args.warmup))
-    res = cpu_oracle_rate(args.batch, target_s=0, steps=args.steps)
+    res = cpu_oracle_rate(args.batch, steps=args.steps, warmup=max(1, args.warmup), budget_s=150.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["per_step_s"] * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "steps": res["steps_run"], "warmup": args.warmup, "ms_per_step": res["per_step_s"] * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, config-1 distributions)",
         "config": {"workload": "config1 MoE FFN decode layer", "batch": args.batch, "hidden": HIDDEN,
-                   "experts": EXPERTS, "top_k": TOPK, "intermediate": INTER, "group": GROUP},
+                   "experts": EXPERTS, "top_k": TOPK, "intermediate": INTER, "group": GROUP,
+                   "tokens_per_step": res["tokens_per_step"]},
         "cpu_baseline": {"value": res["value"], "unit": "tok/s", "cores": res["cores"], "kind": "port",
                          "sample": res["sample"]},
         "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -242,27 +247,54 @@ def main():
 
     B, NL = args.batch, args.layers
     ctx = capi.Context(local)
-    layers = [synth.MoeLayerWeights(dev, seed=1000 * rank + i) for i in range(NL)]
+    ep_mode = world > 1
+    e_begin, e_count = capi.ep_expert_range(EXPERTS, rank, world) if ep_mode else (0, EXPERTS)
+    layers = []
+    for i in range(NL):  # identical weights on every rank; each keeps its expert shard
+        lw = synth.MoeLayerWeights(dev, seed=1000 + i)
+        if ep_mode:
+            lw.experts = lw.experts[e_begin:e_begin + e_count].clone()
+            if rank != 0:
+                lw.shared, lw.shared_gate = None, None
+            torch.cuda.empty_cache()
+        layers.append(lw)
     cfg = capi.moe_config(layers[0].layout, EXPERTS, TOPK)
     ctx.reserve(B, cfg)
+    shard = capi.EpShard(e_begin, e_count, 0)
+    if ep_mode:
+        from pb_b200 import ep as ep_host
+
+        ep_host.connect(ctx, max_tokens=B, hidden=HIDDEN)
     NIN = 2 * NL  # distinct inputs: step j uses layer j % NL and input j % NIN
-    g = synth.gen(dev, 7 + rank)
+    g = synth.gen(dev, 7)  # the same tokens on every rank (replicated activations)
     xs = [synth.normal_bf16((B, HIDDEN), 1.0, g, dev) for _ in range(NIN)]
     outs = [torch.empty(B, HIDDEN, device=dev, dtype=torch.bfloat16) for _ in range(2)]
     weights = [lw.c_weights() for lw in layers]
     stream = torch.cuda.Stream(dev)
 
     def step(j, s=None, debug=None):
-        ctx.moe_layer(cfg, weights[j % NL], xs[j % NIN], outs[j % 2], B, debug=debug, stream=s)
+        if ep_mode:
+            ctx.ep_moe_layer(cfg, weights[j % NL], shard, xs[j % NIN], outs[j % 2], B, stream=s)
+        else:
+            ctx.moe_layer(cfg, weights[j % NL], xs[j % NIN], outs[j % 2], B, debug=debug, stream=s)
 
-    # -- unique experts per (layer, input) combination, from the routes themselves
+    # -- unique experts of this rank per (layer, input) combination, from the
+    #    routes (the layer's own on one GPU; a torch routing of the same
+    #    logits for the byte count of a shard)
     ids = torch.empty(B, TOPK, dtype=torch.int32, device=dev)
     uniq = []
     with torch.cuda.stream(stream):
         for j in range(NIN):
-            step(j, stream, capi.MoeDebug(None, ids.data_ptr(), None, None, None))
-            stream.synchronize()
-            uniq.append(int(torch.unique(ids).numel()))
+            if ep_mode:
+                logits = xs[j].float() @ layers[j % NL].router.float().t()
+                sel = torch.unique(torch.topk(logits, TOPK, dim=1).indices)
+                uniq.append(int(((sel >= e_begin) & (sel < e_begin + e_count)).sum().item()))
+                step(j, stream)
+                stream.synchronize()
+            else:
+                step(j, stream, capi.MoeDebug(None, ids.data_ptr(), None, None, None))
+                stream.synchronize()
+                uniq.append(int(torch.unique(ids).numel()))
     assert ctx.device_status(stream=stream) == 0
 
     # -- CUDA graphs: one per step slot, plus one holding a whole cycle of NIN
@@ -321,13 +353,15 @@ def main():
         ms = float(t.item())
     clock_summary = clocks.summary()
     assert ctx.device_status(stream=stream) == 0
-    value = K * B * world / (ms / 1e3)
+    value = K * B / (ms / 1e3)  # the job's tokens: replicated over the ranks, not multiplied
     steps_u = [uniq[(W + i) % NIN] for i in range(K)]
     mean_u = float(np.mean(steps_u))
-    layer_bytes = ROUTER_BYTES + SHARED_GATE_BYTES + SLOT_BYTES * (1 + mean_u) + 2 * B * HIDDEN * 2
+    # bytes one GPU must read per step (its expert shard, replicated router; shared expert on rank 0)
+    layer_bytes = (ROUTER_BYTES + SHARED_GATE_BYTES + SLOT_BYTES * (mean_u + (1 if rank == 0 else 0)) +
+                   2 * B * HIDDEN * 2)
 
     # -- per-kernel durations (events between the four kernels; serialised, no PDL overlap)
-    NPH = min(K, NIN)
+    NPH = min(K, NIN) if not ep_mode else 0
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(NPH)]
     for row in evs:  # torch creates the CUDA event lazily, on first record
         for e in row:
@@ -346,18 +380,23 @@ def main():
     for e in evs:
         for k, n in enumerate(names):
             dur[n].append(e[k].elapsed_time(e[k + 1]))
-    mean_dur = {n: float(np.mean(v)) for n, v in dur.items()}
-    u_ph = [uniq[(W + i) % NIN] for i in range(NPH)]
+    mean_dur = {n: float(np.mean(v)) if v else 0.0 for n, v in dur.items()}
+    u_ph = [uniq[(W + i) % NIN] for i in range(NPH)] or [mean_u]
     kbytes = {
         "router+topk": ROUTER_BYTES + SHARED_GATE_BYTES + B * HIDDEN * 2,
         "expert_gate_up": float(np.mean([(u + 1) * GATE_UP_BYTES for u in u_ph])) + B * HIDDEN * 2,
         "expert_down": float(np.mean([(u + 1) * DOWN_BYTES for u in u_ph])),
         "combine": B * HIDDEN * 2 * 2 + B * (TOPK + 1) * HIDDEN * 4,
     }
-    dominant = max(mean_dur, key=lambda n: mean_dur[n])
     peak, peak_kind = measured_peaks()
+    if ep_mode:  # no per-kernel events through the EP call: the whole layer per GPU
+        dominant = "layer (per GPU, expert shard)"
+        kbytes[dominant] = layer_bytes
+        mean_dur[dominant] = ms / K
+    else:
+        dominant = max(mean_dur, key=lambda n: mean_dur[n])
     achieved = kbytes[dominant] / (mean_dur[dominant] / 1e3) / 1e9
-    serial_ms = sum(mean_dur.values())
+    serial_ms = sum(v for n, v in mean_dur.items() if n != dominant or not ep_mode)
 
     # -- end to end through the public C-ABI call with host buffers
     h_in = torch.empty(B, HIDDEN, dtype=torch.bfloat16).pin_memory()
@@ -372,7 +411,10 @@ def main():
         e0.record(stream)
         for i in range(KE):
             d_in.copy_(h_in, non_blocking=True)
-            ctx.moe_layer(cfg, weights[i % NL], d_in, outs[0], B, stream=stream)
+            if ep_mode:
+                ctx.ep_moe_layer(cfg, weights[i % NL], shard, d_in, outs[0], B, stream=stream)
+            else:
+                ctx.moe_layer(cfg, weights[i % NL], d_in, outs[0], B, stream=stream)
             h_out.copy_(outs[0], non_blocking=True)
         e1.record(stream)
     stream.synchronize()
@@ -381,7 +423,8 @@ def main():
         t = torch.tensor([ems], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ems = float(t.item())
-    e2e_value = KE * B * world / (ems / 1e3)
+    e2e_value = KE * B / (ems / 1e3)
+    assert ctx.device_status(stream=stream) == 0
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -389,7 +432,7 @@ def main():
             from oracle import pb_oracle
 
             pb_oracle.build()
-            cpu = cpu_oracle_rate(B, target_s=12.0)
+            cpu = cpu_oracle_rate(B, steps=20, warmup=1, budget_s=12.0)
             cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         except Exception as exc:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {exc}"}
@@ -397,13 +440,14 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded; config-1 shapes and distributions)",
             "config": {"workload": "config1 MoE FFN decode layer", "batch": B, "hidden": HIDDEN,
                        "experts": EXPERTS, "top_k": TOPK, "intermediate": INTER, "group": GROUP,
                        "shared_expert": True, "layers_cycled": NL,
                        "l2": f"inputs larger than L2: {NL} distinct layers cycled ({NL * SLOT_BYTES * EXPERTS / 1e9:.1f} GB experts)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"ep{world}: experts sharded {EXPERTS // world}/GPU, one-shot NVLink "
+                                       "P2P combine" if ep_mode else "single GPU"),
                        "graph": f"CUDA graphs of {NIN} steps replayed back to back"},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": B * HIDDEN * 2,
                     "d2h_bytes_per_step": B * HIDDEN * 2, "steps": KE},

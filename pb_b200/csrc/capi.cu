@@ -24,7 +24,7 @@ struct pbmoe_ctx {
     size_t x16_elems = 0;
     void* ep_base = nullptr;  // expert-parallel exchange buffer
     size_t ep_bytes = 0;
-    uint32_t ep_rank = 0, ep_world = 0, ep_max_tokens = 0, ep_hidden = 0, ep_epoch = 0;
+    uint32_t ep_rank = 0, ep_world = 0, ep_max_tokens = 0, ep_hidden = 0;
     void* ep_peer[pbmoe::kMaxEpRanks] = {};
     bool ep_peer_ipc[pbmoe::kMaxEpRanks] = {};  // mapped through CUDA IPC (closed at destroy)
     int num_sms = 0;
@@ -755,7 +755,6 @@ int pbmoe_ep_reserve(pbmoe_ctx* ctx, uint32_t rank, uint32_t world, uint32_t max
     ctx->ep_world = world;
     ctx->ep_max_tokens = max_tokens;
     ctx->ep_hidden = hidden;
-    ctx->ep_epoch = 0;
     ctx->ep_peer[rank] = ctx->ep_base;
     return PBMOE_OK;
 }
@@ -830,18 +829,17 @@ int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_mo
                         "(pbmoe_ep_open_peers / pbmoe_ep_set_peers)", r);
     if (tokens == 0) return PBMOE_OK;
     pbmoe::EpPeers ep{};
-    const size_t recv_bytes = pbmoe::ep_recv_floats(ctx->ep_world, ctx->ep_max_tokens, ctx->ep_hidden) * 4;
+    const size_t flags_off = pbmoe::ep_flags_offset(ctx->ep_world, ctx->ep_max_tokens, ctx->ep_hidden);
     for (uint32_t r = 0; r < ctx->ep_world; ++r) {
         ep.recv[r] = static_cast<float*>(ctx->ep_peer[r]);
-        ep.flags[r] = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->ep_peer[r]) + recv_bytes);
+        ep.flags[r] = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->ep_peer[r]) + flags_off);
     }
+    ep.epoch = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->ep_base) +
+                                           pbmoe::ep_epoch_offset(ctx->ep_world, ctx->ep_max_tokens, ctx->ep_hidden));
     ep.rank = ctx->ep_rank;
     ep.world = ctx->ep_world;
     ep.max_tokens = ctx->ep_max_tokens;
-    ep.epoch = ctx->ep_epoch + 1;
     ep.timeout_ns = shard->timeout_us ? uint64_t(shard->timeout_us) * 1000ull : 2000000000ull;
-    rc = moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
-                        nullptr, stream, shard->expert_begin, shard->expert_count, &ep);
-    if (rc == PBMOE_OK) ctx->ep_epoch = ep.epoch;
-    return rc;
+    return moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
+                          nullptr, stream, shard->expert_begin, shard->expert_count, &ep);
 }

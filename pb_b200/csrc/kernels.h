@@ -50,21 +50,31 @@ struct MoeLayoutDev {
     uint32_t cpg_shift_i;  // same for rows of length inter
 };
 
-// Expert-parallel combine: every rank's receive buffer ([2 parity][world]
+// Expert-parallel combine: every rank's exchange buffer ([2 parity][world]
 // [max_tokens][H] f32 partial outputs, then [world][max_tokens] u32 epoch
-// flags), addressed through peer pointers (this rank's own at index rank).
+// flags, then this rank's u32 epoch counter), addressed through peer pointers
+// (this rank's own at index rank). The counter lives on the device and is
+// advanced once per layer by the router kernel, so captured CUDA graphs
+// replay with fresh epochs.
 constexpr uint32_t kMaxEpRanks = 8;
 struct EpPeers {
     float* recv[kMaxEpRanks];
     uint32_t* flags[kMaxEpRanks];
-    uint32_t rank, world, max_tokens, epoch;
+    uint32_t* epoch;  // this rank's counter
+    uint32_t rank, world, max_tokens;
     uint64_t timeout_ns;
 };
 __host__ __device__ inline size_t ep_recv_floats(uint32_t world, uint32_t max_tokens, uint32_t H) {
     return size_t(2) * world * max_tokens * H;
 }
+__host__ __device__ inline size_t ep_flags_offset(uint32_t world, uint32_t max_tokens, uint32_t H) {
+    return ep_recv_floats(world, max_tokens, H) * 4;
+}
+__host__ __device__ inline size_t ep_epoch_offset(uint32_t world, uint32_t max_tokens, uint32_t H) {
+    return (ep_flags_offset(world, max_tokens, H) + size_t(world) * max_tokens * 4 + 15) / 16 * 16;
+}
 __host__ __device__ inline size_t ep_buffer_bytes(uint32_t world, uint32_t max_tokens, uint32_t H) {
-    return ep_recv_floats(world, max_tokens, H) * 4 + size_t(world) * max_tokens * 4;
+    return ep_epoch_offset(world, max_tokens, H) + 16;
 }
 
 struct MoeLaunch {

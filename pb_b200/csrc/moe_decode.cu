@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(kRouterThreads)
 moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
                   uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
                   const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
-                  MoeWs ws) {
+                  uint32_t* ep_epoch, MoeWs ws) {
     extern __shared__ __align__(16) float smem[];
     float* xs = smem;  // [kRouterTokPass][H]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -224,6 +224,7 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     if (threadIdx.x == 0) {
         *ws.num_groups = U + shared_groups;
         *ws.ticket = 0;  // ready for the next launch
+        if (ep_epoch) *ep_epoch += 1u;  // this layer's expert-parallel exchange epoch
     }
 }
 
@@ -412,7 +413,8 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     const float* ysh = ws.y + (static_cast<size_t>(T) * K + t) * H;
     float ss = 0.f;
     float keep[kCombineEpt];
-    const uint32_t par = ep.epoch & 1u;
+    const uint32_t epoch = kEP ? __ldcg(ep.epoch) : 0u;
+    const uint32_t par = epoch & 1u;
     auto recv_row = [&](uint32_t rank_buf, uint32_t src) {  // partial of `src` in rank `rank_buf`'s buffer
         return ep.recv[rank_buf] + ((static_cast<size_t>(par) * ep.world + src) * ep.max_tokens + t) * H;
     };
@@ -447,13 +449,13 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
         if (threadIdx.x == 0) {
             __threadfence_system();
             for (uint32_t d = 0; d < ep.world; ++d)
-                st_release_sys(ep.flags[d] + static_cast<size_t>(ep.rank) * ep.max_tokens + t, ep.epoch);
+                st_release_sys(ep.flags[d] + static_cast<size_t>(ep.rank) * ep.max_tokens + t, epoch);
         }
         // 2. every rank's partial of this token has landed here
         if (threadIdx.x < ep.world) {
             const uint32_t* f = ep.flags[ep.rank] + static_cast<size_t>(threadIdx.x) * ep.max_tokens + t;
             const uint64_t t0 = global_ns();
-            while (static_cast<int32_t>(ld_acquire_sys(f) - ep.epoch) < 0) {
+            while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
                 if (global_ns() - t0 > ep.timeout_ns) {
                     atomicOr(&missing, 1u << threadIdx.x);
                     if (ws.status) atomicOr(ws.status, PBMOE_DEV_ERR_PEER_TIMEOUT);
@@ -606,8 +608,10 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         float scale = a.routed_scale;
         const uint16_t* rw = a.router_w;
         const uint16_t* sg = a.shared_gate;
-        void* args[] = {(void*)&x, (void*)&T, (void*)&H, (void*)&E, (void*)&K, (void*)&norm, (void*)&scale,
-                        (void*)&rw, (void*)&sg, (void*)&has_shared, (void*)&e_lo, (void*)&e_hi, (void*)&ws};
+        uint32_t* ep_epoch = a.ep ? a.ep->epoch : nullptr;
+        void* args[] = {(void*)&x,  (void*)&T,          (void*)&H,    (void*)&E,    (void*)&K,
+                        (void*)&norm, (void*)&scale,    (void*)&rw,   (void*)&sg,   (void*)&has_shared,
+                        (void*)&e_lo, (void*)&e_hi,     (void*)&ep_epoch, (void*)&ws};
         if ((err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRouterThreads), smem, s, args,
                               a.pdl && pdl)) != cudaSuccess)
             return err;
