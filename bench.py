@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla"],
+                   help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -72,6 +74,13 @@ def measured_peaks():
         d = json.load(open(path))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        return float(json.load(open(path))["bf16_tflops"]), "measured (bf16 burst)"
+    return 1590.0, "fallback"
 
 
 # ------------------------------------------------------------------ clocks
@@ -226,6 +235,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload != "moe":
+        {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla}[args.workload](args)
         return
     import numpy as np
     import torch
@@ -467,6 +479,280 @@ def main():
     ctx.close()
     if dist is not None:
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ other configs
+# Single-GPU measurements of the other hot-path stages (BASELINE.json configs
+# 0, 2 and 3), each one JSON line with the same keys as the headline.
+def _graph_time(calls, stream, steps, warmup):
+    """ms per call of `calls` (a list of no-arg launches) captured as one CUDA
+    graph and replayed until `steps` calls ran, after `warmup` replays."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for c in calls:
+            c()
+        stream.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for c in calls:
+                c()
+        for _ in range(max(3, warmup)):
+            gr.replay()
+        stream.synchronize()
+        reps = max(1, (steps + len(calls) - 1) // len(calls))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(torch.cuda.current_device()) as clocks:
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+            stream.synchronize()
+    return e0.elapsed_time(e1) / (reps * len(calls)), reps * len(calls), clocks.summary()
+
+
+def _e2e_time(call, stream, steps):
+    import torch
+
+    with torch.cuda.stream(stream):
+        call()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            call()
+        e1.record(stream)
+        stream.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _emit(line):
+    print(json.dumps(line), flush=True)
+
+
+def run_matvec(args):
+    """Config 0: y = W x for W Q4 [4096 x 2048] (group 64), x bf16 [1 x 2048],
+    y bf16; 64 distinct weight matrices cycled (303 MB > L2)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    R, Cc, G, NC = 4096, 2048, 64, 64
+    byts = R * Cc // 2 + 2 * R * (Cc // G) * 2 + Cc * 2 + R * 2  # 4,730,880
+    ctx = capi.Context(0)
+    g = synth.gen("cuda", 1)
+    mats = [synth.q4_matrix(R, Cc, G, g, "cuda") for _ in range(NC)]
+    x = synth.normal_bf16((1, Cc), 1.0, g, "cuda")
+    y = torch.empty(1, R, device="cuda", dtype=torch.bfloat16)
+    s = torch.cuda.Stream()
+    calls = [(lambda m=m: ctx.q4_matvec(m[0], m[1], m[2], R, Cc, G, x, y, stream=s)) for m in mats]
+    ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
+    gbs = byts / (ms / 1e3) / 1e9
+    hx = x.cpu().pin_memory()
+    hy = torch.empty(1, R, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(x)
+    it = [0]
+
+    def e2e():
+        m = mats[it[0] % NC]
+        it[0] += 1
+        dx.copy_(hx, non_blocking=True)
+        ctx.q4_matvec(m[0], m[1], m[2], R, Cc, G, dx, y, stream=s)
+        hy.copy_(y, non_blocking=True)
+
+    ems = _e2e_time(e2e, s, min(args.steps, 4 * NC))
+    cpu = None
+    try:
+        import numpy as np
+
+        from oracle import pb_oracle
+
+        pb_oracle.build()
+        p, sc, b = (t.cpu() for t in mats[0])
+        pn = p.numpy().reshape(-1)
+        sn, bn = (synth.bf16_bits(t).numpy().view(np.uint16).reshape(-1) for t in (sc, b))
+        xn = x.float().cpu().numpy().reshape(-1)
+        t0, n = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 5.0:
+            pb_oracle.q4_fma_matvec_bf16(pn, xn, sn, bn, R, Cc, G)
+            n += 1
+        cpu = {"value": byts * n / (time.perf_counter() - t0) / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"{n} matvecs of one config-0 matrix (C++ oracle, 1 thread)"}
+    except Exception as exc:
+        cpu = {"value": None, "unit": "GB/s", "cores": None, "kind": "port", "sample": f"failed: {exc}"}
+    peak, kind = measured_peaks()
+    _emit({
+        "metric": "qmatvec HBM GB/s (config 0: Q4 [4096x2048] x bf16 [1x2048] -> bf16)", "value": gbs,
+        "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; config-0 distributions)",
+        "config": {"workload": "config0 Q4 matvec", "rows": R, "cols": Cc, "group": G,
+                   "l2": f"inputs larger than L2: {NC} distinct matrices cycled ({NC * byts / 1e6:.0f} MB)",
+                   "graph": f"CUDA graph of {NC} launches"},
+        "e2e": {"value": byts / (ems / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": Cc * 2,
+                "d2h_bytes_per_step": R * 2, "steps": min(args.steps, 4 * NC)},
+        "roofline": {"bound": "hbm", "kernel": "q4_matvec", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": byts, "launch_ms": ms},
+        "gpu_launches": steps, "clocks": clocks, "cpu_baseline": cpu,
+    })
+    ctx.close()
+
+
+def run_gemm(args):
+    """Config 2: dense X bf16 [2048 x 2048] . W^T, W Q4 [5120 x 2048]; and the
+    grouped layer-major projection: 2048 tokens routed top-10 over 512
+    experts, gate W [512 x 2048] per expert (plan + gather + GEMM)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    M, N, Kd, NC = 2048, 5120, 2048, 24
+    flops = 2.0 * M * N * Kd
+    ctx = capi.Context(0)
+    ctx.prefill_reserve(20480, Kd)
+    g = synth.gen("cuda", 2002)
+    ws = [synth.q4_matrix(N, Kd, 64, g, "cuda") for _ in range(NC)]  # 142 MB of weights > L2
+    x = synth.normal_bf16((M, Kd), 1.0, g, "cuda")
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    s = torch.cuda.Stream()
+    calls = [(lambda w=w: ctx.q4_gemm(w[0], w[1], w[2], N, Kd, 64, x, y, stream=s)) for w in ws]
+    ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
+    tflops = flops / (ms / 1e3) / 1e12
+    hx = x.cpu().pin_memory()
+    hy = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(x)
+    it = [0]
+
+    def e2e():
+        w = ws[it[0] % NC]
+        it[0] += 1
+        dx.copy_(hx, non_blocking=True)
+        ctx.q4_gemm(w[0], w[1], w[2], N, Kd, 64, dx, y, stream=s)
+        hy.copy_(y, non_blocking=True)
+
+    ems = _e2e_time(e2e, s, min(args.steps, 2 * NC))
+    # grouped
+    E, TK, I = 512, 10, 512
+    layout = capi.fixed_q4_layout(Kd, I, 64)
+    table = synth.expert_table(E, layout, g, "cuda")
+    ids = synth.random_routes(M, E, TK, g, "cuda")
+    i32 = dict(device="cuda", dtype=torch.int32)
+    R = M * TK
+    se, un, sr, oi, gr_ = (torch.zeros(E, **i32), torch.zeros(1, **i32), torch.zeros(R, **i32),
+                           torch.zeros(R, **i32), torch.zeros(E, 2, **i32))
+    mat = capi.expert_matrix(table, layout, E, "gate")
+    yg = torch.empty(R, I, device="cuda", dtype=torch.bfloat16)
+    plan = lambda: ctx.prefill_group_plan(ids, M, TK, E, se, un, sr, oi, gr_, stream=s)
+    gemm_g = lambda: ctx.q4_gemm_grouped(mat, se, un, gr_, sr, R, E, x, yg, stream=s)
+    plan_ms, _, _ = _graph_time([plan], s, 200, 3)
+    g_ms, _, _ = _graph_time([gemm_g], s, 50, 3)
+    gflops = 2.0 * R * I * Kd
+    wbytes = E * (I * Kd // 2 + 2 * I * (Kd // 64) * 2)
+    peak, kind = measured_tensor_peak()
+    hbm, _ = measured_peaks()
+    cpu = None
+    try:
+        import numpy as np
+
+        from oracle import pb_oracle
+
+        pb_oracle.build()
+        w0 = [t.cpu() for t in ws[0]]
+        sn, bn = (synth.bf16_bits(t).numpy().view(np.uint16).reshape(-1) for t in (w0[1], w0[2]))
+        rows = 16
+        xs = x[:rows].float().cpu().numpy()
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        pb_oracle.q4_gemm(xs, w0[0].numpy().reshape(-1), sn, bn, N, Kd, 64, threads=threads)
+        dt = time.perf_counter() - t0
+        cpu = {"value": 2.0 * rows * N * Kd / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{rows} of the {M} token rows against the dense W (C++ oracle, {threads} threads)"}
+    except Exception as exc:
+        cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "port", "sample": f"failed: {exc}"}
+    _emit({
+        "metric": "prefill Q4 GEMM TFLOP/s (config 2 dense: X bf16 [2048x2048] . W Q4 [5120x2048]^T)",
+        "value": tflops, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded; config-2 distributions)",
+        "config": {"workload": "config2 prefill qGEMM", "m": M, "n": N, "k": Kd, "group": 64,
+                   "l2": f"inputs larger than L2: {NC} distinct weights cycled",
+                   "operands": "fp16 (w = q*s+b rounded once; bf16 x converted exactly), fp32 accumulate"},
+        "e2e": {"value": flops / (ems / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": M * Kd * 2,
+                "d2h_bytes_per_step": M * N * 2, "steps": min(args.steps, 2 * NC)},
+        "roofline": {"bound": "tensor", "kernel": "q4_umma_kernel (dense)", "achieved": tflops, "peak": peak,
+                     "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": kind, "traffic": None,
+                     "algorithmic_flops_per_launch": flops, "launch_ms": ms},
+        "grouped": {"routes": R, "experts": E, "projection": "gate [512x2048] per expert",
+                    "plan_ms": plan_ms, "gather_gemm_ms": g_ms, "tflops": gflops / (g_ms / 1e3) / 1e12,
+                    "weight_gbs": wbytes / (g_ms / 1e3) / 1e9, "weight_frac_of_hbm": wbytes / (g_ms / 1e3) / 1e9 / hbm},
+        "gpu_launches": steps * 2, "clocks": clocks, "cpu_baseline": cpu,
+    })
+    ctx.close()
+
+
+def run_mla(args):
+    """Config 3: MLA absorbed decode attention, 16 heads, nope 128, rope 64,
+    latent 512, v 128, bf16 cache; headline at L = 32768, batch 8 (two cache
+    sets cycled, 604 MB > L2), with the four (L, batch) cases listed."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    Hh, NOPE, ROPE, LAT, V = 16, 128, 64, 512, 128
+    ctx = capi.Context(0)
+    cfg = capi.mla_config()
+    ctx.mla_reserve(cfg, 32)
+    g = synth.gen("cuda", 3)
+    wuk = synth.normal_bf16((Hh, NOPE, LAT), 0.02, g, "cuda")
+    wuv = synth.normal_bf16((Hh, V, LAT), 0.02, g, "cuda")
+    s = torch.cuda.Stream()
+    cases, head = [], None
+    for L, B in ((4096, 1), (4096, 8), (32768, 1), (32768, 8)):
+        NC = max(2, min(16, (1 << 30) // (L * 1152 * B)))
+        sets = [([synth.normal_bf16((L, LAT), 1.0, g, "cuda") for _ in range(B)],
+                 [synth.normal_bf16((L, ROPE), 1.0, g, "cuda") for _ in range(B)]) for _ in range(NC)]
+        q = synth.normal_bf16((B, Hh, NOPE + ROPE), 1.0, g, "cuda")
+        out = torch.empty(B, Hh, V, device="cuda")
+        calls = [(lambda st=st: ctx.mla_decode(cfg, q, st[0], st[1], wuk, wuv, out, stream=s)) for st in sets]
+        steps = args.steps if (L, B) == (32768, 8) else 200
+        ms, n, clocks = _graph_time(calls, s, steps, args.warmup)
+        byts = B * L * (LAT + ROPE) * 2 + 2 * Hh * NOPE * LAT * 2
+        case = {"L": L, "batch": B, "us": ms * 1e3, "gbs": byts / (ms / 1e3) / 1e9}
+        cases.append(case)
+        if (L, B) == (32768, 8):
+            hq = q.cpu().pin_memory()
+            ho = torch.empty(B, Hh, V).pin_memory()
+            dq = torch.empty_like(q)
+
+            def e2e():
+                dq.copy_(hq, non_blocking=True)
+                ctx.mla_decode(cfg, dq, sets[0][0], sets[0][1], wuk, wuv, out, stream=s)
+                ho.copy_(out, non_blocking=True)
+
+            ems = _e2e_time(e2e, s, 50)
+            head = dict(ms=ms, steps=n, clocks=clocks, bytes=byts, e2e_ms=ems, B=B, L=L, NC=NC)
+        del sets
+        torch.cuda.empty_cache()
+    peak, kind = measured_peaks()
+    gbs = head["bytes"] / (head["ms"] / 1e3) / 1e9
+    _emit({
+        "metric": "MLA decode latent-cache GB/s (config 3: L=32768, batch 8)", "value": gbs, "unit": "GB/s",
+        "n_gpus": 1, "steps": head["steps"], "warmup": max(3, args.warmup), "ms_per_step": head["ms"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; config-3 distributions)",
+        "config": {"workload": "config3 MLA absorbed decode", "heads": Hh, "nope": NOPE, "rope": ROPE,
+                   "latent": LAT, "v": V, "L": head["L"], "batch": head["B"],
+                   "l2": f"inputs larger than L2: {head['NC']} cache sets cycled"},
+        "e2e": {"value": head["bytes"] / (head["e2e_ms"] / 1e3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": head["B"] * Hh * (NOPE + ROPE) * 2, "d2h_bytes_per_step": head["B"] * Hh * V * 4,
+                "steps": 50},
+        "roofline": {"bound": "hbm", "kernel": "mla decode (4 kernels)", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"]},
+        "cases": cases, "gpu_launches": head["steps"] * 4, "clocks": head["clocks"], "cpu_baseline": None,
+    })
+    ctx.close()
 
 
 def C_void_p_array(events):
