@@ -9,12 +9,32 @@
 // finished with warp shuffles. Shapes outside the fast path (cols % 32 != 0,
 // non power-of-two groups, unaligned rows) run a per-element kernel with the
 // reference's own per-element arithmetic.
+//
+// The fast and tensor-core kernels are launched with programmatic dependent
+// launch: a kernel issues its weight loads (which no earlier kernel writes),
+// lets the next kernel in the stream be scheduled and only then waits for its
+// predecessor (griddepcontrol.wait) before reading x or writing y, so
+// back-to-back matvecs stream weights without a gap between launches.
 
 #include "kernels.h"
 #include "q4_mma.cuh"
 #include "q4_rows.cuh"
 
 namespace pbmoe {
+
+static cudaError_t launch_with_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
 
 constexpr int kMvThreads = 128;
 constexpr int kMvRows = 4;  // rows per lane group per pass
@@ -47,6 +67,10 @@ q4_matvec_fast_kernel(const uint8_t* __restrict__ packed, const uint16_t* __rest
     for (uint32_t b0 = 0; b0 < batch; b0 += NT) {
         const int nt = static_cast<int>(min(batch - b0, static_cast<uint32_t>(NT)));
         frag.load(pk, ps, pb, g, 0);  // weights in flight while x is staged
+        if (b0 == 0) {
+            pdl_launch_dependents();
+            pdl_wait();
+        }
         __syncthreads();
         stage_x_fast<XT>(x + static_cast<size_t>(b0) * g.cols, g.cols, nullptr, nt, g.cols, xs, xe, xo);
         float acc[kMvRows][NT];
@@ -121,6 +145,8 @@ q4_matvec_mma_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restr
     const uint16_t* ba = biases + static_cast<size_t>(ra) * gpr;
     const uint32_t pair_gpr = (rb == ra + 1) ? gpr : 0;
     f.load(wrow, sa, ba, pair_gpr, grp0, t);
+    pdl_launch_dependents();
+    pdl_wait();
     for (uint32_t b0 = 0; b0 < batch; b0 += kPass) {
         const int nt = static_cast<int>(min(batch - b0, static_cast<uint32_t>(kPass)));
         __syncthreads();
@@ -175,7 +201,7 @@ static cudaError_t launch_mma_ks(const Q4MatvecArgs& a, cudaStream_t s) {
     const XT* x = static_cast<const XT*>(a.x);
     YT* y = static_cast<YT*>(a.y);
     void* args[] = {(void*)&p, (void*)&sc, (void*)&bi, (void*)&rows, (void*)&cols, (void*)&x, (void*)&y, (void*)&batch};
-    return cudaLaunchKernel(fn, grid, dim3(256), args, smem, s);
+    return launch_with_pdl(fn, grid, dim3(256), smem, s, args);
 }
 
 // Group-64 weights whose row length is a multiple of 256 columns.
@@ -198,16 +224,24 @@ static cudaError_t launch_fast(const Q4MatvecArgs& a, const Q4Geom& g, cudaStrea
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
     const dim3 grid((g.rows + kRowsPerCta - 1) / kRowsPerCta);
-    fn<<<grid, kMvThreads, smem, s>>>(a.packed, a.scales, a.biases, g, static_cast<const XT*>(a.x),
-                                      static_cast<YT*>(a.y), a.batch);
-    return cudaGetLastError();
+    const uint8_t* p = a.packed;
+    const uint16_t* sc = a.scales;
+    const uint16_t* bi = a.biases;
+    Q4Geom gg = g;
+    const XT* x = static_cast<const XT*>(a.x);
+    YT* y = static_cast<YT*>(a.y);
+    uint32_t batch = a.batch;
+    void* args[] = {(void*)&p, (void*)&sc, (void*)&bi, (void*)&gg, (void*)&x, (void*)&y, (void*)&batch};
+    return launch_with_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kMvThreads), smem, s, args);
 }
 
 template <typename XT, typename YT>
 static cudaError_t q4_matvec_launch_t(const Q4MatvecArgs& a, cudaStream_t s) {
     constexpr size_t kSmemLimit = 200 * 1024;
     const size_t xelem = a.x_dtype == PBMOE_BF16 ? 2 : 4;
-    if (a.group == kMmaGroup && a.cols % 256 == 0 && reinterpret_cast<uintptr_t>(a.packed) % 16 == 0 &&
+    // one or two tokens: the CUDA-core kernel (more weight bytes in flight per
+    // warp, one wave of CTAs); larger batches: the tensor-core kernel
+    if (a.batch > 2 && a.group == kMmaGroup && a.cols % 256 == 0 && reinterpret_cast<uintptr_t>(a.packed) % 16 == 0 &&
         reinterpret_cast<uintptr_t>(a.scales) % 8 == 0 && reinterpret_cast<uintptr_t>(a.biases) % 8 == 0 &&
         reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
         cudaError_t e = launch_mma<XT, YT>(a, s);
