@@ -52,6 +52,10 @@ DOWN_BYTES = 524_288 + 2 * 32_768
 ROUTER_BYTES = EXPERTS * HIDDEN * 2
 SHARED_GATE_BYTES = HIDDEN * 2
 METRIC = "MoE decode tok/s (config 1: one MoE FFN decode layer per step)"
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu --set
+# full capture of each kernel (profiles/ holds the summaries and commands)
+NCU_TRAFFIC = {"expert_gate_up": 95.2e6, "expert_down": 46.6e6, "router+topk": 2.2e6, "combine": 0.75e6}
+NCU_TRAFFIC_SOURCE = "ncu --set full, 4-layer config-1 case at B=8 (profiles/moe_decode_config1.md)"
 
 
 def parse():
@@ -465,7 +469,9 @@ def main():
                     "d2h_bytes_per_step": B * HIDDEN * 2, "steps": KE},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": None, "algorithmic_bytes_per_launch": kbytes[dominant],
+                         # DRAM read+write of one gate/up launch (ncu, config-1 shapes, B = 8)
+                         "traffic": NCU_TRAFFIC.get(dominant), "traffic_source": NCU_TRAFFIC_SOURCE,
+                         "algorithmic_bytes_per_launch": kbytes[dominant],
                          "launch_ms": mean_dur[dominant]},
             "layer": {"unique_experts_mean": mean_u, "algorithmic_bytes": layer_bytes,
                       "achieved_gbs": layer_bytes / (ms / K / 1e3) / 1e9,
@@ -681,7 +687,8 @@ def run_gemm(args):
         "e2e": {"value": flops / (ems / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": M * Kd * 2,
                 "d2h_bytes_per_step": M * N * 2, "steps": min(args.steps, 2 * NC)},
         "roofline": {"bound": "tensor", "kernel": "q4_umma_kernel (dense)", "achieved": tflops, "peak": peak,
-                     "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": kind, "traffic": None,
+                     "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": kind, "traffic": 17.6e6,
+                     "traffic_source": "ncu --set full, one dense launch (profiles/q4_gemm_config2_dense.md)",
                      "algorithmic_flops_per_launch": flops, "launch_ms": ms},
         "grouped": {"routes": R, "experts": E, "projection": "gate [512x2048] per expert",
                     "plan_ms": plan_ms, "gather_gemm_ms": g_ms, "tflops": gflops / (g_ms / 1e3) / 1e12,
