@@ -160,6 +160,11 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // Every other CTA has exited: let the expert kernel be scheduled now, so
+    // its prologue (barrier setup, activation staging) runs under this CTA's
+    // routing and plan; it reads the plan only after griddepcontrol.wait,
+    // i.e. after this grid completes.
+    pdl_launch_dependents();
 
     {
         const uint32_t Ep = (E + 3) & ~3u;
@@ -466,14 +471,18 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
         }
         __syncthreads();
     }
-    for (uint32_t c0 = threadIdx.x; c0 < H; c0 += kCombineEpt * blockDim.x) {
+    // without a next-layer norm or an exchange, CTA (t, y) takes columns
+    // [cb, ce) of the token, so several CTAs share each token's row
+    const uint32_t chunk = (H + gridDim.y - 1) / gridDim.y;
+    const uint32_t cb = blockIdx.y * chunk, ce = min(H, cb + chunk);
+    for (uint32_t c0 = cb + threadIdx.x; c0 < ce; c0 += kCombineEpt * blockDim.x) {
         float yv[KMAX][kCombineEpt];
         float sh[kCombineEpt], rv[kCombineEpt];
         if constexpr (!kEP) {
 #pragma unroll
             for (int i = 0; i < kCombineEpt; ++i) {
                 const uint32_t c = c0 + i * blockDim.x;
-                const bool in = c < H;
+                const bool in = c < ce;
 #pragma unroll
                 for (int k = 0; k < KMAX; ++k)
                     yv[k][i] = (in && static_cast<uint32_t>(k) < K && wsh[k] != 0.f)
@@ -485,7 +494,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
 #pragma unroll
         for (int i = 0; i < kCombineEpt; ++i) {
             const uint32_t c = c0 + i * blockDim.x;
-            rv[i] = (c < H && residual) ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
+            rv[i] = (c < ce && residual) ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
         }
 #pragma unroll
         for (int i = 0; i < kCombineEpt; ++i) {
@@ -494,7 +503,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
             if constexpr (kEP) {
                 // every rank's partial, in rank order (not cached: peers wrote it)
                 for (uint32_t src = 0; src < ep.world; ++src)
-                    if (c < H && !(missing & (1u << src))) moe += __ldcv(recv_row(ep.rank, src) + c);
+                    if (c < ce && !(missing & (1u << src))) moe += __ldcv(recv_row(ep.rank, src) + c);
             } else {
 #pragma unroll
                 for (int k = 0; k < KMAX; ++k)
@@ -503,7 +512,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
             }
             const float v = rv[i] + moe;
             keep[i] = v;
-            if (c < H) {
+            if (c < ce) {
                 store_act<OT>(out, static_cast<size_t>(t) * H + c, v);
                 ss += v * v;
                 if (norm_w) ws.y_tmp[static_cast<size_t>(t) * H + c] = v;
@@ -699,7 +708,12 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
             fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8, false>)
                  : K <= 16 ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 16, false>)
                            : reinterpret_cast<const void*>(moe_combine_kernel<OT, 32, false>);
-        if ((err = launch_pdl(fn, dim3(T), dim3(kCombineThreads), 0, s, args, pdl)) != cudaSuccess) return err;
+        // a row per CTA when the CTA must see the whole row (next-layer norm,
+        // peer exchange); else 256-column pieces over T x H/256 CTAs
+        const bool whole = nw != nullptr || a.ep != nullptr;
+        const uint32_t ysplit = whole ? 1u : (H + 255) / 256;
+        const dim3 block(whole ? kCombineThreads : 256);
+        if ((err = launch_pdl(fn, dim3(T, ysplit), block, 0, s, args, pdl)) != cudaSuccess) return err;
     }
     return mark(4);
 }
