@@ -140,18 +140,17 @@ MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t
     b[11] = R * 4;               // group_tokens
     b[12] = R * I * 4;           // h
     b[13] = R * H * 4;           // y
-    b[14] = size_t(T) * H * 4;   // y_tmp
-    b[15] = R * hperm_stride(I); // h_perm
+    b[14] = R * hperm_stride(I); // h_perm
     s.total = 0;
-    for (int i = 0; i < 16; ++i) s.total += align_up(b[i], 256);
+    for (int i = 0; i < 15; ++i) s.total += align_up(b[i], 256);
     return s;
 }
 
 MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
     MoeWsSizes s = moe_ws_sizes(T, E, K, H, I);
     char* p = static_cast<char*>(base);
-    void* ptr[16];
-    for (int i = 0; i < 16; ++i) {
+    void* ptr[15];
+    for (int i = 0; i < 15; ++i) {
         ptr[i] = p;
         p += align_up(s.bytes[i], 256);
     }
@@ -170,8 +169,7 @@ MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_
     w.group_tokens = static_cast<uint32_t*>(ptr[11]);
     w.h = static_cast<float*>(ptr[12]);
     w.y = static_cast<float*>(ptr[13]);
-    w.y_tmp = static_cast<float*>(ptr[14]);
-    w.h_perm = static_cast<uint8_t*>(ptr[15]);
+    w.h_perm = static_cast<uint8_t*>(ptr[14]);
     return w;
 }
 

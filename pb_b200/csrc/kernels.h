@@ -28,7 +28,6 @@ struct MoeWs {
     uint32_t* group_tokens;  // [T*K + T] token index per grouped position
     float* h;                // [(T*K + T) x I] SwiGLU activations per route
     float* y;                // [(T*K + T) x H] expert outputs per route
-    float* y_tmp;            // [T x H] combined hidden (f32) for the next-layer norm
     uint8_t* h_perm;         // [(T*K + T) x hperm_stride] SwiGLU activations as bf16 hi/lo pair
                              // slots + per-8 partial sums (input layout of the pipelined down kernel)
 };
@@ -51,12 +50,15 @@ struct MoeLayoutDev {
 };
 
 // Expert-parallel combine: every rank's exchange buffer ([2 parity][world]
-// [max_tokens][H] f32 partial outputs, then [world][max_tokens] u32 epoch
-// flags, then this rank's u32 epoch counter), addressed through peer pointers
+// [max_tokens][H] f32 partial outputs, then [world][max_tokens][pieces] u32
+// epoch flags, then this rank's u32 epoch counter), addressed through peer pointers
 // (this rank's own at index rank). The counter lives on the device and is
 // advanced once per layer by the router kernel, so captured CUDA graphs
 // replay with fresh epochs.
 constexpr uint32_t kMaxEpRanks = 8;
+// A token's row is combined in up to this many column pieces (one CTA each,
+// one thread-block cluster per token), each with its own exchange flag.
+constexpr uint32_t kCombinePieces = 8;
 struct EpPeers {
     float* recv[kMaxEpRanks];
     uint32_t* flags[kMaxEpRanks];
@@ -71,7 +73,7 @@ __host__ __device__ inline size_t ep_flags_offset(uint32_t world, uint32_t max_t
     return ep_recv_floats(world, max_tokens, H) * 4;
 }
 __host__ __device__ inline size_t ep_epoch_offset(uint32_t world, uint32_t max_tokens, uint32_t H) {
-    return (ep_flags_offset(world, max_tokens, H) + size_t(world) * max_tokens * 4 + 15) / 16 * 16;
+    return (ep_flags_offset(world, max_tokens, H) + size_t(world) * max_tokens * kCombinePieces * 4 + 15) / 16 * 16;
 }
 __host__ __device__ inline size_t ep_buffer_bytes(uint32_t world, uint32_t max_tokens, uint32_t H) {
     return ep_epoch_offset(world, max_tokens, H) + 16;
@@ -104,7 +106,7 @@ struct MoeLaunch {
 
 // Per-launch bytes of each workspace array, in MoeWs order (host arithmetic).
 struct MoeWsSizes {
-    size_t bytes[16];
+    size_t bytes[15];
     size_t total;
 };
 MoeWsSizes moe_ws_sizes(uint32_t max_tokens, uint32_t E, uint32_t K, uint32_t H, uint32_t I);

@@ -24,12 +24,16 @@
 // Kernels 2-4 are launched with programmatic dependent launch: each waits on
 // griddepcontrol.wait before touching its predecessor's outputs.
 
+#include <cooperative_groups.h>
+
 #include "kernels.h"
 #include "pipe.cuh"
 #include "q4_rows.cuh"
 #include "routing.cuh"
 
 namespace pbmoe {
+
+namespace cg = cooperative_groups;
 
 // ---------------------------------------------------------------- kernel 1
 constexpr int kRouterThreads = 256;
@@ -366,26 +370,47 @@ moe_expert_down_kernel(uint32_t E, const uint8_t* __restrict__ experts, const ui
 }
 
 // ---------------------------------------------------------------- kernel 4
-constexpr int kCombineThreads = 512;
-constexpr int kCombineEpt = 4;  // elements per thread per pass (H <= 2048 in one pass)
+constexpr int kCombineMaxThreads = 256;
+constexpr int kCombineVec = 4;  // float4 groups per thread: a piece is at most 4 * 256 * 4 columns
 
-// One CTA per token. The K routed outputs, the shared output and the
-// residual of a thread's elements are all requested before any arithmetic
-// (K <= KMAX, unrolled), then summed in slot order as the reference does.
-// Routes whose expert lies outside [e_lo, e_hi) belong to another rank and
-// are skipped (their y rows were not written).
-//
-// kEP: expert-parallel combine. The token's partial (local routes plus, on
-// the rank that holds it, the shared expert) goes to every rank's receive
-// buffer over peer memory (NVLink stores); after a CTA barrier thread 0
-// publishes it with a system-scope release of the epoch flag in each peer's
-// flag array. Threads 0..world-1 then wait, bounded, for every rank's flag
-// (acquire); the output is residual + the world partials summed in rank
-// order, identical on every rank. A wait that expires latches
-// PBMOE_DEV_ERR_PEER_TIMEOUT and the missing partial counts as zero.
-// Receive buffers alternate by epoch parity: a rank can run at most one layer
-// ahead of another (its next partial waits for everyone's flags), so the
-// parity a rank writes is never the one a slower rank is still reading.
+template <typename T>
+__device__ __forceinline__ float4 load_act4(const T* p, size_t i);
+template <>
+__device__ __forceinline__ float4 load_act4<float>(const float* p, size_t i) {
+    return *reinterpret_cast<const float4*>(p + i);
+}
+template <>
+__device__ __forceinline__ float4 load_act4<uint16_t>(const uint16_t* p, size_t i) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p + i);
+    return make_float4(bf16_bits_to_f32(u.x & 0xffffu), bf16_bits_to_f32(u.x >> 16), bf16_bits_to_f32(u.y & 0xffffu),
+                       bf16_bits_to_f32(u.y >> 16));
+}
+template <typename T>
+__device__ __forceinline__ void store_act4(T* p, size_t i, float4 v);
+template <>
+__device__ __forceinline__ void store_act4<float>(float* p, size_t i, float4 v) {
+    *reinterpret_cast<float4*>(p + i) = v;
+}
+template <>
+__device__ __forceinline__ void store_act4<uint16_t>(uint16_t* p, size_t i, float4 v) {
+    uint2 u;
+    u.x = f32_to_bf16_bits(v.x) | (static_cast<uint32_t>(f32_to_bf16_bits(v.y)) << 16);
+    u.y = f32_to_bf16_bits(v.z) | (static_cast<uint32_t>(f32_to_bf16_bits(v.w)) << 16);
+    *reinterpret_cast<uint2*>(p + i) = u;
+}
+__device__ __forceinline__ void fma4(float4& a, float w, const float4& b) {
+    a.x += w * b.x;
+    a.y += w * b.y;
+    a.z += w * b.z;
+    a.w += w * b.w;
+}
+__device__ __forceinline__ void add4(float4& a, const float4& b) {
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+}
+
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -395,13 +420,35 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
+// CTA (t, y) combines columns [y*piece, (y+1)*piece) of token t, four
+// consecutive columns per thread (float4). Per element the K routed outputs
+// (weighted, in slot order) and the gated shared output are summed as the
+// reference does, then the residual is added. Routes whose expert lies
+// outside [e_lo, e_hi) belong to another rank and are skipped (their y rows
+// were not written). With a next-layer norm the token's pieces form one
+// thread-block cluster: each CTA's sum of squares is read by every CTA of the
+// cluster over distributed shared memory, in piece order.
+//
+// kEP: expert-parallel combine. A CTA's partial (local routes plus, on the
+// rank that holds it, the shared expert) goes to every other rank's receive
+// buffer over peer memory (16-byte NVLink stores); after a CTA barrier
+// thread 0 publishes it with a system-scope release of the epoch flag of
+// (rank, token, piece) in each peer's flag array. Threads 0..world-1 then
+// wait, bounded, for every rank's flag of this piece (acquire); the output is
+// residual + the world partials summed in rank order, identical on every
+// rank. A wait that expires latches PBMOE_DEV_ERR_PEER_TIMEOUT and the
+// missing partial counts as zero. Receive buffers alternate by epoch parity:
+// a rank can run at most one layer ahead of another (its next partial waits
+// for everyone's flags), so the parity a rank writes is never the one a
+// slower rank is still reading.
 template <typename OT, int KMAX, bool kEP>
-__global__ void __launch_bounds__(kCombineThreads)
+__global__ void __launch_bounds__(kCombineMaxThreads)
 moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_gate, const OT* __restrict__ residual,
                    OT* __restrict__ out, const float* __restrict__ norm_w, OT* __restrict__ next_normed, float eps,
-                   uint32_t e_lo, uint32_t e_hi, MoeWs ws, EpPeers ep) {
-    __shared__ float red[32];
+                   uint32_t e_lo, uint32_t e_hi, uint32_t piece, MoeWs ws, EpPeers ep) {
+    __shared__ float red[kCombineMaxThreads / 32];
     __shared__ float wsh[KMAX];
+    __shared__ float piece_ss;
     __shared__ uint32_t missing;
     const uint32_t t = blockIdx.x;
     pdl_wait();
@@ -416,49 +463,54 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     __syncthreads();
     const float* yt = ws.y + static_cast<size_t>(t) * K * H;
     const float* ysh = ws.y + (static_cast<size_t>(T) * K + t) * H;
-    float ss = 0.f;
-    float keep[kCombineEpt];
-    const uint32_t epoch = kEP ? __ldcg(ep.epoch) : 0u;
-    const uint32_t par = epoch & 1u;
-    auto recv_row = [&](uint32_t rank_buf, uint32_t src) {  // partial of `src` in rank `rank_buf`'s buffer
-        return ep.recv[rank_buf] + ((static_cast<size_t>(par) * ep.world + src) * ep.max_tokens + t) * H;
-    };
+    const uint32_t cb = blockIdx.y * piece, ce = min(H, cb + piece);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v[kCombineVec];
+#pragma unroll
+    for (int j = 0; j < kCombineVec; ++j) {
+        const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
+        float4 acc = zero;
+        if (c < ce) {
+            float4 yv[KMAX];
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k)
+                yv[k] = (static_cast<uint32_t>(k) < K && wsh[k] != 0.f)
+                            ? __ldcg(reinterpret_cast<const float4*>(yt + static_cast<size_t>(k) * H + c))
+                            : zero;
+            const float4 sh = has_shared ? __ldcg(reinterpret_cast<const float4*>(ysh + c)) : zero;
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k)
+                if (static_cast<uint32_t>(k) < K) fma4(acc, wsh[k], yv[k]);
+            fma4(acc, sw, sh);
+        }
+        v[j] = acc;
+    }
     if constexpr (kEP) {
-        // 1. this rank's partial to every rank
-        for (uint32_t c0 = threadIdx.x; c0 < H; c0 += kCombineEpt * blockDim.x) {
-            float yv[KMAX][kCombineEpt], sh[kCombineEpt];
+        const uint32_t epoch = __ldcg(ep.epoch);
+        const uint32_t par = epoch & 1u;
+        auto recv_row = [&](uint32_t rank_buf, uint32_t src) {  // partial of `src` in rank `rank_buf`'s buffer
+            return ep.recv[rank_buf] + ((static_cast<size_t>(par) * ep.world + src) * ep.max_tokens + t) * H;
+        };
+        auto flag = [&](uint32_t rank_buf, uint32_t src) {
+            return ep.flags[rank_buf] + (static_cast<size_t>(src) * ep.max_tokens + t) * kCombinePieces + blockIdx.y;
+        };
+        // 1. this rank's partial to every other rank
 #pragma unroll
-            for (int i = 0; i < kCombineEpt; ++i) {
-                const uint32_t c = c0 + i * blockDim.x;
-                const bool in = c < H;
-#pragma unroll
-                for (int k = 0; k < KMAX; ++k)
-                    yv[k][i] = (in && static_cast<uint32_t>(k) < K && wsh[k] != 0.f)
-                                   ? __ldcg(yt + static_cast<size_t>(k) * H + c)
-                                   : 0.f;
-                sh[i] = (in && has_shared) ? __ldcg(ysh + c) : 0.f;
-            }
-#pragma unroll
-            for (int i = 0; i < kCombineEpt; ++i) {
-                const uint32_t c = c0 + i * blockDim.x;
-                float moe = 0.f;
-#pragma unroll
-                for (int k = 0; k < KMAX; ++k)
-                    if (static_cast<uint32_t>(k) < K) moe += wsh[k] * yv[k][i];
-                const float part = moe + sw * sh[i];
-                if (c < H)
-                    for (uint32_t d = 0; d < ep.world; ++d) recv_row(d, ep.rank)[c] = part;
-            }
+        for (int j = 0; j < kCombineVec; ++j) {
+            const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
+            if (c < ce)
+                for (uint32_t d = 0; d < ep.world; ++d)
+                    if (d != ep.rank) *reinterpret_cast<float4*>(recv_row(d, ep.rank) + c) = v[j];
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
+        if (threadIdx.x == 0 && ep.world > 1) {
             __threadfence_system();
             for (uint32_t d = 0; d < ep.world; ++d)
-                st_release_sys(ep.flags[d] + static_cast<size_t>(ep.rank) * ep.max_tokens + t, epoch);
+                if (d != ep.rank) st_release_sys(flag(d, ep.rank), epoch);
         }
-        // 2. every rank's partial of this token has landed here
-        if (threadIdx.x < ep.world) {
-            const uint32_t* f = ep.flags[ep.rank] + static_cast<size_t>(threadIdx.x) * ep.max_tokens + t;
+        // 2. every rank's partial of this piece has landed here
+        if (threadIdx.x < ep.world && threadIdx.x != ep.rank) {
+            const uint32_t* f = flag(ep.rank, threadIdx.x);
             const uint64_t t0 = global_ns();
             while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
                 if (global_ns() - t0 > ep.timeout_ns) {
@@ -470,77 +522,57 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
             }
         }
         __syncthreads();
+        // every rank's partial in rank order (peer data not cached: peers wrote it)
+#pragma unroll
+        for (int j = 0; j < kCombineVec; ++j) {
+            const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
+            float4 m = zero;
+            if (c < ce)
+                for (uint32_t src = 0; src < ep.world; ++src) {
+                    if (src == ep.rank)
+                        add4(m, v[j]);
+                    else if (!(missing & (1u << src)))
+                        add4(m, __ldcv(reinterpret_cast<const float4*>(recv_row(ep.rank, src) + c)));
+                }
+            v[j] = m;
+        }
     }
-    // without a next-layer norm or an exchange, CTA (t, y) takes columns
-    // [cb, ce) of the token, so several CTAs share each token's row
-    const uint32_t chunk = (H + gridDim.y - 1) / gridDim.y;
-    const uint32_t cb = blockIdx.y * chunk, ce = min(H, cb + chunk);
-    for (uint32_t c0 = cb + threadIdx.x; c0 < ce; c0 += kCombineEpt * blockDim.x) {
-        float yv[KMAX][kCombineEpt];
-        float sh[kCombineEpt], rv[kCombineEpt];
-        if constexpr (!kEP) {
+    float ss = 0.f;
 #pragma unroll
-            for (int i = 0; i < kCombineEpt; ++i) {
-                const uint32_t c = c0 + i * blockDim.x;
-                const bool in = c < ce;
-#pragma unroll
-                for (int k = 0; k < KMAX; ++k)
-                    yv[k][i] = (in && static_cast<uint32_t>(k) < K && wsh[k] != 0.f)
-                                   ? __ldcg(yt + static_cast<size_t>(k) * H + c)
-                                   : 0.f;
-                sh[i] = (in && has_shared) ? __ldcg(ysh + c) : 0.f;
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kCombineEpt; ++i) {
-            const uint32_t c = c0 + i * blockDim.x;
-            rv[i] = (c < ce && residual) ? load_act<OT>(residual, static_cast<size_t>(t) * H + c) : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < kCombineEpt; ++i) {
-            const uint32_t c = c0 + i * blockDim.x;
-            float moe = 0.f;
-            if constexpr (kEP) {
-                // every rank's partial, in rank order (not cached: peers wrote it)
-                for (uint32_t src = 0; src < ep.world; ++src)
-                    if (c < ce && !(missing & (1u << src))) moe += __ldcv(recv_row(ep.rank, src) + c);
-            } else {
-#pragma unroll
-                for (int k = 0; k < KMAX; ++k)
-                    if (static_cast<uint32_t>(k) < K) moe += wsh[k] * yv[k][i];
-                moe += sw * sh[i];
-            }
-            const float v = rv[i] + moe;
-            keep[i] = v;
-            if (c < ce) {
-                store_act<OT>(out, static_cast<size_t>(t) * H + c, v);
-                ss += v * v;
-                if (norm_w) ws.y_tmp[static_cast<size_t>(t) * H + c] = v;
-            }
+    for (int j = 0; j < kCombineVec; ++j) {
+        const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
+        if (c < ce) {
+            float4 o = residual ? load_act4<OT>(residual, static_cast<size_t>(t) * H + c) : zero;
+            add4(o, v[j]);
+            store_act4<OT>(out, static_cast<size_t>(t) * H + c, o);
+            ss += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+            v[j] = o;
         }
     }
     if (!norm_w) return;
+    // the token's sum of squares: warps, then the CTA, then the cluster
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) red[0] = v;
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (uint32_t w = 0; w < blockDim.x / 32; ++w) s += red[w];
+        piece_ss = s;
     }
-    __syncthreads();
-    const float scale = 1.0f / sqrtf(red[0] / static_cast<float>(H) + eps);
-    if (H <= kCombineEpt * blockDim.x) {
-        // one pass: the values are still in registers
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    float tot = 0.f;
+    for (uint32_t r = 0; r < gridDim.y; ++r) tot += *cluster.map_shared_rank(&piece_ss, r);
+    cluster.sync();  // no CTA leaves while another still reads its piece_ss
+    const float scale = 1.0f / sqrtf(tot / static_cast<float>(H) + eps);
 #pragma unroll
-        for (int i = 0; i < kCombineEpt; ++i) {
-            const uint32_t c = threadIdx.x + i * blockDim.x;
-            if (c < H) store_act<OT>(next_normed, static_cast<size_t>(t) * H + c, keep[i] * scale * norm_w[c]);
-        }
-    } else {
-        for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
-            const float v = ws.y_tmp[static_cast<size_t>(t) * H + c];
-            store_act<OT>(next_normed, static_cast<size_t>(t) * H + c, v * scale * norm_w[c]);
+    for (int j = 0; j < kCombineVec; ++j) {
+        const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
+        if (c < ce) {
+            const float4 nw = *reinterpret_cast<const float4*>(norm_w + c);
+            store_act4<OT>(next_normed, static_cast<size_t>(t) * H + c,
+                           make_float4(v[j].x * scale * nw.x, v[j].y * scale * nw.y, v[j].z * scale * nw.z,
+                                       v[j].w * scale * nw.w));
         }
     }
 }
@@ -696,9 +728,6 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         EpPeers ep{};
         if (a.ep) ep = *a.ep;
         uint32_t lo = e_lo, hi = e_hi;
-        void* args[] = {(void*)&T,   (void*)&H,   (void*)&K,   (void*)&has_shared, (void*)&has_gate,
-                        (void*)&res, (void*)&out, (void*)&nw,  (void*)&nn,         (void*)&eps,
-                        (void*)&lo,  (void*)&hi,  (void*)&ws,  (void*)&ep};
         const void* fn;
         if (a.ep)
             fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8, true>)
@@ -708,12 +737,40 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
             fn = K <= 8    ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 8, false>)
                  : K <= 16 ? reinterpret_cast<const void*>(moe_combine_kernel<OT, 16, false>)
                            : reinterpret_cast<const void*>(moe_combine_kernel<OT, 32, false>);
-        // a row per CTA when the CTA must see the whole row (next-layer norm,
-        // peer exchange); else 256-column pieces over T x H/256 CTAs
-        const bool whole = nw != nullptr || a.ep != nullptr;
-        const uint32_t ysplit = whole ? 1u : (H + 255) / 256;
-        const dim3 block(whole ? kCombineThreads : 256);
-        if ((err = launch_pdl(fn, dim3(T, ysplit), block, 0, s, args, pdl)) != cudaSuccess) return err;
+        // T x Y CTAs of `piece` columns each; with a next-layer norm the Y
+        // pieces of a token form one cluster (row-wide sum of squares)
+        uint32_t Y = (H + 255) / 256;
+        if (Y > kCombinePieces) Y = kCombinePieces;
+        uint32_t piece = ((H + Y - 1) / Y + 3) & ~3u;
+        Y = (H + piece - 1) / piece;
+        const uint32_t vecs = piece / 4;
+        uint32_t threads = vecs < static_cast<uint32_t>(kCombineMaxThreads) ? (vecs + 31) & ~31u
+                                                                            : static_cast<uint32_t>(kCombineMaxThreads);
+        if ((H & 3u) != 0 || vecs > threads * kCombineVec) return cudaErrorInvalidValue;
+        void* args[] = {(void*)&T,   (void*)&H,   (void*)&K,     (void*)&has_shared, (void*)&has_gate,
+                        (void*)&res, (void*)&out, (void*)&nw,    (void*)&nn,         (void*)&eps,
+                        (void*)&lo,  (void*)&hi,  (void*)&piece, (void*)&ws,         (void*)&ep};
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(T, Y);
+        cfg.blockDim = dim3(threads);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[2];
+        unsigned na = 0;
+        if (pdl) {
+            attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[na].val.programmaticStreamSerializationAllowed = 1;
+            ++na;
+        }
+        if (nw) {
+            attr[na].id = cudaLaunchAttributeClusterDimension;
+            attr[na].val.clusterDim.x = 1;
+            attr[na].val.clusterDim.y = Y;
+            attr[na].val.clusterDim.z = 1;
+            ++na;
+        }
+        cfg.attrs = attr;
+        cfg.numAttrs = na;
+        if ((err = cudaLaunchKernelExC(&cfg, fn, args)) != cudaSuccess) return err;
     }
     return mark(4);
 }
