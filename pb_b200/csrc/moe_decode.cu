@@ -414,11 +414,12 @@ __device__ __forceinline__ void add4(float4& a, const float4& b) {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
     uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // CTA (t, y) combines columns [y*piece, (y+1)*piece) of token t, four
 // consecutive columns per thread (float4). Per element the K routed outputs
@@ -432,9 +433,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // kEP: expert-parallel combine. A CTA's partial (local routes plus, on the
 // rank that holds it, the shared expert) goes to every other rank's receive
 // buffer over peer memory (16-byte NVLink stores); after a CTA barrier
-// thread 0 publishes it with a system-scope release of the epoch flag of
-// (rank, token, piece) in each peer's flag array. Threads 0..world-1 then
-// wait, bounded, for every rank's flag of this piece (acquire); the output is
+// thread d publishes it with a system-scope release of the epoch flag of
+// (rank, token, piece) in rank d's flag array, then waits, bounded, for rank
+// d's flag of this piece (relaxed polling, then an acquire fence); the output is
 // residual + the world partials summed in rank order, identical on every
 // rank. A wait that expires latches PBMOE_DEV_ERR_PEER_TIMEOUT and the
 // missing partial counts as zero. Receive buffers alternate by epoch parity:
@@ -503,16 +504,14 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
                     if (d != ep.rank) *reinterpret_cast<float4*>(recv_row(d, ep.rank) + c) = v[j];
         }
         __syncthreads();
-        if (threadIdx.x == 0 && ep.world > 1) {
-            __threadfence_system();
-            for (uint32_t d = 0; d < ep.world; ++d)
-                if (d != ep.rank) st_release_sys(flag(d, ep.rank), epoch);
-        }
-        // 2. every rank's partial of this piece has landed here
+        // 2. thread d (d != rank) publishes to rank d and then waits for rank
+        // d's partial of this piece: one system-scope release and one acquire
+        // fence per peer, all peers in parallel
         if (threadIdx.x < ep.world && threadIdx.x != ep.rank) {
+            st_release_sys(flag(threadIdx.x, ep.rank), epoch);
             const uint32_t* f = flag(ep.rank, threadIdx.x);
             const uint64_t t0 = global_ns();
-            while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
+            while (static_cast<int32_t>(ld_relaxed_sys(f) - epoch) < 0) {
                 if (global_ns() - t0 > ep.timeout_ns) {
                     atomicOr(&missing, 1u << threadIdx.x);
                     if (ws.status) atomicOr(ws.status, PBMOE_DEV_ERR_PEER_TIMEOUT);
@@ -520,6 +519,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
                 }
                 __nanosleep(64);
             }
+            fence_acq_rel_sys();
         }
         __syncthreads();
         // every rank's partial in rank order (peer data not cached: peers wrote it)
