@@ -48,7 +48,7 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
                   const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
                   uint32_t* ep_epoch, MoeWs ws) {
     extern __shared__ __align__(16) float smem[];
-    float* xs = smem;  // [kRouterTokPass][H]
+    XT* xs = reinterpret_cast<XT*>(smem);  // [kRouterTokPass][H], in x's own type
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t nrows = E + (shared_gate_w ? 1u : 0u);
     const uint32_t row0 = (blockIdx.x * (kRouterThreads / 32) + warp) * kRouterRowsPerWarp;
@@ -73,33 +73,22 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     for (uint32_t t0 = 0; t0 < T; t0 += kRouterTokPass) {
         const uint32_t nt = min(T - t0, static_cast<uint32_t>(kRouterTokPass));
         __syncthreads();
-        {  // stage x: every 16-byte load issued before any store
+        {  // stage x (a copy): every 16-byte load issued before any store
             constexpr uint32_t kPerVec = 16 / sizeof(XT);
             const uint32_t vpr = H / kPerVec, total = nt * vpr;
+            const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0) * H);
+            uint4* dst = reinterpret_cast<uint4*>(xs);
             for (uint32_t base = 0; base < total; base += 8 * blockDim.x) {
                 uint4 v[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const uint32_t idx = base + i * blockDim.x + threadIdx.x;
-                    if (idx < total)
-                        v[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0) * H +
-                                                               static_cast<size_t>(idx) * kPerVec);
+                    if (idx < total) v[i] = src[idx];
                 }
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const uint32_t idx = base + i * blockDim.x + threadIdx.x;
-                    if (idx < total) {
-                        float4* d = reinterpret_cast<float4*>(xs + static_cast<size_t>(idx) * kPerVec);
-                        if constexpr (sizeof(XT) == 2) {
-                            d[0] = make_float4(__uint_as_float(v[i].x << 16), __uint_as_float(v[i].x & 0xffff0000u),
-                                               __uint_as_float(v[i].y << 16), __uint_as_float(v[i].y & 0xffff0000u));
-                            d[1] = make_float4(__uint_as_float(v[i].z << 16), __uint_as_float(v[i].z & 0xffff0000u),
-                                               __uint_as_float(v[i].w << 16), __uint_as_float(v[i].w & 0xffff0000u));
-                        } else {
-                            d[0] = make_float4(__uint_as_float(v[i].x), __uint_as_float(v[i].y),
-                                               __uint_as_float(v[i].z), __uint_as_float(v[i].w));
-                        }
-                    }
+                    if (idx < total) dst[idx] = v[i];
                 }
             }
         }
@@ -124,8 +113,18 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
 #pragma unroll
                     for (int t = 0; t < kRouterTokPass; ++t) {
                         if (static_cast<uint32_t>(t) < nt) {
-                            const float4* xp = reinterpret_cast<const float4*>(xs + t * H + v * 8);
-                            const float4 a = xp[0], b = xp[1];
+                            float4 a, b;
+                            if constexpr (sizeof(XT) == 2) {  // bf16: one 16-byte read, widened exactly
+                                const uint4 q = *reinterpret_cast<const uint4*>(xs + t * H + v * 8);
+                                a = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
+                                                __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
+                                b = make_float4(__uint_as_float(q.z << 16), __uint_as_float(q.z & 0xffff0000u),
+                                                __uint_as_float(q.w << 16), __uint_as_float(q.w & 0xffff0000u));
+                            } else {
+                                const float4* xp = reinterpret_cast<const float4*>(xs + t * H + v * 8);
+                                a = xp[0];
+                                b = xp[1];
+                            }
                             acc[t] = fmaf(wf[0], a.x, acc[t]);
                             acc[t] = fmaf(wf[1], a.y, acc[t]);
                             acc[t] = fmaf(wf[2], a.z, acc[t]);

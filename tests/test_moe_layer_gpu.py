@@ -249,6 +249,32 @@ def test_route_ties_and_specials(ctx, oracle):
     assert st == 0
 
 
+@pytest.mark.parametrize("k", [1, 2, 10, 16, 32])
+def test_route_selection_paths(ctx, oracle, k):
+    """Rows that take the parallel selection (distinct scores, at most 64
+    insertions) and rows that fall back to the replay (ties among inserted
+    scores, ascending scores with one insertion per expert), all bit-exact."""
+    rng = np.random.default_rng(500 + k)
+    E = 512
+    rows = [rng.standard_normal(E) for _ in range(6)]
+    rows.append(np.sort(rng.standard_normal(E)))  # every expert inserted
+    rows.append(np.sort(rng.standard_normal(E))[::-1])  # only the first k inserted
+    rows.append(np.round(rng.standard_normal(E) * 4))  # ties
+    r = rng.standard_normal(E)
+    r[::7] = np.nan
+    r[3::11] = -np.inf
+    rows.append(r)  # NaN and -inf are never inserted
+    bf = rng.standard_normal(E).astype(np.float32).view(np.uint32) & 0xFFFF0000
+    rows.append(bf.view(np.float32))  # bf16-valued scores
+    rows.append(np.linspace(-1.0, 1.0, E) + rng.standard_normal(E) * 0.05)  # drifting upwards
+    lg = np.stack(rows).astype(np.float32)
+    ids, w, st = _route(ctx, lg, k)
+    rid, rw = _oracle_route(oracle, lg, k)
+    assert np.array_equal(ids, rid)
+    assert_close(w, rw, tol=1e-5, what="weights")
+    assert st == 0
+
+
 def test_route_all_neg_inf_latches_error(ctx):
     """All -inf logits: the reference bails on the selected-probability sum;
     the kernel latches PBMOE_DEV_ERR_ROUTE_WEIGHTS."""
