@@ -397,6 +397,48 @@ PBMOE_API int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config,
                                  void* out, pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
                                  void* next_normed, void* stream);
 
+/* ---------------------------------------------------------------- vocab head
+ * The LM head of sample_from_hidden (runtime/generation.rs:2200-2227):
+ * lm_head_raw_top_candidates_with_metal(_masked) (weights/store.rs:1622-1680)
+ * -> MetalResidentTopKBuilder::execute_with_allowed_tokens / encode_and_read
+ * (metal/mod.rs:2661-2800), i.e. the resident bf16 projection
+ * (dense_mmap_fma_matvec_bf16, shaders.metal:1059-1075) and topk_vocab
+ * (shaders.metal:1796-1831), for up to 32 tokens per call.
+ *
+ * A head may be one vocabulary shard: rows [0, vocab) of `weight` are the
+ * global token ids [id_base, id_base + vocab). */
+typedef struct pbmoe_head {
+    const uint16_t* weight; /* bf16 [vocab x hidden], device */
+    uint32_t vocab;
+    uint32_t hidden; /* a multiple of 512 */
+    uint32_t id_base;
+} pbmoe_head;
+
+/* Workspace for pbmoe_head_topk: logits and per-slice candidate lists for
+ * up to max_tokens tokens (<= 32), vocab rows and top_k <= max_top_k (<= 256). */
+PBMOE_API int pbmoe_head_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, uint32_t vocab, uint32_t max_top_k);
+
+/* Per token t: logits = weight . x[t] (f32 accumulate), then the top_k
+ * candidates in topk_vocab order: value descending, the lower token id first
+ * among equal values, non-finite logits as -inf, tokens whose bit in
+ * `allowed` (device bitmask over global ids, or NULL for all) is clear never
+ * chosen, and slots past the allowed tokens (0, -inf). The reference first
+ * clamps top_k to the vocabulary (execute_with_allowed_tokens); here top_k is
+ * the row length of the outputs, slots past vocab being (0, -inf).
+ * out_ids/out_values [tokens x top_k] device. out_keys (optional, [tokens x
+ * top_k] u32) receives the candidates' ordering keys for pbmoe_head_merge;
+ * out_logits (optional, [tokens x vocab] f32) receives the logits. */
+PBMOE_API int pbmoe_head_topk(pbmoe_ctx* ctx, const pbmoe_head* head, const void* x, pbmoe_dtype x_dtype,
+                              uint32_t tokens, uint32_t top_k, const uint32_t* allowed, uint32_t* out_ids,
+                              float* out_values, uint32_t* out_keys, float* out_logits, void* stream);
+
+/* Merge the candidate lists of `lists` vocabulary shards (keys/ids/values as
+ * [lists][tokens][top_k], shards in id order, e.g. gathered from every rank)
+ * into each token's final top_k (out_ids/out_values [tokens x top_k]). */
+PBMOE_API int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint32_t* ids, const float* values,
+                               uint32_t lists, uint32_t tokens, uint32_t top_k, uint32_t* out_ids,
+                               float* out_values, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -681,4 +681,38 @@ int oracle_q4_gemm(const float* x, size_t m, const uint8_t* packed, const uint16
     return kOk;
 }
 
+// topk_vocab (shaders.metal:1796-1831), the LM-head candidate selection of
+// MetalResidentTopKBuilder (metal/mod.rs:2661-2800): min(top_k, vocab) passes;
+// each takes the first allowed index not chosen by an earlier pass, replaced
+// by a later one only when strictly greater; a non-finite logit counts as
+// -inf; a pass with no allowed index left writes (0, -inf). `allowed` is a
+// bitmask over the vocabulary or null. Returns the number of passes. The
+// shader's "already used" scan over earlier outputs is a bitmap here (the
+// same predicate).
+size_t oracle_topk_vocab(const float* logits, size_t vocab, size_t top_k, const uint32_t* allowed, uint32_t* ids,
+                         float* vals) {
+    const size_t limit = std::min(top_k, vocab);
+    const float neg_inf = -std::numeric_limits<float>::infinity();
+    std::vector<char> used(vocab, 0);
+    for (size_t out = 0; out < limit; ++out) {
+        float best = neg_inf;
+        uint32_t best_i = 0;
+        bool found = false;
+        for (size_t i = 0; i < vocab; ++i) {
+            if (allowed && ((allowed[i >> 5] >> (i & 31)) & 1u) == 0) continue;
+            const float raw = logits[i];
+            const float value = std::isfinite(raw) ? raw : neg_inf;
+            if (!used[i] && (!found || value > best)) {
+                best = value;
+                best_i = static_cast<uint32_t>(i);
+                found = true;
+            }
+        }
+        ids[out] = best_i;
+        vals[out] = best;
+        if (found) used[best_i] = 1;
+    }
+    return limit;
+}
+
 }  // extern "C"

@@ -86,6 +86,8 @@ def _declare(L):
         _sz, _sz, _sz, _sz, _sz, _f32p,
     ]
     L.oracle_q4_gemm.argtypes = [_f32p, _sz, _u8p, _u16p, _u16p, _sz, _sz, _sz, _f32p, C.c_int]
+    L.oracle_topk_vocab.restype = _sz
+    L.oracle_topk_vocab.argtypes = [_f32p, _sz, _sz, C.c_void_p, _u32p, _f32p]
 
 
 def _c(a, dtype):
@@ -311,3 +313,26 @@ def mla_absorbed_attention_q4(query, latents, rotary, eq, uo, heads, nope, rope,
         _c(uo[0], np.uint8), _c(uo[1], np.uint16), _c(uo[2], np.uint16), uo[3], heads, nope, rope, latent,
         v_dim, out), "mla_absorbed_attention_q4")
     return out
+
+
+# ---------------------------------------------------------------- vocab head
+def topk_vocab(logits, top_k, allowed=None):
+    """topk_vocab on one token's logits: (ids, values) of min(top_k, vocab) passes."""
+    lg = _c(logits, np.float32)
+    n = min(int(top_k), lg.size)
+    ids = np.zeros(max(n, 1), np.uint32)
+    vals = np.zeros(max(n, 1), np.float32)
+    al = None if allowed is None else _c(allowed, np.uint32)
+    lib().oracle_topk_vocab(lg, lg.size, int(top_k), None if al is None else al.ctypes.data, ids, vals)
+    return ids[:n], vals[:n]
+
+
+def head_topk(weight_bits, x, top_k, allowed=None):
+    """LM-head candidates per token: dense bf16 projection (fma in column
+    order) then topk_vocab. Returns (ids [T, n], values [T, n], logits [T, V])."""
+    w = _c(weight_bits, np.uint16)
+    V, H = w.shape
+    xs = np.atleast_2d(np.asarray(x, np.float32))
+    logits = np.stack([dense_bf16_matvec(w, row, V, H) for row in xs])
+    res = [topk_vocab(row, top_k, allowed) for row in logits]
+    return np.stack([r[0] for r in res]), np.stack([r[1] for r in res]), logits

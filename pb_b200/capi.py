@@ -43,7 +43,7 @@ EXPORTED = [
     "pbmoe_route_topk", "pbmoe_moe_layer", "pbmoe_moe_layer_static", "pbmoe_mla_reserve", "pbmoe_mla_decode",
     "pbmoe_prefill_reserve", "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
     "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
-    "pbmoe_ep_buffer", "pbmoe_ep_moe_layer",
+    "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -95,6 +95,10 @@ class EpShard(C.Structure):
     _fields_ = [("expert_begin", C.c_uint32), ("expert_count", C.c_uint32), ("timeout_us", C.c_uint32)]
 
 
+class Head(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("vocab", C.c_uint32), ("hidden", C.c_uint32), ("id_base", C.c_uint32)]
+
+
 class PbmoeError(RuntimeError):
     def __init__(self, code, message):
         super().__init__(f"pbmoe status {code}: {message}")
@@ -144,6 +148,9 @@ def load():
         L.pbmoe_ep_buffer.argtypes = [vp]
         L.pbmoe_ep_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), C.POINTER(EpShard), vp, i32,
                                          vp, vp, i32, u32, vp, vp, vp]
+        L.pbmoe_head_reserve.argtypes = [vp, u32, u32, u32]
+        L.pbmoe_head_topk.argtypes = [vp, C.POINTER(Head), vp, i32, u32, u32, vp, vp, vp, vp, vp, vp]
+        L.pbmoe_head_merge.argtypes = [vp, vp, vp, vp, u32, u32, u32, vp, vp, vp]
         _lib = L
     return _lib
 
@@ -248,6 +255,22 @@ class Context:
         args = MlaArgs(b, C.cast(lens, C.c_void_p), query.data_ptr(), _dtype_code(query), C.cast(ckv, C.c_void_p),
                        C.cast(kr, C.c_void_p), w_uk.data_ptr(), w_uv.data_ptr(), out.data_ptr(), _dtype_code(out))
         self.check(self.lib.pbmoe_mla_decode(self.h, C.byref(config), C.byref(args), self.stream_ptr(stream)))
+
+    def head_reserve(self, max_tokens, vocab, max_top_k):
+        self.check(self.lib.pbmoe_head_reserve(self.h, max_tokens, vocab, max_top_k))
+
+    def head_topk(self, weight, x, ids, values, id_base=0, allowed=None, keys=None, logits=None, stream=None):
+        """weight bf16 [vocab, hidden]; x [tokens, hidden] bf16/f32; ids/values [tokens, top_k]."""
+        head = Head(weight.data_ptr(), int(weight.shape[0]), int(weight.shape[1]), id_base)
+        self.check(self.lib.pbmoe_head_topk(self.h, C.byref(head), _ptr(x), _dtype_code(x), int(x.shape[0]),
+                                            int(ids.shape[1]), _ptr(allowed), _ptr(ids), _ptr(values), _ptr(keys),
+                                            _ptr(logits), self.stream_ptr(stream)))
+
+    def head_merge(self, keys, ids, values, out_ids, out_values, stream=None):
+        """keys/ids/values [lists, tokens, top_k] (shards in id order) -> out [tokens, top_k]."""
+        lists, tokens, top_k = (int(d) for d in keys.shape)
+        self.check(self.lib.pbmoe_head_merge(self.h, _ptr(keys), _ptr(ids), _ptr(values), lists, tokens, top_k,
+                                             _ptr(out_ids), _ptr(out_values), self.stream_ptr(stream)))
 
     def prefill_reserve(self, max_rows, max_cols):
         self.check(self.lib.pbmoe_prefill_reserve(self.h, max_rows, max_cols))

@@ -27,6 +27,9 @@ struct pbmoe_ctx {
     uint32_t ep_rank = 0, ep_world = 0, ep_max_tokens = 0, ep_hidden = 0;
     void* ep_peer[pbmoe::kMaxEpRanks] = {};
     bool ep_peer_ipc[pbmoe::kMaxEpRanks] = {};  // mapped through CUDA IPC (closed at destroy)
+    void* head_base = nullptr;  // vocab head: logits, slice candidates, key scratch
+    size_t head_bytes = 0;
+    uint32_t head_tokens = 0, head_vocab = 0, head_k = 0;
     int num_sms = 0;
     std::string last_error;
 };
@@ -215,6 +218,7 @@ int pbmoe_destroy(pbmoe_ctx* ctx) {
         if (ctx->ws_base) cudaFree(ctx->ws_base);
         if (ctx->mla_base) cudaFree(ctx->mla_base);
         if (ctx->x16_base) cudaFree(ctx->x16_base);
+        if (ctx->head_base) cudaFree(ctx->head_base);
         for (uint32_t r = 0; r < pbmoe::kMaxEpRanks; ++r)
             if (ctx->ep_peer_ipc[r]) cudaIpcCloseMemHandle(ctx->ep_peer[r]);
         if (ctx->ep_base) cudaFree(ctx->ep_base);
@@ -840,4 +844,131 @@ int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_mo
     ep.timeout_ns = shard->timeout_us ? uint64_t(shard->timeout_us) * 1000ull : 2000000000ull;
     return moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
                           nullptr, stream, shard->expert_begin, shard->expert_count, &ep);
+}
+
+// ---------------------------------------------------------------- vocab head
+namespace {
+struct HeadWs {
+    float* logits;
+    uint32_t *cand_key, *cand_id;
+    float* cand_val;
+    uint32_t* key_scratch;
+};
+size_t head_ws_bytes(uint32_t T, uint32_t V, uint32_t K, HeadWs* carve, void* base) {
+    const size_t S = pbmoe::head_slices(V);
+    const size_t sizes[5] = {size_t(T) * V * 4, size_t(T) * S * K * 4, size_t(T) * S * K * 4, size_t(T) * S * K * 4,
+                             size_t(T) * K * 4};
+    size_t off = 0;
+    void* ptr[5];
+    for (int i = 0; i < 5; ++i) {
+        ptr[i] = base ? static_cast<char*>(base) + off : nullptr;
+        off += (sizes[i] + 255) / 256 * 256;
+    }
+    if (carve) {
+        carve->logits = static_cast<float*>(ptr[0]);
+        carve->cand_key = static_cast<uint32_t*>(ptr[1]);
+        carve->cand_id = static_cast<uint32_t*>(ptr[2]);
+        carve->cand_val = static_cast<float*>(ptr[3]);
+        carve->key_scratch = static_cast<uint32_t*>(ptr[4]);
+    }
+    return off;
+}
+}  // namespace
+
+int pbmoe_head_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, uint32_t vocab, uint32_t max_top_k) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (max_tokens == 0 || max_tokens > 32 || vocab == 0 || max_top_k == 0 || max_top_k > 256)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head reserve: tokens %u (1..32), vocab %u, top_k %u (1..256)",
+                    max_tokens, vocab, max_top_k);
+    if (pbmoe::head_slices(vocab) * max_top_k > 8192)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported head top-k: %u slices x top_k %u exceed 8192",
+                    pbmoe::head_slices(vocab), max_top_k);
+    if (ctx->head_base && ctx->head_tokens >= max_tokens && ctx->head_vocab >= vocab && ctx->head_k >= max_top_k)
+        return PBMOE_OK;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    if (ctx->head_base) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before head workspace resize");
+        cudaFree(ctx->head_base);
+        ctx->head_base = nullptr;
+    }
+    const size_t bytes = head_ws_bytes(max_tokens, vocab, max_top_k, nullptr, nullptr);
+    cudaError_t e = cudaMalloc(&ctx->head_base, bytes);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "head workspace allocation");
+    ctx->head_bytes = bytes;
+    ctx->head_tokens = max_tokens;
+    ctx->head_vocab = vocab;
+    ctx->head_k = max_top_k;
+    return PBMOE_OK;
+}
+
+int pbmoe_head_topk(pbmoe_ctx* ctx, const pbmoe_head* head, const void* x, pbmoe_dtype x_dtype, uint32_t tokens,
+                    uint32_t top_k, const uint32_t* allowed, uint32_t* out_ids, float* out_values, uint32_t* out_keys,
+                    float* out_logits, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!head || !head->weight || !x || !out_ids || !out_values)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head top-k: null pointer");
+    if (x_dtype != PBMOE_BF16 && x_dtype != PBMOE_F32)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head top-k: x must be bf16 or f32");
+    if (tokens == 0) return PBMOE_OK;
+    if (top_k == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head top-k: top_k must be positive");
+    if (!pbmoe::head_supported(head->vocab, head->hidden, tokens, top_k))
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported head top-k: vocab %u, hidden %u (a multiple of 512), tokens %u (<= 32), "
+                    "top_k %u (<= 256, slices x top_k <= 8192)", head->vocab, head->hidden, tokens, top_k);
+    if (!ctx->head_base || ctx->head_tokens < tokens || ctx->head_vocab < head->vocab || ctx->head_k < top_k)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "head top-k: %u tokens x vocab %u x top_k %u need pbmoe_head_reserve",
+                    tokens, head->vocab, top_k);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    HeadWs w;
+    head_ws_bytes(tokens, head->vocab, top_k, &w, ctx->head_base);
+    pbmoe::HeadArgs a{};
+    a.weight = head->weight;
+    a.vocab = head->vocab;
+    a.hidden = head->hidden;
+    a.id_base = head->id_base;
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.tokens = tokens;
+    a.top_k = top_k;
+    a.allowed = allowed;
+    a.logits = w.logits;
+    a.cand_key = w.cand_key;
+    a.cand_id = w.cand_id;
+    a.cand_val = w.cand_val;
+    a.out_key = out_keys ? out_keys : w.key_scratch;
+    a.out_id = out_ids;
+    a.out_val = out_values;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = pbmoe::head_topk_launch(a, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "head top-k launch");
+    if (out_logits) {
+        e = cudaMemcpyAsync(out_logits, w.logits, size_t(tokens) * head->vocab * 4, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "head logits copy");
+    }
+    return PBMOE_OK;
+}
+
+int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint32_t* ids, const float* values, uint32_t lists,
+                     uint32_t tokens, uint32_t top_k, uint32_t* out_ids, float* out_values, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!keys || !ids || !values || !out_ids || !out_values)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head merge: null pointer");
+    if (tokens == 0) return PBMOE_OK;
+    if (lists == 0 || top_k == 0 || top_k > 256 || size_t(lists) * top_k > 8192)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported head merge: %u lists x top_k %u", lists, top_k);
+    if (!ctx->head_base || ctx->head_tokens < tokens || ctx->head_k < top_k)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "head merge: %u tokens x top_k %u need pbmoe_head_reserve", tokens,
+                    top_k);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    HeadWs w;
+    head_ws_bytes(ctx->head_tokens, ctx->head_vocab, ctx->head_k, &w, ctx->head_base);
+    // [lists][tokens][top_k]: token stride top_k, list stride tokens x top_k
+    cudaError_t e = pbmoe::head_merge_launch(keys, ids, values, tokens, lists, top_k, size_t(tokens) * top_k, top_k,
+                                             w.key_scratch, out_ids, out_values, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "head merge launch");
+    return PBMOE_OK;
 }

@@ -233,4 +233,34 @@ struct PrefillPlanArgs {
 size_t prefill_plan_smem(uint32_t num_experts);
 cudaError_t prefill_plan_launch(const PrefillPlanArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- vocab head (head.cu)
+// logits[t][v] = W[v] . x[t] for the rows [0, vocab) of a (possibly sharded)
+// head whose row 0 is global token id `id_base`, then each token's top_k
+// candidates (key, id, value) in topk_vocab order. Candidate lists of several
+// shards are merged by head_merge_launch.
+struct HeadArgs {
+    const uint16_t* weight;  // bf16 [vocab x hidden]
+    uint32_t vocab, hidden, id_base;
+    const void* x;  // [tokens x hidden]
+    pbmoe_dtype x_dtype;
+    uint32_t tokens, top_k;
+    const uint32_t* allowed;  // bitmask over global ids, or null
+    float* logits;            // [tokens x vocab] workspace (zeroed here)
+    uint32_t* cand_key;       // [tokens x slices x top_k] workspace
+    uint32_t* cand_id;
+    float* cand_val;
+    uint32_t* out_key;  // [tokens x top_k]
+    uint32_t* out_id;
+    float* out_val;
+};
+uint32_t head_slices(uint32_t vocab);
+bool head_supported(uint32_t vocab, uint32_t hidden, uint32_t tokens, uint32_t top_k);
+cudaError_t head_topk_launch(const HeadArgs& a, cudaStream_t s);
+// merge `lists` candidate lists of top_k per token (entry r of list l for
+// token t at t * tok_stride + l * list_stride + r; lists in id order) into
+// the final [tokens x top_k]
+cudaError_t head_merge_launch(const uint32_t* in_key, const uint32_t* in_id, const float* in_val, uint32_t tokens,
+                              uint32_t lists, size_t tok_stride, size_t list_stride, uint32_t top_k,
+                              uint32_t* out_key, uint32_t* out_id, float* out_val, cudaStream_t s);
+
 }  // namespace pbmoe

@@ -121,7 +121,7 @@ __device__ __forceinline__ float float_from_order_key(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-__device__ void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
+__device__ inline void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
                                  float routed_scale, uint32_t* ids_out, float* w_out, uint32_t* status) {
     const int lane = threadIdx.x & 31;
     const float NEG_INF = -__int_as_float(0x7f800000);
@@ -192,7 +192,7 @@ __device__ void route_token_smem(const float* s, uint32_t E, uint32_t K, uint32_
 
 // Block-wide exclusive scan of n <= 4096 u32 values in shared memory, in
 // place; returns the total. Uses `tmp` (>= 32 words of shared memory).
-__device__ uint32_t block_exclusive_scan(uint32_t* a, uint32_t n, uint32_t* tmp) {
+__device__ inline uint32_t block_exclusive_scan(uint32_t* a, uint32_t n, uint32_t* tmp) {
     const uint32_t tid = threadIdx.x, nt = blockDim.x;
     const uint32_t per = (n + nt - 1) / nt;
     const uint32_t lo = tid * per, hi = min(lo + per, n);
