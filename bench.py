@@ -66,8 +66,9 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla"],
-                   help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3")
+    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla", "head"],
+                   help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3; "
+                        "head: config 4's vocab head + top-k")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -241,7 +242,7 @@ def main():
         run_reference(args)
         return
     if args.workload != "moe":
-        {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla}[args.workload](args)
+        {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla, "head": run_head}[args.workload](args)
         return
     import numpy as np
     import torch
@@ -758,6 +759,62 @@ def run_mla(args):
                      "frac": gbs / peak, "peak_kind": kind, "traffic": None,
                      "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"]},
         "cases": cases, "gpu_launches": head["steps"] * 4, "clocks": head["clocks"], "cpu_baseline": None,
+    })
+    ctx.close()
+
+
+def run_head(args):
+    """Config 4's vocab head: logits = W x for W bf16 [151936 x 2048] (622 MB
+    > L2, read once per call) and top-64 candidates per token (topk_vocab
+    order); headline at --batch tokens (1, 8 and 32 listed)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    V, H, K = 151936, 2048, 64
+    ctx = capi.Context(0)
+    ctx.head_reserve(32, V, K)
+    w = synth.normal_bf16((V, H), 0.02, synth.gen("cuda", 4), "cuda")
+    s = torch.cuda.Stream()
+    cases, head = [], None
+    for B in (1, 8, 32):
+        x = synth.normal_bf16((B, H), 1.0, synth.gen("cuda", 40 + B), "cuda")
+        ids = torch.empty(B, K, dtype=torch.int32, device="cuda")
+        vals = torch.empty(B, K, device="cuda")
+        call = lambda x=x, ids=ids, vals=vals: ctx.head_topk(w, x, ids, vals, stream=s)
+        steps = args.steps if B == args.batch else 100
+        ms, n, clocks = _graph_time([call], s, steps, args.warmup)
+        byts = V * H * 2 + B * H * 2 + B * K * 8
+        cases.append({"batch": B, "us": ms * 1e3, "gbs": byts / (ms / 1e3) / 1e9, "tok_s": B / (ms / 1e3)})
+        if B == args.batch:
+            hx = x.cpu().pin_memory()
+            hi = torch.empty(B, K, dtype=torch.int32).pin_memory()
+            hv = torch.empty(B, K).pin_memory()
+            dx = torch.empty_like(x)
+
+            def e2e():
+                dx.copy_(hx, non_blocking=True)
+                ctx.head_topk(w, dx, ids, vals, stream=s)
+                hi.copy_(ids, non_blocking=True)
+                hv.copy_(vals, non_blocking=True)
+
+            ems = _e2e_time(e2e, s, 100)
+            head = dict(ms=ms, steps=n, clocks=clocks, bytes=byts, e2e_ms=ems, B=B)
+    peak, kind = measured_peaks()
+    gbs = head["bytes"] / (head["ms"] / 1e3) / 1e9
+    _emit({
+        "metric": f"vocab head GB/s (config 4 LM head [151936x2048] bf16 + top-{K}, batch {head['B']})",
+        "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": head["steps"], "warmup": max(3, args.warmup),
+        "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded; head weight ~N(0,0.02), x ~N(0,1))",
+        "config": {"workload": "config4 vocab head + topk_vocab", "vocab": V, "hidden": H, "top_k": K,
+                   "batch": head["B"], "l2": "inputs larger than L2: the 622 MB head is read once per call"},
+        "e2e": {"value": head["bytes"] / (head["e2e_ms"] / 1e3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": head["B"] * H * 2, "d2h_bytes_per_step": head["B"] * K * 8, "steps": 100},
+        "roofline": {"bound": "hbm", "kernel": "head (memset + gemv + 2 select)", "achieved": gbs, "peak": peak,
+                     "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"]},
+        "cases": cases, "gpu_launches": head["steps"] * 3, "clocks": head["clocks"], "cpu_baseline": None,
     })
     ctx.close()
 

@@ -880,8 +880,8 @@ int pbmoe_head_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, uint32_t vocab, uint
     if (max_tokens == 0 || max_tokens > 32 || vocab == 0 || max_top_k == 0 || max_top_k > 256)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head reserve: tokens %u (1..32), vocab %u, top_k %u (1..256)",
                     max_tokens, vocab, max_top_k);
-    if (pbmoe::head_slices(vocab) * max_top_k > 8192)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported head top-k: %u slices x top_k %u exceed 8192",
+    if (pbmoe::head_slices(vocab) * max_top_k > 24576)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported head top-k: %u slices x top_k %u exceed 24576",
                     pbmoe::head_slices(vocab), max_top_k);
     if (ctx->head_base && ctx->head_tokens >= max_tokens && ctx->head_vocab >= vocab && ctx->head_k >= max_top_k)
         return PBMOE_OK;
@@ -916,7 +916,7 @@ int pbmoe_head_topk(pbmoe_ctx* ctx, const pbmoe_head* head, const void* x, pbmoe
     if (!pbmoe::head_supported(head->vocab, head->hidden, tokens, top_k))
         return fail(ctx, PBMOE_ERR_UNSUPPORTED,
                     "FlashMoe unsupported head top-k: vocab %u, hidden %u (a multiple of 512), tokens %u (<= 32), "
-                    "top_k %u (<= 256, slices x top_k <= 8192)", head->vocab, head->hidden, tokens, top_k);
+                    "top_k %u (<= 256, slices of 2048 x top_k <= 24576)", head->vocab, head->hidden, tokens, top_k);
     if (!ctx->head_base || ctx->head_tokens < tokens || ctx->head_vocab < head->vocab || ctx->head_k < top_k)
         return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "head top-k: %u tokens x vocab %u x top_k %u need pbmoe_head_reserve",
                     tokens, head->vocab, top_k);
@@ -957,7 +957,7 @@ int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint32_t* ids, 
     if (!keys || !ids || !values || !out_ids || !out_values)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "head merge: null pointer");
     if (tokens == 0) return PBMOE_OK;
-    if (lists == 0 || top_k == 0 || top_k > 256 || size_t(lists) * top_k > 8192)
+    if (lists == 0 || top_k == 0 || top_k > 256 || size_t(lists) * top_k > 24576 || lists + top_k - 1 > 512)
         return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported head merge: %u lists x top_k %u", lists, top_k);
     if (!ctx->head_base || ctx->head_tokens < tokens || ctx->head_k < top_k)
         return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "head merge: %u tokens x top_k %u need pbmoe_head_reserve", tokens,

@@ -11,20 +11,20 @@
 // each lane loads 32 contiguous bytes of its row per 64-column step (four
 // lanes cover one 128-byte line), and the 16 columns of each mma are a fixed
 // permutation of the step's columns, applied identically to the activations.
-// Activations are f32 values split into bf16 hi + lo halves in shared memory
-// (two mma per fragment), so the products keep ~16 significant bits of x and
-// exactly the bf16 weight. The CTA's grid row is one half of H (blockIdx.y):
+// f32 activations are split into bf16 hi + lo halves in shared memory (two
+// mma per fragment), so the products keep ~16 significant bits of x and
+// exactly the bf16 weight; bf16 activations are exact as one half. The CTA's grid row is one half of H (blockIdx.y):
 // the two halves add into zeroed logits with f32 atomics, and a sum of two
 // terms onto zero is the same in either order, so logits are deterministic.
 //
-// Kernel 2, head_select_kernel: per (token, slice of 8192 logits) an exact
+// Kernel 2, head_select_kernel: per (token, slice of 2048 logits) an exact
 // top-k by radix selection of the k-th largest value key, then the selected
 // entries sorted by (value desc, index asc): topk_vocab's order, where a
 // non-finite logit counts as -inf, a disallowed token is never chosen, and
-// slots beyond the allowed tokens are (0, -inf). The same kernel merges the
-// slices' lists (and the lists of vocabulary shards held by other ranks):
-// lists are concatenated in index order and equal keys keep list order, which
-// is index order.
+// slots beyond the allowed tokens are (0, -inf). Kernel 3, head_merge_kernel,
+// merges the slices' sorted lists (and the lists of vocabulary shards held by
+// other ranks): lists are concatenated in index order, so equal keys keep
+// list order, which is index order.
 
 #include "kernels.h"
 #include "q4_mma.cuh"
@@ -45,6 +45,8 @@ template <int NT, typename XT>
 __global__ void __launch_bounds__(kHeadThreads, 1)
 head_gemv_kernel(const uint16_t* __restrict__ W, uint32_t V, uint32_t H, const XT* __restrict__ x, uint32_t T,
                  float* __restrict__ logits) {
+    // bf16 activations are exact in bf16: their lo half is zero and skipped
+    constexpr bool kLo = sizeof(XT) == 4;
     extern __shared__ __align__(16) uint8_t hsm[];
     const uint32_t Hh = H / 2;
     const uint32_t k0 = blockIdx.y * Hh;  // this CTA's half of the columns
@@ -64,7 +66,7 @@ head_gemv_kernel(const uint16_t* __restrict__ W, uint32_t V, uint32_t H, const X
         const uint16_t l0 = f32_to_bf16_bits(v0 - bf16_bits_to_f32(h0));
         const uint16_t l1 = f32_to_bf16_bits(v1 - bf16_bits_to_f32(h1));
         *reinterpret_cast<uint32_t*>(xhi + tok * rb + c * 2) = h0 | (static_cast<uint32_t>(h1) << 16);
-        *reinterpret_cast<uint32_t*>(xlo + tok * rb + c * 2) = l0 | (static_cast<uint32_t>(l1) << 16);
+        if constexpr (kLo) *reinterpret_cast<uint32_t*>(xlo + tok * rb + c * 2) = l0 | (static_cast<uint32_t>(l1) << 16);
     }
     __syncthreads();
 
@@ -109,17 +111,22 @@ head_gemv_kernel(const uint16_t* __restrict__ W, uint32_t V, uint32_t H, const X
                     const uint32_t tok = n * 8 + g;
                     const uint4 h0 = *reinterpret_cast<const uint4*>(xhi + tok * rb + cbyte);
                     const uint4 h1 = *reinterpret_cast<const uint4*>(xhi + tok * rb + cbyte + 16);
-                    const uint4 l0 = *reinterpret_cast<const uint4*>(xlo + tok * rb + cbyte);
-                    const uint4 l1 = *reinterpret_cast<const uint4*>(xlo + tok * rb + cbyte + 16);
                     const uint32_t xh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-                    const uint32_t xl[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+                    uint32_t xl[8] = {};
+                    if constexpr (kLo) {
+                        const uint4 l0 = *reinterpret_cast<const uint4*>(xlo + tok * rb + cbyte);
+                        const uint4 l1 = *reinterpret_cast<const uint4*>(xlo + tok * rb + cbyte + 16);
+                        xl[0] = l0.x, xl[1] = l0.y, xl[2] = l0.z, xl[3] = l0.w;
+                        xl[4] = l1.x, xl[5] = l1.y, xl[6] = l1.z, xl[7] = l1.w;
+                    }
                     // mma `sub`: logical k 2tq+j <-> column 16tq+4sub+j, 2tq+8+j <-> 16tq+4sub+2+j
 #pragma unroll
                     for (int sub = 0; sub < 4; ++sub) {
                         mma_bf16_16816(acc[n], wa[2 * sub], wb[2 * sub], wa[2 * sub + 1], wb[2 * sub + 1],
                                        xh[2 * sub], xh[2 * sub + 1]);
-                        mma_bf16_16816(acc[n], wa[2 * sub], wb[2 * sub], wa[2 * sub + 1], wb[2 * sub + 1],
-                                       xl[2 * sub], xl[2 * sub + 1]);
+                        if constexpr (kLo)
+                            mma_bf16_16816(acc[n], wa[2 * sub], wb[2 * sub], wa[2 * sub + 1], wb[2 * sub + 1],
+                                           xl[2 * sub], xl[2 * sub + 1]);
                     }
                 }
             }
@@ -141,8 +148,10 @@ head_gemv_kernel(const uint16_t* __restrict__ W, uint32_t V, uint32_t H, const X
 }
 
 // ---------------------------------------------------------------- selection
-constexpr int kSelThreads = 512;
-constexpr uint32_t kSelSlice = 8192;  // logits per CTA of the first pass
+constexpr int kSelThreads = 256;
+constexpr uint32_t kSelSlice = 2048;      // logits per CTA of the first pass
+constexpr uint32_t kMergeMax = 24576;     // candidates per token in a merge (lists x k)
+constexpr uint32_t kMergeSort = 512;      // candidates at or above the bound sorted directly
 
 // Candidate key: 0 = no candidate (a disallowed token, or a slot past the
 // allowed tokens), else the order key of the value (non-finite as -inf) + 1.
@@ -151,40 +160,28 @@ __device__ __forceinline__ uint32_t head_value_key(float v) {
     return float_order_key(v) + 1u;
 }
 
-// One CTA selects the top `k` of n entries (key, id, value) by (key desc,
-// position asc) and writes them sorted; positions past the entries get
-// (key 0, id 0, -inf). Source: logits row (ids = id_base + position, keys
-// from the values and the allowed-token bitmask) when `logits` is set, else
-// candidate lists (in_key/in_id/in_val; position p is entry p % k of list
-// p / k, at t * in_tok_stride + (p / k) * in_list_stride + p % k). Keys live
-// in shared memory (kSelSlice u32), then the selected entries.
+// CTA (t, y) selects the top `k` of slice y of token t's logits (ids =
+// id_base + position, keys from the values and the allowed-token bitmask) by
+// (key desc, position asc) and writes them sorted as the slice's list;
+// positions past the slice get (key 0, id 0, -inf). Keys live in shared
+// memory (kSelSlice u32), then the selected entries.
 __global__ void __launch_bounds__(kSelThreads)
 head_select_kernel(const float* __restrict__ logits, size_t logits_stride, uint32_t id_base,
-                   const uint32_t* __restrict__ allowed, const uint32_t* __restrict__ in_key,
-                   const uint32_t* __restrict__ in_id, const float* __restrict__ in_val, size_t in_tok_stride,
-                   size_t in_list_stride, uint32_t n,
-                   uint32_t k, uint32_t* __restrict__ out_key, uint32_t* __restrict__ out_id,
-                   float* __restrict__ out_val, size_t out_stride) {
+                   const uint32_t* __restrict__ allowed, uint32_t n, uint32_t k, uint32_t* __restrict__ out_key,
+                   uint32_t* __restrict__ out_id, float* __restrict__ out_val, size_t out_stride) {
     __shared__ uint32_t keys[kSelSlice];
     __shared__ uint32_t hist[256];
     __shared__ unsigned long long sel[kHeadMaxSelect];  // (key << 32) | ~position, sorted descending
     __shared__ uint32_t scan_tmp[32];
-    __shared__ uint32_t s_prefix, s_rem, s_gt;
+    __shared__ uint32_t s_prefix, s_rem, s_gt, s_eq;
     const uint32_t t = blockIdx.x;
     const uint32_t base = blockIdx.y * kSelSlice;  // first position of this CTA's slice
     if (base >= n) return;
     const uint32_t m = min(kSelSlice, n - base);
     for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
-        const uint32_t p = base + i;
-        uint32_t key;
-        if (logits) {
-            const uint32_t id = id_base + p;
-            const bool ok = !allowed || ((allowed[id >> 5] >> (id & 31)) & 1u);
-            key = ok ? head_value_key(logits[t * logits_stride + p]) : 0u;
-        } else {
-            key = in_key[t * in_tok_stride + (p / k) * in_list_stride + p % k];
-        }
-        keys[i] = key;
+        const uint32_t id = id_base + base + i;
+        const bool ok = !allowed || ((allowed[id >> 5] >> (id & 31)) & 1u);
+        keys[i] = ok ? head_value_key(logits[t * logits_stride + base + i]) : 0u;
     }
     const uint32_t want = min(k, m);
     if (threadIdx.x == 0) {
@@ -236,6 +233,7 @@ head_select_kernel(const float* __restrict__ logits, size_t logits_stride, uint3
                 }
                 s_prefix = prefix | (static_cast<uint32_t>(255 - 8 * lane - j) << shift);
                 s_rem = rem - above;
+                s_eq = c[j];  // after the last pass: the keys equal to the threshold
             }
         }
         pmask |= 255u << shift;
@@ -246,17 +244,19 @@ head_select_kernel(const float* __restrict__ logits, size_t logits_stride, uint3
     const uint32_t n_gt = want - need_eq;
     if (threadIdx.x == 0) s_gt = 0;
     __syncthreads();
-    // entries above the threshold (any order; sorted below)
+    // entries above the threshold, and the equal ones too when all of them
+    // are taken (any order; sorted below)
+    const bool all_eq = s_eq == need_eq;
     for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
         const uint32_t key = keys[i];
-        if (key > thr) {
+        if (key > thr || (all_eq && key == thr)) {
             const uint32_t slot = atomicAdd(&s_gt, 1u);
             sel[slot] = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(~(base + i));
         }
     }
-    // entries equal to the threshold: the need_eq lowest positions (each
+    // otherwise the need_eq lowest positions among the equal ones (each
     // thread scans a contiguous range, ranks from a block scan)
-    {
+    if (!all_eq) {
         const uint32_t per = (m + blockDim.x - 1) / blockDim.x;
         const uint32_t lo = threadIdx.x * per, hi = min(lo + per, m);
         uint32_t cnt = 0;
@@ -321,15 +321,9 @@ head_select_kernel(const float* __restrict__ logits, size_t logits_stride, uint3
             key = static_cast<uint32_t>(e >> 32);
             const uint32_t p = ~static_cast<uint32_t>(e);
             if (key) {
-                if (logits) {
-                    id = id_base + p;
-                    const float v = logits[t * logits_stride + p];
-                    val = isfinite(v) ? v : val;
-                } else {
-                    const size_t q = t * in_tok_stride + (p / k) * in_list_stride + p % k;
-                    id = in_id[q];
-                    val = in_val[q];
-                }
+                id = id_base + p;
+                const float v = logits[t * logits_stride + p];
+                val = isfinite(v) ? v : val;
             }
         }
         out_key[o + r] = key;
@@ -338,25 +332,128 @@ head_select_kernel(const float* __restrict__ logits, size_t logits_stride, uint3
     }
 }
 
+// Merge of sorted candidate lists: entry r of list l of token t sits at
+// t * tok_stride + l * list_stride + r; every list is sorted by (key desc,
+// id asc) and the lists cover increasing id ranges, so (key, position l*k+r)
+// orders entries exactly as (key desc, id asc). The k-th largest of any
+// subset of the union is a lower bound of the union's k-th; the subset taken
+// is the first ceil(k / lists) entries of every list (>= k entries, <= k +
+// lists), sorted once. Only entries at or above that bound can be selected
+// (typically little more than k): they are gathered and sorted directly.
+// When more than kMergeSort entries are at or above it, an entry's rank in
+// the union is counted instead: r plus, per other list, a binary search for
+// the entries ordering before it; ranks below k are written in place.
+__global__ void __launch_bounds__(kSelThreads)
+head_merge_kernel(const uint32_t* __restrict__ in_key, const uint32_t* __restrict__ in_id,
+                  const float* __restrict__ in_val, size_t tok_stride, size_t list_stride, uint32_t lists,
+                  uint32_t k, uint32_t* __restrict__ out_key, uint32_t* __restrict__ out_id,
+                  float* __restrict__ out_val) {
+    extern __shared__ unsigned long long comp[];  // [lists x k]: (key << 32) | ~position
+    __shared__ unsigned long long cand[kMergeSort];  // the bound's subset, then the entries at or above it
+    __shared__ unsigned long long s_bound;
+    __shared__ uint32_t s_cnt;
+    const uint32_t t = blockIdx.x, n = lists * k;
+    for (uint32_t p = threadIdx.x; p < n; p += blockDim.x) {
+        const uint32_t l = p / k, r = p - l * k;
+        const uint32_t key = in_key[t * tok_stride + l * list_stride + r];
+        comp[p] = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(~p);
+    }
+    if (threadIdx.x == 0) s_cnt = 0;
+    // the bound: k-th largest of the first m entries of every list
+    const uint32_t m = (k + lists - 1) / lists;
+    const uint32_t sub = m * lists;  // <= k + lists - 1 <= kMergeSort (host check)
+    auto bitonic_desc = [&](uint32_t cnt) {  // sorts cand[0, cnt) descending; pads with 0
+        uint32_t P = 1;
+        while (P < cnt) P <<= 1;
+        for (uint32_t i = cnt + threadIdx.x; i < P; i += blockDim.x) cand[i] = 0ull;
+        __syncthreads();
+        for (uint32_t size = 2; size <= P; size <<= 1) {
+            for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+                for (uint32_t i = threadIdx.x; i < P / 2; i += blockDim.x) {
+                    const uint32_t a = 2 * i - (i & (stride - 1));
+                    const uint32_t b = a + stride;
+                    const bool desc = (a & size) == 0;
+                    const unsigned long long x = cand[a], y = cand[b];
+                    if ((x < y) == desc) {
+                        cand[a] = y;
+                        cand[b] = x;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+    };
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < sub; i += blockDim.x) cand[i] = comp[(i / m) * k + i % m];
+    __syncthreads();
+    bitonic_desc(sub);
+    if (threadIdx.x == 0) s_bound = cand[k - 1];
+    __syncthreads();
+    const unsigned long long bound = s_bound;
+    for (uint32_t p = threadIdx.x; p < n; p += blockDim.x) {
+        const unsigned long long c = comp[p];
+        if (c >= bound) {
+            const uint32_t slot = atomicAdd(&s_cnt, 1u);
+            if (slot < kMergeSort) cand[slot] = c;
+        }
+    }
+    __syncthreads();
+    const uint32_t cnt = s_cnt;
+    auto emit = [&](uint32_t rank, unsigned long long c) {
+        const uint32_t p = ~static_cast<uint32_t>(c);
+        const uint32_t l = p / k, r = p - l * k;
+        const size_t q = t * tok_stride + l * list_stride + r;
+        const size_t o = static_cast<size_t>(t) * k + rank;
+        const uint32_t key = static_cast<uint32_t>(c >> 32);
+        out_key[o] = key;
+        out_id[o] = key ? in_id[q] : 0u;
+        out_val[o] = key ? in_val[q] : -__int_as_float(0x7f800000);
+    };
+    if (cnt <= kMergeSort) {
+        bitonic_desc(cnt);
+        for (uint32_t r = threadIdx.x; r < k; r += blockDim.x) emit(r, cand[r]);
+        return;
+    }
+    for (uint32_t p = threadIdx.x; p < n; p += blockDim.x) {
+        const unsigned long long c = comp[p];
+        if (c < bound) continue;
+        const uint32_t l = p / k;
+        uint32_t rank = p - l * k;
+        for (uint32_t o = 0; o < lists && rank < k; ++o) {
+            if (o == l) continue;
+            const unsigned long long* lo = comp + static_cast<size_t>(o) * k;
+            uint32_t a = 0, b = k;  // first index of list o whose comp < c
+            while (a < b) {
+                const uint32_t mid = (a + b) >> 1;
+                if (lo[mid] > c) a = mid + 1;
+                else b = mid;
+            }
+            rank += a;
+        }
+        if (rank < k) emit(rank, c);
+    }
+}
+
 // ---------------------------------------------------------------- host side
 uint32_t head_slices(uint32_t vocab) { return (vocab + kSelSlice - 1) / kSelSlice; }
 
 static int head_tiles(uint32_t tokens) { return tokens <= 8 ? 1 : (tokens <= 16 ? 2 : 4); }
-static size_t head_smem(uint32_t hidden, uint32_t tokens) {
-    return 2ull * head_tiles(tokens) * 8 * head_row_bytes(hidden);  // x hi + lo
+static size_t head_smem(uint32_t hidden, uint32_t tokens, bool lo) {
+    return (lo ? 2ull : 1ull) * head_tiles(tokens) * 8 * head_row_bytes(hidden);  // x hi (+ lo)
 }
 
 bool head_supported(uint32_t vocab, uint32_t hidden, uint32_t tokens, uint32_t top_k) {
     const uint32_t steps = hidden / 2 / 64;
     return vocab > 0 && hidden > 0 && hidden % (2 * 64 * kHeadDepth) == 0 && steps % kHeadDepth == 0 &&
            tokens > 0 && tokens <= kHeadMaxTokens && top_k > 0 && top_k <= kHeadMaxSelect &&
-           head_slices(vocab) * top_k <= kSelSlice && head_smem(hidden, tokens) <= 227ull * 1024;
+           head_slices(vocab) * top_k <= kMergeMax && head_slices(vocab) + top_k - 1 <= kMergeSort &&
+           head_smem(hidden, tokens, true) <= 227ull * 1024;
 }
 
 template <int NT, typename XT>
 static cudaError_t head_gemv_t(const HeadArgs& a, cudaStream_t s) {
     auto fn = head_gemv_kernel<NT, XT>;
-    const size_t smem = head_smem(a.hidden, a.tokens);
+    const size_t smem = head_smem(a.hidden, a.tokens, sizeof(XT) == 4);
     cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -387,9 +484,9 @@ cudaError_t head_topk_launch(const HeadArgs& a, cudaStream_t s) {
     e = a.x_dtype == PBMOE_BF16 ? head_gemv<uint16_t>(a, s) : head_gemv<float>(a, s);
     if (e != cudaSuccess) return e;
     const uint32_t S = head_slices(a.vocab);
-    head_select_kernel<<<dim3(a.tokens, S), kSelThreads, 0, s>>>(
-        a.logits, a.vocab, a.id_base, a.allowed, nullptr, nullptr, nullptr, 0, 0, a.vocab, a.top_k, a.cand_key,
-        a.cand_id, a.cand_val, static_cast<size_t>(S) * a.top_k);
+    head_select_kernel<<<dim3(a.tokens, S), kSelThreads, 0, s>>>(a.logits, a.vocab, a.id_base, a.allowed, a.vocab,
+                                                                  a.top_k, a.cand_key, a.cand_id, a.cand_val,
+                                                                  static_cast<size_t>(S) * a.top_k);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     return head_merge_launch(a.cand_key, a.cand_id, a.cand_val, a.tokens, S, static_cast<size_t>(S) * a.top_k,
                              a.top_k, a.top_k, a.out_key, a.out_id, a.out_val, s);
@@ -398,12 +495,15 @@ cudaError_t head_topk_launch(const HeadArgs& a, cudaStream_t s) {
 cudaError_t head_merge_launch(const uint32_t* in_key, const uint32_t* in_id, const float* in_val, uint32_t tokens,
                               uint32_t lists, size_t tok_stride, size_t list_stride, uint32_t top_k,
                               uint32_t* out_key, uint32_t* out_id, float* out_val, cudaStream_t s) {
-    if (tokens == 0 || lists == 0 || top_k == 0 || top_k > kHeadMaxSelect || lists * top_k > kSelSlice)
+    if (tokens == 0 || lists == 0 || top_k == 0 || top_k > kHeadMaxSelect || lists * top_k > kMergeMax ||
+        top_k + lists - 1 > kMergeSort)
         return cudaErrorInvalidValue;
-    const size_t n = static_cast<size_t>(lists) * top_k;
-    head_select_kernel<<<dim3(tokens, 1), kSelThreads, 0, s>>>(nullptr, 0, 0, nullptr, in_key, in_id, in_val,
-                                                               tok_stride, list_stride, static_cast<uint32_t>(n),
-                                                               top_k, out_key, out_id, out_val, top_k);
+    const size_t smem = static_cast<size_t>(lists) * top_k * sizeof(unsigned long long);
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(head_merge_kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    head_merge_kernel<<<tokens, kSelThreads, smem, s>>>(in_key, in_id, in_val, tok_stride, list_stride, lists, top_k,
+                                                        out_key, out_id, out_val);
     return cudaGetLastError();
 }
 
