@@ -66,9 +66,9 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla", "head"],
+    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla", "head", "step"],
                    help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3; "
-                        "head: config 4's vocab head + top-k")
+                        "head: config 4's vocab head + top-k; step: config 4's full decode step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -242,7 +242,8 @@ def main():
         run_reference(args)
         return
     if args.workload != "moe":
-        {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla, "head": run_head}[args.workload](args)
+        {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla, "head": run_head,
+         "step": run_step}[args.workload](args)
         return
     import numpy as np
     import torch
@@ -815,6 +816,76 @@ def run_head(args):
                      "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind, "traffic": None,
                      "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"]},
         "cases": cases, "gpu_launches": head["steps"] * 3, "clocks": head["clocks"], "cpu_baseline": None,
+    })
+    ctx.close()
+
+
+def run_step(args):
+    """Config 4 on one GPU: a full decode step of the 48-layer synthetic model
+    (MLA attention at context 8192 + 512-expert top-10 MoE per layer, vocab
+    head [151936 x 2048] + top-64) for --batch sequences, each attending over
+    8192 cached positions; batches 1, 8 and 32 listed."""
+    import torch
+
+    from pb_b200 import capi, decode
+
+    cfg = decode.StepConfig()
+    ctx = capi.Context(0)
+    model = decode.Model(cfg, seed=4)
+    s = torch.cuda.Stream()
+    cases, head = [], None
+    for B in sorted({1, 8, 32, args.batch}):
+        caches = decode.Caches(cfg, B, seed=B)
+        step = decode.DecodeStep(ctx, model, caches, B, [cfg.context - 1] * B)
+        x0 = torch.randn(B, cfg.hidden, generator=torch.Generator("cuda").manual_seed(B), device="cuda")
+        step.set_input(x0)
+        with torch.cuda.stream(s):
+            step.launch(stream=s, record_routes=True)
+        s.synchronize()
+        U = step.unique_experts()
+        steps = max(3, args.steps // 50) if B == args.batch else 5
+        ms, n, clocks = _graph_time([lambda: (step.set_input(x0), step.launch(stream=s))], s, steps, args.warmup)
+        byts = step.bytes_per_step(U)
+        cases.append({"batch": B, "ms": ms, "tok_s": B / (ms / 1e3), "gbs": byts / (ms / 1e3) / 1e9,
+                      "unique_experts_mean": U})
+        if B == args.batch:
+            hx = x0.cpu().pin_memory()
+            hi = torch.empty(B, cfg.candidates, dtype=torch.int32).pin_memory()
+            hv = torch.empty(B, cfg.candidates).pin_memory()
+
+            def e2e():
+                step.x.copy_(hx, non_blocking=True)
+                step.launch(stream=s)
+                hi.copy_(step.ids, non_blocking=True)
+                hv.copy_(step.vals, non_blocking=True)
+
+            ems = _e2e_time(e2e, s, 5)
+            head = dict(ms=ms, steps=n, clocks=clocks, bytes=byts, e2e_ms=ems, B=B, U=U,
+                        launches=step.launches_per_step())
+        del step, caches
+        torch.cuda.empty_cache()
+    peak, kind = measured_peaks()
+    gbs = head["bytes"] / (head["ms"] / 1e3) / 1e9
+    _emit({
+        "metric": f"full decode step tok/s (config 4: 48 layers MLA + MoE, context 8192, batch {head['B']})",
+        "value": head["B"] / (head["ms"] / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": head["steps"],
+        "warmup": max(3, args.warmup), "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; random-init 48-layer MLA + MoE model, random bf16 caches)",
+        "config": {"workload": "config4 full decode step", "layers": cfg.layers, "hidden": cfg.hidden,
+                   "experts": cfg.experts, "top_k": cfg.top_k, "q_lora": cfg.q_lora, "heads": cfg.heads,
+                   "context": cfg.context, "vocab": cfg.vocab, "head_top_k": cfg.candidates, "batch": head["B"],
+                   "l2": "inputs larger than L2: 45 GB of weights and the caches read once per step",
+                   "graph": "one CUDA graph per step"},
+        "e2e": {"value": head["B"] / (head["e2e_ms"] / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": head["B"] * cfg.hidden * 4, "d2h_bytes_per_step": head["B"] * cfg.candidates * 8,
+                "steps": 5},
+        "roofline": {"bound": "hbm", "kernel": "decode step (all kernels)", "achieved": gbs, "peak": peak,
+                     "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"],
+                     "unique_experts_mean": head["U"]},
+        "cases": cases, "gpu_launches": head["steps"] * head["launches"], "clocks": head["clocks"],
+        "cpu_baseline": None,
     })
     ctx.close()
 

@@ -67,6 +67,7 @@ typedef enum pbmoe_status {
 #define PBMOE_DEV_ERR_PEER_TIMEOUT 0x4u  /* expert-parallel combine wait expired       */
 #define PBMOE_DEV_ERR_PIPE_TIMEOUT 0x8u  /* an asynchronous copy wait expired          */
 #define PBMOE_DEV_ERR_F16_RANGE 0x10u    /* prefill GEMM input |x| >= 65536 or non-finite */
+#define PBMOE_DEV_ERR_POSITION 0x20u     /* decode position past the cache or RoPE table  */
 
 typedef enum pbmoe_dtype {
     PBMOE_F32 = 0,
@@ -438,6 +439,48 @@ PBMOE_API int pbmoe_head_topk(pbmoe_ctx* ctx, const pbmoe_head* head, const void
 PBMOE_API int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint32_t* ids, const float* values,
                                uint32_t lists, uint32_t tokens, uint32_t top_k, uint32_t* out_ids,
                                float* out_values, void* stream);
+
+/* ---------------------------------------------------------------- decode-step glue
+ * Row RMSNorm, optionally fused with the residual add: s = x (+ residual);
+ * sum_out (optional) receives s; out = s * 1/sqrt(mean(s^2) + epsilon) *
+ * weight. Covers rms_norm_reduced (shaders.metal:1176-1213) on q_a and on the
+ * latent part of kv_a in the MLA input projection chain
+ * (metal/qwen_execution.rs:405-437; row stride 576, width 512 there) and the
+ * residual add + post-attention norm ahead of the router (CMD2,
+ * metal/mod.rs:2864-3012). Strides are in elements; out may alias x. */
+typedef struct pbmoe_norm_args {
+    const void* x;
+    pbmoe_dtype x_dtype; /* f32 or bf16; residual has the same dtype */
+    const void* residual;
+    void* sum_out;
+    pbmoe_dtype sum_dtype;
+    const float* weight; /* [width] or NULL (no weight) */
+    float epsilon;
+    void* out;
+    pbmoe_dtype out_dtype;
+    uint32_t rows, width;
+    uint32_t x_stride, residual_stride, sum_stride, out_stride;
+} pbmoe_norm_args;
+PBMOE_API int pbmoe_rms_norm(pbmoe_ctx* ctx, const pbmoe_norm_args* args, void* stream);
+
+/* Cos/sin table of apply_rotary_interleaved_to_split_half (math.rs:822-846)
+ * for positions [0, max_positions): f64 angles position * theta^(-2p/rope),
+ * cast to f32, as the reference builds them (runtime/mod.rs:2825-2836). */
+PBMOE_API int pbmoe_rope_reserve(pbmoe_ctx* ctx, uint32_t max_positions, uint32_t rope_dim, double theta);
+
+/* For each of `batch` tokens: RoPE (interleaved pairs -> split halves) on the
+ * rope part of every head of `query` (f32 [batch x heads x (nope + rope)], in
+ * place) and on the rope part of `kv` (f32 [batch x (latent + rope)], latent
+ * part already normed), then the latent row (bf16) and the rotated key row
+ * (bf16) written at the token's position of its cache (KvCache::record_mla_kv,
+ * state/kv_cache.rs:414-450; the rotation call sites are runtime/mod.rs:
+ * 2896-2913). positions: DEVICE u32 [batch]; c_kv / k_rope: DEVICE arrays
+ * [batch] of bf16 cache pointers ([cache_len x latent], [cache_len x rope]).
+ * A position >= cache_len or outside the RoPE table latches
+ * PBMOE_DEV_ERR_POSITION and writes nothing for that token. */
+PBMOE_API int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* config, uint32_t batch, float* query,
+                                    const float* kv, const uint32_t* positions, uint16_t* const* c_kv,
+                                    uint16_t* const* k_rope, uint32_t cache_len, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

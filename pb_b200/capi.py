@@ -28,6 +28,7 @@ PBMOE_DEV_ERR_EXPERT_ID = 0x2
 PBMOE_DEV_ERR_PEER_TIMEOUT = 0x4
 PBMOE_DEV_ERR_PIPE_TIMEOUT = 0x8
 PBMOE_DEV_ERR_F16_RANGE = 0x10
+PBMOE_DEV_ERR_POSITION = 0x20
 
 PBMOE_F32 = 0
 PBMOE_BF16 = 1
@@ -44,6 +45,7 @@ EXPORTED = [
     "pbmoe_prefill_reserve", "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
     "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
+    "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -99,6 +101,13 @@ class Head(C.Structure):
     _fields_ = [("weight", C.c_void_p), ("vocab", C.c_uint32), ("hidden", C.c_uint32), ("id_base", C.c_uint32)]
 
 
+class NormArgs(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("x_dtype", C.c_int), ("residual", C.c_void_p), ("sum_out", C.c_void_p),
+                ("sum_dtype", C.c_int), ("weight", C.c_void_p), ("epsilon", C.c_float), ("out", C.c_void_p),
+                ("out_dtype", C.c_int), ("rows", C.c_uint32), ("width", C.c_uint32), ("x_stride", C.c_uint32),
+                ("residual_stride", C.c_uint32), ("sum_stride", C.c_uint32), ("out_stride", C.c_uint32)]
+
+
 class PbmoeError(RuntimeError):
     def __init__(self, code, message):
         super().__init__(f"pbmoe status {code}: {message}")
@@ -151,6 +160,9 @@ def load():
         L.pbmoe_head_reserve.argtypes = [vp, u32, u32, u32]
         L.pbmoe_head_topk.argtypes = [vp, C.POINTER(Head), vp, i32, u32, u32, vp, vp, vp, vp, vp, vp]
         L.pbmoe_head_merge.argtypes = [vp, vp, vp, vp, u32, u32, u32, vp, vp, vp]
+        L.pbmoe_rms_norm.argtypes = [vp, C.POINTER(NormArgs), vp]
+        L.pbmoe_rope_reserve.argtypes = [vp, u32, u32, C.c_double]
+        L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, vp, vp, u32, vp]
         _lib = L
     return _lib
 
@@ -271,6 +283,29 @@ class Context:
         lists, tokens, top_k = (int(d) for d in keys.shape)
         self.check(self.lib.pbmoe_head_merge(self.h, _ptr(keys), _ptr(ids), _ptr(values), lists, tokens, top_k,
                                              _ptr(out_ids), _ptr(out_values), self.stream_ptr(stream)))
+
+    def rms_norm(self, x, weight, out, eps=1e-6, residual=None, sum_out=None, width=None, stream=None):
+        """Rows of x (2-D, f32/bf16; `width` leading columns of each row, default all):
+        s = x (+ residual); sum_out <- s; out = rms_norm(s) * weight."""
+        rows = int(x.shape[0])
+        w = int(width if width is not None else x.shape[1])
+        st = lambda t: int(t.stride(0)) if t is not None else 0
+        a = NormArgs(x.data_ptr(), _dtype_code(x), None if residual is None else residual.data_ptr(),
+                     None if sum_out is None else sum_out.data_ptr(),
+                     _dtype_code(sum_out) if sum_out is not None else 0,
+                     None if weight is None else weight.data_ptr(), eps, out.data_ptr(), _dtype_code(out), rows, w,
+                     st(x), st(residual), st(sum_out), st(out))
+        self.check(self.lib.pbmoe_rms_norm(self.h, C.byref(a), self.stream_ptr(stream)))
+
+    def rope_reserve(self, max_positions, rope_dim, theta=10000.0):
+        self.check(self.lib.pbmoe_rope_reserve(self.h, max_positions, rope_dim, theta))
+
+    def mla_rope_append(self, config, query, kv, positions, c_kv_ptrs, k_rope_ptrs, cache_len, stream=None):
+        """query f32 [B, heads, nope+rope] (in place); kv f32 [B, latent+rope]; positions int32 [B] device;
+        c_kv_ptrs / k_rope_ptrs int64 [B] device tensors of cache addresses."""
+        self.check(self.lib.pbmoe_mla_rope_append(self.h, C.byref(config), int(query.shape[0]), _ptr(query), _ptr(kv),
+                                                  _ptr(positions), _ptr(c_kv_ptrs), _ptr(k_rope_ptrs), cache_len,
+                                                  self.stream_ptr(stream)))
 
     def prefill_reserve(self, max_rows, max_cols):
         self.check(self.lib.pbmoe_prefill_reserve(self.h, max_rows, max_cols))

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "kernels.h"
 #include "q4_rows.cuh"
@@ -27,6 +28,8 @@ struct pbmoe_ctx {
     uint32_t ep_rank = 0, ep_world = 0, ep_max_tokens = 0, ep_hidden = 0;
     void* ep_peer[pbmoe::kMaxEpRanks] = {};
     bool ep_peer_ipc[pbmoe::kMaxEpRanks] = {};  // mapped through CUDA IPC (closed at destroy)
+    float2* rope_table = nullptr;  // [rope_positions x rope_dim/2] (cos, sin)
+    uint32_t rope_positions = 0, rope_dim = 0;
     void* head_base = nullptr;  // vocab head: logits, slice candidates, key scratch
     size_t head_bytes = 0;
     uint32_t head_tokens = 0, head_vocab = 0, head_k = 0;
@@ -219,6 +222,7 @@ int pbmoe_destroy(pbmoe_ctx* ctx) {
         if (ctx->mla_base) cudaFree(ctx->mla_base);
         if (ctx->x16_base) cudaFree(ctx->x16_base);
         if (ctx->head_base) cudaFree(ctx->head_base);
+        if (ctx->rope_table) cudaFree(ctx->rope_table);
         for (uint32_t r = 0; r < pbmoe::kMaxEpRanks; ++r)
             if (ctx->ep_peer_ipc[r]) cudaIpcCloseMemHandle(ctx->ep_peer[r]);
         if (ctx->ep_base) cudaFree(ctx->ep_base);
@@ -970,5 +974,95 @@ int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint32_t* ids, 
     cudaError_t e = pbmoe::head_merge_launch(keys, ids, values, tokens, lists, top_k, size_t(tokens) * top_k, top_k,
                                              w.key_scratch, out_ids, out_values, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(ctx, e, "head merge launch");
+    return PBMOE_OK;
+}
+
+// ---------------------------------------------------------------- decode-step glue
+int pbmoe_rms_norm(pbmoe_ctx* ctx, const pbmoe_norm_args* a, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!a || !a->x || !a->out) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "rms norm: null pointer");
+    auto known = [](pbmoe_dtype t) { return t == PBMOE_F32 || t == PBMOE_BF16; };
+    if (!known(a->x_dtype) || !known(a->out_dtype) || (a->sum_out && !known(a->sum_dtype)))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "rms norm: dtypes must be f32 or bf16");
+    if (a->rows == 0) return PBMOE_OK;
+    if (a->width == 0 || a->x_stride < a->width || a->out_stride < a->width ||
+        (a->residual && a->residual_stride < a->width) || (a->sum_out && a->sum_stride < a->width) ||
+        !(a->epsilon >= 0.0f))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "rms norm: width %u with strides x %u out %u", a->width,
+                    a->x_stride, a->out_stride);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    pbmoe::NormArgs n{a->x,      a->x_dtype, a->residual, a->sum_out,   a->sum_dtype,       a->weight,
+                      a->epsilon, a->out,    a->out_dtype, a->rows,     a->width,           a->x_stride,
+                      a->residual_stride,    a->sum_stride, a->out_stride};
+    cudaError_t e = pbmoe::rms_norm_launch(n, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rms norm launch");
+    return PBMOE_OK;
+}
+
+int pbmoe_rope_reserve(pbmoe_ctx* ctx, uint32_t max_positions, uint32_t rope_dim, double theta) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (max_positions == 0 || rope_dim == 0 || rope_dim % 2 || !(theta > 0.0))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "rope reserve: %u positions, rope dim %u (even), theta %g",
+                    max_positions, rope_dim, theta);
+    const uint32_t half = rope_dim / 2;
+    std::vector<float2> table(size_t(max_positions) * half);
+    for (uint32_t pair = 0; pair < half; ++pair) {
+        const double frequency = std::pow(theta, -static_cast<double>(2 * pair) / static_cast<double>(rope_dim));
+        for (uint32_t pos = 0; pos < max_positions; ++pos) {
+            const double angle = static_cast<double>(pos) * frequency;
+            table[size_t(pos) * half + pair] = make_float2(static_cast<float>(std::cos(angle)),
+                                                           static_cast<float>(std::sin(angle)));
+        }
+    }
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    if (ctx->rope_table) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before rope table resize");
+        cudaFree(ctx->rope_table);
+        ctx->rope_table = nullptr;
+    }
+    cudaError_t e = cudaMalloc(&ctx->rope_table, table.size() * sizeof(float2));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rope table allocation");
+    e = cudaMemcpy(ctx->rope_table, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rope table upload");
+    ctx->rope_positions = max_positions;
+    ctx->rope_dim = rope_dim;
+    return PBMOE_OK;
+}
+
+int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* cfg, uint32_t batch, float* query, const float* kv,
+                          const uint32_t* positions, uint16_t* const* c_kv, uint16_t* const* k_rope,
+                          uint32_t cache_len, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!cfg || !query || !kv || !positions || !c_kv || !k_rope)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla rope append: null pointer");
+    if (batch == 0) return PBMOE_OK;
+    if (!ctx->rope_table || ctx->rope_dim != cfg->rope_dim)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "mla rope append: rope dim %u needs pbmoe_rope_reserve",
+                    cfg->rope_dim);
+    if (!pbmoe::rope_append_supported(cfg->heads, cfg->rope_dim) || cfg->latent_dim == 0 || cache_len == 0)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported MLA RoPE append: %u heads x rope %u",
+                    cfg->heads, cfg->rope_dim);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    pbmoe::RopeAppendArgs a{};
+    a.batch = batch;
+    a.heads = cfg->heads;
+    a.nope = cfg->nope_dim;
+    a.rope = cfg->rope_dim;
+    a.latent = cfg->latent_dim;
+    a.query = query;
+    a.kv = kv;
+    a.positions = positions;
+    a.c_kv = c_kv;
+    a.k_rope = k_rope;
+    a.cache_len = cache_len;
+    a.table = ctx->rope_table;
+    a.max_positions = ctx->rope_positions;
+    a.status = ctx->status;
+    cudaError_t e = pbmoe::mla_rope_append_launch(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "mla rope append launch");
     return PBMOE_OK;
 }

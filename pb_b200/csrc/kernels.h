@@ -233,6 +233,36 @@ struct PrefillPlanArgs {
 size_t prefill_plan_smem(uint32_t num_experts);
 cudaError_t prefill_plan_launch(const PrefillPlanArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- decode-step glue (step.cu)
+struct NormArgs {
+    const void* x;
+    pbmoe_dtype x_dtype;
+    const void* residual;
+    void* sum_out;
+    pbmoe_dtype sum_dtype;
+    const float* weight;
+    float epsilon;
+    void* out;
+    pbmoe_dtype out_dtype;
+    uint32_t rows, width, x_stride, residual_stride, sum_stride, out_stride;
+};
+cudaError_t rms_norm_launch(const NormArgs& a, cudaStream_t s);
+
+struct RopeAppendArgs {
+    uint32_t batch, heads, nope, rope, latent;
+    float* query;               // [batch x heads x (nope + rope)]
+    const float* kv;            // [batch x (latent + rope)]
+    const uint32_t* positions;  // [batch]
+    uint16_t* const* c_kv;      // [batch] cache rows [cache_len x latent]
+    uint16_t* const* k_rope;    // [batch] cache rows [cache_len x rope]
+    uint32_t cache_len;
+    const float2* table;  // [max_positions x rope/2] (cos, sin)
+    uint32_t max_positions;
+    uint32_t* status;
+};
+bool rope_append_supported(uint32_t heads, uint32_t rope);
+cudaError_t mla_rope_append_launch(const RopeAppendArgs& a, cudaStream_t s);
+
 // ---------------------------------------------------------------- vocab head (head.cu)
 // logits[t][v] = W[v] . x[t] for the rows [0, vocab) of a (possibly sharded)
 // head whose row 0 is global token id `id_base`, then each token's top_k

@@ -1,0 +1,136 @@
+// step.cu — the per-layer glue of a decode step around the MLA attention and
+// MoE kernels (config 4):
+//
+//   rms_norm_rows_kernel   s = x (+ residual), out = s * rsqrt(mean(s^2) + eps) * w
+//                          per row: rms_norm_reduced (shaders.metal:1176-1213), run on
+//                          q_a and the latent part of kv_a by the MLA input
+//                          projection chain (metal/qwen_execution.rs:405-437), and
+//                          the residual add + post-attention norm ahead of the router
+//                          (CMD2, metal/mod.rs:2864-3012)
+//   mla_rope_append_kernel RoPE on every head's rope part of the query and on the
+//                          key's rope part (apply_rotary_interleaved_to_split_half,
+//                          math.rs:822-846, as called at runtime/mod.rs:2896-2913),
+//                          then the latent and rotated key rows written into the
+//                          sequence's cache at its position (KvCache::record_mla_kv,
+//                          state/kv_cache.rs:414-450)
+//
+// The cos/sin table is built on the host in f64 exactly as the reference
+// builds its angles (runtime/mod.rs:2825-2836), so the rotation, done with
+// unfused f32 multiplies and adds as in the reference, is bit-exact.
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pbmoe {
+
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float ld_any(const void* p, pbmoe_dtype t, size_t i) {
+    return t == PBMOE_BF16 ? bf16_bits_to_f32(static_cast<const uint16_t*>(p)[i]) : static_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void st_any(void* p, pbmoe_dtype t, size_t i, float v) {
+    if (t == PBMOE_BF16)
+        static_cast<uint16_t*>(p)[i] = f32_to_bf16_bits(v);
+    else
+        static_cast<float*>(p)[i] = v;
+}
+
+__global__ void __launch_bounds__(kNormThreads) rms_norm_rows_kernel(NormArgs a) {
+    __shared__ float red[kNormThreads / 32];
+    const uint32_t r = blockIdx.x;
+    const size_t xo = static_cast<size_t>(r) * a.x_stride, ro = static_cast<size_t>(r) * a.residual_stride;
+    const size_t so = static_cast<size_t>(r) * a.sum_stride, oo = static_cast<size_t>(r) * a.out_stride;
+    float ss = 0.f;
+    for (uint32_t i = threadIdx.x; i < a.width; i += blockDim.x) {
+        float s = ld_any(a.x, a.x_dtype, xo + i);
+        if (a.residual) s += ld_any(a.residual, a.x_dtype, ro + i);
+        if (a.sum_out) st_any(a.sum_out, a.sum_dtype, so + i, s);
+        ss += s * s;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
+    const float scale = 1.0f / sqrtf(tot / static_cast<float>(a.width) + a.epsilon);
+    for (uint32_t i = threadIdx.x; i < a.width; i += blockDim.x) {
+        // the sum as written (its own rounding when stored in bf16), else recomputed
+        float s;
+        if (a.sum_out) {
+            s = ld_any(a.sum_out, a.sum_dtype, so + i);
+        } else {
+            s = ld_any(a.x, a.x_dtype, xo + i);
+            if (a.residual) s += ld_any(a.residual, a.x_dtype, ro + i);
+        }
+        st_any(a.out, a.out_dtype, oo + i, s * scale * (a.weight ? a.weight[i] : 1.0f));
+    }
+}
+
+cudaError_t rms_norm_launch(const NormArgs& a, cudaStream_t s) {
+    if (a.rows == 0) return cudaSuccess;
+    rms_norm_rows_kernel<<<a.rows, kNormThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+constexpr int kRopeThreads = 256;
+constexpr uint32_t kRopeMaxPairs = 2048;  // heads x rope/2 rotated per token
+
+__global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppendArgs a) {
+    const uint32_t b = blockIdx.x;
+    const uint32_t pos = a.positions[b];
+    if (pos >= a.max_positions || pos >= a.cache_len) {
+        if (threadIdx.x == 0 && a.status) atomicOr(a.status, PBMOE_DEV_ERR_POSITION);
+        return;
+    }
+    const uint32_t half = a.rope / 2, qk = a.nope + a.rope;
+    const float2* cs = a.table + static_cast<size_t>(pos) * half;
+    // query: read every pair of every head, then write the split halves
+    float* q = a.query + static_cast<size_t>(b) * a.heads * qk;
+    constexpr int kPer = kRopeMaxPairs / kRopeThreads;
+    float va[kPer], vb[kPer];
+    const uint32_t pairs = a.heads * half;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t i = threadIdx.x + j * kRopeThreads;
+        if (i < pairs) {
+            const uint32_t h = i / half, p = i - h * half;
+            va[j] = q[h * qk + a.nope + 2 * p];
+            vb[j] = q[h * qk + a.nope + 2 * p + 1];
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t i = threadIdx.x + j * kRopeThreads;
+        if (i < pairs) {
+            const uint32_t h = i / half, p = i - h * half;
+            const float2 t = cs[p];  // (cos, sin)
+            q[h * qk + a.nope + p] = __fsub_rn(__fmul_rn(va[j], t.x), __fmul_rn(vb[j], t.y));
+            q[h * qk + a.nope + half + p] = __fadd_rn(__fmul_rn(vb[j], t.x), __fmul_rn(va[j], t.y));
+        }
+    }
+    // key: the rope part after the latent, rotated into the cache row
+    const float* kv = a.kv + static_cast<size_t>(b) * (a.latent + a.rope);
+    uint16_t* krow = a.k_rope[b] + static_cast<size_t>(pos) * a.rope;
+    for (uint32_t p = threadIdx.x; p < half; p += blockDim.x) {
+        const float x0 = kv[a.latent + 2 * p], x1 = kv[a.latent + 2 * p + 1];
+        const float2 t = cs[p];
+        krow[p] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)));
+        krow[half + p] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(x1, t.x), __fmul_rn(x0, t.y)));
+    }
+    uint16_t* crow = a.c_kv[b] + static_cast<size_t>(pos) * a.latent;
+    for (uint32_t i = threadIdx.x; i < a.latent; i += blockDim.x) crow[i] = f32_to_bf16_bits(kv[i]);
+}
+
+bool rope_append_supported(uint32_t heads, uint32_t rope) {
+    return rope > 0 && rope % 2 == 0 && heads > 0 && heads * (rope / 2) <= kRopeMaxPairs;
+}
+
+cudaError_t mla_rope_append_launch(const RopeAppendArgs& a, cudaStream_t s) {
+    if (a.batch == 0) return cudaSuccess;
+    if (!rope_append_supported(a.heads, a.rope)) return cudaErrorInvalidValue;
+    mla_rope_append_kernel<<<a.batch, kRopeThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace pbmoe

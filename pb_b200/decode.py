@@ -1,0 +1,203 @@
+"""One decode step of a synthetic MLA + MoE model, composed
+from the C-ABI entry points. Python only enqueues; every operation is a CUDA
+kernel behind pbmoe_*; `DecodeStep.launch` is what a CUDA graph captures.
+
+Per layer, following forward_token_input (runtime/mod.rs:1432-2024) with the
+GLM MLA attention of mla_attention_output_values (runtime/mod.rs:2779-2940):
+
+  q_a  = Q4(q_a_proj) xn          kv = Q4(kv_a_proj_with_mqa) xn      pbmoe_q4_matvec
+  q_a  = rms_norm(q_a) w_qa       kv[:latent] = rms_norm(kv[:latent]) pbmoe_rms_norm
+  q    = Q4(q_b_proj) q_a                                             pbmoe_q4_matvec
+  RoPE on q's and kv's rope parts; latent + key rows into the cache   pbmoe_mla_rope_append
+  attn = absorbed MLA attention over the cache                        pbmoe_mla_decode
+  o    = Q4(o_proj) attn                                              pbmoe_q4_matvec
+  h    = x + o,  n = rms_norm(h) w_post                               pbmoe_rms_norm
+  x    = h + MoE(n),  xn = rms_norm(x) w_in(next layer)               pbmoe_moe_layer
+
+and after the last layer (whose fused norm uses the final norm weight) the
+vocab head top-k (pbmoe_head_topk). The residual stream x is f32; the MLA
+projection inputs are f32; caches are bf16 per (layer, sequence).
+
+The projection shapes (q_lora 1536, kv_a 512 + 64, q_b 16 x 192, o_proj 16 x
+128 -> hidden) are this build's declaration for config 4, which fixes only the
+attention geometry (16 heads, nope 128, rope 64, latent 512, v 128): they are
+GLM-style 4-bit group-64 projections as in the reference's GLM path.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import capi, synth
+
+
+@dataclass
+class StepConfig:
+    hidden: int = 2048
+    layers: int = 48
+    q_lora: int = 1536
+    heads: int = 16
+    nope: int = 128
+    rope: int = 64
+    latent: int = 512
+    v_dim: int = 128
+    experts: int = 512
+    top_k: int = 10
+    inter: int = 512
+    group: int = 64
+    vocab: int = 151936
+    context: int = 8192
+    theta: float = 10000.0
+    eps: float = 1e-6
+    candidates: int = 64  # head top-k
+
+
+class Q4:
+    """A dense Q4 projection [rows x cols] (nibbles, bf16 scales and biases)."""
+
+    def __init__(self, rows, cols, group, g, device):
+        self.rows, self.cols, self.group = rows, cols, group
+        self.packed, self.scales, self.biases = synth.q4_matrix(rows, cols, group, g, device)
+
+    def __call__(self, ctx, x, y, stream):
+        ctx.q4_matvec(self.packed, self.scales, self.biases, self.rows, self.cols, self.group, x, y,
+                      batch=int(x.shape[0]), stream=stream)
+
+    def nbytes(self):
+        return int(self.packed.numel() + 2 * self.scales.numel() + 2 * self.biases.numel())
+
+
+class Layer:
+    def __init__(self, cfg: StepConfig, seed: int, device="cuda"):
+        g = synth.gen(device, seed)
+        H, G = cfg.hidden, cfg.group
+        self.q_a = Q4(cfg.q_lora, H, G, g, device)
+        self.kv_a = Q4(cfg.latent + cfg.rope, H, G, g, device)
+        self.q_b = Q4(cfg.heads * (cfg.nope + cfg.rope), cfg.q_lora, G, g, device)
+        self.o_proj = Q4(H, cfg.heads * cfg.v_dim, G, g, device)
+        norm = lambda n: (1.0 + 0.1 * torch.randn(n, generator=g, device=device)).float()
+        self.q_a_norm, self.kv_a_norm = norm(cfg.q_lora), norm(cfg.latent)
+        self.input_norm, self.post_norm = norm(H), norm(H)
+        self.w_uk = synth.normal_bf16((cfg.heads, cfg.nope, cfg.latent), 0.02, g, device)
+        self.w_uv = synth.normal_bf16((cfg.heads, cfg.v_dim, cfg.latent), 0.02, g, device)
+        self.moe = synth.MoeLayerWeights(device, seed + 7919, hidden=H, num_experts=cfg.experts,
+                                         intermediate=cfg.inter, group=G)
+
+    def nbytes(self):
+        """Weight bytes a decode step reads for this layer, before experts."""
+        return (self.q_a.nbytes() + self.kv_a.nbytes() + self.q_b.nbytes() + self.o_proj.nbytes() +
+                2 * (self.w_uk.numel() + self.w_uv.numel()) +
+                4 * (self.q_a_norm.numel() + self.kv_a_norm.numel() + self.input_norm.numel() +
+                     self.post_norm.numel()))
+
+
+class Model:
+    def __init__(self, cfg: StepConfig, seed=0, device="cuda"):
+        self.cfg = cfg
+        self.layers = [Layer(cfg, seed + 1000 * i, device) for i in range(cfg.layers)]
+        g = synth.gen(device, seed + 17)
+        self.head = synth.normal_bf16((cfg.vocab, cfg.hidden), 0.02, g, device)
+        self.final_norm = (1.0 + 0.1 * torch.randn(cfg.hidden, generator=g, device=device)).float()
+
+
+class Caches:
+    """bf16 latent and rotated-key caches per (layer, sequence), [context x dim]."""
+
+    def __init__(self, cfg: StepConfig, batch: int, seed=0, device="cuda"):
+        g = synth.gen(device, seed + 29)
+        self.c_kv = [[synth.normal_bf16((cfg.context, cfg.latent), 1.0, g, device) for _ in range(batch)]
+                     for _ in range(cfg.layers)]
+        self.k_rope = [[synth.normal_bf16((cfg.context, cfg.rope), 1.0, g, device) for _ in range(batch)]
+                       for _ in range(cfg.layers)]
+        self.c_kv_ptrs = [torch.tensor([t.data_ptr() for t in l], dtype=torch.int64, device=device)
+                          for l in self.c_kv]
+        self.k_rope_ptrs = [torch.tensor([t.data_ptr() for t in l], dtype=torch.int64, device=device)
+                            for l in self.k_rope]
+
+
+class DecodeStep:
+    """Buffers and launch sequence of one decode step for `batch` sequences,
+    each at position positions[b] of its caches (attending over positions
+    0..position)."""
+
+    def __init__(self, ctx: capi.Context, model: Model, caches: Caches, batch: int, positions):
+        cfg = model.cfg
+        self.ctx, self.model, self.caches, self.cfg, self.B = ctx, model, caches, cfg, batch
+        dev = "cuda"
+        f32 = dict(device=dev, dtype=torch.float32)
+        self.positions_host = [int(p) for p in positions]
+        self.positions = torch.tensor(self.positions_host, dtype=torch.int32, device=dev)
+        B, H = batch, cfg.hidden
+        self.x = torch.zeros(B, H, **f32)        # residual stream
+        self.xn = torch.zeros(B, H, **f32)       # normed layer input
+        self.qa = torch.zeros(B, cfg.q_lora, **f32)
+        self.kv = torch.zeros(B, cfg.latent + cfg.rope, **f32)
+        self.q = torch.zeros(B, cfg.heads, cfg.nope + cfg.rope, **f32)
+        self.attn = torch.zeros(B, cfg.heads, cfg.v_dim, **f32)
+        self.o = torch.zeros(B, H, **f32)
+        self.h = torch.zeros(B, H, **f32)
+        self.n = torch.zeros(B, H, device=dev, dtype=torch.bfloat16)
+        self.route_ids = torch.zeros(cfg.layers, B, cfg.top_k, device=dev, dtype=torch.int32)
+        self.ids = torch.zeros(B, cfg.candidates, device=dev, dtype=torch.int32)
+        self.vals = torch.zeros(B, cfg.candidates, **f32)
+        self.mla_cfg = capi.mla_config(cfg.heads, cfg.nope, cfg.rope, cfg.latent, cfg.v_dim)
+        self.moe_cfg = capi.moe_config(model.layers[0].moe.layout, cfg.experts, cfg.top_k)
+        self.moe_w = [l.moe.c_weights() for l in model.layers]
+        ctx.reserve(B, self.moe_cfg)
+        ctx.mla_reserve(self.mla_cfg, B)
+        ctx.rope_reserve(cfg.context, cfg.rope, cfg.theta)
+        ctx.head_reserve(B, cfg.vocab, cfg.candidates)
+
+    def set_input(self, x):
+        """x f32 [B, hidden]: the step's embeddings (residual stream)."""
+        self.x.copy_(x)
+
+    def launch(self, stream=None, record_routes=False):
+        """Enqueue the step; record_routes also writes every layer's route ids
+        to self.route_ids (for counting the experts a step reads)."""
+        ctx, cfg, m = self.ctx, self.cfg, self.model
+        L0 = m.layers[0]
+        ctx.rms_norm(self.x, L0.input_norm, self.xn, eps=cfg.eps, stream=stream)
+        seq_lens = [p + 1 for p in self.positions_host]
+        for i, L in enumerate(m.layers):
+            L.q_a(ctx, self.xn, self.qa, stream)
+            L.kv_a(ctx, self.xn, self.kv, stream)
+            ctx.rms_norm(self.qa, L.q_a_norm, self.qa, eps=cfg.eps, stream=stream)
+            ctx.rms_norm(self.kv, L.kv_a_norm, self.kv, eps=cfg.eps, width=cfg.latent, stream=stream)
+            L.q_b(ctx, self.qa, self.q.view(self.B, -1), stream)
+            ctx.mla_rope_append(self.mla_cfg, self.q, self.kv, self.positions, self.caches.c_kv_ptrs[i],
+                                self.caches.k_rope_ptrs[i], cfg.context, stream=stream)
+            ctx.mla_decode(self.mla_cfg, self.q, [t[:n] for t, n in zip(self.caches.c_kv[i], seq_lens)],
+                           [t[:n] for t, n in zip(self.caches.k_rope[i], seq_lens)], L.w_uk, L.w_uv, self.attn,
+                           stream=stream)
+            L.o_proj(ctx, self.attn.view(self.B, -1), self.o, stream)
+            ctx.rms_norm(self.o, L.post_norm, self.n, eps=cfg.eps, residual=self.x, sum_out=self.h, stream=stream)
+            nxt = m.layers[i + 1].input_norm if i + 1 < len(m.layers) else m.final_norm
+            dbg = capi.MoeDebug(None, self.route_ids[i].data_ptr(), None, None, None) if record_routes else None
+            ctx.moe_layer(self.moe_cfg, self.moe_w[i], self.n, self.x, self.B, residual=self.h,
+                          next_norm_weight=nxt, next_normed=self.xn, debug=dbg, stream=stream)
+        ctx.head_topk(m.head, self.xn, self.ids, self.vals, stream=stream)
+
+    def launches_per_step(self):
+        """CUDA kernels one step launches (q4 matvec 1, norm 1, rope 1, MLA 4,
+        MoE layer 4, head 3 plus a memset)."""
+        return 1 + self.cfg.layers * (4 * 1 + 3 * 1 + 1 + 4 + 4) + 3
+
+    def unique_experts(self):
+        """Distinct routed experts per layer in the recorded routes (mean over layers)."""
+        ids = self.route_ids.cpu()
+        return sum(len(set(ids[i].reshape(-1).tolist())) for i in range(self.cfg.layers)) / self.cfg.layers
+
+    def bytes_per_step(self, unique_experts: float):
+        """Algorithmic bytes of one step: every weight byte read once (MLA
+        projections, absorbed W_UK/W_UV, norms, router, shared gate, shared
+        expert and `unique_experts` routed experts per layer), the cache rows
+        attended, the activations in and out, and the vocab head."""
+        cfg = self.cfg
+        slot = self.model.layers[0].moe.layout.expert_bytes
+        per_layer = (self.model.layers[0].nbytes() + cfg.experts * cfg.hidden * 2 + cfg.hidden * 2 +
+                     (1 + unique_experts) * slot)
+        kv = sum(p + 1 for p in self.positions_host) * (cfg.latent + cfg.rope) * 2
+        return int(cfg.layers * (per_layer + kv) + cfg.vocab * cfg.hidden * 2 + self.B * cfg.hidden * 4)
