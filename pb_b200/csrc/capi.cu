@@ -412,20 +412,45 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     a.expert_count = e_count;
     a.ep = ep;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = moe_layer_launch(a, s);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer launch");
-    if (debug) {
-        if (debug->router_logits)
-            e = cudaMemcpyAsync(debug->router_logits, a.ws.logits, size_t(tokens) * E * 4, cudaMemcpyDeviceToDevice, s);
-        if (e == cudaSuccess && debug->route_ids)
-            e = cudaMemcpyAsync(debug->route_ids, a.ws.route_ids, size_t(tokens) * K * 4, cudaMemcpyDeviceToDevice, s);
-        if (e == cudaSuccess && debug->route_weights)
-            e = cudaMemcpyAsync(debug->route_weights, a.ws.route_w, size_t(tokens) * K * 4, cudaMemcpyDeviceToDevice,
-                                s);
-        if (e == cudaSuccess && debug->shared_logit)
-            e = cudaMemcpyAsync(debug->shared_logit, a.ws.shared_logit, size_t(tokens) * 4, cudaMemcpyDeviceToDevice,
-                                s);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "moe debug copy");
+    // Batches above 8 tokens run as consecutive chunks of 8 through the
+    // pipelined expert kernels when those take the layout: every token's
+    // routing, combine and norm are its own, so the chunks compute exactly
+    // what the 8-token layer computes for those tokens. (Not with phase events,
+    // which time one launch, nor with expert parallelism, whose exchange
+    // buffers hold one launch's tokens.)
+    uint32_t chunk = tokens;
+    if (tokens > 8 && !ep && !a.phase_events) {
+        MoeLaunch probe = a;
+        probe.tokens = 8;
+        if (pbmoe::moe_pipe_supported(probe)) chunk = 8;
+    }
+    const size_t xs = x_dtype == PBMOE_BF16 ? 2 : 4, os = out_dtype == PBMOE_BF16 ? 2 : 4;
+    for (uint32_t c0 = 0; c0 < tokens; c0 += chunk) {
+        MoeLaunch b = a;
+        b.tokens = tokens - c0 < chunk ? tokens - c0 : chunk;
+        b.x = static_cast<const char*>(x) + size_t(c0) * H * xs;
+        b.residual = residual ? static_cast<const char*>(residual) + size_t(c0) * H * os : nullptr;
+        b.out = static_cast<char*>(out) + size_t(c0) * H * os;
+        b.next_normed = next_normed ? static_cast<char*>(next_normed) + size_t(c0) * H * os : nullptr;
+        cudaError_t e = moe_layer_launch(b, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer launch");
+        if (debug) {
+            const size_t n = b.tokens;
+            auto at = [](void* p, size_t off) { return static_cast<char*>(p) + off; };
+            if (debug->router_logits)
+                e = cudaMemcpyAsync(at(debug->router_logits, c0 * E * 4), a.ws.logits, n * E * 4,
+                                    cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && debug->route_ids)
+                e = cudaMemcpyAsync(at(debug->route_ids, c0 * K * 4), a.ws.route_ids, n * K * 4,
+                                    cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && debug->route_weights)
+                e = cudaMemcpyAsync(at(debug->route_weights, c0 * K * 4), a.ws.route_w, n * K * 4,
+                                    cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && debug->shared_logit)
+                e = cudaMemcpyAsync(at(debug->shared_logit, c0 * 4), a.ws.shared_logit, n * 4,
+                                    cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "moe debug copy");
+        }
     }
     return PBMOE_OK;
 }

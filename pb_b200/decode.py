@@ -181,9 +181,11 @@ class DecodeStep:
         ctx.head_topk(m.head, self.xn, self.ids, self.vals, stream=stream)
 
     def launches_per_step(self):
-        """CUDA kernels one step launches (q4 matvec 1, norm 1, rope 1, MLA 4,
-        MoE layer 4, head 3 plus a memset)."""
-        return 1 + self.cfg.layers * (4 * 1 + 3 * 1 + 1 + 4 + 4) + 3
+        """CUDA kernels one step launches: the input norm; per layer 4 q4
+        matvecs, 3 norms, RoPE/append, 4 MLA kernels and 4 MoE kernels per
+        8-token chunk; the head's 3 (plus a memset)."""
+        chunks = (self.B + 7) // 8
+        return 1 + self.cfg.layers * (4 + 3 + 1 + 4 + 4 * chunks) + 3
 
     def unique_experts(self):
         """Distinct routed experts per layer in the recorded routes (mean over layers)."""
