@@ -70,6 +70,8 @@ def parse():
                    help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3; "
                         "head: config 4's vocab head + top-k; step: config 4's full decode step")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--only-batch", action="store_true",
+                   help="head / step workloads: run the --batch case alone (no batch 1/8/32 listing)")
     return p.parse_args()
 
 
@@ -778,7 +780,7 @@ def run_head(args):
     w = synth.normal_bf16((V, H), 0.02, synth.gen("cuda", 4), "cuda")
     s = torch.cuda.Stream()
     cases, head = [], None
-    for B in (1, 8, 32):
+    for B in ([args.batch] if args.only_batch else (1, 8, 32)):
         x = synth.normal_bf16((B, H), 1.0, synth.gen("cuda", 40 + B), "cuda")
         ids = torch.empty(B, K, dtype=torch.int32, device="cuda")
         vals = torch.empty(B, K, device="cuda")
@@ -834,7 +836,7 @@ def run_step(args):
     model = decode.Model(cfg, seed=4)
     s = torch.cuda.Stream()
     cases, head = [], None
-    for B in sorted({1, 8, 32, args.batch}):
+    for B in ([args.batch] if args.only_batch else sorted({1, 8, 32, args.batch})):
         caches = decode.Caches(cfg, B, seed=B)
         step = decode.DecodeStep(ctx, model, caches, B, [cfg.context - 1] * B)
         x0 = torch.randn(B, cfg.hidden, generator=torch.Generator("cuda").manual_seed(B), device="cuda")
