@@ -440,6 +440,31 @@ PBMOE_API int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint3
                                uint32_t lists, uint32_t tokens, uint32_t top_k, uint32_t* out_ids,
                                float* out_values, void* stream);
 
+/* ---------------------------------------------------------------- expert store
+ * The fixed-Q4 expert layer store a pb expert cache holds
+ * (FIXED_Q4_EXPERT_LAYER_V1, experts/mod.rs:44-50): root/layer_NN.json
+ * (ExpertLayerPackMetadata, experts/mod.rs:306-454) and root/layer_NN.bin,
+ * expert e's slot at e * expert_size (experts/store.rs:1154-1158) in the
+ * QwenMoeQ4ExpertLayout byte image (model_family.rs:954-1010). The metadata is
+ * validated as ExpertLayerPackMetadata::validate does (experts/mod.rs:372-429)
+ * and every requested expert's records against `layout`; slot bytes are used
+ * as stored. This replaces the per-token pread of expert slots
+ * (scheduler/mod.rs:662, :808) with one load into the HBM-resident table that
+ * pbmoe_moe_weights.experts points at.
+ *
+ * pbmoe_expert_layer_read: into host memory (no device, no context);
+ * the message of a failure goes to error_buf. */
+PBMOE_API int pbmoe_expert_layer_read(const char* root, uint32_t layer, const pbmoe_expert_layout* layout,
+                                      uint32_t expert_begin, uint32_t expert_count, void* host_dst,
+                                      size_t dst_bytes, char* error_buf, size_t error_len);
+/* pbmoe_expert_layer_load: into device memory (dst_bytes >= expert_count *
+ * layout->expert_bytes), staged through pinned host buffers on `stream`;
+ * returns once the copies are complete. For expert parallelism a rank loads
+ * its own range (pbmoe_ep_expert_range). */
+PBMOE_API int pbmoe_expert_layer_load(pbmoe_ctx* ctx, const char* root, uint32_t layer,
+                                      const pbmoe_expert_layout* layout, uint32_t expert_begin,
+                                      uint32_t expert_count, void* device_dst, size_t dst_bytes, void* stream);
+
 /* ---------------------------------------------------------------- decode-step glue
  * Row RMSNorm, optionally fused with the residual add: s = x (+ residual);
  * sum_out (optional) receives s; out = s * 1/sqrt(mean(s^2) + epsilon) *

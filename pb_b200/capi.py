@@ -45,7 +45,8 @@ EXPORTED = [
     "pbmoe_prefill_reserve", "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
     "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
-    "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append",
+    "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
+    "pbmoe_expert_layer_load",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -163,6 +164,10 @@ def load():
         L.pbmoe_rms_norm.argtypes = [vp, C.POINTER(NormArgs), vp]
         L.pbmoe_rope_reserve.argtypes = [vp, u32, u32, C.c_double]
         L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, vp, vp, u32, vp]
+        L.pbmoe_expert_layer_read.argtypes = [C.c_char_p, u32, C.POINTER(ExpertLayout), u32, u32, vp, C.c_size_t,
+                                              C.c_char_p, C.c_size_t]
+        L.pbmoe_expert_layer_load.argtypes = [vp, C.c_char_p, u32, C.POINTER(ExpertLayout), u32, u32, vp,
+                                              C.c_size_t, vp]
         _lib = L
     return _lib
 
@@ -297,6 +302,12 @@ class Context:
                      st(x), st(residual), st(sum_out), st(out))
         self.check(self.lib.pbmoe_rms_norm(self.h, C.byref(a), self.stream_ptr(stream)))
 
+    def expert_layer_load(self, root, layer, layout: ExpertLayout, expert_begin, expert_count, dst, stream=None):
+        """FIXED_Q4_EXPERT_LAYER_V1 slots into the device tensor dst (>= count x expert_bytes bytes)."""
+        self.check(self.lib.pbmoe_expert_layer_load(self.h, str(root).encode(), layer, C.byref(layout), expert_begin,
+                                                    expert_count, _ptr(dst), dst.numel() * dst.element_size(),
+                                                    self.stream_ptr(stream)))
+
     def rope_reserve(self, max_positions, rope_dim, theta=10000.0):
         self.check(self.lib.pbmoe_rope_reserve(self.h, max_positions, rope_dim, theta))
 
@@ -379,6 +390,20 @@ def expert_matrix(experts, layout: ExpertLayout, num_experts, projection) -> Q4E
 
 def moe_config(layout: ExpertLayout, num_experts, top_k, normalization=0, routed_scale=1.0, eps=1e-6) -> MoeConfig:
     return MoeConfig(layout, num_experts, top_k, normalization, routed_scale, eps)
+
+
+def expert_layer_read(root, layer, layout: ExpertLayout, expert_begin, expert_count):
+    """Slots of experts [begin, begin + count) of a FIXED_Q4_EXPERT_LAYER_V1 store, as host bytes
+    (numpy uint8 [count, expert_bytes]); PbmoeError on invalid metadata."""
+    import numpy as np
+
+    out = np.zeros((expert_count, layout.expert_bytes), np.uint8)
+    err = C.create_string_buffer(512)
+    rc = load().pbmoe_expert_layer_read(str(root).encode(), layer, C.byref(layout), expert_begin, expert_count,
+                                        out.ctypes.data_as(C.c_void_p), out.nbytes, err, 512)
+    if rc != PBMOE_OK:
+        raise PbmoeError(rc, err.value.decode())
+    return out
 
 
 def ep_expert_range(num_experts, rank, world):

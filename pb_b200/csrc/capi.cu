@@ -1091,3 +1091,17 @@ int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* cfg, uint32_t 
     if (e != cudaSuccess) return cuda_fail(ctx, e, "mla rope append launch");
     return PBMOE_OK;
 }
+
+// ---------------------------------------------------------------- expert store
+int pbmoe_expert_layer_load(pbmoe_ctx* ctx, const char* root, uint32_t layer, const pbmoe_expert_layout* layout,
+                            uint32_t expert_begin, uint32_t expert_count, void* device_dst, size_t dst_bytes,
+                            void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    char msg[512] = {0};
+    const int rc = pbmoe::expert_layer_upload(root, layer, layout, expert_begin, expert_count, device_dst, dst_bytes,
+                                              static_cast<cudaStream_t>(stream), msg, sizeof msg);
+    if (rc != PBMOE_OK) return fail(ctx, rc, "%s", msg);
+    return PBMOE_OK;
+}

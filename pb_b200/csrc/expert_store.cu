@@ -1,0 +1,403 @@
+// expert_store.cu — the fixed-Q4 expert layer store (FIXED_Q4_EXPERT_LAYER_V1)
+// read into host or device memory: the HBM-resident expert table that
+// replaces the reference's per-token pread streaming of expert slots.
+//
+// Store format (experts/mod.rs:44-50, :306-430, :2478-2484): a directory
+// holding, per sparse layer N, layer_NN.json — serde JSON of
+// ExpertLayerPackMetadata {format, layer, expert_size, experts, packs[{layer,
+// expert, packed_bytes, records[{tensor, dtype, shape, source_offsets,
+// source_hash?, record_offset, packed_bytes, groups, group_size,
+// scale_bias_dtype}]}]} — and layer_NN.bin, expert e's slot at byte e *
+// expert_size (expert_slot_offset, experts/store.rs:1154-1158). A fixed-Q4
+// slot is the QwenMoeQ4ExpertLayout byte image (gate, up, down, each nibbles
+// then bf16 scales then bf16 biases; model_family.rs:954-1010), one record
+// per projection with record_offset at its nibbles, packed_bytes the nibble
+// bytes and groups the scale count (fixed_q4_pack_from_pbq4_records,
+// experts/slots.rs:984-1113).
+//
+// Validation restates ExpertLayerPackMetadata::validate (experts/mod.rs:
+// 372-429) and checks each requested expert's records against the layout the
+// caller expects. Host code only: the device upload is plain cudaMemcpyAsync
+// of double-buffered pinned chunks.
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <fcntl.h>
+#include <unistd.h>
+
+#include "kernels.h"
+
+namespace {
+
+// ---------------------------------------------------------------- minimal JSON
+struct Json {
+    enum Kind { Null, Bool, Number, String, Array, Object } kind = Null;
+    bool b = false;
+    bool integral = false;
+    unsigned long long u = 0;  // when integral and non-negative
+    double d = 0.0;
+    std::string s;
+    std::vector<Json> a;
+    std::vector<std::pair<std::string, Json>> o;
+    const Json* get(const char* key) const {
+        for (const auto& kv : o)
+            if (kv.first == key) return &kv.second;
+        return nullptr;
+    }
+};
+
+struct Parser {
+    const char* p;
+    const char* end;
+    std::string err;
+    void ws() {
+        while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+    }
+    bool fail(const char* what) {
+        if (err.empty()) err = what;
+        return false;
+    }
+    bool lit(const char* w) {
+        const size_t n = std::strlen(w);
+        if (size_t(end - p) < n || std::strncmp(p, w, n) != 0) return fail("bad literal");
+        p += n;
+        return true;
+    }
+    bool str(std::string& out) {
+        if (p >= end || *p != '"') return fail("expected string");
+        ++p;
+        while (p < end && *p != '"') {
+            char c = *p++;
+            if (c == '\\') {
+                if (p >= end) return fail("bad escape");
+                const char e = *p++;
+                switch (e) {
+                    case '"': case '\\': case '/': out += e; break;
+                    case 'b': out += '\b'; break;
+                    case 'f': out += '\f'; break;
+                    case 'n': out += '\n'; break;
+                    case 'r': out += '\r'; break;
+                    case 't': out += '\t'; break;
+                    case 'u': {  // names and dtypes are ASCII; keep the code unit as '?'
+                        if (end - p < 4) return fail("bad \\u escape");
+                        p += 4;
+                        out += '?';
+                        break;
+                    }
+                    default: return fail("bad escape");
+                }
+            } else {
+                out += c;
+            }
+        }
+        if (p >= end) return fail("unterminated string");
+        ++p;
+        return true;
+    }
+    bool num(Json& v) {
+        const char* s = p;
+        bool neg = false, frac = false;
+        if (p < end && *p == '-') neg = true, ++p;
+        while (p < end && ((*p >= '0' && *p <= '9') || *p == '.' || *p == 'e' || *p == 'E' || *p == '+' || *p == '-')) {
+            if (*p == '.' || *p == 'e' || *p == 'E') frac = true;
+            ++p;
+        }
+        if (p == s) return fail("expected number");
+        const std::string t(s, p);
+        v.kind = Json::Number;
+        v.d = std::strtod(t.c_str(), nullptr);
+        if (!neg && !frac) {
+            v.integral = true;
+            v.u = std::strtoull(t.c_str(), nullptr, 10);
+        }
+        return true;
+    }
+    bool value(Json& v, int depth) {
+        if (depth > 32) return fail("nesting too deep");
+        ws();
+        if (p >= end) return fail("unexpected end");
+        const char c = *p;
+        if (c == '{') {
+            ++p;
+            v.kind = Json::Object;
+            ws();
+            if (p < end && *p == '}') return ++p, true;
+            for (;;) {
+                ws();
+                std::string k;
+                if (!str(k)) return false;
+                ws();
+                if (p >= end || *p != ':') return fail("expected ':'");
+                ++p;
+                v.o.emplace_back(std::move(k), Json());
+                if (!value(v.o.back().second, depth + 1)) return false;
+                ws();
+                if (p < end && *p == ',') { ++p; continue; }
+                if (p < end && *p == '}') return ++p, true;
+                return fail("expected ',' or '}'");
+            }
+        }
+        if (c == '[') {
+            ++p;
+            v.kind = Json::Array;
+            ws();
+            if (p < end && *p == ']') return ++p, true;
+            for (;;) {
+                v.a.emplace_back();
+                if (!value(v.a.back(), depth + 1)) return false;
+                ws();
+                if (p < end && *p == ',') { ++p; continue; }
+                if (p < end && *p == ']') return ++p, true;
+                return fail("expected ',' or ']'");
+            }
+        }
+        if (c == '"') return v.kind = Json::String, str(v.s);
+        if (c == 't') return v.kind = Json::Bool, v.b = true, lit("true");
+        if (c == 'f') return v.kind = Json::Bool, v.b = false, lit("false");
+        if (c == 'n') return v.kind = Json::Null, lit("null");
+        return num(v);
+    }
+};
+
+struct Err {
+    char* buf;
+    size_t len;
+    int fail(int code, const char* fmt, ...) {
+        if (buf && len) {
+            va_list ap;
+            va_start(ap, fmt);
+            vsnprintf(buf, len, fmt, ap);
+            va_end(ap);
+        }
+        return code;
+    }
+};
+
+bool get_u64(const Json& obj, const char* key, unsigned long long& out) {
+    const Json* v = obj.get(key);
+    if (!v || v->kind != Json::Number || !v->integral) return false;
+    out = v->u;
+    return true;
+}
+
+bool ends_with(const std::string& s, const char* suffix) {
+    const size_t n = std::strlen(suffix);
+    return s.size() >= n && s.compare(s.size() - n, n, suffix) == 0;
+}
+
+std::string layer_file(const char* root, uint32_t layer, const char* ext) {
+    char name[64];
+    snprintf(name, sizeof name, "/layer_%02u.%s", layer, ext);
+    return std::string(root) + name;
+}
+
+bool read_file(const std::string& path, std::string& out) {
+    FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return false;
+    char buf[1 << 16];
+    size_t n;
+    while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) out.append(buf, n);
+    const bool ok = !std::ferror(f);
+    std::fclose(f);
+    return ok;
+}
+
+}  // namespace
+
+// Parse and validate layer `layer`'s metadata for the slots of experts
+// [begin, begin + count) in layout L.
+static int check_metadata(const char* root, uint32_t layer, const pbmoe_expert_layout* L, uint32_t begin,
+                          uint32_t count, Err& e) {
+    const std::string path = layer_file(root, layer, "json");
+    std::string text;
+    if (!read_file(path, text))
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s cannot be read", path.c_str());
+    Json meta;
+    Parser ps{text.data(), text.data() + text.size(), {}};
+    if (!ps.value(meta, 0) || meta.kind != Json::Object)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "failed to parse expert metadata %s: %s", path.c_str(),
+                      ps.err.empty() ? "not an object" : ps.err.c_str());
+    const Json* fmt = meta.get("format");
+    if (!fmt || fmt->kind != Json::String)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has no format", path.c_str());
+    if (fmt->s != "FIXED_Q4_EXPERT_LAYER_V1")
+        return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert storage format %s in %s (this loader "
+                      "reads FIXED_Q4_EXPERT_LAYER_V1)", fmt->s.c_str(), path.c_str());
+    unsigned long long mlayer, expert_size, experts;
+    if (!get_u64(meta, "layer", mlayer) || !get_u64(meta, "expert_size", expert_size) ||
+        !get_u64(meta, "experts", experts))
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s lacks layer/expert_size/experts", path.c_str());
+    if (mlayer != layer)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s describes layer %llu, expected layer %u",
+                      path.c_str(), mlayer, layer);
+    if (expert_size == 0) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has zero expert_size", path.c_str());
+    if (experts == 0) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has zero experts", path.c_str());
+    if (expert_size != L->expert_bytes)
+        return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert slot size %llu in %s (layout %llu bytes)",
+                      expert_size, path.c_str(), static_cast<unsigned long long>(L->expert_bytes));
+    if (uint64_t(begin) + count > experts)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "experts [%u, %u) outside the %llu of %s", begin, begin + count,
+                      experts, path.c_str());
+    const Json* packs = meta.get("packs");
+    if (!packs || packs->kind != Json::Array)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has no packs", path.c_str());
+    std::vector<char> seen(experts, 0);
+    // (rows, cols) of gate, up, down and their component indices
+    const uint64_t H = L->hidden, I = L->intermediate, G = L->group_size;
+    const uint64_t shapes[3][2] = {{I, H}, {I, H}, {H, I}};
+    const char* names[3] = {"gate_proj.weight", "up_proj.weight", "down_proj.weight"};
+    for (const Json& pk : packs->a) {
+        unsigned long long pl, ex, pb;
+        if (pk.kind != Json::Object || !get_u64(pk, "layer", pl) || !get_u64(pk, "expert", ex))
+            return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has a malformed pack", path.c_str());
+        if (pl != layer)
+            return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s describes layer %llu expert %llu, expected "
+                          "layer %u expert %llu", path.c_str(), pl, ex, layer, ex);
+        if (ex >= experts)
+            return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s describes expert %llu outside 0..%llu",
+                          path.c_str(), ex, experts);
+        if (seen[ex]) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has duplicate expert %llu", path.c_str(), ex);
+        seen[ex] = 1;
+        if (!get_u64(pk, "packed_bytes", pb)) pb = 0;  // serde default
+        if (pb > expert_size)
+            return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s expert %llu length %llu exceeds slot size %llu",
+                          path.c_str(), ex, pb, expert_size);
+        if (ex < begin || ex >= uint64_t(begin) + count) continue;
+        // the records of a requested expert must describe this layout
+        const Json* recs = pk.get("records");
+        if (!recs || recs->kind != Json::Array || recs->a.size() != 3)
+            return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported fixed-Q4 expert %llu in %s: expected gate, up "
+                          "and down records", ex, path.c_str());
+        for (int j = 0; j < 3; ++j) {
+            const Json& r = recs->a[j];
+            const Json* tn = r.get("tensor");
+            const Json* sb = r.get("scale_bias_dtype");
+            const Json* sh = r.get("shape");
+            unsigned long long off, bytes, groups, gs;
+            const bool ok = r.kind == Json::Object && tn && tn->kind == Json::String && ends_with(tn->s, names[j]) &&
+                            get_u64(r, "record_offset", off) && get_u64(r, "packed_bytes", bytes) &&
+                            get_u64(r, "groups", groups) && get_u64(r, "group_size", gs) && sh &&
+                            sh->kind == Json::Array && sh->a.size() == 2 && sh->a[0].integral && sh->a[1].integral;
+            if (!ok)
+                return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported fixed-Q4 expert %llu in %s: record %d is "
+                              "not a %s record", ex, path.c_str(), j, names[j]);
+            const uint64_t rows = shapes[j][0], cols = shapes[j][1];
+            const bool match = sh->a[0].u == rows && sh->a[1].u == cols && gs == G && off == L->component_offsets[3 * j] &&
+                               bytes == rows * cols / 2 && groups == rows * (cols / G) &&
+                               (!sb || (sb->kind == Json::String && sb->s == "BF16"));
+            if (!match)
+                return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported fixed-Q4 expert %llu in %s: %s does not "
+                              "match the layout (hidden %llu, intermediate %llu, group %llu)", ex, path.c_str(),
+                              tn->s.c_str(), (unsigned long long)H, (unsigned long long)I, (unsigned long long)G);
+        }
+    }
+    for (uint64_t x = begin; x < uint64_t(begin) + count; ++x)
+        if (!seen[x])
+            return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer %u has no metadata for expert %llu", layer,
+                          static_cast<unsigned long long>(x));
+    return PBMOE_OK;
+}
+
+// pread of `bytes` at `offset`, all or nothing
+static bool pread_all(int fd, void* dst, size_t bytes, uint64_t offset) {
+    char* p = static_cast<char*>(dst);
+    while (bytes) {
+        const ssize_t n = pread(fd, p, bytes, static_cast<off_t>(offset));
+        if (n <= 0) return false;
+        p += n;
+        bytes -= size_t(n);
+        offset += uint64_t(n);
+    }
+    return true;
+}
+
+static int open_slots(const char* root, uint32_t layer, const pbmoe_expert_layout* L, uint32_t begin,
+                      uint32_t count, size_t dst_bytes, Err& e, int* fd_out) {
+    if (!root || !L || L->expert_bytes == 0)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer read: null root or layout");
+    if (count == 0) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer read: no experts requested");
+    if (dst_bytes < uint64_t(count) * L->expert_bytes)
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer read: %u slots of %llu bytes exceed the destination "
+                      "(%zu bytes)", count, static_cast<unsigned long long>(L->expert_bytes), dst_bytes);
+    const int rc = check_metadata(root, layer, L, begin, count, e);
+    if (rc != PBMOE_OK) return rc;
+    const std::string bin = layer_file(root, layer, "bin");
+    const int fd = open(bin.c_str(), O_RDONLY);
+    if (fd < 0) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer %s cannot be opened", bin.c_str());
+    const off_t size = lseek(fd, 0, SEEK_END);
+    if (size < 0 || uint64_t(size) < (uint64_t(begin) + count) * L->expert_bytes) {
+        close(fd);
+        return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer %s is %lld bytes, shorter than experts [%u, %u)",
+                      bin.c_str(), static_cast<long long>(size), begin, begin + count);
+    }
+    *fd_out = fd;
+    return PBMOE_OK;
+}
+
+extern "C" int pbmoe_expert_layer_read(const char* root, uint32_t layer, const pbmoe_expert_layout* layout,
+                                       uint32_t expert_begin, uint32_t expert_count, void* host_dst,
+                                       size_t dst_bytes, char* error_buf, size_t error_len) {
+    Err e{error_buf, error_len};
+    if (!host_dst) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer read: null destination");
+    int fd = -1;
+    const int rc = open_slots(root, layer, layout, expert_begin, expert_count, dst_bytes, e, &fd);
+    if (rc != PBMOE_OK) return rc;
+    const bool ok = pread_all(fd, host_dst, size_t(expert_count) * layout->expert_bytes,
+                              uint64_t(expert_begin) * layout->expert_bytes);
+    close(fd);
+    if (!ok) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer %u: read of experts [%u, %u) failed", layer,
+                           expert_begin, expert_begin + expert_count);
+    return PBMOE_OK;
+}
+
+// Device upload through two pinned staging buffers: while chunk i copies to
+// the device, chunk i+1 is read from the file.
+int pbmoe::expert_layer_upload(const char* root, uint32_t layer, const pbmoe_expert_layout* layout,
+                               uint32_t expert_begin, uint32_t expert_count, void* device_dst, size_t dst_bytes,
+                               cudaStream_t stream, char* error_buf, size_t error_len) {
+    Err e{error_buf, error_len};
+    if (!device_dst) return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer load: null destination");
+    int fd = -1;
+    int rc = open_slots(root, layer, layout, expert_begin, expert_count, dst_bytes, e, &fd);
+    if (rc != PBMOE_OK) return rc;
+    constexpr size_t kChunk = size_t(64) << 20;
+    const size_t total = size_t(expert_count) * layout->expert_bytes;
+    const uint64_t base = uint64_t(expert_begin) * layout->expert_bytes;
+    void* stage[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    rc = PBMOE_OK;
+    for (int i = 0; i < 2 && rc == PBMOE_OK; ++i) {
+        if (cudaMallocHost(&stage[i], kChunk) != cudaSuccess || cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) != cudaSuccess)
+            rc = e.fail(PBMOE_ERR_CUDA, "expert layer load: pinned staging allocation failed");
+    }
+    for (size_t off = 0, i = 0; rc == PBMOE_OK && off < total; off += kChunk, ++i) {
+        const int b = int(i & 1);
+        const size_t n = total - off < kChunk ? total - off : kChunk;
+        if (i >= 2 && cudaEventSynchronize(done[b]) != cudaSuccess) {
+            rc = e.fail(PBMOE_ERR_CUDA, "expert layer load: staging wait failed");
+            break;
+        }
+        if (!pread_all(fd, stage[b], n, base + off)) {
+            rc = e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert layer %u: read at offset %llu failed", layer,
+                        static_cast<unsigned long long>(base + off));
+            break;
+        }
+        if (cudaMemcpyAsync(static_cast<char*>(device_dst) + off, stage[b], n, cudaMemcpyHostToDevice, stream) !=
+                cudaSuccess ||
+            cudaEventRecord(done[b], stream) != cudaSuccess)
+            rc = e.fail(PBMOE_ERR_CUDA, "expert layer load: copy to the device failed");
+    }
+    for (int i = 0; i < 2; ++i) {
+        if (done[i]) {
+            cudaEventSynchronize(done[i]);
+            cudaEventDestroy(done[i]);
+        }
+        if (stage[i]) cudaFreeHost(stage[i]);
+    }
+    close(fd);
+    return rc;
+}

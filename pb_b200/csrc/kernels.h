@@ -263,6 +263,14 @@ struct RopeAppendArgs {
 bool rope_append_supported(uint32_t heads, uint32_t rope);
 cudaError_t mla_rope_append_launch(const RopeAppendArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- expert store (expert_store.cu)
+// Validated FIXED_Q4_EXPERT_LAYER_V1 slots of experts [expert_begin,
+// expert_begin + expert_count) copied to device memory on `stream`
+// (synchronised before return); a PBMOE_* status, message in error_buf.
+int expert_layer_upload(const char* root, uint32_t layer, const pbmoe_expert_layout* layout, uint32_t expert_begin,
+                        uint32_t expert_count, void* device_dst, size_t dst_bytes, cudaStream_t stream,
+                        char* error_buf, size_t error_len);
+
 // ---------------------------------------------------------------- vocab head (head.cu)
 // logits[t][v] = W[v] . x[t] for the rows [0, vocab) of a (possibly sharded)
 // head whose row 0 is global token id `id_base`, then each token's top_k

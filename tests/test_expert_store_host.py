@@ -1,0 +1,103 @@
+"""The fixed-Q4 expert layer store reader (pbmoe_expert_layer_read) on CPU:
+slots read back byte-exact, and the metadata checks of
+ExpertLayerPackMetadata::validate (experts/mod.rs:372-429) plus the record
+checks against the layout, each failing with its message."""
+
+import numpy as np
+import pytest
+
+from expert_store_writer import write_layer
+
+H, I, G, E = 128, 64, 32, 6
+
+
+@pytest.fixture()
+def store(tmp_path):
+    from pb_b200 import capi
+
+    lay = capi.fixed_q4_layout(H, I, G)
+    rng = np.random.default_rng(1)
+    slots = rng.integers(0, 256, (E, lay.expert_bytes), dtype=np.uint8)
+    offs = list(lay.component_offsets)
+    return tmp_path, lay, slots, offs
+
+
+def test_read_all_and_a_range(store):
+    from pb_b200 import capi
+
+    root, lay, slots, offs = store
+    write_layer(str(root), 3, slots, H, I, G, offs)
+    assert np.array_equal(capi.expert_layer_read(root, 3, lay, 0, E), slots)
+    assert np.array_equal(capi.expert_layer_read(root, 3, lay, 2, 3), slots[2:5])
+
+
+@pytest.mark.parametrize("edit,match", [
+    (lambda m: m.update(format="PBQ4EXPERT_LAYER_V2"), "unsupported expert storage format"),
+    (lambda m: m.update(layer=4), "describes layer 4"),
+    (lambda m: m.update(expert_size=m["expert_size"] + 16), "unsupported expert slot size"),
+    (lambda m: m.update(experts=0), "zero experts"),
+    (lambda m: m["packs"][1].update(expert=0), "duplicate expert 0"),
+    (lambda m: m["packs"][1].update(expert=99), "outside 0..6"),
+    (lambda m: m["packs"][2].update(packed_bytes=m["expert_size"] + 1), "exceeds slot size"),
+    (lambda m: m["packs"].pop(4), "no metadata for expert 4"),
+    (lambda m: m["packs"][0]["records"][1].update(record_offset=0), "does not match the layout"),
+    (lambda m: m["packs"][0]["records"][2].update(shape=[I, H]), "does not match the layout"),
+    (lambda m: m["packs"][0]["records"][0].update(group_size=64), "does not match the layout"),
+    (lambda m: m["packs"][0]["records"][0].update(tensor="x.up_proj.weight"), "not a gate_proj.weight record"),
+    (lambda m: m["packs"][0].update(records=m["packs"][0]["records"][:2]), "expected gate, up and down"),
+])
+def test_invalid_metadata(store, edit, match):
+    from pb_b200 import capi
+
+    root, lay, slots, offs = store
+    write_layer(str(root), 3, slots, H, I, G, offs, meta_edit=edit)
+    with pytest.raises(capi.PbmoeError, match=match):
+        capi.expert_layer_read(root, 3, lay, 0, E)
+
+
+def test_range_outside_and_short_file(store):
+    from pb_b200 import capi
+
+    root, lay, slots, offs = store
+    write_layer(str(root), 0, slots, H, I, G, offs)
+    with pytest.raises(capi.PbmoeError, match="outside the 6"):
+        capi.expert_layer_read(root, 0, lay, 4, 3)
+    with open(root / "layer_00.bin", "r+b") as f:
+        f.truncate(lay.expert_bytes * 4 + 10)
+    with pytest.raises(capi.PbmoeError, match="shorter than experts"):
+        capi.expert_layer_read(root, 0, lay, 0, E)
+    assert np.array_equal(capi.expert_layer_read(root, 0, lay, 1, 3), slots[1:4])
+
+
+def test_missing_and_malformed_metadata(store):
+    from pb_b200 import capi
+
+    root, lay, slots, offs = store
+    with pytest.raises(capi.PbmoeError, match="cannot be read"):
+        capi.expert_layer_read(root, 7, lay, 0, 1)
+    write_layer(str(root), 7, slots, H, I, G, offs)
+    (root / "layer_07.json").write_text('{"format": "FIXED_Q4_EXPERT_LAYER_V1", "layer": 7,')
+    with pytest.raises(capi.PbmoeError, match="failed to parse"):
+        capi.expert_layer_read(root, 7, lay, 0, 1)
+
+
+def test_partial_groups_rejected(tmp_path):
+    """The reference's fixed layout allows a partial last group (its test at
+    experts/parity_tests.rs:405-461 uses a down projection of 2 columns with
+    group 64); the kernels here need whole groups, so such a store is
+    refused: pbmoe_fixed_q4_layout rejects the shape outright."""
+    from pb_b200 import capi
+
+    with pytest.raises(capi.PbmoeError):
+        capi.fixed_q4_layout(64, 2, 64)
+
+
+def test_record_offsets_are_the_weight_components(store):
+    """Each record's record_offset is its projection's nibble offset in the
+    slot (gate, up, down), as fixed_q4_pack_from_pbq4_records writes it."""
+    from expert_store_writer import records_for
+
+    _, lay, _, offs = store
+    recs = records_for(0, 0, H, I, G, offs)
+    assert [r["record_offset"] for r in recs] == [offs[0], offs[3], offs[6]]
+    assert offs[3] == offs[0] + I * H // 2 + 2 * 2 * I * (H // G)
