@@ -66,9 +66,10 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla", "head", "step"],
+    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla", "head", "step", "mxfp4"],
                    help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3; "
-                        "head: config 4's vocab head + top-k; step: config 4's full decode step")
+                        "head: config 4's vocab head + top-k; step: config 4's full decode step; "
+                        "mxfp4: the config-0 matvec in MXFP4")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--only-batch", action="store_true",
                    help="head / step workloads: run the --batch case alone (no batch 1/8/32 listing)")
@@ -245,7 +246,7 @@ def main():
         return
     if args.workload != "moe":
         {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla, "head": run_head,
-         "step": run_step}[args.workload](args)
+         "step": run_step, "mxfp4": run_mxfp4}[args.workload](args)
         return
     import numpy as np
     import torch
@@ -762,6 +763,58 @@ def run_mla(args):
                      "frac": gbs / peak, "peak_kind": kind, "traffic": None,
                      "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"]},
         "cases": cases, "gpu_launches": head["steps"] * 4, "clocks": head["clocks"], "cpu_baseline": None,
+    })
+    ctx.close()
+
+
+def run_mxfp4(args):
+    """The config-0 matvec shape in MXFP4 (survey row f4): W [4096 x 2048]
+    E2M1 + E8M0 per 32 columns, x bf16 [1 x 2048], y bf16; 64 distinct
+    matrices cycled (285 MB > L2)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    R, Cc, NC = 4096, 2048, 64
+    byts = R * Cc // 2 + R * Cc // 32 + Cc * 2 + R * 2
+    ctx = capi.Context(0)
+    g = torch.Generator("cuda").manual_seed(5)
+    mats = [(torch.randint(0, 256, (R, Cc // 2), dtype=torch.uint8, device="cuda", generator=g),
+             torch.randint(118, 136, (R, Cc // 32), dtype=torch.uint8, device="cuda", generator=g)) for _ in range(NC)]
+    x = synth.normal_bf16((1, Cc), 1.0, synth.gen("cuda", 6), "cuda")
+    y = torch.empty(1, R, device="cuda", dtype=torch.bfloat16)
+    s = torch.cuda.Stream()
+    calls = [(lambda m=m: ctx.mxfp4_matvec(m[0], m[1], R, Cc, x, y, stream=s)) for m in mats]
+    ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
+    gbs = byts / (ms / 1e3) / 1e9
+    hx = x.cpu().pin_memory()
+    hy = torch.empty(1, R, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(x)
+    it = [0]
+
+    def e2e():
+        m = mats[it[0] % NC]
+        it[0] += 1
+        dx.copy_(hx, non_blocking=True)
+        ctx.mxfp4_matvec(m[0], m[1], R, Cc, dx, y, stream=s)
+        hy.copy_(y, non_blocking=True)
+
+    ems = _e2e_time(e2e, s, min(args.steps, 4 * NC))
+    peak, kind = measured_peaks()
+    _emit({
+        "metric": "MXFP4 matvec HBM GB/s (W E2M1/E8M0 [4096x2048] x bf16 [1x2048] -> bf16)", "value": gbs,
+        "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; uniform nibbles, E8M0 in [118, 136))",
+        "config": {"workload": "MXFP4 matvec (config-0 shape)", "rows": R, "cols": Cc, "group": 32,
+                   "l2": f"inputs larger than L2: {NC} distinct matrices cycled ({NC * byts / 1e6:.0f} MB)",
+                   "graph": f"CUDA graph of {NC} launches"},
+        "e2e": {"value": byts / (ems / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": Cc * 2,
+                "d2h_bytes_per_step": R * 2, "steps": min(args.steps, 4 * NC)},
+        "roofline": {"bound": "hbm", "kernel": "mxfp4_matvec", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": byts, "launch_ms": ms},
+        "gpu_launches": steps, "clocks": clocks, "cpu_baseline": None,
     })
     ctx.close()
 

@@ -68,6 +68,7 @@ typedef enum pbmoe_status {
 #define PBMOE_DEV_ERR_PIPE_TIMEOUT 0x8u  /* an asynchronous copy wait expired          */
 #define PBMOE_DEV_ERR_F16_RANGE 0x10u    /* prefill GEMM input |x| >= 65536 or non-finite */
 #define PBMOE_DEV_ERR_POSITION 0x20u     /* decode position past the cache or RoPE table  */
+#define PBMOE_DEV_ERR_MXFP4_SCALE 0x40u  /* an E8M0 scale byte 255 (not finite)           */
 
 typedef enum pbmoe_dtype {
     PBMOE_F32 = 0,
@@ -439,6 +440,25 @@ PBMOE_API int pbmoe_head_topk(pbmoe_ctx* ctx, const pbmoe_head* head, const void
 PBMOE_API int pbmoe_head_merge(pbmoe_ctx* ctx, const uint32_t* keys, const uint32_t* ids, const float* values,
                                uint32_t lists, uint32_t tokens, uint32_t top_k, uint32_t* out_ids,
                                float* out_values, void* stream);
+
+/* ---------------------------------------------------------------- MXFP4
+ * An MXFP4 matrix [rows x cols]: E2M1 nibbles row-major (low nibble = even
+ * column; magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6, bit 3 the sign) and one E8M0
+ * scale byte per 32 columns (2^(e-127); e = 0 is 2^-127), the GLM-5.2 expert
+ * format (FIXED_MXFP4_EXPERT_LAYER_V1, experts/mod.rs:49). */
+typedef struct pbmoe_mxfp4_tensor {
+    const void* packed;    /* [rows x cols/2], 16-byte aligned rows */
+    const uint8_t* scales; /* [rows x cols/group]                   */
+    uint32_t rows, cols;   /* cols a multiple of 32                 */
+    uint32_t group_size;   /* 32                                    */
+} pbmoe_mxfp4_tensor;
+
+/* y[t] = W x[t] for `batch` tokens (x bf16 or f32 [batch x cols], y [batch x
+ * rows]), f32 accumulate: mxfp4_fma_matvec_e8m0 (shaders.metal:200-298) /
+ * mxfp4_fma_matvec_with_group_size (experts/slots.rs:1239-1287). A scale
+ * byte 255, where the reference bails, latches PBMOE_DEV_ERR_MXFP4_SCALE. */
+PBMOE_API int pbmoe_mxfp4_matvec(pbmoe_ctx* ctx, const pbmoe_mxfp4_tensor* w, const void* x, pbmoe_dtype x_dtype,
+                                 void* y, pbmoe_dtype y_dtype, uint32_t batch, void* stream);
 
 /* ---------------------------------------------------------------- expert store
  * The fixed-Q4 expert layer store a pb expert cache holds

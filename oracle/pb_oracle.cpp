@@ -681,6 +681,35 @@ int oracle_q4_gemm(const float* x, size_t m, const uint8_t* packed, const uint16
     return kOk;
 }
 
+// mxfp4_fma_matvec_with_group_size (experts/slots.rs:1239-1287): E2M1 nibbles
+// (low nibble = even column; magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6, bit 3 the
+// sign) times E8M0 scales (2^(e-127); e = 0 is the f32 bit pattern
+// 0x00400000, i.e. 2^-127) per group, sum += weight * scale * x in column
+// order. A non-finite scale (e = 255) is the reference's bail: returns -2.
+int oracle_mxfp4_matvec(const uint8_t* packed, const float* input, const uint8_t* scales, size_t rows,
+                        size_t cols, size_t group, float* out) {
+    static const float kMag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    if (group == 0) return kInvalid;
+    const size_t row_bytes = (cols + 1) / 2, groups = (cols + group - 1) / group;
+    for (size_t r = 0; r < rows; ++r) {
+        float sum = 0.0f;
+        for (size_t c = 0; c < cols; ++c) {
+            const uint8_t byte = packed[r * row_bytes + c / 2];
+            const uint8_t nib = (c % 2 == 0) ? (byte & 0x0f) : (byte >> 4);
+            const float mag = kMag[nib & 0x07];
+            const float weight = (nib & 0x08) == 0 ? mag : -mag;
+            const uint8_t sb = scales[r * groups + c / group];
+            const uint32_t bits = sb == 0 ? 0x00400000u : (uint32_t(sb) << 23);
+            float scale;
+            std::memcpy(&scale, &bits, 4);
+            if (!std::isfinite(scale)) return -2;
+            sum += weight * scale * input[c];
+        }
+        out[r] = sum;
+    }
+    return kOk;
+}
+
 // topk_vocab (shaders.metal:1796-1831), the LM-head candidate selection of
 // MetalResidentTopKBuilder (metal/mod.rs:2661-2800): min(top_k, vocab) passes;
 // each takes the first allowed index not chosen by an earlier pass, replaced

@@ -86,6 +86,7 @@ def _declare(L):
         _sz, _sz, _sz, _sz, _sz, _f32p,
     ]
     L.oracle_q4_gemm.argtypes = [_f32p, _sz, _u8p, _u16p, _u16p, _sz, _sz, _sz, _f32p, C.c_int]
+    L.oracle_mxfp4_matvec.argtypes = [_u8p, _f32p, _u8p, _sz, _sz, _sz, _f32p]
     L.oracle_topk_vocab.restype = _sz
     L.oracle_topk_vocab.argtypes = [_f32p, _sz, _sz, C.c_void_p, _u32p, _f32p]
 
@@ -336,3 +337,12 @@ def head_topk(weight_bits, x, top_k, allowed=None):
     logits = np.stack([dense_bf16_matvec(w, row, V, H) for row in xs])
     res = [topk_vocab(row, top_k, allowed) for row in logits]
     return np.stack([r[0] for r in res]), np.stack([r[1] for r in res]), logits
+
+
+# ---------------------------------------------------------------- MXFP4
+def mxfp4_matvec(packed, x, scales, rows, cols, group=32):
+    """y = W x for MXFP4 W (E2M1 nibbles, E8M0 scale bytes per group)."""
+    out = np.zeros(rows, np.float32)
+    _check(lib().oracle_mxfp4_matvec(_c(packed, np.uint8), _c(x, np.float32), _c(scales, np.uint8), rows, cols,
+                                     group, out), "mxfp4_matvec")
+    return out

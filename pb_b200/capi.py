@@ -29,6 +29,7 @@ PBMOE_DEV_ERR_PEER_TIMEOUT = 0x4
 PBMOE_DEV_ERR_PIPE_TIMEOUT = 0x8
 PBMOE_DEV_ERR_F16_RANGE = 0x10
 PBMOE_DEV_ERR_POSITION = 0x20
+PBMOE_DEV_ERR_MXFP4_SCALE = 0x40
 
 PBMOE_F32 = 0
 PBMOE_BF16 = 1
@@ -46,7 +47,7 @@ EXPORTED = [
     "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
     "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
-    "pbmoe_expert_layer_load",
+    "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -100,6 +101,11 @@ class EpShard(C.Structure):
 
 class Head(C.Structure):
     _fields_ = [("weight", C.c_void_p), ("vocab", C.c_uint32), ("hidden", C.c_uint32), ("id_base", C.c_uint32)]
+
+
+class Mxfp4Tensor(C.Structure):
+    _fields_ = [("packed", C.c_void_p), ("scales", C.c_void_p), ("rows", C.c_uint32), ("cols", C.c_uint32),
+                ("group_size", C.c_uint32)]
 
 
 class NormArgs(C.Structure):
@@ -164,6 +170,7 @@ def load():
         L.pbmoe_rms_norm.argtypes = [vp, C.POINTER(NormArgs), vp]
         L.pbmoe_rope_reserve.argtypes = [vp, u32, u32, C.c_double]
         L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, vp, vp, u32, vp]
+        L.pbmoe_mxfp4_matvec.argtypes = [vp, C.POINTER(Mxfp4Tensor), vp, i32, vp, i32, u32, vp]
         L.pbmoe_expert_layer_read.argtypes = [C.c_char_p, u32, C.POINTER(ExpertLayout), u32, u32, vp, C.c_size_t,
                                               C.c_char_p, C.c_size_t]
         L.pbmoe_expert_layer_load.argtypes = [vp, C.c_char_p, u32, C.POINTER(ExpertLayout), u32, u32, vp,
@@ -307,6 +314,12 @@ class Context:
         self.check(self.lib.pbmoe_expert_layer_load(self.h, str(root).encode(), layer, C.byref(layout), expert_begin,
                                                     expert_count, _ptr(dst), dst.numel() * dst.element_size(),
                                                     self.stream_ptr(stream)))
+
+    def mxfp4_matvec(self, packed, scales, rows, cols, x, y, group=32, stream=None):
+        """y [batch, rows] = W x for MXFP4 W: packed uint8 [rows, cols/2], scales uint8 [rows, cols/group]."""
+        t = Mxfp4Tensor(packed.data_ptr(), scales.data_ptr(), rows, cols, group)
+        self.check(self.lib.pbmoe_mxfp4_matvec(self.h, C.byref(t), _ptr(x), _dtype_code(x), _ptr(y), _dtype_code(y),
+                                               int(x.shape[0]), self.stream_ptr(stream)))
 
     def rope_reserve(self, max_positions, rope_dim, theta=10000.0):
         self.check(self.lib.pbmoe_rope_reserve(self.h, max_positions, rope_dim, theta))

@@ -1105,3 +1105,24 @@ int pbmoe_expert_layer_load(pbmoe_ctx* ctx, const char* root, uint32_t layer, co
     if (rc != PBMOE_OK) return fail(ctx, rc, "%s", msg);
     return PBMOE_OK;
 }
+
+// ---------------------------------------------------------------- MXFP4
+int pbmoe_mxfp4_matvec(pbmoe_ctx* ctx, const pbmoe_mxfp4_tensor* w, const void* x, pbmoe_dtype x_dtype, void* y,
+                       pbmoe_dtype y_dtype, uint32_t batch, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!w || !w->packed || !w->scales || !x || !y)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mxfp4 matvec: null pointer");
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mxfp4 matvec: dtypes must be f32 or bf16");
+    if (batch == 0 || w->rows == 0) return PBMOE_OK;
+    if (!pbmoe::mxfp4_supported(w->rows, w->cols, w->group_size, batch) || !aligned(w->packed, 16))
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported MXFP4 matvec: %u x %u, group %u (needs group 32, "
+                    "cols a multiple of 32, 16-byte aligned rows)", w->rows, w->cols, w->group_size);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    pbmoe::Mxfp4Args a{static_cast<const uint8_t*>(w->packed), w->scales, w->rows, w->cols, w->group_size, batch,
+                       x, x_dtype, y, y_dtype, ctx->status};
+    cudaError_t e = pbmoe::mxfp4_matvec_launch(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "mxfp4 matvec launch");
+    return PBMOE_OK;
+}

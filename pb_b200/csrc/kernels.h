@@ -263,6 +263,20 @@ struct RopeAppendArgs {
 bool rope_append_supported(uint32_t heads, uint32_t rope);
 cudaError_t mla_rope_append_launch(const RopeAppendArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- MXFP4 matvec (mxfp4.cu)
+struct Mxfp4Args {
+    const uint8_t* packed;  // [rows x cols/2] E2M1 nibbles, low nibble = even column
+    const uint8_t* scales;  // [rows x cols/32] E8M0
+    uint32_t rows, cols, group, batch;
+    const void* x;  // [batch x cols]
+    pbmoe_dtype x_dtype;
+    void* y;  // [batch x rows]
+    pbmoe_dtype y_dtype;
+    uint32_t* status;
+};
+bool mxfp4_supported(uint32_t rows, uint32_t cols, uint32_t group, uint32_t batch);
+cudaError_t mxfp4_matvec_launch(const Mxfp4Args& a, cudaStream_t s);
+
 // ---------------------------------------------------------------- expert store (expert_store.cu)
 // Validated FIXED_Q4_EXPERT_LAYER_V1 slots of experts [expert_begin,
 // expert_begin + expert_count) copied to device memory on `stream`
