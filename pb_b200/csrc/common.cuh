@@ -168,4 +168,23 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" :::);
 }
 
+// Host: launch `fn` with programmatic stream serialization, so it may start
+// while its predecessor in the stream finishes; the kernel must call
+// pdl_wait() before reading anything an earlier kernel wrote.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_kernel(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, static_cast<KArgs>(args)...);
+}
+
 }  // namespace pbmoe

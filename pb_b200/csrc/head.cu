@@ -48,6 +48,8 @@ head_gemv_kernel(const uint16_t* __restrict__ W, uint32_t V, uint32_t H, const X
     // bf16 activations are exact in bf16: their lo half is zero and skipped
     constexpr bool kLo = sizeof(XT) == 4;
     extern __shared__ __align__(16) uint8_t hsm[];
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t Hh = H / 2;
     const uint32_t k0 = blockIdx.y * Hh;  // this CTA's half of the columns
     const uint32_t rb = head_row_bytes(H);
@@ -174,6 +176,8 @@ head_select_kernel(const float* __restrict__ logits, size_t logits_stride, uint3
     __shared__ unsigned long long sel[kHeadMaxSelect];  // (key << 32) | ~position, sorted descending
     __shared__ uint32_t scan_tmp[32];
     __shared__ uint32_t s_prefix, s_rem, s_gt, s_eq;
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t t = blockIdx.x;
     const uint32_t base = blockIdx.y * kSelSlice;  // first position of this CTA's slice
     if (base >= n) return;
@@ -352,6 +356,8 @@ head_merge_kernel(const uint32_t* __restrict__ in_key, const uint32_t* __restric
     __shared__ unsigned long long cand[kMergeSort];  // the bound's subset, then the entries at or above it
     __shared__ unsigned long long s_bound;
     __shared__ uint32_t s_cnt;
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t t = blockIdx.x, n = lists * k;
     for (uint32_t p = threadIdx.x; p < n; p += blockDim.x) {
         const uint32_t l = p / k, r = p - l * k;
@@ -465,9 +471,8 @@ static cudaError_t head_gemv_t(const HeadArgs& a, cudaStream_t s) {
     uint32_t per_half = static_cast<uint32_t>(sms > 1 ? sms / 2 : 1);
     const uint32_t need = (nblk + kHeadWarps - 1) / kHeadWarps;
     if (per_half > need) per_half = need;
-    fn<<<dim3(per_half, 2), kHeadThreads, smem, s>>>(a.weight, a.vocab, a.hidden, static_cast<const XT*>(a.x),
-                                                     a.tokens, a.logits);
-    return cudaGetLastError();
+    return launch_pdl_kernel(fn, dim3(per_half, 2), dim3(kHeadThreads), smem, s, a.weight, a.vocab, a.hidden,
+                             static_cast<const XT*>(a.x), a.tokens, a.logits);
 }
 
 template <typename XT>
@@ -484,10 +489,10 @@ cudaError_t head_topk_launch(const HeadArgs& a, cudaStream_t s) {
     e = a.x_dtype == PBMOE_BF16 ? head_gemv<uint16_t>(a, s) : head_gemv<float>(a, s);
     if (e != cudaSuccess) return e;
     const uint32_t S = head_slices(a.vocab);
-    head_select_kernel<<<dim3(a.tokens, S), kSelThreads, 0, s>>>(a.logits, a.vocab, a.id_base, a.allowed, a.vocab,
-                                                                  a.top_k, a.cand_key, a.cand_id, a.cand_val,
-                                                                  static_cast<size_t>(S) * a.top_k);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = launch_pdl_kernel(head_select_kernel, dim3(a.tokens, S), dim3(kSelThreads), 0, s, a.logits,
+                               static_cast<size_t>(a.vocab), a.id_base, a.allowed, a.vocab, a.top_k, a.cand_key,
+                               a.cand_id, a.cand_val, static_cast<size_t>(S) * a.top_k)) != cudaSuccess)
+        return e;
     return head_merge_launch(a.cand_key, a.cand_id, a.cand_val, a.tokens, S, static_cast<size_t>(S) * a.top_k,
                              a.top_k, a.top_k, a.out_key, a.out_id, a.out_val, s);
 }
@@ -502,9 +507,8 @@ cudaError_t head_merge_launch(const uint32_t* in_key, const uint32_t* in_id, con
     cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(head_merge_kernel),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    head_merge_kernel<<<tokens, kSelThreads, smem, s>>>(in_key, in_id, in_val, tok_stride, list_stride, lists, top_k,
-                                                        out_key, out_id, out_val);
-    return cudaGetLastError();
+    return launch_pdl_kernel(head_merge_kernel, dim3(tokens), dim3(kSelThreads), smem, s, in_key, in_id, in_val,
+                             tok_stride, list_stride, lists, top_k, out_key, out_id, out_val);
 }
 
 }  // namespace pbmoe

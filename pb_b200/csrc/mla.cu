@@ -94,6 +94,8 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
                                                          float* __restrict__ qp) {
     __shared__ float qs[kMlaMaxBatch * kAbsorbMaxNope];
     __shared__ float red[4][8][64];
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t h = blockIdx.x, tid = threadIdx.x;
     const uint32_t quarter = tid >> 6, cc = tid & 63, c = blockIdx.y * 64 + cc;
     const uint32_t qdim = nope + kMlaRope;
@@ -147,6 +149,8 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
                                                                       uint32_t split_tokens, uint32_t splits,
                                                                       float* __restrict__ partial) {
     extern __shared__ __align__(128) unsigned char smem[];
+    pdl_wait();
+    pdl_launch_dependents();
     unsigned char* qhi = smem;
     unsigned char* qlo = qhi + kMlaHeads * kQRow;
     unsigned char* stage0 = qlo + kMlaHeads * kQRow;
@@ -369,6 +373,8 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(const float* __restric
                                                            float* __restrict__ ctx) {
     __shared__ float wsc[1024];
     __shared__ float red[4];
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t h = blockIdx.x, b = blockIdx.y, c = blockIdx.z * 128 + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* base = partial + static_cast<size_t>(b) * splits * kMlaHeads * kMlaPartialFloats +
@@ -432,6 +438,10 @@ __global__ void __launch_bounds__(256) mla_out_kernel(const float* __restrict__ 
             wf[r][2 * i + 1] = bf16_bits_to_f32(wv[i] >> 16);
         }
     }
+    // W_UV does not depend on the earlier kernels: its loads are issued
+    // before waiting for them
+    pdl_wait();
+    pdl_launch_dependents();
     for (uint32_t i = threadIdx.x; i < batch * kMlaLatent / 4; i += blockDim.x) {
         const uint32_t bb = i / (kMlaLatent / 4), c4 = i % (kMlaLatent / 4);
         reinterpret_cast<float4*>(cs)[i] =
@@ -489,36 +499,36 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     {
         const dim3 grid(kMlaHeads, kMlaLatent / 64);
         if (a.q_dtype == PBMOE_F32)
-            mla_absorb_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(a.q), a.batch, a.nope, a.w_uk,
-                                                          k, a.qp);
+            e = launch_pdl_kernel(mla_absorb_kernel<float>, grid, dim3(256), 0, s, static_cast<const float*>(a.q),
+                                  a.batch, a.nope, a.w_uk, k, a.qp);
         else
-            mla_absorb_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(a.q), a.batch, a.nope,
-                                                             a.w_uk, k, a.qp);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            e = launch_pdl_kernel(mla_absorb_kernel<uint16_t>, grid, dim3(256), 0, s,
+                                  static_cast<const uint16_t*>(a.q), a.batch, a.nope, a.w_uk, k, a.qp);
+        if (e != cudaSuccess) return e;
     }
     if ((e = cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(kMlaSmem))) != cudaSuccess)
         return e;
-    mla_attn_kernel<<<dim3(a.splits, a.batch), kMlaWarps * 32, kMlaSmem, s>>>(a.qp, a.seqs, a.split_tokens, a.splits,
-                                                                             a.partial);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    mla_combine_kernel<<<dim3(kMlaHeads, a.batch, kMlaLatent / 128), 128, 0, s>>>(a.partial, a.splits, a.ctx);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = launch_pdl_kernel(mla_attn_kernel, dim3(a.splits, a.batch), dim3(kMlaWarps * 32), kMlaSmem, s, a.qp,
+                               a.seqs, a.split_tokens, a.splits, a.partial)) != cudaSuccess)
+        return e;
+    if ((e = launch_pdl_kernel(mla_combine_kernel, dim3(kMlaHeads, a.batch, kMlaLatent / 128), dim3(128), 0, s,
+                               a.partial, a.splits, a.ctx)) != cudaSuccess)
+        return e;
     const size_t osm = static_cast<size_t>(a.batch) * kMlaLatent * sizeof(float);
     if (a.out_dtype == PBMOE_F32) {
         if ((e = cudaFuncSetAttribute(mla_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(osm))) != cudaSuccess)
             return e;
-        mla_out_kernel<float><<<dim3(kMlaHeads, kMlaV / 16), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
-                                                                            static_cast<float*>(a.out));
+        return launch_pdl_kernel(mla_out_kernel<float>, dim3(kMlaHeads, kMlaV / 16), dim3(256), osm, s, a.ctx,
+                                 a.batch, a.w_uv, static_cast<float*>(a.out));
     } else {
         if ((e = cudaFuncSetAttribute(mla_out_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(osm))) != cudaSuccess)
             return e;
-        mla_out_kernel<uint16_t><<<dim3(kMlaHeads, kMlaV / 16), 256, osm, s>>>(a.ctx, a.batch, a.w_uv,
-                                                                               static_cast<uint16_t*>(a.out));
+        return launch_pdl_kernel(mla_out_kernel<uint16_t>, dim3(kMlaHeads, kMlaV / 16), dim3(256), osm, s, a.ctx,
+                                 a.batch, a.w_uv, static_cast<uint16_t*>(a.out));
     }
-    return cudaGetLastError();
 }
 
 }  // namespace pbmoe

@@ -16,7 +16,8 @@
 //
 // The cos/sin table is built on the host in f64 exactly as the reference
 // builds its angles (runtime/mod.rs:2825-2836), so the rotation, done with
-// unfused f32 multiplies and adds as in the reference, is bit-exact.
+// unfused f32 multiplies and adds as in the reference, is bit-exact. Both
+// kernels use programmatic dependent launch (griddepcontrol.wait first).
 
 #include "common.cuh"
 #include "kernels.h"
@@ -37,6 +38,8 @@ __device__ __forceinline__ void st_any(void* p, pbmoe_dtype t, size_t i, float v
 
 __global__ void __launch_bounds__(kNormThreads) rms_norm_rows_kernel(NormArgs a) {
     __shared__ float red[kNormThreads / 32];
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t r = blockIdx.x;
     const size_t xo = static_cast<size_t>(r) * a.x_stride, ro = static_cast<size_t>(r) * a.residual_stride;
     const size_t so = static_cast<size_t>(r) * a.sum_stride, oo = static_cast<size_t>(r) * a.out_stride;
@@ -68,14 +71,15 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_rows_kernel(NormArgs a)
 
 cudaError_t rms_norm_launch(const NormArgs& a, cudaStream_t s) {
     if (a.rows == 0) return cudaSuccess;
-    rms_norm_rows_kernel<<<a.rows, kNormThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl_kernel(rms_norm_rows_kernel, dim3(a.rows), dim3(kNormThreads), 0, s, a);
 }
 
 constexpr int kRopeThreads = 256;
 constexpr uint32_t kRopeMaxPairs = 2048;  // heads x rope/2 rotated per token
 
 __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppendArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
     const uint32_t b = blockIdx.x;
     const uint32_t pos = a.positions[b];
     if (pos >= a.max_positions || pos >= a.cache_len) {
@@ -129,8 +133,7 @@ bool rope_append_supported(uint32_t heads, uint32_t rope) {
 cudaError_t mla_rope_append_launch(const RopeAppendArgs& a, cudaStream_t s) {
     if (a.batch == 0) return cudaSuccess;
     if (!rope_append_supported(a.heads, a.rope)) return cudaErrorInvalidValue;
-    mla_rope_append_kernel<<<a.batch, kRopeThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl_kernel(mla_rope_append_kernel, dim3(a.batch), dim3(kRopeThreads), 0, s, a);
 }
 
 }  // namespace pbmoe
