@@ -399,6 +399,17 @@ PBMOE_API int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config,
                                  void* out, pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
                                  void* next_normed, void* stream);
 
+/* The MoE decode layer on HOST rows, as the reference's facade takes them
+ * (submit_scheduled_expert_command, runtime/mod.rs:922-961: normed and
+ * residual as host slices; the submission's wait, metal/mod.rs:3041-3127,
+ * hands back the host output): x and residual are copied into device rows
+ * owned by the context (sized by pbmoe_reserve), the layer runs, and out is
+ * copied back, all ordered on `stream` (synchronise it before reading out;
+ * pinned host memory makes the copies asynchronous). No next-layer norm. */
+PBMOE_API int pbmoe_moe_layer_host(pbmoe_ctx* ctx, const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
+                                   const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
+                                   pbmoe_dtype out_dtype, uint32_t tokens, void* stream);
+
 /* ---------------------------------------------------------------- vocab head
  * The LM head of sample_from_hidden (runtime/generation.rs:2200-2227):
  * lm_head_raw_top_candidates_with_metal(_masked) (weights/store.rs:1622-1680)

@@ -23,6 +23,8 @@ struct pbmoe_ctx {
     uint32_t mla_batch = 0;
     void* x16_base = nullptr;  // prefill fp16 activation image
     size_t x16_elems = 0;
+    void* io_base = nullptr;  // device rows of pbmoe_moe_layer_host: x, residual, out
+    size_t io_bytes = 0;
     void* ep_base = nullptr;  // expert-parallel exchange buffer
     size_t ep_bytes = 0;
     uint32_t ep_rank = 0, ep_world = 0, ep_max_tokens = 0, ep_hidden = 0;
@@ -219,6 +221,7 @@ int pbmoe_destroy(pbmoe_ctx* ctx) {
     {
         DeviceGuard g(ctx->device);
         if (ctx->ws_base) cudaFree(ctx->ws_base);
+        if (ctx->io_base) cudaFree(ctx->io_base);
         if (ctx->mla_base) cudaFree(ctx->mla_base);
         if (ctx->x16_base) cudaFree(ctx->x16_base);
         if (ctx->head_base) cudaFree(ctx->head_base);
@@ -267,17 +270,22 @@ int pbmoe_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, const pbmoe_moe_config* c
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
     const size_t need = moe_ws_sizes(max_tokens, E, K, H, I).total;
+    const size_t io_need = 3ull * max_tokens * H * sizeof(float);
     if (ctx->ws_base && ctx->ws_bytes >= need && ctx->ws_E == E && ctx->ws_K == K && ctx->ws_H == H &&
-        ctx->ws_I == I && ctx->ws_tokens >= max_tokens)
+        ctx->ws_I == I && ctx->ws_tokens >= max_tokens && ctx->io_bytes >= io_need)
         return PBMOE_OK;
-    if (ctx->ws_base) {
+    if (ctx->ws_base || ctx->io_base) {
         cudaError_t e = cudaDeviceSynchronize();
         if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before workspace resize");
-        cudaFree(ctx->ws_base);
-        ctx->ws_base = nullptr;
-        ctx->ws_bytes = 0;
+        if (ctx->ws_base) cudaFree(ctx->ws_base);
+        if (ctx->io_base) cudaFree(ctx->io_base);
+        ctx->ws_base = ctx->io_base = nullptr;
+        ctx->ws_bytes = ctx->io_bytes = 0;
     }
-    cudaError_t e = cudaMalloc(&ctx->ws_base, need);
+    cudaError_t e = cudaMalloc(&ctx->io_base, io_need);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "host-call staging allocation");
+    ctx->io_bytes = io_need;
+    e = cudaMalloc(&ctx->ws_base, need);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "workspace allocation");
     e = cudaMemset(ctx->ws_base, 0, need);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "workspace clear");
@@ -461,6 +469,38 @@ int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_w
                     const float* next_norm_weight, void* next_normed, const pbmoe_moe_debug* debug, void* stream) {
     return moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
                           debug, stream, 0, 0, nullptr);
+}
+
+int pbmoe_moe_layer_host(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w, const void* x,
+                         pbmoe_dtype x_dtype, const void* residual, void* out, pbmoe_dtype out_dtype, uint32_t tokens,
+                         void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!c || !x || !out) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "moe layer (host rows): null pointer");
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (out_dtype != PBMOE_F32 && out_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (tokens == 0) return PBMOE_OK;
+    const uint32_t H = c->layout.hidden;
+    if (!ctx->io_base || tokens > ctx->ws_tokens || H != ctx->ws_H)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "moe layer (host rows): %u tokens of hidden %u need pbmoe_reserve",
+                    tokens, H);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    const size_t xs = x_dtype == PBMOE_BF16 ? 2 : 4, os = out_dtype == PBMOE_BF16 ? 2 : 4;
+    const size_t slot = size_t(ctx->ws_tokens) * H * sizeof(float);
+    char* dx = static_cast<char*>(ctx->io_base);
+    char* dres = dx + slot;
+    char* dout = dres + slot;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(dx, x, size_t(tokens) * H * xs, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && residual)
+        e = cudaMemcpyAsync(dres, residual, size_t(tokens) * H * os, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer (host rows) input copy");
+    const int rc = moe_layer_impl(ctx, c, w, dx, x_dtype, residual ? dres : nullptr, dout, out_dtype, tokens, nullptr,
+                                  nullptr, nullptr, stream, 0, 0, nullptr);
+    if (rc != PBMOE_OK) return rc;
+    e = cudaMemcpyAsync(out, dout, size_t(tokens) * H * os, cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer (host rows) output copy");
+    return PBMOE_OK;
 }
 
 }  // extern "C"

@@ -315,3 +315,28 @@ def test_moe_layer_rejects_bad_calls(ctx, small_layer):
     with pytest.raises(capi.PbmoeError) as e:
         ctx.moe_layer(bad, small_layer.c_weights(), x, out, 1)
     assert e.value.code == capi.PBMOE_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("tokens,out_f32", [(1, False), (8, True), (12, False)])
+def test_moe_layer_host_rows(ctx, config1_layer, tokens, out_f32):
+    """pbmoe_moe_layer_host (host x / residual / out, copies inside the call)
+    equals pbmoe_moe_layer on device rows, bit for bit."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    w = config1_layer
+    cfg = capi.moe_config(w.layout, w.num_experts, 10)
+    ctx.reserve(32, cfg)
+    dt = torch.float32 if out_f32 else torch.bfloat16
+    x = synth.normal_bf16((tokens, w.hidden), 1.0, synth.gen("cuda", 90 + tokens), "cuda")
+    res = synth.normal_bf16((tokens, w.hidden), 1.0, synth.gen("cuda", 91), "cuda").to(dt)
+    ref = torch.empty(tokens, w.hidden, device="cuda", dtype=dt)
+    ctx.moe_layer(cfg, w.c_weights(), x, ref, tokens, residual=res)
+    hx, hres = x.cpu().pin_memory(), res.cpu().pin_memory()
+    hout = torch.empty(tokens, w.hidden, dtype=dt).pin_memory()
+    s = torch.cuda.current_stream()
+    ctx.moe_layer_host(cfg, w.c_weights(), hx, hout, tokens, residual=hres, stream=s)
+    s.synchronize()
+    assert ctx.device_status() == 0
+    assert torch.equal(hout, ref.cpu())
