@@ -479,7 +479,10 @@ PBMOE_API int pbmoe_mxfp4_matvec(pbmoe_ctx* ctx, const pbmoe_mxfp4_tensor* w, co
  * QwenMoeQ4ExpertLayout byte image (model_family.rs:954-1010). The metadata is
  * validated as ExpertLayerPackMetadata::validate does (experts/mod.rs:372-429)
  * and every requested expert's records against `layout`; slot bytes are used
- * as stored. This replaces the per-token pread of expert slots
+ * as stored. A PBQ4EXPERT_LAYER_V1/V2 layer (a variable-length pack per slot:
+ * experts/mod.rs:546-653) is read as the fixed-Q4 images the reference's
+ * upgrade writes (experts/slots.rs:984-1113; f32 scales rounded to bf16).
+ * This replaces the per-token pread of expert slots
  * (scheduler/mod.rs:662, :808) with one load into the HBM-resident table that
  * pbmoe_moe_weights.experts points at.
  *

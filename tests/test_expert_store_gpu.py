@@ -47,3 +47,34 @@ def test_load_matches_and_runs(tmp_path):
         assert torch.equal(outs[0], outs[1])
     finally:
         ctx.close()
+
+
+def test_pbq4_load_equals_host_read(tmp_path):
+    """A PBQ4 layer (f32 scales) at config-1 shapes: the device load equals
+    the host read, which the CPU tests pin to fixed_q4_pack_from_pbq4_records."""
+    import torch
+
+    from expert_store_writer import pbq4_pack, write_pbq4_layer
+
+    from pb_b200 import capi
+
+    ctx = capi.Context(0)
+    try:
+        H, I, G = 2048, 512, 64
+        lay = capi.fixed_q4_layout(H, I, G)
+        rng = np.random.default_rng(3)
+        packs = []
+        for e in range(5):
+            parts = []
+            for rows, cols in ((I, H), (I, H), (H, I)):
+                parts.append((rows, cols, G, rng.integers(0, 256, rows * cols // 2, dtype=np.uint8),
+                              rng.uniform(0.004, 0.02, rows * cols // G).astype(np.float32),
+                              (rng.standard_normal(rows * cols // G) * 0.1).astype(np.float32)))
+            packs.append(pbq4_pack(0, e, parts, True, order=(1, 2, 0)))
+        write_pbq4_layer(str(tmp_path), 0, packs, max(len(d) for d, _ in packs))
+        host = capi.expert_layer_read(tmp_path, 0, lay, 0, 5)
+        dev = torch.zeros(5 * lay.expert_bytes, dtype=torch.uint8, device="cuda")
+        ctx.expert_layer_load(tmp_path, 0, lay, 0, 5, dev)
+        assert np.array_equal(dev.cpu().numpy(), host.reshape(-1))
+    finally:
+        ctx.close()

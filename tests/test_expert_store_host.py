@@ -32,7 +32,7 @@ def test_read_all_and_a_range(store):
 
 
 @pytest.mark.parametrize("edit,match", [
-    (lambda m: m.update(format="PBQ4EXPERT_LAYER_V2"), "unsupported expert storage format"),
+    (lambda m: m.update(format="FIXED_MXFP4_EXPERT_LAYER_V1"), "unsupported expert storage format"),
     (lambda m: m.update(layer=4), "describes layer 4"),
     (lambda m: m.update(expert_size=m["expert_size"] + 16), "unsupported expert slot size"),
     (lambda m: m.update(experts=0), "zero experts"),
@@ -101,3 +101,82 @@ def test_record_offsets_are_the_weight_components(store):
     recs = records_for(0, 0, H, I, G, offs)
     assert [r["record_offset"] for r in recs] == [offs[0], offs[3], offs[6]]
     assert offs[3] == offs[0] + I * H // 2 + 2 * 2 * I * (H // G)
+
+
+# ---------------------------------------------------------------- PBQ4 packs
+def _pbq4_store(tmp_path, f32, order=(0, 1, 2), pack_edit=None, corrupt=None):
+    """Three experts as PBQ4 packs and the fixed-Q4 slot images they must give."""
+    from expert_store_writer import bf16_bytes, pbq4_pack, write_pbq4_layer
+
+    from pb_b200 import capi
+
+    lay = capi.fixed_q4_layout(H, I, G)
+    offs = list(lay.component_offsets)
+    rng = np.random.default_rng(7)
+    packs, want = [], []
+    for e in range(3):
+        parts, slot = [], bytearray(lay.expert_bytes)
+        for j, (rows, cols) in enumerate(((I, H), (I, H), (H, I))):
+            nib = rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)
+            sc = (rng.uniform(0.004, 0.02, rows * cols // G)).astype(np.float32)
+            bi = (rng.standard_normal(rows * cols // G) * 0.1).astype(np.float32)
+            parts.append((rows, cols, G, nib, sc, bi))
+            slot[offs[3 * j]:offs[3 * j] + len(nib)] = nib.tobytes()
+            slot[offs[3 * j + 1]:offs[3 * j + 1] + 2 * len(sc)] = bf16_bytes(sc)
+            slot[offs[3 * j + 2]:offs[3 * j + 2] + 2 * len(bi)] = bf16_bytes(bi)
+        data, recs = pbq4_pack(1, e, parts, f32, order)
+        if corrupt:
+            data = corrupt(e, data)
+        packs.append((data, recs))
+        want.append(np.frombuffer(bytes(slot), np.uint8))
+    size = max(len(d) for d, _ in packs) + 64
+    write_pbq4_layer(str(tmp_path), 1, packs, size, pack_edit=pack_edit)
+    return lay, np.stack(want)
+
+
+@pytest.mark.parametrize("f32", [True, False])
+def test_pbq4_becomes_fixed_slots(tmp_path, f32):
+    """A PBQ4 layer (PBQ4EXPERT_LAYER_V2) reads as the fixed-Q4 images
+    fixed_q4_pack_from_pbq4_records builds: nibbles copied, f32 scales and
+    biases rounded to bf16 (experts/slots.rs:984-1169)."""
+    from pb_b200 import capi
+
+    lay, want = _pbq4_store(tmp_path, f32)
+    assert np.array_equal(capi.expert_layer_read(tmp_path, 1, lay, 0, 3), want)
+    assert np.array_equal(capi.expert_layer_read(tmp_path, 1, lay, 1, 2), want[1:])
+
+
+def test_pbq4_record_order_free(tmp_path):
+    from pb_b200 import capi
+
+    lay, want = _pbq4_store(tmp_path, True, order=(2, 0, 1))
+    assert np.array_equal(capi.expert_layer_read(tmp_path, 1, lay, 0, 3), want)
+
+
+@pytest.mark.parametrize("corrupt,edit,match", [
+    (lambda e, d: b"XBQ4EXPERT " + d[11:], None, "missing PBQ4EXPERT header"),
+    (lambda e, d: d + b"\0", None, "trailing bytes"),
+    (None, lambda m: m["packs"][0]["records"][1].update(record_offset=m["packs"][0]["records"][1]["record_offset"] + 4),
+     "metadata offset mismatch"),
+    (lambda e, d: d.replace(b"up_proj", b"up_prox", 1), None, "name mismatch"),
+    (None, lambda m: m["packs"][2]["records"][0].update(scale_bias_dtype="F16"), "does not match the layout"),
+])
+def test_pbq4_invalid(tmp_path, corrupt, edit, match):
+    """Each check of parse_pbq4_expert_pack_with_metadata failing with its message
+    (the metadata's pack length always follows the bytes written)."""
+    from pb_b200 import capi
+
+    lay, _ = _pbq4_store(tmp_path, True, pack_edit=edit, corrupt=corrupt)
+    with pytest.raises(capi.PbmoeError, match=match):
+        capi.expert_layer_read(tmp_path, 1, lay, 0, 3)
+
+
+def test_pbq4_duplicate_projection(tmp_path):
+    from pb_b200 import capi
+
+    def dup(meta):
+        meta["packs"][0]["records"][1]["tensor"] = meta["packs"][0]["records"][0]["tensor"]
+
+    lay, _ = _pbq4_store(tmp_path, True, pack_edit=dup)
+    with pytest.raises(capi.PbmoeError, match="distinct projection"):
+        capi.expert_layer_read(tmp_path, 1, lay, 0, 3)
