@@ -22,7 +22,7 @@
 // caller expects. A PBQ4 slot holds a variable-length pack, parsed against
 // its metadata and turned into the fixed image in memory, the conversion the
 // reference applies when it rewrites such a layer (rewrite_pbq4_layer_to_
-// fixed_q4, experts/mod.rs:2300-2375); files are never rewritten here. Host
+// fixed_q4, experts/mod.rs:2304-2375); files are never rewritten here. Host
 // code only: the device upload is plain cudaMemcpyAsync of double-buffered
 // pinned chunks of whole slots.
 
