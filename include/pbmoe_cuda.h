@@ -164,6 +164,13 @@ PBMOE_API size_t pbmoe_moe_workspace_bytes(uint32_t max_tokens, const pbmoe_moe_
  * synchronising `stream`. *out receives PBMOE_DEV_ERR_* bits. */
 PBMOE_API int pbmoe_device_status(pbmoe_ctx* ctx, void* stream, uint32_t* out, int clear);
 
+/* Bounded wait for everything queued on `stream` (the CMD3 submission's
+ * wait(), metal/mod.rs:3041-3127): PBMOE_OK once the stream is idle,
+ * PBMOE_ERR_TIMEOUT if it is still busy after timeout_ms (the work is not
+ * cancelled; the call may be repeated), PBMOE_ERR_CUDA if queued work failed.
+ * timeout_ms 0 only polls. */
+PBMOE_API int pbmoe_sync(pbmoe_ctx* ctx, void* stream, uint32_t timeout_ms);
+
 /* Fill *out with the reference's fixed whole-expert layout
  * (QwenMoeQ4ExpertLayout::fixed_bf16, model_family.rs:954-1010). Host-only. */
 PBMOE_API int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group_size,

@@ -47,7 +47,7 @@ EXPORTED = [
     "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
     "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
-    "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host",
+    "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host", "pbmoe_sync",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -170,6 +170,7 @@ def load():
         L.pbmoe_rms_norm.argtypes = [vp, C.POINTER(NormArgs), vp]
         L.pbmoe_rope_reserve.argtypes = [vp, u32, u32, C.c_double]
         L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, vp, vp, u32, vp]
+        L.pbmoe_sync.argtypes = [vp, vp, u32]
         L.pbmoe_moe_layer_host.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
                                            u32, vp]
         L.pbmoe_mxfp4_matvec.argtypes = [vp, C.POINTER(Mxfp4Tensor), vp, i32, vp, i32, u32, vp]
@@ -268,6 +269,10 @@ class Context:
             self.h, C.byref(config), C.byref(weights), _ptr(x), _dtype_code(x), _ptr(residual), _ptr(out),
             _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed),
             C.byref(debug) if debug is not None else None, self.stream_ptr(stream)))
+
+    def sync(self, stream=None, timeout_ms=10000):
+        """Bounded wait for `stream`; PbmoeError (PBMOE_ERR_TIMEOUT) if it is still busy."""
+        self.check(self.lib.pbmoe_sync(self.h, self.stream_ptr(stream), timeout_ms))
 
     def moe_layer_host(self, config, weights: MoeWeights, x, out, tokens, residual=None, stream=None):
         """The layer on host tensors (pinned for asynchronous copies): x [tokens, H] bf16/f32,

@@ -6,7 +6,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <chrono>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "kernels.h"
@@ -296,6 +298,22 @@ int pbmoe_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, const pbmoe_moe_config* c
     ctx->ws_H = H;
     ctx->ws_I = I;
     return PBMOE_OK;
+}
+
+int pbmoe_sync(pbmoe_ctx* ctx, void* stream, uint32_t timeout_ms) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return PBMOE_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "stream wait");
+        if (std::chrono::steady_clock::now() >= deadline)
+            return fail(ctx, PBMOE_ERR_TIMEOUT, "stream still busy after %u ms", timeout_ms);
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
 }
 
 int pbmoe_device_status(pbmoe_ctx* ctx, void* stream, uint32_t* out, int clear) {

@@ -340,3 +340,20 @@ def test_moe_layer_host_rows(ctx, config1_layer, tokens, out_f32):
     s.synchronize()
     assert ctx.device_status() == 0
     assert torch.equal(hout, ref.cpu())
+
+
+def test_sync_bounded_wait(ctx, small_layer):
+    """pbmoe_sync returns once the stream is idle (the CMD3 submission's wait)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    cfg = capi.moe_config(small_layer.layout, small_layer.num_experts, 6)
+    ctx.reserve(4, cfg)
+    x = synth.normal_bf16((4, small_layer.hidden), 1.0, synth.gen("cuda", 5), "cuda")
+    out = torch.empty_like(x)
+    for _ in range(20):
+        ctx.moe_layer(cfg, small_layer.c_weights(), x, out, 4)
+    ctx.sync(timeout_ms=10000)
+    assert torch.cuda.current_stream().query()
+    ctx.sync(timeout_ms=0)  # idle: polling succeeds
