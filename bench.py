@@ -23,6 +23,12 @@ Reported (one JSON line on rank 0):
 `--impl reference` times the oracle alone (the reference cannot be built:
 Rust toolchain absent; its GPU path is Metal).
 
+Other lines (`--workload`, one GPU): matvec (config 0, Q4 [4096x2048]),
+gemm (config 2, tcgen05 prefill GEMM, dense and grouped), mla (config 3,
+absorbed MLA decode), head (config 4's vocab head + top-64), step (config
+4's full 48-layer decode step at context 8192), mxfp4 (the config-0 shape
+in MXFP4). Each prints the same keys as the headline line.
+
 Multi-GPU (torchrun, N>1): expert parallelism. Rank r holds experts
 [r*512/N, (r+1)*512/N) of every cycled layer (router and shared expert
 replicated, the shared expert computed on rank 0); every rank routes the same
