@@ -180,3 +180,34 @@ def test_pbq4_duplicate_projection(tmp_path):
     lay, _ = _pbq4_store(tmp_path, True, pack_edit=dup)
     with pytest.raises(capi.PbmoeError, match="distinct projection"):
         capi.expert_layer_read(tmp_path, 1, lay, 0, 3)
+
+
+def test_metadata_json_forms(store):
+    """serde's output variants parse: pretty-printed, source_hash null or a
+    string, escaped characters in other fields, unknown fields ignored."""
+    import json
+
+    from pb_b200 import capi
+
+    root, lay, slots, offs = store
+
+    def edit(m):
+        m["generator"] = {"name": 'pb "cache"\n', "version": [1, 2.5, -3, True, None]}
+        for p in m["packs"]:
+            for i, r in enumerate(p["records"]):
+                r["source_hash"] = None if i % 2 else "ab\u00e9cd"
+                r["dtype"] = "BF16\t"
+
+    write_layer(str(root), 5, slots, H, I, G, offs, meta_edit=edit)
+    path = root / "layer_05.json"
+    path.write_text(json.dumps(json.loads(path.read_text()), indent=2))
+    assert np.array_equal(capi.expert_layer_read(root, 5, lay, 0, E), slots)
+
+
+def test_metadata_numbers_must_be_integers(store):
+    from pb_b200 import capi
+
+    root, lay, slots, offs = store
+    write_layer(str(root), 6, slots, H, I, G, offs, meta_edit=lambda m: m.update(expert_size=float(m["expert_size"])))
+    with pytest.raises(capi.PbmoeError, match="lacks layer/expert_size/experts"):
+        capi.expert_layer_read(root, 6, lay, 0, E)
