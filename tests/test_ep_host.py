@@ -85,3 +85,59 @@ def test_connect_exchanges_handles_in_rank_order(tmp_path):
     world = 2
     mp.spawn(_connect_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     assert sorted(os.listdir(tmp_path)) == ["ok0", "ok1"]
+
+
+def test_vocab_ranges_cover_every_id_once():
+    from pb_b200 import ep
+
+    for V, world in [(151936, 8), (151936, 3), (10, 10), (1000, 1)]:
+        ranges = ep.vocab_ranges(V, world)
+        assert [b for b, _ in ranges] == sorted(b for b, _ in ranges)
+        assert sum(n for _, n in ranges) == V and ranges[0][0] == 0
+        assert all(b + n == nb for (b, n), (nb, _) in zip(ranges, ranges[1:]))
+        assert max(n for _, n in ranges) - min(n for _, n in ranges) <= 1
+    with pytest.raises(ValueError):
+        ep.vocab_ranges(3, 4)
+
+
+def _vocab_worker(rank, world, port, out_dir):
+    """Each rank selects its shard's candidates (the oracle's topk_vocab with
+    ids offset by the shard's base), the lists are gathered in rank order,
+    and the best k of the union (value desc, id asc) equal topk_vocab over
+    the whole vocabulary."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from oracle import pb_oracle
+    from pb_b200 import ep
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        V, T, k = 5000, 3, 16
+        rng = np.random.default_rng(0)
+        logits = np.round(rng.standard_normal((T, V)) * 8).astype(np.float32) / 8  # many ties
+        base, n = ep.vocab_ranges(V, world)[rank]
+        ids = np.zeros((T, k), np.int64)
+        vals = np.zeros((T, k), np.float32)
+        for t in range(T):
+            i, v = pb_oracle.topk_vocab(logits[t, base:base + n], k)
+            ids[t], vals[t] = i.astype(np.int64) + base, v
+        keys = torch.zeros(T, k, dtype=torch.int32)
+        gk, gi, gv = ep.gather_candidates(keys, torch.tensor(ids), torch.tensor(vals))
+        assert gi.shape == (world, T, k)
+        for t in range(T):
+            cand = sorted(zip(gv[:, t].reshape(-1).tolist(), gi[:, t].reshape(-1).tolist()),
+                          key=lambda c: (-c[0], c[1]))[:k]
+            ref_i, ref_v = pb_oracle.topk_vocab(logits[t], k)
+            assert [c[1] for c in cand] == ref_i.tolist() and [c[0] for c in cand] == ref_v.tolist()
+        open(os.path.join(out_dir, f"ok{rank}"), "w").write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_shard_candidates_merge_to_the_full_topk(tmp_path):
+    import torch.multiprocessing as mp
+
+    mp.spawn(_vocab_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    assert sorted(os.listdir(tmp_path)) == ["ok0", "ok1"]
