@@ -176,6 +176,12 @@ PBMOE_API int pbmoe_sync(pbmoe_ctx* ctx, void* stream, uint32_t timeout_ms);
 PBMOE_API int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group_size,
                           pbmoe_expert_layout* out);
 
+/* The fixed MXFP4 whole-expert layout (QwenMoeQ4ExpertLayout::fixed_mxfp4,
+ * model_family.rs:846-952): per projection the E2M1 nibbles then one E8M0
+ * byte per group, the bias components zero-sized. Host-only. */
+PBMOE_API int pbmoe_fixed_mxfp4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group_size,
+                                       pbmoe_expert_layout* out);
+
 /* ---------------------------------------------------------------- kernels */
 
 /* y[b, r] = sum_c (q[r,c] * scale + bias) * x[b, c] for b < batch.
@@ -486,7 +492,10 @@ PBMOE_API int pbmoe_mxfp4_matvec(pbmoe_ctx* ctx, const pbmoe_mxfp4_tensor* w, co
  * QwenMoeQ4ExpertLayout byte image (model_family.rs:954-1010). The metadata is
  * validated as ExpertLayerPackMetadata::validate does (experts/mod.rs:372-429)
  * and every requested expert's records against `layout`; slot bytes are used
- * as stored. A PBQ4EXPERT_LAYER_V1/V2 layer (a variable-length pack per slot:
+ * as stored. A FIXED_MXFP4_EXPERT_LAYER_V1 layer (experts/mod.rs:49) is read
+ * as stored too, with a layout from pbmoe_fixed_mxfp4_layout; its records are
+ * not checked, as the reference resolves it from the pack-level metadata
+ * alone. A PBQ4EXPERT_LAYER_V1/V2 layer (a variable-length pack per slot:
  * experts/mod.rs:546-653) is read as the fixed-Q4 images the reference's
  * upgrade writes (experts/slots.rs:984-1113; f32 scales rounded to bf16).
  * This replaces the per-token pread of expert slots

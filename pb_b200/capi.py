@@ -48,6 +48,7 @@ EXPORTED = [
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
     "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
     "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host", "pbmoe_sync",
+    "pbmoe_fixed_mxfp4_layout",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -142,6 +143,7 @@ def load():
         L.pbmoe_moe_workspace_bytes.argtypes = [u32, C.POINTER(MoeConfig)]
         L.pbmoe_device_status.argtypes = [vp, vp, C.POINTER(u32), i32]
         L.pbmoe_fixed_q4_layout.argtypes = [u32, u32, u32, C.POINTER(ExpertLayout)]
+        L.pbmoe_fixed_mxfp4_layout.argtypes = [u32, u32, u32, C.POINTER(ExpertLayout)]
         L.pbmoe_q4_matvec.argtypes = [vp, C.POINTER(Q4Tensor), vp, i32, vp, i32, u32, vp]
         L.pbmoe_route_topk.argtypes = [vp, vp, u32, u32, u32, u32, C.c_float, vp, vp, vp]
         L.pbmoe_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32, u32,
@@ -180,6 +182,15 @@ def load():
                                               C.c_size_t, vp]
         _lib = L
     return _lib
+
+
+def fixed_mxfp4_layout(hidden, intermediate, group=32):
+    """The fixed MXFP4 expert slot layout (nibbles + E8M0 per projection, no biases)."""
+    lay = ExpertLayout()
+    rc = load().pbmoe_fixed_mxfp4_layout(hidden, intermediate, group, C.byref(lay))
+    if rc != PBMOE_OK:
+        raise PbmoeError(rc, "invalid fixed-MXFP4 layout")
+    return lay
 
 
 def fixed_q4_layout(hidden, intermediate, group):

@@ -255,6 +255,25 @@ int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group
     return PBMOE_OK;
 }
 
+int pbmoe_fixed_mxfp4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group, pbmoe_expert_layout* out) {
+    if (!out || hidden == 0 || intermediate == 0 || group == 0 || hidden % group || intermediate % group ||
+        (uint64_t(hidden) * intermediate) % 2)
+        return PBMOE_ERR_INVALID_ARGUMENT;
+    const uint64_t gw = uint64_t(intermediate) * hidden / 2, gs = uint64_t(intermediate) * (hidden / group);
+    const uint64_t dw = uint64_t(hidden) * intermediate / 2, ds = uint64_t(hidden) * (intermediate / group);
+    const uint64_t sizes[9] = {gw, gs, 0, gw, gs, 0, dw, ds, 0};  // biases: none
+    uint64_t off = 0;
+    for (int i = 0; i < 9; ++i) {
+        out->component_offsets[i] = off;
+        off += sizes[i];
+    }
+    out->expert_bytes = off;
+    out->hidden = hidden;
+    out->intermediate = intermediate;
+    out->group_size = group;
+    return PBMOE_OK;
+}
+
 size_t pbmoe_moe_workspace_bytes(uint32_t max_tokens, const pbmoe_moe_config* c) {
     if (!c || max_tokens == 0) return 0;
     return moe_ws_sizes(max_tokens, c->num_experts, c->top_k, c->layout.hidden, c->layout.intermediate).total;

@@ -225,7 +225,8 @@ struct PackRec {
 };
 // What the metadata says about the requested experts.
 struct StoreInfo {
-    bool fixed = true;            // FIXED_Q4 (slot = layout image) or PBQ4 V1/V2 (pack per slot)
+    bool fixed = true;            // a fixed image per slot (FIXED_Q4 / FIXED_MXFP4) or PBQ4 V1/V2 (pack per slot)
+    bool mxfp4 = false;           // FIXED_MXFP4: records not checked (pack-level metadata only)
     uint64_t expert_size = 0;     // slot stride in layer_NN.bin
     std::vector<uint64_t> pack_bytes;        // per requested expert
     std::vector<std::vector<PackRec>> recs;  // per requested expert, in metadata order
@@ -258,11 +259,18 @@ static int check_metadata(const char* root, uint32_t layer, const pbmoe_expert_l
         return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has no format", path.c_str());
     if (fmt->s == "FIXED_Q4_EXPERT_LAYER_V1") {
         info.fixed = true;
+    } else if (fmt->s == "FIXED_MXFP4_EXPERT_LAYER_V1") {
+        info.fixed = info.mxfp4 = true;
+        const auto& o = L->component_offsets;
+        if (o[2] != o[3] || o[5] != o[6] || o[8] != L->expert_bytes)
+            return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert layout for %s: an MXFP4 layer needs the "
+                          "MXFP4 layout (no bias components)", path.c_str());
     } else if (fmt->s == "PBQ4EXPERT_LAYER_V1" || fmt->s == "PBQ4EXPERT_LAYER_V2") {
         info.fixed = false;
     } else {
         return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert storage format %s in %s (this loader "
-                      "reads FIXED_Q4_EXPERT_LAYER_V1 and PBQ4EXPERT_LAYER_V1/V2)", fmt->s.c_str(), path.c_str());
+                      "reads FIXED_Q4_EXPERT_LAYER_V1, FIXED_MXFP4_EXPERT_LAYER_V1 and PBQ4EXPERT_LAYER_V1/V2)",
+                      fmt->s.c_str(), path.c_str());
     }
     unsigned long long mlayer, expert_size, experts;
     if (!get_u64(meta, "layer", mlayer) || !get_u64(meta, "expert_size", expert_size) ||
@@ -306,6 +314,8 @@ static int check_metadata(const char* root, uint32_t layer, const pbmoe_expert_l
             return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s expert %llu length %llu exceeds slot size %llu",
                           path.c_str(), ex, pb, expert_size);
         if (ex < begin || ex >= uint64_t(begin) + count) continue;
+        info.pack_bytes[ex - begin] = pb;
+        if (info.mxfp4) continue;  // slot used as stored
         // the records of a requested expert must describe this layout: one
         // record per projection (in gate, up, down order for the fixed
         // image; found by suffix for a PBQ4 pack, pbq4_record_by_suffix)

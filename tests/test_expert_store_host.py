@@ -32,7 +32,7 @@ def test_read_all_and_a_range(store):
 
 
 @pytest.mark.parametrize("edit,match", [
-    (lambda m: m.update(format="FIXED_MXFP4_EXPERT_LAYER_V1"), "unsupported expert storage format"),
+    (lambda m: m.update(format="FIXED_DENSE_EXPERT_LAYER_V1"), "unsupported expert storage format"),
     (lambda m: m.update(layer=4), "describes layer 4"),
     (lambda m: m.update(expert_size=m["expert_size"] + 16), "unsupported expert slot size"),
     (lambda m: m.update(experts=0), "zero experts"),
@@ -211,3 +211,40 @@ def test_metadata_numbers_must_be_integers(store):
     write_layer(str(root), 6, slots, H, I, G, offs, meta_edit=lambda m: m.update(expert_size=float(m["expert_size"])))
     with pytest.raises(capi.PbmoeError, match="lacks layer/expert_size/experts"):
         capi.expert_layer_read(root, 6, lay, 0, E)
+
+
+def test_fixed_mxfp4_layout_offsets():
+    """QwenMoeQ4ExpertLayout::fixed_mxfp4 (model_family.rs:846-952): per
+    projection the nibbles then one E8M0 byte per group, zero-byte biases."""
+    from pb_b200 import capi
+
+    lay = capi.fixed_mxfp4_layout(64, 32, 32)
+    gw, gs = 32 * 64 // 2, 32 * (64 // 32)
+    dw, ds = 64 * 32 // 2, 64 * (32 // 32)
+    assert list(lay.component_offsets) == [0, gw, gw + gs, gw + gs, 2 * gw + gs, 2 * gw + 2 * gs,
+                                           2 * gw + 2 * gs, 2 * gw + 2 * gs + dw, 2 * gw + 2 * gs + dw + ds]
+    assert lay.expert_bytes == 2 * gw + 2 * gs + dw + ds
+    big = capi.fixed_mxfp4_layout(2048, 512, 32)
+    assert big.expert_bytes == 3 * (2048 * 512 // 2 + 2048 * 512 // 32)
+    with pytest.raises(capi.PbmoeError):
+        capi.fixed_mxfp4_layout(64, 48, 32)
+
+
+def test_mxfp4_layer_reads_as_stored(tmp_path):
+    """A FIXED_MXFP4_EXPERT_LAYER_V1 layer: slots as stored, checked at the
+    pack level only; a Q4 layout is refused for it."""
+    from pb_b200 import capi
+
+    lay = capi.fixed_mxfp4_layout(H, I, 32)
+    rng = np.random.default_rng(4)
+    slots = rng.integers(0, 256, (E, lay.expert_bytes), dtype=np.uint8)
+
+    def fmt(m):
+        m["format"] = "FIXED_MXFP4_EXPERT_LAYER_V1"
+        for p in m["packs"]:
+            p["records"] = []
+
+    write_layer(str(tmp_path), 2, slots, H, I, 32, list(lay.component_offsets), meta_edit=fmt)
+    assert np.array_equal(capi.expert_layer_read(tmp_path, 2, lay, 1, 4), slots[1:5])
+    with pytest.raises(capi.PbmoeError, match="MXFP4 layout"):
+        capi.expert_layer_read(tmp_path, 2, capi.fixed_q4_layout(H, I, 32), 0, 1)
