@@ -5,8 +5,8 @@
  * Jc2k/pb's FlashMoE runtime (src/inference/flashmoe/metal/, driven through
  * MetalExecutionFacade, runtime/mod.rs:648-1416). The runtime's host code keeps
  * its model/scheduler API and calls these entry points instead of encoding
- * Metal command buffers; INTEGRATION.md shows the Rust `extern "C"` block and
- * build.rs a maintainer would add.
+ * Metal command buffers, binding them from Rust with an `extern "C"` block
+ * and linking the library from its build script.
  *
  * Conventions
  *  - Plain C: pointers, sizes, enums. No CUDA or torch types; a stream is a
@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define PBMOE_ABI_VERSION 1
+#define PBMOE_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define PBMOE_API __attribute__((visibility("default")))
@@ -125,6 +125,13 @@ typedef struct pbmoe_moe_weights {
     const uint8_t* experts;             /* E slots, layout.expert_bytes apart          */
     const uint8_t* shared_expert;       /* one slot in the same layout, or NULL        */
     const uint16_t* shared_expert_gate; /* bf16 [hidden] sigmoid gate, or NULL (= 1.0)  */
+    /* f32 [hidden] weight of the norm ahead of the router, or NULL. When given,
+     * x is the un-normalised hidden state (the residual sum after attention) and
+     * the layer routes and runs its experts on bf16(RMSNorm(x) * weight), with
+     * config.norm_epsilon: the post-attention norm the reference encodes ahead
+     * of the router (CMD2, metal/mod.rs:2864-3012; rms_norm_reduced,
+     * shaders.metal:1176-1213), fused into the router kernel. 16-byte aligned. */
+    const float* input_norm_weight;
 } pbmoe_moe_weights;
 
 /* Optional outputs of pbmoe_moe_layer for inspection and parity checks. Any
@@ -140,6 +147,9 @@ typedef struct pbmoe_moe_debug {
      * reference's per-phase timing buckets (FlashMoeTimingBuckets,
      * types.rs:600-640). Recording serialises the four kernels. */
     void* const* phase_events;
+    /* bf16 [tokens x hidden]: the normalised layer input when
+     * weights->input_norm_weight is given (what the router and experts read). */
+    uint16_t* normed_input;
 } pbmoe_moe_debug;
 
 /* ---------------------------------------------------------------- context */
@@ -193,6 +203,34 @@ PBMOE_API int pbmoe_fixed_mxfp4_layout(uint32_t hidden, uint32_t intermediate, u
 PBMOE_API int pbmoe_q4_matvec(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbmoe_dtype x_dtype,
                     void* y, pbmoe_dtype y_dtype, uint32_t batch, void* stream);
 
+/* Fused decode projections of one layer, one launch:
+ *   y[0][b] = W0 . n(x[b])  (+ residual[b])     and, when w[1] != NULL,
+ *   y[1][b] = W1 . n(x[b])
+ * where n(x) = x, or RMSNorm(x) * input_norm_weight (1/sqrt(mean(x^2) +
+ * epsilon)) when input_norm_weight is given. It folds the separate dispatches
+ * of the reference's MLA input projection chain and attention output
+ * (execute_glm_mla_input_projection_chain, metal/qwen_execution.rs:289-480,
+ * and mla_attention_output_values, runtime/mod.rs:2779-2940) into one kernel
+ * each: q_a and kv_a read the same normed hidden state (two matrices); q_b
+ * reads RMSNorm(q_a) (rms_norm_reduced, shaders.metal:1176-1213, as its
+ * prologue); o_proj adds the residual stream (its epilogue). Both matrices
+ * share cols and group_size. input_norm_weight (f32 [cols], 16-byte aligned)
+ * needs f32 x; residual ([batch x w[0].rows] in y_dtype) needs w[1] == NULL.
+ * The per-element fallback of pbmoe_q4_matvec has no fused forms: shapes that
+ * need it are PBMOE_ERR_UNSUPPORTED here. */
+typedef struct pbmoe_q4_fused_args {
+    const pbmoe_q4_tensor* w[2]; /* w[0] required, w[1] optional */
+    void* y[2];                  /* y[i]: [batch x w[i]->rows] in y_dtype */
+    const void* x;               /* [batch x cols] in x_dtype */
+    pbmoe_dtype x_dtype;
+    pbmoe_dtype y_dtype;
+    uint32_t batch;
+    const float* input_norm_weight;
+    float epsilon;
+    const void* residual;
+} pbmoe_q4_fused_args;
+PBMOE_API int pbmoe_q4_matvec_fused(pbmoe_ctx* ctx, const pbmoe_q4_fused_args* args, void* stream);
+
 /* Routing on given logits: logits f32 [tokens x E] -> route_ids u32 [tokens x K]
  * (replacement-slot order of routing_top_k_iter, math.rs:746-765) and
  * route_weights f32 [tokens x K] (routing_softmax_top_k, math.rs:771-783, then
@@ -224,17 +262,22 @@ PBMOE_API int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config, co
  * graph capture, loops that must not risk the synchronisation an allocation
  * can cause) and therefore cannot create a pbmoe_ctx either.
  *
- * Same arithmetic and arguments as pbmoe_moe_layer, with no context. Its
- * scratch is a fixed PBMOE_STATIC_SCRATCH_BYTES device array inside the
+ * Same arithmetic, arguments and checks as pbmoe_moe_layer, with no context.
+ * Its scratch is a fixed PBMOE_STATIC_SCRATCH_BYTES device array inside the
  * library, present on every GPU where the library's kernels are loaded until
- * the process exits; calls whose workspace does not fit (more than 34 tokens at
- * hidden 2048 / 512 experts / top-10 / intermediate 512) return
- * PBMOE_ERR_UNSUPPORTED. The array's device address is looked up on the first
- * call on each device (the calling thread's current device): make that first
- * call before any stream capture. All calls share the array: calls that may
+ * the process exits; a call fits when 256 + pbmoe_moe_workspace_bytes(tokens,
+ * config) <= PBMOE_STATIC_SCRATCH_BYTES (at most 29 tokens at hidden 2048 /
+ * 512 experts / top-10 / intermediate 512), larger calls return
+ * PBMOE_ERR_UNSUPPORTED. Up to 8 tokens it launches exactly pbmoe_moe_layer's
+ * kernels; larger calls run as one launch (pbmoe_moe_layer runs them as
+ * 8-token chunks). The array's device address is looked up on the first call
+ * on each device (the calling thread's current device): make that first call
+ * before any stream capture. All calls share the array: calls that may
  * overlap on the GPU race and must be serialised by the caller.
- * device_status (nullable, device u32) receives PBMOE_DEV_ERR_* bits; the
- * message of a failed call goes to error_buf (nullable). */
+ * device_status (nullable, device u32) receives PBMOE_DEV_ERR_* bits; when it
+ * is NULL the bits land in the shared array, which the next call clears, so
+ * errors detected on the device are not observable. The message of a failed
+ * call goes to error_buf (nullable). */
 #define PBMOE_STATIC_SCRATCH_BYTES (4u << 20)
 PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
                                      const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
@@ -545,17 +588,22 @@ PBMOE_API int pbmoe_rope_reserve(pbmoe_ctx* ctx, uint32_t max_positions, uint32_
 
 /* For each of `batch` tokens: RoPE (interleaved pairs -> split halves) on the
  * rope part of every head of `query` (f32 [batch x heads x (nope + rope)], in
- * place) and on the rope part of `kv` (f32 [batch x (latent + rope)], latent
- * part already normed), then the latent row (bf16) and the rotated key row
- * (bf16) written at the token's position of its cache (KvCache::record_mla_kv,
- * state/kv_cache.rs:414-450; the rotation call sites are runtime/mod.rs:
- * 2896-2913). positions: DEVICE u32 [batch]; c_kv / k_rope: DEVICE arrays
- * [batch] of bf16 cache pointers ([cache_len x latent], [cache_len x rope]).
- * A position >= cache_len or outside the RoPE table latches
- * PBMOE_DEV_ERR_POSITION and writes nothing for that token. */
+ * place) and on the rope part of `kv` (f32 [batch x (latent + rope)]), then
+ * the latent row (bf16) and the rotated key row (bf16) written at the token's
+ * position of its cache (KvCache::record_mla_kv, state/kv_cache.rs:414-450;
+ * the rotation call sites are runtime/mod.rs:2896-2913). With
+ * latent_norm_weight (f32 [latent]) the latent part is the kv_a output before
+ * its norm, and the row written is RMSNorm(latent) * weight (epsilon): the
+ * chain's second rms_norm_reduced (metal/qwen_execution.rs:405-437) fused
+ * here; NULL = the latent part is already normed. positions: DEVICE u32
+ * [batch]; c_kv / k_rope: DEVICE arrays [batch] of bf16 cache pointers
+ * ([cache_len x latent], [cache_len x rope]). A position >= cache_len or
+ * outside the RoPE table latches PBMOE_DEV_ERR_POSITION and writes nothing for
+ * that token. */
 PBMOE_API int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* config, uint32_t batch, float* query,
-                                    const float* kv, const uint32_t* positions, uint16_t* const* c_kv,
-                                    uint16_t* const* k_rope, uint32_t cache_len, void* stream);
+                                    const float* kv, const float* latent_norm_weight, float epsilon,
+                                    const uint32_t* positions, uint16_t* const* c_kv, uint16_t* const* k_rope,
+                                    uint32_t cache_len, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -48,7 +48,7 @@ EXPORTED = [
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
     "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
     "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host", "pbmoe_sync",
-    "pbmoe_fixed_mxfp4_layout",
+    "pbmoe_fixed_mxfp4_layout", "pbmoe_q4_matvec_fused",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -71,12 +71,12 @@ class MoeConfig(C.Structure):
 
 class MoeWeights(C.Structure):
     _fields_ = [("router_weight", C.c_void_p), ("experts", C.c_void_p), ("shared_expert", C.c_void_p),
-                ("shared_expert_gate", C.c_void_p)]
+                ("shared_expert_gate", C.c_void_p), ("input_norm_weight", C.c_void_p)]
 
 
 class MoeDebug(C.Structure):
     _fields_ = [("router_logits", C.c_void_p), ("route_ids", C.c_void_p), ("route_weights", C.c_void_p),
-                ("shared_logit", C.c_void_p), ("phase_events", C.c_void_p)]
+                ("shared_logit", C.c_void_p), ("phase_events", C.c_void_p), ("normed_input", C.c_void_p)]
 
 
 class MlaConfig(C.Structure):
@@ -114,6 +114,12 @@ class NormArgs(C.Structure):
                 ("sum_dtype", C.c_int), ("weight", C.c_void_p), ("epsilon", C.c_float), ("out", C.c_void_p),
                 ("out_dtype", C.c_int), ("rows", C.c_uint32), ("width", C.c_uint32), ("x_stride", C.c_uint32),
                 ("residual_stride", C.c_uint32), ("sum_stride", C.c_uint32), ("out_stride", C.c_uint32)]
+
+
+class Q4FusedArgs(C.Structure):
+    _fields_ = [("w", C.POINTER(Q4Tensor) * 2), ("y", C.c_void_p * 2), ("x", C.c_void_p), ("x_dtype", C.c_int),
+                ("y_dtype", C.c_int), ("batch", C.c_uint32), ("input_norm_weight", C.c_void_p),
+                ("epsilon", C.c_float), ("residual", C.c_void_p)]
 
 
 class PbmoeError(RuntimeError):
@@ -171,7 +177,9 @@ def load():
         L.pbmoe_head_merge.argtypes = [vp, vp, vp, vp, u32, u32, u32, vp, vp, vp]
         L.pbmoe_rms_norm.argtypes = [vp, C.POINTER(NormArgs), vp]
         L.pbmoe_rope_reserve.argtypes = [vp, u32, u32, C.c_double]
-        L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, vp, vp, u32, vp]
+        L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, C.c_float, vp, vp, vp, u32,
+                                             vp]
+        L.pbmoe_q4_matvec_fused.argtypes = [vp, C.POINTER(Q4FusedArgs), vp]
         L.pbmoe_sync.argtypes = [vp, vp, u32]
         L.pbmoe_moe_layer_host.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
                                            u32, vp]
@@ -350,12 +358,30 @@ class Context:
     def rope_reserve(self, max_positions, rope_dim, theta=10000.0):
         self.check(self.lib.pbmoe_rope_reserve(self.h, max_positions, rope_dim, theta))
 
-    def mla_rope_append(self, config, query, kv, positions, c_kv_ptrs, k_rope_ptrs, cache_len, stream=None):
-        """query f32 [B, heads, nope+rope] (in place); kv f32 [B, latent+rope]; positions int32 [B] device;
-        c_kv_ptrs / k_rope_ptrs int64 [B] device tensors of cache addresses."""
+    def mla_rope_append(self, config, query, kv, positions, c_kv_ptrs, k_rope_ptrs, cache_len, latent_norm=None,
+                        eps=1e-6, stream=None):
+        """query f32 [B, heads, nope+rope] (in place); kv f32 [B, latent+rope] (latent part normed here when
+        latent_norm, f32 [latent], is given); positions int32 [B] device; c_kv_ptrs / k_rope_ptrs int64 [B]
+        device tensors of cache addresses."""
         self.check(self.lib.pbmoe_mla_rope_append(self.h, C.byref(config), int(query.shape[0]), _ptr(query), _ptr(kv),
-                                                  _ptr(positions), _ptr(c_kv_ptrs), _ptr(k_rope_ptrs), cache_len,
-                                                  self.stream_ptr(stream)))
+                                                  _ptr(latent_norm), eps, _ptr(positions), _ptr(c_kv_ptrs),
+                                                  _ptr(k_rope_ptrs), cache_len, self.stream_ptr(stream)))
+
+    def q4_fused(self, mats, x, ys, norm=None, eps=1e-6, residual=None, stream=None):
+        """One launch of pbmoe_q4_matvec_fused: mats = [(packed, scales, biases, rows, cols, group)] (one or two
+        on the same x), ys the outputs [batch, rows_i]; norm (f32 [cols]) normalises x first; residual is
+        added to the single output."""
+        ts = [Q4Tensor(p.data_ptr(), s.data_ptr(), b.data_ptr(), r, c, g) for (p, s, b, r, c, g) in mats]
+        a = Q4FusedArgs()
+        a.w[0] = C.pointer(ts[0])
+        a.w[1] = C.pointer(ts[1]) if len(ts) > 1 else C.POINTER(Q4Tensor)()
+        a.y[0] = ys[0].data_ptr()
+        a.y[1] = ys[1].data_ptr() if len(ys) > 1 else None
+        a.x, a.x_dtype, a.y_dtype, a.batch = x.data_ptr(), _dtype_code(x), _dtype_code(ys[0]), int(x.shape[0])
+        a.input_norm_weight = None if norm is None else norm.data_ptr()
+        a.epsilon = eps
+        a.residual = None if residual is None else residual.data_ptr()
+        self.check(self.lib.pbmoe_q4_matvec_fused(self.h, C.byref(a), self.stream_ptr(stream)))
 
     def prefill_reserve(self, max_rows, max_cols):
         self.check(self.lib.pbmoe_prefill_reserve(self.h, max_rows, max_cols))

@@ -77,59 +77,78 @@ bool aligned(const void* p, size_t a) { return reinterpret_cast<uintptr_t>(p) % 
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Validates an expert layout for the MoE fast path. Returns 0 or a status.
-int check_layout(pbmoe_ctx* ctx, const pbmoe_expert_layout& L) {
-    const uint32_t H = L.hidden, I = L.intermediate, G = L.group_size;
-    if (H == 0 || I == 0 || G == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "expert layout has a zero dimension");
-    if (H % G != 0 || I % G != 0)
-        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
-                    "fixed-Q4 expert dimensions hidden=%u intermediate=%u must be divisible by group_size=%u", H, I,
-                    G);
-    const bool pow2 = G >= 32 && (G & (G - 1)) == 0;
-    if (!pow2 || H % 32 != 0 || I % 32 != 0 || H > 16384 || I > 16384)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
-                    "FlashMoe unsupported expert geometry on CUDA: needs group_size a power of two >= 32 and "
-                    "hidden, intermediate multiples of 32 up to 16384 (got hidden=%u intermediate=%u group=%u)",
-                    H, I, G);
-    const uint64_t gate_w = uint64_t(I) * H / 2, gate_sb = uint64_t(I) * (H / G) * 2;
-    const uint64_t down_w = uint64_t(H) * I / 2, down_sb = uint64_t(H) * (I / G) * 2;
-    const uint64_t sizes[9] = {gate_w, gate_sb, gate_sb, gate_w, gate_sb, gate_sb, down_w, down_sb, down_sb};
-    for (int i = 0; i < 9; ++i) {
-        const uint64_t o = L.component_offsets[i];
-        if (o + sizes[i] > L.expert_bytes)
-            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "expert component %d [%llu, +%llu) exceeds slot bytes %llu",
-                        i, (unsigned long long)o, (unsigned long long)sizes[i], (unsigned long long)L.expert_bytes);
-        const uint64_t need = (i % 3 == 0) ? 16 : 2;
-        if (o % need != 0)
-            return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert component %d offset %llu is not %llu-byte aligned", i,
-                        (unsigned long long)o, (unsigned long long)need);
-    }
-    if (L.expert_bytes % 16 != 0)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert slot stride %llu is not a multiple of 16",
-                    (unsigned long long)L.expert_bytes);
-    return PBMOE_OK;
-}
-
+// Shared checks (pbmoe::moe_check_config) with the message into the context.
 int check_moe_config(pbmoe_ctx* ctx, const pbmoe_moe_config* c) {
-    if (!c) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "null MoE config");
-    int rc = check_layout(ctx, c->layout);
-    if (rc) return rc;
-    if (c->num_experts == 0 || c->num_experts > 4096)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "num_experts %u outside 1..4096", c->num_experts);
-    if (c->top_k == 0 || c->top_k > 32 || c->top_k > c->num_experts)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "top_k %u outside 1..min(32, num_experts)", c->top_k);
-    if (c->normalization > PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
-                    "FlashMoe unsupported routing weights: normalisation %u is not implemented on CUDA",
-                    c->normalization);
-    if (!(c->routed_scaling_factor > 0.f) || !std::isfinite(c->routed_scaling_factor))
-        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "routed expert scale must be positive and finite");
-    return PBMOE_OK;
+    char msg[512];
+    const int rc = pbmoe::moe_check_config(c, msg, sizeof msg);
+    return rc == PBMOE_OK ? rc : fail(ctx, rc, "%s", msg);
 }
 
 }  // namespace
 
 namespace pbmoe {
+
+namespace {
+int say(char* msg, size_t len, int code, const char* fmt, ...) {
+    if (msg && len) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(msg, len, fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+}  // namespace
+
+int moe_check_layout(const pbmoe_expert_layout& L, char* msg, size_t len) {
+    const uint32_t H = L.hidden, I = L.intermediate, G = L.group_size;
+    if (H == 0 || I == 0 || G == 0) return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT, "expert layout has a zero dimension");
+    if (H % G != 0 || I % G != 0)
+        return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT,
+                   "fixed-Q4 expert dimensions hidden=%u intermediate=%u must be divisible by group_size=%u", H, I, G);
+    const bool pow2 = G >= 32 && (G & (G - 1)) == 0;
+    if (!pow2 || H % 32 != 0 || I % 32 != 0 || H > 16384 || I > 16384)
+        return say(msg, len, PBMOE_ERR_UNSUPPORTED,
+                   "FlashMoe unsupported expert geometry on CUDA: needs group_size a power of two >= 32 and "
+                   "hidden, intermediate multiples of 32 up to 16384 (got hidden=%u intermediate=%u group=%u)",
+                   H, I, G);
+    const uint64_t gate_w = uint64_t(I) * H / 2, gate_sb = uint64_t(I) * (H / G) * 2;
+    const uint64_t down_w = uint64_t(H) * I / 2, down_sb = uint64_t(H) * (I / G) * 2;
+    const uint64_t sizes[9] = {gate_w, gate_sb, gate_sb, gate_w, gate_sb, gate_sb, down_w, down_sb, down_sb};
+    for (int i = 0; i < 9; ++i) {
+        const uint64_t o = L.component_offsets[i];
+        if (o > L.expert_bytes || sizes[i] > L.expert_bytes - o)
+            return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT, "expert component %d [%llu, +%llu) exceeds slot bytes %llu",
+                       i, (unsigned long long)o, (unsigned long long)sizes[i], (unsigned long long)L.expert_bytes);
+        const uint64_t need = (i % 3 == 0) ? 16 : 2;
+        if (o % need != 0)
+            return say(msg, len, PBMOE_ERR_UNSUPPORTED, "expert component %d offset %llu is not %llu-byte aligned", i,
+                       (unsigned long long)o, (unsigned long long)need);
+    }
+    if (L.expert_bytes % 16 != 0)
+        return say(msg, len, PBMOE_ERR_UNSUPPORTED, "expert slot stride %llu is not a multiple of 16",
+                   (unsigned long long)L.expert_bytes);
+    return PBMOE_OK;
+}
+
+int moe_check_config(const pbmoe_moe_config* c, char* msg, size_t len) {
+    if (!c) return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT, "null MoE config");
+    int rc = moe_check_layout(c->layout, msg, len);
+    if (rc) return rc;
+    if (c->num_experts == 0 || c->num_experts > 4096)
+        return say(msg, len, PBMOE_ERR_UNSUPPORTED, "num_experts %u outside 1..4096", c->num_experts);
+    if (c->top_k == 0 || c->top_k > 32 || c->top_k > c->num_experts)
+        return say(msg, len, PBMOE_ERR_UNSUPPORTED, "top_k %u outside 1..min(32, num_experts)", c->top_k);
+    if (c->normalization > PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR)
+        return say(msg, len, PBMOE_ERR_UNSUPPORTED,
+                   "FlashMoe unsupported routing weights: normalisation %u is not implemented on CUDA",
+                   c->normalization);
+    if (!(c->routed_scaling_factor > 0.f) || !std::isfinite(c->routed_scaling_factor))
+        return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT, "routed expert scale must be positive and finite");
+    if (!(c->norm_epsilon >= 0.f) || !std::isfinite(c->norm_epsilon))
+        return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT, "norm epsilon must be finite and >= 0");
+    return PBMOE_OK;
+}
 
 MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
     MoeWsSizes s{};
@@ -137,7 +156,7 @@ MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t
     const size_t gmax = size_t(T) * K + 1;
     size_t* b = s.bytes;
     b[0] = 0;                    // status lives in the context
-    b[1] = 4;                    // ticket
+    b[1] = 8;                    // ticket[2]
     b[2] = size_t(T) * E * 4;    // logits
     b[3] = size_t(T) * 4;        // shared_logit
     b[4] = size_t(T) * K * 4;    // route_ids
@@ -151,16 +170,17 @@ MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t
     b[12] = R * I * 4;           // h
     b[13] = R * H * 4;           // y
     b[14] = R * hperm_stride(I); // h_perm
+    b[15] = size_t(T) * H * 2;   // xn
     s.total = 0;
-    for (int i = 0; i < 15; ++i) s.total += align_up(b[i], 256);
+    for (int i = 0; i < 16; ++i) s.total += align_up(b[i], 256);
     return s;
 }
 
 MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
     MoeWsSizes s = moe_ws_sizes(T, E, K, H, I);
     char* p = static_cast<char*>(base);
-    void* ptr[15];
-    for (int i = 0; i < 15; ++i) {
+    void* ptr[16];
+    for (int i = 0; i < 16; ++i) {
         ptr[i] = p;
         p += align_up(s.bytes[i], 256);
     }
@@ -180,6 +200,7 @@ MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t T, uint32_t E, uint32_
     w.h = static_cast<float*>(ptr[12]);
     w.y = static_cast<float*>(ptr[13]);
     w.h_perm = static_cast<uint8_t*>(ptr[14]);
+    w.xn = static_cast<uint16_t*>(ptr[15]);
     return w;
 }
 
@@ -373,6 +394,60 @@ int pbmoe_q4_matvec(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, const void* x, pbm
     return PBMOE_OK;
 }
 
+int pbmoe_q4_matvec_fused(pbmoe_ctx* ctx, const pbmoe_q4_fused_args* f, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!f || !f->w[0] || !f->x || !f->y[0] || (f->w[1] && !f->y[1]))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: null pointer");
+    for (int i = 0; i < 2; ++i) {
+        const pbmoe_q4_tensor* w = f->w[i];
+        if (!w) continue;
+        if (!w->packed || !w->scales || !w->biases)
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: null weight pointer");
+        if (w->group_size == 0 || w->rows == 0)
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: empty matrix or zero group");
+        if (!aligned(w->scales, 2) || !aligned(w->biases, 2))
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: misaligned scales / biases");
+    }
+    const pbmoe_q4_tensor* w0 = f->w[0];
+    const pbmoe_q4_tensor* w1 = f->w[1];
+    if (w1 && (w1->cols != w0->cols || w1->group_size != w0->group_size))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: the two matrices differ in cols or group");
+    if ((f->x_dtype != PBMOE_F32 && f->x_dtype != PBMOE_BF16) || (f->y_dtype != PBMOE_F32 && f->y_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (f->input_norm_weight && (f->x_dtype != PBMOE_F32 || !aligned(f->input_norm_weight, 16) ||
+                                 !(f->epsilon >= 0.f) || !std::isfinite(f->epsilon)))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
+                    "q4 fused matvec: the input norm needs f32 x, a 16-byte aligned weight and a finite epsilon");
+    if (f->residual && w1)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: a residual goes with one matrix only");
+    const size_t ys = f->y_dtype == PBMOE_F32 ? 4 : 2;
+    if (!aligned(f->x, f->x_dtype == PBMOE_F32 ? 4 : 2) || !aligned(f->y[0], ys) || (w1 && !aligned(f->y[1], ys)) ||
+        (f->residual && !aligned(f->residual, ys)))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 fused matvec: misaligned x / y / residual");
+    if (f->batch == 0 || w0->cols == 0) return PBMOE_OK;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    Q4MatvecArgs a{static_cast<const uint8_t*>(w0->packed), w0->scales, w0->biases, w0->rows, w0->cols, w0->group_size,
+                   f->x, f->x_dtype, f->y[0], f->y_dtype, f->batch};
+    a.norm_w = f->input_norm_weight;
+    a.eps = f->epsilon;
+    a.residual = f->residual;
+    if (w1) {
+        a.packed2 = static_cast<const uint8_t*>(w1->packed);
+        a.scales2 = w1->scales;
+        a.biases2 = w1->biases;
+        a.rows2 = w1->rows;
+        a.y2 = f->y[1];
+    }
+    cudaError_t e = q4_matvec_launch(a, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorNotSupported)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported fused q4 matvec: cols=%u group=%u needs the fast path (cols a multiple of 32, "
+                    "group a power of two >= 32, 16-byte aligned rows and x)", w0->cols, w0->group_size);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 fused matvec launch");
+    return PBMOE_OK;
+}
+
 int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint32_t E, uint32_t K,
                      uint32_t normalization, float routed_scale, uint32_t* ids, float* weights, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
@@ -413,8 +488,10 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     if (!aligned(x, 16))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "moe layer: x must be 16-byte aligned (rows are read as 16-byte vectors)");
     if (!aligned(w->experts, 16) || (w->shared_expert && !aligned(w->shared_expert, 16)) ||
-        !aligned(w->router_weight, 16) || (w->shared_expert_gate && !aligned(w->shared_expert_gate, 16)))
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "expert table, shared expert and router weights must be 16-byte aligned");
+        !aligned(w->router_weight, 16) || (w->shared_expert_gate && !aligned(w->shared_expert_gate, 16)) ||
+        (w->input_norm_weight && !aligned(w->input_norm_weight, 16)))
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "expert table, shared expert, router and input-norm weights must be 16-byte aligned");
     if (tokens == 0) return PBMOE_OK;
     const uint32_t E = c->num_experts, K = c->top_k, H = c->layout.hidden, I = c->layout.intermediate;
     if (!ctx->ws_base || tokens > ctx->ws_tokens || ctx->ws_E != E || ctx->ws_K != K || ctx->ws_H != H ||
@@ -451,6 +528,8 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     a.shared_gate = w->shared_expert_gate;
     a.experts = w->experts;
     a.shared_slot = w->shared_expert;
+    a.in_norm_w = w->input_norm_weight;
+    a.in_eps = c->norm_epsilon;
     a.pdl = true;
     a.phase_events = debug ? debug->phase_events : nullptr;
     a.expert_lo = e_lo;
@@ -467,6 +546,7 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     if (tokens > 8 && !ep && !a.phase_events) {
         MoeLaunch probe = a;
         probe.tokens = 8;
+        if (a.in_norm_w) probe.x_dtype = PBMOE_BF16;  // the experts read the normalised bf16 rows
         if (pbmoe::moe_pipe_supported(probe)) chunk = 8;
     }
     const size_t xs = x_dtype == PBMOE_BF16 ? 2 : 4, os = out_dtype == PBMOE_BF16 ? 2 : 4;
@@ -493,6 +573,9 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
                                     cudaMemcpyDeviceToDevice, s);
             if (e == cudaSuccess && debug->shared_logit)
                 e = cudaMemcpyAsync(at(debug->shared_logit, c0 * 4), a.ws.shared_logit, n * 4,
+                                    cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && debug->normed_input && a.in_norm_w)
+                e = cudaMemcpyAsync(at(debug->normed_input, c0 * H * 2), a.ws.xn, n * H * 2,
                                     cudaMemcpyDeviceToDevice, s);
             if (e != cudaSuccess) return cuda_fail(ctx, e, "moe debug copy");
         }
@@ -1135,11 +1218,13 @@ int pbmoe_rope_reserve(pbmoe_ctx* ctx, uint32_t max_positions, uint32_t rope_dim
 }
 
 int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* cfg, uint32_t batch, float* query, const float* kv,
-                          const uint32_t* positions, uint16_t* const* c_kv, uint16_t* const* k_rope,
-                          uint32_t cache_len, void* stream) {
+                          const float* latent_norm_weight, float epsilon, const uint32_t* positions,
+                          uint16_t* const* c_kv, uint16_t* const* k_rope, uint32_t cache_len, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
     if (!cfg || !query || !kv || !positions || !c_kv || !k_rope)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla rope append: null pointer");
+    if (latent_norm_weight && (!(epsilon >= 0.f) || !std::isfinite(epsilon)))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla rope append: norm epsilon must be finite and >= 0");
     if (batch == 0) return PBMOE_OK;
     if (!ctx->rope_table || ctx->rope_dim != cfg->rope_dim)
         return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "mla rope append: rope dim %u needs pbmoe_rope_reserve",
@@ -1157,6 +1242,8 @@ int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* cfg, uint32_t 
     a.latent = cfg->latent_dim;
     a.query = query;
     a.kv = kv;
+    a.latent_norm_w = latent_norm_weight;
+    a.eps = epsilon;
     a.positions = positions;
     a.c_kv = c_kv;
     a.k_rope = k_rope;

@@ -261,10 +261,17 @@ static int check_metadata(const char* root, uint32_t layer, const pbmoe_expert_l
         info.fixed = true;
     } else if (fmt->s == "FIXED_MXFP4_EXPERT_LAYER_V1") {
         info.fixed = info.mxfp4 = true;
-        const auto& o = L->component_offsets;
-        if (o[2] != o[3] || o[5] != o[6] || o[8] != L->expert_bytes)
-            return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert layout for %s: an MXFP4 layer needs the "
-                          "MXFP4 layout (no bias components)", path.c_str());
+        // the slot image of QwenMoeQ4ExpertLayout::fixed_mxfp4 (model_family.rs:846-952) for the layout's
+        // shape: any other offsets would read the slot's bytes in the wrong places
+        pbmoe_expert_layout want{};
+        bool same = pbmoe_fixed_mxfp4_layout(L->hidden, L->intermediate, L->group_size, &want) == PBMOE_OK &&
+                    want.expert_bytes == L->expert_bytes;
+        for (int i = 0; same && i < 9; ++i) same = want.component_offsets[i] == L->component_offsets[i];
+        if (!same)
+            return e.fail(PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert layout for %s: an MXFP4 layer needs "
+                          "the fixed MXFP4 layout of hidden %u, intermediate %u, group %u (E2M1 nibbles and E8M0 "
+                          "scales per projection, no bias components)",
+                          path.c_str(), L->hidden, L->intermediate, L->group_size);
     } else if (fmt->s == "PBQ4EXPERT_LAYER_V1" || fmt->s == "PBQ4EXPERT_LAYER_V2") {
         info.fixed = false;
     } else {

@@ -15,7 +15,8 @@ namespace pbmoe {
 // t*K + k for routed routes and T*K + t for token t's shared-expert route.
 struct MoeWs {
     uint32_t* status;        // device status word (PBMOE_DEV_ERR_*)
-    uint32_t* ticket;        // last-CTA counter of the router kernel, kept at 0 between launches
+    uint32_t* ticket;        // [2] router-kernel counters (CTAs with logits written, CTAs done
+                             // routing), kept at 0 between launches
     float* logits;           // [T x E]
     float* shared_logit;     // [T]
     uint32_t* route_ids;     // [T x K]
@@ -30,6 +31,7 @@ struct MoeWs {
     float* y;                // [(T*K + T) x H] expert outputs per route
     uint8_t* h_perm;         // [(T*K + T) x hperm_stride] SwiGLU activations as bf16 hi/lo pair
                              // slots + per-8 partial sums (input layout of the pipelined down kernel)
+    uint16_t* xn;            // [T x H] bf16 RMSNorm(x) * w when the layer normalises its own input
 };
 
 // Bytes per route of MoeWs::h_perm for intermediate size I: hi slots, lo
@@ -93,6 +95,11 @@ struct MoeLaunch {
     void* next_normed;
     const uint16_t* router_w;
     const uint16_t* shared_gate;
+    // when set, x is the un-normalised hidden state: the router kernel writes
+    // ws.xn = bf16(RMSNorm(x) * in_norm_w) (epsilon in_eps), and routing and
+    // the experts run on it (the post-attention norm of CMD2)
+    const float* in_norm_w;
+    float in_eps;
     const uint8_t* experts;
     const uint8_t* shared_slot;
     bool pdl;  // launch the router kernel with programmatic dependent launch
@@ -106,12 +113,17 @@ struct MoeLaunch {
 
 // Per-launch bytes of each workspace array, in MoeWs order (host arithmetic).
 struct MoeWsSizes {
-    size_t bytes[15];
+    size_t bytes[16];
     size_t total;
 };
 MoeWsSizes moe_ws_sizes(uint32_t max_tokens, uint32_t E, uint32_t K, uint32_t H, uint32_t I);
 MoeWs moe_ws_carve(void* base, uint32_t* status, uint32_t max_tokens, uint32_t E, uint32_t K, uint32_t H,
                    uint32_t I);
+
+// Layout and config checks shared by every MoE layer entry point: a PBMOE_*
+// status, the failure's text in msg (len bytes).
+int moe_check_layout(const pbmoe_expert_layout& L, char* msg, size_t len);
+int moe_check_config(const pbmoe_moe_config* c, char* msg, size_t len);
 
 cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s);
 // Tensor-core expert kernels (group-64 layouts, moe_mma.cu).
@@ -137,6 +149,16 @@ struct Q4MatvecArgs {
     void* y;
     pbmoe_dtype y_dtype;
     uint32_t batch;
+    // fusions (pbmoe_q4_matvec_fused); zero = off
+    const float* norm_w;  // x -> RMSNorm(x) * norm_w (epsilon eps) before the products; f32 x
+    float eps;
+    const void* residual;  // y = W x + residual ([batch x rows] in y_dtype)
+    // a second matrix [rows2 x cols] (same group) on the same x, output y2
+    const uint8_t* packed2;
+    const uint16_t* scales2;
+    const uint16_t* biases2;
+    uint32_t rows2;
+    void* y2;
 };
 // Returns cudaErrorNotSupported when the shape needs more shared memory than
 // a CTA has.
@@ -252,6 +274,8 @@ struct RopeAppendArgs {
     uint32_t batch, heads, nope, rope, latent;
     float* query;               // [batch x heads x (nope + rope)]
     const float* kv;            // [batch x (latent + rope)]
+    const float* latent_norm_w;  // [latent]: the latent part is normalised here (NULL: already normed)
+    float eps;
     const uint32_t* positions;  // [batch]
     uint16_t* const* c_kv;      // [batch] cache rows [cache_len x latent]
     uint16_t* const* k_rope;    // [batch] cache rows [cache_len x rope]

@@ -36,157 +36,446 @@ namespace pbmoe {
 namespace cg = cooperative_groups;
 
 // ---------------------------------------------------------------- kernel 1
-constexpr int kRouterThreads = 256;
-constexpr int kRouterRowsPerWarp = 1;
-constexpr int kRouterTokPass = 8;
-constexpr int kRouterVec = 8;  // 16-byte weight vectors per lane loaded before use
+// Router logits in exactly the reference's arithmetic. dense_mmap_fma_matvec_bf16
+// (shaders.metal:1059-1075), restated on the CPU as the oracle's router, runs one
+// sequential fp32 fma chain per (row, token): acc = fma(w[c], x[c], acc) for
+// c = 0, 1, ..., H-1. Route ids are integer outputs and must match bit for bit,
+// so every (row, token) chain here is one thread walking the columns in that
+// order: the sum is never split or reassociated, and identical inputs give
+// identical logits, hence identical top-k ids.
+//
+// A CTA owns kRtRows consecutive rows (row E is the shared-expert gate). Their
+// bf16 weights arrive in shared memory by bulk copies (one per row and
+// kRtChunk-column chunk, each chunk completing on its own mbarrier), issued
+// before the programmatic-dependent-launch wait since they do not depend on
+// the previous kernel. Activations are staged per chunk as f32 in a padded,
+// double-buffered layout (the next chunk's loads are in flight while the
+// current chunk's fmas run). Warp w runs row w and lane t token t of a pass of
+// up to kRtTokPass tokens, so a warp's weight reads are broadcasts and its
+// activation reads hit distinct banks.
+//
+// With in_norm_w the layer input x is the un-normalised hidden state: every
+// CTA computes the tokens' RMSNorm scales, the staged values are
+// bf16(x * scale * w) (the post-attention norm the reference runs ahead of the
+// router, rms_norm_reduced, shaders.metal:1176-1213), and the CTAs together
+// write those rows to ws.xn, the expert kernels' input.
+//
+// Routing and the group plan are spread over several CTAs: each CTA counts
+// itself in ticket[0] once its logits are written; the first NR CTAs (at most
+// kRtRouteCtas, so the other CTAs always find SM slots) wait, bounded, for
+// ticket[0] == gridDim.x, route one token per warp (route_token_smem: the
+// exact slot order of routing_top_k_iter, math.rs:746-765), count themselves
+// in ticket[1], and the last of them builds the layer-major plan (unique
+// experts ascending, routes in route order inside each group, the shared
+// expert as group 0) and resets both counters for the next launch.
+constexpr int kRtRows = 4;
+constexpr int kRtThreads = 32 * kRtRows;
+constexpr uint32_t kRtTokPass = 32;
+constexpr uint32_t kRtChunk = 256;
+constexpr uint32_t kRtXStride = kRtChunk + 4;  // padded f32 row of a staged chunk
+constexpr uint32_t kRtMaxChunks = 64;          // hidden <= 16384
+constexpr uint32_t kRtRouteCtas = 64;
+constexpr size_t kRtStageBudget = 200 * 1024;  // weights + bf16 token rows of one pass
+constexpr int kRtVecs = static_cast<int>(kRtTokPass * kRtChunk / 4 / kRtThreads);  // float4 per thread per chunk
+
+// Activation staging: bf16 rows when the layer input is bf16 or is
+// normalised here (the normalised rows are bf16 by definition) — a pass's
+// token rows are staged once, [pass][H + 8] bf16 (the pad puts consecutive
+// tokens' 16-byte reads in distinct banks); f32 rows otherwise — 256-column
+// chunks of f32, double-buffered.
+//
+// With bf16 rows the weights are also converted once to f32 rows in shared
+// memory (wf_bytes, when they fit), so the chains' inner step is two f32
+// weight reads, one bf16 activation read and eight fmas.
+struct RtSmem {
+    size_t w_bytes, wf_bytes, x_bytes, total;
+    uint32_t pass;    // tokens per pass
+    uint32_t stride;  // bf16 elements per staged row (bf16 rows)
+};
+__host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_t E, uint32_t K, bool bf16_rows) {
+    RtSmem s;
+    s.w_bytes = (static_cast<size_t>(kRtRows) * H * 2 + 127) / 128 * 128;
+    s.wf_bytes = 0;
+    if (bf16_rows) {
+        if (static_cast<size_t>(kRtRows) * H * 4 + s.w_bytes <= 96 * 1024) s.wf_bytes = static_cast<size_t>(kRtRows) * H * 4;
+        s.stride = H + 8;
+        const size_t row = static_cast<size_t>(s.stride) * 2;
+        const size_t used = s.w_bytes + s.wf_bytes;
+        size_t pass = used < kRtStageBudget ? (kRtStageBudget - used) / row : 1;
+        if (pass < 1) pass = 1;
+        if (pass > kRtTokPass) pass = kRtTokPass;
+        if (pass > T) pass = T;
+        s.pass = static_cast<uint32_t>(pass);
+        s.x_bytes = (pass * row + 15) / 16 * 16;
+    } else {
+        s.stride = 0;
+        s.pass = kRtTokPass;
+        s.x_bytes = static_cast<size_t>(2) * kRtTokPass * kRtXStride * 4;
+    }
+    const size_t stage = s.w_bytes + s.wf_bytes + s.x_bytes + static_cast<size_t>(T) * 4;  // + norm scales
+    const size_t plan = (3ull * E + 2ull * T * K + 32) * 4;
+    const size_t route = static_cast<size_t>(kRtRows) * ((E + 3) & ~3u) * 4;
+    size_t m = stage > plan ? stage : plan;
+    s.total = m > route ? m : route;
+    return s;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float4 rt_load4(const T* p, size_t i);
+template <>
+__device__ __forceinline__ float4 rt_load4<float>(const float* p, size_t i) {
+    return *reinterpret_cast<const float4*>(p + i);
+}
+template <>
+__device__ __forceinline__ float4 rt_load4<uint16_t>(const uint16_t* p, size_t i) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p + i);
+    return make_float4(bf16_bits_to_f32(u.x & 0xffffu), bf16_bits_to_f32(u.x >> 16), bf16_bits_to_f32(u.y & 0xffffu),
+                       bf16_bits_to_f32(u.y >> 16));
+}
 
 template <typename XT>
-__global__ void __launch_bounds__(kRouterThreads)
+__global__ void __launch_bounds__(kRtThreads)
 moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
                   uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
                   const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
-                  uint32_t* ep_epoch, MoeWs ws) {
-    extern __shared__ __align__(16) float smem[];
-    XT* xs = reinterpret_cast<XT*>(smem);  // [kRouterTokPass][H], in x's own type
+                  uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps, MoeWs ws) {
+    extern __shared__ __align__(128) unsigned char rt_smem[];
+    __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
+    __shared__ uint32_t cta_flag;  // plan CTA selection
+    __shared__ uint32_t failed;    // a bounded wait expired
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool bf16_rows = sizeof(XT) == 2 || in_norm_w != nullptr;
+    const RtSmem SL = rt_smem_layout(T, H, E, K, bf16_rows);
+    uint16_t* w_s = reinterpret_cast<uint16_t*>(rt_smem);
+    float* wf_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes);
+    float* x_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes);
+    uint16_t* xb_s = reinterpret_cast<uint16_t*>(rt_smem + SL.w_bytes + SL.wf_bytes);
+    float* scale_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes + SL.x_bytes);
     const uint32_t nrows = E + (shared_gate_w ? 1u : 0u);
-    const uint32_t row0 = (blockIdx.x * (kRouterThreads / 32) + warp) * kRouterRowsPerWarp;
-    const uint32_t vec_per_row = H / 8;  // 16-byte vectors of 8 bf16
+    const uint32_t row0 = blockIdx.x * kRtRows;
+    const uint32_t rows_here = min(nrows - row0, static_cast<uint32_t>(kRtRows));
+    const uint32_t nchunks = (H + kRtChunk - 1) / kRtChunk;
 
-    // The router row does not depend on earlier kernels: start its loads
-    // before waiting for the previous kernel (programmatic dependent launch).
-    const uint32_t row = row0;
-    const bool has_row = row < nrows;
-    const uint16_t* wrow = !has_row ? nullptr : (row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w);
-    uint4 w4[kRouterVec];
-    auto load_block = [&](uint32_t vb) {
-#pragma unroll
-        for (int i = 0; i < kRouterVec; ++i) {
-            const uint32_t v = vb + i * 32 + lane;
-            w4[i] = (has_row && v < vec_per_row) ? ld_stream_u4(wrow + static_cast<size_t>(v) * 8)
-                                                 : make_uint4(0, 0, 0, 0);
-        }
-    };
-    load_block(0);
-    pdl_wait();
-    for (uint32_t t0 = 0; t0 < T; t0 += kRouterTokPass) {
-        const uint32_t nt = min(T - t0, static_cast<uint32_t>(kRouterTokPass));
-        __syncthreads();
-        {  // stage x (a copy): every 16-byte load issued before any store
-            constexpr uint32_t kPerVec = 16 / sizeof(XT);
-            const uint32_t vpr = H / kPerVec, total = nt * vpr;
-            const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0) * H);
-            uint4* dst = reinterpret_cast<uint4*>(xs);
-            for (uint32_t base = 0; base < total; base += 8 * blockDim.x) {
-                uint4 v[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t idx = base + i * blockDim.x + threadIdx.x;
-                    if (idx < total) v[i] = src[idx];
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t idx = base + i * blockDim.x + threadIdx.x;
-                    if (idx < total) dst[idx] = v[i];
-                }
-            }
-        }
-        __syncthreads();
-        if (has_row) {
-            float acc[kRouterTokPass];
-#pragma unroll
-            for (int t = 0; t < kRouterTokPass; ++t) acc[t] = 0.f;
-            for (uint32_t vb = 0; vb < vec_per_row; vb += 32 * kRouterVec) {
-                if (vb > 0 || t0 > 0) load_block(vb);
-#pragma unroll
-                for (int i = 0; i < kRouterVec; ++i) {
-                    const uint32_t v = vb + i * 32 + lane;
-                    if (v >= vec_per_row) break;
-                    const uint32_t wv[4] = {w4[i].x, w4[i].y, w4[i].z, w4[i].w};
-                    float wf[8];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        wf[2 * q] = __uint_as_float(wv[q] << 16);
-                        wf[2 * q + 1] = __uint_as_float(wv[q] & 0xffff0000u);
-                    }
-#pragma unroll
-                    for (int t = 0; t < kRouterTokPass; ++t) {
-                        if (static_cast<uint32_t>(t) < nt) {
-                            float4 a, b;
-                            if constexpr (sizeof(XT) == 2) {  // bf16: one 16-byte read, widened exactly
-                                const uint4 q = *reinterpret_cast<const uint4*>(xs + t * H + v * 8);
-                                a = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
-                                                __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
-                                b = make_float4(__uint_as_float(q.z << 16), __uint_as_float(q.z & 0xffff0000u),
-                                                __uint_as_float(q.w << 16), __uint_as_float(q.w & 0xffff0000u));
-                            } else {
-                                const float4* xp = reinterpret_cast<const float4*>(xs + t * H + v * 8);
-                                a = xp[0];
-                                b = xp[1];
-                            }
-                            acc[t] = fmaf(wf[0], a.x, acc[t]);
-                            acc[t] = fmaf(wf[1], a.y, acc[t]);
-                            acc[t] = fmaf(wf[2], a.z, acc[t]);
-                            acc[t] = fmaf(wf[3], a.w, acc[t]);
-                            acc[t] = fmaf(wf[4], b.x, acc[t]);
-                            acc[t] = fmaf(wf[5], b.y, acc[t]);
-                            acc[t] = fmaf(wf[6], b.z, acc[t]);
-                            acc[t] = fmaf(wf[7], b.w, acc[t]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < kRouterTokPass; ++t) {
-                if (static_cast<uint32_t>(t) < nt) {
-                    const float sum = warp_sum(acc[t]);
-                    if (lane == 0) {
-                        if (row < E)
-                            ws.logits[static_cast<size_t>(t0 + t) * E + row] = sum;
-                        else
-                            ws.shared_logit[t0 + t] = sum;
-                    }
+    // weights: the CTA's router rows (contiguous) in one bulk copy, the gate
+    // row in another; with f32 weight rows the chains start once all have
+    // landed (bars[0]), otherwise chunk by chunk (bars[k] per 256 columns)
+    if (threadIdx.x == 0) {
+        failed = 0;
+        const uint32_t router_rows = row0 < E ? min(E - row0, rows_here) : 0u;
+        if (SL.wf_bytes) {
+            mbar_init(&bars[0], 1);
+            fence_mbar_init();
+            mbar_arrive_expect_tx(&bars[0], rows_here * H * 2);
+            if (router_rows) bulk_load(w_s, router_w + static_cast<size_t>(row0) * H, router_rows * H * 2, &bars[0]);
+            if (router_rows < rows_here)
+                bulk_load(w_s + static_cast<size_t>(router_rows) * H, shared_gate_w, H * 2, &bars[0]);
+        } else {
+            for (uint32_t k = 0; k < nchunks; ++k) mbar_init(&bars[k], 1);
+            fence_mbar_init();
+            for (uint32_t k = 0; k < nchunks; ++k) {
+                const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+                mbar_arrive_expect_tx(&bars[k], rows_here * cw * 2);
+                for (uint32_t r = 0; r < rows_here; ++r) {
+                    const uint32_t row = row0 + r;
+                    const uint16_t* src = (row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w) + c0;
+                    bulk_load(w_s + static_cast<size_t>(r) * H + c0, src, cw * 2, &bars[k]);
                 }
             }
         }
     }
+    pdl_wait();
 
-    // ---- last CTA: routing + group plan
-    __shared__ uint32_t is_last;
+    // per-token RMSNorm scales of the layer input (same formula as
+    // rms_norm_rows_kernel: 1 / sqrt(mean(s^2) + eps))
+    if (in_norm_w) {
+        for (uint32_t t = warp; t < T; t += kRtRows) {
+            float ss = 0.f;
+            for (uint32_t c = lane * 4; c < H; c += 128) {
+                const float4 v = rt_load4<XT>(x, static_cast<size_t>(t) * H + c);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) scale_s[t] = 1.0f / sqrtf(ss / static_cast<float>(H) + in_eps);
+        }
+    }
+    __syncthreads();
+
+    const uint16_t* wrow = w_s + static_cast<size_t>(warp) * H;
+    const uint32_t nchunk_cols = kRtChunk;
+    auto wait_chunk = [&](uint32_t k) {
+        if (!failed && !mbar_wait_bounded(&bars[k], 0, kPipeWaitNs)) {
+            failed = 1;
+            latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+        }
+    };
+    auto write_logit = [&](uint32_t t, float acc) {
+        const uint32_t row = row0 + warp;
+        if (row < E)
+            ws.logits[static_cast<size_t>(t) * E + row] = acc;
+        else
+            ws.shared_logit[t] = acc;
+    };
+
+    if (bf16_rows) {
+        // ---- bf16 token rows, staged once per pass
+        const uint32_t vpr = H / 8;  // 8-column vectors per row
+        for (uint32_t t0 = 0; t0 < T; t0 += SL.pass) {
+            const uint32_t tp = min(T - t0, SL.pass);
+            if (t0 > 0) __syncthreads();  // the previous pass's chains are done with the rows
+            constexpr int kTok = 4;
+            for (uint32_t tt0 = 0; tt0 < tp; tt0 += kTok) {
+                for (uint32_t v0 = threadIdx.x; v0 < vpr; v0 += 2 * kRtThreads) {
+                    constexpr int kW = sizeof(XT) == 2 ? 1 : 2;  // 16-byte words per 8 columns
+                    uint4 raw[kTok][2][kW];
+#pragma unroll
+                    for (int a = 0; a < kTok; ++a)
+#pragma unroll
+                        for (int bb = 0; bb < 2; ++bb) {
+                            const uint32_t tt = tt0 + a, v = v0 + bb * kRtThreads;
+                            if (tt < tp && v < vpr) {
+                                const uint4* src = reinterpret_cast<const uint4*>(
+                                    x + static_cast<size_t>(t0 + tt) * H + static_cast<size_t>(v) * 8);
+#pragma unroll
+                                for (int q = 0; q < kW; ++q) raw[a][bb][q] = src[q];
+                            }
+                        }
+#pragma unroll
+                    for (int a = 0; a < kTok; ++a)
+#pragma unroll
+                        for (int bb = 0; bb < 2; ++bb) {
+                            const uint32_t tt = tt0 + a, v = v0 + bb * kRtThreads;
+                            if (tt < tp && v < vpr) {
+                                uint4 pk;
+                                if (sizeof(XT) == 2 && !in_norm_w) {
+                                    pk = raw[a][bb][0];  // bf16 rows as they are
+                                } else {
+                                    float f[8];
+                                    if constexpr (sizeof(XT) == 2) {
+                                        const uint4 r = raw[a][bb][0];
+                                        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                                        for (int q = 0; q < 4; ++q) {
+                                            f[2 * q] = __uint_as_float(w4[q] << 16);
+                                            f[2 * q + 1] = __uint_as_float(w4[q] & 0xffff0000u);
+                                        }
+                                    } else {
+#pragma unroll
+                                        for (int q = 0; q < 2; ++q) {
+                                            const uint4 r = raw[a][bb][q % kW];
+                                            f[4 * q] = __uint_as_float(r.x), f[4 * q + 1] = __uint_as_float(r.y);
+                                            f[4 * q + 2] = __uint_as_float(r.z), f[4 * q + 3] = __uint_as_float(r.w);
+                                        }
+                                    }
+                                    uint32_t bits[8];
+                                    if (in_norm_w) {
+                                        const float sc = scale_s[t0 + tt];
+                                        const float4 n0 = *reinterpret_cast<const float4*>(in_norm_w + v * 8);
+                                        const float4 n1 = *reinterpret_cast<const float4*>(in_norm_w + v * 8 + 4);
+                                        const float nn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                                        for (int q = 0; q < 8; ++q) bits[q] = f32_to_bf16_bits(f[q] * sc * nn[q]);
+                                    } else {
+#pragma unroll
+                                        for (int q = 0; q < 8; ++q) bits[q] = f32_to_bf16_bits(f[q]);
+                                    }
+                                    pk = make_uint4(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16),
+                                                    bits[4] | (bits[5] << 16), bits[6] | (bits[7] << 16));
+                                }
+                                *reinterpret_cast<uint4*>(xb_s + static_cast<size_t>(tt) * SL.stride + v * 8) = pk;
+                                // the normalised rows for the experts: token t's row by CTA t mod grid
+                                if (in_norm_w && (t0 + tt) % gridDim.x == blockIdx.x)
+                                    *reinterpret_cast<uint4*>(ws.xn + static_cast<size_t>(t0 + tt) * H + v * 8) = pk;
+                            }
+                        }
+                }
+            }
+            if (SL.wf_bytes && t0 == 0) {
+                // the weights have landed: f32 copy of the rows, once
+                wait_chunk(0);
+                const uint32_t nvec = rows_here * H / 8;
+                for (uint32_t i = threadIdx.x; i < nvec; i += kRtThreads) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(w_s + static_cast<size_t>(i) * 8);
+                    float4* d = reinterpret_cast<float4*>(wf_s + static_cast<size_t>(i) * 8);
+                    d[0] = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
+                                       __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
+                    d[1] = make_float4(__uint_as_float(q.z << 16), __uint_as_float(q.z & 0xffff0000u),
+                                       __uint_as_float(q.w << 16), __uint_as_float(q.w & 0xffff0000u));
+                }
+            }
+            __syncthreads();
+            if (SL.wf_bytes && static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp) {
+                const uint16_t* xr = xb_s + static_cast<size_t>(lane) * SL.stride;
+                const float* wr = wf_s + static_cast<size_t>(warp) * H;
+                float acc = 0.f;
+#pragma unroll 4
+                for (uint32_t c = 0; c < H; c += 8) {
+                    const float4 w0 = *reinterpret_cast<const float4*>(wr + c);
+                    const float4 w1 = *reinterpret_cast<const float4*>(wr + c + 4);
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
+                    acc = fmaf(w0.x, __uint_as_float(xv.x << 16), acc);
+                    acc = fmaf(w0.y, __uint_as_float(xv.x & 0xffff0000u), acc);
+                    acc = fmaf(w0.z, __uint_as_float(xv.y << 16), acc);
+                    acc = fmaf(w0.w, __uint_as_float(xv.y & 0xffff0000u), acc);
+                    acc = fmaf(w1.x, __uint_as_float(xv.z << 16), acc);
+                    acc = fmaf(w1.y, __uint_as_float(xv.z & 0xffff0000u), acc);
+                    acc = fmaf(w1.z, __uint_as_float(xv.w << 16), acc);
+                    acc = fmaf(w1.w, __uint_as_float(xv.w & 0xffff0000u), acc);
+                }
+                write_logit(t0 + lane, acc);
+            } else if (static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp) {
+                const uint16_t* xr = xb_s + static_cast<size_t>(lane) * SL.stride;
+                float acc = 0.f;
+                for (uint32_t k = 0; k < nchunks; ++k) {
+                    wait_chunk(k);
+                    const uint32_t c0 = k * nchunk_cols, ce = min(H, c0 + nchunk_cols);
+#pragma unroll 4
+                    for (uint32_t c = c0; c < ce; c += 8) {
+                        const uint4 q = *reinterpret_cast<const uint4*>(wrow + c);
+                        const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
+                        acc = fmaf(__uint_as_float(q.x << 16), __uint_as_float(xv.x << 16), acc);
+                        acc = fmaf(__uint_as_float(q.x & 0xffff0000u), __uint_as_float(xv.x & 0xffff0000u), acc);
+                        acc = fmaf(__uint_as_float(q.y << 16), __uint_as_float(xv.y << 16), acc);
+                        acc = fmaf(__uint_as_float(q.y & 0xffff0000u), __uint_as_float(xv.y & 0xffff0000u), acc);
+                        acc = fmaf(__uint_as_float(q.z << 16), __uint_as_float(xv.z << 16), acc);
+                        acc = fmaf(__uint_as_float(q.z & 0xffff0000u), __uint_as_float(xv.z & 0xffff0000u), acc);
+                        acc = fmaf(__uint_as_float(q.w << 16), __uint_as_float(xv.w << 16), acc);
+                        acc = fmaf(__uint_as_float(q.w & 0xffff0000u), __uint_as_float(xv.w & 0xffff0000u), acc);
+                    }
+                }
+                write_logit(t0 + lane, acc);
+            }
+        }
+    } else {
+        // ---- f32 token rows (f32 input, no norm): 256-column chunks, double-buffered
+        float4 reg[kRtVecs];
+        auto load_regs = [&](uint32_t t0, uint32_t tp, uint32_t k) {
+            const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+            const uint32_t vpr = cw / 4, total = tp * vpr;
+#pragma unroll
+            for (int j = 0; j < kRtVecs; ++j) {
+                const uint32_t i = threadIdx.x + j * kRtThreads;
+                if (i < total) {
+                    const uint32_t tt = i / vpr, cc = (i - tt * vpr) * 4;
+                    reg[j] = rt_load4<XT>(x, static_cast<size_t>(t0 + tt) * H + c0 + cc);
+                }
+            }
+        };
+        auto store_regs = [&](uint32_t tp, uint32_t k, float* dst) {
+            const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+            const uint32_t vpr = cw / 4, total = tp * vpr;
+#pragma unroll
+            for (int j = 0; j < kRtVecs; ++j) {
+                const uint32_t i = threadIdx.x + j * kRtThreads;
+                if (i < total) {
+                    const uint32_t tt = i / vpr, cc = (i - tt * vpr) * 4;
+                    *reinterpret_cast<float4*>(dst + tt * kRtXStride + cc) = reg[j];
+                }
+            }
+        };
+        const uint32_t xbuf = kRtTokPass * kRtXStride;  // floats per staging buffer
+        for (uint32_t t0 = 0; t0 < T; t0 += kRtTokPass) {
+            const uint32_t tp = min(T - t0, kRtTokPass);
+            const bool mine = static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp;
+            load_regs(t0, tp, 0);
+            store_regs(tp, 0, x_s);
+            __syncthreads();
+            float acc = 0.f;
+            for (uint32_t k = 0; k < nchunks; ++k) {
+                if (k + 1 < nchunks) load_regs(t0, tp, k + 1);
+                if (mine) {
+                    wait_chunk(k);
+                    const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+                    const uint16_t* wr = wrow + c0;
+                    const float* xr = x_s + (k & 1u) * xbuf + lane * kRtXStride;
+#pragma unroll 4
+                    for (uint32_t c = 0; c < cw; c += 8) {
+                        const uint4 q = *reinterpret_cast<const uint4*>(wr + c);
+                        const float4 a = *reinterpret_cast<const float4*>(xr + c);
+                        const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+                        acc = fmaf(__uint_as_float(q.x << 16), a.x, acc);
+                        acc = fmaf(__uint_as_float(q.x & 0xffff0000u), a.y, acc);
+                        acc = fmaf(__uint_as_float(q.y << 16), a.z, acc);
+                        acc = fmaf(__uint_as_float(q.y & 0xffff0000u), a.w, acc);
+                        acc = fmaf(__uint_as_float(q.z << 16), b.x, acc);
+                        acc = fmaf(__uint_as_float(q.z & 0xffff0000u), b.y, acc);
+                        acc = fmaf(__uint_as_float(q.w << 16), b.z, acc);
+                        acc = fmaf(__uint_as_float(q.w & 0xffff0000u), b.w, acc);
+                    }
+                }
+                if (k + 1 < nchunks) store_regs(tp, k + 1, x_s + ((k + 1) & 1u) * xbuf);
+                __syncthreads();
+            }
+            if (mine) write_logit(t0 + lane, acc);
+        }
+    }
+
+    // ---- arrival; the routing CTAs wait for every CTA's logits
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        const uint32_t prev = atomicAdd(ws.ticket, 1u);
-        is_last = (prev == gridDim.x - 1) ? 1u : 0u;
+        atomicAdd(&ws.ticket[0], 1u);
+    }
+    const uint32_t route_ctas = min(min(gridDim.x, kRtRouteCtas), (T + kRtRows - 1) / kRtRows);
+    auto drain = [&]() {  // after an expired wait, let this CTA's own copies land (bounded) before it exits
+        if (threadIdx.x == 0 && failed)
+            for (uint32_t k = 0; k < (SL.wf_bytes ? 1u : nchunks); ++k) mbar_wait_bounded(&bars[k], 0, kPipeWaitNs);
+    };
+    if (blockIdx.x >= route_ctas) {
+        drain();
+        return;
+    }
+    if (threadIdx.x == 0) {
+        const uint64_t t_start = global_ns();
+        while (ld_acquire_gpu(&ws.ticket[0]) < gridDim.x) {
+            if (global_ns() - t_start > kPipeWaitNs) {
+                latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
     }
     __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    // Every other CTA has exited: let the expert kernel be scheduled now, so
-    // its prologue (barrier setup, activation staging) runs under this CTA's
-    // routing and plan; it reads the plan only after griddepcontrol.wait,
-    // i.e. after this grid completes.
+    // every CTA of this grid has started: the expert kernel may be scheduled
+    // now and run its prologue under the routing; it reads the plan only after
+    // griddepcontrol.wait, i.e. after this grid completes
     pdl_launch_dependents();
-
     {
         const uint32_t Ep = (E + 3) & ~3u;
-        float* s = smem + warp * Ep;  // the x staging area is free now
-        for (uint32_t t = warp; t < T; t += blockDim.x / 32) {
+        float* s = reinterpret_cast<float*>(rt_smem) + warp * Ep;  // the staging area is free now
+        for (uint32_t t = blockIdx.x * kRtRows + warp; t < T; t += route_ctas * kRtRows) {
             stage_logits_warp(ws.logits + static_cast<size_t>(t) * E, E, s);
-            route_token_smem(s, E, K, normalization, routed_scale, ws.route_ids + static_cast<size_t>(t) * K,
-                             ws.route_w + static_cast<size_t>(t) * K, ws.status);
+            route_token(s, E, K, normalization, routed_scale, ws.route_ids + static_cast<size_t>(t) * K,
+                        ws.route_w + static_cast<size_t>(t) * K, ws.status);
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        cta_flag = (atomicAdd(&ws.ticket[1], 1u) == route_ctas - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!cta_flag) {
+        drain();
+        return;
+    }
+    __threadfence();
 
-    // group plan; shared memory reuses the activation staging area
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(smem);  // [E] counts -> starts
-    uint32_t* gidx = cnt + E;                           // [E] used flags -> group index
-    uint32_t* ids = gidx + E;                           // [T*K]
-    uint32_t* tmp = ids + T * K;                        // [32]
+    // group plan (the last routing CTA); shared memory reuses the staging area
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(rt_smem);  // [E] counts -> starts
+    uint32_t* gidx = cnt + E;                          // [E] used flags -> group index
+    uint32_t* run = gidx + E;                          // [E] routes of each expert placed so far
+    uint32_t* ids = run + E;                           // [T*K]
+    uint32_t* rnk = ids + T * K;                       // [T*K] rank of each route inside its group
+    uint32_t* tmp = rnk + T * K;                       // [32]
     const uint32_t R = T * K;
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = run[e] = 0;
     __syncthreads();
     // only the experts of this rank's range [e_lo, e_hi) form groups (all of
     // them on a single GPU); group_expert holds the slot index e - e_lo
@@ -200,13 +489,29 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     __syncthreads();
     const uint32_t U = block_exclusive_scan(gidx, E, tmp);
     const uint32_t RL = block_exclusive_scan(cnt, E, tmp);  // cnt[e] = start of expert e; RL local routes
+    // rank of each route among the earlier routes of its expert: warp 0 walks
+    // the routes 32 at a time; lanes with the same expert find each other with
+    // __match_any_sync and a per-expert running count carries across chunks
+    if (warp == 0) {
+        for (uint32_t r0 = 0; r0 < R; r0 += 32) {
+            const uint32_t r = r0 + lane;
+            const uint32_t e = r < R ? ids[r] : 0xffffffffu;
+            const uint32_t peers = __match_any_sync(kFull, e);
+            const uint32_t below = peers & ((1u << lane) - 1u);
+            if (r < R && e < E) {
+                rnk[r] = run[e] + __popc(below);
+                if ((peers >> lane) == 1u) run[e] += __popc(peers);  // the group's highest lane
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
     const uint32_t shared_groups = has_shared ? 1u : 0u;
     const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared group
     for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
         const uint32_t e = ids[r];
         if (e < e_lo || e >= e_hi) continue;
-        uint32_t rank = 0;
-        for (uint32_t q = 0; q < r; ++q) rank += (ids[q] == e) ? 1u : 0u;
+        const uint32_t rank = rnk[r];
         const uint32_t pos = routed_base + cnt[e] + rank;
         ws.group_routes[pos] = r;
         ws.group_tokens[pos] = r / K;
@@ -231,9 +536,11 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     }
     if (threadIdx.x == 0) {
         *ws.num_groups = U + shared_groups;
-        *ws.ticket = 0;  // ready for the next launch
+        ws.ticket[0] = 0;  // ready for the next launch
+        ws.ticket[1] = 0;
         if (ep_epoch) *ep_epoch += 1u;  // this layer's expert-parallel exchange epoch
     }
+    drain();
 }
 
 // ---------------------------------------------------------------- kernel 2
@@ -587,8 +894,8 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, uint32_t T, 
     const uint32_t Ep = (E + 3) & ~3u;
     float* s = rsm + warp * Ep;
     stage_logits_warp(logits + static_cast<size_t>(t) * E, E, s);
-    route_token_smem(s, E, K, normalization, routed_scale, ids + static_cast<size_t>(t) * K,
-                     w + static_cast<size_t>(t) * K, status);
+    route_token(s, E, K, normalization, routed_scale, ids + static_cast<size_t>(t) * K,
+                w + static_cast<size_t>(t) * K, status);
 }
 
 // ---------------------------------------------------------------- host side
@@ -608,17 +915,40 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
 }
 
 size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K) {
-    const size_t stage = static_cast<size_t>(kRouterTokPass) * H * sizeof(float);
-    const size_t plan = (2ull * E + static_cast<size_t>(T) * K + 32) * sizeof(uint32_t);
-    const size_t route = static_cast<size_t>(kRouterThreads / 32) * ((E + 3) & ~3u) * sizeof(float);
-    size_t m = stage > plan ? stage : plan;
-    return m > route ? m : route;
+    const size_t a = rt_smem_layout(T, H, E, K, true).total, b = rt_smem_layout(T, H, E, K, false).total;
+    return a > b ? a : b;
 }
 
 template <typename F>
 static cudaError_t set_smem(F* fn, size_t bytes) {
     return cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(bytes));
+}
+
+// CUDA-core gate/up kernel for layouts the tensor-core kernels do not take.
+template <typename XT>
+static cudaError_t moe_up_fallback_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl) {
+    cudaError_t err;
+    const uint32_t T = a.tokens, H = a.layout.hidden, I = a.layout.inter;
+    uint32_t E = a.num_experts;
+    MoeLayoutDev L = a.layout;
+    MoeWs ws = a.ws;
+    const uint8_t* experts = a.experts;
+    const uint8_t* shared = a.shared_slot;
+    const uint32_t chunks = H >> 5;
+    dim3 grid((I + kUpRowsPerCta - 1) / kUpRowsPerCta, gmax);
+    const XT* x = static_cast<const XT*>(a.x);
+    void* args[] = {(void*)&x, (void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
+    if (T == 1) {
+        const size_t smem = (1ull * H + 2ull * chunks) * sizeof(float);
+        auto fn = moe_expert_up_kernel<XT, 1>;
+        if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
+        return launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
+    }
+    const size_t smem = 4ull * (H + 2ull * chunks) * sizeof(float);
+    auto fn = moe_expert_up_kernel<XT, 4>;
+    if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
+    return launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
 }
 
 template <typename XT, typename OT>
@@ -638,9 +968,8 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     // 1. router + routing + plan
     {
         const uint32_t nrows = E + (has_gate ? 1u : 0u);
-        const uint32_t rows_per_cta = (kRouterThreads / 32) * kRouterRowsPerWarp;
-        dim3 grid((nrows + rows_per_cta - 1) / rows_per_cta);
-        const size_t smem = moe_router_smem(T, H, E, K);
+        dim3 grid((nrows + kRtRows - 1) / kRtRows);
+        const size_t smem = rt_smem_layout(T, H, E, K, sizeof(XT) == 2 || a.in_norm_w != nullptr).total;
         auto fn = moe_router_kernel<XT>;
         if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
         const XT* x = static_cast<const XT*>(a.x);
@@ -649,10 +978,12 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         const uint16_t* rw = a.router_w;
         const uint16_t* sg = a.shared_gate;
         uint32_t* ep_epoch = a.ep ? a.ep->epoch : nullptr;
-        void* args[] = {(void*)&x,  (void*)&T,          (void*)&H,    (void*)&E,    (void*)&K,
-                        (void*)&norm, (void*)&scale,    (void*)&rw,   (void*)&sg,   (void*)&has_shared,
-                        (void*)&e_lo, (void*)&e_hi,     (void*)&ep_epoch, (void*)&ws};
-        if ((err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRouterThreads), smem, s, args,
+        const float* inw = a.in_norm_w;
+        float ineps = a.in_eps;
+        void* args[] = {(void*)&x,    (void*)&T,     (void*)&H,  (void*)&E,  (void*)&K,
+                        (void*)&norm, (void*)&scale, (void*)&rw, (void*)&sg, (void*)&has_shared,
+                        (void*)&e_lo, (void*)&e_hi,  (void*)&ep_epoch, (void*)&inw, (void*)&ineps, (void*)&ws};
+        if ((err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRtThreads), smem, s, args,
                               a.pdl && pdl)) != cudaSuccess)
             return err;
     }
@@ -661,29 +992,22 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     MoeLayoutDev L = a.layout;
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
+    // the experts' input: x itself, or the router's normalised rows
+    MoeLaunch ex = a;
+    if (a.in_norm_w) {
+        ex.x = ws.xn;
+        ex.x_dtype = PBMOE_BF16;
+    }
     const bool mma = moe_mma_supported(a.layout);
-    const bool pipe = moe_pipe_supported(a);
+    const bool pipe = moe_pipe_supported(ex);
     // 2. gate/up/SwiGLU
     if (pipe) {
-        if ((err = moe_up_pipe_launch(a, s, pdl)) != cudaSuccess) return err;
+        if ((err = moe_up_pipe_launch(ex, s, pdl)) != cudaSuccess) return err;
     } else if (mma) {
-        if ((err = moe_up_mma_launch(a, gmax, s, pdl)) != cudaSuccess) return err;
+        if ((err = moe_up_mma_launch(ex, gmax, s, pdl)) != cudaSuccess) return err;
     } else {
-        const uint32_t chunks = H >> 5;
-        dim3 grid((I + kUpRowsPerCta - 1) / kUpRowsPerCta, gmax);
-        const XT* x = static_cast<const XT*>(a.x);
-        void* args[] = {(void*)&x, (void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws};
-        if (T == 1) {
-            const size_t smem = (1ull * H + 2ull * chunks) * sizeof(float);
-            auto fn = moe_expert_up_kernel<XT, 1>;
-            if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
-            err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
-        } else {
-            const size_t smem = 4ull * (H + 2ull * chunks) * sizeof(float);
-            auto fn = moe_expert_up_kernel<XT, 4>;
-            if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
-            err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
-        }
+        err = ex.x_dtype == PBMOE_BF16 ? moe_up_fallback_launch<uint16_t>(ex, gmax, s, pdl)
+                                       : moe_up_fallback_launch<float>(ex, gmax, s, pdl);
         if (err != cudaSuccess) return err;
     }
     if ((err = mark(2)) != cudaSuccess) return err;

@@ -189,7 +189,7 @@ template <typename XT, uint32_t H, uint32_t I>
 __global__ void __launch_bounds__(kUpThreads, UpCfg<XT>::kCtasPerSm)
 moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8_t* __restrict__ experts,
                    const uint8_t* __restrict__ shared_slot, MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g,
-                   uint32_t cap_r) {
+                   uint32_t cap_r, int x_from_router) {
     constexpr bool kLo = sizeof(XT) == 4;
     constexpr int S = UpCfg<XT>::kStages;
     constexpr UpStage SL = up_stage(H);
@@ -215,14 +215,20 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
         fence_mbar_init();
     }
     // The batch's tokens are the layer input, complete before the router
-    // started: stage them before waiting for the router.
-    if (warp < kWarps) {
-        if constexpr (kLo)
-            stage_act_mma<XT>(x, H, nullptr, static_cast<int>(T), H, tile, kBarStage, kComputeThreads);
-        else
-            stage_act_rows8_tok<XT>(x, H, static_cast<int>(T), H, tile, kBarStage, kComputeThreads);
-    }
+    // started: stage them before waiting for the router, unless the router
+    // writes them (the normalised input, x_from_router), in which case they
+    // are read only after the wait.
+    auto stage_tokens = [&]() {
+        if (warp < kWarps) {
+            if constexpr (kLo)
+                stage_act_mma<XT>(x, H, nullptr, static_cast<int>(T), H, tile, kBarStage, kComputeThreads);
+            else
+                stage_act_rows8_tok<XT>(x, H, static_cast<int>(T), H, tile, kBarStage, kComputeThreads);
+        }
+    };
+    if (!x_from_router) stage_tokens();
     pdl_wait();
+    if (x_from_router) stage_tokens();
     const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
     uint32_t k0, k1;
     item_run(ng * kTiles, k0, k1);
@@ -631,18 +637,19 @@ cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     plan_caps(a, cg, cr);
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
+    int from_router = a.in_norm_w != nullptr;
     if (a.x_dtype == PBMOE_BF16) {
         const dim3 grid(device_sm_count() * UpCfg<uint16_t>::kCtasPerSm);
         const uint16_t* x = static_cast<const uint16_t*>(a.x);
         void* args[] = {(void*)&x,       (void*)&T,  (void*)&E,  (void*)&experts, (void*)&shared,
-                        (void*)&L,       (void*)&ws, (void*)&cg, (void*)&cr};
+                        (void*)&L,       (void*)&ws, (void*)&cg, (void*)&cr, (void*)&from_router};
         return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<uint16_t, kPipeH, kPipeI>), grid,
                            kUpThreads, up_pipe_smem(L.hidden, false, cg, cr), s, args, pdl);
     }
     const float* x = static_cast<const float*>(a.x);
     const dim3 grid(device_sm_count() * UpCfg<float>::kCtasPerSm);
     void* args[] = {(void*)&x, (void*)&T, (void*)&E, (void*)&experts, (void*)&shared,
-                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr};
+                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr, (void*)&from_router};
     return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<float, kPipeH, kPipeI>), grid, kUpThreads,
                        up_pipe_smem(L.hidden, true, cg, cr), s, args, pdl);
 }

@@ -88,22 +88,11 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
         return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT, "moe layer (static): null pointer");
     const pbmoe_expert_layout& L = c->layout;
     const uint32_t H = L.hidden, I = L.intermediate, G = L.group_size, E = c->num_experts, K = c->top_k;
-    if (H == 0 || I == 0 || G == 0 || H % G || I % G)
-        return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT,
-                      "fixed-Q4 expert dimensions hidden=%u intermediate=%u must be divisible by group_size=%u", H,
-                      I, G);
-    if (G < 32 || (G & (G - 1)) || H % 32 || I % 32 || H > 16384 || I > 16384 || L.expert_bytes % 16)
-        return report(error_buf, error_len, PBMOE_ERR_UNSUPPORTED,
-                      "FlashMoe unsupported expert geometry on CUDA (hidden=%u intermediate=%u group=%u)", H, I, G);
-    for (int i = 0; i < 9; ++i)
-        if (L.component_offsets[i] % ((i % 3 == 0) ? 16 : 2) || L.component_offsets[i] >= L.expert_bytes)
-            return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT,
-                          "expert component %d offset is misaligned or outside the slot", i);
-    if (E == 0 || E > 4096 || K == 0 || K > 32 || K > E)
-        return report(error_buf, error_len, PBMOE_ERR_UNSUPPORTED, "experts=%u top_k=%u not supported", E, K);
-    if (c->normalization > PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR || !(c->routed_scaling_factor > 0.f) ||
-        !std::isfinite(c->routed_scaling_factor))
-        return report(error_buf, error_len, PBMOE_ERR_UNSUPPORTED, "routing normalisation/scale not supported");
+    {  // the same layout and config checks as pbmoe_moe_layer
+        char msg[512];
+        const int rc = moe_check_config(c, msg, sizeof msg);
+        if (rc != PBMOE_OK) return report(error_buf, error_len, rc, "%s", msg);
+    }
     if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (out_dtype != PBMOE_F32 && out_dtype != PBMOE_BF16))
         return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
     if ((next_norm_weight == nullptr) != (next_normed == nullptr) || (w->shared_expert_gate && !w->shared_expert))
@@ -111,7 +100,8 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w->experts) % 16 ||
         reinterpret_cast<uintptr_t>(w->router_weight) % 16 ||
         (w->shared_expert && reinterpret_cast<uintptr_t>(w->shared_expert) % 16) ||
-        (w->shared_expert_gate && reinterpret_cast<uintptr_t>(w->shared_expert_gate) % 16))
+        (w->shared_expert_gate && reinterpret_cast<uintptr_t>(w->shared_expert_gate) % 16) ||
+        (w->input_norm_weight && reinterpret_cast<uintptr_t>(w->input_norm_weight) % 16))
         return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT,
                       "moe layer (static): x, experts, router and shared weights must be 16-byte aligned");
     if (tokens == 0) return PBMOE_OK;
@@ -140,7 +130,7 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
     a.ws = moe_ws_carve(static_cast<char*>(base) + kStatusBytes, status, tokens, E, K, H, I);
     // state that must start at zero: the router's arrival counter (and the
     // status word when it lives in the array)
-    e = cudaMemsetAsync(a.ws.ticket, 0, sizeof(uint32_t), s);
+    e = cudaMemsetAsync(a.ws.ticket, 0, 2 * sizeof(uint32_t), s);
     if (e == cudaSuccess && !device_status) e = cudaMemsetAsync(base, 0, sizeof(uint32_t), s);
     if (e != cudaSuccess)
         return report(error_buf, error_len, PBMOE_ERR_CUDA, "scratch clear failed: %s", cudaGetErrorString(e));
@@ -168,6 +158,8 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
     a.shared_gate = w->shared_expert_gate;
     a.experts = w->experts;
     a.shared_slot = w->shared_expert;
+    a.in_norm_w = w->input_norm_weight;
+    a.in_eps = c->norm_epsilon;
     a.pdl = false;  // the memset above must complete before the router kernel reads the counter
     a.phase_events = nullptr;
     e = moe_layer_launch(a, s);

@@ -64,6 +64,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+// Contiguous copy global -> shared through the TMA unit (both addresses 16-byte
+// aligned, size a multiple of 16), completing as transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // 16-byte asynchronous copy global -> shared through L2 (no L1 allocation).
 // Unlike a bulk copy, each is a plain LSU request, so thousands of small
 // row pieces per stage cost no per-copy TMA setup, and the destination may

@@ -39,29 +39,61 @@ static cudaError_t launch_with_pdl(const void* fn, dim3 grid, dim3 block, size_t
 constexpr int kMvThreads = 128;
 constexpr int kMvRows = 4;  // rows per lane group per pass
 
+// One matrix of a launch: weights, output and row count. A launch covers one
+// or two matrices on the same x (the second one's CTAs follow the first's),
+// e.g. the MLA chain's q_a and kv_a projections, which read the same normed
+// hidden state (execute_glm_mla_input_projection_chain,
+// metal/qwen_execution.rs:289-480).
+struct MvMat {
+    const uint8_t* packed;
+    const uint16_t* scales;
+    const uint16_t* biases;
+    void* y;
+    uint32_t rows;
+};
+
+// Optional fusions: the input RMSNorm (norm_w, eps) and a residual added to y.
+struct MvFuse {
+    const float* norm_w;
+    float eps;
+    const void* residual;
+};
+
+template <typename YT>
+__device__ __forceinline__ void store_y(const MvFuse& fz, YT* y, size_t i, float v) {
+    if (fz.residual) v += load_act<YT>(static_cast<const YT*>(fz.residual), i);
+    store_act<YT>(y, i, v);
+}
+
 template <typename XT, typename YT, int LPR, int CPL, int NT>
 __global__ void __launch_bounds__(kMvThreads, 3)
-q4_matvec_fast_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
-                      const uint16_t* __restrict__ biases, Q4Geom g, const XT* __restrict__ x,
-                      YT* __restrict__ y, uint32_t batch) {
+q4_matvec_fast_kernel(MvMat m0, MvMat m1, uint32_t grid0, Q4Geom g0, const XT* __restrict__ x, uint32_t batch,
+                      MvFuse fz) {
     extern __shared__ __align__(16) float smem[];
+    __shared__ float nscale[NT];
     constexpr int kGroups = 32 / LPR;
     constexpr int kRowsPerCta = kMvRows * kGroups * (kMvThreads / 32);
+    const bool second = blockIdx.x >= grid0;
+    const MvMat m = second ? m1 : m0;
+    const uint32_t bx = second ? blockIdx.x - grid0 : blockIdx.x;
+    Q4Geom g = g0;
+    g.rows = m.rows;
+    YT* y = static_cast<YT*>(m.y);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sub = lane / LPR;
     float* xs = smem;
     float* xe = xs + NT * g.cols;
     float* xo = xe + NT * g.chunks;
-    const uint32_t r0 = blockIdx.x * kRowsPerCta + (warp * kGroups + sub) * kMvRows;
+    const uint32_t r0 = bx * kRowsPerCta + (warp * kGroups + sub) * kMvRows;
     const uint8_t* pk[kMvRows];
     const uint16_t* ps[kMvRows];
     const uint16_t* pb[kMvRows];
 #pragma unroll
     for (int r = 0; r < kMvRows; ++r) {
         const uint32_t row = r0 + r;
-        pk[r] = row < g.rows ? packed + static_cast<size_t>(row) * (g.cols / 2) : nullptr;
-        ps[r] = scales + static_cast<size_t>(row) * g.gpr;
-        pb[r] = biases + static_cast<size_t>(row) * g.gpr;
+        pk[r] = row < g.rows ? m.packed + static_cast<size_t>(row) * (g.cols / 2) : nullptr;
+        ps[r] = m.scales + static_cast<size_t>(row) * g.gpr;
+        pb[r] = m.biases + static_cast<size_t>(row) * g.gpr;
     }
     Q4RowFrag<LPR, kMvRows, CPL> frag;
     for (uint32_t b0 = 0; b0 < batch; b0 += NT) {
@@ -72,7 +104,8 @@ q4_matvec_fast_kernel(const uint8_t* __restrict__ packed, const uint16_t* __rest
             pdl_wait();
         }
         __syncthreads();
-        stage_x_fast<XT>(x + static_cast<size_t>(b0) * g.cols, g.cols, nullptr, nt, g.cols, xs, xe, xo);
+        stage_x_fast<XT>(x + static_cast<size_t>(b0) * g.cols, g.cols, nullptr, nt, g.cols, xs, xe, xo, fz.norm_w,
+                         fz.eps, nscale);
         float acc[kMvRows][NT];
         q4_rows_finish<LPR, kMvRows, CPL, NT>(frag, pk, ps, pb, g, xs, xe, xo, nt, acc);
 #pragma unroll
@@ -81,7 +114,7 @@ q4_matvec_fast_kernel(const uint8_t* __restrict__ packed, const uint16_t* __rest
             for (int t = 0; t < NT; ++t) {
                 const float s = group_sum<LPR>(acc[r][t]);
                 if ((lane & (LPR - 1)) == 0 && t < nt && r0 + r < g.rows)
-                    store_act<YT>(y, static_cast<size_t>(b0 + t) * g.rows + r0 + r, s);
+                    store_y<YT>(fz, y, static_cast<size_t>(b0 + t) * g.rows + r0 + r, s);
             }
         }
     }
@@ -114,17 +147,23 @@ q4_matvec_generic_kernel(const uint8_t* __restrict__ packed, const uint16_t* __r
 // Tensor-core matvec for group-64 weights (q4_mma.cuh): CTA = 8 warps =
 // (8/KS) tiles of 8 rows x KS K-slices; slices are summed in shared memory.
 // kTok16: bf16 activations, up to 16 tokens per pass; f32 activations use
-// hi/lo rows (8 tokens per pass).
+// hi/lo rows (8 tokens per pass). With fz.norm_w (f32 activations) the CTA
+// computes each token's 1/rms from x first and stages the normalised rows.
 template <typename XT, typename YT, int KS, bool kTok16>
 __global__ void __launch_bounds__(256, 2)
-q4_matvec_mma_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
-                     const uint16_t* __restrict__ biases, uint32_t rows, uint32_t cols, const XT* __restrict__ x,
-                     YT* __restrict__ y, uint32_t batch) {
+q4_matvec_mma_kernel(MvMat m0, MvMat m1, uint32_t grid0, uint32_t cols, const XT* __restrict__ x, uint32_t batch,
+                     MvFuse fz) {
     constexpr bool kLo = sizeof(XT) == 4;
     constexpr bool kRows16 = kLo || kTok16;
     constexpr int kPass = kTok16 ? 16 : 8;
     constexpr int kTiles = 8 / KS;
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ float nscale[kPass];
+    const bool second = blockIdx.x >= grid0;
+    const MvMat m = second ? m1 : m0;
+    const uint32_t bx = second ? blockIdx.x - grid0 : blockIdx.x;
+    const uint32_t rows = m.rows;
+    YT* y = static_cast<YT*>(m.y);
     const uint32_t trows = kRows16 ? 16 : 8;
     const ActTile tile = act_tile_at(smem_raw, cols, trows);
     float* red = reinterpret_cast<float*>(smem_raw + act_tile_bytes(cols, trows));
@@ -133,16 +172,16 @@ q4_matvec_mma_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restr
     const int tl = warp / KS, ks = warp % KS;
     const uint32_t gpr = cols / kMmaGroup;
     const uint32_t gps = gpr / KS;
-    const uint32_t r0 = blockIdx.x * (8 * kTiles) + tl * 8;
+    const uint32_t r0 = bx * (8 * kTiles) + tl * 8;
     // rows past the end read the last row and are never stored
     const uint32_t rg = min(r0 + g, rows - 1), ra = min(r0 + 2 * t, rows - 1), rb = min(r0 + 2 * t + 1, rows - 1);
-    const uint8_t* wrow = packed + static_cast<size_t>(rg) * (cols / 2);
+    const uint8_t* wrow = m.packed + static_cast<size_t>(rg) * (cols / 2);
     const uint32_t grp0 = ks * gps;
     Q4MmaFrag4 f;
     // scale rows ra and rb = ra + 1 unless clamped; load them through the
     // (row 2t, row 2t+1) pair when both exist, else clamp both to ra
-    const uint16_t* sa = scales + static_cast<size_t>(ra) * gpr;
-    const uint16_t* ba = biases + static_cast<size_t>(ra) * gpr;
+    const uint16_t* sa = m.scales + static_cast<size_t>(ra) * gpr;
+    const uint16_t* ba = m.biases + static_cast<size_t>(ra) * gpr;
     const uint32_t pair_gpr = (rb == ra + 1) ? gpr : 0;
     f.load(wrow, sa, ba, pair_gpr, grp0, t);
     pdl_launch_dependents();
@@ -150,8 +189,24 @@ q4_matvec_mma_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restr
     for (uint32_t b0 = 0; b0 < batch; b0 += kPass) {
         const int nt = static_cast<int>(min(batch - b0, static_cast<uint32_t>(kPass)));
         __syncthreads();
+        if constexpr (kLo) {
+            if (fz.norm_w) {  // 1/rms of each token of the pass, one warp per token
+                for (int tok = warp; tok < nt; tok += 8) {
+                    const float* xr = reinterpret_cast<const float*>(x) + static_cast<size_t>(b0 + tok) * cols;
+                    float ss = 0.f;
+                    for (uint32_t i = lane * 4; i < cols; i += 128) {
+                        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    }
+                    ss = warp_sum(ss);
+                    if (lane == 0) nscale[tok] = 1.0f / sqrtf(ss / static_cast<float>(cols) + fz.eps);
+                }
+                __syncthreads();
+            }
+        }
         if constexpr (kRows16)
-            stage_act_mma<XT>(x + static_cast<size_t>(b0) * cols, cols, nullptr, nt, cols, tile);
+            stage_act_mma<XT>(x + static_cast<size_t>(b0) * cols, cols, nullptr, nt, cols, tile, 0, 0, fz.norm_w,
+                              nscale);
         else
             stage_act_rows8_tok<XT>(x + static_cast<size_t>(b0) * cols, cols, nt, cols, tile);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -170,15 +225,20 @@ q4_matvec_mma_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restr
         __syncthreads();
         for (uint32_t i = threadIdx.x; i < kTiles * 16 * 8; i += blockDim.x) {
             const uint32_t tile_i = i / 128, tok = (i / 8) % 16, r = i % 8;
-            const uint32_t row = blockIdx.x * (8 * kTiles) + tile_i * 8 + r;
+            const uint32_t row = bx * (8 * kTiles) + tile_i * 8 + r;
             if (tok < static_cast<uint32_t>(nt) && row < rows) {
                 float sum = 0.f;
 #pragma unroll
                 for (int k = 0; k < KS; ++k) sum += red[(tile_i * KS + k) * 128 + tok * 8 + r];
-                store_act<YT>(y, static_cast<size_t>(b0 + tok) * rows + row, sum);
+                store_y<YT>(fz, y, static_cast<size_t>(b0 + tok) * rows + row, sum);
             }
         }
     }
+}
+
+static void mats_of(const Q4MatvecArgs& a, MvMat& m0, MvMat& m1) {
+    m0 = MvMat{a.packed, a.scales, a.biases, a.y, a.rows};
+    m1 = a.packed2 ? MvMat{a.packed2, a.scales2, a.biases2, a.y2, a.rows2} : m0;
 }
 
 template <typename XT, typename YT, int KS>
@@ -193,15 +253,16 @@ static cudaError_t launch_mma_ks(const Q4MatvecArgs& a, cudaStream_t s) {
                            : reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, false>);
     cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    const dim3 grid((a.rows + 8 * kTiles - 1) / (8 * kTiles));
-    const uint8_t* p = a.packed;
-    const uint16_t* sc = a.scales;
-    const uint16_t* bi = a.biases;
-    uint32_t rows = a.rows, cols = a.cols, batch = a.batch;
+    const uint32_t per_cta = 8 * kTiles;
+    uint32_t grid0 = (a.rows + per_cta - 1) / per_cta;
+    const uint32_t grid1 = a.packed2 ? (a.rows2 + per_cta - 1) / per_cta : 0;
+    MvMat m0, m1;
+    mats_of(a, m0, m1);
+    MvFuse fz{a.norm_w, a.eps, a.residual};
+    uint32_t cols = a.cols, batch = a.batch;
     const XT* x = static_cast<const XT*>(a.x);
-    YT* y = static_cast<YT*>(a.y);
-    void* args[] = {(void*)&p, (void*)&sc, (void*)&bi, (void*)&rows, (void*)&cols, (void*)&x, (void*)&y, (void*)&batch};
-    return launch_with_pdl(fn, grid, dim3(256), smem, s, args);
+    void* args[] = {(void*)&m0, (void*)&m1, (void*)&grid0, (void*)&cols, (void*)&x, (void*)&batch, (void*)&fz};
+    return launch_with_pdl(fn, dim3(grid0 + grid1), dim3(256), smem, s, args);
 }
 
 // Group-64 weights whose row length is a multiple of 256 columns.
@@ -223,32 +284,38 @@ static cudaError_t launch_fast(const Q4MatvecArgs& a, const Q4Geom& g, cudaStrea
     cudaError_t err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    const dim3 grid((g.rows + kRowsPerCta - 1) / kRowsPerCta);
-    const uint8_t* p = a.packed;
-    const uint16_t* sc = a.scales;
-    const uint16_t* bi = a.biases;
+    uint32_t grid0 = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
+    const uint32_t grid1 = a.packed2 ? (a.rows2 + kRowsPerCta - 1) / kRowsPerCta : 0;
+    MvMat m0, m1;
+    mats_of(a, m0, m1);
+    MvFuse fz{a.norm_w, a.eps, a.residual};
     Q4Geom gg = g;
     const XT* x = static_cast<const XT*>(a.x);
-    YT* y = static_cast<YT*>(a.y);
     uint32_t batch = a.batch;
-    void* args[] = {(void*)&p, (void*)&sc, (void*)&bi, (void*)&gg, (void*)&x, (void*)&y, (void*)&batch};
-    return launch_with_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kMvThreads), smem, s, args);
+    void* args[] = {(void*)&m0, (void*)&m1, (void*)&grid0, (void*)&gg, (void*)&x, (void*)&batch, (void*)&fz};
+    return launch_with_pdl(reinterpret_cast<const void*>(fn), dim3(grid0 + grid1), dim3(kMvThreads), smem, s, args);
+}
+
+static bool weights_aligned(const uint8_t* p, const uint16_t* sc, const uint16_t* bi) {
+    return reinterpret_cast<uintptr_t>(p) % 16 == 0 && reinterpret_cast<uintptr_t>(sc) % 8 == 0 &&
+           reinterpret_cast<uintptr_t>(bi) % 8 == 0;
 }
 
 template <typename XT, typename YT>
 static cudaError_t q4_matvec_launch_t(const Q4MatvecArgs& a, cudaStream_t s) {
     constexpr size_t kSmemLimit = 200 * 1024;
     const size_t xelem = a.x_dtype == PBMOE_BF16 ? 2 : 4;
+    const bool fused = a.norm_w || a.residual || a.packed2;
+    const bool aligned2 = !a.packed2 || weights_aligned(a.packed2, a.scales2, a.biases2);
     // one or two tokens: the CUDA-core kernel (more weight bytes in flight per
     // warp, one wave of CTAs); larger batches: the tensor-core kernel
-    if (a.batch > 2 && a.group == kMmaGroup && a.cols % 256 == 0 && reinterpret_cast<uintptr_t>(a.packed) % 16 == 0 &&
-        reinterpret_cast<uintptr_t>(a.scales) % 8 == 0 && reinterpret_cast<uintptr_t>(a.biases) % 8 == 0 &&
-        reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
+    if (a.batch > 2 && a.group == kMmaGroup && a.cols % 256 == 0 && weights_aligned(a.packed, a.scales, a.biases) &&
+        aligned2 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
         cudaError_t e = launch_mma<XT, YT>(a, s);
         if (e != cudaErrorNotSupported) return e;
     }
-    if (q4_fast_ok(a.cols, a.group, a.packed) && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
-        (a.cols * xelem) % 16 == 0) {
+    if (q4_fast_ok(a.cols, a.group, a.packed) && (!a.packed2 || q4_fast_ok(a.cols, a.group, a.packed2)) &&
+        reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && (a.cols * xelem) % 16 == 0) {
         Q4Geom g{a.rows, a.cols, (a.cols + a.group - 1) / a.group, a.cols / 32, ilog2_u32(a.group / 32)};
         const size_t per_tok = (g.cols + 2ull * g.chunks) * sizeof(float);
         const bool multi = a.batch > 1 && 4 * per_tok <= kSmemLimit;
@@ -262,6 +329,7 @@ static cudaError_t q4_matvec_launch_t(const Q4MatvecArgs& a, cudaStream_t s) {
             }
         }
     }
+    if (fused) return cudaErrorNotSupported;  // the per-element kernel has no fused forms
     const size_t smem = static_cast<size_t>(a.cols) * sizeof(float);
     if (smem > kSmemLimit) return cudaErrorNotSupported;
     auto fn = q4_matvec_generic_kernel<XT, YT>;

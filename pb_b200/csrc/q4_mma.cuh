@@ -108,9 +108,14 @@ __device__ __forceinline__ void tile_sync(int bar_id, uint32_t nthreads) {
 // source row (NULL = identity). All global loads of a thread are issued before
 // its shared stores. Run by threads 0..nthreads-1 (the whole CTA when
 // nthreads == 0) and ends with their barrier (tile_sync).
+//
+// f32 rows may be normalised on the way in: with norm_w, activation c of token
+// t is staged as x * nscale[t] * norm_w[c] (nscale: the tokens' 1/rms, in
+// shared memory, computed by the caller).
 template <typename XT>
 __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx, int ntok,
-                              uint32_t K, const ActTile& tile, int bar_id = 0, uint32_t nthreads = 0) {
+                              uint32_t K, const ActTile& tile, int bar_id = 0, uint32_t nthreads = 0,
+                              const float* __restrict__ norm_w = nullptr, const float* nscale = nullptr) {
     constexpr bool kLo = sizeof(XT) == 4;
     const uint32_t nthr = nthreads ? nthreads : blockDim.x;
     const uint32_t slots = K / 8;
@@ -163,6 +168,14 @@ __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const u
                     float f[8] = {__uint_as_float(v[i][0].x), __uint_as_float(v[i][0].y), __uint_as_float(v[i][0].z),
                                   __uint_as_float(v[i][0].w), __uint_as_float(v[i][1].x), __uint_as_float(v[i][1].y),
                                   __uint_as_float(v[i][1].z), __uint_as_float(v[i][1].w)};
+                    if (norm_w) {
+                        const float sc = nscale[t];
+                        const float4 n0 = *reinterpret_cast<const float4*>(norm_w + static_cast<size_t>(w) * 8);
+                        const float4 n1 = *reinterpret_cast<const float4*>(norm_w + static_cast<size_t>(w) * 8 + 4);
+                        const float nn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) f[q] = f[q] * sc * nn[q];
+                    }
                     uint32_t hi[4], lo[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {

@@ -40,9 +40,14 @@ __host__ __device__ inline uint32_t ilog2_u32(uint32_t v) {
 // Phase 1 issues every 16-byte load of the thread before storing any of them
 // (one memory round trip for the whole staging); phase 2 forms the chunk sums
 // from shared memory. Ends with __syncthreads.
+//
+// With norm_w, each staged row is replaced by its RMSNorm times norm_w
+// (x * (1 / sqrt(mean(x^2) + eps)) * w, rms_norm_reduced, shaders.metal:
+// 1176-1213) before the chunk sums; `nscale` is shared memory for ntok floats.
 template <typename XT>
 __device__ void stage_x_fast(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx,
-                             int ntok, uint32_t cols, float* xs, float* xe, float* xo) {
+                             int ntok, uint32_t cols, float* xs, float* xe, float* xo,
+                             const float* __restrict__ norm_w = nullptr, float eps = 0.f, float* nscale = nullptr) {
     constexpr uint32_t kPerVec = 16 / sizeof(XT);  // elements per 16-byte vector
     constexpr int kBatch = 8;                       // vectors in flight per thread
     const uint32_t chunks = cols >> 5;
@@ -85,6 +90,27 @@ __device__ void stage_x_fast(const XT* __restrict__ x, size_t x_stride, const ui
         }
     }
     __syncthreads();
+    if (norm_w) {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+        for (int t = warp; t < ntok; t += nw) {
+            const float* row = xs + static_cast<size_t>(t) * cols;
+            float ss = 0.f;
+            for (uint32_t i = lane * 4; i < cols; i += 128) {
+                const float4 v = *reinterpret_cast<const float4*>(row + i);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) nscale[t] = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+        }
+        __syncthreads();
+        const uint32_t n = static_cast<uint32_t>(ntok) * cols;
+        for (uint32_t p = threadIdx.x; p < n; p += blockDim.x) {
+            const uint32_t t = p / cols, q = p - t * cols, j = q >> 5, pp = q & 31u;
+            const uint32_t c = ((((pp >> 2) ^ (j & 7u)) << 2) | (pp & 3u));  // logical column of slot pp
+            xs[p] = xs[p] * nscale[t] * norm_w[(j << 5) + c];
+        }
+        __syncthreads();
+    }
     const uint32_t nsum = static_cast<uint32_t>(ntok) * chunks;
     for (uint32_t i = threadIdx.x; i < nsum; i += blockDim.x) {
         const uint32_t t = i / chunks, j = i - t * chunks;

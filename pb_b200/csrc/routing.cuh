@@ -190,6 +190,127 @@ __device__ inline void route_token_smem(const float* s, uint32_t E, uint32_t K, 
     route_weights_lanes(sval, sid, m, sum, K, normalization, routed_scale, ids_out, w_out, status);
 }
 
+// route_token_smem with the K slots replicated in registers of every lane.
+// The selection is the same replay of routing_top_k_iter (math.rs:746-765):
+// experts in index order, 32 at a time; lanes whose score beats the current
+// minimum are candidates, replayed in ascending order; an admitted expert
+// replaces the first minimum slot. Here every lane holds all KMAX slots
+// (slots >= K hold +inf and are never a minimum, since real slots come first
+// and ties go to the lower slot), so an admission is a register select and a
+// min tree over the slots instead of warp-wide reductions; after each
+// admission one ballot drops the chunk's candidates that no longer beat the
+// minimum. When the first K scores are all finite and above -inf, the replay
+// would put expert k into slot k for k < K (each fills the first -inf slot),
+// so those slots are filled directly. The chunk loop stays rolled (the
+// admission code is emitted once).
+template <int KMAX>
+__device__ __noinline__ void route_token_regs(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
+                                              float routed_scale, uint32_t* ids_out, float* w_out,
+                                              uint32_t* status) {
+    const int lane = threadIdx.x & 31;
+    const float NEG_INF = -__int_as_float(0x7f800000), POS_INF = __int_as_float(0x7f800000);
+    float m = NEG_INF;
+    for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, s[e]);
+    m = warp_max(m);
+    float sum = 0.f;
+    for (uint32_t e = lane; e < E; e += 32) sum += expf(s[e] - m);
+    sum = warp_sum(sum);
+
+    float sval[KMAX];
+    uint32_t sid[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        sval[k] = static_cast<uint32_t>(k) < K ? NEG_INF : POS_INF;
+        sid[k] = 0;
+    }
+    float mv = NEG_INF;  // current minimum value and its (first) slot, one-hot
+    uint32_t mslot = 1u;
+    auto new_min = [&]() {
+        // minimum over the slots, the lowest slot among equals: pairs (a, b)
+        // with every index of a below b's keep a unless b is strictly smaller
+        float tv[KMAX];
+        uint32_t ti[KMAX];
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+            tv[k] = sval[k];
+            ti[k] = 1u << k;
+        }
+#pragma unroll
+        for (int w = 1; w < KMAX; w *= 2) {
+#pragma unroll
+            for (int k = 0; k + w < KMAX; k += 2 * w) {
+                const bool b = tv[k + w] < tv[k];
+                tv[k] = b ? tv[k + w] : tv[k];
+                ti[k] = b ? ti[k + w] : ti[k];
+            }
+        }
+        mv = tv[0];
+        mslot = ti[0];  // one-hot: the slot an admission replaces
+    };
+    uint32_t start = 0;
+    {  // the first K experts straight into slots 0..K-1 when all of them are admitted in turn
+        const float f = static_cast<uint32_t>(lane) < K ? s[lane] : 0.f;
+        if (__all_sync(kFull, static_cast<uint32_t>(lane) >= K || f > NEG_INF)) {
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k) {
+                const float fk = __shfl_sync(kFull, f, k);
+                if (static_cast<uint32_t>(k) < K) {
+                    sval[k] = fk;
+                    sid[k] = static_cast<uint32_t>(k);
+                }
+            }
+            new_min();
+            start = K;
+        }
+    }
+    for (uint32_t base = start & ~31u; base < E; base += 32) {
+        const uint32_t e = base + lane;
+        const float vc = (e < E && e >= start) ? s[e] : NEG_INF;
+        uint32_t cand = __ballot_sync(kFull, vc > mv);
+        while (cand) {
+            const int src = __ffs(cand) - 1;
+            const float ve = __shfl_sync(kFull, vc, src);
+            // admit (ve > mv holds: stale candidates were dropped below)
+            const uint32_t e_new = base + static_cast<uint32_t>(src);
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k) {
+                const bool hit = (mslot >> k) & 1u;
+                sval[k] = hit ? ve : sval[k];
+                sid[k] = hit ? e_new : sid[k];
+            }
+            new_min();
+            cand &= __ballot_sync(kFull, vc > mv) & ~((2u << src) - 1u);
+        }
+    }
+    // lane k takes slot k
+    float my_val = NEG_INF;
+    uint32_t my_id = 0;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+        if (k == lane) {
+            my_val = sval[k];
+            my_id = sid[k];
+        }
+    route_weights_lanes(my_val, my_id, m, sum, K, normalization, routed_scale, ids_out, w_out, status);
+}
+
+// One warp routes one token whose logits are in shared memory `s` (K <= 32).
+__device__ inline void route_token(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
+                                   float routed_scale, uint32_t* ids_out, float* w_out, uint32_t* status) {
+    // slot counts instantiated: the smallest that holds K (10 is the
+    // 512-expert top-10 configuration's)
+    if (K <= 4)
+        route_token_regs<4>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+    else if (K <= 8)
+        route_token_regs<8>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+    else if (K <= 10)
+        route_token_regs<10>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+    else if (K <= 16)
+        route_token_regs<16>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+    else
+        route_token_regs<32>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+}
+
 // Block-wide exclusive scan of n <= 4096 u32 values in shared memory, in
 // place; returns the total. Uses `tmp` (>= 32 words of shared memory).
 __device__ inline uint32_t block_exclusive_scan(uint32_t* a, uint32_t n, uint32_t* tmp) {

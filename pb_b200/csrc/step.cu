@@ -122,8 +122,22 @@ __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppen
         krow[p] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)));
         krow[half + p] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(x1, t.x), __fmul_rn(x0, t.y)));
     }
+    // latent row, normalised here when the norm is fused (rms_norm_rows_kernel's formula)
+    float scale = 1.0f;
+    if (a.latent_norm_w) {
+        __shared__ float red[kRopeThreads / 32];
+        float ss = 0.f;
+        for (uint32_t i = threadIdx.x; i < a.latent; i += blockDim.x) ss += kv[i] * kv[i];
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int w = 0; w < kRopeThreads / 32; ++w) tot += red[w];
+        scale = 1.0f / sqrtf(tot / static_cast<float>(a.latent) + a.eps);
+    }
     uint16_t* crow = a.c_kv[b] + static_cast<size_t>(pos) * a.latent;
-    for (uint32_t i = threadIdx.x; i < a.latent; i += blockDim.x) crow[i] = f32_to_bf16_bits(kv[i]);
+    for (uint32_t i = threadIdx.x; i < a.latent; i += blockDim.x)
+        crow[i] = f32_to_bf16_bits(a.latent_norm_w ? kv[i] * scale * a.latent_norm_w[i] : kv[i]);
 }
 
 bool rope_append_supported(uint32_t heads, uint32_t rope) {

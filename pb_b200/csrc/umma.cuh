@@ -161,13 +161,5 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int32_t
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
         : "memory");
 }
-// Contiguous copy global -> shared through the TMA unit (both addresses 16-byte
-// aligned, size a multiple of 16), completing as transaction bytes on `bar`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
 
 }  // namespace pbmoe

@@ -1,18 +1,21 @@
-"""One decode step of a synthetic MLA + MoE model, composed
-from the C-ABI entry points. Python only enqueues; every operation is a CUDA
-kernel behind pbmoe_*; `DecodeStep.launch` is what a CUDA graph captures.
+"""Harness of one decode step of a synthetic MLA + MoE model (BASELINE config
+4), standing in for the reference runtime's Rust layer loop
+(forward_token_input, runtime/mod.rs:1432-2024), which stays in the
+reference: this module allocates the step's buffers with torch and enqueues the
+C-ABI calls a Rust host would make per layer, so the benchmark and the tests
+can run the whole step. Python only enqueues; every operation is a CUDA kernel
+behind pbmoe_*; `DecodeStep.launch` is what a CUDA graph captures.
 
-Per layer, following forward_token_input (runtime/mod.rs:1432-2024) with the
-GLM MLA attention of mla_attention_output_values (runtime/mod.rs:2779-2940):
+Per layer, with the GLM MLA attention of mla_attention_output_values
+(runtime/mod.rs:2779-2940):
 
-  q_a  = Q4(q_a_proj) xn          kv = Q4(kv_a_proj_with_mqa) xn      pbmoe_q4_matvec
-  q_a  = rms_norm(q_a) w_qa       kv[:latent] = rms_norm(kv[:latent]) pbmoe_rms_norm
-  q    = Q4(q_b_proj) q_a                                             pbmoe_q4_matvec
-  RoPE on q's and kv's rope parts; latent + key rows into the cache   pbmoe_mla_rope_append
-  attn = absorbed MLA attention over the cache                        pbmoe_mla_decode
-  o    = Q4(o_proj) attn                                              pbmoe_q4_matvec
-  h    = x + o,  n = rms_norm(h) w_post                               pbmoe_rms_norm
-  x    = h + MoE(n),  xn = rms_norm(x) w_in(next layer)               pbmoe_moe_layer
+  qa, kv = Q4(q_a_proj) xn, Q4(kv_a_proj_with_mqa) xn            pbmoe_q4_matvec_fused (2 matrices)
+  q      = Q4(q_b_proj) rms_norm(qa) w_qa                         pbmoe_q4_matvec_fused (input norm)
+  RoPE on q's and kv's rope parts; rms_norm(kv[:latent]) w_kv
+  and the rotated key written into the caches                     pbmoe_mla_rope_append (latent norm)
+  attn   = absorbed MLA attention over the cache                  pbmoe_mla_decode
+  h      = x + Q4(o_proj) attn                                    pbmoe_q4_matvec_fused (residual)
+  x      = h + MoE(rms_norm(h) w_post), xn = rms_norm(x) w_in'    pbmoe_moe_layer (input norm, next norm)
 
 and after the last layer (whose fused norm uses the final norm weight) the
 vocab head top-k (pbmoe_head_topk). The residual stream x is f32; the MLA
@@ -60,6 +63,9 @@ class Q4:
     def __init__(self, rows, cols, group, g, device):
         self.rows, self.cols, self.group = rows, cols, group
         self.packed, self.scales, self.biases = synth.q4_matrix(rows, cols, group, g, device)
+
+    def mat(self):
+        return (self.packed, self.scales, self.biases, self.rows, self.cols, self.group)
 
     def __call__(self, ctx, x, y, stream):
         ctx.q4_matvec(self.packed, self.scales, self.biases, self.rows, self.cols, self.group, x, y,
@@ -138,13 +144,18 @@ class DecodeStep:
         self.attn = torch.zeros(B, cfg.heads, cfg.v_dim, **f32)
         self.o = torch.zeros(B, H, **f32)
         self.h = torch.zeros(B, H, **f32)
-        self.n = torch.zeros(B, H, device=dev, dtype=torch.bfloat16)
+        self.n = torch.zeros(B, H, device=dev, dtype=torch.bfloat16)  # normalised MoE input (recorded only)
+        self.logits = torch.zeros(B, cfg.vocab, **f32)  # head logits (recorded only)
         self.route_ids = torch.zeros(cfg.layers, B, cfg.top_k, device=dev, dtype=torch.int32)
         self.ids = torch.zeros(B, cfg.candidates, device=dev, dtype=torch.int32)
         self.vals = torch.zeros(B, cfg.candidates, **f32)
         self.mla_cfg = capi.mla_config(cfg.heads, cfg.nope, cfg.rope, cfg.latent, cfg.v_dim)
         self.moe_cfg = capi.moe_config(model.layers[0].moe.layout, cfg.experts, cfg.top_k)
-        self.moe_w = [l.moe.c_weights() for l in model.layers]
+        self.moe_w = []
+        for l in model.layers:  # the post-attention norm runs inside the MoE layer's router kernel
+            w = l.moe.c_weights()
+            w.input_norm_weight = l.post_norm.data_ptr()
+            self.moe_w.append(w)
         ctx.reserve(B, self.moe_cfg)
         ctx.mla_reserve(self.mla_cfg, B)
         ctx.rope_reserve(cfg.context, cfg.rope, cfg.theta)
@@ -154,38 +165,59 @@ class DecodeStep:
         """x f32 [B, hidden]: the step's embeddings (residual stream)."""
         self.x.copy_(x)
 
-    def launch(self, stream=None, record_routes=False):
-        """Enqueue the step; record_routes also writes every layer's route ids
-        to self.route_ids (for counting the experts a step reads)."""
+    def launch(self, stream=None, record_routes=False, record=None):
+        """Enqueue the step. record_routes writes every layer's route ids to
+        self.route_ids (for counting the experts a step reads); record (a dict)
+        receives per-layer copies of the intermediates for parity checks."""
         ctx, cfg, m = self.ctx, self.cfg, self.model
         L0 = m.layers[0]
         ctx.rms_norm(self.x, L0.input_norm, self.xn, eps=cfg.eps, stream=stream)
         seq_lens = [p + 1 for p in self.positions_host]
         for i, L in enumerate(m.layers):
-            L.q_a(ctx, self.xn, self.qa, stream)
-            L.kv_a(ctx, self.xn, self.kv, stream)
-            ctx.rms_norm(self.qa, L.q_a_norm, self.qa, eps=cfg.eps, stream=stream)
-            ctx.rms_norm(self.kv, L.kv_a_norm, self.kv, eps=cfg.eps, width=cfg.latent, stream=stream)
-            L.q_b(ctx, self.qa, self.q.view(self.B, -1), stream)
+            if record is not None:
+                record.setdefault("x", []).append(self.x.clone())
+                record.setdefault("xn", []).append(self.xn.clone())
+            ctx.q4_fused([L.q_a.mat(), L.kv_a.mat()], self.xn, [self.qa, self.kv], stream=stream)
+            ctx.q4_fused([L.q_b.mat()], self.qa, [self.q.view(self.B, -1)], norm=L.q_a_norm, eps=cfg.eps,
+                         stream=stream)
+            if record is not None:
+                record.setdefault("qa", []).append(self.qa.clone())
+                record.setdefault("kv", []).append(self.kv.clone())
+                record.setdefault("q_prerope", []).append(self.q.clone())
             ctx.mla_rope_append(self.mla_cfg, self.q, self.kv, self.positions, self.caches.c_kv_ptrs[i],
-                                self.caches.k_rope_ptrs[i], cfg.context, stream=stream)
+                                self.caches.k_rope_ptrs[i], cfg.context, latent_norm=L.kv_a_norm, eps=cfg.eps,
+                                stream=stream)
             ctx.mla_decode(self.mla_cfg, self.q, [t[:n] for t, n in zip(self.caches.c_kv[i], seq_lens)],
                            [t[:n] for t, n in zip(self.caches.k_rope[i], seq_lens)], L.w_uk, L.w_uv, self.attn,
                            stream=stream)
-            L.o_proj(ctx, self.attn.view(self.B, -1), self.o, stream)
-            ctx.rms_norm(self.o, L.post_norm, self.n, eps=cfg.eps, residual=self.x, sum_out=self.h, stream=stream)
+            ctx.q4_fused([L.o_proj.mat()], self.attn.view(self.B, -1), [self.h], residual=self.x, stream=stream)
+            if record is not None:
+                record.setdefault("q", []).append(self.q.clone())
+                record.setdefault("attn", []).append(self.attn.clone())
+                record.setdefault("h", []).append(self.h.clone())
             nxt = m.layers[i + 1].input_norm if i + 1 < len(m.layers) else m.final_norm
-            dbg = capi.MoeDebug(None, self.route_ids[i].data_ptr(), None, None, None) if record_routes else None
-            ctx.moe_layer(self.moe_cfg, self.moe_w[i], self.n, self.x, self.B, residual=self.h,
+            dbg = None
+            if record_routes or record is not None:
+                dbg = capi.MoeDebug(None, self.route_ids[i].data_ptr(), None, None, None,
+                                    self.n.data_ptr() if record is not None else None)
+            ctx.moe_layer(self.moe_cfg, self.moe_w[i], self.h, self.x, self.B, residual=self.h,
                           next_norm_weight=nxt, next_normed=self.xn, debug=dbg, stream=stream)
-        ctx.head_topk(m.head, self.xn, self.ids, self.vals, stream=stream)
+            if record is not None:
+                record.setdefault("n", []).append(self.n.clone())
+                record.setdefault("route_ids", []).append(self.route_ids[i].clone())
+        if record is not None:
+            record["x_final"] = self.x.clone()
+            record["xn_final"] = self.xn.clone()
+            ctx.head_topk(m.head, self.xn, self.ids, self.vals, logits=self.logits, stream=stream)
+        else:
+            ctx.head_topk(m.head, self.xn, self.ids, self.vals, stream=stream)
 
     def launches_per_step(self):
-        """CUDA kernels one step launches: the input norm; per layer 4 q4
-        matvecs, 3 norms, RoPE/append, 4 MLA kernels and 4 MoE kernels per
-        8-token chunk; the head's 3 (plus a memset)."""
+        """CUDA kernels one step launches: the input norm; per layer 2 fused
+        projection launches, RoPE/append, 4 MLA kernels, the o_proj launch and
+        4 MoE kernels per 8-token chunk; the head's 3 (plus a memset)."""
         chunks = (self.B + 7) // 8
-        return 1 + self.cfg.layers * (4 + 3 + 1 + 4 + 4 * chunks) + 3
+        return 1 + self.cfg.layers * (2 + 1 + 4 + 1 + 4 * chunks) + 3
 
     def unique_experts(self):
         """Distinct routed experts per layer in the recorded routes (mean over layers)."""

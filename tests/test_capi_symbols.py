@@ -43,7 +43,7 @@ def test_library_loads_without_gpu(lib_path):
     lib = ctypes.CDLL(lib_path)
     for name in declared_symbols():
         assert hasattr(lib, name)
-    assert lib.pbmoe_abi_version() == 1
+    assert lib.pbmoe_abi_version() == 2
 
 
 def test_host_only_entry_points(lib_path):

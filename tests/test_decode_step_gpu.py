@@ -122,54 +122,236 @@ def test_mla_rope_append_bad_position(ctx):
     assert torch.equal(ckv, before)
 
 
-def _oracle_step(oracle, model, caches_np, x, positions):
-    """The same step on the CPU from the oracle's functions."""
+def test_mla_rope_append_latent_norm(ctx, oracle):
+    """The kv_a latent norm fused into the append: the cache row is
+    bf16(rms_norm(kv[:512]) * w) (within one bf16 rounding of the oracle, whose
+    sum of squares runs in another order); the key row stays bit-exact."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    cfg = capi.mla_config()
+    B, ctxlen = 4, 64
+    ctx.rope_reserve(ctxlen, 64, 10000.0)
+    g = torch.Generator("cuda").manual_seed(15)
+    q = torch.randn(B, 16, 192, generator=g, device="cuda")
+    kv = torch.randn(B, 576, generator=g, device="cuda") * 2.0
+    w = (1 + 0.1 * torch.randn(512, generator=g, device="cuda")).float()
+    pos = [0, 9, 33, 63]
+    ckv = [synth.normal_bf16((ctxlen, 512), 1.0, synth.gen("cuda", 40 + b), "cuda") for b in range(B)]
+    kr = [synth.normal_bf16((ctxlen, 64), 1.0, synth.gen("cuda", 50 + b), "cuda") for b in range(B)]
+    ptr = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+    kv0 = kv.cpu().numpy()
+    ctx.mla_rope_append(cfg, q, kv, torch.tensor(pos, dtype=torch.int32, device="cuda"), ptr(ckv), ptr(kr), ctxlen,
+                        latent_norm=w, eps=1e-6)
+    torch.cuda.synchronize()
+    assert ctx.device_status() == 0
+    for b in range(B):
+        ref = oracle.rms_norm(kv0[b, :512], w.cpu().numpy(), 1e-6)
+        assert_close(_f32_of_bf16(ckv[b][pos[b]]), ref, tol=8e-3, what="normed latent row")
+        kref = oracle.rope_interleaved_to_split_half(kv0[b, 512:], pos[b], 64, 10000.0)
+        assert np.array_equal(_f32_of_bf16(kr[b][pos[b]]), oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(kref)))
+
+
+@pytest.mark.parametrize("batch", [1, 2, 8, 11])
+def test_q4_fused_two_matrices_norm_residual(ctx, oracle, batch):
+    """pbmoe_q4_matvec_fused: q_a + kv_a on one input (two matrices, one
+    launch), q_b on RMSNorm(x) (fused input norm) and o_proj + residual, on the
+    CUDA-core (batch <= 2) and tensor-core kernels, against the oracle's
+    q4_fma_matvec_bf16 within 1e-2."""
+    import torch
+
+    from pb_b200 import decode, synth
+
+    g = synth.gen("cuda", 70 + batch)
+    qa, kva = decode.Q4(1536, 2048, 64, g, "cuda"), decode.Q4(576, 2048, 64, g, "cuda")
+    qb, op = decode.Q4(3072, 1536, 64, g, "cuda"), decode.Q4(2048, 2048, 64, g, "cuda")
+    x = torch.randn(batch, 2048, generator=g, device="cuda")
+    y1, y2 = torch.empty(batch, 1536, device="cuda"), torch.empty(batch, 576, device="cuda")
+    ctx.q4_fused([qa.mat(), kva.mat()], x, [y1, y2])
+    w = (1 + 0.1 * torch.randn(1536, generator=g, device="cuda")).float()
+    z = torch.randn(batch, 1536, generator=g, device="cuda") * 3
+    y3 = torch.empty(batch, 3072, device="cuda")
+    ctx.q4_fused([qb.mat()], z, [y3], norm=w, eps=1e-6)
+    res = torch.randn(batch, 2048, generator=g, device="cuda")
+    y4 = torch.empty(batch, 2048, device="cuda")
+    ctx.q4_fused([op.mat()], x, [y4], residual=res)
+    torch.cuda.synchronize()
+    u16 = lambda t: synth.bf16_bits(t).cpu().numpy().view(np.uint16).reshape(-1)
+    mv = lambda P, v: oracle.q4_fma_matvec_bf16(P.packed.cpu().numpy(), v, u16(P.scales), u16(P.biases), P.rows,
+                                                P.cols, P.group)
+    xs, zs, rs = x.cpu().numpy(), z.cpu().numpy(), res.cpu().numpy()
+    for b in range(batch):
+        assert_close(y1[b].cpu().numpy(), mv(qa, xs[b]), what=f"q_a b={b}")
+        assert_close(y2[b].cpu().numpy(), mv(kva, xs[b]), what=f"kv_a b={b}")
+        assert_close(y3[b].cpu().numpy(), mv(qb, oracle.rms_norm(zs[b], w.cpu().numpy(), 1e-6)), what=f"q_b b={b}")
+        assert_close(y4[b].cpu().numpy(), rs[b] + mv(op, xs[b]), what=f"o_proj + residual b={b}")
+
+
+def test_q4_fused_refusals(ctx):
+    import torch
+
+    from pb_b200 import capi, decode, synth
+
+    g = synth.gen("cuda", 90)
+    a, b = decode.Q4(64, 512, 64, g, "cuda"), decode.Q4(64, 256, 64, g, "cuda")
+    x = torch.randn(2, 512, device="cuda")
+    y = torch.empty(2, 64, device="cuda")
+    with pytest.raises(capi.PbmoeError, match="differ in cols"):
+        ctx.q4_fused([a.mat(), b.mat()], x, [y, y])
+    with pytest.raises(capi.PbmoeError, match="f32 x"):
+        ctx.q4_fused([a.mat()], x.to(torch.bfloat16), [y], norm=torch.ones(512, device="cuda"))
+    with pytest.raises(capi.PbmoeError, match="one matrix"):
+        ctx.q4_fused([a.mat(), a.mat()], x, [y, y], residual=y)
+
+
+def _u16(t):
     from pb_b200 import synth
 
+    return synth.bf16_bits(t).cpu().numpy().view(np.uint16)
+
+
+def _q4(oracle, P, v, threads=8):
+    return oracle.q4_fma_matvec_bf16(P.packed.cpu().numpy(), np.ascontiguousarray(v, np.float32),
+                                     _u16(P.scales).reshape(-1), _u16(P.biases).reshape(-1), P.rows, P.cols, P.group,
+                                     threads=threads)
+
+
+def _bf(oracle, a):
+    return oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(np.asarray(a, np.float32)))
+
+
+def _mla(oracle, L, cfg, q, lat, rot):
+    return oracle.mla_absorbed_attention(np.ascontiguousarray(q.reshape(-1), np.float32), lat, rot, _u16(L.w_uk),
+                                         _u16(L.w_uv), cfg.heads, cfg.nope, cfg.rope, cfg.latent, cfg.v_dim)
+
+
+def _oracle_step(oracle, model, caches_np, x, positions):
+    """The same step on the CPU from the oracle's functions, free-running from
+    the input embeddings (the reference's order: runtime/mod.rs:1432-2024)."""
     cfg = model.cfg
-    u16 = lambda t: synth.bf16_bits(t).cpu().numpy().view(np.uint16)
-    bf = lambda a: oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(np.asarray(a, np.float32)))
-    q4 = lambda P, v: oracle.q4_fma_matvec_bf16(P.packed.cpu().numpy(), v, u16(P.scales).reshape(-1),
-                                                u16(P.biases).reshape(-1), P.rows, P.cols, P.group)
     B = x.shape[0]
     x = x.copy()
     xn = np.stack([oracle.rms_norm(x[b], model.layers[0].input_norm.cpu().numpy(), cfg.eps) for b in range(B)])
+    ids_all = []
     for i, L in enumerate(model.layers):
         n_rows, h_rows = [], []
         for b in range(B):
-            qa = oracle.rms_norm(q4(L.q_a, xn[b]), L.q_a_norm.cpu().numpy(), cfg.eps)
-            kv = q4(L.kv_a, xn[b])
+            qa = oracle.rms_norm(_q4(oracle, L.q_a, xn[b]), L.q_a_norm.cpu().numpy(), cfg.eps)
+            kv = _q4(oracle, L.kv_a, xn[b])
             kv[:cfg.latent] = oracle.rms_norm(kv[:cfg.latent], L.kv_a_norm.cpu().numpy(), cfg.eps)
-            q = q4(L.q_b, qa).reshape(cfg.heads, cfg.nope + cfg.rope)
+            q = _q4(oracle, L.q_b, qa).reshape(cfg.heads, cfg.nope + cfg.rope)
             for h in range(cfg.heads):
                 q[h, cfg.nope:] = oracle.rope_interleaved_to_split_half(q[h, cfg.nope:], positions[b], cfg.rope,
                                                                         cfg.theta)
             krot = oracle.rope_interleaved_to_split_half(kv[cfg.latent:], positions[b], cfg.rope, cfg.theta)
             lat, rot = caches_np[0][i][b], caches_np[1][i][b]
-            lat[positions[b]] = bf(kv[:cfg.latent])
-            rot[positions[b]] = bf(krot)
+            lat[positions[b]] = _bf(oracle, kv[:cfg.latent])
+            rot[positions[b]] = _bf(oracle, krot)
             n = positions[b] + 1
-            attn = oracle.mla_absorbed_attention(q.reshape(-1), lat[:n], rot[:n], u16(L.w_uk), u16(L.w_uv),
-                                                 cfg.heads, cfg.nope, cfg.rope, cfg.latent, cfg.v_dim)
-            o = q4(L.o_proj, attn)
-            h_row = x[b] + o
+            attn = _mla(oracle, L, cfg, q, lat[:n], rot[:n])
+            h_row = x[b] + _q4(oracle, L.o_proj, attn)
             h_rows.append(h_row)
-            n_rows.append(bf(oracle.rms_norm(h_row, L.post_norm.cpu().numpy(), cfg.eps)))
+            n_rows.append(_bf(oracle, oracle.rms_norm(h_row, L.post_norm.cpu().numpy(), cfg.eps)))
         m = L.moe
         offs = np.array(list(m.layout.component_offsets), np.uint64)
-        out, ids, _, _ = oracle.moe_layer(np.stack(n_rows), u16(m.router), m.experts.cpu().numpy(), offs,
+        out, ids, _, _ = oracle.moe_layer(np.stack(n_rows), _u16(m.router), m.experts.cpu().numpy(), offs,
                                           int(m.layout.expert_bytes), cfg.experts, cfg.top_k, cfg.inter, cfg.group,
-                                          shared_slot=m.shared.cpu().numpy(), shared_gate_bits=u16(m.shared_gate),
-                                          residual=np.stack(h_rows))
+                                          shared_slot=m.shared.cpu().numpy(), shared_gate_bits=_u16(m.shared_gate),
+                                          residual=np.stack(h_rows), threads=8)
+        ids_all.append(ids)
         x = out
         nxt = model.layers[i + 1].input_norm if i + 1 < len(model.layers) else model.final_norm
         xn = np.stack([oracle.rms_norm(x[b], nxt.cpu().numpy(), cfg.eps) for b in range(B)])
-    return x, xn
+    return x, xn, ids_all
+
+
+def check_step_teacher_forced(oracle, model, caches, rec, positions, what=""):
+    """Every stage of every layer recomputed by the oracle from the GPU's own
+    inputs to that stage (so the checks do not compound): projections, norms,
+    RoPE and cache rows, MLA attention, o_proj + residual, the MoE input norm,
+    routing (ids bit-exact: the router chain is the reference's) and the layer
+    output, then the head (logits within 1e-4 of an f32 product, candidates
+    bit-exact against topk_vocab on the kernel's own logits)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    cfg = model.cfg
+    f = lambda t: t.float().cpu().numpy()
+    B = len(positions)
+    pool = ThreadPoolExecutor(max_workers=8)
+    for i, L in enumerate(model.layers):
+        xn, x = f(rec["xn"][i]), f(rec["x"][i])
+        qa, kv, qpre, q = f(rec["qa"][i]), f(rec["kv"][i]), f(rec["q_prerope"][i]), f(rec["q"][i])
+        attn, h, n = f(rec["attn"][i]), f(rec["h"][i]), f(rec["n"][i])
+        for b in range(B):
+            assert_close(qa[b], _q4(oracle, L.q_a, xn[b]), what=f"{what} L{i} q_a b{b}")
+            assert_close(kv[b], _q4(oracle, L.kv_a, xn[b]), what=f"{what} L{i} kv_a b{b}")
+            qa_n = oracle.rms_norm(qa[b], L.q_a_norm.cpu().numpy(), cfg.eps)
+            assert_close(qpre[b].reshape(-1), _q4(oracle, L.q_b, qa_n), what=f"{what} L{i} q_b b{b}")
+            for hh in range(cfg.heads):
+                ref = oracle.rope_interleaved_to_split_half(qpre[b, hh, cfg.nope:], positions[b], cfg.rope, cfg.theta)
+                assert np.array_equal(q[b, hh, cfg.nope:], ref), f"{what} L{i} b{b} h{hh}: query RoPE not bit-exact"
+            lat = f(caches.c_kv[i][b][positions[b]])
+            assert_close(lat, oracle.rms_norm(kv[b, :cfg.latent], L.kv_a_norm.cpu().numpy(), cfg.eps), tol=8e-3,
+                         what=f"{what} L{i} latent row b{b}")
+            kref = oracle.rope_interleaved_to_split_half(kv[b, cfg.latent:], positions[b], cfg.rope, cfg.theta)
+            assert np.array_equal(f(caches.k_rope[i][b][positions[b]]), _bf(oracle, kref)), \
+                f"{what} L{i} b{b}: key row not bit-exact"
+        nl = [p + 1 for p in positions]
+        attn_ref = list(pool.map(lambda b: _mla(oracle, L, cfg, q[b], f(caches.c_kv[i][b][:nl[b]]),
+                                                f(caches.k_rope[i][b][:nl[b]])), range(B)))
+        for b in range(B):
+            assert_close(attn[b].reshape(-1), attn_ref[b], what=f"{what} L{i} attention b{b}")
+            assert_close(h[b], x[b] + _q4(oracle, L.o_proj, attn[b].reshape(-1)), what=f"{what} L{i} o_proj b{b}")
+            assert_close(n[b], oracle.rms_norm(h[b], L.post_norm.cpu().numpy(), cfg.eps), tol=8e-3,
+                         what=f"{what} L{i} post-attention norm b{b}")
+        m = L.moe
+        offs = np.array(list(m.layout.component_offsets), np.uint64)
+        out, ids, _, _ = oracle.moe_layer(n, _u16(m.router), m.experts.cpu().numpy(), offs, int(m.layout.expert_bytes),
+                                          cfg.experts, cfg.top_k, cfg.inter, cfg.group,
+                                          shared_slot=m.shared.cpu().numpy(), shared_gate_bits=_u16(m.shared_gate),
+                                          residual=h, threads=8)
+        gids = rec["route_ids"][i].cpu().numpy().view(np.uint32)
+        assert np.array_equal(gids, ids), f"{what} L{i}: route ids differ ({int(np.sum(gids != ids))} slots)"
+        x_next = f(rec["x"][i + 1]) if i + 1 < len(model.layers) else f(rec["x_final"])
+        xn_next = f(rec["xn"][i + 1]) if i + 1 < len(model.layers) else f(rec["xn_final"])
+        assert_close(x_next, out, what=f"{what} L{i} MoE layer output")
+        nw = (model.layers[i + 1].input_norm if i + 1 < len(model.layers) else model.final_norm).cpu().numpy()
+        assert_close(xn_next, np.stack([oracle.rms_norm(x_next[b], nw, cfg.eps) for b in range(B)]),
+                     what=f"{what} L{i} next-layer norm")
+    pool.shutdown()
+    xn_f = f(rec["xn_final"])
+    logits = rec["logits"].cpu().numpy()
+    head = model.head.float().cpu().numpy()
+    assert_close(logits, xn_f @ head.T, tol=1e-4, what=f"{what} head logits")
+    ids = rec["ids"].cpu().numpy().view(np.uint32)
+    for b in range(B):
+        sid, _ = oracle.topk_vocab(logits[b], cfg.candidates)
+        assert np.array_equal(ids[b], sid), f"{what} b{b}: head candidates differ from topk_vocab on its logits"
+
+
+def _run_recorded(ctx, model, caches, B, positions, seed):
+    import torch
+
+    from pb_b200 import decode
+
+    step = decode.DecodeStep(ctx, model, caches, B, positions)
+    x0 = torch.randn(B, model.cfg.hidden, generator=torch.Generator("cuda").manual_seed(seed), device="cuda")
+    step.set_input(x0)
+    rec = {}
+    step.launch(record=rec)
+    torch.cuda.synchronize()
+    assert ctx.device_status() == 0
+    rec["logits"], rec["ids"] = step.logits.clone(), step.ids.clone()
+    return step, x0, rec
 
 
 def test_decode_step_two_layers(ctx, oracle):
-    import torch
-
+    """A small two-layer model: every stage teacher-forced (route ids bit-exact
+    there), and the whole step free-running against the oracle chain within
+    1e-2. Free-running, the MoE inputs of the two chains differ by rounding,
+    so a near-tie may replace slots in another order; every token must still
+    route to the same set of experts."""
     from pb_b200 import decode
 
     cfg = decode.StepConfig(hidden=512, layers=2, q_lora=512, experts=64, top_k=6, inter=256, vocab=3000,
@@ -179,20 +361,42 @@ def test_decode_step_two_layers(ctx, oracle):
     caches = decode.Caches(cfg, B, seed=3)
     caches_np = ([[t.float().cpu().numpy() for t in l] for l in caches.c_kv],
                  [[t.float().cpu().numpy() for t in l] for l in caches.k_rope])
-    step = decode.DecodeStep(ctx, model, caches, B, positions)
-    x0 = torch.randn(B, cfg.hidden, generator=torch.Generator("cuda").manual_seed(9), device="cuda")
-    step.set_input(x0)
-    step.launch()
-    torch.cuda.synchronize()
-    assert ctx.device_status() == 0
-    rx, rxn = _oracle_step(oracle, model, caches_np, x0.cpu().numpy(), positions)
-    assert_close(step.x.cpu().numpy(), rx, tol=2e-2, what="hidden after two layers")
-    assert_close(step.xn.cpu().numpy(), rxn, tol=2e-2, what="final-normed hidden")
-    # the head ran on the kernel's final-normed hidden: its selection is the oracle's on those inputs
-    from pb_b200 import synth
+    step, x0, rec = _run_recorded(ctx, model, caches, B, positions, 9)
+    check_step_teacher_forced(oracle, model, caches, rec, positions, what="small")
+    rx, rxn, rids = _oracle_step(oracle, model, caches_np, x0.cpu().numpy(), positions)
+    for i in range(cfg.layers):
+        gids = rec["route_ids"][i].cpu().numpy().view(np.uint32)
+        assert np.array_equal(np.sort(gids, axis=1), np.sort(rids[i], axis=1)), f"free-running L{i} route sets"
+        reordered = int(np.sum(np.any(gids != rids[i], axis=1)))
+        print(f"free-running L{i}: {reordered} of {B} tokens with the same experts in another slot order")
+    assert_close(step.x.cpu().numpy(), rx, what="hidden after two layers")
+    assert_close(step.xn.cpu().numpy(), rxn, what="final-normed hidden")
 
-    ids = step.ids.cpu().numpy().view(np.uint32)
-    rid, _, _ = oracle.head_topk(synth.bf16_bits(model.head).cpu().numpy().view(np.uint16),
-                                 step.xn.cpu().numpy(), cfg.candidates)
-    overlap = np.mean([len(set(ids[b]) & set(rid[b])) / cfg.candidates for b in range(B)])
-    assert overlap >= 0.9, f"head candidates overlap {overlap:.2f}"
+
+@pytest.fixture(scope="module")
+def config4_model():
+    from pb_b200 import decode
+
+    cfg = decode.StepConfig(layers=2)  # config-4 shapes: hidden 2048, 512 experts top-10, MLA, vocab 151936
+    return decode.Model(cfg, seed=44)
+
+
+@pytest.mark.parametrize("B", [1, 8, 32])
+def test_decode_step_config4_shapes(ctx, oracle, config4_model, B):
+    """Config 4 at its real shapes (two of the 48 layers): hidden 2048, MLA
+    over an 8192-row cache (16 heads, nope 128, rope 64, latent 512), 512
+    experts top-10 with the shared expert, the 151936-row vocab head; batch 1,
+    8 and 32 at positions spread over the cache. Every stage teacher-forced
+    within 1e-2, route ids and head candidates bit-exact."""
+    import torch
+
+    from pb_b200 import decode
+
+    model = config4_model
+    cfg = model.cfg
+    positions = [cfg.context - 1 - (977 * b) % 4096 for b in range(B)]
+    caches = decode.Caches(cfg, B, seed=100 + B)
+    step, x0, rec = _run_recorded(ctx, model, caches, B, positions, 200 + B)
+    check_step_teacher_forced(oracle, model, caches, rec, positions, what=f"config4 B={B}")
+    del step, caches, rec
+    torch.cuda.empty_cache()

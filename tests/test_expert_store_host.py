@@ -248,3 +248,26 @@ def test_mxfp4_layer_reads_as_stored(tmp_path):
     assert np.array_equal(capi.expert_layer_read(tmp_path, 2, lay, 1, 4), slots[1:5])
     with pytest.raises(capi.PbmoeError, match="MXFP4 layout"):
         capi.expert_layer_read(tmp_path, 2, capi.fixed_q4_layout(H, I, 32), 0, 1)
+
+
+def test_mxfp4_layer_refuses_other_offsets(tmp_path):
+    """An MXFP4 layer read with offsets other than the fixed MXFP4 image's
+    (here the up nibbles moved but the slot size and empty biases kept) would
+    read its bytes in the wrong places, so it is refused."""
+    from pb_b200 import capi
+
+    lay = capi.fixed_mxfp4_layout(H, I, 32)
+    rng = np.random.default_rng(5)
+    slots = rng.integers(0, 256, (E, lay.expert_bytes), dtype=np.uint8)
+
+    def fmt(m):
+        m["format"] = "FIXED_MXFP4_EXPERT_LAYER_V1"
+        for p in m["packs"]:
+            p["records"] = []
+
+    write_layer(str(tmp_path), 2, slots, H, I, 32, list(lay.component_offsets), meta_edit=fmt)
+    bad = capi.fixed_mxfp4_layout(H, I, 32)
+    bad.component_offsets[3] += 16  # up nibbles shifted; gate scales now overlap them
+    with pytest.raises(capi.PbmoeError, match="fixed MXFP4 layout"):
+        capi.expert_layer_read(tmp_path, 2, bad, 0, 1)
+    assert np.array_equal(capi.expert_layer_read(tmp_path, 2, lay, 0, 2), slots[:2])

@@ -51,11 +51,15 @@ def _make(seed, lens, q_scale=1.0, device="cuda"):
 
 
 def _oracle(oracle, q, ckv, kr, wuk, wuv):
-    outs = []
-    for b in range(len(ckv)):
-        outs.append(oracle.mla_absorbed_attention(q[b].float().cpu().numpy(), ckv[b].float().cpu().numpy(),
-                                                  kr[b].float().cpu().numpy(), _bits(wuk), _bits(wuv), H, NOPE,
-                                                  ROPE, LAT, V))
+    """The oracle per sequence, sequences on parallel threads (each call is
+    independent and releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    bk, bv = _bits(wuk), _bits(wuv)
+    one = lambda b: oracle.mla_absorbed_attention(q[b].float().cpu().numpy(), ckv[b].float().cpu().numpy(),
+                                                  kr[b].float().cpu().numpy(), bk, bv, H, NOPE, ROPE, LAT, V)
+    with ThreadPoolExecutor(max_workers=8) as pool:
+        outs = list(pool.map(one, range(len(ckv))))
     return np.stack(outs).reshape(len(ckv), H, V)
 
 
@@ -98,8 +102,9 @@ def test_mla_peaked_scores(ctx, oracle):
     assert_close(got, ref, what="mla peaked")
 
 
-@pytest.mark.parametrize("L,batch", [(4096, 1), (4096, 8), (32768, 1)])
+@pytest.mark.parametrize("L,batch", [(4096, 1), (4096, 8), (32768, 1), (32768, 8)])
 def test_mla_config3(ctx, oracle, L, batch):
+    """Every config-3 case, including the benchmarked (32768, 8)."""
     lens = [L] * batch
     q, ckv, kr, wuk, wuv = _make(3 + L + batch, lens)
     ref = _oracle(oracle, q, ckv, kr, wuk, wuv)
