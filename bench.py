@@ -1,40 +1,47 @@
 #!/usr/bin/env python3
 """Benchmark of the FlashMoE hot path on B200.
 
-Workload: one MoE FFN decode layer per step — hidden
-2048, 512 routed experts top-10 (softmax, renormalised), 1 shared expert with
-a sigmoid gate, expert intermediate 512, 4-bit group-64 affine weights, bf16
-activations ~N(0,1) — on `--batch` tokens. Consecutive steps cycle through
-`--layers` (default 48) independently seeded layers (43.5 GB of expert
-weights) and distinct inputs, so every step's weights come from HBM rather
-than L2 (126 MB): the per-layer router + shared expert alone are 182 MB over
-48 layers.
+Default workload (the metric "MoE decode tok/s at
+1/2/4/8 B200"): one full decode step of the synthetic 48-layer model — per
+layer MLA latent attention (16 heads, nope 128, rope 64, latent 512) over an
+8192-row cache and a 512-expert top-10 4-bit MoE FFN with a shared expert,
+then the 151936-row vocabulary head and its top-64 candidates — for --batch
+sequences (default 8). Random-init weights of that architecture (45 GB) and
+random caches; every step reads all its weights and cache rows from HBM
+(inputs larger than L2).
 
 Reported (one JSON line on rank 0):
-  value     tokens/s of the whole job, device-timed (CUDA events, max over
-            ranks) over exactly --steps graph-replayed steps, inputs resident.
-  e2e       the same metric through the public C-ABI call per step with host
-            buffers: pinned H2D of the step's tokens, pbmoe_moe_layer, D2H of
-            its output, all inside the timed region.
-  roofline  dominant kernel's algorithmic bytes / its event-timed duration vs
-            the measured HBM copy bandwidth (MEASURED_PEAKS.json).
-  cpu_baseline  the C++ oracle (restatement of the reference's Rust CPU path)
-            on this host's cores, bounded sample.
-`--impl reference` times the oracle alone (the reference cannot be built:
-Rust toolchain absent; its GPU path is Metal).
+  value     tokens/s of the whole job (batch / step time), device-timed with
+            CUDA events over exactly --steps graph-replayed steps (max over
+            ranks), inputs resident.
+  e2e       the same metric with host buffers: per step, the H2D copy of the
+            step's input embeddings from pinned memory, the step, and the D2H
+            of its candidate ids and values, all inside the timed region.
+  roofline  the dominant kernel (largest share of the step in a per-call
+            event-timed pass): its algorithmic bytes per launch / its mean
+            launch time vs the measured HBM copy bandwidth; `step` gives the
+            whole step's algorithmic bytes / step time.
+  cpu_baseline  the C++ oracle chain (restatement of the reference's Rust CPU
+            path) on this host's cores, one and all threads, on a bounded
+            sample (tokens through 2 of the 48 layers plus the head), scaled to
+            the 48-layer step.
+`--impl reference` times that oracle chain alone on all host threads (the
+reference cannot be built: Rust toolchain absent; its GPU path is Metal).
 
-Other lines (`--workload`, one GPU): matvec (config 0, Q4 [4096x2048]),
-gemm (config 2, tcgen05 prefill GEMM, dense and grouped), mla (config 3,
-absorbed MLA decode), head (config 4's vocab head + top-64), step (config
-4's full 48-layer decode step at context 8192), mxfp4 (the config-0 shape
+Multi-GPU (torchrun, N>1): expert and vocabulary parallelism. Rank r holds
+experts [r*512/N, (r+1)*512/N) of every layer (the shared expert on rank 0)
+and rows [r*V/N, (r+1)*V/N) of the head; attention, router and norms are
+replicated, so every rank routes the same tokens and runs its own experts'
+routes; each layer's output is the one-shot NVLink peer-memory combine of the
+ranks' partials (pbmoe_ep_moe_layer), and the head's candidate lists are
+all-gathered (NCCL) and merged (pbmoe_head_merge). The job processes the same
+--batch tokens per step at every N ("strong" scaling).
+
+Other lines (`--workload`, one GPU): moe (config 1: one MoE FFN decode layer
+per step, 48 layers cycled), matvec (config 0, Q4 [4096x2048]), gemm
+(config 2, tcgen05 prefill GEMM, dense and grouped), mla (config 3, absorbed
+MLA decode), head (config 4's vocab head + top-64), mxfp4 (the config-0 shape
 in MXFP4). Each prints the same keys as the headline line.
-
-Multi-GPU (torchrun, N>1): expert parallelism. Rank r holds experts
-[r*512/N, (r+1)*512/N) of every cycled layer (router and shared expert
-replicated, the shared expert computed on rank 0); every rank routes the same
-tokens and runs its own experts' routes; the layer output is the one-shot
-NVLink peer-memory combine of the ranks' partials (pbmoe_ep_moe_layer). The
-job processes the same --batch tokens per step at every N ("strong" scaling).
 """
 
 from __future__ import annotations
@@ -61,20 +68,20 @@ METRIC = "MoE decode tok/s (config 1: one MoE FFN decode layer per step)"
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu --set
 # full capture of each kernel (profiles/ holds the summaries and commands)
 NCU_TRAFFIC = {"expert_gate_up": 95.2e6, "expert_down": 46.6e6, "router+topk": 2.2e6, "combine": 0.75e6}
-NCU_TRAFFIC_SOURCE = "ncu --set full, 4-layer config-1 case at B=8 (profiles/moe_decode_config1.md)"
+NCU_TRAFFIC_SOURCE = "ncu --set full of each kernel, 4-layer config-1 case at B=8"
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20000)
-    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    p.add_argument("--workload", default="moe", choices=["moe", "matvec", "gemm", "mla", "head", "step", "mxfp4"],
-                   help="moe: config 1 (the headline line); matvec: config 0; gemm: config 2; mla: config 3; "
-                        "head: config 4's vocab head + top-k; step: config 4's full decode step; "
+    p.add_argument("--workload", default="step", choices=["step", "moe", "matvec", "gemm", "mla", "head", "mxfp4"],
+                   help="step: config 4's full 48-layer decode step (the headline line); moe: config 1; "
+                        "matvec: config 0; gemm: config 2; mla: config 3; head: config 4's vocab head + top-k; "
                         "mxfp4: the config-0 matvec in MXFP4")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--only-batch", action="store_true",
@@ -248,12 +255,14 @@ def run_reference(args):
 def main():
     args = parse()
     if args.impl == "reference":
-        run_reference(args)
+        (run_reference_step if args.workload == "step" else run_reference)(args)
         return
-    if args.workload != "moe":
-        {"matvec": run_matvec, "gemm": run_gemm, "mla": run_mla, "head": run_head,
-         "step": run_step, "mxfp4": run_mxfp4}[args.workload](args)
-        return
+    {"moe": run_moe, "matvec": run_matvec, "gemm": run_gemm, "mla": run_mla, "head": run_head,
+     "step": run_step, "mxfp4": run_mxfp4}[args.workload](args)
+
+
+def run_moe(args):
+    """Config 1: one MoE FFN decode layer per step (48 seeded layers cycled)."""
     import numpy as np
     import torch
 
@@ -882,74 +891,400 @@ def run_head(args):
     ctx.close()
 
 
+# ------------------------------------------------------------------ config 4: the decode step
+STEP_SAMPLE_LAYERS = 2  # layers of the CPU sample (scaled to the model's 48)
+
+
+def host_step_model(cfg, layers: int, seed: int = 0):
+    """Config-4 weights on the host (numpy) for the CPU baseline: `layers`
+    layers at full shapes plus the vocabulary head, the synthetic
+    distributions of the GPU model (not the same draws: a timing sample; the
+    512 expert slots repeat 16 distinct ones and the head's rows a 4096-row
+    block, which changes no operation count)."""
+    import numpy as np
+
+    from oracle import pb_oracle
+
+    rng = np.random.default_rng(seed)
+
+    def bf(a):  # f32 -> bf16 bits, round to nearest even (finite inputs), in u32 arithmetic
+        u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+        return ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+
+    def q4(rows, cols):
+        s = rng.uniform(0.004, 0.02, (rows, cols // cfg.group)).astype(np.float32)
+        sb = bf(s)
+        b = bf(-8.0 * pb_oracle.bf16_bits_to_f32(sb) + rng.normal(0, 1e-3, s.shape))
+        return dict(packed=np.frombuffer(rng.bytes(rows * cols // 2), dtype=np.uint8).reshape(rows, cols // 2).copy(),
+                    s=sb.reshape(-1),
+                    b=b.reshape(-1), rows=rows, cols=cols)
+
+    def table(n):
+        offs, nbytes = pb_oracle.fixed_q4_layout(cfg.hidden, cfg.inter, cfg.group)
+        m = min(n, 16)
+        t = np.frombuffer(rng.bytes(m * nbytes), dtype=np.uint8).reshape(m, nbytes).copy()
+        for p, (rows, cols) in enumerate([(cfg.inter, cfg.hidden), (cfg.inter, cfg.hidden), (cfg.hidden, cfg.inter)]):
+            s = rng.uniform(0.004, 0.02, (m, rows * cols // cfg.group)).astype(np.float32)
+            sb = bf(s)
+            b = bf(-8.0 * pb_oracle.bf16_bits_to_f32(sb) + rng.normal(0, 1e-3, s.shape))
+            so, bo = int(offs[3 * p + 1]), int(offs[3 * p + 2])
+            t[:, so:so + sb.shape[1] * 2] = sb.view(np.uint8).reshape(m, -1)
+            t[:, bo:bo + b.shape[1] * 2] = b.view(np.uint8).reshape(m, -1)
+        return np.ascontiguousarray(np.tile(t, (n // m + 1, 1))[:n]), offs, nbytes
+
+    norm = lambda n: (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    out = []
+    for _ in range(layers):
+        experts, offs, nbytes = table(cfg.experts)
+        shared, _, _ = table(1)
+        out.append(dict(
+            q_a=q4(cfg.q_lora, cfg.hidden), kv_a=q4(cfg.latent + cfg.rope, cfg.hidden),
+            q_b=q4(cfg.heads * (cfg.nope + cfg.rope), cfg.q_lora), o_proj=q4(cfg.hidden, cfg.heads * cfg.v_dim),
+            q_a_norm=norm(cfg.q_lora), kv_a_norm=norm(cfg.latent), post_norm=norm(cfg.hidden),
+            in_norm=norm(cfg.hidden), w_uk=bf(rng.normal(0, 0.02, cfg.heads * cfg.nope * cfg.latent)),
+            w_uv=bf(rng.normal(0, 0.02, cfg.heads * cfg.v_dim * cfg.latent)),
+            router=bf(rng.normal(0, 0.02, cfg.experts * cfg.hidden)), gate=bf(rng.normal(0, 0.02, cfg.hidden)),
+            experts=experts, shared=shared[0], offs=offs, nbytes=nbytes,
+            lat=pb_oracle.bf16_bits_to_f32(bf(rng.standard_normal((cfg.context, cfg.latent), dtype=np.float32))),
+            rot=pb_oracle.bf16_bits_to_f32(bf(rng.standard_normal((cfg.context, cfg.rope), dtype=np.float32)))))
+    block = bf(rng.standard_normal((4096, cfg.hidden), dtype=np.float32) * np.float32(0.02))
+    head = np.ascontiguousarray(np.tile(block, (cfg.vocab // 4096 + 1, 1))[:cfg.vocab])
+    return out, head
+
+
+def cpu_step_chain(cfg, layers, head, x, position, threads):
+    """One token through the sampled layers and the head on the CPU oracle,
+    in the decode step's order (runtime/mod.rs:1432-2024, 2779-2940): returns
+    (seconds in the layers, seconds in the head)."""
+    import numpy as np
+
+    from oracle import pb_oracle as o
+
+    q4 = lambda P, v: o.q4_fma_matvec_bf16(P["packed"], np.ascontiguousarray(v, np.float32), P["s"], P["b"],
+                                           P["rows"], P["cols"], cfg.group, threads=threads)
+    bf = lambda a: o.bf16_bits_to_f32(o.f32_to_bf16_bits(np.asarray(a, np.float32)))
+    t0 = time.perf_counter()
+    xn = o.rms_norm(x, layers[0]["in_norm"], cfg.eps)
+    for L in layers:
+        qa = o.rms_norm(q4(L["q_a"], xn), L["q_a_norm"], cfg.eps)
+        kv = q4(L["kv_a"], xn)
+        kv[:cfg.latent] = o.rms_norm(kv[:cfg.latent], L["kv_a_norm"], cfg.eps)
+        q = q4(L["q_b"], qa).reshape(cfg.heads, cfg.nope + cfg.rope)
+        for h in range(cfg.heads):
+            q[h, cfg.nope:] = o.rope_interleaved_to_split_half(q[h, cfg.nope:], position, cfg.rope, cfg.theta)
+        L["lat"][position] = bf(kv[:cfg.latent])
+        L["rot"][position] = bf(o.rope_interleaved_to_split_half(kv[cfg.latent:], position, cfg.rope, cfg.theta))
+        attn = o.mla_absorbed_attention(q.reshape(-1), L["lat"][:position + 1], L["rot"][:position + 1], L["w_uk"],
+                                        L["w_uv"], cfg.heads, cfg.nope, cfg.rope, cfg.latent, cfg.v_dim)
+        h_row = x + q4(L["o_proj"], attn)
+        n = bf(o.rms_norm(h_row, L["post_norm"], cfg.eps))
+        out, _, _, _ = o.moe_layer(n[None, :], L["router"], L["experts"], L["offs"], L["nbytes"], cfg.experts,
+                                   cfg.top_k, cfg.inter, cfg.group, shared_slot=L["shared"], shared_gate_bits=L["gate"],
+                                   residual=h_row[None, :], threads=threads)
+        x = out[0]
+        xn = o.rms_norm(x, L["in_norm"], cfg.eps)
+    t1 = time.perf_counter()
+    o.head_topk(head, xn[None, :], cfg.candidates)
+    return t1 - t0, time.perf_counter() - t1
+
+
+def cpu_step_rate(cfg, batch, threads, model=None, reps=1):
+    """Tokens/s of the oracle chain for the 48-layer step: `threads` = 1 runs
+    one token at a time on one thread; more threads run min(batch, threads)
+    tokens concurrently (one token per thread, each oracle call on one
+    thread). Layer time is scaled from the sampled layers to cfg.layers."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    layers, head = model if model is not None else host_step_model(cfg, STEP_SAMPLE_LAYERS)
+    conc = 1 if threads <= 1 else max(1, min(batch, threads))
+    rng = np.random.default_rng(3)
+    xs = [rng.standard_normal(cfg.hidden).astype(np.float32) for _ in range(conc)]
+    cpu_step_chain(cfg, layers, head, xs[0], cfg.context - 1, 1)  # warm caches and code
+    walls = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        if conc == 1:
+            tl, th = cpu_step_chain(cfg, layers, head, xs[0], cfg.context - 1, 1)
+        else:
+            with ThreadPoolExecutor(max_workers=conc) as pool:
+                res = list(pool.map(lambda x: cpu_step_chain(cfg, layers, head, x, cfg.context - 1, 1), xs))
+            tl, th = max(r[0] for r in res), max(r[1] for r in res)
+        walls.append(time.perf_counter() - t0)
+        per_step = tl * cfg.layers / len(layers) + th  # seconds for conc tokens through the whole model
+    return dict(value=conc / per_step, unit="tok/s", cores=conc, kind="port", seconds=sum(walls), per_step_s=per_step,
+                sample=(f"{conc} token(s) on {conc} thread(s) through {len(layers)} of the {cfg.layers} layers "
+                        f"(context {cfg.context}) and the {cfg.vocab}-row head, layer time scaled x"
+                        f"{cfg.layers // len(layers)} (C++ oracle chain)"))
+
+
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference_step(args):
+    """The reference arm for the config-4 step: the oracle chain on all host
+    threads (one token per thread), each step a bounded sample."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import pb_oracle
+
+    from pb_b200 import decode
+
+    pb_oracle.build()
+    cfg = decode.StepConfig()
+    threads = os.cpu_count() or 1
+    model = host_step_model(cfg, STEP_SAMPLE_LAYERS)
+    cpu_step_rate(cfg, args.batch, threads, model=model, reps=max(1, min(args.warmup, 2)))  # warm-up samples
+    res = cpu_step_rate(cfg, args.batch, threads, model=model, reps=args.steps)
+    line = {
+        "impl": "reference", "metric": STEP_METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["per_step_s"] * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; config-4 shapes and distributions)",
+        "config": {"workload": "config4 decode step", "batch": args.batch, "layers": cfg.layers,
+                   "context": cfg.context, "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
+                   "vocab": cfg.vocab},
+        "cpu_baseline": {"value": res["value"], "unit": "tok/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"], "cpu": cpu_model_name()},
+        "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference = C++ restatement of pb's Rust CPU path (Rust toolchain absent; Metal GPU path "
+                "unavailable on this box)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+STEP_METRIC = "MoE decode tok/s (config 4: 48-layer MLA + 512-expert top-10 MoE decode step, context 8192)"
+
+
 def run_step(args):
-    """Config 4 on one GPU: a full decode step of the 48-layer synthetic model
-    (MLA attention at context 8192 + 512-expert top-10 MoE per layer, vocab
-    head [151936 x 2048] + top-64) for --batch sequences, each attending over
-    8192 cached positions; batches 1, 8 and 32 listed."""
+    """Config 4: the full 48-layer decode step for --batch sequences at
+    position 8191 of their 8192-row caches; expert and vocabulary parallel
+    under torchrun."""
+    import numpy as np
     import torch
 
     from pb_b200 import capi, decode
 
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
     cfg = decode.StepConfig()
-    ctx = capi.Context(0)
-    model = decode.Model(cfg, seed=4)
-    s = torch.cuda.Stream()
-    cases, head = [], None
-    for B in ([args.batch] if args.only_batch else sorted({1, 8, 32, args.batch})):
-        caches = decode.Caches(cfg, B, seed=B)
-        step = decode.DecodeStep(ctx, model, caches, B, [cfg.context - 1] * B)
-        x0 = torch.randn(B, cfg.hidden, generator=torch.Generator("cuda").manual_seed(B), device="cuda")
+    B = args.batch
+    ctx = capi.Context(local)
+    model = decode.Model(cfg, seed=4, ep=(rank, world) if world > 1 else None)
+    caches = decode.Caches(cfg, B, seed=B)
+    step = decode.DecodeStep(ctx, model, caches, B, [cfg.context - 1] * B)
+    x0 = torch.randn(B, cfg.hidden, generator=torch.Generator("cuda").manual_seed(11), device=dev)
+    s = torch.cuda.Stream(dev)
+
+    # one recorded step: the routes give the experts each layer reads on this rank
+    with torch.cuda.stream(s):
         step.set_input(x0)
-        with torch.cuda.stream(s):
-            step.launch(stream=s, record_routes=True)
+        step.launch(stream=s, record_routes=True)
+        step.finish(stream=s)
+    s.synchronize()
+    assert ctx.device_status(stream=s) == 0
+    routes = step.route_ids.cpu().numpy()
+    lo, cnt = model.expert_range if model.expert_range is not None else (0, cfg.experts)
+    uniq = [len({int(e) for e in routes[i].reshape(-1) if lo <= e < lo + cnt}) for i in range(cfg.layers)]
+    mean_u = float(np.mean(uniq))
+    slot = int(model.layers[0].moe.layout.expert_bytes)
+    kv_bytes = cfg.layers * B * cfg.context * (cfg.latent + cfg.rope) * 2
+    step_bytes = step.step_weight_bytes() + sum(uniq) * slot + kv_bytes + B * cfg.hidden * 4
+
+    # the step as one CUDA graph (the head's cross-rank merge follows it)
+    with torch.cuda.stream(s):
+        step.launch(stream=s)
         s.synchronize()
-        U = step.unique_experts()
-        steps = max(3, args.steps // 50) if B == args.batch else 5
-        ms, n, clocks = _graph_time([lambda: (step.set_input(x0), step.launch(stream=s))], s, steps, args.warmup)
-        byts = step.bytes_per_step(U)
-        cases.append({"batch": B, "ms": ms, "tok_s": B / (ms / 1e3), "gbs": byts / (ms / 1e3) / 1e9,
-                      "unique_experts_mean": U})
-        if B == args.batch:
-            hx = x0.cpu().pin_memory()
-            hi = torch.empty(B, cfg.candidates, dtype=torch.int32).pin_memory()
-            hv = torch.empty(B, cfg.candidates).pin_memory()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            step.launch(stream=s)
 
-            def e2e():
-                step.x.copy_(hx, non_blocking=True)
-                step.launch(stream=s)
-                hi.copy_(step.ids, non_blocking=True)
-                hv.copy_(step.vals, non_blocking=True)
+    def one_step(copy_in=None):
+        if copy_in is not None:
+            step.x.copy_(copy_in, non_blocking=True)
+        else:
+            step.x.copy_(x0)
+        graph.replay()
+        step.finish(stream=s)
 
-            ems = _e2e_time(e2e, s, 5)
-            head = dict(ms=ms, steps=n, clocks=clocks, bytes=byts, e2e_ms=ems, B=B, U=U,
-                        launches=step.launches_per_step())
-        del step, caches
-        torch.cuda.empty_cache()
-    peak, kind = measured_peaks()
-    gbs = head["bytes"] / (head["ms"] / 1e3) / 1e9
-    _emit({
-        "metric": f"full decode step tok/s (config 4: 48 layers MLA + MoE, context 8192, batch {head['B']})",
-        "value": head["B"] / (head["ms"] / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": head["steps"],
-        "warmup": max(3, args.warmup), "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded; random-init 48-layer MLA + MoE model, random bf16 caches)",
-        "config": {"workload": "config4 full decode step", "layers": cfg.layers, "hidden": cfg.hidden,
-                   "experts": cfg.experts, "top_k": cfg.top_k, "q_lora": cfg.q_lora, "heads": cfg.heads,
-                   "context": cfg.context, "vocab": cfg.vocab, "head_top_k": cfg.candidates, "batch": head["B"],
-                   "l2": "inputs larger than L2: 45 GB of weights and the caches read once per step",
-                   "graph": "one CUDA graph per step"},
-        "e2e": {"value": head["B"] / (head["e2e_ms"] / 1e3), "unit": "tok/s",
-                "h2d_bytes_per_step": head["B"] * cfg.hidden * 4, "d2h_bytes_per_step": head["B"] * cfg.candidates * 8,
-                "steps": 5},
-        "roofline": {"bound": "hbm", "kernel": "decode step (all kernels)", "achieved": gbs, "peak": peak,
-                     "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind, "traffic": None,
-                     "algorithmic_bytes_per_launch": head["bytes"], "launch_ms": head["ms"],
-                     "unique_experts_mean": head["U"]},
-        "cases": cases, "gpu_launches": head["steps"] * head["launches"], "clocks": head["clocks"],
-        "cpu_baseline": None,
-    })
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    W, K = max(3, args.warmup), args.steps
+    with torch.cuda.stream(s):
+        for _ in range(W):
+            one_step()
+    s.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(s):
+            ev0.record(s)
+            for _ in range(K):
+                one_step()
+            ev1.record(s)
+        s.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / K)
+    clock_summary = clocks.summary()
+    assert ctx.device_status(stream=s) == 0
+    value = B / (ms / 1e3)
+
+    # end to end with host buffers: embeddings in, candidates out, every step
+    hx = x0.cpu().pin_memory()
+    hi = torch.empty(B, cfg.candidates, dtype=torch.int32).pin_memory()
+    hv = torch.empty(B, cfg.candidates).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(K):
+            one_step(copy_in=hx)
+            hi.copy_(step.ids, non_blocking=True)
+            hv.copy_(step.vals, non_blocking=True)
+        e1.record(s)
+    s.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K)
+    assert ctx.device_status(stream=s) == 0
+
+    # per-call timing: one step launched call by call with events between the
+    # calls (and the MoE layer's phase events on one GPU); serialised, so the
+    # shares are the figure, not the sum
+    names_ev = []
+
+    def mark(name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(s)
+        names_ev.append((name, e))
+
+    moe_ev = []
+    if world == 1:
+        moe_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(cfg.layers)]
+        for row in moe_ev:
+            for e in row:
+                e.record(s)
+        s.synchronize()
+    handles = [C_void_p_array(r) for r in moe_ev]
+    with torch.cuda.stream(s):
+        step.x.copy_(x0)
+        torch.cuda._sleep(20_000_000)
+        step.launch(stream=s, mark=mark, moe_events=(lambda i: handles[i][0]) if moe_ev else None)
+    s.synchronize()
+    tot, cnt_l = {}, {}
+    for (n0, a), (_, b) in zip(names_ev[:-1], names_ev[1:]):
+        if n0 == "moe_layer" and moe_ev:
+            continue
+        tot[n0] = tot.get(n0, 0.0) + a.elapsed_time(b)
+        cnt_l[n0] = cnt_l.get(n0, 0) + 1
+    for row in moe_ev:
+        for k, n in enumerate(["moe_router", "moe_gate_up", "moe_down", "moe_combine"]):
+            tot[n] = tot.get(n, 0.0) + row[k].elapsed_time(row[k + 1])
+            cnt_l[n] = cnt_l.get(n, 0) + 1
+    L0 = model.layers[0]
+    H, Bf = cfg.hidden, B * 4
+    mla_bytes = B * cfg.context * (cfg.latent + cfg.rope) * 2 + 2 * cfg.heads * cfg.latent * (cfg.nope + cfg.v_dim)
+    launch_bytes = {
+        "q_a+kv_a": L0.q_a.nbytes() + L0.kv_a.nbytes() + Bf * H + Bf * (cfg.q_lora + cfg.latent + cfg.rope),
+        "q_b": L0.q_b.nbytes() + Bf * cfg.q_lora + Bf * cfg.heads * (cfg.nope + cfg.rope),
+        "mla_decode": mla_bytes + Bf * cfg.heads * (cfg.nope + cfg.rope + cfg.v_dim),
+        "o_proj": L0.o_proj.nbytes() + Bf * (cfg.heads * cfg.v_dim + 2 * H),
+        "moe_router": cfg.experts * H * 2 + H * 2 + Bf * H + B * H * 2,
+        "moe_gate_up": (mean_u + 1) * 2 * (524_288 + 2 * 32_768) + B * H * 2,
+        "moe_down": (mean_u + 1) * (524_288 + 2 * 32_768),
+        "head": int(model.head.numel()) * 2 + Bf * H,
+    }
+    per_launch = {n: tot[n] / cnt_l[n] for n in tot}
+    dominant = max((n for n in tot if n in launch_bytes), key=lambda n: tot[n])
+    achieved = launch_bytes[dominant] / (per_launch[dominant] / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+    serial = sum(tot.values())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            from oracle import pb_oracle
+
+            pb_oracle.build()
+            hm = host_step_model(cfg, STEP_SAMPLE_LAYERS)
+            one = cpu_step_rate(cfg, B, 1, model=hm)
+            allt = cpu_step_rate(cfg, B, os.cpu_count() or 1, model=hm)
+            cpu = {"value": allt["value"], "unit": "tok/s", "cores": allt["cores"], "kind": "port",
+                   "sample": allt["sample"], "cpu": cpu_model_name(),
+                   "single_thread": {"value": one["value"], "cores": 1, "sample": one["sample"]}}
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {exc}"}
+
+    if rank == 0:
+        line = {
+            "metric": STEP_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; random-init 48-layer MLA + MoE model of the config-4 architecture, "
+                    "random bf16 caches)",
+            "config": {"workload": "config4 decode step", "batch": B, "layers": cfg.layers, "hidden": cfg.hidden,
+                       "experts": cfg.experts, "top_k": cfg.top_k, "q_lora": cfg.q_lora, "heads": cfg.heads,
+                       "context": cfg.context, "vocab": cfg.vocab, "head_top_k": cfg.candidates,
+                       "l2": "inputs larger than L2: 45 GB of weights and the caches read once per step",
+                       "parallelism": (f"ep{world}: experts {cfg.experts // world}/GPU and the head {cfg.vocab // world}"
+                                       " rows/GPU, NVLink P2P combine, NCCL candidate all-gather"
+                                       if world > 1 else "single GPU"),
+                       "graph": "one CUDA graph per step"},
+            "e2e": {"value": B / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * cfg.hidden * 4,
+                    "d2h_bytes_per_step": B * cfg.candidates * 8, "steps": K},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": STEP_NCU_TRAFFIC.get(dominant),
+                         "traffic_source": STEP_NCU_SOURCE.get(dominant),
+                         "algorithmic_bytes_per_launch": launch_bytes[dominant],
+                         "launch_ms": per_launch[dominant], "share_of_serial": tot[dominant] / serial},
+            "step": {"algorithmic_bytes_per_gpu": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
+                     "frac_of_peak": step_bytes / (ms / 1e3) / 1e9 / peak, "unique_experts_per_layer": mean_u,
+                     "kernel_ms_per_step": {n: round(v, 4) for n, v in sorted(tot.items(), key=lambda kv: -kv[1])},
+                     "kernel_ms_serial_sum": serial},
+            "gpu_launches": K * step.launches_per_step(),
+            "clocks": clock_summary,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
     ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the step's kernels
+# from one ncu capture (config-4 shapes, batch 8); filled per kernel captured
+STEP_NCU_TRAFFIC: dict = {}
+STEP_NCU_SOURCE: dict = {}
 
 
 def C_void_p_array(events):

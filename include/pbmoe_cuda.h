@@ -449,11 +449,13 @@ typedef struct pbmoe_ep_shard {
  * weights->shared_expert (and its gate) is given on exactly one rank. Output
  * (and next_normed) is the full layer, identical on every rank. A peer that
  * does not arrive within the timeout latches PBMOE_DEV_ERR_PEER_TIMEOUT
- * (pbmoe_device_status) and its partial counts as zero. */
+ * (pbmoe_device_status) and its partial counts as zero. debug (nullable) is
+ * pbmoe_moe_layer's: router logits, every token's route ids and weights (the
+ * same on every rank), the normalised input; phase_events is not taken here. */
 PBMOE_API int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
                                  const pbmoe_ep_shard* shard, const void* x, pbmoe_dtype x_dtype, const void* residual,
                                  void* out, pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight,
-                                 void* next_normed, void* stream);
+                                 void* next_normed, const pbmoe_moe_debug* debug, void* stream);
 
 /* The MoE decode layer on HOST rows, as the reference's facade takes them
  * (submit_scheduled_expert_command, runtime/mod.rs:922-961: normed and

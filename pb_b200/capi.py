@@ -171,7 +171,7 @@ def load():
         L.pbmoe_ep_buffer.restype = vp
         L.pbmoe_ep_buffer.argtypes = [vp]
         L.pbmoe_ep_moe_layer.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), C.POINTER(EpShard), vp, i32,
-                                         vp, vp, i32, u32, vp, vp, vp]
+                                         vp, vp, i32, u32, vp, vp, C.POINTER(MoeDebug), vp]
         L.pbmoe_head_reserve.argtypes = [vp, u32, u32, u32]
         L.pbmoe_head_topk.argtypes = [vp, C.POINTER(Head), vp, i32, u32, u32, vp, vp, vp, vp, vp, vp]
         L.pbmoe_head_merge.argtypes = [vp, vp, vp, vp, u32, u32, u32, vp, vp, vp]
@@ -427,11 +427,12 @@ class Context:
         self.check(self.lib.pbmoe_ep_set_peers(self.h, C.cast(arr, C.c_void_p)))
 
     def ep_moe_layer(self, config, weights: MoeWeights, shard: EpShard, x, out, tokens, residual=None,
-                     next_norm_weight=None, next_normed=None, stream=None):
+                     next_norm_weight=None, next_normed=None, debug: MoeDebug | None = None, stream=None):
         _same_dtype(out, residual, next_normed)
         self.check(self.lib.pbmoe_ep_moe_layer(
             self.h, C.byref(config), C.byref(weights), C.byref(shard), _ptr(x), _dtype_code(x), _ptr(residual),
-            _ptr(out), _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed), self.stream_ptr(stream)))
+            _ptr(out), _dtype_code(out), tokens, _ptr(next_norm_weight), _ptr(next_normed),
+            C.byref(debug) if debug is not None else None, self.stream_ptr(stream)))
 
     def device_status(self, clear=True, stream=None) -> int:
         v = C.c_uint32()

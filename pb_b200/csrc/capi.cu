@@ -1001,7 +1001,7 @@ int pbmoe_ep_set_peers(pbmoe_ctx* ctx, void* const* buffers) {
 int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_weights* w,
                        const pbmoe_ep_shard* shard, const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
                        pbmoe_dtype out_dtype, uint32_t tokens, const float* next_norm_weight, void* next_normed,
-                       void* stream) {
+                       const pbmoe_moe_debug* debug, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
     int rc = check_moe_config(ctx, c);
     if (rc) return rc;
@@ -1031,8 +1031,10 @@ int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_mo
     ep.world = ctx->ep_world;
     ep.max_tokens = ctx->ep_max_tokens;
     ep.timeout_ns = shard->timeout_us ? uint64_t(shard->timeout_us) * 1000ull : 2000000000ull;
+    if (debug && debug->phase_events)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "ep moe layer: phase events are not taken here");
     return moe_layer_impl(ctx, c, w, x, x_dtype, residual, out, out_dtype, tokens, next_norm_weight, next_normed,
-                          nullptr, stream, shard->expert_begin, shard->expert_count, &ep);
+                          debug, stream, shard->expert_begin, shard->expert_count, &ep);
 }
 
 // ---------------------------------------------------------------- vocab head

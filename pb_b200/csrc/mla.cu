@@ -11,7 +11,7 @@
 // with scale = 1/sqrt(nope + rope) (store.rs:1262) and k_rope already rotated
 // when the cache was written (runtime/mod.rs:2906-2913).
 //
-// Four launches:
+// Three launches:
 //   1. mla_absorb_kernel   q_lat for every (sequence, head), W_UK read once;
 //                          writes Q' = [q_lat | q_rope] * scale * log2(e) (f32).
 //   2. mla_attn_kernel     one CTA per (KV split, sequence): every 64-token
@@ -21,8 +21,11 @@
 //                          bf16 hi + lo so scores keep ~16 mantissa bits),
 //                          online softmax in base 2, O += P C with P in bf16.
 //                          Writes the split's (max, sum, O[16 x 512]).
-//   3. mla_combine_kernel  merges the splits of each (sequence, head) -> ctx.
-//   4. mla_out_kernel      out = W_UV ctx, W_UV read once for the batch.
+//   3. mla_out_kernel      one CTA per (head, sequence): merges the splits'
+//                          partials into ctx (in shared memory), then
+//                          out = W_UV[h] ctx.
+// The split plan keeps batch x splits within one wave of SMs (the attention
+// kernel runs one CTA per SM).
 // Shapes: 16 heads, latent 512, rope 64, v 128, nope <= 128, batch <= 32.
 
 #include "common.cuh"
@@ -366,108 +369,104 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
     }
 }
 
-// ---------------------------------------------------------------- 3. combine
-// grid (heads, batch, latent/128), 128 threads = latent columns:
-// ctx[b][h][c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s
-__global__ void __launch_bounds__(128) mla_combine_kernel(const float* __restrict__ partial, uint32_t splits,
-                                                           float* __restrict__ ctx) {
-    __shared__ float wsc[1024];
-    __shared__ float red[4];
+// ---------------------------------------------------------------- 3. merge + output
+// grid (heads, batch), 256 threads. The splits of (sequence b, head h) are
+// merged as ctx[c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s into
+// shared memory, then warp w computes out rows d = w, w + 8, ... of
+// W_UV[h] ctx (16 rows per warp, 16-byte weight loads; W_UV[h] is read from
+// L2 by the batch's CTAs of head h after the first brings it in).
+constexpr uint32_t kOutThreads = 256;
+constexpr uint32_t kOutMaxSplits = 1024;
+template <typename OT>
+__global__ void __launch_bounds__(kOutThreads) mla_merge_out_kernel(const float* __restrict__ partial,
+                                                                     uint32_t splits, const uint16_t* __restrict__ w_uv,
+                                                                     OT* __restrict__ out) {
+    __shared__ float wsc[kOutMaxSplits];
+    __shared__ __align__(16) float cs[kMlaLatent];
+    __shared__ float red[kOutThreads / 32];
+    const uint32_t h = blockIdx.x, b = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // W_UV rows do not depend on the earlier kernels: the first rows' loads
+    // are issued before waiting for them
+    constexpr uint32_t kRowsPerWarp = kMlaV / (kOutThreads / 32);  // 16
+    const uint16_t* wrow0 = w_uv + (static_cast<size_t>(h) * kMlaV + warp) * kMlaLatent + lane * 16;
+    uint4 wa[2] = {__ldg(reinterpret_cast<const uint4*>(wrow0)), __ldg(reinterpret_cast<const uint4*>(wrow0 + 8))};
     pdl_wait();
     pdl_launch_dependents();
-    const uint32_t h = blockIdx.x, b = blockIdx.y, c = blockIdx.z * 128 + threadIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* base = partial + static_cast<size_t>(b) * splits * kMlaHeads * kMlaPartialFloats +
                         h * kMlaPartialFloats;
     const size_t stride = static_cast<size_t>(kMlaHeads) * kMlaPartialFloats;
     const float NEG_INF = -__int_as_float(0x7f800000);
     float M = NEG_INF;
-    for (uint32_t s = threadIdx.x; s < splits; s += blockDim.x) M = fmaxf(M, __ldcg(base + s * stride));
+    for (uint32_t sp = threadIdx.x; sp < splits; sp += blockDim.x) M = fmaxf(M, __ldcg(base + sp * stride));
     M = warp_max(M);
     if (lane == 0) red[warp] = M;
     __syncthreads();
-    M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    M = red[0];
+#pragma unroll
+    for (int w = 1; w < kOutThreads / 32; ++w) M = fmaxf(M, red[w]);
     float tot = 0.f;
-    for (uint32_t s = threadIdx.x; s < splits; s += blockDim.x) {
-        const float m = __ldcg(base + s * stride);
+    for (uint32_t sp = threadIdx.x; sp < splits; sp += blockDim.x) {
+        const float m = __ldcg(base + sp * stride);
         const float w = (m == NEG_INF) ? 0.f : exp2f(m - M);
-        wsc[s] = w;
-        tot += w * __ldcg(base + s * stride + 1);
+        wsc[sp] = w;
+        tot += w * __ldcg(base + sp * stride + 1);
     }
     tot = warp_sum(tot);
-    __syncthreads();
+    __syncthreads();  // everyone has read red[] (M) and written wsc[]
     if (lane == 0) red[warp] = tot;
     __syncthreads();
-    tot = red[0] + red[1] + red[2] + red[3];
+    tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kOutThreads / 32; ++w) tot += red[w];
     const float inv = tot > 0.f ? 1.0f / tot : 0.f;
-    const float* oc = base + 2 + c;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t s = 0;
-    for (; s + 8 <= splits; s += 8) {
-        float v[8];
+    // context: thread c of 256 takes columns c and c + 256
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __ldcg(oc + (s + j) * stride);
+    for (int half = 0; half < 2; ++half) {
+        const uint32_t c = threadIdx.x + half * kOutThreads;
+        const float* oc = base + 2 + c;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t sp = 0;
+        for (; sp + 8 <= splits; sp += 8) {
+            float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j & 3] = fmaf(wsc[s + j], v[j], acc[j & 3]);
-    }
-    for (; s < splits; ++s) acc[0] = fmaf(wsc[s], __ldcg(oc + s * stride), acc[0]);
-    ctx[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaLatent + c] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * inv;
-}
-
-// ---------------------------------------------------------------- 4. output
-// grid (heads, v/16), 256 threads: warp w -> rows d = 16*blockIdx.y + 2w, +1;
-// W_UV rows are read once (all loads in flight) and dotted with every
-// sequence's context.
-template <typename OT>
-__global__ void __launch_bounds__(256) mla_out_kernel(const float* __restrict__ ctx, uint32_t batch,
-                                                       const uint16_t* __restrict__ w_uv, OT* __restrict__ out) {
-    extern __shared__ __align__(16) float cs[];  // [batch][latent]
-    const uint32_t h = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float wf[2][16];
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(oc + (sp + j) * stride);
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const uint32_t d = blockIdx.y * 16 + warp * 2 + r;
-        const uint16_t* wrow = w_uv + (static_cast<size_t>(h) * kMlaV + d) * kMlaLatent + lane * 16;
-        const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(wrow));
-        const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(wrow + 8));
-        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            wf[r][2 * i] = bf16_bits_to_f32(wv[i] & 0xffffu);
-            wf[r][2 * i + 1] = bf16_bits_to_f32(wv[i] >> 16);
+            for (int j = 0; j < 8; ++j) acc[j & 3] = fmaf(wsc[sp + j], v[j], acc[j & 3]);
         }
-    }
-    // W_UV does not depend on the earlier kernels: its loads are issued
-    // before waiting for them
-    pdl_wait();
-    pdl_launch_dependents();
-    for (uint32_t i = threadIdx.x; i < batch * kMlaLatent / 4; i += blockDim.x) {
-        const uint32_t bb = i / (kMlaLatent / 4), c4 = i % (kMlaLatent / 4);
-        reinterpret_cast<float4*>(cs)[i] =
-            __ldcg(reinterpret_cast<const float4*>(ctx + (static_cast<size_t>(bb) * kMlaHeads + h) * kMlaLatent) + c4);
+        for (; sp < splits; ++sp) acc[0] = fmaf(wsc[sp], __ldcg(oc + sp * stride), acc[0]);
+        cs[c] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * inv;
     }
     __syncthreads();
-    for (uint32_t bb = 0; bb < batch; ++bb) {
-        const float4* c4 = reinterpret_cast<const float4*>(cs + bb * kMlaLatent + lane * 16);
-        float acc[2] = {0.f, 0.f};
+    // out rows: warp w takes d = w + 8 i; lane covers 16 latent columns
+    float cv[16];
+    {
+        const float4* c4 = reinterpret_cast<const float4*>(cs + lane * 16);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float4 v = c4[i];
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                acc[r] = fmaf(wf[r][4 * i], v.x, acc[r]);
-                acc[r] = fmaf(wf[r][4 * i + 1], v.y, acc[r]);
-                acc[r] = fmaf(wf[r][4 * i + 2], v.z, acc[r]);
-                acc[r] = fmaf(wf[r][4 * i + 3], v.w, acc[r]);
-            }
+            cv[4 * i] = v.x, cv[4 * i + 1] = v.y, cv[4 * i + 2] = v.z, cv[4 * i + 3] = v.w;
         }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const float v = warp_sum(acc[r]);
-            if (lane == 0)
-                store_act(out, (static_cast<size_t>(bb) * kMlaHeads + h) * kMlaV + blockIdx.y * 16 + warp * 2 + r, v);
+    }
+    for (uint32_t i = 0; i < kRowsPerWarp; ++i) {
+        const uint32_t d = warp + i * (kOutThreads / 32);
+        uint4 wn[2] = {wa[0], wa[1]};
+        if (i + 1 < kRowsPerWarp) {  // next row in flight
+            const uint16_t* wr = w_uv + (static_cast<size_t>(h) * kMlaV + d + kOutThreads / 32) * kMlaLatent + lane * 16;
+            wn[0] = __ldg(reinterpret_cast<const uint4*>(wr));
+            wn[1] = __ldg(reinterpret_cast<const uint4*>(wr + 8));
         }
+        const uint32_t wv[8] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w, wa[1].x, wa[1].y, wa[1].z, wa[1].w};
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            acc = fmaf(bf16_bits_to_f32(wv[q] & 0xffffu), cv[2 * q], acc);
+            acc = fmaf(bf16_bits_to_f32(wv[q] >> 16), cv[2 * q + 1], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) store_act(out, (static_cast<size_t>(b) * kMlaHeads + h) * kMlaV + d, acc);
+        wa[0] = wn[0];
+        wa[1] = wn[1];
     }
 }
 
@@ -478,19 +477,23 @@ bool mla_shape_supported(uint32_t heads, uint32_t rope, uint32_t latent, uint32_
     return heads == kMlaHeads && rope == kMlaRope && latent == kMlaLatent && v_dim == kMlaV;
 }
 
+// Splits of the longest cache such that batch x splits CTAs fill at most one
+// wave of SMs (one attention CTA per SM), each split at least one 64-token
+// tile; a split need not be a whole number of tiles (the last tile of a
+// split is masked).
 void mla_plan_splits(const MlaLaunch& a, int num_sms, uint32_t& split_tokens, uint32_t& splits) {
     uint32_t lmax = 1;
     for (uint32_t b = 0; b < a.batch; ++b) lmax = a.seqs.len[b] > lmax ? a.seqs.len[b] : lmax;
-    const uint64_t per_sm = (static_cast<uint64_t>(lmax) * a.batch + num_sms - 1) / num_sms;
-    uint64_t st = (per_sm + kMlaTile - 1) / kMlaTile * kMlaTile;
+    uint32_t want = static_cast<uint32_t>(num_sms) / (a.batch ? a.batch : 1);
+    if (want < 1) want = 1;
+    uint32_t st = (lmax + want - 1) / want;
     if (st < kMlaTile) st = kMlaTile;
-    split_tokens = static_cast<uint32_t>(st);
-    splits = static_cast<uint32_t>((lmax + st - 1) / st);
+    split_tokens = st;
+    splits = (lmax + st - 1) / st;
 }
 
 uint32_t mla_max_splits(uint32_t max_batch, int num_sms) {
-    // splits <= lmax / split_tokens + 1 <= num_sms / batch + 1 (split_tokens >= lmax * batch / num_sms)
-    return static_cast<uint32_t>(num_sms) / (max_batch ? max_batch : 1) + 2;
+    return static_cast<uint32_t>(num_sms) / (max_batch ? max_batch : 1) + 1;
 }
 
 cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
@@ -512,23 +515,13 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     if ((e = launch_pdl_kernel(mla_attn_kernel, dim3(a.splits, a.batch), dim3(kMlaWarps * 32), kMlaSmem, s, a.qp,
                                a.seqs, a.split_tokens, a.splits, a.partial)) != cudaSuccess)
         return e;
-    if ((e = launch_pdl_kernel(mla_combine_kernel, dim3(kMlaHeads, a.batch, kMlaLatent / 128), dim3(128), 0, s,
-                               a.partial, a.splits, a.ctx)) != cudaSuccess)
-        return e;
-    const size_t osm = static_cast<size_t>(a.batch) * kMlaLatent * sizeof(float);
-    if (a.out_dtype == PBMOE_F32) {
-        if ((e = cudaFuncSetAttribute(mla_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(osm))) != cudaSuccess)
-            return e;
-        return launch_pdl_kernel(mla_out_kernel<float>, dim3(kMlaHeads, kMlaV / 16), dim3(256), osm, s, a.ctx,
-                                 a.batch, a.w_uv, static_cast<float*>(a.out));
-    } else {
-        if ((e = cudaFuncSetAttribute(mla_out_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(osm))) != cudaSuccess)
-            return e;
-        return launch_pdl_kernel(mla_out_kernel<uint16_t>, dim3(kMlaHeads, kMlaV / 16), dim3(256), osm, s, a.ctx,
-                                 a.batch, a.w_uv, static_cast<uint16_t*>(a.out));
-    }
+    if (a.splits > kOutMaxSplits) return cudaErrorInvalidValue;
+    const dim3 og(kMlaHeads, a.batch);
+    if (a.out_dtype == PBMOE_F32)
+        return launch_pdl_kernel(mla_merge_out_kernel<float>, og, dim3(kOutThreads), 0, s, a.partial, a.splits, a.w_uv,
+                                 static_cast<float*>(a.out));
+    return launch_pdl_kernel(mla_merge_out_kernel<uint16_t>, og, dim3(kOutThreads), 0, s, a.partial, a.splits, a.w_uv,
+                             static_cast<uint16_t*>(a.out));
 }
 
 }  // namespace pbmoe

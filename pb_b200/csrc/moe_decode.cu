@@ -759,6 +759,10 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     __shared__ uint32_t missing;
     const uint32_t t = blockIdx.x;
     pdl_wait();
+    // every CTA of this grid is resident: the next layer's first kernel may be
+    // scheduled now and prefetch its weights while the combine runs (it reads
+    // this kernel's outputs only after its own griddepcontrol.wait)
+    pdl_launch_dependents();
     if (threadIdx.x < K) {
         const uint32_t e = __ldcg(ws.route_ids + static_cast<size_t>(t) * K + threadIdx.x);
         wsh[threadIdx.x] = (e >= e_lo && e < e_hi) ? __ldcg(ws.route_w + static_cast<size_t>(t) * K + threadIdx.x)

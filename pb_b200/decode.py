@@ -31,9 +31,15 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import contextlib
+
 import torch
 
 from . import capi, synth
+
+
+def _null():
+    return contextlib.nullcontext()
 
 
 @dataclass
@@ -76,7 +82,12 @@ class Q4:
 
 
 class Layer:
-    def __init__(self, cfg: StepConfig, seed: int, device="cuda"):
+    """One layer's weights. With `experts` = (begin, count) only that expert
+    shard is kept (every rank generates the same full table from the same seed
+    and keeps its slots), and `shared` says whether this rank holds the shared
+    expert and its gate (expert parallelism: exactly one rank does)."""
+
+    def __init__(self, cfg: StepConfig, seed: int, device="cuda", experts=None, shared=True):
         g = synth.gen(device, seed)
         H, G = cfg.hidden, cfg.group
         self.q_a = Q4(cfg.q_lora, H, G, g, device)
@@ -90,6 +101,12 @@ class Layer:
         self.w_uv = synth.normal_bf16((cfg.heads, cfg.v_dim, cfg.latent), 0.02, g, device)
         self.moe = synth.MoeLayerWeights(device, seed + 7919, hidden=H, num_experts=cfg.experts,
                                          intermediate=cfg.inter, group=G)
+        if experts is not None:
+            b, n = experts
+            self.moe.experts = self.moe.experts[b:b + n].clone()
+            if not shared:
+                self.moe.shared, self.moe.shared_gate = None, None
+            torch.cuda.empty_cache()
 
     def nbytes(self):
         """Weight bytes a decode step reads for this layer, before experts."""
@@ -100,12 +117,28 @@ class Layer:
 
 
 class Model:
-    def __init__(self, cfg: StepConfig, seed=0, device="cuda"):
+    """The synthetic model. With ep = (rank, world) this rank keeps expert
+    shard rank of every layer (the shared expert on rank 0) and vocabulary
+    shard rank of the head (rows [head_base, head_base + head rows)), the
+    expert- and vocabulary-parallel layout of a multi-GPU step."""
+
+    def __init__(self, cfg: StepConfig, seed=0, device="cuda", ep=None):
+        from . import ep as ep_host
+
         self.cfg = cfg
-        self.layers = [Layer(cfg, seed + 1000 * i, device) for i in range(cfg.layers)]
+        rank, world = ep if ep is not None else (0, 1)
+        self.rank, self.world = rank, world
+        self.expert_range = capi.ep_expert_range(cfg.experts, rank, world) if ep is not None else None
+        self.layers = [Layer(cfg, seed + 1000 * i, device, experts=self.expert_range, shared=rank == 0)
+                       for i in range(cfg.layers)]
         g = synth.gen(device, seed + 17)
         self.head = synth.normal_bf16((cfg.vocab, cfg.hidden), 0.02, g, device)
         self.final_norm = (1.0 + 0.1 * torch.randn(cfg.hidden, generator=g, device=device)).float()
+        self.head_base = 0
+        if ep is not None:
+            self.head_base, rows = ep_host.vocab_ranges(cfg.vocab, world)[rank]
+            self.head = self.head[self.head_base:self.head_base + rows].clone()
+            torch.cuda.empty_cache()
 
 
 class Caches:
@@ -151,12 +184,25 @@ class DecodeStep:
         self.vals = torch.zeros(B, cfg.candidates, **f32)
         self.mla_cfg = capi.mla_config(cfg.heads, cfg.nope, cfg.rope, cfg.latent, cfg.v_dim)
         self.moe_cfg = capi.moe_config(model.layers[0].moe.layout, cfg.experts, cfg.top_k)
+        self.ep = model.expert_range is not None
+        self.shard = capi.EpShard(model.expert_range[0], model.expert_range[1], 0) if self.ep else None
+        K = cfg.candidates
+        # this rank's candidate lists (vocabulary shard) and, under expert
+        # parallelism, every rank's after the all-gather
+        self.keys = torch.zeros(B, K, device=dev, dtype=torch.int32)
+        self.lids = torch.zeros(B, K, device=dev, dtype=torch.int32)
+        self.lvals = torch.zeros(B, K, **f32)
+        self.gathered = torch.zeros(model.world, 3, B, K, device=dev, dtype=torch.int32) if self.ep else None
         self.moe_w = []
         for l in model.layers:  # the post-attention norm runs inside the MoE layer's router kernel
             w = l.moe.c_weights()
             w.input_norm_weight = l.post_norm.data_ptr()
             self.moe_w.append(w)
         ctx.reserve(B, self.moe_cfg)
+        if self.ep:
+            from . import ep as ep_host
+
+            ep_host.connect(ctx, max_tokens=B, hidden=H)
         ctx.mla_reserve(self.mla_cfg, B)
         ctx.rope_reserve(cfg.context, cfg.rope, cfg.theta)
         ctx.head_reserve(B, cfg.vocab, cfg.candidates)
@@ -165,31 +211,43 @@ class DecodeStep:
         """x f32 [B, hidden]: the step's embeddings (residual stream)."""
         self.x.copy_(x)
 
-    def launch(self, stream=None, record_routes=False, record=None):
-        """Enqueue the step. record_routes writes every layer's route ids to
-        self.route_ids (for counting the experts a step reads); record (a dict)
-        receives per-layer copies of the intermediates for parity checks."""
+    def launch(self, stream=None, record_routes=False, record=None, mark=None, moe_events=None):
+        """Enqueue the step (under expert parallelism: up to this rank's
+        vocabulary-shard candidates; `finish` merges every rank's).
+        record_routes writes every layer's route ids to self.route_ids (for
+        counting the experts a step reads); record (a dict) receives per-layer
+        copies of the intermediates for parity checks (they are copied on the
+        current stream: launch on it). mark(name), when given, is called before
+        each C-ABI call and once at the end (per-call timing with events);
+        moe_events(i) may return the MoE layer's phase-event array for layer i."""
         ctx, cfg, m = self.ctx, self.cfg, self.model
+        mk = mark if mark is not None else (lambda name: None)
         L0 = m.layers[0]
+        mk("input_norm")
         ctx.rms_norm(self.x, L0.input_norm, self.xn, eps=cfg.eps, stream=stream)
         seq_lens = [p + 1 for p in self.positions_host]
         for i, L in enumerate(m.layers):
             if record is not None:
                 record.setdefault("x", []).append(self.x.clone())
                 record.setdefault("xn", []).append(self.xn.clone())
+            mk("q_a+kv_a")
             ctx.q4_fused([L.q_a.mat(), L.kv_a.mat()], self.xn, [self.qa, self.kv], stream=stream)
+            mk("q_b")
             ctx.q4_fused([L.q_b.mat()], self.qa, [self.q.view(self.B, -1)], norm=L.q_a_norm, eps=cfg.eps,
                          stream=stream)
             if record is not None:
                 record.setdefault("qa", []).append(self.qa.clone())
                 record.setdefault("kv", []).append(self.kv.clone())
                 record.setdefault("q_prerope", []).append(self.q.clone())
+            mk("rope_append")
             ctx.mla_rope_append(self.mla_cfg, self.q, self.kv, self.positions, self.caches.c_kv_ptrs[i],
                                 self.caches.k_rope_ptrs[i], cfg.context, latent_norm=L.kv_a_norm, eps=cfg.eps,
                                 stream=stream)
+            mk("mla_decode")
             ctx.mla_decode(self.mla_cfg, self.q, [t[:n] for t, n in zip(self.caches.c_kv[i], seq_lens)],
                            [t[:n] for t, n in zip(self.caches.k_rope[i], seq_lens)], L.w_uk, L.w_uv, self.attn,
                            stream=stream)
+            mk("o_proj")
             ctx.q4_fused([L.o_proj.mat()], self.attn.view(self.B, -1), [self.h], residual=self.x, stream=stream)
             if record is not None:
                 record.setdefault("q", []).append(self.q.clone())
@@ -197,20 +255,59 @@ class DecodeStep:
                 record.setdefault("h", []).append(self.h.clone())
             nxt = m.layers[i + 1].input_norm if i + 1 < len(m.layers) else m.final_norm
             dbg = None
-            if record_routes or record is not None:
-                dbg = capi.MoeDebug(None, self.route_ids[i].data_ptr(), None, None, None,
-                                    self.n.data_ptr() if record is not None else None)
-            ctx.moe_layer(self.moe_cfg, self.moe_w[i], self.h, self.x, self.B, residual=self.h,
-                          next_norm_weight=nxt, next_normed=self.xn, debug=dbg, stream=stream)
+            ev = moe_events(i) if moe_events is not None else None
+            if record_routes or record is not None or ev is not None:
+                dbg = capi.MoeDebug(None, self.route_ids[i].data_ptr() if (record_routes or record is not None)
+                                    else None, None, None, ev, self.n.data_ptr() if record is not None else None)
+            mk("moe_layer")
+            if self.ep:
+                if dbg is not None:
+                    dbg.phase_events = None
+                ctx.ep_moe_layer(self.moe_cfg, self.moe_w[i], self.shard, self.h, self.x, self.B, residual=self.h,
+                                 next_norm_weight=nxt, next_normed=self.xn, debug=dbg, stream=stream)
+            else:
+                ctx.moe_layer(self.moe_cfg, self.moe_w[i], self.h, self.x, self.B, residual=self.h,
+                              next_norm_weight=nxt, next_normed=self.xn, debug=dbg, stream=stream)
             if record is not None:
                 record.setdefault("n", []).append(self.n.clone())
                 record.setdefault("route_ids", []).append(self.route_ids[i].clone())
+        mk("head")
         if record is not None:
             record["x_final"] = self.x.clone()
             record["xn_final"] = self.xn.clone()
             ctx.head_topk(m.head, self.xn, self.ids, self.vals, logits=self.logits, stream=stream)
+        elif self.ep:
+            ctx.head_topk(m.head, self.xn, self.lids, self.lvals, id_base=m.head_base, keys=self.keys,
+                          stream=stream)
         else:
             ctx.head_topk(m.head, self.xn, self.ids, self.vals, stream=stream)
+        mk("end")
+
+    def finish(self, stream=None):
+        """Under expert parallelism: all-gather every rank's vocabulary-shard
+        candidate lists (one NCCL collective, ranks in id order) and merge them
+        into self.ids / self.vals (pbmoe_head_merge). Nothing on one GPU."""
+        if not self.ep:
+            return
+        import torch.distributed as dist
+
+        local = torch.stack([self.keys, self.lids, self.lvals.view(torch.int32)])
+        with torch.cuda.stream(stream) if stream is not None else _null():
+            dist.all_gather_into_tensor(self.gathered, local.unsqueeze(0).contiguous())
+            g = self.gathered
+            self.ctx.head_merge(g[:, 0].contiguous(), g[:, 1].contiguous(), g[:, 2].contiguous().view(torch.float32),
+                                self.ids, self.vals, stream=stream)
+
+    def step_weight_bytes(self):
+        """Weight bytes one step reads on this rank before routed experts:
+        every layer's MLA projections, W_UK/W_UV, norms, router, shared gate
+        and shared expert (when this rank holds it), and the head shard."""
+        cfg, m = self.cfg, self.model
+        L0 = m.layers[0]
+        shared = L0.moe.shared is not None
+        per_layer = (L0.nbytes() + cfg.experts * cfg.hidden * 2 + (cfg.hidden * 2 if shared else 0) +
+                     (int(L0.moe.layout.expert_bytes) if shared else 0))
+        return cfg.layers * per_layer + int(m.head.numel()) * 2
 
     def launches_per_step(self):
         """CUDA kernels one step launches: the input norm; per layer 2 fused
