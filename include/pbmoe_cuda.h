@@ -89,16 +89,28 @@ typedef struct pbmoe_q4_tensor {
     uint32_t group_size;
 } pbmoe_q4_tensor;
 
+/* How an expert slot's weights are encoded (FixedQ4ExpertEncoding,
+ * experts/slots.rs:3-45). */
+typedef enum pbmoe_expert_encoding {
+    /* AffineBf16: 4-bit q per weight, bf16 scale and bias per group_size
+     * columns, w = q * scale + bias (FIXED_Q4_EXPERT_LAYER_V1) */
+    PBMOE_EXPERT_AFFINE_Q4 = 0,
+    /* MlxMxfp4: E2M1 nibbles, one E8M0 scale byte per 32 columns, no biases
+     * (FIXED_MXFP4_EXPERT_LAYER_V1); group_size must be 32 */
+    PBMOE_EXPERT_MXFP4 = 1
+} pbmoe_expert_encoding;
+
 /* Whole-expert slot layout. Replaces QwenMoeQ4ExpertLayout
  * (model_family.rs:839-1010): nine components in the order gate{W,S,B},
  * up{W,S,B}, down{W,S,B}; gate/up are [intermediate x hidden], down is
- * [hidden x intermediate]. */
+ * [hidden x intermediate]. MXFP4 slots have zero-sized bias components. */
 typedef struct pbmoe_expert_layout {
     uint64_t component_offsets[9];
     uint64_t expert_bytes; /* slot stride in the expert table */
     uint32_t hidden;
     uint32_t intermediate;
     uint32_t group_size;
+    uint32_t encoding;     /* pbmoe_expert_encoding; zero-initialised = affine Q4 */
 } pbmoe_expert_layout;
 
 /* Routing weight normalisation (QwenMoeRoutingWeightNormalization,
@@ -132,6 +144,14 @@ typedef struct pbmoe_moe_weights {
      * of the router (CMD2, metal/mod.rs:2864-3012; rms_norm_reduced,
      * shaders.metal:1176-1213), fused into the router kernel. 16-byte aligned. */
     const float* input_norm_weight;
+    /* f32 [E] router correction bias, or NULL. When given, the layer routes as
+     * GLM/DeepSeek noaux models do (routing_sigmoid_noaux_top_k, math.rs:
+     * 788-819; QwenMoeRoutingPlacement::CpuSigmoidNoAuxTopK): experts are
+     * selected on sigmoid(logit) + bias with routing_top_k_iter's slot order,
+     * and a selected expert's weight is its raw sigmoid(logit), then the
+     * config's normalisation and routed_scaling_factor. NULL = softmax top-k.
+     * 16-byte aligned. */
+    const float* router_correction_bias;
 } pbmoe_moe_weights;
 
 /* Optional outputs of pbmoe_moe_layer for inspection and parity checks. Any
@@ -188,7 +208,10 @@ PBMOE_API int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint
 
 /* The fixed MXFP4 whole-expert layout (QwenMoeQ4ExpertLayout::fixed_mxfp4,
  * model_family.rs:846-952): per projection the E2M1 nibbles then one E8M0
- * byte per group, the bias components zero-sized. Host-only. */
+ * byte per group, the bias components zero-sized; encoding
+ * PBMOE_EXPERT_MXFP4. The MoE layer runs such slots with group_size 32, the
+ * only group the reference builds them with (experts/slots.rs:67-80).
+ * Host-only. */
 PBMOE_API int pbmoe_fixed_mxfp4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group_size,
                                        pbmoe_expert_layout* out);
 
@@ -241,6 +264,19 @@ PBMOE_API int pbmoe_q4_matvec_fused(pbmoe_ctx* ctx, const pbmoe_q4_fused_args* a
 PBMOE_API int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint32_t num_experts,
                      uint32_t top_k, uint32_t normalization, float routed_scaling_factor,
                      uint32_t* route_ids, float* route_weights, void* stream);
+
+/* Sigmoid/noaux routing on given logits (routing_sigmoid_noaux_top_k,
+ * math.rs:788-819, the CpuSigmoidNoAuxTopK stage, capabilities.rs:96): per
+ * token, experts selected on sigmoid(logit) + correction_bias[e] (f32 [E],
+ * device) in routing_top_k_iter's slot order; route_weights = the selected
+ * experts' raw sigmoid(logit), then `normalization` x routed_scaling_factor
+ * (scheduler/expert_access.rs:80-133). The sigmoid is computed as the
+ * reference's f32 arithmetic with a correctly rounded exp, so ids match it
+ * bit for bit on identical logits. */
+PBMOE_API int pbmoe_route_sigmoid_noaux(pbmoe_ctx* ctx, const float* logits, const float* correction_bias,
+                                        uint32_t tokens, uint32_t num_experts, uint32_t top_k,
+                                        uint32_t normalization, float routed_scaling_factor, uint32_t* route_ids,
+                                        float* route_weights, void* stream);
 
 /* One MoE FFN decode layer for `tokens` tokens (1..max_tokens of pbmoe_reserve):
  *   router logits -> top-k routing -> per-route SwiGLU expert on Q4 weights

@@ -168,6 +168,47 @@ void expert_swiglu(const SlotView& v, size_t hidden, size_t inter, size_t group,
     }
 }
 
+// One MXFP4 row dot (mxfp4_fma_matvec_with_group_size, experts/slots.rs:
+// 1239-1287): sum += weight * scale * x in column order; false on a
+// non-finite E8M0 scale (the reference's bail).
+bool mxfp4_row(const uint8_t* packed, const uint8_t* scales, const float* x, size_t r, size_t cols, size_t group,
+               float* out) {
+    static const float kMag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const size_t row_bytes = (cols + 1) / 2, groups = (cols + group - 1) / group;
+    float sum = 0.0f;
+    for (size_t c = 0; c < cols; ++c) {
+        const uint8_t byte = packed[r * row_bytes + c / 2];
+        const uint8_t nib = (c % 2 == 0) ? (byte & 0x0f) : (byte >> 4);
+        const float mag = kMag[nib & 0x07];
+        const float weight = (nib & 0x08) == 0 ? mag : -mag;
+        const uint8_t sb = scales[r * groups + c / group];
+        const uint32_t bits = sb == 0 ? 0x00400000u : (uint32_t(sb) << 23);
+        float scale;
+        std::memcpy(&scale, &bits, 4);
+        if (!std::isfinite(scale)) return false;
+        sum += weight * scale * x[c];
+    }
+    *out = sum;
+    return true;
+}
+
+// The MXFP4 expert of a FIXED_MXFP4_EXPERT_LAYER_V1 slot (model_family.rs:
+// 846-952: per projection the E2M1 nibbles, then one E8M0 byte per group,
+// no biases): gate and up rows, silu(g) * u (shaders.metal:1699-1708), down.
+bool expert_swiglu_mxfp4(const uint8_t* slot, const uint64_t* offsets, size_t hidden, size_t inter, size_t group,
+                         const float* x, float* out, float* scratch_inter) {
+    for (size_t r = 0; r < inter; ++r) {
+        float g, u;
+        if (!mxfp4_row(slot + offsets[0], slot + offsets[1], x, r, hidden, group, &g) ||
+            !mxfp4_row(slot + offsets[3], slot + offsets[4], x, r, hidden, group, &u))
+            return false;
+        scratch_inter[r] = g / (1.0f + std::exp(-g)) * u;
+    }
+    for (size_t r = 0; r < hidden; ++r)
+        if (!mxfp4_row(slot + offsets[6], slot + offsets[7], scratch_inter, r, inter, group, &out[r])) return false;
+    return true;
+}
+
 // math.rs:746-765 (routing_top_k_iter): K replacement slots initialised to
 // (0, -inf); each score replaces the first minimum slot when strictly greater.
 size_t routing_top_k_iter(const float* scores, size_t n, size_t k, uint32_t* ids, float* vals) {
@@ -317,20 +358,23 @@ size_t oracle_routing_softmax_top_k(const float* scores, size_t n, size_t k, uin
     return kk;
 }
 
+// 1 / (1 + e^-x) in f32 (math.rs:788-819 writes 1.0 / (1.0 + (-x).exp()) on
+// f32). Rust's f32::exp is the platform libm's expf; this pins it to the
+// correctly rounded value, e^-x evaluated in double and rounded once to
+// float, the same value the CUDA router computes.
+static float sigmoid_f32(float x) {
+    const float e = static_cast<float>(std::exp(-static_cast<double>(x)));
+    return 1.0f / (1.0f + e);
+}
+
 // math.rs:788-819 (routing_sigmoid_noaux_top_k): selection on sigmoid(s)+bias,
 // returned weights are the unbiased sigmoid.
 size_t oracle_routing_sigmoid_noaux_top_k(const float* logits, const float* correction_bias,
                                           size_t n, size_t k, uint32_t* ids, float* weights) {
     std::vector<float> biased(n);
-    for (size_t e = 0; e < n; ++e) {
-        float raw = 1.0f / (1.0f + std::exp(-logits[e]));
-        biased[e] = raw + correction_bias[e];
-    }
+    for (size_t e = 0; e < n; ++e) biased[e] = sigmoid_f32(logits[e]) + correction_bias[e];
     size_t kk = routing_top_k_iter(biased.data(), n, k, ids, weights);
-    for (size_t s = 0; s < kk; ++s) {
-        float score = logits[ids[s]];
-        weights[s] = 1.0f / (1.0f + std::exp(-score));
-    }
+    for (size_t s = 0; s < kk; ++s) weights[s] = sigmoid_f32(logits[ids[s]]);
     return kk;
 }
 
@@ -509,14 +553,22 @@ int oracle_combine(const float* residual, const float* expert_out, const float* 
 // `offsets`; the shared expert (nullable) uses the same offsets. A NULL
 // shared_gate gives the shared expert weight 1. ids/weights/logits outputs are
 // nullable. threads > 1 parallelises over tokens only.
+// correction_bias (nullable, f32 [num_experts]) selects routing_sigmoid_noaux_top_k
+// (math.rs:788-819) instead of routing_softmax_top_k; mxfp4 != 0 reads the
+// slots as FIXED_MXFP4 experts (expert_swiglu_mxfp4).
 int oracle_moe_layer(const float* x, const float* residual, size_t tokens, size_t hidden,
                      size_t num_experts, size_t top_k, size_t inter, size_t group,
                      float routed_scale, const uint16_t* router_weight,
                      const uint16_t* shared_gate, const uint8_t* expert_table,
                      const uint64_t* offsets, size_t slot_stride, const uint8_t* shared_slot,
                      float* out, uint32_t* ids_out, float* weights_out, float* logits_out,
-                     int threads) {
+                     int threads, const float* correction_bias, int mxfp4) {
     if (group == 0 || top_k == 0 || top_k > num_experts) return kInvalid;
+    auto swiglu = [&](const uint8_t* slot, const float* xt, float* y, float* tmp) {
+        if (mxfp4) return expert_swiglu_mxfp4(slot, offsets, hidden, inter, group, xt, y, tmp);
+        expert_swiglu(slot_view(slot, offsets), hidden, inter, group, xt, y, tmp);
+        return true;
+    };
     auto one_token = [&](size_t t) -> int {
         const float* xt = x + t * hidden;
         std::vector<float> logits(num_experts);
@@ -524,7 +576,11 @@ int oracle_moe_layer(const float* x, const float* residual, size_t tokens, size_
         if (logits_out) std::memcpy(logits_out + t * num_experts, logits.data(), num_experts * 4);
         std::vector<uint32_t> ids(top_k);
         std::vector<float> probs(top_k), weights(top_k);
-        oracle_routing_softmax_top_k(logits.data(), num_experts, top_k, ids.data(), probs.data());
+        if (correction_bias)
+            oracle_routing_sigmoid_noaux_top_k(logits.data(), correction_bias, num_experts, top_k, ids.data(),
+                                               probs.data());
+        else
+            oracle_routing_softmax_top_k(logits.data(), num_experts, top_k, ids.data(), probs.data());
         if (oracle_renormalize_routes(probs.data(), top_k, 0, routed_scale, weights.data()) != kOk)
             return kInvalid;
         if (ids_out) std::memcpy(ids_out + t * top_k, ids.data(), top_k * 4);
@@ -532,13 +588,11 @@ int oracle_moe_layer(const float* x, const float* residual, size_t tokens, size_
         std::vector<float> y(top_k * hidden), tmp(inter), shared(hidden, 0.0f);
         for (size_t k = 0; k < top_k; ++k) {
             const uint8_t* slot = expert_table + static_cast<size_t>(ids[k]) * slot_stride;
-            expert_swiglu(slot_view(slot, offsets), hidden, inter, group, xt, y.data() + k * hidden,
-                          tmp.data());
+            if (!swiglu(slot, xt, y.data() + k * hidden, tmp.data())) return kInvalid;
         }
         float shared_weight = 0.0f;
         if (shared_slot) {
-            expert_swiglu(slot_view(shared_slot, offsets), hidden, inter, group, xt, shared.data(),
-                          tmp.data());
+            if (!swiglu(shared_slot, xt, shared.data(), tmp.data())) return kInvalid;
             if (shared_gate) {
                 float route;
                 oracle_dense_bf16_matvec(shared_gate, xt, 1, hidden, &route);

@@ -76,7 +76,7 @@ def _declare(L):
     L.oracle_combine.argtypes = [C.c_void_p, _f32p, _f32p, C.c_void_p, C.c_void_p, _sz, _sz, _sz, _f32p]
     L.oracle_moe_layer.argtypes = [
         _f32p, C.c_void_p, _sz, _sz, _sz, _sz, _sz, _sz, C.c_float, _u16p, C.c_void_p,
-        _u8p, _u64p, _sz, C.c_void_p, _f32p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+        _u8p, _u64p, _sz, C.c_void_p, _f32p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
     ]
     L.oracle_mla_absorbed_attention.argtypes = [
         _f32p, _f32p, _f32p, _sz, _u16p, _u16p, _sz, _sz, _sz, _sz, _sz, _f32p,
@@ -272,8 +272,11 @@ def combine(expert_out, weights, residual=None, shared=None, shared_weight=None)
 
 
 def moe_layer(x, router_bits, expert_table, offsets, slot_stride, num_experts, top_k, inter, group,
-              shared_slot=None, shared_gate_bits=None, residual=None, routed_scale=1.0, threads=1):
-    """Full MoE FFN decode layer per token. Returns (out, ids, weights, logits)."""
+              shared_slot=None, shared_gate_bits=None, residual=None, routed_scale=1.0, threads=1,
+              correction_bias=None, mxfp4=False):
+    """Full MoE FFN decode layer per token. Returns (out, ids, weights, logits).
+    correction_bias (f32 [E]) routes by sigmoid/noaux; mxfp4 reads MXFP4 expert slots."""
+    cb = None if correction_bias is None else _c(correction_bias, np.float32)
     x = _c(x, np.float32)
     tokens, hidden = x.shape
     out = np.zeros((tokens, hidden), np.float32)
@@ -286,7 +289,7 @@ def moe_layer(x, router_bits, expert_table, offsets, slot_stride, num_experts, t
     _check(lib().oracle_moe_layer(x, _ptr(r), tokens, hidden, num_experts, top_k, inter, group, routed_scale,
                                   _c(router_bits, np.uint16), _ptr(sg), _c(expert_table, np.uint8),
                                   _c(offsets, np.uint64), slot_stride, _ptr(ss), out, _ptr(ids), _ptr(w),
-                                  _ptr(logits), threads), "moe_layer")
+                                  _ptr(logits), threads, _ptr(cb), 1 if mxfp4 else 0), "moe_layer")
     return out, ids, w, logits
 
 

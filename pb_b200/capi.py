@@ -48,7 +48,7 @@ EXPORTED = [
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
     "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
     "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host", "pbmoe_sync",
-    "pbmoe_fixed_mxfp4_layout", "pbmoe_q4_matvec_fused",
+    "pbmoe_fixed_mxfp4_layout", "pbmoe_q4_matvec_fused", "pbmoe_route_sigmoid_noaux",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -61,7 +61,12 @@ class Q4Tensor(C.Structure):
 
 class ExpertLayout(C.Structure):
     _fields_ = [("component_offsets", C.c_uint64 * 9), ("expert_bytes", C.c_uint64),
-                ("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("group_size", C.c_uint32)]
+                ("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("group_size", C.c_uint32),
+                ("encoding", C.c_uint32)]
+
+
+PBMOE_EXPERT_AFFINE_Q4 = 0
+PBMOE_EXPERT_MXFP4 = 1
 
 
 class MoeConfig(C.Structure):
@@ -71,7 +76,8 @@ class MoeConfig(C.Structure):
 
 class MoeWeights(C.Structure):
     _fields_ = [("router_weight", C.c_void_p), ("experts", C.c_void_p), ("shared_expert", C.c_void_p),
-                ("shared_expert_gate", C.c_void_p), ("input_norm_weight", C.c_void_p)]
+                ("shared_expert_gate", C.c_void_p), ("input_norm_weight", C.c_void_p),
+                ("router_correction_bias", C.c_void_p)]
 
 
 class MoeDebug(C.Structure):
@@ -180,6 +186,7 @@ def load():
         L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, C.c_float, vp, vp, vp, u32,
                                              vp]
         L.pbmoe_q4_matvec_fused.argtypes = [vp, C.POINTER(Q4FusedArgs), vp]
+        L.pbmoe_route_sigmoid_noaux.argtypes = [vp, vp, vp, u32, u32, u32, u32, C.c_float, vp, vp, vp]
         L.pbmoe_sync.argtypes = [vp, vp, u32]
         L.pbmoe_moe_layer_host.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
                                            u32, vp]
@@ -277,6 +284,12 @@ class Context:
     def route_topk(self, logits, tokens, num_experts, top_k, ids, weights, normalization=0, scale=1.0, stream=None):
         self.check(self.lib.pbmoe_route_topk(self.h, _ptr(logits), tokens, num_experts, top_k, normalization, scale,
                                              _ptr(ids), _ptr(weights), self.stream_ptr(stream)))
+
+    def route_sigmoid_noaux(self, logits, bias, tokens, num_experts, top_k, ids, weights, normalization=0,
+                            scale=1.0, stream=None):
+        self.check(self.lib.pbmoe_route_sigmoid_noaux(self.h, _ptr(logits), _ptr(bias), tokens, num_experts, top_k,
+                                                      normalization, scale, _ptr(ids), _ptr(weights),
+                                                      self.stream_ptr(stream)))
 
     def reserve(self, max_tokens, config: MoeConfig):
         self.check(self.lib.pbmoe_reserve(self.h, max_tokens, C.byref(config)))

@@ -103,6 +103,33 @@ int say(char* msg, size_t len, int code, const char* fmt, ...) {
 int moe_check_layout(const pbmoe_expert_layout& L, char* msg, size_t len) {
     const uint32_t H = L.hidden, I = L.intermediate, G = L.group_size;
     if (H == 0 || I == 0 || G == 0) return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT, "expert layout has a zero dimension");
+    if (L.encoding == PBMOE_EXPERT_MXFP4) {
+        // E2M1 nibbles [rows x cols/2] (16-byte groups of 32 columns), one E8M0 byte per group, no biases
+        if (G != 32 || H % 32 != 0 || I % 32 != 0 || H > 16384 || I > 16384)
+            return say(msg, len, PBMOE_ERR_UNSUPPORTED,
+                       "FlashMoe unsupported MXFP4 expert geometry on CUDA: needs group_size 32 and hidden, "
+                       "intermediate multiples of 32 up to 16384 (got hidden=%u intermediate=%u group=%u)",
+                       H, I, G);
+        const uint64_t gw = uint64_t(I) * H / 2, gs = uint64_t(I) * (H / 32);
+        const uint64_t dw = uint64_t(H) * I / 2, ds = uint64_t(H) * (I / 32);
+        const uint64_t sizes[9] = {gw, gs, 0, gw, gs, 0, dw, ds, 0};
+        for (int i = 0; i < 9; ++i) {
+            const uint64_t o = L.component_offsets[i];
+            if (o > L.expert_bytes || sizes[i] > L.expert_bytes - o)
+                return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT,
+                           "expert component %d [%llu, +%llu) exceeds slot bytes %llu", i, (unsigned long long)o,
+                           (unsigned long long)sizes[i], (unsigned long long)L.expert_bytes);
+            if (i % 3 == 0 && o % 16 != 0)
+                return say(msg, len, PBMOE_ERR_UNSUPPORTED, "expert component %d offset %llu is not 16-byte aligned",
+                           i, (unsigned long long)o);
+        }
+        if (L.expert_bytes % 16 != 0)
+            return say(msg, len, PBMOE_ERR_UNSUPPORTED, "expert slot stride %llu is not a multiple of 16",
+                       (unsigned long long)L.expert_bytes);
+        return PBMOE_OK;
+    }
+    if (L.encoding != PBMOE_EXPERT_AFFINE_Q4)
+        return say(msg, len, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported expert encoding %u", L.encoding);
     if (H % G != 0 || I % G != 0)
         return say(msg, len, PBMOE_ERR_INVALID_ARGUMENT,
                    "fixed-Q4 expert dimensions hidden=%u intermediate=%u must be divisible by group_size=%u", H, I, G);
@@ -273,6 +300,7 @@ int pbmoe_fixed_q4_layout(uint32_t hidden, uint32_t intermediate, uint32_t group
     out->hidden = hidden;
     out->intermediate = intermediate;
     out->group_size = group;
+    out->encoding = PBMOE_EXPERT_AFFINE_Q4;
     return PBMOE_OK;
 }
 
@@ -292,6 +320,7 @@ int pbmoe_fixed_mxfp4_layout(uint32_t hidden, uint32_t intermediate, uint32_t gr
     out->hidden = hidden;
     out->intermediate = intermediate;
     out->group_size = group;
+    out->encoding = PBMOE_EXPERT_MXFP4;
     return PBMOE_OK;
 }
 
@@ -467,6 +496,27 @@ int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint3
     return PBMOE_OK;
 }
 
+int pbmoe_route_sigmoid_noaux(pbmoe_ctx* ctx, const float* logits, const float* bias, uint32_t tokens, uint32_t E,
+                              uint32_t K, uint32_t normalization, float routed_scale, uint32_t* ids, float* weights,
+                              void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!logits || !bias || !ids || !weights)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "sigmoid/noaux routing: null pointer");
+    if (E == 0 || K == 0 || K > 32 || K > E)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "sigmoid/noaux routing: K=%u over E=%u outside 1..min(32, E)", K, E);
+    if (normalization > PBMOE_ROUTE_DEEPSEEK_RENORMALIZE_WITH_FLOOR)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                    "FlashMoe unsupported routing weights: normalisation %u is not implemented on CUDA", normalization);
+    if (!(routed_scale > 0.f) || !std::isfinite(routed_scale))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "routed expert scale must be positive and finite");
+    if (tokens == 0) return PBMOE_OK;
+    DeviceGuard g(ctx->device);
+    cudaError_t e = route_topk_launch(logits, tokens, E, K, normalization, routed_scale, ids, weights, ctx->status,
+                                      static_cast<cudaStream_t>(stream), bias);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "sigmoid/noaux routing launch");
+    return PBMOE_OK;
+}
+
 namespace {
 // One decode layer; with `ep` set, the experts of [e_lo, e_lo + e_count) only
 // and the expert-parallel combine.
@@ -489,7 +539,8 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "moe layer: x must be 16-byte aligned (rows are read as 16-byte vectors)");
     if (!aligned(w->experts, 16) || (w->shared_expert && !aligned(w->shared_expert, 16)) ||
         !aligned(w->router_weight, 16) || (w->shared_expert_gate && !aligned(w->shared_expert_gate, 16)) ||
-        (w->input_norm_weight && !aligned(w->input_norm_weight, 16)))
+        (w->input_norm_weight && !aligned(w->input_norm_weight, 16)) ||
+        (w->router_correction_bias && !aligned(w->router_correction_bias, 16)))
         return fail(ctx, PBMOE_ERR_UNSUPPORTED,
                     "expert table, shared expert, router and input-norm weights must be 16-byte aligned");
     if (tokens == 0) return PBMOE_OK;
@@ -511,6 +562,7 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     a.layout.group = L.group_size;
     a.layout.cpg_shift_h = ilog2_u32(L.group_size / 32);
     a.layout.cpg_shift_i = ilog2_u32(L.group_size / 32);
+    a.layout.mxfp4 = L.encoding == PBMOE_EXPERT_MXFP4;
     a.tokens = tokens;
     a.num_experts = E;
     a.top_k = K;
@@ -530,6 +582,7 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     a.shared_slot = w->shared_expert;
     a.in_norm_w = w->input_norm_weight;
     a.in_eps = c->norm_epsilon;
+    a.router_bias = w->router_correction_bias;
     a.pdl = true;
     a.phase_events = debug ? debug->phase_events : nullptr;
     a.expert_lo = e_lo;

@@ -257,6 +257,14 @@ static int check_metadata(const char* root, uint32_t layer, const pbmoe_expert_l
     const Json* fmt = meta.get("format");
     if (!fmt || fmt->kind != Json::String)
         return e.fail(PBMOE_ERR_INVALID_ARGUMENT, "expert metadata %s has no format", path.c_str());
+    const bool mx_layout = L->encoding == PBMOE_EXPERT_MXFP4;
+    if (mx_layout != (fmt->s == "FIXED_MXFP4_EXPERT_LAYER_V1"))
+        return e.fail(PBMOE_ERR_UNSUPPORTED,
+                      mx_layout ? "FlashMoe unsupported expert layout for %s: an MXFP4 layout reads only "
+                                  "FIXED_MXFP4_EXPERT_LAYER_V1 layers, not %s"
+                                : "FlashMoe unsupported expert layout for %s: format %s needs the fixed MXFP4 layout "
+                                  "(encoding PBMOE_EXPERT_MXFP4)",
+                      path.c_str(), fmt->s.c_str());
     if (fmt->s == "FIXED_Q4_EXPERT_LAYER_V1") {
         info.fixed = true;
     } else if (fmt->s == "FIXED_MXFP4_EXPERT_LAYER_V1") {

@@ -49,6 +49,7 @@ struct MoeLayoutDev {
     uint32_t group;
     uint32_t cpg_shift_h;  // log2(group/32) for rows of length hidden
     uint32_t cpg_shift_i;  // same for rows of length inter
+    uint32_t mxfp4;        // slots are FIXED_MXFP4 (E2M1 + E8M0 per 32 columns), not affine Q4
 };
 
 // Expert-parallel combine: every rank's exchange buffer ([2 parity][world]
@@ -100,6 +101,8 @@ struct MoeLaunch {
     // the experts run on it (the post-attention norm of CMD2)
     const float* in_norm_w;
     float in_eps;
+    // f32 [E] router correction bias: sigmoid/noaux routing (NULL: softmax)
+    const float* router_bias;
     const uint8_t* experts;
     const uint8_t* shared_slot;
     bool pdl;  // launch the router kernel with programmatic dependent launch
@@ -126,6 +129,11 @@ int moe_check_layout(const pbmoe_expert_layout& L, char* msg, size_t len);
 int moe_check_config(const pbmoe_moe_config* c, char* msg, size_t len);
 
 cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s);
+// cudaLaunchKernelExC, with programmatic dependent launch when `pdl`.
+cudaError_t moe_launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args, bool pdl);
+// CUDA-core expert kernels for FIXED_MXFP4 slots (moe_mxfp4.cu).
+cudaError_t moe_up_mxfp4_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
+cudaError_t moe_down_mxfp4_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
 // Tensor-core expert kernels (group-64 layouts, moe_mma.cu).
 bool moe_mma_supported(const MoeLayoutDev& L);
 cudaError_t moe_up_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
@@ -137,7 +145,8 @@ cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
 cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
 size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K);
 cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
-                              float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s);
+                              float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s,
+                              const float* bias = nullptr);
 
 struct Q4MatvecArgs {
     const uint8_t* packed;

@@ -144,7 +144,8 @@ __global__ void __launch_bounds__(kRtThreads)
 moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
                   uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
                   const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
-                  uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps, MoeWs ws) {
+                  uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps,
+                  const float* __restrict__ router_bias, MoeWs ws) {
     extern __shared__ __align__(128) unsigned char rt_smem[];
     __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
     __shared__ uint32_t cta_flag;  // plan CTA selection
@@ -452,7 +453,8 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
         for (uint32_t t = blockIdx.x * kRtRows + warp; t < T; t += route_ctas * kRtRows) {
             stage_logits_warp(ws.logits + static_cast<size_t>(t) * E, E, s);
             route_token(s, E, K, normalization, routed_scale, ws.route_ids + static_cast<size_t>(t) * K,
-                        ws.route_w + static_cast<size_t>(t) * K, ws.status);
+                        ws.route_w + static_cast<size_t>(t) * K, ws.status, router_bias,
+                        ws.logits + static_cast<size_t>(t) * E);
         }
     }
     __syncthreads();
@@ -890,7 +892,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
 // ---------------------------------------------------------------- routing only
 __global__ void route_topk_kernel(const float* __restrict__ logits, uint32_t T, uint32_t E, uint32_t K,
                                   uint32_t normalization, float routed_scale, uint32_t* ids, float* w,
-                                  uint32_t* status) {
+                                  uint32_t* status, const float* __restrict__ bias) {
     extern __shared__ __align__(16) float rsm[];  // per warp: E logits (padded to 4)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t t = blockIdx.x * (blockDim.x / 32) + warp;
@@ -899,12 +901,12 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, uint32_t T, 
     float* s = rsm + warp * Ep;
     stage_logits_warp(logits + static_cast<size_t>(t) * E, E, s);
     route_token(s, E, K, normalization, routed_scale, ids + static_cast<size_t>(t) * K,
-                w + static_cast<size_t>(t) * K, status);
+                w + static_cast<size_t>(t) * K, status, bias, logits + static_cast<size_t>(t) * E);
 }
 
 // ---------------------------------------------------------------- host side
-static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args,
-                              bool pdl) {
+cudaError_t moe_launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args,
+                           bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -947,12 +949,12 @@ static cudaError_t moe_up_fallback_launch(const MoeLaunch& a, uint32_t gmax, cud
         const size_t smem = (1ull * H + 2ull * chunks) * sizeof(float);
         auto fn = moe_expert_up_kernel<XT, 1>;
         if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
-        return launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
+        return moe_launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
     }
     const size_t smem = 4ull * (H + 2ull * chunks) * sizeof(float);
     auto fn = moe_expert_up_kernel<XT, 4>;
     if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
-    return launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
+    return moe_launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kUpThreads), smem, s, args, pdl);
 }
 
 template <typename XT, typename OT>
@@ -984,10 +986,12 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         uint32_t* ep_epoch = a.ep ? a.ep->epoch : nullptr;
         const float* inw = a.in_norm_w;
         float ineps = a.in_eps;
+        const float* rbias = a.router_bias;
         void* args[] = {(void*)&x,    (void*)&T,     (void*)&H,  (void*)&E,  (void*)&K,
                         (void*)&norm, (void*)&scale, (void*)&rw, (void*)&sg, (void*)&has_shared,
-                        (void*)&e_lo, (void*)&e_hi,  (void*)&ep_epoch, (void*)&inw, (void*)&ineps, (void*)&ws};
-        if ((err = launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRtThreads), smem, s, args,
+                        (void*)&e_lo, (void*)&e_hi,  (void*)&ep_epoch, (void*)&inw, (void*)&ineps, (void*)&rbias,
+                        (void*)&ws};
+        if ((err = moe_launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRtThreads), smem, s, args,
                               a.pdl && pdl)) != cudaSuccess)
             return err;
     }
@@ -1002,10 +1006,13 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         ex.x = ws.xn;
         ex.x_dtype = PBMOE_BF16;
     }
-    const bool mma = moe_mma_supported(a.layout);
-    const bool pipe = moe_pipe_supported(ex);
+    const bool mx = a.layout.mxfp4 != 0;
+    const bool mma = !mx && moe_mma_supported(a.layout);
+    const bool pipe = mma && moe_pipe_supported(ex);
     // 2. gate/up/SwiGLU
-    if (pipe) {
+    if (mx) {
+        if ((err = moe_up_mxfp4_launch(ex, gmax, s, pdl)) != cudaSuccess) return err;
+    } else if (pipe) {
         if ((err = moe_up_pipe_launch(ex, s, pdl)) != cudaSuccess) return err;
     } else if (mma) {
         if ((err = moe_up_mma_launch(ex, gmax, s, pdl)) != cudaSuccess) return err;
@@ -1016,7 +1023,9 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     }
     if ((err = mark(2)) != cudaSuccess) return err;
     // 3. down
-    if (pipe) {
+    if (mx) {
+        if ((err = moe_down_mxfp4_launch(a, gmax, s, pdl)) != cudaSuccess) return err;
+    } else if (pipe) {
         if ((err = moe_down_pipe_launch(a, s, pdl)) != cudaSuccess) return err;
     } else if (mma) {
         if ((err = moe_down_mma_launch(a, gmax, s, pdl)) != cudaSuccess) return err;
@@ -1042,7 +1051,7 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         if ((err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) !=
             cudaSuccess)
             return err;
-        if ((err = launch_pdl(fn, grid, dim3(kDownThreads), smem, s, args, pdl)) != cudaSuccess) return err;
+        if ((err = moe_launch_pdl(fn, grid, dim3(kDownThreads), smem, s, args, pdl)) != cudaSuccess) return err;
     }
     if ((err = mark(3)) != cudaSuccess) return err;
     // 4. combine (+ next-layer norm)
@@ -1111,14 +1120,15 @@ cudaError_t moe_layer_launch(const MoeLaunch& a, cudaStream_t s) {
 }
 
 cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
-                              float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s) {
+                              float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s,
+                              const float* bias) {
     const int warps = 4;
     const size_t smem = warps * ((E + 3) & ~3u) * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(route_topk_kernel),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     route_topk_kernel<<<(T + warps - 1) / warps, warps * 32, smem, s>>>(logits, T, E, K, normalization,
-                                                                          routed_scale, ids, w, status);
+                                                                          routed_scale, ids, w, status, bias);
     return cudaGetLastError();
 }
 

@@ -225,7 +225,7 @@ bool moe_mma_supported(const MoeLayoutDev& L) {
     // group 64; hidden a multiple of 8*4*64 (eight K-slices of 4-group
     // blocks in the up kernel); intermediate 256 or 512 (one or two 4-group
     // blocks held in registers by the down kernel)
-    return L.group == kMmaGroup && L.hidden % 2048 == 0 && (L.inter == 256 || L.inter == 512) &&
+    return !L.mxfp4 && L.group == kMmaGroup && L.hidden % 2048 == 0 && (L.inter == 256 || L.inter == 512) &&
            L.off[0] % 16 == 0 && L.off[3] % 16 == 0 && L.off[6] % 16 == 0 && L.off[1] % 8 == 0 && L.off[2] % 8 == 0 &&
            L.off[4] % 8 == 0 && L.off[5] % 8 == 0 && L.off[7] % 8 == 0 && L.off[8] % 8 == 0 && L.expert_bytes % 16 == 0;
 }

@@ -101,7 +101,8 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
         reinterpret_cast<uintptr_t>(w->router_weight) % 16 ||
         (w->shared_expert && reinterpret_cast<uintptr_t>(w->shared_expert) % 16) ||
         (w->shared_expert_gate && reinterpret_cast<uintptr_t>(w->shared_expert_gate) % 16) ||
-        (w->input_norm_weight && reinterpret_cast<uintptr_t>(w->input_norm_weight) % 16))
+        (w->input_norm_weight && reinterpret_cast<uintptr_t>(w->input_norm_weight) % 16) ||
+        (w->router_correction_bias && reinterpret_cast<uintptr_t>(w->router_correction_bias) % 16))
         return report(error_buf, error_len, PBMOE_ERR_INVALID_ARGUMENT,
                       "moe layer (static): x, experts, router and shared weights must be 16-byte aligned");
     if (tokens == 0) return PBMOE_OK;
@@ -141,6 +142,7 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
     a.layout.group = G;
     a.layout.cpg_shift_h = ilog2_u32(G / 32);
     a.layout.cpg_shift_i = ilog2_u32(G / 32);
+    a.layout.mxfp4 = L.encoding == PBMOE_EXPERT_MXFP4;
     a.tokens = tokens;
     a.num_experts = E;
     a.top_k = K;
@@ -160,6 +162,7 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
     a.shared_slot = w->shared_expert;
     a.in_norm_w = w->input_norm_weight;
     a.in_eps = c->norm_epsilon;
+    a.router_bias = w->router_correction_bias;
     a.pdl = false;  // the memset above must complete before the router kernel reads the counter
     a.phase_events = nullptr;
     e = moe_layer_launch(a, s);

@@ -9,35 +9,15 @@
 // R rows at once (2 for 1-2 tokens, 1 for wider batches, whose per-token
 // accumulators take the registers) so each lane has several loads in flight.
 //
-// Decode: two nibbles at a time are placed into the exponent/mantissa fields
-// of an fp16 pair (bits (n & 7) << 9 and sign (n & 8) << 12): the fp16 value
-// is e2m1(n) * 2^-14 exactly (e = 0 lands in the fp16 subnormals), converted
-// to f32 exactly. Products with x accumulate per group; the group sum is then
-// scaled by 2^14 and by the E8M0 scale, both powers of two, so each term
-// rounds as the reference's weight * scale * x does and only the summation
-// order differs. E8M0 255 (not finite, where the reference bails) latches
-// PBMOE_DEV_ERR_MXFP4_SCALE.
+// Decode and per-group arithmetic: mxfp4.cuh. E8M0 255 (not finite, where
+// the reference bails) latches PBMOE_DEV_ERR_MXFP4_SCALE.
 
-#include <cuda_fp16.h>
-
-#include "common.cuh"
 #include "kernels.h"
+#include "mxfp4.cuh"
 
 namespace pbmoe {
 
 constexpr int kMxWarps = 8;
-
-// nibbles n0 (bits 0-3) and n1 (bits 16-19) of `v` -> two floats e2m1 * 2^-14
-__device__ __forceinline__ float2 e2m1_pair(uint32_t v) {
-    const uint32_t h = ((v & 0x00070007u) << 9) | ((v & 0x00080008u) << 12);
-    __half2 hh;
-    memcpy(&hh, &h, 4);
-    return __half22float2(hh);
-}
-
-__device__ __forceinline__ float e8m0_scale(uint32_t e) {
-    return __uint_as_float(e == 0 ? 0x00400000u : (e << 23));
-}
 
 template <typename XT, typename YT, int NT, int kMxRows>
 __global__ void __launch_bounds__(kMxWarps * 32)
@@ -78,35 +58,10 @@ mxfp4_matvec_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restric
 #pragma unroll
             for (int r = 0; r < kMxRows; ++r) {
                 if (sb[r] == 255u && r0 + r < rows && status) atomicOr(status, PBMOE_DEV_ERR_MXFP4_SCALE);
-                const uint32_t words[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
                 float part[NT];
 #pragma unroll
                 for (int t = 0; t < NT; ++t) part[t] = 0.f;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    // bytes b0..b3 of the word = columns 8q + 2j (low nibble), 8q + 2j + 1 (high)
-                    const uint32_t v = words[q];
-                    const float2 lo02 = e2m1_pair(__byte_perm(v, 0, 0x4140));         // cols 0, 2
-                    const float2 hi02 = e2m1_pair(__byte_perm(v, 0, 0x4140) >> 4);    // cols 1, 3
-                    const float2 lo46 = e2m1_pair(__byte_perm(v, 0, 0x4342));         // cols 4, 6
-                    const float2 hi46 = e2m1_pair(__byte_perm(v, 0, 0x4342) >> 4);    // cols 5, 7
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        const float* xr = xs + t * pcols + g * 36 + q * 8;
-                        const float4 xa = *reinterpret_cast<const float4*>(xr);
-                        const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
-                        float s = part[t];
-                        s = fmaf(lo02.x, xa.x, s);
-                        s = fmaf(hi02.x, xa.y, s);
-                        s = fmaf(lo02.y, xa.z, s);
-                        s = fmaf(hi02.y, xa.w, s);
-                        s = fmaf(lo46.x, xb.x, s);
-                        s = fmaf(hi46.x, xb.y, s);
-                        s = fmaf(lo46.y, xb.z, s);
-                        s = fmaf(hi46.y, xb.w, s);
-                        part[t] = s;
-                    }
-                }
+                mx_group_dot<NT>(w[r], xs + g * 36, pcols, part);
                 const float scale = e8m0_scale(sb[r]);
 #pragma unroll
                 for (int t = 0; t < NT; ++t) acc[r][t] += (part[t] * 16384.0f) * scale;

@@ -16,6 +16,18 @@ __device__ __forceinline__ uint32_t float_order_key(float f) {
 
 constexpr uint32_t kMaxTopK = 32;
 
+// 1 / (1 + exp(-x)) in f32 as the reference computes it (f32 exp, add,
+// divide). The exponential is the double-precision exp rounded once to f32,
+// which is the correctly rounded f32 exp (the double result is far closer to
+// the exact value than any f32 rounding boundary it could straddle, except
+// on a set of inputs too small to meet); the host reference's f32 exp is
+// correctly rounded too, so biased scores, and the ids selected on them,
+// match it bit for bit.
+__device__ __forceinline__ float router_sigmoid(float x) {
+    const float e = static_cast<float>(exp(-static_cast<double>(x)));
+    return 1.0f / (1.0f + e);
+}
+
 // Copy one token's E logits from global memory (written by an earlier kernel
 // or CTA: read through L2) into shared memory, with every load of the lane in
 // flight at once. `s` must be 16-byte aligned; ends with __syncwarp.
@@ -76,9 +88,11 @@ __device__ __forceinline__ void stage_logits_warp(const float* __restrict__ lg, 
 // (where the reference bails) and write zero weights.
 // Weights of the K selected slots (lane k = slot k holds its score `sval` and
 // expert `sid`), given the token's logit maximum m and softmax denominator sum.
+// With `raw` (sigmoid/noaux scoring) the slot's probability is instead the
+// raw sigmoid of its expert's logit, raw[sid] (routing_sigmoid_noaux_top_k).
 __device__ __forceinline__ void route_weights_lanes(float sval, uint32_t sid, float m, float sum, uint32_t K,
                                                     uint32_t normalization, float routed_scale, uint32_t* ids_out,
-                                                    float* w_out, uint32_t* status) {
+                                                    float* w_out, uint32_t* status, const float* raw = nullptr) {
     const int lane = threadIdx.x & 31;
     const bool is_slot = static_cast<uint32_t>(lane) < K;
     // softmax probability of each selected slot
@@ -86,8 +100,12 @@ __device__ __forceinline__ void route_weights_lanes(float sval, uint32_t sid, fl
     const float inverse_sum = have_inverse ? 1.0f / sum : 0.f;
     float p = 0.f;
     if (is_slot) {
-        p = expf(sval - m);
-        if (have_inverse) p *= inverse_sum;
+        if (raw) {
+            p = router_sigmoid(__ldcg(raw + sid));
+        } else {
+            p = expf(sval - m);
+            if (have_inverse) p *= inverse_sum;
+        }
     }
     // normalisation over the K selected, summed in slot order
     float ssum = 0.f;
@@ -204,17 +222,23 @@ __device__ inline void route_token_smem(const float* s, uint32_t E, uint32_t K, 
 // so those slots are filled directly. The chunk loop stays rolled (the
 // admission code is emitted once).
 template <int KMAX>
-__device__ __noinline__ void route_token_regs(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
+__device__ __noinline__ void route_token_regs(float* s, uint32_t E, uint32_t K, uint32_t normalization,
                                               float routed_scale, uint32_t* ids_out, float* w_out,
-                                              uint32_t* status) {
+                                              uint32_t* status, const float* bias, const float* raw) {
     const int lane = threadIdx.x & 31;
     const float NEG_INF = -__int_as_float(0x7f800000), POS_INF = __int_as_float(0x7f800000);
     float m = NEG_INF;
-    for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, s[e]);
-    m = warp_max(m);
     float sum = 0.f;
-    for (uint32_t e = lane; e < E; e += 32) sum += expf(s[e] - m);
-    sum = warp_sum(sum);
+    if (bias) {
+        // sigmoid/noaux (math.rs:788-819): select on sigmoid(logit) + bias
+        for (uint32_t e = lane; e < E; e += 32) s[e] = router_sigmoid(s[e]) + __ldg(bias + e);
+        __syncwarp();
+    } else {
+        for (uint32_t e = lane; e < E; e += 32) m = fmaxf(m, s[e]);
+        m = warp_max(m);
+        for (uint32_t e = lane; e < E; e += 32) sum += expf(s[e] - m);
+        sum = warp_sum(sum);
+    }
 
     float sval[KMAX];
     uint32_t sid[KMAX];
@@ -291,24 +315,29 @@ __device__ __noinline__ void route_token_regs(const float* s, uint32_t E, uint32
             my_val = sval[k];
             my_id = sid[k];
         }
-    route_weights_lanes(my_val, my_id, m, sum, K, normalization, routed_scale, ids_out, w_out, status);
+    route_weights_lanes(my_val, my_id, m, sum, K, normalization, routed_scale, ids_out, w_out, status,
+                        bias ? raw : nullptr);
 }
 
-// One warp routes one token whose logits are in shared memory `s` (K <= 32).
-__device__ inline void route_token(const float* s, uint32_t E, uint32_t K, uint32_t normalization,
-                                   float routed_scale, uint32_t* ids_out, float* w_out, uint32_t* status) {
+// One warp routes one token whose logits are in shared memory `s` (K <= 32):
+// softmax top-k, or with `bias` (f32 [E]) sigmoid/noaux top-k, whose weights
+// are the raw sigmoid of the token's logits `raw` (global, [E]); `s` is
+// overwritten with the biased scores then.
+__device__ inline void route_token(float* s, uint32_t E, uint32_t K, uint32_t normalization, float routed_scale,
+                                   uint32_t* ids_out, float* w_out, uint32_t* status, const float* bias = nullptr,
+                                   const float* raw = nullptr) {
     // slot counts instantiated: the smallest that holds K (10 is the
     // 512-expert top-10 configuration's)
     if (K <= 4)
-        route_token_regs<4>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+        route_token_regs<4>(s, E, K, normalization, routed_scale, ids_out, w_out, status, bias, raw);
     else if (K <= 8)
-        route_token_regs<8>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+        route_token_regs<8>(s, E, K, normalization, routed_scale, ids_out, w_out, status, bias, raw);
     else if (K <= 10)
-        route_token_regs<10>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+        route_token_regs<10>(s, E, K, normalization, routed_scale, ids_out, w_out, status, bias, raw);
     else if (K <= 16)
-        route_token_regs<16>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+        route_token_regs<16>(s, E, K, normalization, routed_scale, ids_out, w_out, status, bias, raw);
     else
-        route_token_regs<32>(s, E, K, normalization, routed_scale, ids_out, w_out, status);
+        route_token_regs<32>(s, E, K, normalization, routed_scale, ids_out, w_out, status, bias, raw);
 }
 
 // Block-wide exclusive scan of n <= 4096 u32 values in shared memory, in

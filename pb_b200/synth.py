@@ -67,6 +67,20 @@ def expert_table(num_experts: int, layout: capi.ExpertLayout, g: torch.Generator
     return table
 
 
+def mxfp4_expert_table(num_experts: int, layout: capi.ExpertLayout, g: torch.Generator, device) -> torch.Tensor:
+    """[num_experts, expert_bytes] u8 in the fixed MXFP4 layout: random E2M1
+    nibbles, E8M0 scale bytes 119..122 (2^-8..2^-5, weights of magnitude up to
+    about 0.2), the zero-sized bias components absent."""
+    E, stride = num_experts, int(layout.expert_bytes)
+    H, I = int(layout.hidden), int(layout.intermediate)
+    table = torch.randint(0, 256, (E, stride), device=device, dtype=torch.uint8, generator=g)
+    offs = [int(o) for o in layout.component_offsets]
+    for p, (rows, cols) in enumerate([(I, H), (I, H), (H, I)]):
+        so, nb = offs[3 * p + 1], rows * (cols // 32)
+        table[:, so:so + nb] = torch.randint(119, 123, (E, nb), device=device, dtype=torch.uint8, generator=g)
+    return table
+
+
 def normal_bf16(shape, std: float, g: torch.Generator, device) -> torch.Tensor:
     return (torch.randn(*shape, device=device, dtype=torch.float32, generator=g) * std).to(torch.bfloat16)
 
@@ -84,13 +98,18 @@ class MoeLayerWeights:
     shared expert with a sigmoid gate)."""
 
     def __init__(self, device, seed: int, hidden=2048, num_experts=512, intermediate=512, group=64,
-                 shared=True, shared_gate=True):
+                 shared=True, shared_gate=True, mxfp4=False):
         g = gen(device, seed)
+        if mxfp4:
+            group = 32  # FIXED_MXFP4 slots: one E8M0 scale per 32 columns
         self.hidden, self.num_experts, self.intermediate, self.group = hidden, num_experts, intermediate, group
-        self.layout = capi.fixed_q4_layout(hidden, intermediate, group)
+        self.mxfp4 = mxfp4
+        self.layout = (capi.fixed_mxfp4_layout(hidden, intermediate, group) if mxfp4
+                       else capi.fixed_q4_layout(hidden, intermediate, group))
+        table = mxfp4_expert_table if mxfp4 else expert_table
         self.router = normal_bf16((num_experts, hidden), 0.02, g, device)
-        self.experts = expert_table(num_experts, self.layout, g, device)
-        self.shared = expert_table(1, self.layout, g, device)[0].contiguous() if shared else None
+        self.experts = table(num_experts, self.layout, g, device)
+        self.shared = table(1, self.layout, g, device)[0].contiguous() if shared else None
         self.shared_gate = normal_bf16((hidden,), 0.02, g, device) if (shared and shared_gate) else None
 
     def c_weights(self) -> capi.MoeWeights:

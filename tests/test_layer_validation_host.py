@@ -76,3 +76,57 @@ def test_workspace_bytes_match_the_static_capacity():
     cfg = _cfg()
     need = lambda t: 256 + capi.load().pbmoe_moe_workspace_bytes(t, ctypes.byref(cfg))
     assert need(29) <= 4 << 20 < need(30)
+
+
+def _mx_cfg(edit=None, hidden=2048, inter=512, group=32):
+    from pb_b200 import capi
+
+    lay = capi.fixed_mxfp4_layout(hidden, inter, group)
+    if edit:
+        edit(lay)
+    return capi.moe_config(lay, 512, 10)
+
+
+def test_expert_layout_struct_and_encodings():
+    """pbmoe_expert_layout is 96 bytes with the encoding in its last word; the
+    two fixed layouts say which encoding they are."""
+    from pb_b200 import capi
+
+    assert ctypes.sizeof(capi.ExpertLayout) == 96
+    assert capi.fixed_q4_layout(2048, 512, 64).encoding == capi.PBMOE_EXPERT_AFFINE_Q4
+    assert capi.fixed_mxfp4_layout(2048, 512, 32).encoding == capi.PBMOE_EXPERT_MXFP4
+
+
+def test_mxfp4_layout_is_accepted():
+    from pb_b200 import capi
+
+    rc, msg = _static(_mx_cfg(), tokens=0)
+    assert rc == capi.PBMOE_OK and msg == ""
+
+
+def test_mxfp4_group_other_than_32_is_unsupported():
+    """The reference builds MXFP4 slots with group 32 only (experts/slots.rs:67-80)."""
+    from pb_b200 import capi
+
+    rc, msg = _static(_mx_cfg(group=64))
+    assert rc == capi.PBMOE_ERR_UNSUPPORTED and "MXFP4" in msg
+
+
+def test_mxfp4_overlong_scales_are_refused():
+    from pb_b200 import capi
+
+    def edit(lay):
+        lay.component_offsets[7] = lay.expert_bytes - 8  # down scales: 32,768 bytes from 8 before the end
+
+    rc, msg = _static(_mx_cfg(edit))
+    assert rc == capi.PBMOE_ERR_INVALID_ARGUMENT and "exceeds slot bytes" in msg
+
+
+def test_unknown_encoding_is_unsupported():
+    from pb_b200 import capi
+
+    def edit(lay):
+        lay.encoding = 7
+
+    rc, msg = _static(_cfg(edit))
+    assert rc == capi.PBMOE_ERR_UNSUPPORTED and "encoding" in msg
