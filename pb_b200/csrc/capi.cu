@@ -336,7 +336,7 @@ int pbmoe_reserve(pbmoe_ctx* ctx, uint32_t max_tokens, const pbmoe_moe_config* c
     if (max_tokens == 0 || max_tokens > 4096)
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "max_tokens %u outside 1..4096", max_tokens);
     const uint32_t E = c->num_experts, K = c->top_k, H = c->layout.hidden, I = c->layout.intermediate;
-    if (moe_router_smem(max_tokens, H, E, K) > 200 * 1024)
+    if (moe_router_smem(max_tokens, H, E, K) > kRouterSmemLimit)
         return fail(ctx, PBMOE_ERR_UNSUPPORTED, "router staging for %u tokens exceeds shared memory", max_tokens);
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);

@@ -67,13 +67,32 @@ __device__ __forceinline__ float group_sum(float v) {
     return v;
 }
 
+// L2 policy for bytes a decode step reads once (weights, KV cache rows):
+// evict first. The step streams far more than L2 holds, and with the normal
+// policy those bytes push out what its kernels keep re-reading (activations,
+// workspace, the kernels' own instructions).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // Streaming 128-bit load of weight bytes that are read once per launch:
-// bypass L1 allocation, keep the normal L2 policy.
+// bypass L1 allocation, evict first from L2.
 __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
+                 : "l"(p), "l"(l2_evict_first()));
+    return r;
+}
+
+// The same for 8 bytes.
+__device__ __forceinline__ uint2 ld_stream_u2(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "l"(p), "l"(l2_evict_first()));
     return r;
 }
 

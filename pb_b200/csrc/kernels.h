@@ -144,6 +144,9 @@ bool moe_pipe_supported(const MoeLaunch& a);
 cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
 cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
 size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K);
+// Dynamic shared memory the router kernel may use (the 227 KB per-CTA limit
+// less its static shared memory, rounded down).
+constexpr size_t kRouterSmemLimit = 224 * 1024;
 cudaError_t route_topk_launch(const float* logits, uint32_t T, uint32_t E, uint32_t K, uint32_t normalization,
                               float routed_scale, uint32_t* ids, float* w, uint32_t* status, cudaStream_t s,
                               const float* bias = nullptr);

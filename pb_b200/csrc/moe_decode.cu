@@ -2,11 +2,11 @@
 // kernels:
 //
 //   1. moe_router_kernel   router GEMV (bf16 [E x H]) + shared-expert gate
-//                          logit; the last CTA to finish routes every token
-//                          (route_token_smem) and builds the layer-major group
-//                          plan (unique experts in ascending id order, routes
-//                          in route order inside each group, shared expert as
-//                          group 0 with every token).
+//                          logit; the first CTAs route the tokens once every
+//                          CTA's logits are written (route_token) and build the
+//                          layer-major group plan (unique experts in ascending
+//                          id order, routes in route order inside each group,
+//                          shared expert as group 0 with every token).
 //   2. moe_expert_up_kernel   gate and up rows of one group's expert for the
 //                          group's tokens, SwiGLU fused: h = silu(g) * u.
 //   3. moe_expert_down_kernel down rows of the group's expert on h -> y.
@@ -42,71 +42,80 @@ namespace cg = cooperative_groups;
 // c = 0, 1, ..., H-1. Route ids are integer outputs and must match bit for bit,
 // so every (row, token) chain here is one thread walking the columns in that
 // order: the sum is never split or reassociated, and identical inputs give
-// identical logits, hence identical top-k ids.
+// identical logits, hence identical top-k ids. A chain of H dependent fmas is
+// the kernel's floor (H x the fma latency); everything else is arranged around
+// it.
 //
-// A CTA owns kRtRows consecutive rows (row E is the shared-expert gate). Their
-// bf16 weights arrive in shared memory by bulk copies (one per row and
-// kRtChunk-column chunk, each chunk completing on its own mbarrier), issued
-// before the programmatic-dependent-launch wait since they do not depend on
-// the previous kernel. Activations are staged per chunk as f32 in a padded,
-// double-buffered layout (the next chunk's loads are in flight while the
-// current chunk's fmas run). Warp w runs row w and lane t token t of a pass of
-// up to kRtTokPass tokens, so a warp's weight reads are broadcasts and its
-// activation reads hit distinct banks.
+// A CTA owns rpc consecutive rows (kRtRows, or fewer when rows of a wide
+// hidden size would not fit in shared memory; row E is the shared-expert
+// gate) and runs their chains for a pass of up to kRtTokPass tokens, a warp
+// covering 4 rows x 8 tokens so that each shared-memory read serves 8 or 4
+// chains.
+// The rows' bf16 weights arrive in shared memory by bulk copies issued before
+// the programmatic-dependent-launch wait (they do not depend on the previous
+// kernel).
 //
-// With in_norm_w the layer input x is the un-normalised hidden state: every
-// CTA computes the tokens' RMSNorm scales, the staged values are
-// bf16(x * scale * w) (the post-attention norm the reference runs ahead of the
-// router, rms_norm_reduced, shaders.metal:1176-1213), and the CTAs together
-// write those rows to ws.xn, the expert kernels' input.
+// Staged rows (bf16 input, or an input normalised here): one warp per token
+// reads the token's row with all of a lane's loads in flight, and writes it
+// to shared memory as f32, [pass][H + 4] (the pad puts consecutive tokens'
+// 16-byte reads in distinct banks). With in_norm_w the layer input x is the
+// un-normalised hidden state: the warp first computes the token's RMSNorm
+// scale, the staged values are bf16(x * scale * w) (the post-attention norm
+// the reference runs ahead of the router, rms_norm_reduced,
+// shaders.metal:1176-1213), and the CTAs together write those rows to ws.xn,
+// the expert kernels' input. The weights are converted once to f32 rows in
+// shared memory when they fit (else read as bf16, chunk by chunk as they
+// land), padded so that a warp's 4 weight rows and 8 token rows fall in
+// distinct banks; a chain step is 16 columns, the next step's reads issued
+// before the current fmas.
+// f32 input without a norm is staged per 256-column chunk instead,
+// double-buffered.
 //
-// Routing and the group plan are spread over several CTAs: each CTA counts
-// itself in ticket[0] once its logits are written; the first NR CTAs (at most
-// kRtRouteCtas, so the other CTAs always find SM slots) wait, bounded, for
-// ticket[0] == gridDim.x, route one token per warp (route_token_smem: the
-// exact slot order of routing_top_k_iter, math.rs:746-765), count themselves
-// in ticket[1], and the last of them builds the layer-major plan (unique
-// experts ascending, routes in route order inside each group, the shared
-// expert as group 0) and resets both counters for the next launch.
-constexpr int kRtRows = 4;
+// Routing and the group plan: each CTA counts itself in ticket[0] (a release
+// add) once its logits are written; the first NR = ceil(T / kRtRows) CTAs (at
+// most kRtRouteCtas, so the other CTAs always find SM slots) wait, bounded,
+// for ticket[0] == gridDim.x, route one token per warp (route_token: the
+// exact slot order of routing_top_k_iter, math.rs:746-765), and build the
+// layer-major plan (unique experts ascending, routes in route order inside
+// each group, the shared expert as group 0): directly when NR is 1, else the
+// last of them (counted in ticket[1]). The plan CTA resets both counters for
+// the next launch.
+constexpr int kRtRows = 8;
 constexpr int kRtThreads = 32 * kRtRows;
 constexpr uint32_t kRtTokPass = 32;
 constexpr uint32_t kRtChunk = 256;
 constexpr uint32_t kRtXStride = kRtChunk + 4;  // padded f32 row of a staged chunk
 constexpr uint32_t kRtMaxChunks = 64;          // hidden <= 16384
 constexpr uint32_t kRtRouteCtas = 64;
-constexpr size_t kRtStageBudget = 200 * 1024;  // weights + bf16 token rows of one pass
+constexpr size_t kRtStageBudget = 216 * 1024;  // weights + staged token rows of one pass
 constexpr int kRtVecs = static_cast<int>(kRtTokPass * kRtChunk / 4 / kRtThreads);  // float4 per thread per chunk
+constexpr uint32_t kRtWarpPlanRoutes = 256;    // plans of at most this many routes are built by one warp
 
-// Activation staging: bf16 rows when the layer input is bf16 or is
-// normalised here (the normalised rows are bf16 by definition) — a pass's
-// token rows are staged once, [pass][H + 8] bf16 (the pad puts consecutive
-// tokens' 16-byte reads in distinct banks); f32 rows otherwise — 256-column
-// chunks of f32, double-buffered.
-//
-// With bf16 rows the weights are also converted once to f32 rows in shared
-// memory (wf_bytes, when they fit), so the chains' inner step is two f32
-// weight reads, one bf16 activation read and eight fmas.
+// router rows per CTA for hidden size H: all kRtRows warps when their bf16
+// rows leave room for a staged token row, else half
+__host__ __device__ inline uint32_t rt_rows_per_cta(uint32_t H) { return H <= 8192 ? kRtRows : kRtRows / 2; }
+
 struct RtSmem {
     size_t w_bytes, wf_bytes, x_bytes, total;
     uint32_t pass;    // tokens per pass
-    uint32_t stride;  // bf16 elements per staged row (bf16 rows)
+    uint32_t stride;  // floats per staged row (staged rows)
 };
-__host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_t E, uint32_t K, bool bf16_rows) {
+__host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_t E, uint32_t K, bool staged_rows) {
     RtSmem s;
-    s.w_bytes = (static_cast<size_t>(kRtRows) * H * 2 + 127) / 128 * 128;
+    const size_t rpc = rt_rows_per_cta(H);
+    s.w_bytes = (rpc * (H + 8) * 2 + 127) / 128 * 128;
     s.wf_bytes = 0;
-    if (bf16_rows) {
-        if (static_cast<size_t>(kRtRows) * H * 4 + s.w_bytes <= 96 * 1024) s.wf_bytes = static_cast<size_t>(kRtRows) * H * 4;
-        s.stride = H + 8;
-        const size_t row = static_cast<size_t>(s.stride) * 2;
-        const size_t used = s.w_bytes + s.wf_bytes;
+    if (staged_rows) {
+        if (rpc * (H + 4) * 4 + s.w_bytes <= 100 * 1024) s.wf_bytes = rpc * (H + 4) * 4;
+        s.stride = H + 4;
+        const size_t row = static_cast<size_t>(s.stride) * 4;
+        const size_t used = s.w_bytes + s.wf_bytes + static_cast<size_t>(T) * 4;
         size_t pass = used < kRtStageBudget ? (kRtStageBudget - used) / row : 1;
         if (pass < 1) pass = 1;
         if (pass > kRtTokPass) pass = kRtTokPass;
         if (pass > T) pass = T;
         s.pass = static_cast<uint32_t>(pass);
-        s.x_bytes = (pass * row + 15) / 16 * 16;
+        s.x_bytes = pass * row;
     } else {
         s.stride = 0;
         s.pass = kRtTokPass;
@@ -126,6 +135,19 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
+// atomic adds at gpu scope: release (the CTA's writes ordered before it by
+// the preceding __syncthreads are visible to an acquirer that reads the
+// count), and acquire-release (also sees the writes of the CTAs that counted
+// before)
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 template <typename T>
 __device__ __forceinline__ float4 rt_load4(const T* p, size_t i);
 template <>
@@ -139,343 +161,164 @@ __device__ __forceinline__ float4 rt_load4<uint16_t>(const uint16_t* p, size_t i
                        bf16_bits_to_f32(u.y >> 16));
 }
 
-template <typename XT>
-__global__ void __launch_bounds__(kRtThreads)
-moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
-                  uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
-                  const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
-                  uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps,
-                  const float* __restrict__ router_bias, MoeWs ws) {
-    extern __shared__ __align__(128) unsigned char rt_smem[];
-    __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
-    __shared__ uint32_t cta_flag;  // plan CTA selection
-    __shared__ uint32_t failed;    // a bounded wait expired
+__device__ __forceinline__ float bf16_round(float v) { return bf16_bits_to_f32(f32_to_bf16_bits(v)); }
+
+// acc = fma(w[c], x[c], acc) for c = 0..H-1 in order, f32 weights and
+// activations in shared memory (H a multiple of 16). A step is 16 columns;
+// the next step's reads are issued before the current 16 fmas, which take
+// longer than a shared-memory read's latency.
+__device__ __forceinline__ float rt_chain_f32(const float* __restrict__ wr, const float* __restrict__ xr, uint32_t H) {
+    float acc = 0.f;
+    float4 a[4], b[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        a[q] = *reinterpret_cast<const float4*>(wr + 4 * q);
+        b[q] = *reinterpret_cast<const float4*>(xr + 4 * q);
+    }
+    for (uint32_t c = 16;; c += 16) {
+        const uint32_t cn = c < H ? c : 0u;  // the last step re-reads column 0, unused
+        float4 na[4], nb[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            na[q] = *reinterpret_cast<const float4*>(wr + cn + 4 * q);
+            nb[q] = *reinterpret_cast<const float4*>(xr + cn + 4 * q);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            acc = fmaf(a[q].x, b[q].x, acc);
+            acc = fmaf(a[q].y, b[q].y, acc);
+            acc = fmaf(a[q].z, b[q].z, acc);
+            acc = fmaf(a[q].w, b[q].w, acc);
+        }
+        if (c >= H) break;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            a[q] = na[q];
+            b[q] = nb[q];
+        }
+    }
+    return acc;
+}
+
+// the same chain over columns [c0, ce) with bf16 weights
+__device__ __forceinline__ float rt_chain_bf16w(const uint16_t* __restrict__ wr, const float* __restrict__ xr,
+                                                uint32_t c0, uint32_t ce, float acc) {
+#pragma unroll 4
+    for (uint32_t c = c0; c < ce; c += 8) {
+        const uint4 q = *reinterpret_cast<const uint4*>(wr + c);
+        const float4 a = *reinterpret_cast<const float4*>(xr + c);
+        const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+        acc = fmaf(__uint_as_float(q.x << 16), a.x, acc);
+        acc = fmaf(__uint_as_float(q.x & 0xffff0000u), a.y, acc);
+        acc = fmaf(__uint_as_float(q.y << 16), a.z, acc);
+        acc = fmaf(__uint_as_float(q.y & 0xffff0000u), a.w, acc);
+        acc = fmaf(__uint_as_float(q.z << 16), b.x, acc);
+        acc = fmaf(__uint_as_float(q.z & 0xffff0000u), b.y, acc);
+        acc = fmaf(__uint_as_float(q.w << 16), b.z, acc);
+        acc = fmaf(__uint_as_float(q.w & 0xffff0000u), b.w, acc);
+    }
+    return acc;
+}
+
+// Layer-major group plan of the R = T*K routes, built by one warp: per-expert
+// counts in shared memory, an exclusive scan over the experts (a lane owns a
+// contiguous block of them), then the routes placed 32 at a time in route
+// order, lanes of the same expert ranked by __match_any_sync and a running
+// count per expert. Experts come out ascending and each expert's routes in
+// route order, the plan the block version builds. Loops stay rolled: the plan
+// runs once per launch, so its code size is its cost. `gs` is shared scratch
+// of 2 * (e_hi - e_lo) + 1 words.
+__device__ __noinline__ void plan_warp(uint32_t T, uint32_t K, uint32_t E, uint32_t e_lo, uint32_t e_hi,
+                                       bool has_shared, const MoeWs& ws, uint32_t* gs) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t R = T * K, EL = e_hi - e_lo;
+    uint32_t* cnt = gs;       // [EL] counts, then starts
+    uint32_t* run = gs + EL;  // [EL] routes of each expert placed so far
+#pragma unroll 1
+    for (uint32_t e = lane; e < EL; e += 32) cnt[e] = run[e] = 0;
+    __syncwarp();
+#pragma unroll 1
+    for (uint32_t r = lane; r < R; r += 32) {
+        const uint32_t e = __ldcg(ws.route_ids + r);
+        if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e - e_lo], 1u);
+    }
+    __syncwarp();
+    // exclusive scans of the counts and of the used flags over the experts
+    const uint32_t per = (EL + 31) / 32, lo = min(lane * per, EL), hi = min(lo + per, EL);
+    uint32_t routes = 0, used = 0;
+#pragma unroll 1
+    for (uint32_t e = lo; e < hi; ++e) {
+        routes += cnt[e];
+        used += cnt[e] ? 1u : 0u;
+    }
+    uint32_t r_incl = routes, u_incl = used;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t a = __shfl_up_sync(kFull, r_incl, o), b = __shfl_up_sync(kFull, u_incl, o);
+        if (lane >= o) {
+            r_incl += a;
+            u_incl += b;
+        }
+    }
+    const uint32_t U = __shfl_sync(kFull, u_incl, 31);
+    const uint32_t shared_groups = has_shared ? 1u : 0u;
+    const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared group
+    uint32_t start = r_incl - routes, g = u_incl - used;
+#pragma unroll 1
+    for (uint32_t e = lo; e < hi; ++e) {
+        const uint32_t c = cnt[e];
+        if (c) {
+            ws.group_expert[shared_groups + g] = e;
+            ws.group_start[shared_groups + g] = routed_base + start;
+            ws.group_count[shared_groups + g] = c;
+            ++g;
+        }
+        cnt[e] = start;
+        start += c;
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (uint32_t r0 = 0; r0 < R; r0 += 32) {
+        const uint32_t r = r0 + lane;
+        const uint32_t e = r < R ? __ldcg(ws.route_ids + r) : 0xffffffffu;
+        const bool mine = e >= e_lo && e < e_hi;
+        const uint32_t peers = __match_any_sync(kFull, mine ? e : 0xffffffffu);
+        if (mine) {
+            const uint32_t el = e - e_lo;
+            const uint32_t pos = routed_base + cnt[el] + run[el] + __popc(peers & ((1u << lane) - 1u));
+            ws.group_routes[pos] = r;
+            ws.group_tokens[pos] = r / K;
+        }
+        __syncwarp();
+        if (mine && (peers >> lane) == 1u) run[e - e_lo] += __popc(peers);  // the group's highest lane
+        __syncwarp();
+    }
+    if (has_shared) {
+#pragma unroll 1
+        for (uint32_t t = lane; t < T; t += 32) {
+            ws.group_routes[t] = R + t;
+            ws.group_tokens[t] = t;
+        }
+        if (lane == 0) {
+            ws.group_expert[0] = E;
+            ws.group_start[0] = 0;
+            ws.group_count[0] = T;
+        }
+    }
+    if (lane == 0) *ws.num_groups = U + shared_groups;
+}
+
+// The same plan by the whole CTA, for any number of routes: per-expert counts
+// and two block scans, ranks inside each expert from __match_any_sync.
+__device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint32_t e_lo, uint32_t e_hi,
+                                        bool has_shared, const MoeWs& ws, uint32_t* smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool bf16_rows = sizeof(XT) == 2 || in_norm_w != nullptr;
-    const RtSmem SL = rt_smem_layout(T, H, E, K, bf16_rows);
-    uint16_t* w_s = reinterpret_cast<uint16_t*>(rt_smem);
-    float* wf_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes);
-    float* x_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes);
-    uint16_t* xb_s = reinterpret_cast<uint16_t*>(rt_smem + SL.w_bytes + SL.wf_bytes);
-    float* scale_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes + SL.x_bytes);
-    const uint32_t nrows = E + (shared_gate_w ? 1u : 0u);
-    const uint32_t row0 = blockIdx.x * kRtRows;
-    const uint32_t rows_here = min(nrows - row0, static_cast<uint32_t>(kRtRows));
-    const uint32_t nchunks = (H + kRtChunk - 1) / kRtChunk;
-
-    // weights: the CTA's router rows (contiguous) in one bulk copy, the gate
-    // row in another; with f32 weight rows the chains start once all have
-    // landed (bars[0]), otherwise chunk by chunk (bars[k] per 256 columns)
-    if (threadIdx.x == 0) {
-        failed = 0;
-        const uint32_t router_rows = row0 < E ? min(E - row0, rows_here) : 0u;
-        if (SL.wf_bytes) {
-            mbar_init(&bars[0], 1);
-            fence_mbar_init();
-            mbar_arrive_expect_tx(&bars[0], rows_here * H * 2);
-            if (router_rows) bulk_load(w_s, router_w + static_cast<size_t>(row0) * H, router_rows * H * 2, &bars[0]);
-            if (router_rows < rows_here)
-                bulk_load(w_s + static_cast<size_t>(router_rows) * H, shared_gate_w, H * 2, &bars[0]);
-        } else {
-            for (uint32_t k = 0; k < nchunks; ++k) mbar_init(&bars[k], 1);
-            fence_mbar_init();
-            for (uint32_t k = 0; k < nchunks; ++k) {
-                const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
-                mbar_arrive_expect_tx(&bars[k], rows_here * cw * 2);
-                for (uint32_t r = 0; r < rows_here; ++r) {
-                    const uint32_t row = row0 + r;
-                    const uint16_t* src = (row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w) + c0;
-                    bulk_load(w_s + static_cast<size_t>(r) * H + c0, src, cw * 2, &bars[k]);
-                }
-            }
-        }
-    }
-    pdl_wait();
-
-    // per-token RMSNorm scales of the layer input (same formula as
-    // rms_norm_rows_kernel: 1 / sqrt(mean(s^2) + eps))
-    if (in_norm_w) {
-        for (uint32_t t = warp; t < T; t += kRtRows) {
-            float ss = 0.f;
-            for (uint32_t c = lane * 4; c < H; c += 128) {
-                const float4 v = rt_load4<XT>(x, static_cast<size_t>(t) * H + c);
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) scale_s[t] = 1.0f / sqrtf(ss / static_cast<float>(H) + in_eps);
-        }
-    }
-    __syncthreads();
-
-    const uint16_t* wrow = w_s + static_cast<size_t>(warp) * H;
-    const uint32_t nchunk_cols = kRtChunk;
-    auto wait_chunk = [&](uint32_t k) {
-        if (!failed && !mbar_wait_bounded(&bars[k], 0, kPipeWaitNs)) {
-            failed = 1;
-            latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
-        }
-    };
-    auto write_logit = [&](uint32_t t, float acc) {
-        const uint32_t row = row0 + warp;
-        if (row < E)
-            ws.logits[static_cast<size_t>(t) * E + row] = acc;
-        else
-            ws.shared_logit[t] = acc;
-    };
-
-    if (bf16_rows) {
-        // ---- bf16 token rows, staged once per pass
-        const uint32_t vpr = H / 8;  // 8-column vectors per row
-        for (uint32_t t0 = 0; t0 < T; t0 += SL.pass) {
-            const uint32_t tp = min(T - t0, SL.pass);
-            if (t0 > 0) __syncthreads();  // the previous pass's chains are done with the rows
-            constexpr int kTok = 4;
-            for (uint32_t tt0 = 0; tt0 < tp; tt0 += kTok) {
-                for (uint32_t v0 = threadIdx.x; v0 < vpr; v0 += 2 * kRtThreads) {
-                    constexpr int kW = sizeof(XT) == 2 ? 1 : 2;  // 16-byte words per 8 columns
-                    uint4 raw[kTok][2][kW];
-#pragma unroll
-                    for (int a = 0; a < kTok; ++a)
-#pragma unroll
-                        for (int bb = 0; bb < 2; ++bb) {
-                            const uint32_t tt = tt0 + a, v = v0 + bb * kRtThreads;
-                            if (tt < tp && v < vpr) {
-                                const uint4* src = reinterpret_cast<const uint4*>(
-                                    x + static_cast<size_t>(t0 + tt) * H + static_cast<size_t>(v) * 8);
-#pragma unroll
-                                for (int q = 0; q < kW; ++q) raw[a][bb][q] = src[q];
-                            }
-                        }
-#pragma unroll
-                    for (int a = 0; a < kTok; ++a)
-#pragma unroll
-                        for (int bb = 0; bb < 2; ++bb) {
-                            const uint32_t tt = tt0 + a, v = v0 + bb * kRtThreads;
-                            if (tt < tp && v < vpr) {
-                                uint4 pk;
-                                if (sizeof(XT) == 2 && !in_norm_w) {
-                                    pk = raw[a][bb][0];  // bf16 rows as they are
-                                } else {
-                                    float f[8];
-                                    if constexpr (sizeof(XT) == 2) {
-                                        const uint4 r = raw[a][bb][0];
-                                        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                                        for (int q = 0; q < 4; ++q) {
-                                            f[2 * q] = __uint_as_float(w4[q] << 16);
-                                            f[2 * q + 1] = __uint_as_float(w4[q] & 0xffff0000u);
-                                        }
-                                    } else {
-#pragma unroll
-                                        for (int q = 0; q < 2; ++q) {
-                                            const uint4 r = raw[a][bb][q % kW];
-                                            f[4 * q] = __uint_as_float(r.x), f[4 * q + 1] = __uint_as_float(r.y);
-                                            f[4 * q + 2] = __uint_as_float(r.z), f[4 * q + 3] = __uint_as_float(r.w);
-                                        }
-                                    }
-                                    uint32_t bits[8];
-                                    if (in_norm_w) {
-                                        const float sc = scale_s[t0 + tt];
-                                        const float4 n0 = *reinterpret_cast<const float4*>(in_norm_w + v * 8);
-                                        const float4 n1 = *reinterpret_cast<const float4*>(in_norm_w + v * 8 + 4);
-                                        const float nn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-#pragma unroll
-                                        for (int q = 0; q < 8; ++q) bits[q] = f32_to_bf16_bits(f[q] * sc * nn[q]);
-                                    } else {
-#pragma unroll
-                                        for (int q = 0; q < 8; ++q) bits[q] = f32_to_bf16_bits(f[q]);
-                                    }
-                                    pk = make_uint4(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16),
-                                                    bits[4] | (bits[5] << 16), bits[6] | (bits[7] << 16));
-                                }
-                                *reinterpret_cast<uint4*>(xb_s + static_cast<size_t>(tt) * SL.stride + v * 8) = pk;
-                                // the normalised rows for the experts: token t's row by CTA t mod grid
-                                if (in_norm_w && (t0 + tt) % gridDim.x == blockIdx.x)
-                                    *reinterpret_cast<uint4*>(ws.xn + static_cast<size_t>(t0 + tt) * H + v * 8) = pk;
-                            }
-                        }
-                }
-            }
-            if (SL.wf_bytes && t0 == 0) {
-                // the weights have landed: f32 copy of the rows, once
-                wait_chunk(0);
-                const uint32_t nvec = rows_here * H / 8;
-                for (uint32_t i = threadIdx.x; i < nvec; i += kRtThreads) {
-                    const uint4 q = *reinterpret_cast<const uint4*>(w_s + static_cast<size_t>(i) * 8);
-                    float4* d = reinterpret_cast<float4*>(wf_s + static_cast<size_t>(i) * 8);
-                    d[0] = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
-                                       __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
-                    d[1] = make_float4(__uint_as_float(q.z << 16), __uint_as_float(q.z & 0xffff0000u),
-                                       __uint_as_float(q.w << 16), __uint_as_float(q.w & 0xffff0000u));
-                }
-            }
-            __syncthreads();
-            if (SL.wf_bytes && static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp) {
-                const uint16_t* xr = xb_s + static_cast<size_t>(lane) * SL.stride;
-                const float* wr = wf_s + static_cast<size_t>(warp) * H;
-                float acc = 0.f;
-#pragma unroll 4
-                for (uint32_t c = 0; c < H; c += 8) {
-                    const float4 w0 = *reinterpret_cast<const float4*>(wr + c);
-                    const float4 w1 = *reinterpret_cast<const float4*>(wr + c + 4);
-                    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
-                    acc = fmaf(w0.x, __uint_as_float(xv.x << 16), acc);
-                    acc = fmaf(w0.y, __uint_as_float(xv.x & 0xffff0000u), acc);
-                    acc = fmaf(w0.z, __uint_as_float(xv.y << 16), acc);
-                    acc = fmaf(w0.w, __uint_as_float(xv.y & 0xffff0000u), acc);
-                    acc = fmaf(w1.x, __uint_as_float(xv.z << 16), acc);
-                    acc = fmaf(w1.y, __uint_as_float(xv.z & 0xffff0000u), acc);
-                    acc = fmaf(w1.z, __uint_as_float(xv.w << 16), acc);
-                    acc = fmaf(w1.w, __uint_as_float(xv.w & 0xffff0000u), acc);
-                }
-                write_logit(t0 + lane, acc);
-            } else if (static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp) {
-                const uint16_t* xr = xb_s + static_cast<size_t>(lane) * SL.stride;
-                float acc = 0.f;
-                for (uint32_t k = 0; k < nchunks; ++k) {
-                    wait_chunk(k);
-                    const uint32_t c0 = k * nchunk_cols, ce = min(H, c0 + nchunk_cols);
-#pragma unroll 4
-                    for (uint32_t c = c0; c < ce; c += 8) {
-                        const uint4 q = *reinterpret_cast<const uint4*>(wrow + c);
-                        const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
-                        acc = fmaf(__uint_as_float(q.x << 16), __uint_as_float(xv.x << 16), acc);
-                        acc = fmaf(__uint_as_float(q.x & 0xffff0000u), __uint_as_float(xv.x & 0xffff0000u), acc);
-                        acc = fmaf(__uint_as_float(q.y << 16), __uint_as_float(xv.y << 16), acc);
-                        acc = fmaf(__uint_as_float(q.y & 0xffff0000u), __uint_as_float(xv.y & 0xffff0000u), acc);
-                        acc = fmaf(__uint_as_float(q.z << 16), __uint_as_float(xv.z << 16), acc);
-                        acc = fmaf(__uint_as_float(q.z & 0xffff0000u), __uint_as_float(xv.z & 0xffff0000u), acc);
-                        acc = fmaf(__uint_as_float(q.w << 16), __uint_as_float(xv.w << 16), acc);
-                        acc = fmaf(__uint_as_float(q.w & 0xffff0000u), __uint_as_float(xv.w & 0xffff0000u), acc);
-                    }
-                }
-                write_logit(t0 + lane, acc);
-            }
-        }
-    } else {
-        // ---- f32 token rows (f32 input, no norm): 256-column chunks, double-buffered
-        float4 reg[kRtVecs];
-        auto load_regs = [&](uint32_t t0, uint32_t tp, uint32_t k) {
-            const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
-            const uint32_t vpr = cw / 4, total = tp * vpr;
-#pragma unroll
-            for (int j = 0; j < kRtVecs; ++j) {
-                const uint32_t i = threadIdx.x + j * kRtThreads;
-                if (i < total) {
-                    const uint32_t tt = i / vpr, cc = (i - tt * vpr) * 4;
-                    reg[j] = rt_load4<XT>(x, static_cast<size_t>(t0 + tt) * H + c0 + cc);
-                }
-            }
-        };
-        auto store_regs = [&](uint32_t tp, uint32_t k, float* dst) {
-            const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
-            const uint32_t vpr = cw / 4, total = tp * vpr;
-#pragma unroll
-            for (int j = 0; j < kRtVecs; ++j) {
-                const uint32_t i = threadIdx.x + j * kRtThreads;
-                if (i < total) {
-                    const uint32_t tt = i / vpr, cc = (i - tt * vpr) * 4;
-                    *reinterpret_cast<float4*>(dst + tt * kRtXStride + cc) = reg[j];
-                }
-            }
-        };
-        const uint32_t xbuf = kRtTokPass * kRtXStride;  // floats per staging buffer
-        for (uint32_t t0 = 0; t0 < T; t0 += kRtTokPass) {
-            const uint32_t tp = min(T - t0, kRtTokPass);
-            const bool mine = static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp;
-            load_regs(t0, tp, 0);
-            store_regs(tp, 0, x_s);
-            __syncthreads();
-            float acc = 0.f;
-            for (uint32_t k = 0; k < nchunks; ++k) {
-                if (k + 1 < nchunks) load_regs(t0, tp, k + 1);
-                if (mine) {
-                    wait_chunk(k);
-                    const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
-                    const uint16_t* wr = wrow + c0;
-                    const float* xr = x_s + (k & 1u) * xbuf + lane * kRtXStride;
-#pragma unroll 4
-                    for (uint32_t c = 0; c < cw; c += 8) {
-                        const uint4 q = *reinterpret_cast<const uint4*>(wr + c);
-                        const float4 a = *reinterpret_cast<const float4*>(xr + c);
-                        const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
-                        acc = fmaf(__uint_as_float(q.x << 16), a.x, acc);
-                        acc = fmaf(__uint_as_float(q.x & 0xffff0000u), a.y, acc);
-                        acc = fmaf(__uint_as_float(q.y << 16), a.z, acc);
-                        acc = fmaf(__uint_as_float(q.y & 0xffff0000u), a.w, acc);
-                        acc = fmaf(__uint_as_float(q.z << 16), b.x, acc);
-                        acc = fmaf(__uint_as_float(q.z & 0xffff0000u), b.y, acc);
-                        acc = fmaf(__uint_as_float(q.w << 16), b.z, acc);
-                        acc = fmaf(__uint_as_float(q.w & 0xffff0000u), b.w, acc);
-                    }
-                }
-                if (k + 1 < nchunks) store_regs(tp, k + 1, x_s + ((k + 1) & 1u) * xbuf);
-                __syncthreads();
-            }
-            if (mine) write_logit(t0 + lane, acc);
-        }
-    }
-
-    // ---- arrival; the routing CTAs wait for every CTA's logits
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&ws.ticket[0], 1u);
-    }
-    const uint32_t route_ctas = min(min(gridDim.x, kRtRouteCtas), (T + kRtRows - 1) / kRtRows);
-    auto drain = [&]() {  // after an expired wait, let this CTA's own copies land (bounded) before it exits
-        if (threadIdx.x == 0 && failed)
-            for (uint32_t k = 0; k < (SL.wf_bytes ? 1u : nchunks); ++k) mbar_wait_bounded(&bars[k], 0, kPipeWaitNs);
-    };
-    if (blockIdx.x >= route_ctas) {
-        drain();
-        return;
-    }
-    if (threadIdx.x == 0) {
-        const uint64_t t_start = global_ns();
-        while (ld_acquire_gpu(&ws.ticket[0]) < gridDim.x) {
-            if (global_ns() - t_start > kPipeWaitNs) {
-                latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
-                break;
-            }
-            __nanosleep(64);
-        }
-        __threadfence();
-    }
-    __syncthreads();
-    // every CTA of this grid has started: the expert kernel may be scheduled
-    // now and run its prologue under the routing; it reads the plan only after
-    // griddepcontrol.wait, i.e. after this grid completes
-    pdl_launch_dependents();
-    {
-        const uint32_t Ep = (E + 3) & ~3u;
-        float* s = reinterpret_cast<float*>(rt_smem) + warp * Ep;  // the staging area is free now
-        for (uint32_t t = blockIdx.x * kRtRows + warp; t < T; t += route_ctas * kRtRows) {
-            stage_logits_warp(ws.logits + static_cast<size_t>(t) * E, E, s);
-            route_token(s, E, K, normalization, routed_scale, ws.route_ids + static_cast<size_t>(t) * K,
-                        ws.route_w + static_cast<size_t>(t) * K, ws.status, router_bias,
-                        ws.logits + static_cast<size_t>(t) * E);
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        cta_flag = (atomicAdd(&ws.ticket[1], 1u) == route_ctas - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (!cta_flag) {
-        drain();
-        return;
-    }
-    __threadfence();
-
-    // group plan (the last routing CTA); shared memory reuses the staging area
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(rt_smem);  // [E] counts -> starts
-    uint32_t* gidx = cnt + E;                          // [E] used flags -> group index
-    uint32_t* run = gidx + E;                          // [E] routes of each expert placed so far
-    uint32_t* ids = run + E;                           // [T*K]
-    uint32_t* rnk = ids + T * K;                       // [T*K] rank of each route inside its group
-    uint32_t* tmp = rnk + T * K;                       // [32]
+    uint32_t* cnt = smem;             // [E] counts -> starts
+    uint32_t* gidx = cnt + E;         // [E] used flags -> group index
+    uint32_t* run = gidx + E;         // [E] routes of each expert placed so far
+    uint32_t* ids = run + E;          // [T*K]
+    uint32_t* rnk = ids + T * K;      // [T*K] rank of each route inside its group
+    uint32_t* tmp = rnk + T * K;      // [32]
     const uint32_t R = T * K;
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = run[e] = 0;
     __syncthreads();
@@ -536,8 +379,292 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
             ws.group_count[0] = T;
         }
     }
+    if (threadIdx.x == 0) *ws.num_groups = U + shared_groups;
+}
+
+template <typename XT>
+__global__ void __launch_bounds__(kRtThreads)
+moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
+                  uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
+                  const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
+                  uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps,
+                  const float* __restrict__ router_bias, MoeWs ws) {
+    extern __shared__ __align__(128) unsigned char rt_smem[];
+    __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
+    __shared__ uint32_t cta_flag;  // plan CTA selection
+    __shared__ uint32_t failed;    // a bounded wait expired
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool staged_rows = sizeof(XT) == 2 || in_norm_w != nullptr;
+    const RtSmem SL = rt_smem_layout(T, H, E, K, staged_rows);
+    uint16_t* w_s = reinterpret_cast<uint16_t*>(rt_smem);
+    float* wf_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes);
+    float* x_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes);
+    float* scale_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes + SL.x_bytes);
+    const uint32_t nrows = E + (shared_gate_w ? 1u : 0u);
+    const uint32_t rpc = rt_rows_per_cta(H);
+    const uint32_t row0 = blockIdx.x * rpc;
+    const uint32_t rows_here = min(nrows - row0, rpc);
+    const uint32_t nchunks = (H + kRtChunk - 1) / kRtChunk;
+
+    // weights: the CTA's router rows (contiguous) in one bulk copy, the gate
+    // row in another; with f32 weight rows the chains start once all have
+    // landed (bars[0]), otherwise chunk by chunk (bars[k] per 256 columns)
     if (threadIdx.x == 0) {
-        *ws.num_groups = U + shared_groups;
+        failed = 0;
+        const uint32_t router_rows = row0 < E ? min(E - row0, rows_here) : 0u;
+        if (SL.wf_bytes) {
+            mbar_init(&bars[0], 1);
+            fence_mbar_init();
+            mbar_arrive_expect_tx(&bars[0], rows_here * H * 2);
+            if (router_rows) bulk_load(w_s, router_w + static_cast<size_t>(row0) * H, router_rows * H * 2, &bars[0]);
+            if (router_rows < rows_here)
+                bulk_load(w_s + static_cast<size_t>(router_rows) * H, shared_gate_w, H * 2, &bars[0]);
+        } else {
+            for (uint32_t k = 0; k < nchunks; ++k) mbar_init(&bars[k], 1);
+            fence_mbar_init();
+            for (uint32_t k = 0; k < nchunks; ++k) {
+                const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+                mbar_arrive_expect_tx(&bars[k], rows_here * cw * 2);
+                for (uint32_t r = 0; r < rows_here; ++r) {
+                    const uint32_t row = row0 + r;
+                    const uint16_t* src = (row < E ? router_w + static_cast<size_t>(row) * H : shared_gate_w) + c0;
+                    bulk_load(w_s + static_cast<size_t>(r) * (H + 8) + c0, src, cw * 2, &bars[k]);
+                }
+            }
+        }
+    }
+    pdl_wait();
+    __syncthreads();  // `failed` initialised
+
+    auto wait_chunk = [&](uint32_t k) {
+        if (!failed && !mbar_wait_bounded(&bars[k], 0, kPipeWaitNs)) {
+            failed = 1;
+            latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+        }
+    };
+    auto write_logit = [&](uint32_t t, uint32_t r, float acc) {
+        const uint32_t row = row0 + r;
+        if (row < E)
+            ws.logits[static_cast<size_t>(t) * E + row] = acc;
+        else
+            ws.shared_logit[t] = acc;
+    };
+
+    if (staged_rows) {
+        // per-token RMSNorm scales of the layer input (the formula of
+        // rms_norm_rows_kernel: 1 / sqrt(mean(x^2) + eps)), one warp per token
+        if (in_norm_w) {
+            for (uint32_t t = warp; t < T; t += kRtRows) {
+                const XT* xr = x + static_cast<size_t>(t) * H;
+                float ss = 0.f;
+                for (uint32_t c0 = 0; c0 < H; c0 += 128 * 8) {
+                    float4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c = c0 + j * 128 + lane * 4;
+                        v[j] = c < H ? rt_load4<XT>(xr, c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+                }
+                ss = warp_sum(ss);
+                if (lane == 0) scale_s[t] = 1.0f / sqrtf(ss / static_cast<float>(H) + in_eps);
+            }
+            __syncthreads();
+        }
+        for (uint32_t t0 = 0; t0 < T; t0 += SL.pass) {
+            const uint32_t tp = min(T - t0, SL.pass);
+            if (t0 > 0) __syncthreads();  // the previous pass's chains are done with the rows
+            // one warp per token: the row as f32 (bf16-rounded when normalised
+            // here), the normalised row also to ws.xn from CTA t mod grid
+            for (uint32_t tt = warp; tt < tp; tt += kRtRows) {
+                const uint32_t t = t0 + tt;
+                const XT* xr = x + static_cast<size_t>(t) * H;
+                float* dst = x_s + static_cast<size_t>(tt) * SL.stride;
+                const float sc = in_norm_w ? scale_s[t] : 1.f;
+                const bool owner = in_norm_w && t % gridDim.x == blockIdx.x;
+                for (uint32_t c0 = 0; c0 < H; c0 += 128 * 8) {
+                    float4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c = c0 + j * 128 + lane * 4;
+                        if (c < H) v[j] = rt_load4<XT>(xr, c);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c = c0 + j * 128 + lane * 4;
+                        if (c >= H) continue;
+                        float4 o = v[j];
+                        if (in_norm_w) {
+                            const float4 n = *reinterpret_cast<const float4*>(in_norm_w + c);
+                            o = make_float4(bf16_round(o.x * sc * n.x), bf16_round(o.y * sc * n.y),
+                                            bf16_round(o.z * sc * n.z), bf16_round(o.w * sc * n.w));
+                            if (owner) {
+                                const uint2 pk = make_uint2(f32_to_bf16_bits(o.x) | (f32_to_bf16_bits(o.y) << 16),
+                                                            f32_to_bf16_bits(o.z) | (f32_to_bf16_bits(o.w) << 16));
+                                *reinterpret_cast<uint2*>(ws.xn + static_cast<size_t>(t) * H + c) = pk;
+                            }
+                        }
+                        *reinterpret_cast<float4*>(dst + c) = o;
+                    }
+                }
+            }
+            if (SL.wf_bytes && t0 == 0) {
+                // the weights have landed: f32 copy of the rows, once
+                wait_chunk(0);
+                const uint32_t vpr = H / 8, nvec = rows_here * vpr;
+                for (uint32_t i = threadIdx.x; i < nvec; i += kRtThreads) {
+                    const uint32_t r = i / vpr, c = (i - r * vpr) * 8;
+                    const uint4 q = *reinterpret_cast<const uint4*>(w_s + static_cast<size_t>(i) * 8);
+                    float4* d = reinterpret_cast<float4*>(wf_s + static_cast<size_t>(r) * (H + 4) + c);
+                    d[0] = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
+                                       __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
+                    d[1] = make_float4(__uint_as_float(q.z << 16), __uint_as_float(q.z & 0xffff0000u),
+                                       __uint_as_float(q.w << 16), __uint_as_float(q.w & 0xffff0000u));
+                }
+            }
+            __syncthreads();
+            // a warp runs 4 rows x 8 tokens (its weight reads are 4 distinct
+            // 16-byte words, its activation reads 8): row group rg, token group tg
+            const uint32_t rgroups = rpc / 4, rg = warp % rgroups, tg = warp / rgroups;
+            const uint32_t r = rg * 4 + (lane >> 3), tt = tg * 8 + (lane & 7);
+            if (r < rows_here && tt < tp) {
+                const float* xr = x_s + static_cast<size_t>(tt) * SL.stride;
+                float acc;
+                if (SL.wf_bytes) {
+                    acc = rt_chain_f32(wf_s + static_cast<size_t>(r) * (H + 4), xr, H);
+                } else {
+                    acc = 0.f;
+                    const uint16_t* wrow = w_s + static_cast<size_t>(r) * (H + 8);
+                    for (uint32_t k = 0; k < nchunks; ++k) {
+                        wait_chunk(k);
+                        acc = rt_chain_bf16w(wrow, xr, k * kRtChunk, min(H, (k + 1) * kRtChunk), acc);
+                    }
+                }
+                write_logit(t0 + tt, r, acc);
+            }
+        }
+    } else {
+        // ---- f32 token rows (f32 input, no norm): 256-column chunks, double-buffered
+        const uint16_t* wrow = w_s + static_cast<size_t>(warp) * (H + 8);
+        float4 reg[kRtVecs];
+        auto load_regs = [&](uint32_t t0, uint32_t tp, uint32_t k) {
+            const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+            const uint32_t vpr = cw / 4, total = tp * vpr;
+#pragma unroll
+            for (int j = 0; j < kRtVecs; ++j) {
+                const uint32_t i = threadIdx.x + j * kRtThreads;
+                if (i < total) {
+                    const uint32_t tt = i / vpr, cc = (i - tt * vpr) * 4;
+                    reg[j] = rt_load4<XT>(x, static_cast<size_t>(t0 + tt) * H + c0 + cc);
+                }
+            }
+        };
+        auto store_regs = [&](uint32_t tp, uint32_t k, float* dst) {
+            const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+            const uint32_t vpr = cw / 4, total = tp * vpr;
+#pragma unroll
+            for (int j = 0; j < kRtVecs; ++j) {
+                const uint32_t i = threadIdx.x + j * kRtThreads;
+                if (i < total) {
+                    const uint32_t tt = i / vpr, cc = (i - tt * vpr) * 4;
+                    *reinterpret_cast<float4*>(dst + tt * kRtXStride + cc) = reg[j];
+                }
+            }
+        };
+        const uint32_t xbuf = kRtTokPass * kRtXStride;  // floats per staging buffer
+        for (uint32_t t0 = 0; t0 < T; t0 += kRtTokPass) {
+            const uint32_t tp = min(T - t0, kRtTokPass);
+            const bool mine = static_cast<uint32_t>(warp) < rows_here && static_cast<uint32_t>(lane) < tp;
+            if (t0 > 0) __syncthreads();
+            load_regs(t0, tp, 0);
+            store_regs(tp, 0, x_s);
+            __syncthreads();
+            float acc = 0.f;
+            for (uint32_t k = 0; k < nchunks; ++k) {
+                if (k + 1 < nchunks) load_regs(t0, tp, k + 1);
+                if (mine) {
+                    wait_chunk(k);
+                    const uint32_t c0 = k * kRtChunk, cw = min(kRtChunk, H - c0);
+                    const uint16_t* wr = wrow + c0;
+                    const float* xr = x_s + (k & 1u) * xbuf + lane * kRtXStride;
+#pragma unroll 4
+                    for (uint32_t c = 0; c < cw; c += 8) {
+                        const uint4 q = *reinterpret_cast<const uint4*>(wr + c);
+                        const float4 a = *reinterpret_cast<const float4*>(xr + c);
+                        const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+                        acc = fmaf(__uint_as_float(q.x << 16), a.x, acc);
+                        acc = fmaf(__uint_as_float(q.x & 0xffff0000u), a.y, acc);
+                        acc = fmaf(__uint_as_float(q.y << 16), a.z, acc);
+                        acc = fmaf(__uint_as_float(q.y & 0xffff0000u), a.w, acc);
+                        acc = fmaf(__uint_as_float(q.z << 16), b.x, acc);
+                        acc = fmaf(__uint_as_float(q.z & 0xffff0000u), b.y, acc);
+                        acc = fmaf(__uint_as_float(q.w << 16), b.z, acc);
+                        acc = fmaf(__uint_as_float(q.w & 0xffff0000u), b.w, acc);
+                    }
+                }
+                if (k + 1 < nchunks) store_regs(tp, k + 1, x_s + ((k + 1) & 1u) * xbuf);
+                __syncthreads();
+            }
+            if (mine) write_logit(t0 + lane, warp, acc);
+        }
+    }
+
+    // ---- arrival; the routing CTAs wait for every CTA's logits
+    __syncthreads();
+    if (threadIdx.x == 0) red_add_release_gpu(&ws.ticket[0], 1u);
+    const uint32_t route_ctas = min(min(gridDim.x, kRtRouteCtas), (T + kRtRows - 1) / kRtRows);
+    auto drain = [&]() {  // after an expired wait, let this CTA's own copies land (bounded) before it exits
+        if (threadIdx.x == 0 && failed)
+            for (uint32_t k = 0; k < (SL.wf_bytes ? 1u : nchunks); ++k) mbar_wait_bounded(&bars[k], 0, kPipeWaitNs);
+    };
+    if (blockIdx.x >= route_ctas) {
+        drain();
+        return;
+    }
+    if (threadIdx.x == 0) {
+        const uint64_t t_start = global_ns();
+        while (ld_acquire_gpu(&ws.ticket[0]) < gridDim.x) {
+            if (global_ns() - t_start > kPipeWaitNs) {
+                latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+                break;
+            }
+            __nanosleep(32);
+        }
+    }
+    __syncthreads();
+    // every CTA of this grid has started: the expert kernel may be scheduled
+    // now and run its prologue under the routing; it reads the plan only after
+    // griddepcontrol.wait, i.e. after this grid completes
+    pdl_launch_dependents();
+    {
+        const uint32_t Ep = (E + 3) & ~3u;
+        float* s = reinterpret_cast<float*>(rt_smem) + warp * Ep;  // the staging area is free now
+        for (uint32_t t = blockIdx.x * kRtRows + warp; t < T; t += route_ctas * kRtRows) {
+            stage_logits_warp(ws.logits + static_cast<size_t>(t) * E, E, s);
+            route_token(s, E, K, normalization, routed_scale, ws.route_ids + static_cast<size_t>(t) * K,
+                        ws.route_w + static_cast<size_t>(t) * K, ws.status, router_bias,
+                        ws.logits + static_cast<size_t>(t) * E);
+        }
+    }
+    __syncthreads();
+    if (route_ctas > 1) {
+        if (threadIdx.x == 0) cta_flag = (atom_add_acq_rel_gpu(&ws.ticket[1], 1u) == route_ctas - 1) ? 1u : 0u;
+        __syncthreads();
+        if (!cta_flag) {
+            drain();
+            return;
+        }
+    }
+
+    // group plan; shared memory reuses the staging area
+    uint32_t* plan_smem = reinterpret_cast<uint32_t*>(rt_smem);
+    if (T * K <= kRtWarpPlanRoutes) {
+        if (warp == 0) plan_warp(T, K, E, e_lo, e_hi, has_shared != 0, ws, plan_smem);
+    } else {
+        plan_block(T, K, E, e_lo, e_hi, has_shared != 0, ws, plan_smem);
+    }
+    if (threadIdx.x == 0) {
         ws.ticket[0] = 0;  // ready for the next launch
         ws.ticket[1] = 0;
         if (ep_epoch) *ep_epoch += 1u;  // this layer's expert-parallel exchange epoch
@@ -974,7 +1101,8 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     // 1. router + routing + plan
     {
         const uint32_t nrows = E + (has_gate ? 1u : 0u);
-        dim3 grid((nrows + kRtRows - 1) / kRtRows);
+        const uint32_t rpc = rt_rows_per_cta(H);
+        dim3 grid((nrows + rpc - 1) / rpc);
         const size_t smem = rt_smem_layout(T, H, E, K, sizeof(XT) == 2 || a.in_norm_w != nullptr).total;
         auto fn = moe_router_kernel<XT>;
         if ((err = set_smem(fn, smem)) != cudaSuccess) return err;

@@ -112,7 +112,7 @@ extern "C" PBMOE_API int pbmoe_moe_layer_static(const pbmoe_moe_config* c, const
                       "moe layer (static): %u tokens need %zu scratch bytes, more than the fixed %zu-byte array "
                       "(use pbmoe_moe_layer with pbmoe_reserve)",
                       tokens, need, kStaticScratchBytes);
-    if (moe_router_smem(tokens, H, E, K) > 200 * 1024)
+    if (moe_router_smem(tokens, H, E, K) > kRouterSmemLimit)
         return report(error_buf, error_len, PBMOE_ERR_UNSUPPORTED, "router staging exceeds shared memory");
 
     int device = 0;

@@ -263,7 +263,7 @@ struct Q4MmaFrag4 {
                                          uint32_t gpr, uint32_t grp0, int t) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            w[j] = *reinterpret_cast<const uint2*>(row_g + (grp0 + j) * (kMmaGroup / 2) + 8 * t);
+            w[j] = ld_stream_u2(row_g + (grp0 + j) * (kMmaGroup / 2) + 8 * t);
         sa = *reinterpret_cast<const uint2*>(s_row_2t + grp0);
         sb = *reinterpret_cast<const uint2*>(s_row_2t + gpr + grp0);
         ba = *reinterpret_cast<const uint2*>(b_row_2t + grp0);
