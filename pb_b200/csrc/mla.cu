@@ -97,21 +97,23 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
                                                          float* __restrict__ qp) {
     __shared__ float qs[kMlaMaxBatch * kAbsorbMaxNope];
     __shared__ float red[4][8][64];
-    pdl_wait();
-    pdl_launch_dependents();
     const uint32_t h = blockIdx.x, tid = threadIdx.x;
     const uint32_t quarter = tid >> 6, cc = tid & 63, c = blockIdx.y * 64 + cc;
     const uint32_t qdim = nope + kMlaRope;
-    for (uint32_t i = tid; i < batch * nope; i += blockDim.x) {
-        const uint32_t b = i / nope, d = i % nope;
-        qs[i] = load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + d);
-    }
+    // W_UK does not depend on the earlier kernels: its loads are issued before
+    // waiting for them
     const uint32_t dq = (nope + 3) / 4, d0 = quarter * dq;
     float w[kAbsorbMaxNope / 4];
     const uint16_t* wcol = w_uk + static_cast<size_t>(h) * nope * kMlaLatent + c;
 #pragma unroll
     for (uint32_t i = 0; i < kAbsorbMaxNope / 4; ++i)
         w[i] = (i < dq && d0 + i < nope) ? bf16_bits_to_f32(wcol[static_cast<size_t>(d0 + i) * kMlaLatent]) : 0.f;
+    pdl_wait();
+    pdl_launch_dependents();
+    for (uint32_t i = tid; i < batch * nope; i += blockDim.x) {
+        const uint32_t b = i / nope, d = i % nope;
+        qs[i] = load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + d);
+    }
     __syncthreads();
     for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
         float acc[8];

@@ -90,18 +90,21 @@ constexpr uint32_t kRtRouteCtas = 64;
 constexpr size_t kRtStageBudget = 216 * 1024;  // weights + staged token rows of one pass
 constexpr int kRtVecs = static_cast<int>(kRtTokPass * kRtChunk / 4 / kRtThreads);  // float4 per thread per chunk
 constexpr uint32_t kRtWarpPlanRoutes = 256;    // plans of at most this many routes are built by one warp
+constexpr uint32_t kRtBlk = 2048;              // columns of a token row held in registers while staging
 
 // router rows per CTA for hidden size H: all kRtRows warps when their bf16
 // rows leave room for a staged token row, else half
 __host__ __device__ inline uint32_t rt_rows_per_cta(uint32_t H) { return H <= 8192 ? kRtRows : kRtRows / 2; }
 
 struct RtSmem {
-    size_t w_bytes, wf_bytes, x_bytes, total;
+    size_t w_bytes, wf_bytes, x_bytes, nw_bytes, total;
     uint32_t pass;    // tokens per pass
     uint32_t stride;  // floats per staged row (staged rows)
 };
-__host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_t E, uint32_t K, bool staged_rows) {
+__host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_t E, uint32_t K, bool staged_rows,
+                                                  bool norm) {
     RtSmem s;
+    s.nw_bytes = norm ? static_cast<size_t>(H) * 4 : 0;  // the input norm's weights
     const size_t rpc = rt_rows_per_cta(H);
     s.w_bytes = (rpc * (H + 8) * 2 + 127) / 128 * 128;
     s.wf_bytes = 0;
@@ -109,7 +112,7 @@ __host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_
         if (rpc * (H + 4) * 4 + s.w_bytes <= 100 * 1024) s.wf_bytes = rpc * (H + 4) * 4;
         s.stride = H + 4;
         const size_t row = static_cast<size_t>(s.stride) * 4;
-        const size_t used = s.w_bytes + s.wf_bytes + static_cast<size_t>(T) * 4;
+        const size_t used = s.w_bytes + s.wf_bytes + s.nw_bytes;
         size_t pass = used < kRtStageBudget ? (kRtStageBudget - used) / row : 1;
         if (pass < 1) pass = 1;
         if (pass > kRtTokPass) pass = kRtTokPass;
@@ -121,7 +124,7 @@ __host__ __device__ inline RtSmem rt_smem_layout(uint32_t T, uint32_t H, uint32_
         s.pass = kRtTokPass;
         s.x_bytes = static_cast<size_t>(2) * kRtTokPass * kRtXStride * 4;
     }
-    const size_t stage = s.w_bytes + s.wf_bytes + s.x_bytes + static_cast<size_t>(T) * 4;  // + norm scales
+    const size_t stage = s.w_bytes + s.wf_bytes + s.x_bytes + s.nw_bytes;
     const size_t plan = (3ull * E + 2ull * T * K + 32) * 4;
     const size_t route = static_cast<size_t>(kRtRows) * ((E + 3) & ~3u) * 4;
     size_t m = stage > plan ? stage : plan;
@@ -391,15 +394,16 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
                   const float* __restrict__ router_bias, MoeWs ws) {
     extern __shared__ __align__(128) unsigned char rt_smem[];
     __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
+    __shared__ __align__(8) uint64_t nbar;  // the norm weights
     __shared__ uint32_t cta_flag;  // plan CTA selection
     __shared__ uint32_t failed;    // a bounded wait expired
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool staged_rows = sizeof(XT) == 2 || in_norm_w != nullptr;
-    const RtSmem SL = rt_smem_layout(T, H, E, K, staged_rows);
+    const RtSmem SL = rt_smem_layout(T, H, E, K, staged_rows, in_norm_w != nullptr);
     uint16_t* w_s = reinterpret_cast<uint16_t*>(rt_smem);
     float* wf_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes);
     float* x_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes);
-    float* scale_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes + SL.x_bytes);
+    float* nw_s = reinterpret_cast<float*>(rt_smem + SL.w_bytes + SL.wf_bytes + SL.x_bytes);
     const uint32_t nrows = E + (shared_gate_w ? 1u : 0u);
     const uint32_t rpc = rt_rows_per_cta(H);
     const uint32_t row0 = blockIdx.x * rpc;
@@ -408,9 +412,16 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
 
     // weights: the CTA's router rows (contiguous) in one bulk copy, the gate
     // row in another; with f32 weight rows the chains start once all have
-    // landed (bars[0]), otherwise chunk by chunk (bars[k] per 256 columns)
+    // landed (bars[0]), otherwise chunk by chunk (bars[k] per 256 columns).
+    // The input norm's weights land on nbar.
     if (threadIdx.x == 0) {
         failed = 0;
+        if (in_norm_w) {
+            mbar_init(&nbar, 1);
+            fence_mbar_init();
+            mbar_arrive_expect_tx(&nbar, H * 4);
+            bulk_load(nw_s, in_norm_w, H * 4, &nbar);
+        }
         const uint32_t router_rows = row0 < E ? min(E - row0, rows_here) : 0u;
         if (SL.wf_bytes) {
             mbar_init(&bars[0], 1);
@@ -451,52 +462,53 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     };
 
     if (staged_rows) {
-        // per-token RMSNorm scales of the layer input (the formula of
-        // rms_norm_rows_kernel: 1 / sqrt(mean(x^2) + eps)), one warp per token
-        if (in_norm_w) {
-            for (uint32_t t = warp; t < T; t += kRtRows) {
-                const XT* xr = x + static_cast<size_t>(t) * H;
-                float ss = 0.f;
-                for (uint32_t c0 = 0; c0 < H; c0 += 128 * 8) {
-                    float4 v[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t c = c0 + j * 128 + lane * 4;
-                        v[j] = c < H ? rt_load4<XT>(xr, c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
-                }
-                ss = warp_sum(ss);
-                if (lane == 0) scale_s[t] = 1.0f / sqrtf(ss / static_cast<float>(H) + in_eps);
-            }
-            __syncthreads();
+        if (in_norm_w && !failed && !mbar_wait_bounded(&nbar, 0, kPipeWaitNs)) {
+            failed = 1;
+            latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
         }
         for (uint32_t t0 = 0; t0 < T; t0 += SL.pass) {
             const uint32_t tp = min(T - t0, SL.pass);
             if (t0 > 0) __syncthreads();  // the previous pass's chains are done with the rows
-            // one warp per token: the row as f32 (bf16-rounded when normalised
-            // here), the normalised row also to ws.xn from CTA t mod grid
+            // One warp per token reads the row once per kRtBlk columns into
+            // registers (a whole row at hidden sizes up to kRtBlk), takes the
+            // RMSNorm scale from them (the formula of rms_norm_rows_kernel:
+            // 1 / sqrt(mean(x^2) + eps)) and writes the row as f32
+            // (bf16-rounded when normalised here); the normalised row also
+            // goes to ws.xn from CTA t mod grid.
             for (uint32_t tt = warp; tt < tp; tt += kRtRows) {
                 const uint32_t t = t0 + tt;
                 const XT* xr = x + static_cast<size_t>(t) * H;
                 float* dst = x_s + static_cast<size_t>(tt) * SL.stride;
-                const float sc = in_norm_w ? scale_s[t] : 1.f;
                 const bool owner = in_norm_w && t % gridDim.x == blockIdx.x;
-                for (uint32_t c0 = 0; c0 < H; c0 += 128 * 8) {
-                    float4 v[8];
+                float4 v[kRtBlk / 128];
+                auto load_blk = [&](uint32_t c0) {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
+                    for (int j = 0; j < static_cast<int>(kRtBlk / 128); ++j) {
                         const uint32_t c = c0 + j * 128 + lane * 4;
-                        if (c < H) v[j] = rt_load4<XT>(xr, c);
+                        v[j] = c < H ? rt_load4<XT>(xr, c) : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
+                };
+                float sc = 1.f;
+                if (in_norm_w) {
+                    float ss = 0.f;
+                    for (uint32_t c0 = 0; c0 < H; c0 += kRtBlk) {
+                        load_blk(c0);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
+                        for (int j = 0; j < static_cast<int>(kRtBlk / 128); ++j)
+                            ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+                    }
+                    ss = warp_sum(ss);
+                    sc = 1.0f / sqrtf(ss / static_cast<float>(H) + in_eps);
+                }
+                for (uint32_t c0 = 0; c0 < H; c0 += kRtBlk) {
+                    if (!in_norm_w || H > kRtBlk) load_blk(c0);  // else the row is still in v
+#pragma unroll
+                    for (int j = 0; j < static_cast<int>(kRtBlk / 128); ++j) {
                         const uint32_t c = c0 + j * 128 + lane * 4;
                         if (c >= H) continue;
                         float4 o = v[j];
                         if (in_norm_w) {
-                            const float4 n = *reinterpret_cast<const float4*>(in_norm_w + c);
+                            const float4 n = *reinterpret_cast<const float4*>(nw_s + c);
                             o = make_float4(bf16_round(o.x * sc * n.x), bf16_round(o.y * sc * n.y),
                                             bf16_round(o.z * sc * n.z), bf16_round(o.w * sc * n.w));
                             if (owner) {
@@ -615,8 +627,10 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
     if (threadIdx.x == 0) red_add_release_gpu(&ws.ticket[0], 1u);
     const uint32_t route_ctas = min(min(gridDim.x, kRtRouteCtas), (T + kRtRows - 1) / kRtRows);
     auto drain = [&]() {  // after an expired wait, let this CTA's own copies land (bounded) before it exits
-        if (threadIdx.x == 0 && failed)
+        if (threadIdx.x == 0 && failed) {
             for (uint32_t k = 0; k < (SL.wf_bytes ? 1u : nchunks); ++k) mbar_wait_bounded(&bars[k], 0, kPipeWaitNs);
+            if (in_norm_w) mbar_wait_bounded(&nbar, 0, kPipeWaitNs);
+        }
     };
     if (blockIdx.x >= route_ctas) {
         drain();
@@ -1048,7 +1062,7 @@ cudaError_t moe_launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, c
 }
 
 size_t moe_router_smem(uint32_t T, uint32_t H, uint32_t E, uint32_t K) {
-    const size_t a = rt_smem_layout(T, H, E, K, true).total, b = rt_smem_layout(T, H, E, K, false).total;
+    const size_t a = rt_smem_layout(T, H, E, K, true, true).total, b = rt_smem_layout(T, H, E, K, false, false).total;
     return a > b ? a : b;
 }
 
@@ -1103,7 +1117,8 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         const uint32_t nrows = E + (has_gate ? 1u : 0u);
         const uint32_t rpc = rt_rows_per_cta(H);
         dim3 grid((nrows + rpc - 1) / rpc);
-        const size_t smem = rt_smem_layout(T, H, E, K, sizeof(XT) == 2 || a.in_norm_w != nullptr).total;
+        const size_t smem =
+            rt_smem_layout(T, H, E, K, sizeof(XT) == 2 || a.in_norm_w != nullptr, a.in_norm_w != nullptr).total;
         auto fn = moe_router_kernel<XT>;
         if ((err = set_smem(fn, smem)) != cudaSuccess) return err;
         const XT* x = static_cast<const XT*>(a.x);
