@@ -575,6 +575,13 @@ def run_matvec(args):
     calls = [(lambda m=m: ctx.q4_matvec(m[0], m[1], m[2], R, Cc, G, x, y, stream=s)) for m in mats]
     ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
     gbs = byts / (ms / 1e3) / 1e9
+    # the same 64 matrices as one resident projection batch on the input
+    # (pbmoe_q4_matvec_batch, resident_mmap_matvec_batch): 4 launches of 16
+    ys = [torch.empty(1, R, device="cuda", dtype=torch.bfloat16) for _ in range(NC)]
+    spec = [(m[0], m[1], m[2], R, Cc, G) for m in mats]
+    bms, _, _ = _graph_time([lambda: ctx.q4_matvec_batch(spec, x, ys, stream=s)], s, max(8, args.steps // NC),
+                            args.warmup)
+    bgbs = NC * byts / (bms / 1e3) / 1e9
     hx = x.cpu().pin_memory()
     hy = torch.empty(1, R, dtype=torch.bfloat16).pin_memory()
     dx = torch.empty_like(x)
@@ -621,6 +628,9 @@ def run_matvec(args):
         "roofline": {"bound": "hbm", "kernel": "q4_matvec", "achieved": gbs, "peak": peak, "unit": "GB/s",
                      "frac": gbs / peak, "peak_kind": kind, "traffic": None,
                      "algorithmic_bytes_per_launch": byts, "launch_ms": ms},
+        "projection_batch": {"value": bgbs, "unit": "GB/s", "frac": bgbs / peak, "matrices": NC,
+                             "launches": (NC + 15) // 16, "ms_per_batch": bms,
+                             "note": "the 64 config-0 matrices on one input through pbmoe_q4_matvec_batch"},
         "gpu_launches": steps, "clocks": clocks, "cpu_baseline": cpu,
     })
     ctx.close()
@@ -709,7 +719,7 @@ def run_gemm(args):
                 "d2h_bytes_per_step": M * N * 2, "steps": min(args.steps, 2 * NC)},
         "roofline": {"bound": "tensor", "kernel": "q4_umma_kernel (dense)", "achieved": tflops, "peak": peak,
                      "unit": "TFLOP/s", "frac": tflops / peak, "peak_kind": kind, "traffic": 17.6e6,
-                     "traffic_source": "ncu --set full, one dense launch (profiles/q4_gemm_config2_dense.md)",
+                     "traffic_source": "ncu --set full, one dense launch of the config-2 GEMM",
                      "algorithmic_flops_per_launch": flops, "launch_ms": ms},
         "grouped": {"routes": R, "experts": E, "projection": "gate [512x2048] per expert",
                     "plan_ms": plan_ms, "gather_gemm_ms": g_ms, "tflops": gflops / (g_ms / 1e3) / 1e12,
@@ -803,6 +813,13 @@ def run_mxfp4(args):
     calls = [(lambda m=m: ctx.mxfp4_matvec(m[0], m[1], R, Cc, x, y, stream=s)) for m in mats]
     ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
     gbs = byts / (ms / 1e3) / 1e9
+    # the same 64 matrices as one resident projection batch on the input
+    # (pbmoe_q4_matvec_batch, resident_mmap_matvec_batch): 4 launches of 16
+    ys = [torch.empty(1, R, device="cuda", dtype=torch.bfloat16) for _ in range(NC)]
+    spec = [(m[0], m[1], m[2], R, Cc, G) for m in mats]
+    bms, _, _ = _graph_time([lambda: ctx.q4_matvec_batch(spec, x, ys, stream=s)], s, max(8, args.steps // NC),
+                            args.warmup)
+    bgbs = NC * byts / (bms / 1e3) / 1e9
     hx = x.cpu().pin_memory()
     hy = torch.empty(1, R, dtype=torch.bfloat16).pin_memory()
     dx = torch.empty_like(x)

@@ -254,6 +254,21 @@ typedef struct pbmoe_q4_fused_args {
 } pbmoe_q4_fused_args;
 PBMOE_API int pbmoe_q4_matvec_fused(pbmoe_ctx* ctx, const pbmoe_q4_fused_args* args, void* stream);
 
+/* A batch of resident projections on one input: y[i] = W_i x for the
+ * `count` matrices of `weights` (all with the same cols and group_size; rows
+ * may differ), y[i] [batch x weights[i].rows] in y_dtype. Replaces
+ * resident_mmap_matvec_batch (runtime/mod.rs:1184), which encodes every
+ * projection of the batch over the same input buffer: here up to 16 matrices
+ * share one launch (more run as further launches of 16), so the projections
+ * stream their weights back to back instead of paying a launch each. Needs
+ * the fast or tensor-core path (cols a multiple of 32, group a power of two
+ * >= 32, 16-byte aligned rows and x): other shapes are PBMOE_ERR_UNSUPPORTED
+ * (use pbmoe_q4_matvec per matrix). Results equal pbmoe_q4_matvec's on each
+ * matrix. */
+PBMOE_API int pbmoe_q4_matvec_batch(pbmoe_ctx* ctx, const pbmoe_q4_tensor* weights, uint32_t count, const void* x,
+                                    pbmoe_dtype x_dtype, void* const* y, pbmoe_dtype y_dtype, uint32_t batch,
+                                    void* stream);
+
 /* Routing on given logits: logits f32 [tokens x E] -> route_ids u32 [tokens x K]
  * (replacement-slot order of routing_top_k_iter, math.rs:746-765) and
  * route_weights f32 [tokens x K] (routing_softmax_top_k, math.rs:771-783, then

@@ -48,7 +48,7 @@ EXPORTED = [
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
     "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
     "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host", "pbmoe_sync",
-    "pbmoe_fixed_mxfp4_layout", "pbmoe_q4_matvec_fused", "pbmoe_route_sigmoid_noaux",
+    "pbmoe_fixed_mxfp4_layout", "pbmoe_q4_matvec_fused", "pbmoe_q4_matvec_batch", "pbmoe_route_sigmoid_noaux",
 ]
 
 EP_HANDLE_BYTES = 64
@@ -186,6 +186,8 @@ def load():
         L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, C.c_float, vp, vp, vp, u32,
                                              vp]
         L.pbmoe_q4_matvec_fused.argtypes = [vp, C.POINTER(Q4FusedArgs), vp]
+        L.pbmoe_q4_matvec_batch.argtypes = [vp, C.POINTER(Q4Tensor), u32, vp, C.c_int, C.POINTER(vp), C.c_int, u32,
+                                            vp]
         L.pbmoe_route_sigmoid_noaux.argtypes = [vp, vp, vp, u32, u32, u32, u32, C.c_float, vp, vp, vp]
         L.pbmoe_sync.argtypes = [vp, vp, u32]
         L.pbmoe_moe_layer_host.argtypes = [vp, C.POINTER(MoeConfig), C.POINTER(MoeWeights), vp, i32, vp, vp, i32,
@@ -395,6 +397,15 @@ class Context:
         a.epsilon = eps
         a.residual = None if residual is None else residual.data_ptr()
         self.check(self.lib.pbmoe_q4_matvec_fused(self.h, C.byref(a), self.stream_ptr(stream)))
+
+    def q4_matvec_batch(self, mats, x, ys, stream=None):
+        """pbmoe_q4_matvec_batch: mats = [(packed, scales, biases, rows, cols, group)] on the same x, ys the
+        outputs [batch, rows_i] (one dtype)."""
+        n = len(mats)
+        ts = (Q4Tensor * n)(*[Q4Tensor(p.data_ptr(), s.data_ptr(), b.data_ptr(), r, c, g) for (p, s, b, r, c, g) in mats])
+        yp = (C.c_void_p * n)(*[y.data_ptr() for y in ys])
+        self.check(self.lib.pbmoe_q4_matvec_batch(self.h, ts, n, x.data_ptr(), _dtype_code(x), yp,
+                                                  _dtype_code(ys[0]), int(x.shape[0]), self.stream_ptr(stream)))
 
     def prefill_reserve(self, max_rows, max_cols):
         self.check(self.lib.pbmoe_prefill_reserve(self.h, max_rows, max_cols))

@@ -477,6 +477,51 @@ int pbmoe_q4_matvec_fused(pbmoe_ctx* ctx, const pbmoe_q4_fused_args* f, void* st
     return PBMOE_OK;
 }
 
+int pbmoe_q4_matvec_batch(pbmoe_ctx* ctx, const pbmoe_q4_tensor* w, uint32_t count, const void* x,
+                          pbmoe_dtype x_dtype, void* const* y, pbmoe_dtype y_dtype, uint32_t batch, void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (count == 0 || batch == 0) return PBMOE_OK;
+    if (!w || !x || !y) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec batch: null pointer");
+    if ((x_dtype != PBMOE_F32 && x_dtype != PBMOE_BF16) || (y_dtype != PBMOE_F32 && y_dtype != PBMOE_BF16))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "unknown dtype");
+    const size_t ys = y_dtype == PBMOE_F32 ? 4 : 2;
+    if (!aligned(x, x_dtype == PBMOE_F32 ? 4 : 2))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec batch: misaligned x");
+    const uint32_t cols = w[0].cols, group = w[0].group_size;
+    if (cols == 0 || group == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec batch: empty matrix or zero group");
+    for (uint32_t i = 0; i < count; ++i) {
+        if (!w[i].packed || !w[i].scales || !w[i].biases || !y[i])
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec batch: null pointer in matrix %u", i);
+        if (w[i].cols != cols || w[i].group_size != group)
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT,
+                        "q4 matvec batch: matrix %u has cols %u group %u, matrix 0 has cols %u group %u", i, w[i].cols,
+                        w[i].group_size, cols, group);
+        if (w[i].rows == 0) return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec batch: matrix %u has no rows", i);
+        if (!aligned(w[i].scales, 2) || !aligned(w[i].biases, 2) || !aligned(y[i], ys))
+            return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "q4 matvec batch: misaligned pointer in matrix %u", i);
+    }
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
+    for (uint32_t i0 = 0; i0 < count; i0 += pbmoe::kQ4MaxMats) {
+        const uint32_t n = std::min(count - i0, pbmoe::kQ4MaxMats);
+        pbmoe::Q4MatSpec set[pbmoe::kQ4MaxMats];
+        for (uint32_t i = 0; i < n; ++i)
+            set[i] = {static_cast<const uint8_t*>(w[i0 + i].packed), w[i0 + i].scales, w[i0 + i].biases, w[i0 + i].rows,
+                      y[i0 + i]};
+        Q4MatvecArgs a{set[0].packed, set[0].scales, set[0].biases, set[0].rows, cols, group, x, x_dtype,
+                       set[0].y, y_dtype, batch};
+        a.set_count = n;
+        a.set = set;
+        cudaError_t e = q4_matvec_launch(a, static_cast<cudaStream_t>(stream));
+        if (e == cudaErrorNotSupported)
+            return fail(ctx, PBMOE_ERR_UNSUPPORTED,
+                        "FlashMoe unsupported q4 matvec batch: cols=%u group=%u needs the fast path (cols a multiple "
+                        "of 32, group a power of two >= 32, 16-byte aligned rows and x)", cols, group);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "q4 matvec batch launch");
+    }
+    return PBMOE_OK;
+}
+
 int pbmoe_route_topk(pbmoe_ctx* ctx, const float* logits, uint32_t tokens, uint32_t E, uint32_t K,
                      uint32_t normalization, float routed_scale, uint32_t* ids, float* weights, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;

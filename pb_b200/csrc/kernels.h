@@ -171,7 +171,20 @@ struct Q4MatvecArgs {
     const uint16_t* biases2;
     uint32_t rows2;
     void* y2;
+    // or a set of up to kQ4MaxMats matrices [rows_i x cols] (same group) on the
+    // same x, one launch (pbmoe_q4_matvec_batch); replaces packed/packed2
+    uint32_t set_count;
+    const struct Q4MatSpec* set;
 };
+// One matrix of a multi-matrix launch.
+struct Q4MatSpec {
+    const uint8_t* packed;
+    const uint16_t* scales;
+    const uint16_t* biases;
+    uint32_t rows;
+    void* y;
+};
+constexpr uint32_t kQ4MaxMats = 16;
 // Returns cudaErrorNotSupported when the shape needs more shared memory than
 // a CTA has.
 cudaError_t q4_matvec_launch(const Q4MatvecArgs& a, cudaStream_t s);

@@ -81,6 +81,18 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
+// 4-byte asynchronous copy global -> shared (both addresses 4-byte aligned).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Close this thread's current group of cp.async copies; wait until at most N
+// of its groups are still in flight.
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Arrive on `bar` once every cp.async this thread issued so far has landed.
 // The arrival is not added to the pending count: the barrier's expected
 // count must include one arrival per issuing thread and phase.

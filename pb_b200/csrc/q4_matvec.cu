@@ -16,7 +16,10 @@
 // predecessor (griddepcontrol.wait) before reading x or writing y, so
 // back-to-back matvecs stream weights without a gap between launches.
 
+#include <algorithm>
+
 #include "kernels.h"
+#include "pipe.cuh"
 #include "q4_mma.cuh"
 #include "q4_rows.cuh"
 
@@ -39,11 +42,12 @@ static cudaError_t launch_with_pdl(const void* fn, dim3 grid, dim3 block, size_t
 constexpr int kMvThreads = 128;
 constexpr int kMvRows = 4;  // rows per lane group per pass
 
-// One matrix of a launch: weights, output and row count. A launch covers one
-// or two matrices on the same x (the second one's CTAs follow the first's),
-// e.g. the MLA chain's q_a and kv_a projections, which read the same normed
+// One matrix of a launch: weights, output and row count. A launch covers up
+// to kQ4MaxMats matrices on the same x, each one's CTAs after the previous
+// one's: the MLA chain's q_a and kv_a projections, which read the same normed
 // hidden state (execute_glm_mla_input_projection_chain,
-// metal/qwen_execution.rs:289-480).
+// metal/qwen_execution.rs:289-480), or a batch of resident projections on one
+// input (resident_mmap_matvec_batch, runtime/mod.rs:1184).
 struct MvMat {
     const uint8_t* packed;
     const uint16_t* scales;
@@ -51,6 +55,19 @@ struct MvMat {
     void* y;
     uint32_t rows;
 };
+struct MvSet {
+    MvMat m[kQ4MaxMats];
+    uint32_t first[kQ4MaxMats];  // first CTA of matrix i
+    uint32_t count;
+};
+
+// The matrix of this CTA and the CTA's index within it.
+__device__ __forceinline__ const MvMat& mv_pick(const MvSet& set, uint32_t& bx) {
+    uint32_t i = 0;
+    while (i + 1 < set.count && blockIdx.x >= set.first[i + 1]) ++i;
+    bx = blockIdx.x - set.first[i];
+    return set.m[i];
+}
 
 // Optional fusions: the input RMSNorm (norm_w, eps) and a residual added to y.
 struct MvFuse {
@@ -67,15 +84,14 @@ __device__ __forceinline__ void store_y(const MvFuse& fz, YT* y, size_t i, float
 
 template <typename XT, typename YT, int LPR, int CPL, int NT>
 __global__ void __launch_bounds__(kMvThreads, 3)
-q4_matvec_fast_kernel(MvMat m0, MvMat m1, uint32_t grid0, Q4Geom g0, const XT* __restrict__ x, uint32_t batch,
+q4_matvec_fast_kernel(const __grid_constant__ MvSet set, Q4Geom g0, const XT* __restrict__ x, uint32_t batch,
                       MvFuse fz) {
     extern __shared__ __align__(16) float smem[];
     __shared__ float nscale[NT];
     constexpr int kGroups = 32 / LPR;
     constexpr int kRowsPerCta = kMvRows * kGroups * (kMvThreads / 32);
-    const bool second = blockIdx.x >= grid0;
-    const MvMat m = second ? m1 : m0;
-    const uint32_t bx = second ? blockIdx.x - grid0 : blockIdx.x;
+    uint32_t bx;
+    const MvMat m = mv_pick(set, bx);
     Q4Geom g = g0;
     g.rows = m.rows;
     YT* y = static_cast<YT*>(m.y);
@@ -120,6 +136,125 @@ q4_matvec_fast_kernel(MvMat m0, MvMat m1, uint32_t grid0, Q4Geom g0, const XT* _
     }
 }
 
+// Persistent, cp.async-pipelined form for launches of many rows (a
+// projection batch): a CTA stages x once, then walks 32-row blocks
+// `gridDim.x` apart over every matrix of the set. A block's nibbles, scales
+// and biases are copied into one of kSmStages shared-memory stages by every
+// thread (16-byte cp.async), kSmStages - 1 blocks ahead of the one being
+// computed, so each SM keeps ~100 KB of weights in flight. Warp w computes
+// rows 4w..4w+3 of the block; a lane takes chunks lane, lane + 32, ... of each
+// row (the fast kernel's chunk arithmetic, weights read from shared memory).
+// Rows of up to kSmMaxCols columns (a block's bytes fit a stage).
+constexpr int kSmThreads = 256;
+constexpr int kSmRows = 32;       // rows per block
+constexpr int kSmStages = 4;
+constexpr uint32_t kSmMaxCols = 2048;
+constexpr uint32_t kSmStageBytes = kSmRows * (kSmMaxCols / 2) + 2 * kSmRows * (kSmMaxCols / 32) * 2;
+
+__device__ __forceinline__ const MvMat& mv_pick_block(const MvSet& set, uint32_t blk, uint32_t& bx) {
+    uint32_t i = 0;
+    while (i + 1 < set.count && blk >= set.first[i + 1]) ++i;
+    bx = blk - set.first[i];
+    return set.m[i];
+}
+
+template <typename XT, typename YT, int NT>
+__global__ void __launch_bounds__(kSmThreads, 1)
+q4_matvec_stream_kernel(const __grid_constant__ MvSet set, uint32_t nblocks, Q4Geom g0, const XT* __restrict__ x,
+                        uint32_t batch) {
+    extern __shared__ __align__(16) unsigned char sm_raw[];
+    const uint32_t cols = g0.cols, chunks = g0.chunks, gpr = g0.gpr, rb = cols / 2;
+    float* xs = reinterpret_cast<float*>(sm_raw);
+    float* xe = xs + NT * cols;
+    float* xo = xe + NT * chunks;
+    unsigned char* stage0 = sm_raw + ((NT * (cols + 2 * chunks) * 4 + 127) / 128) * 128;
+    const uint32_t sbytes = kSmRows * rb + 2 * kSmRows * gpr * 2;  // nibbles, then scales, then biases
+    const uint32_t sstride = (sbytes + 127) / 128 * 128;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nt = static_cast<int>(batch);
+
+    auto issue = [&](uint32_t blk, int st) {
+        uint32_t bx;
+        const MvMat& m = mv_pick_block(set, blk, bx);
+        const uint32_t r0 = bx * kSmRows;
+        const uint32_t nr = min(static_cast<uint32_t>(kSmRows), m.rows - r0);
+        unsigned char* d = stage0 + st * sstride;
+        // nibbles: nr rows of rb bytes, contiguous in the matrix
+        const uint32_t nvec = nr * rb / 16;
+        const unsigned char* src = m.packed + static_cast<size_t>(r0) * rb;
+        for (uint32_t i = threadIdx.x; i < nvec; i += kSmThreads) cp_async16(d + i * 16, src + i * 16);
+        // scales and biases: nr * gpr bf16 each (gpr * 2 bytes per row)
+        const uint32_t sb = nr * gpr * 2;
+        const unsigned char* ssrc = reinterpret_cast<const unsigned char*>(m.scales + static_cast<size_t>(r0) * gpr);
+        const unsigned char* bsrc = reinterpret_cast<const unsigned char*>(m.biases + static_cast<size_t>(r0) * gpr);
+        for (uint32_t i = threadIdx.x * 4; i < sb; i += kSmThreads * 4) {
+            cp_async4(d + kSmRows * rb + i, ssrc + i);
+            cp_async4(d + kSmRows * rb + kSmRows * gpr * 2 + i, bsrc + i);
+        }
+    };
+    uint32_t blk = blockIdx.x;
+    for (int st = 0; st < kSmStages - 1; ++st) {
+        const uint32_t b = blk + st * gridDim.x;
+        if (b < nblocks) issue(b, st);
+        cp_async_commit();
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    stage_x_fast<XT>(x, cols, nullptr, nt, cols, xs, xe, xo);
+    for (int it = 0; blk < nblocks; ++it, blk += gridDim.x) {
+        const int st = it % kSmStages;
+        {  // the block kSmStages - 1 ahead goes into the stage freed last iteration
+            const uint32_t b = blk + (kSmStages - 1) * gridDim.x;
+            if (b < nblocks) issue(b, (it + kSmStages - 1) % kSmStages);
+            cp_async_commit();
+        }
+        cp_async_wait_group<kSmStages - 1>();
+        __syncthreads();
+        uint32_t bx;
+        const MvMat& m = mv_pick_block(set, blk, bx);
+        const unsigned char* d = stage0 + st * sstride;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(d + kSmRows * rb);
+        const uint16_t* bi = sc + kSmRows * gpr;
+        float acc[4][NT];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+        for (uint32_t j = lane; j < chunks; j += 32) {
+            const uint32_t gi = j >> g0.cpg_shift;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t row = warp * 4 + r;
+                const uint4 w = *reinterpret_cast<const uint4*>(d + row * rb + j * 16);
+                const float s = bf16_bits_to_f32(sc[row * gpr + gi]);
+                const float bv = bf16_bits_to_f32(bi[row * gpr + gi]);
+                ChunkF f;
+                decode_chunk(w, f);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if (t < nt) {
+                        const float e = xe[t * chunks + j], o = xo[t * chunks + j];
+                        const float qd = chunk_qdot(f, xs + static_cast<size_t>(t) * cols + (j << 5), j & 7u, e, o);
+                        acc[r][t] = fmaf(s, qd, fmaf(bv, e + o, acc[r][t]));
+                    }
+                }
+            }
+        }
+        YT* y = static_cast<YT*>(m.y);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = warp_sum(acc[r][t]);
+                const uint32_t row = bx * kSmRows + warp * 4 + r;
+                if (lane == 0 && t < nt && row < m.rows) store_act<YT>(y, static_cast<size_t>(t) * m.rows + row, v);
+            }
+        }
+        __syncthreads();  // stage st is read: the next iteration refills it
+    }
+    cp_async_wait_group<0>();
+}
+
 template <typename XT, typename YT>
 __global__ void __launch_bounds__(kMvThreads)
 q4_matvec_generic_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales,
@@ -151,7 +286,7 @@ q4_matvec_generic_kernel(const uint8_t* __restrict__ packed, const uint16_t* __r
 // computes each token's 1/rms from x first and stages the normalised rows.
 template <typename XT, typename YT, int KS, bool kTok16>
 __global__ void __launch_bounds__(256, 2)
-q4_matvec_mma_kernel(MvMat m0, MvMat m1, uint32_t grid0, uint32_t cols, const XT* __restrict__ x, uint32_t batch,
+q4_matvec_mma_kernel(const __grid_constant__ MvSet set, uint32_t cols, const XT* __restrict__ x, uint32_t batch,
                      MvFuse fz) {
     constexpr bool kLo = sizeof(XT) == 4;
     constexpr bool kRows16 = kLo || kTok16;
@@ -159,9 +294,8 @@ q4_matvec_mma_kernel(MvMat m0, MvMat m1, uint32_t grid0, uint32_t cols, const XT
     constexpr int kTiles = 8 / KS;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ float nscale[kPass];
-    const bool second = blockIdx.x >= grid0;
-    const MvMat m = second ? m1 : m0;
-    const uint32_t bx = second ? blockIdx.x - grid0 : blockIdx.x;
+    uint32_t bx;
+    const MvMat m = mv_pick(set, bx);
     const uint32_t rows = m.rows;
     YT* y = static_cast<YT*>(m.y);
     const uint32_t trows = kRows16 ? 16 : 8;
@@ -236,9 +370,37 @@ q4_matvec_mma_kernel(MvMat m0, MvMat m1, uint32_t grid0, uint32_t cols, const XT
     }
 }
 
-static void mats_of(const Q4MatvecArgs& a, MvMat& m0, MvMat& m1) {
-    m0 = MvMat{a.packed, a.scales, a.biases, a.y, a.rows};
-    m1 = a.packed2 ? MvMat{a.packed2, a.scales2, a.biases2, a.y2, a.rows2} : m0;
+static int mv_sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// The launch's matrices (the set, or packed [+ packed2]) with each one's
+// first CTA for `rows_per_cta`; returns the total CTA count.
+static uint32_t set_of(const Q4MatvecArgs& a, uint32_t rows_per_cta, MvSet& set) {
+    set = MvSet{};
+    if (a.set_count) {
+        set.count = a.set_count;
+        for (uint32_t i = 0; i < a.set_count; ++i)
+            set.m[i] = MvMat{a.set[i].packed, a.set[i].scales, a.set[i].biases, a.set[i].y, a.set[i].rows};
+    } else {
+        set.count = a.packed2 ? 2u : 1u;
+        set.m[0] = MvMat{a.packed, a.scales, a.biases, a.y, a.rows};
+        if (a.packed2) set.m[1] = MvMat{a.packed2, a.scales2, a.biases2, a.y2, a.rows2};
+    }
+    uint32_t ctas = 0;
+    for (uint32_t i = 0; i < set.count; ++i) {
+        set.first[i] = ctas;
+        ctas += (set.m[i].rows + rows_per_cta - 1) / rows_per_cta;
+    }
+    return ctas;
 }
 
 template <typename XT, typename YT, int KS>
@@ -253,16 +415,13 @@ static cudaError_t launch_mma_ks(const Q4MatvecArgs& a, cudaStream_t s) {
                            : reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, false>);
     cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    const uint32_t per_cta = 8 * kTiles;
-    uint32_t grid0 = (a.rows + per_cta - 1) / per_cta;
-    const uint32_t grid1 = a.packed2 ? (a.rows2 + per_cta - 1) / per_cta : 0;
-    MvMat m0, m1;
-    mats_of(a, m0, m1);
+    MvSet set;
+    const uint32_t ctas = set_of(a, 8 * kTiles, set);
     MvFuse fz{a.norm_w, a.eps, a.residual};
     uint32_t cols = a.cols, batch = a.batch;
     const XT* x = static_cast<const XT*>(a.x);
-    void* args[] = {(void*)&m0, (void*)&m1, (void*)&grid0, (void*)&cols, (void*)&x, (void*)&batch, (void*)&fz};
-    return launch_with_pdl(fn, dim3(grid0 + grid1), dim3(256), smem, s, args);
+    void* args[] = {(void*)&set, (void*)&cols, (void*)&x, (void*)&batch, (void*)&fz};
+    return launch_with_pdl(fn, dim3(ctas), dim3(256), smem, s, args);
 }
 
 // Group-64 weights whose row length is a multiple of 256 columns.
@@ -279,21 +438,44 @@ template <typename XT, typename YT, int LPR, int CPL, int NT>
 static cudaError_t launch_fast(const Q4MatvecArgs& a, const Q4Geom& g, cudaStream_t s) {
     constexpr int kGroups = 32 / LPR;
     constexpr int kRowsPerCta = kMvRows * kGroups * (kMvThreads / 32);
+    bool stream_aligned = a.set_count > 1;
+    for (uint32_t i = 0; i < a.set_count; ++i)
+        stream_aligned = stream_aligned && reinterpret_cast<uintptr_t>(a.set[i].packed) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(a.set[i].scales) % 4 == 0 &&
+                         reinterpret_cast<uintptr_t>(a.set[i].biases) % 4 == 0;
+    if (stream_aligned && !a.norm_w && !a.residual && a.batch <= static_cast<uint32_t>(NT) &&
+        g.cols <= kSmMaxCols && (g.cols / 2) % 16 == 0 && g.gpr % 2 == 0) {
+        // a projection batch: the persistent pipelined kernel (weights 16-byte
+        // aligned per row: packed base 16-byte aligned and cols/2 a multiple of 16)
+        const size_t xbytes = (static_cast<size_t>(NT) * (g.cols + 2ull * g.chunks) * 4 + 127) / 128 * 128;
+        const size_t sstride = ((size_t(kSmRows) * (g.cols / 2) + 2ull * kSmRows * g.gpr * 2) + 127) / 128 * 128;
+        const size_t smem = xbytes + kSmStages * sstride;
+        auto fn = q4_matvec_stream_kernel<XT, YT, NT>;
+        cudaError_t err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (err != cudaSuccess) return err;
+        MvSet set;
+        uint32_t nblocks = set_of(a, kSmRows, set);
+        const uint32_t grid = std::min(nblocks, static_cast<uint32_t>(mv_sm_count()));
+        Q4Geom gg = g;
+        const XT* x = static_cast<const XT*>(a.x);
+        uint32_t batch = a.batch;
+        void* args[] = {(void*)&set, (void*)&nblocks, (void*)&gg, (void*)&x, (void*)&batch};
+        return launch_with_pdl(reinterpret_cast<const void*>(fn), dim3(grid), dim3(kSmThreads), smem, s, args);
+    }
     const size_t smem = static_cast<size_t>(NT) * (g.cols + 2ull * g.chunks) * sizeof(float);
     auto fn = q4_matvec_fast_kernel<XT, YT, LPR, CPL, NT>;
     cudaError_t err = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    uint32_t grid0 = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
-    const uint32_t grid1 = a.packed2 ? (a.rows2 + kRowsPerCta - 1) / kRowsPerCta : 0;
-    MvMat m0, m1;
-    mats_of(a, m0, m1);
+    MvSet set;
+    const uint32_t ctas = set_of(a, kRowsPerCta, set);
     MvFuse fz{a.norm_w, a.eps, a.residual};
     Q4Geom gg = g;
     const XT* x = static_cast<const XT*>(a.x);
     uint32_t batch = a.batch;
-    void* args[] = {(void*)&m0, (void*)&m1, (void*)&grid0, (void*)&gg, (void*)&x, (void*)&batch, (void*)&fz};
-    return launch_with_pdl(reinterpret_cast<const void*>(fn), dim3(grid0 + grid1), dim3(kMvThreads), smem, s, args);
+    void* args[] = {(void*)&set, (void*)&gg, (void*)&x, (void*)&batch, (void*)&fz};
+    return launch_with_pdl(reinterpret_cast<const void*>(fn), dim3(ctas), dim3(kMvThreads), smem, s, args);
 }
 
 static bool weights_aligned(const uint8_t* p, const uint16_t* sc, const uint16_t* bi) {
@@ -305,17 +487,27 @@ template <typename XT, typename YT>
 static cudaError_t q4_matvec_launch_t(const Q4MatvecArgs& a, cudaStream_t s) {
     constexpr size_t kSmemLimit = 200 * 1024;
     const size_t xelem = a.x_dtype == PBMOE_BF16 ? 2 : 4;
-    const bool fused = a.norm_w || a.residual || a.packed2;
-    const bool aligned2 = !a.packed2 || weights_aligned(a.packed2, a.scales2, a.biases2);
+    const bool fused = a.norm_w || a.residual || a.packed2 || a.set_count > 1;
+    // every matrix of the launch must suit the kernel
+    bool all_aligned = true, all_fast = true;
+    auto visit = [&](const uint8_t* p, const uint16_t* sc, const uint16_t* bi) {
+        all_aligned = all_aligned && weights_aligned(p, sc, bi);
+        all_fast = all_fast && q4_fast_ok(a.cols, a.group, p);
+    };
+    if (a.set_count) {
+        for (uint32_t i = 0; i < a.set_count; ++i) visit(a.set[i].packed, a.set[i].scales, a.set[i].biases);
+    } else {
+        visit(a.packed, a.scales, a.biases);
+        if (a.packed2) visit(a.packed2, a.scales2, a.biases2);
+    }
     // one or two tokens: the CUDA-core kernel (more weight bytes in flight per
     // warp, one wave of CTAs); larger batches: the tensor-core kernel
-    if (a.batch > 2 && a.group == kMmaGroup && a.cols % 256 == 0 && weights_aligned(a.packed, a.scales, a.biases) &&
-        aligned2 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
+    if (a.batch > 2 && a.group == kMmaGroup && a.cols % 256 == 0 && all_aligned &&
+        reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
         cudaError_t e = launch_mma<XT, YT>(a, s);
         if (e != cudaErrorNotSupported) return e;
     }
-    if (q4_fast_ok(a.cols, a.group, a.packed) && (!a.packed2 || q4_fast_ok(a.cols, a.group, a.packed2)) &&
-        reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && (a.cols * xelem) % 16 == 0) {
+    if (all_fast && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && (a.cols * xelem) % 16 == 0) {
         Q4Geom g{a.rows, a.cols, (a.cols + a.group - 1) / a.group, a.cols / 32, ilog2_u32(a.group / 32)};
         const size_t per_tok = (g.cols + 2ull * g.chunks) * sizeof(float);
         const bool multi = a.batch > 1 && 4 * per_tok <= kSmemLimit;

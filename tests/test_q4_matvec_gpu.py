@@ -120,3 +120,47 @@ def test_zero_rows_and_invalid_group(ctx):
     with pytest.raises(capi.PbmoeError) as e:
         ctx.q4_matvec(z, s, s, 1, 32, 0, x, y)
     assert e.value.code == capi.PBMOE_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("x_dtype", ["bf16", "f32"])
+def test_matvec_batch_matches_single_calls(ctx, oracle, batch, x_dtype):
+    """pbmoe_q4_matvec_batch (resident_mmap_matvec_batch, runtime/mod.rs:1184):
+    20 projections of different row counts on one input, run as launches of
+    up to 16 matrices, equal pbmoe_q4_matvec on each matrix bit for bit (same
+    kernel, same arithmetic), and the oracle within 1e-2."""
+    import torch
+
+    from pb_b200 import synth
+
+    g = synth.gen("cuda", 700 + batch)
+    rows = [4096, 1536, 576, 3072, 2048, 64, 128, 1024, 512, 2048, 96, 4096, 1536, 256, 32, 2048, 1024, 576, 3072, 64]
+    cols, group = 2048, 64
+    mats = [synth.q4_matrix(r, cols, group, g, "cuda") for r in rows]
+    dt = torch.bfloat16 if x_dtype == "bf16" else torch.float32
+    x = synth.normal_bf16((batch, cols), 1.0, g, "cuda").to(dt)
+    ys = [torch.empty(batch, r, device="cuda", dtype=torch.float32) for r in rows]
+    ctx.q4_matvec_batch([(p, s, b, r, cols, group) for (p, s, b), r in zip(mats, rows)], x, ys)
+    torch.cuda.synchronize()
+    for i, ((p, s, b), r) in enumerate(zip(mats, rows)):
+        ref = torch.empty(batch, r, device="cuda", dtype=torch.float32)
+        ctx.q4_matvec(p, s, b, r, cols, group, x, ref, batch=batch)
+        torch.cuda.synchronize()
+        assert torch.equal(ys[i], ref), f"matrix {i} ({r} rows) differs from pbmoe_q4_matvec"
+    for i in (0, 5, 19):
+        p, s, b = mats[i]
+        assert_close(ys[i].cpu().numpy(), _oracle(oracle, p, s, b, rows[i], cols, group, x), what=f"batch matrix {i}")
+
+
+def test_matvec_batch_refuses_mixed_columns(ctx):
+    import torch
+
+    from pb_b200 import capi, synth
+
+    g = synth.gen("cuda", 710)
+    a = synth.q4_matrix(64, 2048, 64, g, "cuda")
+    b = synth.q4_matrix(64, 1024, 64, g, "cuda")
+    x = synth.normal_bf16((1, 2048), 1.0, g, "cuda")
+    ys = [torch.empty(1, 64, device="cuda") for _ in range(2)]
+    with pytest.raises(capi.PbmoeError, match="cols"):
+        ctx.q4_matvec_batch([(*a, 64, 2048, 64), (*b, 64, 1024, 64)], x, ys)
