@@ -21,7 +21,7 @@
 //                          bf16 hi + lo so scores keep ~16 mantissa bits),
 //                          online softmax in base 2, O += P C with P in bf16.
 //                          Writes the split's (max, sum, O[16 x 512]).
-//   3. mla_out_kernel      one CTA per (head, sequence): merges the splits'
+//   3. mla_merge_out_kernel one CTA per (head, sequence): merges the splits'
 //                          partials into ctx (in shared memory), then
 //                          out = W_UV[h] ctx.
 // The split plan keeps batch x splits within one wave of SMs (the attention
@@ -37,6 +37,7 @@ constexpr uint32_t kMlaHeads = 16, kMlaLatent = 512, kMlaRope = 64, kMlaV = 128;
 constexpr uint32_t kMlaK = kMlaLatent + kMlaRope;  // 576: score dimension
 constexpr uint32_t kMlaTile = 64;                  // tokens per tile
 constexpr uint32_t kMlaWarps = 4;
+constexpr uint32_t kMlaThreads = kMlaWarps * 32;
 // shared-memory row strides (bytes), padded by 16 against ldmatrix bank conflicts
 constexpr uint32_t kQRow = kMlaK * 2 + 16;        // Q' hi / lo rows
 constexpr uint32_t kCRow = kMlaLatent * 2 + 16;   // c_kv rows
@@ -44,8 +45,14 @@ constexpr uint32_t kRRow = kMlaRope * 2 + 16;     // k_rope rows
 constexpr uint32_t kPRow = kMlaTile * 2 + 16;     // P rows
 constexpr uint32_t kStageBytes = kMlaTile * (kCRow + kRRow);
 constexpr uint32_t kMlaPartialFloats = 2 + kMlaLatent;  // max, sum, O
+// Scores: warp w sums k-steps 9w .. 9w+8 of the 36 for every token of the tile
+constexpr uint32_t kKSteps = kMlaK / 16;                   // 36 k-steps of the score MMAs
+constexpr uint32_t kKStepsPerWarp = kKSteps / kMlaWarps;   // 9
+constexpr uint32_t kColsPerWarp = kMlaLatent / kMlaWarps;  // 128 context columns per warp
+static_assert(kKSteps % kMlaWarps == 0, "score k-steps split evenly over the warps");
+constexpr uint32_t kSRow = kMlaTile + 8;  // partial-score rows (floats), padded against bank conflicts
 constexpr size_t kMlaSmem = 2 * size_t(kMlaHeads) * kQRow + 2 * size_t(kStageBytes) + kMlaHeads * kPRow +
-                            kMlaWarps * kMlaHeads * 4 * 2;
+                            kMlaWarps * kMlaHeads * 4 * 2 + size_t(kMlaWarps) * kMlaHeads * kSRow * 4;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -75,6 +82,10 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 __device__ __forceinline__ void cp16_zfill(void* dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
                  : "memory");
+}
+// 16-byte global -> shared async copy of a chunk known to be in range.
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -147,12 +158,17 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
 }
 
 // ---------------------------------------------------------------- 2. attention
-// grid (splits, batch), 128 threads (4 warps). Warp w computes the scores of
-// tokens 16w..16w+15 of each tile (two n-tiles, all 576 dims) and owns the
-// context columns 128w..128w+127.
-__global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float* __restrict__ qp, MlaSeqs seqs,
-                                                                      uint32_t split_tokens, uint32_t splits,
-                                                                      float* __restrict__ partial) {
+// grid (splits, batch), 128 threads (4 warps). Per 64-token tile (double-
+// buffered cp.async): warp w computes partial scores of every token of the
+// tile over score dims 144w .. 144w+143 (eight independent n-tile
+// accumulators); the partials meet in shared memory, summed in warp order;
+// warp w then owns tokens 16w .. 16w+15 for the online softmax and context
+// columns 128w .. 128w+127 for O += P C. Fragment loads run one k-step ahead
+// of the MMAs that use them (an ldmatrix takes ~95 cycles to return, an MMA
+// step 32-128 cycles of the tensor pipe).
+__global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* __restrict__ qp, MlaSeqs seqs,
+                                                                   uint32_t split_tokens, uint32_t splits,
+                                                                   float* __restrict__ partial) {
     extern __shared__ __align__(128) unsigned char smem[];
     pdl_wait();
     pdl_launch_dependents();
@@ -161,6 +177,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
     unsigned char* stage0 = qlo + kMlaHeads * kQRow;
     unsigned char* pbuf = stage0 + 2 * kStageBytes;
     float* wmax = reinterpret_cast<float*>(pbuf + kMlaHeads * kPRow);  // [warps][16]
+    float* spart = wmax + kMlaWarps * kMlaHeads * 2;                     // [warps][16 heads][kSRow]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t b = blockIdx.y, sp = blockIdx.x;
@@ -177,24 +194,35 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
     const uint16_t* krope = seqs.k_rope[b];
     const uint32_t ntiles = (t1 - t0 + kMlaTile - 1) / kMlaTile;
 
+    // Thread i copies 16-byte chunk (i % 64) of tile rows i / 64 + 2j (c_kv)
+    // and chunk (i % 8) of rows i / 8 + 16j (k_rope); a whole tile takes
+    // fixed offsets from two base pointers, the split's last tile zero-fills
+    // rows past its end.
+    static_assert(kMlaThreads == 128 && kMlaTile == 64, "copy mapping assumes 128 threads, 64-token tiles");
+    const uint32_t c_row = threadIdx.x >> 6, c_ch = threadIdx.x & 63;
+    const uint32_t r_row = threadIdx.x >> 3, r_ch = threadIdx.x & 7;
     auto issue_tile = [&](uint32_t tile, int buf) {
         unsigned char* st = stage0 + buf * kStageBytes;
-        const uint32_t tb = t0 + tile * kMlaTile;
-        // c_kv: 64 rows x 64 chunks; k_rope: 64 rows x 8 chunks
-        for (uint32_t i = threadIdx.x; i < kMlaTile * 64; i += blockDim.x) {
-            const uint32_t r = i >> 6, ch = i & 63;
-            const uint32_t tok = tb + r;
-            const bool ok = tok < t1;
-            cp16_zfill(st + r * kCRow + ch * 16, ckv + static_cast<size_t>(ok ? tok : t0) * kMlaLatent + ch * 8,
-                       ok ? 16u : 0u);
-        }
         unsigned char* rt = st + kMlaTile * kCRow;
-        for (uint32_t i = threadIdx.x; i < kMlaTile * 8; i += blockDim.x) {
-            const uint32_t r = i >> 3, ch = i & 7;
-            const uint32_t tok = tb + r;
-            const bool ok = tok < t1;
-            cp16_zfill(rt + r * kRRow + ch * 16, krope + static_cast<size_t>(ok ? tok : t0) * kMlaRope + ch * 8,
-                       ok ? 16u : 0u);
+        const uint32_t tb = t0 + tile * kMlaTile;
+        const uint16_t* csrc = ckv + static_cast<size_t>(tb + c_row) * kMlaLatent + c_ch * 8;
+        const uint16_t* rsrc = krope + static_cast<size_t>(tb + r_row) * kMlaRope + r_ch * 8;
+        unsigned char* cdst = st + c_row * kCRow + c_ch * 16;
+        unsigned char* rdst = rt + r_row * kRRow + r_ch * 16;
+        if (tb + kMlaTile <= t1) {
+#pragma unroll
+            for (uint32_t j = 0; j < kMlaTile / 2; ++j) cp16(cdst + j * 2 * kCRow, csrc + j * 2 * kMlaLatent);
+#pragma unroll
+            for (uint32_t j = 0; j < kMlaTile / 16; ++j) cp16(rdst + j * 16 * kRRow, rsrc + j * 16 * kMlaRope);
+        } else {
+            for (uint32_t j = 0; j < kMlaTile / 2; ++j) {
+                const bool ok = tb + c_row + 2 * j < t1;
+                cp16_zfill(cdst + j * 2 * kCRow, ok ? csrc + j * 2 * kMlaLatent : ckv, ok ? 16u : 0u);
+            }
+            for (uint32_t j = 0; j < kMlaTile / 16; ++j) {
+                const bool ok = tb + r_row + 16 * j < t1;
+                cp16_zfill(rdst + j * 16 * kRRow, ok ? rsrc + j * 16 * kMlaRope : krope, ok ? 16u : 0u);
+            }
         }
     };
     issue_tile(0, 0);
@@ -205,14 +233,14 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
     {
         const float4* q4 = reinterpret_cast<const float4*>(qp + static_cast<size_t>(b) * kMlaHeads * kMlaK);
         constexpr uint32_t kVec = kMlaHeads * kMlaK / 4;  // 2304 float4
-        constexpr uint32_t kPer = kVec / (kMlaWarps * 32);
-        static_assert(kVec % (kMlaWarps * 32) == 0, "whole float4 per thread");
+        constexpr uint32_t kPer = kVec / kMlaThreads;
+        static_assert(kVec % kMlaThreads == 0, "whole float4 per thread");
         float4 v[kPer];
 #pragma unroll
-        for (uint32_t j = 0; j < kPer; ++j) v[j] = __ldcg(q4 + j * kMlaWarps * 32 + threadIdx.x);
+        for (uint32_t j = 0; j < kPer; ++j) v[j] = __ldcg(q4 + j * kMlaThreads + threadIdx.x);
 #pragma unroll
         for (uint32_t j = 0; j < kPer; ++j) {
-            const uint32_t i = j * kMlaWarps * 32 + threadIdx.x;
+            const uint32_t i = j * kMlaThreads + threadIdx.x;
             const uint32_t h = i / (kMlaK / 4), c4 = i % (kMlaK / 4);
             const uint32_t h0 = pack_bf16x2(v[j].x, v[j].y), h1 = pack_bf16x2(v[j].z, v[j].w);
             const uint32_t l0 = pack_bf16x2(v[j].x - bf16_bits_to_f32(h0 & 0xffffu), v[j].y - bf16_bits_to_f32(h0 >> 16));
@@ -224,15 +252,18 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
 
     // running state: heads g and g+8 (per lane), context columns of this warp
     float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
-    float o[16][4];
+    constexpr int kONt = kColsPerWarp / 8;  // 16 n-tiles of context columns
+    float o[kONt][4];
 #pragma unroll
-    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int n = 0; n < kONt; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
     // ldmatrix lane addressing: A (16 x 16 block): lane -> row (lane & 15), col half (lane >> 4)
     const uint32_t a_row = lane & 15, a_col = (lane >> 4) * 8;
     // B (n8 x k16) from [n][k] rows: lane -> row (lane & 7) + 8 * ((lane >> 4) & 1) for x4 over 2 n-tiles,
     // k half ((lane >> 3) & 1)
     const uint32_t b_row = (lane & 7) + ((lane >> 4) << 3), b_k = ((lane >> 3) & 1) * 8;
+    const uint32_t kk0 = warp * kKStepsPerWarp;
+    const uint32_t tok0 = warp * 16;  // first token of this warp's softmax columns
 
     for (uint32_t tile = 0; tile < ntiles; ++tile) {
         const int buf = tile & 1;
@@ -243,34 +274,62 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
         const unsigned char* st = stage0 + buf * kStageBytes;
         const unsigned char* rt = st + kMlaTile * kCRow;
 
-        // ---- scores of tokens 16w .. 16w+15: two n-tiles, hi and lo accumulators
-        float sh[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        float sl[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const uint32_t tok0 = warp * 16;
+        // ---- partial scores over this warp's k-steps, all 64 tokens
+        {
+            float sc[8][4];
 #pragma unroll
-        for (uint32_t kk = 0; kk < kMlaK / 16; ++kk) {
-            uint32_t ah[4], al[4], bb[4];
-            ldsm_x4(ah, qhi + a_row * kQRow + (kk * 16 + a_col) * 2);
-            ldsm_x4(al, qlo + a_row * kQRow + (kk * 16 + a_col) * 2);
-            const uint32_t kc = kk * 16 + b_k;
-            if (kk < kMlaLatent / 16)
-                ldsm_x4(bb, st + (tok0 + b_row) * kCRow + kc * 2);
-            else
-                ldsm_x4(bb, rt + (tok0 + b_row) * kRRow + (kc - kMlaLatent) * 2);
-            mma16816(sh[0], ah, bb[0], bb[1]);
-            mma16816(sl[0], al, bb[0], bb[1]);
-            mma16816(sh[1], ah, bb[2], bb[3]);
-            mma16816(sl[1], al, bb[2], bb[3]);
+            for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+            uint32_t fa[2][2][4], fb[2][4][4];  // [step parity][hi, lo | 16-token block][4]
+            auto load_step = [&](int f, uint32_t kk) {
+                ldsm_x4(fa[f][0], qhi + a_row * kQRow + (kk * 16 + a_col) * 2);
+                ldsm_x4(fa[f][1], qlo + a_row * kQRow + (kk * 16 + a_col) * 2);
+                const uint32_t kc = kk * 16 + b_k;
+                const bool lat = kk < kMlaLatent / 16;
+                const unsigned char* bsrc =
+                    lat ? st + b_row * kCRow + kc * 2 : rt + b_row * kRRow + (kc - kMlaLatent) * 2;
+                const uint32_t bstep = lat ? 16 * kCRow : 16 * kRRow;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) ldsm_x4(fb[f][q], bsrc + q * bstep);
+            };
+            load_step(0, kk0);
+#pragma unroll
+            for (uint32_t j = 0; j < kKStepsPerWarp; ++j) {
+                const int f = j & 1;
+                if (j + 1 < kKStepsPerWarp) load_step(f ^ 1, kk0 + j + 1);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        mma16816(sc[2 * q], fa[f][h], fb[f][q][0], fb[f][q][1]);
+                        mma16816(sc[2 * q + 1], fa[f][h], fb[f][q][2], fb[f][q][3]);
+                    }
+            }
+            float* sw = spart + warp * kMlaHeads * kSRow;
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                *reinterpret_cast<float2*>(sw + g * kSRow + n * 8 + 2 * t) = make_float2(sc[n][0], sc[n][1]);
+                *reinterpret_cast<float2*>(sw + (g + 8) * kSRow + n * 8 + 2 * t) = make_float2(sc[n][2], sc[n][3]);
+            }
         }
-        // s[n][i]: n-tile n, (head g | g+8) x (token 2t | 2t+1)
+        __syncthreads();  // every warp's partial scores written
+        // s[n][i]: n-tile n of tokens 16w .. 16w+15, (head g | g+8) x (token 2t | 2t+1)
         float s[2][4];
         const uint32_t tbase = t0 + tile * kMlaTile + tok0;
 #pragma unroll
         for (int n = 0; n < 2; ++n)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t tok = tbase + n * 8 + 2 * t + (i & 1);
-                s[n][i] = tok < t1 ? sh[n][i] + sl[n][i] : NEG_INF;
+            for (int r = 0; r < 2; ++r) {
+                float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int w = 0; w < kMlaWarps; ++w) {
+                    const float2 v = *reinterpret_cast<const float2*>(spart + (w * kMlaHeads + g + 8 * r) * kSRow +
+                                                                      tok0 + n * 8 + 2 * t);
+                    acc.x += v.x;
+                    acc.y += v.y;
+                }
+                const uint32_t tok = tbase + n * 8 + 2 * t;
+                s[n][2 * r] = tok < t1 ? acc.x : NEG_INF;
+                s[n][2 * r + 1] = tok + 1 < t1 ? acc.y : NEG_INF;
             }
         // per-head maximum over the tile: warp's 16 tokens, then across warps
         float mx[2];
@@ -319,26 +378,34 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
             l_run[r] = l_run[r] * alpha[r] + lsum[r];  // this warp's tokens only; summed over warps at the end
         }
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
+        for (int n = 0; n < kONt; ++n) {
             o[n][0] *= alpha[0];
             o[n][1] *= alpha[0];
             o[n][2] *= alpha[1];
             o[n][3] *= alpha[1];
         }
         __syncthreads();  // P complete
-        // ---- O[:, 128w .. 128w+127] += P (16 x 64) C (64 x 128)
+        // ---- O[:, 128w .. 128w+127] += P (16 x 64) C (64 x 128), fragments one k-step ahead
+        {
+            uint32_t pa[2][4], cb[2][kONt / 2][4];
+            auto load_pv = [&](int f, uint32_t kk) {
+                ldsm_x4(pa[f], pbuf + a_row * kPRow + (kk * 16 + a_col) * 2);
+                // trans loads: rows = tokens kk*16 + (lane & 15), columns 8-wide blocks
+                const unsigned char* crow = st + (kk * 16 + (lane & 15)) * kCRow;
 #pragma unroll
-        for (uint32_t kk = 0; kk < kMlaTile / 16; ++kk) {
-            uint32_t pa[4];
-            ldsm_x4(pa, pbuf + a_row * kPRow + (kk * 16 + a_col) * 2);
-            // trans loads: rows = tokens kk*16 + (lane & 15), columns 8-wide blocks
-            const unsigned char* crow = st + (kk * 16 + (lane & 15)) * kCRow;
+                for (int n = 0; n < kONt; n += 2)
+                    ldsm_x4_t(cb[f][n / 2], crow + (warp * kColsPerWarp + n * 8 + (lane >> 4) * 8) * 2);
+            };
+            load_pv(0, 0);
 #pragma unroll
-            for (int n = 0; n < 16; n += 2) {
-                uint32_t bb[4];
-                ldsm_x4_t(bb, crow + (warp * 128 + n * 8 + (lane >> 4) * 8) * 2);
-                mma16816(o[n], pa, bb[0], bb[1]);
-                mma16816(o[n + 1], pa, bb[2], bb[3]);
+            for (uint32_t kk = 0; kk < kMlaTile / 16; ++kk) {
+                const int f = kk & 1;
+                if (kk + 1 < kMlaTile / 16) load_pv(f ^ 1, kk + 1);
+#pragma unroll
+                for (int n = 0; n < kONt; n += 2) {
+                    mma16816(o[n], pa[f], cb[f][n / 2][0], cb[f][n / 2][1]);
+                    mma16816(o[n + 1], pa[f], cb[f][n / 2][2], cb[f][n / 2][3]);
+                }
             }
         }
         __syncthreads();  // stage `buf` and P free for reuse
@@ -364,8 +431,8 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
         out[(g + 8) * kMlaPartialFloats] = m_run[1];
     }
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-        const uint32_t col = warp * 128 + n * 8 + 2 * t;
+    for (int n = 0; n < kONt; ++n) {
+        const uint32_t col = warp * kColsPerWarp + n * 8 + 2 * t;
         *reinterpret_cast<float2*>(out + g * kMlaPartialFloats + 2 + col) = make_float2(o[n][0], o[n][1]);
         *reinterpret_cast<float2*>(out + (g + 8) * kMlaPartialFloats + 2 + col) = make_float2(o[n][2], o[n][3]);
     }
@@ -375,32 +442,56 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1) mla_attn_kernel(const float
 // grid (heads, batch), 256 threads. The splits of (sequence b, head h) are
 // merged as ctx[c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s into
 // shared memory, then warp w computes out rows d = w, w + 8, ... of
-// W_UV[h] ctx (16 rows per warp, 16-byte weight loads; W_UV[h] is read from
-// L2 by the batch's CTAs of head h after the first brings it in).
+// W_UV[h] ctx (16 rows per warp). Every W_UV load of the thread (its 16
+// rows x 16 latent columns) is issued before the dependency wait, and the
+// first 16 splits' partials of its two context columns are loaded together
+// with the split maxima and sums: the merge waits on one L2 round trip for up
+// to 16 splits and on one more per further 16.
 constexpr uint32_t kOutThreads = 256;
 constexpr uint32_t kOutMaxSplits = 1024;
+constexpr uint32_t kOutChunk = 16;  // splits whose partials a thread holds in registers at once
 template <typename OT>
-__global__ void __launch_bounds__(kOutThreads) mla_merge_out_kernel(const float* __restrict__ partial,
-                                                                     uint32_t splits, const uint16_t* __restrict__ w_uv,
-                                                                     OT* __restrict__ out) {
+__global__ void __launch_bounds__(kOutThreads, 1) mla_merge_out_kernel(const float* __restrict__ partial,
+                                                                        uint32_t splits,
+                                                                        const uint16_t* __restrict__ w_uv,
+                                                                        OT* __restrict__ out) {
     __shared__ float wsc[kOutMaxSplits];
+    __shared__ float lsc[kOutMaxSplits];
     __shared__ __align__(16) float cs[kMlaLatent];
     __shared__ float red[kOutThreads / 32];
     const uint32_t h = blockIdx.x, b = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // W_UV rows do not depend on the earlier kernels: the first rows' loads
-    // are issued before waiting for them
+    // W_UV rows do not depend on the earlier kernels
     constexpr uint32_t kRowsPerWarp = kMlaV / (kOutThreads / 32);  // 16
-    const uint16_t* wrow0 = w_uv + (static_cast<size_t>(h) * kMlaV + warp) * kMlaLatent + lane * 16;
-    uint4 wa[2] = {__ldg(reinterpret_cast<const uint4*>(wrow0)), __ldg(reinterpret_cast<const uint4*>(wrow0 + 8))};
+    uint4 wv[kRowsPerWarp][2];
+#pragma unroll
+    for (uint32_t i = 0; i < kRowsPerWarp; ++i) {
+        const uint16_t* wr =
+            w_uv + (static_cast<size_t>(h) * kMlaV + warp + i * (kOutThreads / 32)) * kMlaLatent + lane * 16;
+        wv[i][0] = __ldg(reinterpret_cast<const uint4*>(wr));
+        wv[i][1] = __ldg(reinterpret_cast<const uint4*>(wr + 8));
+    }
     pdl_wait();
     pdl_launch_dependents();
     const float* base = partial + static_cast<size_t>(b) * splits * kMlaHeads * kMlaPartialFloats +
                         h * kMlaPartialFloats;
     const size_t stride = static_cast<size_t>(kMlaHeads) * kMlaPartialFloats;
     const float NEG_INF = -__int_as_float(0x7f800000);
+    // the first chunk of this thread's context partials (columns c and c + 256)
+    const float* oc = base + 2 + threadIdx.x;
+    float v[2][kOutChunk];
+#pragma unroll
+    for (uint32_t j = 0; j < kOutChunk; ++j) {
+        v[0][j] = j < splits ? __ldcg(oc + j * stride) : 0.f;
+        v[1][j] = j < splits ? __ldcg(oc + kOutThreads + j * stride) : 0.f;
+    }
     float M = NEG_INF;
-    for (uint32_t sp = threadIdx.x; sp < splits; sp += blockDim.x) M = fmaxf(M, __ldcg(base + sp * stride));
+    for (uint32_t sp = threadIdx.x; sp < splits; sp += blockDim.x) {
+        const float m = __ldcg(base + sp * stride), l = __ldcg(base + sp * stride + 1);
+        wsc[sp] = m;
+        lsc[sp] = l;
+        M = fmaxf(M, m);
+    }
     M = warp_max(M);
     if (lane == 0) red[warp] = M;
     __syncthreads();
@@ -409,10 +500,10 @@ __global__ void __launch_bounds__(kOutThreads) mla_merge_out_kernel(const float*
     for (int w = 1; w < kOutThreads / 32; ++w) M = fmaxf(M, red[w]);
     float tot = 0.f;
     for (uint32_t sp = threadIdx.x; sp < splits; sp += blockDim.x) {
-        const float m = __ldcg(base + sp * stride);
+        const float m = wsc[sp];
         const float w = (m == NEG_INF) ? 0.f : exp2f(m - M);
         wsc[sp] = w;
-        tot += w * __ldcg(base + sp * stride + 1);
+        tot += w * lsc[sp];
     }
     tot = warp_sum(tot);
     __syncthreads();  // everyone has read red[] (M) and written wsc[]
@@ -423,22 +514,24 @@ __global__ void __launch_bounds__(kOutThreads) mla_merge_out_kernel(const float*
     for (int w = 0; w < kOutThreads / 32; ++w) tot += red[w];
     const float inv = tot > 0.f ? 1.0f / tot : 0.f;
     // context: thread c of 256 takes columns c and c + 256
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (uint32_t sp0 = 0; sp0 < splits; sp0 += kOutChunk) {
+        if (sp0 > 0) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const uint32_t c = threadIdx.x + half * kOutThreads;
-        const float* oc = base + 2 + c;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t sp = 0;
-        for (; sp + 8 <= splits; sp += 8) {
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __ldcg(oc + (sp + j) * stride);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j & 3] = fmaf(wsc[sp + j], v[j], acc[j & 3]);
+            for (uint32_t j = 0; j < kOutChunk; ++j) {
+                v[0][j] = sp0 + j < splits ? __ldcg(oc + (sp0 + j) * stride) : 0.f;
+                v[1][j] = sp0 + j < splits ? __ldcg(oc + kOutThreads + (sp0 + j) * stride) : 0.f;
+            }
         }
-        for (; sp < splits; ++sp) acc[0] = fmaf(wsc[sp], __ldcg(oc + sp * stride), acc[0]);
-        cs[c] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * inv;
+#pragma unroll
+        for (uint32_t j = 0; j < kOutChunk; ++j) {
+            const float w = sp0 + j < splits ? wsc[sp0 + j] : 0.f;
+            acc[0][j & 3] = fmaf(w, v[0][j], acc[0][j & 3]);
+            acc[1][j & 3] = fmaf(w, v[1][j], acc[1][j & 3]);
+        }
     }
+    cs[threadIdx.x] = ((acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3])) * inv;
+    cs[threadIdx.x + kOutThreads] = ((acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3])) * inv;
     __syncthreads();
     // out rows: warp w takes d = w + 8 i; lane covers 16 latent columns
     float cv[16];
@@ -446,29 +539,23 @@ __global__ void __launch_bounds__(kOutThreads) mla_merge_out_kernel(const float*
         const float4* c4 = reinterpret_cast<const float4*>(cs + lane * 16);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const float4 v = c4[i];
-            cv[4 * i] = v.x, cv[4 * i + 1] = v.y, cv[4 * i + 2] = v.z, cv[4 * i + 3] = v.w;
+            const float4 q = c4[i];
+            cv[4 * i] = q.x, cv[4 * i + 1] = q.y, cv[4 * i + 2] = q.z, cv[4 * i + 3] = q.w;
         }
     }
+#pragma unroll
     for (uint32_t i = 0; i < kRowsPerWarp; ++i) {
         const uint32_t d = warp + i * (kOutThreads / 32);
-        uint4 wn[2] = {wa[0], wa[1]};
-        if (i + 1 < kRowsPerWarp) {  // next row in flight
-            const uint16_t* wr = w_uv + (static_cast<size_t>(h) * kMlaV + d + kOutThreads / 32) * kMlaLatent + lane * 16;
-            wn[0] = __ldg(reinterpret_cast<const uint4*>(wr));
-            wn[1] = __ldg(reinterpret_cast<const uint4*>(wr + 8));
-        }
-        const uint32_t wv[8] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w, wa[1].x, wa[1].y, wa[1].z, wa[1].w};
-        float acc = 0.f;
+        const uint32_t wq[8] = {wv[i][0].x, wv[i][0].y, wv[i][0].z, wv[i][0].w,
+                                wv[i][1].x, wv[i][1].y, wv[i][1].z, wv[i][1].w};
+        float a = 0.f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            acc = fmaf(bf16_bits_to_f32(wv[q] & 0xffffu), cv[2 * q], acc);
-            acc = fmaf(bf16_bits_to_f32(wv[q] >> 16), cv[2 * q + 1], acc);
+            a = fmaf(bf16_bits_to_f32(wq[q] & 0xffffu), cv[2 * q], a);
+            a = fmaf(bf16_bits_to_f32(wq[q] >> 16), cv[2 * q + 1], a);
         }
-        acc = warp_sum(acc);
-        if (lane == 0) store_act(out, (static_cast<size_t>(b) * kMlaHeads + h) * kMlaV + d, acc);
-        wa[0] = wn[0];
-        wa[1] = wn[1];
+        a = warp_sum(a);
+        if (lane == 0) store_act(out, (static_cast<size_t>(b) * kMlaHeads + h) * kMlaV + d, a);
     }
 }
 
@@ -514,7 +601,7 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     if ((e = cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(kMlaSmem))) != cudaSuccess)
         return e;
-    if ((e = launch_pdl_kernel(mla_attn_kernel, dim3(a.splits, a.batch), dim3(kMlaWarps * 32), kMlaSmem, s, a.qp,
+    if ((e = launch_pdl_kernel(mla_attn_kernel, dim3(a.splits, a.batch), dim3(kMlaThreads), kMlaSmem, s, a.qp,
                                a.seqs, a.split_tokens, a.splits, a.partial)) != cudaSuccess)
         return e;
     if (a.splits > kOutMaxSplits) return cudaErrorInvalidValue;
