@@ -284,8 +284,11 @@ q4_matvec_generic_kernel(const uint8_t* __restrict__ packed, const uint16_t* __r
 // kTok16: bf16 activations, up to 16 tokens per pass; f32 activations use
 // hi/lo rows (8 tokens per pass). With fz.norm_w (f32 activations) the CTA
 // computes each token's 1/rms from x first and stages the normalised rows.
-template <typename XT, typename YT, int KS, bool kTok16>
-__global__ void __launch_bounds__(256, 2)
+// NB > 1: each warp's K-slice is exactly NB 4-group blocks, all held in
+// registers and loaded before the dependency wait (one CTA per SM for the
+// registers); NB = 1 streams the blocks one at a time.
+template <typename XT, typename YT, int KS, bool kTok16, int NB = 1>
+__global__ void __launch_bounds__(256, NB > 1 ? 1 : 2)
 q4_matvec_mma_kernel(const __grid_constant__ MvSet set, uint32_t cols, const XT* __restrict__ x, uint32_t batch,
                      MvFuse fz) {
     constexpr bool kLo = sizeof(XT) == 4;
@@ -311,13 +314,14 @@ q4_matvec_mma_kernel(const __grid_constant__ MvSet set, uint32_t cols, const XT*
     const uint32_t rg = min(r0 + g, rows - 1), ra = min(r0 + 2 * t, rows - 1), rb = min(r0 + 2 * t + 1, rows - 1);
     const uint8_t* wrow = m.packed + static_cast<size_t>(rg) * (cols / 2);
     const uint32_t grp0 = ks * gps;
-    Q4MmaFrag4 f;
+    Q4MmaFrag4 f[NB];
     // scale rows ra and rb = ra + 1 unless clamped; load them through the
     // (row 2t, row 2t+1) pair when both exist, else clamp both to ra
     const uint16_t* sa = m.scales + static_cast<size_t>(ra) * gpr;
     const uint16_t* ba = m.biases + static_cast<size_t>(ra) * gpr;
     const uint32_t pair_gpr = (rb == ra + 1) ? gpr : 0;
-    f.load(wrow, sa, ba, pair_gpr, grp0, t);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) f[j].load(wrow, sa, ba, pair_gpr, grp0 + 4 * j, t);
     pdl_launch_dependents();
     pdl_wait();
     for (uint32_t b0 = 0; b0 < batch; b0 += kPass) {
@@ -344,11 +348,16 @@ q4_matvec_mma_kernel(const __grid_constant__ MvSet set, uint32_t cols, const XT*
         else
             stage_act_rows8_tok<XT>(x + static_cast<size_t>(b0) * cols, cols, nt, cols, tile);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (uint32_t b = 0; b < gps; b += 4) {
-            if (b > 0) f.load(wrow, sa, ba, pair_gpr, grp0 + b, t);
-            f.compute<kLo, kTok16>(tile, grp0 + b, g, t, acc);
+        if constexpr (NB > 1) {
+#pragma unroll
+            for (int j = 0; j < NB; ++j) f[j].template compute<kLo, kTok16>(tile, grp0 + 4 * j, g, t, acc);
+        } else {
+            for (uint32_t b = 0; b < gps; b += 4) {
+                if (b > 0) f[0].load(wrow, sa, ba, pair_gpr, grp0 + b, t);
+                f[0].template compute<kLo, kTok16>(tile, grp0 + b, g, t, acc);
+            }
+            if (gps > 4) f[0].load(wrow, sa, ba, pair_gpr, grp0, t);  // block 0 again for the next pass
         }
-        if (gps > 4) f.load(wrow, sa, ba, pair_gpr, grp0, t);  // block 0 again for the next pass
         float* rw = red + warp * (16 * 8);
         rw[g * 8 + 2 * t] = acc[0];
         rw[g * 8 + 2 * t + 1] = acc[1];
@@ -411,8 +420,13 @@ static cudaError_t launch_mma_ks(const Q4MatvecArgs& a, cudaStream_t s) {
     const size_t trows = (lo || tok16) ? 16 : 8;
     const size_t smem = act_tile_bytes(a.cols, static_cast<uint32_t>(trows)) + 8 * 16 * 8 * 4;
     if (smem > 200 * 1024) return cudaErrorNotSupported;
+    // f32 activations whose warp slices are 2 or 3 blocks: every block in
+    // registers before the wait (the decode step's q_b: 1536 columns, KS 2)
+    const uint32_t nb = a.cols / 256 / KS;
     const void* fn = tok16 ? reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, true>)
                            : reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, false>);
+    if (lo && nb == 2) fn = reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, false, 2>);
+    if (lo && nb == 3) fn = reinterpret_cast<const void*>(q4_matvec_mma_kernel<XT, YT, KS, false, 3>);
     cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (err != cudaSuccess) return err;
     MvSet set;
