@@ -1329,9 +1329,10 @@ int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* cfg, uint32_t 
     if (!ctx->rope_table || ctx->rope_dim != cfg->rope_dim)
         return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "mla rope append: rope dim %u needs pbmoe_rope_reserve",
                     cfg->rope_dim);
-    if (!pbmoe::rope_append_supported(cfg->heads, cfg->rope_dim) || cfg->latent_dim == 0 || cache_len == 0)
-        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported MLA RoPE append: %u heads x rope %u",
-                    cfg->heads, cfg->rope_dim);
+    if (!pbmoe::rope_append_supported(cfg->heads, cfg->rope_dim) || cfg->latent_dim == 0 ||
+        cfg->latent_dim > 1024 || cache_len == 0)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported MLA RoPE append: %u heads x rope %u, latent %u",
+                    cfg->heads, cfg->rope_dim, cfg->latent_dim);
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
     pbmoe::RopeAppendArgs a{};

@@ -121,9 +121,35 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
         w[i] = (i < dq && d0 + i < nope) ? bf16_bits_to_f32(wcol[static_cast<size_t>(d0 + i) * kMlaLatent]) : 0.f;
     pdl_wait();
     pdl_launch_dependents();
-    for (uint32_t i = tid; i < batch * nope; i += blockDim.x) {
-        const uint32_t b = i / nope, d = i % nope;
-        qs[i] = load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + d);
+    // the query of every sequence (and, in the first column block, its rope
+    // part), 4 and 8 values per thread in flight at a time: one L2 round
+    // trip each at batch <= 8
+    const bool rope_cta = blockIdx.y == 0 && tid < kMlaRope;
+    for (uint32_t i0 = 0; i0 < batch * nope; i0 += 4 * 256) {
+        float qv[4];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t i = i0 + tid + j * 256;
+            qv[j] = i < batch * nope ? load_act(q, (static_cast<size_t>(i / nope) * kMlaHeads + h) * qdim + i % nope)
+                                     : 0.f;
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t i = i0 + tid + j * 256;
+            if (i < batch * nope) qs[i] = qv[j];
+        }
+    }
+    if (rope_cta) {
+        for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
+            float rv[8];
+#pragma unroll
+            for (uint32_t j = 0; j < 8; ++j)
+                rv[j] = b0 + j < batch ? load_act(q, (static_cast<size_t>(b0 + j) * kMlaHeads + h) * qdim + nope + tid)
+                                       : 0.f;
+#pragma unroll
+            for (uint32_t j = 0; j < 8; ++j)
+                if (b0 + j < batch) qp[(static_cast<size_t>(b0 + j) * kMlaHeads + h) * kMlaK + kMlaLatent + tid] = rv[j] * k;
+        }
     }
     __syncthreads();
     for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
@@ -149,11 +175,6 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
                 }
         }
         __syncthreads();
-    }
-    if (blockIdx.y == 0 && tid < kMlaRope) {
-        for (uint32_t b = 0; b < batch; ++b)
-            qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + kMlaLatent + tid] =
-                load_act(q, (static_cast<size_t>(b) * kMlaHeads + h) * qdim + nope + tid) * k;
     }
 }
 

@@ -77,6 +77,10 @@ cudaError_t rms_norm_launch(const NormArgs& a, cudaStream_t s) {
 constexpr int kRopeThreads = 256;
 constexpr uint32_t kRopeMaxPairs = 2048;  // heads x rope/2 rotated per token
 
+// Every load of a thread (query pairs, cos/sin, the key's rope pair, its
+// latent values and their norm weights) is issued once the token's position
+// is known, before any is used: two dependent round trips per token.
+constexpr uint32_t kRopeMaxLatent = 4 * kRopeThreads;
 __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppendArgs a) {
     pdl_wait();
     pdl_launch_dependents();
@@ -88,10 +92,12 @@ __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppen
     }
     const uint32_t half = a.rope / 2, qk = a.nope + a.rope;
     const float2* cs = a.table + static_cast<size_t>(pos) * half;
-    // query: read every pair of every head, then write the split halves
     float* q = a.query + static_cast<size_t>(b) * a.heads * qk;
+    const float* kv = a.kv + static_cast<size_t>(b) * (a.latent + a.rope);
     constexpr int kPer = kRopeMaxPairs / kRopeThreads;
+    constexpr int kLat = kRopeMaxLatent / kRopeThreads;
     float va[kPer], vb[kPer];
+    float2 tq[kPer];
     const uint32_t pairs = a.heads * half;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
@@ -100,34 +106,49 @@ __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppen
             const uint32_t h = i / half, p = i - h * half;
             va[j] = q[h * qk + a.nope + 2 * p];
             vb[j] = q[h * qk + a.nope + 2 * p + 1];
+            tq[j] = cs[p];  // (cos, sin)
         }
     }
-    __syncthreads();
+    const bool key_lane = threadIdx.x < half;
+    float k0 = 0.f, k1 = 0.f;
+    float2 tk = make_float2(0.f, 0.f);
+    if (key_lane) {
+        k0 = kv[a.latent + 2 * threadIdx.x];
+        k1 = kv[a.latent + 2 * threadIdx.x + 1];
+        tk = cs[threadIdx.x];
+    }
+    float lv[kLat], nw[kLat];
+#pragma unroll
+    for (int j = 0; j < kLat; ++j) {
+        const uint32_t i = threadIdx.x + j * kRopeThreads;
+        lv[j] = i < a.latent ? kv[i] : 0.f;
+        nw[j] = (i < a.latent && a.latent_norm_w) ? a.latent_norm_w[i] : 1.0f;
+    }
+    __syncthreads();  // every query pair read before the split halves are written
+    // query: the rotated halves of every head
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const uint32_t i = threadIdx.x + j * kRopeThreads;
         if (i < pairs) {
             const uint32_t h = i / half, p = i - h * half;
-            const float2 t = cs[p];  // (cos, sin)
-            q[h * qk + a.nope + p] = __fsub_rn(__fmul_rn(va[j], t.x), __fmul_rn(vb[j], t.y));
-            q[h * qk + a.nope + half + p] = __fadd_rn(__fmul_rn(vb[j], t.x), __fmul_rn(va[j], t.y));
+            q[h * qk + a.nope + p] = __fsub_rn(__fmul_rn(va[j], tq[j].x), __fmul_rn(vb[j], tq[j].y));
+            q[h * qk + a.nope + half + p] = __fadd_rn(__fmul_rn(vb[j], tq[j].x), __fmul_rn(va[j], tq[j].y));
         }
     }
     // key: the rope part after the latent, rotated into the cache row
-    const float* kv = a.kv + static_cast<size_t>(b) * (a.latent + a.rope);
-    uint16_t* krow = a.k_rope[b] + static_cast<size_t>(pos) * a.rope;
-    for (uint32_t p = threadIdx.x; p < half; p += blockDim.x) {
-        const float x0 = kv[a.latent + 2 * p], x1 = kv[a.latent + 2 * p + 1];
-        const float2 t = cs[p];
-        krow[p] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.y)));
-        krow[half + p] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(x1, t.x), __fmul_rn(x0, t.y)));
+    if (key_lane) {
+        uint16_t* krow = a.k_rope[b] + static_cast<size_t>(pos) * a.rope;
+        krow[threadIdx.x] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(k0, tk.x), __fmul_rn(k1, tk.y)));
+        krow[half + threadIdx.x] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(k1, tk.x), __fmul_rn(k0, tk.y)));
     }
-    // latent row, normalised here when the norm is fused (rms_norm_rows_kernel's formula)
+    // latent row, normalised here when the norm is fused (rms_norm_rows_kernel's
+    // formula; the sum of squares in the same per-thread order as a strided loop)
     float scale = 1.0f;
     if (a.latent_norm_w) {
         __shared__ float red[kRopeThreads / 32];
         float ss = 0.f;
-        for (uint32_t i = threadIdx.x; i < a.latent; i += blockDim.x) ss += kv[i] * kv[i];
+#pragma unroll
+        for (int j = 0; j < kLat; ++j) ss += lv[j] * lv[j];
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
         __syncthreads();
@@ -136,17 +157,20 @@ __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppen
         scale = 1.0f / sqrtf(tot / static_cast<float>(a.latent) + a.eps);
     }
     uint16_t* crow = a.c_kv[b] + static_cast<size_t>(pos) * a.latent;
-    for (uint32_t i = threadIdx.x; i < a.latent; i += blockDim.x)
-        crow[i] = f32_to_bf16_bits(a.latent_norm_w ? kv[i] * scale * a.latent_norm_w[i] : kv[i]);
+#pragma unroll
+    for (int j = 0; j < kLat; ++j) {
+        const uint32_t i = threadIdx.x + j * kRopeThreads;
+        if (i < a.latent) crow[i] = f32_to_bf16_bits(a.latent_norm_w ? lv[j] * scale * nw[j] : lv[j]);
+    }
 }
 
 bool rope_append_supported(uint32_t heads, uint32_t rope) {
-    return rope > 0 && rope % 2 == 0 && heads > 0 && heads * (rope / 2) <= kRopeMaxPairs;
+    return rope > 0 && rope % 2 == 0 && heads > 0 && heads * (rope / 2) <= kRopeMaxPairs && rope / 2 <= kRopeThreads;
 }
 
 cudaError_t mla_rope_append_launch(const RopeAppendArgs& a, cudaStream_t s) {
     if (a.batch == 0) return cudaSuccess;
-    if (!rope_append_supported(a.heads, a.rope)) return cudaErrorInvalidValue;
+    if (!rope_append_supported(a.heads, a.rope) || a.latent > kRopeMaxLatent) return cudaErrorInvalidValue;
     return launch_pdl_kernel(mla_rope_append_kernel, dim3(a.batch), dim3(kRopeThreads), 0, s, a);
 }
 
