@@ -733,8 +733,8 @@ struct MlaWsSizes {
 MlaWsSizes mla_ws_sizes(uint32_t max_batch, int num_sms) {
     MlaWsSizes w{};
     w.qp = align_up(size_t(max_batch) * 16 * 576 * 4, 256);
-    // batch x splits <= num_sms + batch (pbmoe::mla_plan_splits)
-    w.partial = align_up((size_t(num_sms) + 2 * max_batch) * 16 * 514 * 4, 256);
+    // batch x splits <= kMlaCtasPerSm * num_sms + batch (pbmoe::mla_plan_splits)
+    w.partial = align_up((size_t(pbmoe::kMlaCtasPerSm) * num_sms + 2 * max_batch) * 16 * 514 * 4, 256);
     w.ctx = align_up(size_t(max_batch) * 16 * 512 * 4, 256);
     w.total = w.qp + w.partial + w.ctx;
     return w;

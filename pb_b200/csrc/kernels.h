@@ -191,6 +191,7 @@ cudaError_t q4_matvec_launch(const Q4MatvecArgs& a, cudaStream_t s);
 
 // ---------------------------------------------------------------- MLA decode (mla.cu)
 constexpr uint32_t kMlaMaxBatch = 32;
+constexpr uint32_t kMlaCtasPerSm = 2;  // attention CTAs resident per SM (the split plan fills them)
 
 // Per-sequence latent caches, passed by value to the attention kernel.
 struct MlaSeqs {

@@ -14,7 +14,7 @@
 // Three launches:
 //   1. mla_absorb_kernel   q_lat for every (sequence, head), W_UK read once;
 //                          writes Q' = [q_lat | q_rope] * scale * log2(e) (f32).
-//   2. mla_attn_kernel     one CTA per (KV split, sequence): every 64-token
+//   2. mla_attn_kernel     one CTA per (KV split, sequence): every 32-token
 //                          tile of the split's latent cache is read from HBM
 //                          once (cp.async, double-buffered) and serves all 16
 //                          heads. S = Q' K^T (16 heads = the mma's M; Q' as
@@ -24,8 +24,8 @@
 //   3. mla_merge_out_kernel one CTA per (head, sequence): merges the splits'
 //                          partials into ctx (in shared memory), then
 //                          out = W_UV[h] ctx.
-// The split plan keeps batch x splits within one wave of SMs (the attention
-// kernel runs one CTA per SM).
+// The split plan keeps batch x splits within one wave (the attention kernel
+// runs two CTAs per SM).
 // Shapes: 16 heads, latent 512, rope 64, v 128, nope <= 128, batch <= 32.
 
 #include "common.cuh"
@@ -35,11 +35,10 @@ namespace pbmoe {
 
 constexpr uint32_t kMlaHeads = 16, kMlaLatent = 512, kMlaRope = 64, kMlaV = 128;
 constexpr uint32_t kMlaK = kMlaLatent + kMlaRope;  // 576: score dimension
-constexpr uint32_t kMlaTile = 64;                  // tokens per tile
+constexpr uint32_t kMlaTile = 32;                  // tokens per tile
 constexpr uint32_t kMlaWarps = 4;
 constexpr uint32_t kMlaThreads = kMlaWarps * 32;
 // shared-memory row strides (bytes), padded by 16 against ldmatrix bank conflicts
-constexpr uint32_t kQRow = kMlaK * 2 + 16;        // Q' hi / lo rows
 constexpr uint32_t kCRow = kMlaLatent * 2 + 16;   // c_kv rows
 constexpr uint32_t kRRow = kMlaRope * 2 + 16;     // k_rope rows
 constexpr uint32_t kPRow = kMlaTile * 2 + 16;     // P rows
@@ -49,10 +48,13 @@ constexpr uint32_t kMlaPartialFloats = 2 + kMlaLatent;  // max, sum, O
 constexpr uint32_t kKSteps = kMlaK / 16;                   // 36 k-steps of the score MMAs
 constexpr uint32_t kKStepsPerWarp = kKSteps / kMlaWarps;   // 9
 constexpr uint32_t kColsPerWarp = kMlaLatent / kMlaWarps;  // 128 context columns per warp
+constexpr uint32_t kTokNt = kMlaTile / 8;                  // 4 n-tiles of tokens per tile
 static_assert(kKSteps % kMlaWarps == 0, "score k-steps split evenly over the warps");
+static_assert(kMlaTile == 8 * kMlaWarps, "one n-tile of tokens per warp in the softmax");
 constexpr uint32_t kSRow = kMlaTile + 8;  // partial-score rows (floats), padded against bank conflicts
-constexpr size_t kMlaSmem = 2 * size_t(kMlaHeads) * kQRow + 2 * size_t(kStageBytes) + kMlaHeads * kPRow +
-                            kMlaWarps * kMlaHeads * 4 * 2 + size_t(kMlaWarps) * kMlaHeads * kSRow * 4;
+constexpr size_t kMlaSmem = 2 * size_t(kStageBytes) + kMlaHeads * kPRow + kMlaWarps * kMlaHeads * 4 * 2 +
+                            size_t(kMlaWarps) * kMlaHeads * kSRow * 4;
+static_assert(kMlaCtasPerSm * (kMlaSmem + 1024) <= 228 * 1024, "two attention CTAs per SM");
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -179,23 +181,23 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
 }
 
 // ---------------------------------------------------------------- 2. attention
-// grid (splits, batch), 128 threads (4 warps). Per 64-token tile (double-
-// buffered cp.async): warp w computes partial scores of every token of the
-// tile over score dims 144w .. 144w+143 (eight independent n-tile
-// accumulators); the partials meet in shared memory, summed in warp order;
-// warp w then owns tokens 16w .. 16w+15 for the online softmax and context
-// columns 128w .. 128w+127 for O += P C. Fragment loads run one k-step ahead
-// of the MMAs that use them (an ldmatrix takes ~95 cycles to return, an MMA
-// step 32-128 cycles of the tensor pipe).
-__global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* __restrict__ qp, MlaSeqs seqs,
-                                                                   uint32_t split_tokens, uint32_t splits,
-                                                                   float* __restrict__ partial) {
+// grid (splits, batch), 128 threads (4 warps), two CTAs per SM so that one
+// CTA's softmax and barriers overlap the other's MMAs. Per 32-token tile
+// (double-buffered cp.async): warp w computes partial scores of every token
+// of the tile over score dims 144w .. 144w+143 (its Q' hi and lo fragments
+// held in registers for the whole split: four independent n-tile
+// accumulators per half), the partials meet in shared memory, summed in warp
+// order; warp w then owns tokens 8w .. 8w+7 for the online softmax and
+// context columns 128w .. 128w+127 for O += P C. Fragment loads run one step
+// ahead of the MMAs that use them.
+__global__ void __launch_bounds__(kMlaThreads, kMlaCtasPerSm) mla_attn_kernel(const float* __restrict__ qp,
+                                                                               MlaSeqs seqs, uint32_t split_tokens,
+                                                                               uint32_t splits,
+                                                                               float* __restrict__ partial) {
     extern __shared__ __align__(128) unsigned char smem[];
     pdl_wait();
     pdl_launch_dependents();
-    unsigned char* qhi = smem;
-    unsigned char* qlo = qhi + kMlaHeads * kQRow;
-    unsigned char* stage0 = qlo + kMlaHeads * kQRow;
+    unsigned char* stage0 = smem;
     unsigned char* pbuf = stage0 + 2 * kStageBytes;
     float* wmax = reinterpret_cast<float*>(pbuf + kMlaHeads * kPRow);  // [warps][16]
     float* spart = wmax + kMlaWarps * kMlaHeads * 2;                     // [warps][16 heads][kSRow]
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* _
     // and chunk (i % 8) of rows i / 8 + 16j (k_rope); a whole tile takes
     // fixed offsets from two base pointers, the split's last tile zero-fills
     // rows past its end.
-    static_assert(kMlaThreads == 128 && kMlaTile == 64, "copy mapping assumes 128 threads, 64-token tiles");
+    static_assert(kMlaThreads == 128 && kMlaTile == 32, "copy mapping assumes 128 threads, 32-token tiles");
     const uint32_t c_row = threadIdx.x >> 6, c_ch = threadIdx.x & 63;
     const uint32_t r_row = threadIdx.x >> 3, r_ch = threadIdx.x & 7;
     auto issue_tile = [&](uint32_t tile, int buf) {
@@ -249,26 +251,30 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* _
     issue_tile(0, 0);
     cp_commit();
 
-    // Q' of this sequence as bf16 hi and lo (residue) rows; every load of the
-    // thread is issued before any conversion
+    // This warp's Q' (dims 144w .. 144w+143) as mma A fragments, bf16 hi and lo
+    // (residue): for k-step kk the fragment holds Q'[g][16kk + 2t, +1],
+    // Q'[g+8][...], Q'[g][16kk + 8 + 2t, +1], Q'[g+8][...]
+    const uint32_t kk0 = warp * kKStepsPerWarp;
+    uint32_t qh[kKStepsPerWarp][4], ql[kKStepsPerWarp][4];
     {
-        const float4* q4 = reinterpret_cast<const float4*>(qp + static_cast<size_t>(b) * kMlaHeads * kMlaK);
-        constexpr uint32_t kVec = kMlaHeads * kMlaK / 4;  // 2304 float4
-        constexpr uint32_t kPer = kVec / kMlaThreads;
-        static_assert(kVec % kMlaThreads == 0, "whole float4 per thread");
-        float4 v[kPer];
+        const float* qb = qp + static_cast<size_t>(b) * kMlaHeads * kMlaK;
+        float2 v[kKStepsPerWarp][4];
 #pragma unroll
-        for (uint32_t j = 0; j < kPer; ++j) v[j] = __ldcg(q4 + j * kMlaThreads + threadIdx.x);
-#pragma unroll
-        for (uint32_t j = 0; j < kPer; ++j) {
-            const uint32_t i = j * kMlaThreads + threadIdx.x;
-            const uint32_t h = i / (kMlaK / 4), c4 = i % (kMlaK / 4);
-            const uint32_t h0 = pack_bf16x2(v[j].x, v[j].y), h1 = pack_bf16x2(v[j].z, v[j].w);
-            const uint32_t l0 = pack_bf16x2(v[j].x - bf16_bits_to_f32(h0 & 0xffffu), v[j].y - bf16_bits_to_f32(h0 >> 16));
-            const uint32_t l1 = pack_bf16x2(v[j].z - bf16_bits_to_f32(h1 & 0xffffu), v[j].w - bf16_bits_to_f32(h1 >> 16));
-            *reinterpret_cast<uint2*>(qhi + h * kQRow + c4 * 8) = make_uint2(h0, h1);
-            *reinterpret_cast<uint2*>(qlo + h * kQRow + c4 * 8) = make_uint2(l0, l1);
+        for (uint32_t j = 0; j < kKStepsPerWarp; ++j) {
+            const uint32_t c = (kk0 + j) * 16 + 2 * t;
+            v[j][0] = __ldcg(reinterpret_cast<const float2*>(qb + g * kMlaK + c));
+            v[j][1] = __ldcg(reinterpret_cast<const float2*>(qb + (g + 8) * kMlaK + c));
+            v[j][2] = __ldcg(reinterpret_cast<const float2*>(qb + g * kMlaK + c + 8));
+            v[j][3] = __ldcg(reinterpret_cast<const float2*>(qb + (g + 8) * kMlaK + c + 8));
         }
+#pragma unroll
+        for (uint32_t j = 0; j < kKStepsPerWarp; ++j)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t h = pack_bf16x2(v[j][r].x, v[j][r].y);
+                qh[j][r] = h;
+                ql[j][r] = pack_bf16x2(v[j][r].x - bf16_bits_to_f32(h & 0xffffu), v[j][r].y - bf16_bits_to_f32(h >> 16));
+            }
     }
 
     // running state: heads g and g+8 (per lane), context columns of this warp
@@ -283,79 +289,79 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* _
     // B (n8 x k16) from [n][k] rows: lane -> row (lane & 7) + 8 * ((lane >> 4) & 1) for x4 over 2 n-tiles,
     // k half ((lane >> 3) & 1)
     const uint32_t b_row = (lane & 7) + ((lane >> 4) << 3), b_k = ((lane >> 3) & 1) * 8;
-    const uint32_t kk0 = warp * kKStepsPerWarp;
-    const uint32_t tok0 = warp * 16;  // first token of this warp's softmax columns
+    const uint32_t tok0 = warp * 8;  // first token of this warp's softmax columns
 
     for (uint32_t tile = 0; tile < ntiles; ++tile) {
         const int buf = tile & 1;
         if (tile + 1 < ntiles) issue_tile(tile + 1, buf ^ 1);
         cp_commit();
         cp_wait<1>();
-        __syncthreads();  // tile `tile` landed (and, on the first pass, Q')
+        __syncthreads();  // tile `tile` landed
         const unsigned char* st = stage0 + buf * kStageBytes;
         const unsigned char* rt = st + kMlaTile * kCRow;
 
-        // ---- partial scores over this warp's k-steps, all 64 tokens
+        // ---- partial scores over this warp's k-steps, all 32 tokens
         {
-            float sc[8][4];
+            float sh[kTokNt][4], sl[kTokNt][4];
 #pragma unroll
-            for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-            uint32_t fa[2][2][4], fb[2][4][4];  // [step parity][hi, lo | 16-token block][4]
-            auto load_step = [&](int f, uint32_t kk) {
-                ldsm_x4(fa[f][0], qhi + a_row * kQRow + (kk * 16 + a_col) * 2);
-                ldsm_x4(fa[f][1], qlo + a_row * kQRow + (kk * 16 + a_col) * 2);
+            for (int n = 0; n < kTokNt; ++n)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sh[n][i] = sl[n][i] = 0.f;
+            uint32_t fb[2][2][4];  // [step parity][16-token block][4]
+            auto load_b = [&](int f, uint32_t kk) {
                 const uint32_t kc = kk * 16 + b_k;
                 const bool lat = kk < kMlaLatent / 16;
                 const unsigned char* bsrc =
                     lat ? st + b_row * kCRow + kc * 2 : rt + b_row * kRRow + (kc - kMlaLatent) * 2;
                 const uint32_t bstep = lat ? 16 * kCRow : 16 * kRRow;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) ldsm_x4(fb[f][q], bsrc + q * bstep);
+                ldsm_x4(fb[f][0], bsrc);
+                ldsm_x4(fb[f][1], bsrc + bstep);
             };
-            load_step(0, kk0);
+            load_b(0, kk0);
 #pragma unroll
             for (uint32_t j = 0; j < kKStepsPerWarp; ++j) {
                 const int f = j & 1;
-                if (j + 1 < kKStepsPerWarp) load_step(f ^ 1, kk0 + j + 1);
+                if (j + 1 < kKStepsPerWarp) load_b(f ^ 1, kk0 + j + 1);
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
+                for (int q = 0; q < 2; ++q) {
+                    mma16816(sh[2 * q], qh[j], fb[f][q][0], fb[f][q][1]);
+                    mma16816(sh[2 * q + 1], qh[j], fb[f][q][2], fb[f][q][3]);
+                }
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        mma16816(sc[2 * q], fa[f][h], fb[f][q][0], fb[f][q][1]);
-                        mma16816(sc[2 * q + 1], fa[f][h], fb[f][q][2], fb[f][q][3]);
-                    }
+                for (int q = 0; q < 2; ++q) {
+                    mma16816(sl[2 * q], ql[j], fb[f][q][0], fb[f][q][1]);
+                    mma16816(sl[2 * q + 1], ql[j], fb[f][q][2], fb[f][q][3]);
+                }
             }
             float* sw = spart + warp * kMlaHeads * kSRow;
 #pragma unroll
-            for (int n = 0; n < 8; ++n) {
-                *reinterpret_cast<float2*>(sw + g * kSRow + n * 8 + 2 * t) = make_float2(sc[n][0], sc[n][1]);
-                *reinterpret_cast<float2*>(sw + (g + 8) * kSRow + n * 8 + 2 * t) = make_float2(sc[n][2], sc[n][3]);
+            for (int n = 0; n < kTokNt; ++n) {
+                const uint32_t col = n * 8 + 2 * t;
+                *reinterpret_cast<float2*>(sw + g * kSRow + col) = make_float2(sh[n][0] + sl[n][0], sh[n][1] + sl[n][1]);
+                *reinterpret_cast<float2*>(sw + (g + 8) * kSRow + col) =
+                    make_float2(sh[n][2] + sl[n][2], sh[n][3] + sl[n][3]);
             }
         }
         __syncthreads();  // every warp's partial scores written
-        // s[n][i]: n-tile n of tokens 16w .. 16w+15, (head g | g+8) x (token 2t | 2t+1)
-        float s[2][4];
+        // s[i]: (head g | g+8) x (token tok0 + 2t | +1), the warps' partials summed in order
+        float s[4];
         const uint32_t tbase = t0 + tile * kMlaTile + tok0;
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
+        for (int r = 0; r < 2; ++r) {
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-                for (int w = 0; w < kMlaWarps; ++w) {
-                    const float2 v = *reinterpret_cast<const float2*>(spart + (w * kMlaHeads + g + 8 * r) * kSRow +
-                                                                      tok0 + n * 8 + 2 * t);
-                    acc.x += v.x;
-                    acc.y += v.y;
-                }
-                const uint32_t tok = tbase + n * 8 + 2 * t;
-                s[n][2 * r] = tok < t1 ? acc.x : NEG_INF;
-                s[n][2 * r + 1] = tok + 1 < t1 ? acc.y : NEG_INF;
+            for (int w = 0; w < kMlaWarps; ++w) {
+                const float2 v =
+                    *reinterpret_cast<const float2*>(spart + (w * kMlaHeads + g + 8 * r) * kSRow + tok0 + 2 * t);
+                acc.x += v.x;
+                acc.y += v.y;
             }
-        // per-head maximum over the tile: warp's 16 tokens, then across warps
-        float mx[2];
-        mx[0] = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-        mx[1] = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+            const uint32_t tok = tbase + 2 * t;
+            s[2 * r] = tok < t1 ? acc.x : NEG_INF;
+            s[2 * r + 1] = tok + 1 < t1 ? acc.y : NEG_INF;
+        }
+        // per-head maximum over the tile: warp's 8 tokens, then across warps
+        float mx[2] = {fmaxf(s[0], s[1]), fmaxf(s[2], s[3])};
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 1));
@@ -377,26 +383,25 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* _
             m_run[r] = m;
         }
         // p = 2^(s - m) rounded to bf16; the row sums use the rounded values
-        float lsum[2] = {0.f, 0.f};
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
+        {
+            float lsum[2];
             uint32_t pw[2];
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const float p0 = (m_new[r] == NEG_INF) ? 0.f : exp2f(s[n][2 * r] - m_new[r]);
-                const float p1 = (m_new[r] == NEG_INF) ? 0.f : exp2f(s[n][2 * r + 1] - m_new[r]);
+                const float p0 = (m_new[r] == NEG_INF) ? 0.f : exp2f(s[2 * r] - m_new[r]);
+                const float p1 = (m_new[r] == NEG_INF) ? 0.f : exp2f(s[2 * r + 1] - m_new[r]);
                 pw[r] = pack_bf16x2(p0, p1);
-                lsum[r] += bf16_bits_to_f32(pw[r] & 0xffffu) + bf16_bits_to_f32(pw[r] >> 16);
+                lsum[r] = bf16_bits_to_f32(pw[r] & 0xffffu) + bf16_bits_to_f32(pw[r] >> 16);
             }
-            const uint32_t col = (tok0 + n * 8 + 2 * t) * 2;
+            const uint32_t col = (tok0 + 2 * t) * 2;
             *reinterpret_cast<uint32_t*>(pbuf + g * kPRow + col) = pw[0];
             *reinterpret_cast<uint32_t*>(pbuf + (g + 8) * kPRow + col) = pw[1];
-        }
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            lsum[r] += __shfl_xor_sync(kFull, lsum[r], 1);
-            lsum[r] += __shfl_xor_sync(kFull, lsum[r], 2);
-            l_run[r] = l_run[r] * alpha[r] + lsum[r];  // this warp's tokens only; summed over warps at the end
+            for (int r = 0; r < 2; ++r) {
+                lsum[r] += __shfl_xor_sync(kFull, lsum[r], 1);
+                lsum[r] += __shfl_xor_sync(kFull, lsum[r], 2);
+                l_run[r] = l_run[r] * alpha[r] + lsum[r];  // this warp's tokens only; summed over warps at the end
+            }
         }
 #pragma unroll
         for (int n = 0; n < kONt; ++n) {
@@ -406,26 +411,30 @@ __global__ void __launch_bounds__(kMlaThreads, 1) mla_attn_kernel(const float* _
             o[n][3] *= alpha[1];
         }
         __syncthreads();  // P complete
-        // ---- O[:, 128w .. 128w+127] += P (16 x 64) C (64 x 128), fragments one k-step ahead
+        // ---- O[:, 128w .. 128w+127] += P (16 x 32) C (32 x 128): four steps
+        // (16 tokens x 64 columns each), fragments one step ahead
         {
-            uint32_t pa[2][4], cb[2][kONt / 2][4];
-            auto load_pv = [&](int f, uint32_t kk) {
+            uint32_t pa[2][4], cb[2][4][4];
+            auto load_pv = [&](int f, uint32_t step) {
+                const uint32_t kk = step >> 1, hh = step & 1u;
                 ldsm_x4(pa[f], pbuf + a_row * kPRow + (kk * 16 + a_col) * 2);
                 // trans loads: rows = tokens kk*16 + (lane & 15), columns 8-wide blocks
                 const unsigned char* crow = st + (kk * 16 + (lane & 15)) * kCRow;
 #pragma unroll
-                for (int n = 0; n < kONt; n += 2)
-                    ldsm_x4_t(cb[f][n / 2], crow + (warp * kColsPerWarp + n * 8 + (lane >> 4) * 8) * 2);
+                for (int q = 0; q < 4; ++q)
+                    ldsm_x4_t(cb[f][q], crow + (warp * kColsPerWarp + hh * 64 + q * 16 + (lane >> 4) * 8) * 2);
             };
             load_pv(0, 0);
 #pragma unroll
-            for (uint32_t kk = 0; kk < kMlaTile / 16; ++kk) {
-                const int f = kk & 1;
-                if (kk + 1 < kMlaTile / 16) load_pv(f ^ 1, kk + 1);
+            for (uint32_t step = 0; step < 2 * (kMlaTile / 16); ++step) {
+                const int f = step & 1;
+                if (step + 1 < 2 * (kMlaTile / 16)) load_pv(f ^ 1, step + 1);
+                const int hh = step & 1;
 #pragma unroll
-                for (int n = 0; n < kONt; n += 2) {
-                    mma16816(o[n], pa[f], cb[f][n / 2][0], cb[f][n / 2][1]);
-                    mma16816(o[n + 1], pa[f], cb[f][n / 2][2], cb[f][n / 2][3]);
+                for (int q = 0; q < 4; ++q) {
+                    const int n = hh * 8 + 2 * q;
+                    mma16816(o[n], pa[f], cb[f][q][0], cb[f][q][1]);
+                    mma16816(o[n + 1], pa[f], cb[f][q][2], cb[f][q][3]);
                 }
             }
         }
@@ -588,22 +597,24 @@ bool mla_shape_supported(uint32_t heads, uint32_t rope, uint32_t latent, uint32_
 }
 
 // Splits of the longest cache such that batch x splits CTAs fill at most one
-// wave of SMs (one attention CTA per SM), each split at least one 64-token
-// tile; a split need not be a whole number of tiles (the last tile of a
-// split is masked).
+// wave (kMlaCtasPerSm attention CTAs per SM from batch 4 up; below that one
+// per SM, since the merge reads every split's partial serially), each split
+// at least two tiles; a split need not be a whole number of tiles (the last
+// tile of a split is masked).
 void mla_plan_splits(const MlaLaunch& a, int num_sms, uint32_t& split_tokens, uint32_t& splits) {
     uint32_t lmax = 1;
     for (uint32_t b = 0; b < a.batch; ++b) lmax = a.seqs.len[b] > lmax ? a.seqs.len[b] : lmax;
-    uint32_t want = static_cast<uint32_t>(num_sms) / (a.batch ? a.batch : 1);
+    const uint32_t per_sm = a.batch >= 4 ? kMlaCtasPerSm : 1u;
+    uint32_t want = per_sm * static_cast<uint32_t>(num_sms) / (a.batch ? a.batch : 1);
     if (want < 1) want = 1;
     uint32_t st = (lmax + want - 1) / want;
-    if (st < kMlaTile) st = kMlaTile;
+    if (st < 2 * kMlaTile) st = 2 * kMlaTile;
     split_tokens = st;
     splits = (lmax + st - 1) / st;
 }
 
 uint32_t mla_max_splits(uint32_t max_batch, int num_sms) {
-    return static_cast<uint32_t>(num_sms) / (max_batch ? max_batch : 1) + 1;
+    return kMlaCtasPerSm * static_cast<uint32_t>(num_sms) / (max_batch ? max_batch : 1) + 1;
 }
 
 cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
