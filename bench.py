@@ -42,6 +42,10 @@ per step, 48 layers cycled), matvec (config 0, Q4 [4096x2048]), gemm
 (config 2, tcgen05 prefill GEMM, dense and grouped), mla (config 3, absorbed
 MLA decode), head (config 4's vocab head + top-64), mxfp4 (the config-0 shape
 in MXFP4). Each prints the same keys as the headline line.
+
+`--timeline` (step, one GPU) also prints to stderr each kernel's share of the
+graph-replayed step's critical path from a CUPTI kernel timeline; it is
+analysis only and changes nothing in the JSON line.
 """
 
 from __future__ import annotations
@@ -84,6 +88,10 @@ def parse():
                         "matvec: config 0; gemm: config 2; mla: config 3; head: config 4's vocab head + top-k; "
                         "mxfp4: the config-0 matvec in MXFP4")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--timeline", action="store_true",
+                   help="step workload, one GPU: after the timed runs, print to stderr each kernel's share of the "
+                        "graph-replayed step's critical path from a CUPTI kernel timeline (torch.profiler); "
+                        "analysis only, never part of the JSON line")
     p.add_argument("--only-batch", action="store_true",
                    help="head / step workloads: run the --batch case alone (no batch 1/8/32 listing)")
     return p.parse_args()
@@ -813,13 +821,6 @@ def run_mxfp4(args):
     calls = [(lambda m=m: ctx.mxfp4_matvec(m[0], m[1], R, Cc, x, y, stream=s)) for m in mats]
     ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
     gbs = byts / (ms / 1e3) / 1e9
-    # the same 64 matrices as one resident projection batch on the input
-    # (pbmoe_q4_matvec_batch, resident_mmap_matvec_batch): 4 launches of 16
-    ys = [torch.empty(1, R, device="cuda", dtype=torch.bfloat16) for _ in range(NC)]
-    spec = [(m[0], m[1], m[2], R, Cc, G) for m in mats]
-    bms, _, _ = _graph_time([lambda: ctx.q4_matvec_batch(spec, x, ys, stream=s)], s, max(8, args.steps // NC),
-                            args.warmup)
-    bgbs = NC * byts / (bms / 1e3) / 1e9
     hx = x.cpu().pin_memory()
     hy = torch.empty(1, R, dtype=torch.bfloat16).pin_memory()
     dx = torch.empty_like(x)
@@ -1195,6 +1196,9 @@ def run_step(args):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K)
     assert ctx.device_status(stream=s) == 0
 
+    if args.timeline and world == 1:
+        _print_timeline(graph, step, x0, s, cfg.layers)
+
     # per-call timing: one step launched call by call with events between the
     # calls (and the MoE layer's phase events on one GPU); serialised, so the
     # shares are the figure, not the sum
@@ -1300,8 +1304,55 @@ def run_step(args):
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the step's kernels
 # from one ncu capture (config-4 shapes, batch 8); filled per kernel captured
-STEP_NCU_TRAFFIC: dict = {}
-STEP_NCU_SOURCE: dict = {}
+# DRAM read + write bytes per call, summed over the call's kernels (ncu flushes
+# the caches before each profiled kernel, so reads that hit L2 in a replayed
+# step, e.g. the MLA split partials, count here)
+STEP_NCU_TRAFFIC: dict = {
+    "mla_decode": (2.230272 + 75.826176 + 2.808832 + 11.858176) * 1e6,  # absorb, attention (+ partials written), merge
+    "moe_router": 2.26e6,
+    "moe_gate_up": (73.21 + 2.15) * 1e6,
+    "moe_down": (36.80 + 0.13) * 1e6,
+    "q_a+kv_a": 2.52e6,
+    "q_b": 2.74432e6,
+}
+_STEP_NCU_CMD = ("ncu --set full --clock-control none -k regex:<kernel> -s <n> -c 1 python bench.py --workload step "
+                 "--layers 2 --steps 3 --warmup 3 --no-cpu-baseline (one launch per kernel, config-4 shapes, batch 8)")
+STEP_NCU_SOURCE: dict = {k: _STEP_NCU_CMD for k in STEP_NCU_TRAFFIC}
+
+
+def _print_timeline(graph, step, x0, s, layers):
+    """Each kernel's contribution to the critical path of one graph-replayed
+    step (how far it extends the timeline past every earlier kernel's end),
+    from a CUPTI kernel timeline; written to stderr."""
+    import json
+    import tempfile
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with torch.cuda.stream(s):
+            step.x.copy_(x0)
+            graph.replay()
+        s.synchronize()
+    with tempfile.NamedTemporaryFile(suffix=".json") as fh:
+        prof.export_chrome_trace(fh.name)
+        ev = json.load(open(fh.name))["traceEvents"]
+    ks = sorted((e for e in ev if e.get("cat") == "kernel"), key=lambda e: e["ts"])
+    agg, prev_end = {}, None
+    for e in ks:
+        name = e["name"].split("(")[0].split("<")[0].replace("void ", "").replace("pbmoe::", "")
+        st, end = e["ts"], e["ts"] + e["dur"]
+        a = agg.setdefault(name, [0, 0.0, 0.0])
+        a[0] += 1
+        a[1] += e["dur"]
+        a[2] += end - st if prev_end is None else max(0.0, end - max(prev_end, st))
+        prev_end = end if prev_end is None else max(prev_end, end)
+    span = (ks[-1]["ts"] + ks[-1]["dur"] - ks[0]["ts"]) if ks else 0.0
+    print(f"timeline: {len(ks)} kernels, span {span / 1e3:.3f} ms (under the profiler)", file=sys.stderr)
+    print(f"{'kernel':30s} {'launches':>8s} {'busy ms':>8s} {'critical ms':>11s} {'us/layer':>9s}", file=sys.stderr)
+    for name, (n, busy, crit) in sorted(agg.items(), key=lambda kv: -kv[1][2]):
+        print(f"{name:30s} {n:8d} {busy / 1e3:8.3f} {crit / 1e3:11.3f} {crit / layers:9.2f}", file=sys.stderr)
 
 
 def C_void_p_array(events):
