@@ -363,7 +363,8 @@ typedef struct pbmoe_mla_args {
     const uint16_t* const* k_rope;  /* HOST array [batch] of device pointers:
                                        bf16 [seq_len x rope], rotated at write,
                                        16-byte aligned                                   */
-    const uint16_t* w_uk;           /* bf16 [heads x nope x latent] (absorbed into q)    */
+    const uint16_t* w_uk;           /* bf16 [heads x nope x latent] (absorbed into q),
+                                       16-byte aligned                                   */
     const uint16_t* w_uv;           /* bf16 [heads x v x latent], 16-byte aligned        */
     void* out;                      /* [batch x heads x v] in out_dtype                  */
     pbmoe_dtype out_dtype;

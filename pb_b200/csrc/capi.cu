@@ -805,7 +805,7 @@ int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_
         return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "mla: workspace reserved for batch<=%u, call needs %u "
                     "(call pbmoe_mla_reserve)", ctx->mla_batch, a->batch);
     if (!aligned(a->query, a->query_dtype == PBMOE_F32 ? 4 : 2) ||
-        !aligned(a->out, a->out_dtype == PBMOE_F32 ? 4 : 2) || !aligned(a->w_uk, 2) || !aligned(a->w_uv, 16))
+        !aligned(a->out, a->out_dtype == PBMOE_F32 ? 4 : 2) || !aligned(a->w_uk, 16) || !aligned(a->w_uv, 16))
         return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla: misaligned query / out / W_UK / W_UV");
     pbmoe::MlaLaunch L{};
     L.batch = a->batch;

@@ -98,29 +98,33 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---------------------------------------------------------------- 1. absorb
-// grid (heads, latent/64), 256 threads: thread (quarter = tid/64, column
-// c = 64*blockIdx.y + tid%64) sums a quarter of the nope dims for every
-// sequence, with all its W_UK loads in flight at once; the quarters meet in
-// shared memory. Writes Q'[b][h][0..511] = q_lat * k and Q'[b][h][512..575] =
-// q_rope * k, k = scale * log2(e). nope <= 128 (host-checked).
+// grid (heads, latent/64), 256 threads. Thread (rg = tid/8, cb = tid%8) holds
+// W_UK[h][d][64*blockIdx.y + 8cb .. +7] for d = rg, rg+32, rg+64, rg+96 (four
+// 16-byte loads issued before the dependency wait) and sums those rows'
+// contributions for 8 sequences at a time; the 4 lanes of a warp that share
+// cb add theirs with shuffles, the 8 warps theirs in shared memory. Writes
+// Q'[b][h][0..511] = q_lat * k and Q'[b][h][512..575] = q_rope * k,
+// k = scale * log2(e). nope <= 128 (host-checked).
 constexpr uint32_t kAbsorbMaxNope = 128;
 template <typename QT>
 __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ q, uint32_t batch, uint32_t nope,
                                                          const uint16_t* __restrict__ w_uk, float k,
                                                          float* __restrict__ qp) {
     __shared__ float qs[kMlaMaxBatch * kAbsorbMaxNope];
-    __shared__ float red[4][8][64];
-    const uint32_t h = blockIdx.x, tid = threadIdx.x;
-    const uint32_t quarter = tid >> 6, cc = tid & 63, c = blockIdx.y * 64 + cc;
+    __shared__ float red[8][8][64];  // [warp][sequence of the pass][column]
+    const uint32_t h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t cb = tid & 7, rg = tid >> 3;
     const uint32_t qdim = nope + kMlaRope;
     // W_UK does not depend on the earlier kernels: its loads are issued before
     // waiting for them
-    const uint32_t dq = (nope + 3) / 4, d0 = quarter * dq;
-    float w[kAbsorbMaxNope / 4];
-    const uint16_t* wcol = w_uk + static_cast<size_t>(h) * nope * kMlaLatent + c;
+    uint4 wv[kAbsorbMaxNope / 32];
 #pragma unroll
-    for (uint32_t i = 0; i < kAbsorbMaxNope / 4; ++i)
-        w[i] = (i < dq && d0 + i < nope) ? bf16_bits_to_f32(wcol[static_cast<size_t>(d0 + i) * kMlaLatent]) : 0.f;
+    for (uint32_t i = 0; i < kAbsorbMaxNope / 32; ++i) {
+        const uint32_t d = rg + 32 * i;
+        wv[i] = d < nope ? __ldg(reinterpret_cast<const uint4*>(w_uk + (static_cast<size_t>(h) * nope + d) * kMlaLatent +
+                                                                blockIdx.y * 64 + cb * 8))
+                         : make_uint4(0, 0, 0, 0);
+    }
     pdl_wait();
     pdl_launch_dependents();
     // the query of every sequence (and, in the first column block, its rope
@@ -155,26 +159,53 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
     }
     __syncthreads();
     for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
-        float acc[8];
+        float acc[8][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            acc[j] = 0.f;
-            if (b0 + j < batch) {
-                const float* qb = qs + (b0 + j) * nope + d0;
+        for (int j = 0; j < 8; ++j)
 #pragma unroll
-                for (uint32_t i = 0; i < kAbsorbMaxNope / 4; ++i)
-                    if (i < dq && d0 + i < nope) acc[j] = fmaf(qb[i], w[i], acc[j]);
+            for (int c = 0; c < 8; ++c) acc[j][c] = 0.f;
+#pragma unroll
+        for (uint32_t i = 0; i < kAbsorbMaxNope / 32; ++i) {
+            const uint32_t d = rg + 32 * i;
+            if (d < nope) {
+                const uint32_t wq[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+                float wf[8];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    wf[2 * c] = bf16_bits_to_f32(wq[c] & 0xffffu);
+                    wf[2 * c + 1] = bf16_bits_to_f32(wq[c] >> 16);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float qv = b0 + j < batch ? qs[(b0 + j) * nope + d] : 0.f;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) acc[j][c] = fmaf(qv, wf[c], acc[j][c]);
+                }
             }
-            red[quarter][j][cc] = acc[j];
         }
-        __syncthreads();
-        if (quarter == 0) {
+        // the warp's 4 row groups of column block cb: lanes cb, cb+8, cb+16, cb+24
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                acc[j][c] += __shfl_xor_sync(kFull, acc[j][c], 8);
+                acc[j][c] += __shfl_xor_sync(kFull, acc[j][c], 16);
+            }
+        if (lane < 8) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-                if (b0 + j < batch) {
-                    const float v = red[0][j][cc] + red[1][j][cc] + red[2][j][cc] + red[3][j][cc];
-                    qp[(static_cast<size_t>(b0 + j) * kMlaHeads + h) * kMlaK + c] = v * k;
-                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c) red[warp][j][lane * 8 + c] = acc[j][c];
+        }
+        __syncthreads();
+        for (uint32_t o = tid; o < 8 * 64; o += 256) {
+            const uint32_t j = o / 64, col = o % 64;
+            if (b0 + j < batch) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) v += red[w][j][col];
+                qp[(static_cast<size_t>(b0 + j) * kMlaHeads + h) * kMlaK + blockIdx.y * 64 + col] = v * k;
+            }
         }
         __syncthreads();
     }
