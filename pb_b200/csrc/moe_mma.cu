@@ -115,7 +115,7 @@ moe_expert_up_mma_kernel(const XT* __restrict__ x, uint32_t E, const uint8_t* __
         const int nt = static_cast<int>(min(n - p0, static_cast<uint32_t>(kPass)));
         __syncthreads();
         if (kRows16)
-            stage_act_mma<XT>(x, H, ws.group_tokens + start + p0, nt, H, tile);
+            stage_act_mma<XT, 1>(x, H, ws.group_tokens + start + p0, nt, H, tile);
         else
             stage_act_rows8<XT>(x, H, ws.group_tokens + start + p0, nt, H, tile);
         float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
@@ -190,7 +190,7 @@ moe_expert_down_mma_kernel(uint32_t E, const uint8_t* __restrict__ experts, cons
     for (uint32_t p0 = 0; p0 < n; p0 += 8) {
         const int nt = static_cast<int>(min(n - p0, 8u));
         __syncthreads();
-        stage_act_mma<float>(ws.h, I, ws.group_routes + start + p0, nt, I, tile);
+        stage_act_mma<float, 1>(ws.h, I, ws.group_routes + start + p0, nt, I, tile);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         f0.compute<true, false>(tile, 0, g, t, acc);
         if (gpr > 4) f1.compute<true, false>(tile, 4, g, t, acc);

@@ -149,7 +149,6 @@ constexpr int kSmThreads = 256;
 constexpr int kSmRows = 32;       // rows per block
 constexpr int kSmStages = 4;
 constexpr uint32_t kSmMaxCols = 2048;
-constexpr uint32_t kSmStageBytes = kSmRows * (kSmMaxCols / 2) + 2 * kSmRows * (kSmMaxCols / 32) * 2;
 
 __device__ __forceinline__ const MvMat& mv_pick_block(const MvSet& set, uint32_t blk, uint32_t& bx) {
     uint32_t i = 0;

@@ -112,90 +112,97 @@ __device__ __forceinline__ void tile_sync(int bar_id, uint32_t nthreads) {
 // f32 rows may be normalised on the way in: with norm_w, activation c of token
 // t is staged as x * nscale[t] * norm_w[c] (nscale: the tokens' 1/rms, in
 // shared memory, computed by the caller).
-template <typename XT>
+template <typename XT, uint32_t kBatch = 4>
 __device__ void stage_act_mma(const XT* __restrict__ x, size_t x_stride, const uint32_t* rows_idx, int ntok,
                               uint32_t K, const ActTile& tile, int bar_id = 0, uint32_t nthreads = 0,
                               const float* __restrict__ norm_w = nullptr, const float* nscale = nullptr) {
     constexpr bool kLo = sizeof(XT) == 4;
     const uint32_t nthr = nthreads ? nthreads : blockDim.x;
     const uint32_t slots = K / 8;
-    const uint32_t nrows = 16;
-    // zero the unused rows (and, for bf16, rows ntok..15; for f32, rows ntok..7 and 8+ntok..15)
-    for (uint32_t i = threadIdx.x; i < nrows * slots; i += nthr) {
-        const uint32_t row = i / slots;
+    const uint32_t nt = static_cast<uint32_t>(ntok);
+    // zero the unused rows (and, for bf16, rows ntok..15; for f32, rows ntok..7
+    // and 8+ntok..15) and their group sums (for f32 also rows 8..15), row by
+    // row: no division by the row length
+    for (uint32_t row = 0; row < 16; ++row) {
         const uint32_t tok = kLo ? (row & 7u) : row;
-        if (tok >= static_cast<uint32_t>(ntok)) tile.act[(i / slots) * tile.stride + (i % slots)] = make_uint4(0, 0, 0, 0);
+        if (tok >= nt)
+            for (uint32_t w = threadIdx.x; w < slots; w += nthr) tile.act[row * tile.stride + w] = make_uint4(0, 0, 0, 0);
+        if (tok >= nt || (kLo && row >= 8))
+            for (uint32_t gi = threadIdx.x; gi < tile.groups; gi += nthr) tile.gsum[row * tile.groups + gi] = 0.f;
     }
-    for (uint32_t i = threadIdx.x; i < nrows * tile.groups; i += nthr) {
-        const uint32_t row = i / tile.groups;
-        const uint32_t tok = kLo ? (row & 7u) : row;
-        if (tok >= static_cast<uint32_t>(ntok) || (kLo && row >= 8)) tile.gsum[i] = 0.f;
-    }
-    // one thread per (token, word): 8 activations
-    const uint32_t total = static_cast<uint32_t>(ntok) * slots;
-    constexpr int kBatch = kLo ? 1 : 4;
-    for (uint32_t base = 0; base < total; base += kBatch * nthr) {
-        uint4 v[kBatch][kLo ? 2 : 1];
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * nthr + threadIdx.x;
-            if (idx < total) {
-                const uint32_t t = idx / slots, w = idx - t * slots;
-                const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
-                const uint4* p = reinterpret_cast<const uint4*>(x + src * x_stride + static_cast<size_t>(w) * 8);
-                v[i][0] = p[0];
-                if constexpr (kLo) v[i][1] = p[1];
+    // a thread keeps word w = w0 + threadIdx.x of every token (8 activations):
+    // kBatch tokens' loads in flight at once (1 for register-heavy callers),
+    // the word's norm weights loaded once; the 8 words of a 64-column group
+    // are 8 consecutive lanes
+    for (uint32_t w0 = 0; w0 < slots; w0 += nthr) {
+        const uint32_t w = w0 + threadIdx.x;
+        const bool okw = w < slots;
+        float nn[8];
+        if constexpr (kLo) {
+            if (norm_w && okw) {
+                const float4 n0 = *reinterpret_cast<const float4*>(norm_w + static_cast<size_t>(w) * 8);
+                const float4 n1 = *reinterpret_cast<const float4*>(norm_w + static_cast<size_t>(w) * 8 + 4);
+                nn[0] = n0.x, nn[1] = n0.y, nn[2] = n0.z, nn[3] = n0.w, nn[4] = n1.x, nn[5] = n1.y, nn[6] = n1.z,
+                nn[7] = n1.w;
             }
         }
+        for (uint32_t t0 = 0; t0 < nt; t0 += kBatch) {
+            uint4 v[kBatch][kLo ? 2 : 1];
 #pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * nthr + threadIdx.x;
-            float sum = 0.f;
-            uint32_t t = 0, w = 0;
-            const bool ok = idx < total;
-            if (ok) {
-                t = idx / slots;
-                w = idx - t * slots;
-                if constexpr (!kLo) {
-                    const uint4 r = v[i][0];  // (x0,x1) (x2,x3) (x4,x5) (x6,x7)
-                    tile.act[t * tile.stride + w] =
-                        make_uint4(pack_pairs_lo(r.x, r.z), pack_pairs_hi(r.x, r.z), pack_pairs_lo(r.y, r.w),
-                                   pack_pairs_hi(r.y, r.w));
-                    const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) sum += __uint_as_float(rr[q] << 16) + __uint_as_float(rr[q] & 0xffff0000u);
-                } else {
-                    float f[8] = {__uint_as_float(v[i][0].x), __uint_as_float(v[i][0].y), __uint_as_float(v[i][0].z),
-                                  __uint_as_float(v[i][0].w), __uint_as_float(v[i][1].x), __uint_as_float(v[i][1].y),
-                                  __uint_as_float(v[i][1].z), __uint_as_float(v[i][1].w)};
-                    if (norm_w) {
-                        const float sc = nscale[t];
-                        const float4 n0 = *reinterpret_cast<const float4*>(norm_w + static_cast<size_t>(w) * 8);
-                        const float4 n1 = *reinterpret_cast<const float4*>(norm_w + static_cast<size_t>(w) * 8 + 4);
-                        const float nn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) f[q] = f[q] * sc * nn[q];
-                    }
-                    uint32_t hi[4], lo[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        // pair order (x_q, x_{q+4})
-                        const uint32_t h = f2_to_bf16x2(f[q], f[q + 4]);
-                        const float h0 = __uint_as_float(h << 16), h1 = __uint_as_float(h & 0xffff0000u);
-                        hi[q] = h;
-                        lo[q] = f2_to_bf16x2(f[q] - h0, f[q + 4] - h1);
-                        sum += f[q] + f[q + 4];
-                    }
-                    tile.act[t * tile.stride + w] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    tile.act[(t + 8) * tile.stride + w] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            for (uint32_t i = 0; i < kBatch; ++i) {
+                const uint32_t t = t0 + i;
+                if (okw && t < nt) {
+                    const size_t src = rows_idx ? rows_idx[t] : static_cast<size_t>(t);
+                    const uint4* p = reinterpret_cast<const uint4*>(x + src * x_stride + static_cast<size_t>(w) * 8);
+                    v[i][0] = p[0];
+                    if constexpr (kLo) v[i][1] = p[1];
                 }
             }
-            // group sums: the 8 words of a group are 8 consecutive threads
-            // when slots % 8 == 0 (always: K % 64 == 0)
-            sum += __shfl_xor_sync(kFull, sum, 1);
-            sum += __shfl_xor_sync(kFull, sum, 2);
-            sum += __shfl_xor_sync(kFull, sum, 4);
-            if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
+#pragma unroll
+            for (uint32_t i = 0; i < kBatch; ++i) {
+                const uint32_t t = t0 + i;
+                if (t >= nt) break;  // uniform: every lane has the same token
+                const bool ok = okw;
+                float sum = 0.f;
+                if (ok) {
+                    if constexpr (!kLo) {
+                        const uint4 r = v[i][0];  // (x0,x1) (x2,x3) (x4,x5) (x6,x7)
+                        tile.act[t * tile.stride + w] =
+                            make_uint4(pack_pairs_lo(r.x, r.z), pack_pairs_hi(r.x, r.z), pack_pairs_lo(r.y, r.w),
+                                       pack_pairs_hi(r.y, r.w));
+                        const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            sum += __uint_as_float(rr[q] << 16) + __uint_as_float(rr[q] & 0xffff0000u);
+                    } else {
+                        float f[8] = {__uint_as_float(v[i][0].x), __uint_as_float(v[i][0].y),
+                                      __uint_as_float(v[i][0].z), __uint_as_float(v[i][0].w),
+                                      __uint_as_float(v[i][1].x), __uint_as_float(v[i][1].y),
+                                      __uint_as_float(v[i][1].z), __uint_as_float(v[i][1].w)};
+                        if (norm_w) {
+                            const float sc = nscale[t];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) f[q] = f[q] * sc * nn[q];
+                        }
+                        uint32_t hi[4], lo[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            // pair order (x_q, x_{q+4})
+                            const uint32_t h = f2_to_bf16x2(f[q], f[q + 4]);
+                            const float h0 = __uint_as_float(h << 16), h1 = __uint_as_float(h & 0xffff0000u);
+                            hi[q] = h;
+                            lo[q] = f2_to_bf16x2(f[q] - h0, f[q + 4] - h1);
+                            sum += f[q] + f[q + 4];
+                        }
+                        tile.act[t * tile.stride + w] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        tile.act[(t + 8) * tile.stride + w] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    }
+                }
+                sum += __shfl_xor_sync(kFull, sum, 1);
+                sum += __shfl_xor_sync(kFull, sum, 2);
+                sum += __shfl_xor_sync(kFull, sum, 4);
+                if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
+            }
         }
     }
     tile_sync(bar_id, nthreads);
@@ -209,34 +216,28 @@ __device__ void stage_act_rows8_tok(const XT* __restrict__ x, size_t x_stride, i
     const uint32_t nthr = nthreads ? nthreads : blockDim.x;
     static_assert(sizeof(XT) == 2, "8-row tiles hold bf16 activations");
     const uint32_t slots = K / 8;
-    for (uint32_t i = threadIdx.x; i < 8 * slots; i += nthr)
-        if (i / slots >= static_cast<uint32_t>(ntok)) tile.act[(i / slots) * tile.stride + (i % slots)] = make_uint4(0, 0, 0, 0);
-    for (uint32_t i = threadIdx.x; i < 8 * tile.groups; i += nthr)
-        if (i / tile.groups >= static_cast<uint32_t>(ntok)) tile.gsum[i] = 0.f;
-    const uint32_t total = static_cast<uint32_t>(ntok) * slots;
-    constexpr int kBatch = 4;
-    for (uint32_t base = 0; base < total; base += kBatch * nthr) {
-        uint4 v[kBatch];
+    const uint32_t nt = static_cast<uint32_t>(ntok);
+    for (uint32_t row = nt; row < 8; ++row) {  // absent tokens: zero rows and group sums
+        for (uint32_t w = threadIdx.x; w < slots; w += nthr) tile.act[row * tile.stride + w] = make_uint4(0, 0, 0, 0);
+        for (uint32_t gi = threadIdx.x; gi < tile.groups; gi += nthr) tile.gsum[row * tile.groups + gi] = 0.f;
+    }
+    // a thread keeps word w = w0 + threadIdx.x of every token, all tokens'
+    // loads in flight at once; the 8 words of a group are 8 consecutive lanes
+    for (uint32_t w0 = 0; w0 < slots; w0 += nthr) {
+        const uint32_t w = w0 + threadIdx.x;
+        const bool okw = w < slots;
+        uint4 v[8];
 #pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * nthr + threadIdx.x;
-            if (idx < total) {
-                const uint32_t t = idx / slots, w = idx - t * slots;
-                v[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * x_stride + static_cast<size_t>(w) * 8);
-            }
-        }
+        for (uint32_t t = 0; t < 8; ++t)
+            if (okw && t < nt) v[t] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * x_stride + static_cast<size_t>(w) * 8);
 #pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-            const uint32_t idx = base + i * nthr + threadIdx.x;
+        for (uint32_t t = 0; t < 8; ++t) {
+            if (t >= nt) break;  // uniform
             float sum = 0.f;
-            uint32_t t = 0, w = 0;
-            const bool ok = idx < total;
-            if (ok) {
-                t = idx / slots;
-                w = idx - t * slots;
-                const uint4 r = v[i];
+            if (okw) {
+                const uint4 r = v[t];
                 tile.act[t * tile.stride + w] = make_uint4(pack_pairs_lo(r.x, r.z), pack_pairs_hi(r.x, r.z),
-                                                                  pack_pairs_lo(r.y, r.w), pack_pairs_hi(r.y, r.w));
+                                                           pack_pairs_lo(r.y, r.w), pack_pairs_hi(r.y, r.w));
                 const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) sum += __uint_as_float(rr[q] << 16) + __uint_as_float(rr[q] & 0xffff0000u);
@@ -244,7 +245,7 @@ __device__ void stage_act_rows8_tok(const XT* __restrict__ x, size_t x_stride, i
             sum += __shfl_xor_sync(kFull, sum, 1);
             sum += __shfl_xor_sync(kFull, sum, 2);
             sum += __shfl_xor_sync(kFull, sum, 4);
-            if (ok && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
+            if (okw && (w & 7u) == 0) tile.gsum[t * tile.groups + (w >> 3)] = sum;
         }
     }
     tile_sync(bar_id, nthreads);
