@@ -331,9 +331,18 @@ q4_matvec_mma_kernel(const __grid_constant__ MvSet set, uint32_t cols, const XT*
                 for (int tok = warp; tok < nt; tok += 8) {
                     const float* xr = reinterpret_cast<const float*>(x) + static_cast<size_t>(b0 + tok) * cols;
                     float ss = 0.f;
-                    for (uint32_t i = lane * 4; i < cols; i += 128) {
-                        const float4 v = *reinterpret_cast<const float4*>(xr + i);
-                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    // the lane's float4 of the row 8 at a time, each batch's loads in
+                    // flight together (two round trips at 1536 columns), summed in order
+                    for (uint32_t c0 = 0; c0 < cols; c0 += 8 * 128) {
+                        float4 v[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t i = c0 + lane * 4 + j * 128;
+                            v[j] = i < cols ? *reinterpret_cast<const float4*>(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
                     }
                     ss = warp_sum(ss);
                     if (lane == 0) nscale[tok] = 1.0f / sqrtf(ss / static_cast<float>(cols) + fz.eps);
