@@ -500,37 +500,36 @@ __global__ void __launch_bounds__(kMlaThreads, kMlaCtasPerSm) mla_attn_kernel(co
 }
 
 // ---------------------------------------------------------------- 3. merge + output
-// grid (heads, batch), 256 threads. The splits of (sequence b, head h) are
-// merged as ctx[c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s into
-// shared memory, then warp w computes out rows d = w, w + 8, ... of
-// W_UV[h] ctx (16 rows per warp). Every W_UV load of the thread (its 16
-// rows x 16 latent columns) is issued before the dependency wait, and the
-// first 16 splits' partials of its two context columns are loaded together
-// with the split maxima and sums: the merge waits on one L2 round trip for up
-// to 16 splits and on one more per further 16.
+// grid (heads, batch), 256 threads, one CTA per SM. W_UV[h] (128 KB) is copied
+// into shared memory by cp.async before the dependency wait. The splits of
+// (sequence b, head h) are merged as
+// ctx[c] = sum_s 2^(m_s - M) O_s[c] / sum_s 2^(m_s - M) l_s into shared memory:
+// thread c holds columns c and c + 256 of up to kOutChunk splits, loaded
+// together with the split maxima and sums (one L2 round trip up to kOutChunk
+// splits). Then warp w computes out rows d = w, w + 8, ... of W_UV[h] ctx, a
+// lane covering latent columns 8 lane .. +7 and 256 + 8 lane .. +7.
 constexpr uint32_t kOutThreads = 256;
 constexpr uint32_t kOutMaxSplits = 1024;
-constexpr uint32_t kOutChunk = 16;  // splits whose partials a thread holds in registers at once
+constexpr uint32_t kOutChunk = 48;  // splits whose partials a thread holds in registers at once
+constexpr size_t kOutSmem = size_t(kMlaV) * kMlaLatent * 2;  // W_UV[h]
 template <typename OT>
 __global__ void __launch_bounds__(kOutThreads, 1) mla_merge_out_kernel(const float* __restrict__ partial,
                                                                         uint32_t splits,
                                                                         const uint16_t* __restrict__ w_uv,
                                                                         OT* __restrict__ out) {
+    extern __shared__ __align__(16) unsigned char wuv_s[];  // [128 rows][512] bf16
     __shared__ float wsc[kOutMaxSplits];
     __shared__ float lsc[kOutMaxSplits];
     __shared__ __align__(16) float cs[kMlaLatent];
     __shared__ float red[kOutThreads / 32];
     const uint32_t h = blockIdx.x, b = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // W_UV rows do not depend on the earlier kernels
-    constexpr uint32_t kRowsPerWarp = kMlaV / (kOutThreads / 32);  // 16
-    uint4 wv[kRowsPerWarp][2];
-#pragma unroll
-    for (uint32_t i = 0; i < kRowsPerWarp; ++i) {
-        const uint16_t* wr =
-            w_uv + (static_cast<size_t>(h) * kMlaV + warp + i * (kOutThreads / 32)) * kMlaLatent + lane * 16;
-        wv[i][0] = __ldg(reinterpret_cast<const uint4*>(wr));
-        wv[i][1] = __ldg(reinterpret_cast<const uint4*>(wr + 8));
+    // W_UV[h] does not depend on the earlier kernels
+    {
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(w_uv + static_cast<size_t>(h) * kMlaV * kMlaLatent);
+#pragma unroll 4
+        for (uint32_t i = threadIdx.x; i < kOutSmem / 16; i += kOutThreads) cp16(wuv_s + i * 16, src + i * 16);
+        cp_commit();
     }
     pdl_wait();
     pdl_launch_dependents();
@@ -593,22 +592,27 @@ __global__ void __launch_bounds__(kOutThreads, 1) mla_merge_out_kernel(const flo
     }
     cs[threadIdx.x] = ((acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3])) * inv;
     cs[threadIdx.x + kOutThreads] = ((acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3])) * inv;
-    __syncthreads();
-    // out rows: warp w takes d = w + 8 i; lane covers 16 latent columns
+    cp_wait<0>();
+    __syncthreads();  // ctx and W_UV[h] in shared memory
+    // out rows: warp w takes d = w + 8 i; lane covers latent columns 8 lane .. +7
+    // and 256 + 8 lane .. +7 (16-byte shared reads, conflict-free)
     float cv[16];
     {
-        const float4* c4 = reinterpret_cast<const float4*>(cs + lane * 16);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 q = c4[i];
-            cv[4 * i] = q.x, cv[4 * i + 1] = q.y, cv[4 * i + 2] = q.z, cv[4 * i + 3] = q.w;
-        }
+        const float4* c0 = reinterpret_cast<const float4*>(cs + lane * 8);
+        const float4* c1 = reinterpret_cast<const float4*>(cs + kOutThreads + lane * 8);
+        const float4 a0 = c0[0], a1 = c0[1], b0 = c1[0], b1 = c1[1];
+        cv[0] = a0.x, cv[1] = a0.y, cv[2] = a0.z, cv[3] = a0.w, cv[4] = a1.x, cv[5] = a1.y, cv[6] = a1.z, cv[7] = a1.w;
+        cv[8] = b0.x, cv[9] = b0.y, cv[10] = b0.z, cv[11] = b0.w, cv[12] = b1.x, cv[13] = b1.y, cv[14] = b1.z,
+        cv[15] = b1.w;
     }
+    constexpr uint32_t kRowsPerWarp = kMlaV / (kOutThreads / 32);  // 16
 #pragma unroll
     for (uint32_t i = 0; i < kRowsPerWarp; ++i) {
         const uint32_t d = warp + i * (kOutThreads / 32);
-        const uint32_t wq[8] = {wv[i][0].x, wv[i][0].y, wv[i][0].z, wv[i][0].w,
-                                wv[i][1].x, wv[i][1].y, wv[i][1].z, wv[i][1].w};
+        const uint16_t* wr = reinterpret_cast<const uint16_t*>(wuv_s) + static_cast<size_t>(d) * kMlaLatent;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(wr + lane * 8);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(wr + kOutThreads + lane * 8);
+        const uint32_t wq[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float a = 0.f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -669,10 +673,15 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
         return e;
     if (a.splits > kOutMaxSplits) return cudaErrorInvalidValue;
     const dim3 og(kMlaHeads, a.batch);
+    if ((e = cudaFuncSetAttribute(mla_merge_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kOutSmem))) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(mla_merge_out_kernel<uint16_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kOutSmem))) != cudaSuccess)
+        return e;
     if (a.out_dtype == PBMOE_F32)
-        return launch_pdl_kernel(mla_merge_out_kernel<float>, og, dim3(kOutThreads), 0, s, a.partial, a.splits, a.w_uv,
+        return launch_pdl_kernel(mla_merge_out_kernel<float>, og, dim3(kOutThreads), kOutSmem, s, a.partial, a.splits, a.w_uv,
                                  static_cast<float*>(a.out));
-    return launch_pdl_kernel(mla_merge_out_kernel<uint16_t>, og, dim3(kOutThreads), 0, s, a.partial, a.splits, a.w_uv,
+    return launch_pdl_kernel(mla_merge_out_kernel<uint16_t>, og, dim3(kOutThreads), kOutSmem, s, a.partial, a.splits, a.w_uv,
                              static_cast<uint16_t*>(a.out));
 }
 
