@@ -228,7 +228,8 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     };
     if (!x_from_router) stage_tokens();
     pdl_wait();
-    if (x_from_router) stage_tokens();
+    // the plan first: the producer's first weight copies are then in flight
+    // while the compute warps stage tokens written by the router
     const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
     uint32_t k0, k1;
     item_run(ng * kTiles, k0, k1);
@@ -281,6 +282,7 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
         cp_async_wait_all();  // no copy of this CTA outlives it
         return;
     }
+    if (x_from_router) stage_tokens();
 
     if (warp == kWarps + 1) {
         // epilogue: lane (q = lane/4, c = lane%4) finishes route q of the
