@@ -1286,7 +1286,17 @@ def run_step(args):
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": STEP_NCU_TRAFFIC.get(dominant),
                          "traffic_source": STEP_NCU_SOURCE.get(dominant),
                          "algorithmic_bytes_per_launch": launch_bytes[dominant],
-                         "launch_ms": per_launch[dominant], "share_of_serial": tot[dominant] / serial},
+                         "launch_ms": per_launch[dominant], "share_of_serial": tot[dominant] / serial,
+                         "note": ("the call with the largest share in the per-call pass; the router is bound by "
+                                  "its serial routing replay and plan (latency), not by its 2 MB of bytes"
+                                  if dominant == "moe_router" else "the call with the largest share in the "
+                                  "per-call pass"),
+                         # the streaming calls (>= 10 MB per call) against the same peak
+                         "streaming_calls": {n: {"algorithmic_bytes_per_launch": launch_bytes[n],
+                                                 "launch_ms": per_launch[n],
+                                                 "frac": launch_bytes[n] / (per_launch[n] / 1e3) / 1e9 / peak,
+                                                 "traffic": STEP_NCU_TRAFFIC.get(n)}
+                                             for n in launch_bytes if n in per_launch and launch_bytes[n] >= 1e7}},
             "step": {"algorithmic_bytes_per_gpu": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
                      "frac_of_peak": step_bytes / (ms / 1e3) / 1e9 / peak, "unique_experts_per_layer": mean_u,
                      "kernel_ms_per_step": {n: round(v, 4) for n, v in sorted(tot.items(), key=lambda kv: -kv[1])},
@@ -1308,11 +1318,11 @@ def run_step(args):
 # the caches before each profiled kernel, so reads that hit L2 in a replayed
 # step, e.g. the MLA split partials, count here)
 STEP_NCU_TRAFFIC: dict = {
-    "mla_decode": (2.230272 + 75.826176 + 2.808832 + 11.858176) * 1e6,  # absorb, attention (+ partials written), merge
+    "mla_decode": (2.218496 + 75.826176 + 2.808832 + 11.866368) * 1e6,  # absorb, attention (+ partials written), merge
     "moe_router": 2.26e6,
     "moe_gate_up": (73.21 + 2.15) * 1e6,
     "moe_down": (36.80 + 0.13) * 1e6,
-    "q_a+kv_a": 2.52e6,
+    "q_a+kv_a": 2.526464e6,
     "q_b": 2.74432e6,
 }
 _STEP_NCU_CMD = ("ncu --set full --clock-control none -k regex:<kernel> -s <n> -c 1 python bench.py --workload step "
