@@ -659,6 +659,23 @@ PBMOE_API int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* conf
                                     const uint32_t* positions, uint16_t* const* c_kv, uint16_t* const* k_rope,
                                     uint32_t cache_len, void* stream);
 
+/* pbmoe_mla_rope_append followed by pbmoe_mla_decode on the same tokens, in
+ * one launch fewer: the RoPE rotation and the cache append run inside the
+ * decode's first kernel (the query absorb), so a decode step's chain
+ * (runtime/mod.rs:2896-2913 then resident_glm_mla_absorbed_attention,
+ * runtime/mod.rs:1327-1403) loses one dependent launch. Same results as the
+ * two calls: args->query (f32 only) is rotated in place, the latent and key
+ * rows are written at each token's position (kv, latent_norm_weight,
+ * epsilon, positions, c_kv_rows, k_rope_rows, cache_len as in
+ * pbmoe_mla_rope_append; c_kv_rows / k_rope_rows are its DEVICE arrays of
+ * cache row pointers, args->c_kv / args->k_rope the HOST arrays of the same
+ * caches), then the attention reads every sequence's args->seq_lens rows,
+ * the appended one included. */
+PBMOE_API int pbmoe_mla_append_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* config, const pbmoe_mla_args* args,
+                                      const float* kv, const float* latent_norm_weight, float epsilon,
+                                      const uint32_t* positions, uint16_t* const* c_kv_rows,
+                                      uint16_t* const* k_rope_rows, uint32_t cache_len, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

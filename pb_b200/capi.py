@@ -46,7 +46,7 @@ EXPORTED = [
     "pbmoe_prefill_reserve", "pbmoe_q4_gemm", "pbmoe_prefill_group_plan", "pbmoe_q4_gemm_grouped",
     "pbmoe_ep_expert_range", "pbmoe_ep_reserve", "pbmoe_ep_ipc_handle", "pbmoe_ep_open_peers", "pbmoe_ep_set_peers",
     "pbmoe_ep_buffer", "pbmoe_ep_moe_layer", "pbmoe_head_reserve", "pbmoe_head_topk", "pbmoe_head_merge",
-    "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_expert_layer_read",
+    "pbmoe_rms_norm", "pbmoe_rope_reserve", "pbmoe_mla_rope_append", "pbmoe_mla_append_decode", "pbmoe_expert_layer_read",
     "pbmoe_expert_layer_load", "pbmoe_mxfp4_matvec", "pbmoe_moe_layer_host", "pbmoe_sync",
     "pbmoe_fixed_mxfp4_layout", "pbmoe_q4_matvec_fused", "pbmoe_q4_matvec_batch", "pbmoe_route_sigmoid_noaux",
 ]
@@ -185,6 +185,8 @@ def load():
         L.pbmoe_rope_reserve.argtypes = [vp, u32, u32, C.c_double]
         L.pbmoe_mla_rope_append.argtypes = [vp, C.POINTER(MlaConfig), u32, vp, vp, vp, C.c_float, vp, vp, vp, u32,
                                              vp]
+        L.pbmoe_mla_append_decode.argtypes = [vp, C.POINTER(MlaConfig), C.POINTER(MlaArgs), vp, vp, C.c_float, vp,
+                                               vp, vp, u32, vp]
         L.pbmoe_q4_matvec_fused.argtypes = [vp, C.POINTER(Q4FusedArgs), vp]
         L.pbmoe_q4_matvec_batch.argtypes = [vp, C.POINTER(Q4Tensor), u32, vp, C.c_int, C.POINTER(vp), C.c_int, u32,
                                             vp]
@@ -372,6 +374,21 @@ class Context:
 
     def rope_reserve(self, max_positions, rope_dim, theta=10000.0):
         self.check(self.lib.pbmoe_rope_reserve(self.h, max_positions, rope_dim, theta))
+
+    def mla_append_decode(self, config, query, kv, positions, c_kv_ptrs, k_rope_ptrs, cache_len, c_kv, k_rope, w_uk,
+                          w_uv, out, latent_norm=None, eps=1e-6, stream=None):
+        """mla_rope_append followed by mla_decode in one call (pbmoe_mla_append_decode): query f32 [B, heads,
+        nope+rope] rotated in place; kv, positions, c_kv_ptrs, k_rope_ptrs, cache_len, latent_norm as for
+        mla_rope_append; c_kv / k_rope lists of B device tensors (the attended rows) as for mla_decode."""
+        b = len(c_kv)
+        lens = (C.c_uint32 * b)(*[int(t.shape[0]) for t in c_kv])
+        ckv = (C.c_void_p * b)(*[t.data_ptr() for t in c_kv])
+        kr = (C.c_void_p * b)(*[t.data_ptr() for t in k_rope])
+        args = MlaArgs(b, C.cast(lens, C.c_void_p), query.data_ptr(), _dtype_code(query), C.cast(ckv, C.c_void_p),
+                       C.cast(kr, C.c_void_p), w_uk.data_ptr(), w_uv.data_ptr(), out.data_ptr(), _dtype_code(out))
+        self.check(self.lib.pbmoe_mla_append_decode(self.h, C.byref(config), C.byref(args), _ptr(kv), _ptr(latent_norm),
+                                                    eps, _ptr(positions), _ptr(c_kv_ptrs), _ptr(k_rope_ptrs),
+                                                    cache_len, self.stream_ptr(stream)))
 
     def mla_rope_append(self, config, query, kv, positions, c_kv_ptrs, k_rope_ptrs, cache_len, latent_norm=None,
                         eps=1e-6, stream=None):

@@ -790,7 +790,56 @@ int pbmoe_mla_reserve(pbmoe_ctx* ctx, const pbmoe_mla_config* c, uint32_t max_ba
     return PBMOE_OK;
 }
 
+namespace {
+int mla_decode_impl(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_args* a,
+                    const pbmoe::RopeAppendArgs* rope, void* stream);
+}  // namespace
+
 int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_args* a, void* stream) {
+    return mla_decode_impl(ctx, c, a, nullptr, stream);
+}
+
+int pbmoe_mla_append_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_args* a, const float* kv,
+                            const float* latent_norm_weight, float epsilon, const uint32_t* positions,
+                            uint16_t* const* c_kv_rows, uint16_t* const* k_rope_rows, uint32_t cache_len,
+                            void* stream) {
+    if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
+    if (!c || !a || !kv || !positions || !c_kv_rows || !k_rope_rows)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla append + decode: null pointer");
+    if (a->query_dtype != PBMOE_F32)
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla append + decode: the query must be f32 (rotated in place)");
+    if (latent_norm_weight && (!(epsilon >= 0.f) || !std::isfinite(epsilon)))
+        return fail(ctx, PBMOE_ERR_INVALID_ARGUMENT, "mla append + decode: norm epsilon must be finite and >= 0");
+    if (!ctx->rope_table || ctx->rope_dim != c->rope_dim)
+        return fail(ctx, PBMOE_ERR_NO_WORKSPACE, "mla append + decode: rope dim %u needs pbmoe_rope_reserve",
+                    c->rope_dim);
+    if (!pbmoe::rope_append_supported(c->heads, c->rope_dim) || c->latent_dim == 0 ||
+        c->latent_dim > 4 * 256 || cache_len == 0)
+        return fail(ctx, PBMOE_ERR_UNSUPPORTED, "FlashMoe unsupported MLA RoPE append: %u heads x rope %u, latent %u",
+                    c->heads, c->rope_dim, c->latent_dim);
+    pbmoe::RopeAppendArgs r{};
+    r.batch = a->batch;
+    r.heads = c->heads;
+    r.nope = c->nope_dim;
+    r.rope = c->rope_dim;
+    r.latent = c->latent_dim;
+    r.query = static_cast<float*>(const_cast<void*>(a->query));
+    r.kv = kv;
+    r.latent_norm_w = latent_norm_weight;
+    r.eps = epsilon;
+    r.positions = positions;
+    r.c_kv = c_kv_rows;
+    r.k_rope = k_rope_rows;
+    r.cache_len = cache_len;
+    r.table = ctx->rope_table;
+    r.max_positions = ctx->rope_positions;
+    r.status = ctx->status;
+    return mla_decode_impl(ctx, c, a, &r, stream);
+}
+
+namespace {
+int mla_decode_impl(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_args* a,
+                    const pbmoe::RopeAppendArgs* rope, void* stream) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;
     int rc = check_mla_config(ctx, c);
     if (rc) return rc;
@@ -833,6 +882,7 @@ int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_
     L.qp = reinterpret_cast<float*>(base);
     L.partial = reinterpret_cast<float*>(base + w.qp);
     L.ctx = reinterpret_cast<float*>(base + w.qp + w.partial);
+    L.rope = rope;
     pbmoe::mla_plan_splits(L, sm_count(ctx), L.split_tokens, L.splits);
     DeviceGuard g(ctx->device);
     if (!g.ok) return fail(ctx, PBMOE_ERR_CUDA, "cannot select device %d", ctx->device);
@@ -840,6 +890,7 @@ int pbmoe_mla_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* c, const pbmoe_mla_
     if (e != cudaSuccess) return cuda_fail(ctx, e, "MLA decode launch");
     return PBMOE_OK;
 }
+}  // namespace
 
 int pbmoe_prefill_reserve(pbmoe_ctx* ctx, uint32_t max_rows, uint32_t max_cols) {
     if (!ctx) return PBMOE_ERR_INVALID_ARGUMENT;

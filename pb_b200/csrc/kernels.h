@@ -215,6 +215,7 @@ struct MlaLaunch {
     float* partial;  // [batch x splits x 16 x 514] per-split (max, sum, O)
     float* ctx;      // [batch x 16 x 512]
     uint32_t split_tokens, splits;
+    const struct RopeAppendArgs* rope;  // non-null: the RoPE + cache append done by the absorb launch (f32 q)
 };
 
 bool mla_shape_supported(uint32_t heads, uint32_t rope, uint32_t latent, uint32_t v_dim);

@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "rope.cuh"
 
 namespace pbmoe {
 
@@ -105,14 +106,32 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // cb add theirs with shuffles, the 8 warps theirs in shared memory. Writes
 // Q'[b][h][0..511] = q_lat * k and Q'[b][h][512..575] = q_rope * k,
 // k = scale * log2(e). nope <= 128 (host-checked).
+//
+// kRope (f32 queries): the call also does the RoPE + cache append of
+// mla_rope_append_kernel on the way. The first column block's rope threads
+// rotate each sequence's rope part of head h in place (as that kernel does) and
+// scale the rotated values into Q'; grid rows past latent/64 append the key
+// and latent rows, one token per CTA (rope_append_kv). A token whose position
+// is past its cache or the RoPE table is left unrotated and unwritten, with
+// PBMOE_DEV_ERR_POSITION latched.
 constexpr uint32_t kAbsorbMaxNope = 128;
-template <typename QT>
+template <typename QT, bool kRope = false>
 __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ q, uint32_t batch, uint32_t nope,
                                                          const uint16_t* __restrict__ w_uk, float k,
-                                                         float* __restrict__ qp) {
+                                                         float* __restrict__ qp, RopeAppendArgs ra) {
     __shared__ float qs[kMlaMaxBatch * kAbsorbMaxNope];
     __shared__ float red[8][8][64];  // [warp][sequence of the pass][column]
     const uint32_t h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if constexpr (kRope) {
+        if (blockIdx.y >= kMlaLatent / 64) {  // the cache append of token (row - 8) * 16 + h
+            pdl_wait();
+            pdl_launch_dependents();
+            const uint32_t b = (blockIdx.y - kMlaLatent / 64) * kMlaHeads + blockIdx.x;
+            uint32_t pos;
+            if (b < batch && rope_token_position(ra, b, pos)) rope_append_kv(ra, b, pos, &red[0][0][0]);
+            return;
+        }
+    }
     const uint32_t cb = tid & 7, rg = tid >> 3;
     const uint32_t qdim = nope + kMlaRope;
     // W_UK does not depend on the earlier kernels: its loads are issued before
@@ -146,15 +165,55 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
         }
     }
     if (rope_cta) {
-        for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
-            float rv[8];
+        if constexpr (kRope) {
+            // thread tid writes split-half element tid of head h's rope part: from
+            // pair p = tid % 32, cos/sin of the token's position
+            float* qf = reinterpret_cast<float*>(const_cast<QT*>(q));
+            const uint32_t p = tid & 31u, half = kMlaRope / 2;
+            for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
+                float x0[8], x1[8], xs[8];
+                float2 c[8];
+                bool ok[8];
 #pragma unroll
-            for (uint32_t j = 0; j < 8; ++j)
-                rv[j] = b0 + j < batch ? load_act(q, (static_cast<size_t>(b0 + j) * kMlaHeads + h) * qdim + nope + tid)
-                                       : 0.f;
+                for (uint32_t j = 0; j < 8; ++j) {
+                    const uint32_t b = b0 + j;
+                    ok[j] = false;
+                    x0[j] = x1[j] = xs[j] = 0.f;
+                    c[j] = make_float2(0.f, 0.f);
+                    if (b < batch) {
+                        const float* qr = qf + (static_cast<size_t>(b) * kMlaHeads + h) * qdim + nope;
+                        const uint32_t pos = ra.positions[b];
+                        ok[j] = pos < ra.max_positions && pos < ra.cache_len;
+                        x0[j] = qr[2 * p];
+                        x1[j] = qr[2 * p + 1];
+                        xs[j] = qr[tid];
+                        if (ok[j]) c[j] = ra.table[static_cast<size_t>(pos) * half + p];
+                    }
+                }
+                asm volatile("bar.sync 1, 64;" ::: "memory");  // the 64 rope threads: every read before any write
 #pragma unroll
-            for (uint32_t j = 0; j < 8; ++j)
-                if (b0 + j < batch) qp[(static_cast<size_t>(b0 + j) * kMlaHeads + h) * kMlaK + kMlaLatent + tid] = rv[j] * k;
+                for (uint32_t j = 0; j < 8; ++j) {
+                    const uint32_t b = b0 + j;
+                    if (b < batch) {
+                        const float r = !ok[j] ? xs[j]
+                                        : tid < half ? __fsub_rn(__fmul_rn(x0[j], c[j].x), __fmul_rn(x1[j], c[j].y))
+                                                     : __fadd_rn(__fmul_rn(x1[j], c[j].x), __fmul_rn(x0[j], c[j].y));
+                        if (ok[j]) qf[(static_cast<size_t>(b) * kMlaHeads + h) * qdim + nope + tid] = r;
+                        qp[(static_cast<size_t>(b) * kMlaHeads + h) * kMlaK + kMlaLatent + tid] = r * k;
+                    }
+                }
+            }
+        } else {
+            for (uint32_t b0 = 0; b0 < batch; b0 += 8) {
+                float rv[8];
+#pragma unroll
+                for (uint32_t j = 0; j < 8; ++j)
+                    rv[j] = b0 + j < batch ? load_act(q, (static_cast<size_t>(b0 + j) * kMlaHeads + h) * qdim + nope + tid)
+                                           : 0.f;
+#pragma unroll
+                for (uint32_t j = 0; j < 8; ++j)
+                    if (b0 + j < batch) qp[(static_cast<size_t>(b0 + j) * kMlaHeads + h) * kMlaK + kMlaLatent + tid] = rv[j] * k;
+            }
         }
     }
     __syncthreads();
@@ -656,13 +715,18 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     const float k = a.scale * 1.4426950408889634f;  // scores in base 2
     cudaError_t e;
     {
-        const dim3 grid(kMlaHeads, kMlaLatent / 64);
-        if (a.q_dtype == PBMOE_F32)
-            e = launch_pdl_kernel(mla_absorb_kernel<float>, grid, dim3(256), 0, s, static_cast<const float*>(a.q),
-                                  a.batch, a.nope, a.w_uk, k, a.qp);
-        else
-            e = launch_pdl_kernel(mla_absorb_kernel<uint16_t>, grid, dim3(256), 0, s,
-                                  static_cast<const uint16_t*>(a.q), a.batch, a.nope, a.w_uk, k, a.qp);
+        const RopeAppendArgs ra = a.rope ? *a.rope : RopeAppendArgs{};
+        if (a.rope) {  // f32 query (host-checked); append CTAs: ceil(batch / 16) more grid rows
+            const dim3 grid(kMlaHeads, kMlaLatent / 64 + (a.batch + kMlaHeads - 1) / kMlaHeads);
+            e = launch_pdl_kernel(mla_absorb_kernel<float, true>, grid, dim3(256), 0, s, static_cast<const float*>(a.q),
+                                  a.batch, a.nope, a.w_uk, k, a.qp, ra);
+        } else if (a.q_dtype == PBMOE_F32) {
+            e = launch_pdl_kernel(mla_absorb_kernel<float>, dim3(kMlaHeads, kMlaLatent / 64), dim3(256), 0, s,
+                                  static_cast<const float*>(a.q), a.batch, a.nope, a.w_uk, k, a.qp, ra);
+        } else {
+            e = launch_pdl_kernel(mla_absorb_kernel<uint16_t>, dim3(kMlaHeads, kMlaLatent / 64), dim3(256), 0, s,
+                                  static_cast<const uint16_t*>(a.q), a.batch, a.nope, a.w_uk, k, a.qp, ra);
+        }
         if (e != cudaSuccess) return e;
     }
     if ((e = cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

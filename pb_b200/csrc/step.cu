@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "rope.cuh"
 
 namespace pbmoe {
 
@@ -77,25 +78,21 @@ cudaError_t rms_norm_launch(const NormArgs& a, cudaStream_t s) {
 constexpr int kRopeThreads = 256;
 constexpr uint32_t kRopeMaxPairs = 2048;  // heads x rope/2 rotated per token
 
-// Every load of a thread (query pairs, cos/sin, the key's rope pair, its
-// latent values and their norm weights) is issued once the token's position
-// is known, before any is used: two dependent round trips per token.
-constexpr uint32_t kRopeMaxLatent = 4 * kRopeThreads;
+// The query pairs of every head rotated in place (all of a thread's pairs
+// read before any is written), then the key and latent rows appended
+// (rope_append_kv, rope.cuh).
+constexpr uint32_t kRopeMaxLatent = kRopeMaxLatentPerThread * kRopeThreads;
 __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppendArgs a) {
+    __shared__ float red[kRopeThreads / 32];
     pdl_wait();
     pdl_launch_dependents();
     const uint32_t b = blockIdx.x;
-    const uint32_t pos = a.positions[b];
-    if (pos >= a.max_positions || pos >= a.cache_len) {
-        if (threadIdx.x == 0 && a.status) atomicOr(a.status, PBMOE_DEV_ERR_POSITION);
-        return;
-    }
+    uint32_t pos;
+    if (!rope_token_position(a, b, pos)) return;
     const uint32_t half = a.rope / 2, qk = a.nope + a.rope;
     const float2* cs = a.table + static_cast<size_t>(pos) * half;
     float* q = a.query + static_cast<size_t>(b) * a.heads * qk;
-    const float* kv = a.kv + static_cast<size_t>(b) * (a.latent + a.rope);
     constexpr int kPer = kRopeMaxPairs / kRopeThreads;
-    constexpr int kLat = kRopeMaxLatent / kRopeThreads;
     float va[kPer], vb[kPer];
     float2 tq[kPer];
     const uint32_t pairs = a.heads * half;
@@ -109,23 +106,7 @@ __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppen
             tq[j] = cs[p];  // (cos, sin)
         }
     }
-    const bool key_lane = threadIdx.x < half;
-    float k0 = 0.f, k1 = 0.f;
-    float2 tk = make_float2(0.f, 0.f);
-    if (key_lane) {
-        k0 = kv[a.latent + 2 * threadIdx.x];
-        k1 = kv[a.latent + 2 * threadIdx.x + 1];
-        tk = cs[threadIdx.x];
-    }
-    float lv[kLat], nw[kLat];
-#pragma unroll
-    for (int j = 0; j < kLat; ++j) {
-        const uint32_t i = threadIdx.x + j * kRopeThreads;
-        lv[j] = i < a.latent ? kv[i] : 0.f;
-        nw[j] = (i < a.latent && a.latent_norm_w) ? a.latent_norm_w[i] : 1.0f;
-    }
     __syncthreads();  // every query pair read before the split halves are written
-    // query: the rotated halves of every head
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
         const uint32_t i = threadIdx.x + j * kRopeThreads;
@@ -135,33 +116,7 @@ __global__ void __launch_bounds__(kRopeThreads) mla_rope_append_kernel(RopeAppen
             q[h * qk + a.nope + half + p] = __fadd_rn(__fmul_rn(vb[j], tq[j].x), __fmul_rn(va[j], tq[j].y));
         }
     }
-    // key: the rope part after the latent, rotated into the cache row
-    if (key_lane) {
-        uint16_t* krow = a.k_rope[b] + static_cast<size_t>(pos) * a.rope;
-        krow[threadIdx.x] = f32_to_bf16_bits(__fsub_rn(__fmul_rn(k0, tk.x), __fmul_rn(k1, tk.y)));
-        krow[half + threadIdx.x] = f32_to_bf16_bits(__fadd_rn(__fmul_rn(k1, tk.x), __fmul_rn(k0, tk.y)));
-    }
-    // latent row, normalised here when the norm is fused (rms_norm_rows_kernel's
-    // formula; the sum of squares in the same per-thread order as a strided loop)
-    float scale = 1.0f;
-    if (a.latent_norm_w) {
-        __shared__ float red[kRopeThreads / 32];
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < kLat; ++j) ss += lv[j] * lv[j];
-        ss = warp_sum(ss);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-        __syncthreads();
-        float tot = 0.f;
-        for (int w = 0; w < kRopeThreads / 32; ++w) tot += red[w];
-        scale = 1.0f / sqrtf(tot / static_cast<float>(a.latent) + a.eps);
-    }
-    uint16_t* crow = a.c_kv[b] + static_cast<size_t>(pos) * a.latent;
-#pragma unroll
-    for (int j = 0; j < kLat; ++j) {
-        const uint32_t i = threadIdx.x + j * kRopeThreads;
-        if (i < a.latent) crow[i] = f32_to_bf16_bits(a.latent_norm_w ? lv[j] * scale * nw[j] : lv[j]);
-    }
+    rope_append_kv(a, b, pos, red);
 }
 
 bool rope_append_supported(uint32_t heads, uint32_t rope) {

@@ -11,9 +11,9 @@ Per layer, with the GLM MLA attention of mla_attention_output_values
 
   qa, kv = Q4(q_a_proj) xn, Q4(kv_a_proj_with_mqa) xn            pbmoe_q4_matvec_fused (2 matrices)
   q      = Q4(q_b_proj) rms_norm(qa) w_qa                         pbmoe_q4_matvec_fused (input norm)
-  RoPE on q's and kv's rope parts; rms_norm(kv[:latent]) w_kv
-  and the rotated key written into the caches                     pbmoe_mla_rope_append (latent norm)
-  attn   = absorbed MLA attention over the cache                  pbmoe_mla_decode
+  RoPE on q's and kv's rope parts; rms_norm(kv[:latent]) w_kv,
+  the rotated key written into the caches, then
+  attn   = absorbed MLA attention over the cache                  pbmoe_mla_append_decode (latent norm)
   h      = x + Q4(o_proj) attn                                    pbmoe_q4_matvec_fused (residual)
   x      = h + MoE(rms_norm(h) w_post), xn = rms_norm(x) w_in'    pbmoe_moe_layer (input norm, next norm)
 
@@ -239,14 +239,12 @@ class DecodeStep:
                 record.setdefault("qa", []).append(self.qa.clone())
                 record.setdefault("kv", []).append(self.kv.clone())
                 record.setdefault("q_prerope", []).append(self.q.clone())
-            mk("rope_append")
-            ctx.mla_rope_append(self.mla_cfg, self.q, self.kv, self.positions, self.caches.c_kv_ptrs[i],
-                                self.caches.k_rope_ptrs[i], cfg.context, latent_norm=L.kv_a_norm, eps=cfg.eps,
-                                stream=stream)
-            mk("mla_decode")
-            ctx.mla_decode(self.mla_cfg, self.q, [t[:n] for t, n in zip(self.caches.c_kv[i], seq_lens)],
-                           [t[:n] for t, n in zip(self.caches.k_rope[i], seq_lens)], L.w_uk, L.w_uv, self.attn,
-                           stream=stream)
+            mk("mla_decode")  # the RoPE + cache append runs inside the decode's first kernel
+            ctx.mla_append_decode(self.mla_cfg, self.q, self.kv, self.positions, self.caches.c_kv_ptrs[i],
+                                  self.caches.k_rope_ptrs[i], cfg.context,
+                                  [t[:n] for t, n in zip(self.caches.c_kv[i], seq_lens)],
+                                  [t[:n] for t, n in zip(self.caches.k_rope[i], seq_lens)], L.w_uk, L.w_uv, self.attn,
+                                  latent_norm=L.kv_a_norm, eps=cfg.eps, stream=stream)
             mk("o_proj")
             ctx.q4_fused([L.o_proj.mat()], self.attn.view(self.B, -1), [self.h], residual=self.x, stream=stream)
             if record is not None:
@@ -311,10 +309,11 @@ class DecodeStep:
 
     def launches_per_step(self):
         """CUDA kernels one step launches: the input norm; per layer 2 fused
-        projection launches, RoPE/append, 4 MLA kernels, the o_proj launch and
-        4 MoE kernels per 8-token chunk; the head's 3 (plus a memset)."""
+        projection launches, 3 MLA kernels (the first also doing RoPE and the
+        cache append), the o_proj launch and 4 MoE kernels per 8-token chunk;
+        the head's 3 (plus a memset)."""
         chunks = (self.B + 7) // 8
-        return 1 + self.cfg.layers * (2 + 1 + 4 + 1 + 4 * chunks) + 3
+        return 1 + self.cfg.layers * (2 + 3 + 1 + 4 * chunks) + 3
 
     def unique_experts(self):
         """Distinct routed experts per layer in the recorded routes (mean over layers)."""

@@ -5,7 +5,9 @@
                          (math.rs:151-167), with the fused residual add
   pbmoe_mla_rope_append  apply_rotary_interleaved_to_split_half (math.rs:
                          822-846) on the query and key rope parts, bit-exact,
-                         and the cache rows of KvCache::record_mla_kv
+                         and the cache rows of KvCache::record_mla_kv;
+                         pbmoe_mla_append_decode bit-identical to it followed
+                         by pbmoe_mla_decode
   DecodeStep             two layers of MLA attention + MoE and the vocab head,
                          chained from the oracle's functions in the same order
                          (runtime/mod.rs:1432-2024, 2779-2940); hidden state
@@ -151,6 +153,68 @@ def test_mla_rope_append_latent_norm(ctx, oracle):
         assert_close(_f32_of_bf16(ckv[b][pos[b]]), ref, tol=8e-3, what="normed latent row")
         kref = oracle.rope_interleaved_to_split_half(kv0[b, 512:], pos[b], 64, 10000.0)
         assert np.array_equal(_f32_of_bf16(kr[b][pos[b]]), oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(kref)))
+
+
+@pytest.mark.parametrize("batch", [1, 8, 20])
+def test_mla_append_decode_matches_separate_calls(ctx, batch):
+    """pbmoe_mla_append_decode (the RoPE + cache append inside the decode's
+    first kernel) against pbmoe_mla_rope_append then pbmoe_mla_decode on
+    copies of the same inputs: rotated query, cache rows and attention output
+    bit-identical; with batch 20 the append runs on two extra grid rows, and
+    one token's position lies past its cache (nothing rotated or written for
+    it, the position error latched by both forms)."""
+    import torch
+
+    from pb_b200 import capi, synth
+
+    cfg = capi.mla_config()
+    ctxlen = 300
+    ctx.rope_reserve(ctxlen, 64, 10000.0)
+    ctx.mla_reserve(cfg, 32)
+    g = torch.Generator("cuda").manual_seed(60 + batch)
+    q = torch.randn(batch, 16, 192, generator=g, device="cuda")
+    kv = torch.randn(batch, 576, generator=g, device="cuda")
+    w = (1 + 0.1 * torch.randn(512, generator=g, device="cuda")).float()
+    w_uk = synth.normal_bf16((16, 128, 512), 0.02, synth.gen("cuda", 70), "cuda")
+    w_uv = synth.normal_bf16((16, 128, 512), 0.02, synth.gen("cuda", 71), "cuda")
+    pos = [(37 * b + 11) % ctxlen for b in range(batch)]
+    bad = batch == 20
+    if bad:
+        pos[13] = ctxlen  # past the cache
+    lens = [min(p + 1, ctxlen) for p in pos]
+
+    def caches(seed):
+        ckv = [synth.normal_bf16((ctxlen, 512), 1.0, synth.gen("cuda", seed + b), "cuda") for b in range(batch)]
+        kr = [synth.normal_bf16((ctxlen, 64), 1.0, synth.gen("cuda", seed + 100 + b), "cuda") for b in range(batch)]
+        return ckv, kr
+
+    ptr = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+    positions = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    # separate calls
+    q1, kv1 = q.clone(), kv.clone()
+    ckv1, kr1 = caches(200)
+    out1 = torch.empty(batch, 16, 128, device="cuda")
+    ctx.device_status(clear=True)
+    ctx.mla_rope_append(cfg, q1, kv1, positions, ptr(ckv1), ptr(kr1), ctxlen, latent_norm=w, eps=1e-6)
+    ctx.mla_decode(cfg, q1, [t[:n] for t, n in zip(ckv1, lens)], [t[:n] for t, n in zip(kr1, lens)], w_uk, w_uv,
+                   out1)
+    torch.cuda.synchronize()
+    st1 = ctx.device_status(clear=True)
+    # one call
+    q2, kv2 = q.clone(), kv.clone()
+    ckv2, kr2 = caches(200)
+    out2 = torch.empty(batch, 16, 128, device="cuda")
+    ctx.mla_append_decode(cfg, q2, kv2, positions, ptr(ckv2), ptr(kr2), ctxlen,
+                          [t[:n] for t, n in zip(ckv2, lens)], [t[:n] for t, n in zip(kr2, lens)], w_uk, w_uv, out2,
+                          latent_norm=w, eps=1e-6)
+    torch.cuda.synchronize()
+    st2 = ctx.device_status(clear=True)
+    assert st1 == st2
+    assert bool(st1 & capi.PBMOE_DEV_ERR_POSITION) == bad
+    assert torch.equal(q1, q2), "rotated query differs"
+    for b in range(batch):
+        assert torch.equal(ckv1[b], ckv2[b]) and torch.equal(kr1[b], kr2[b]), f"cache rows differ (b{b})"
+    assert torch.equal(out1, out2), "attention output differs"
 
 
 @pytest.mark.parametrize("batch", [1, 2, 8, 11])
