@@ -319,11 +319,11 @@ PBMOE_API int pbmoe_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config, co
  * the process exits; a call fits when 256 + pbmoe_moe_workspace_bytes(tokens,
  * config) <= PBMOE_STATIC_SCRATCH_BYTES (at most 29 tokens at hidden 2048 /
  * 512 experts / top-10 / intermediate 512), larger calls return
- * PBMOE_ERR_UNSUPPORTED. Up to 8 tokens it launches exactly pbmoe_moe_layer's
- * kernels; larger calls run as one launch (pbmoe_moe_layer runs them as
- * 8-token chunks). The array's device address is looked up on the first call
- * on each device (the calling thread's current device): make that first call
- * before any stream capture. All calls share the array: calls that may
+ * PBMOE_ERR_UNSUPPORTED. It launches exactly pbmoe_moe_layer's kernels (one
+ * launch for up to 32 tokens, which is every call that fits). The array's
+ * device address is looked up on the first call on each device (the calling
+ * thread's current device): make that first call before any stream capture.
+ * All calls share the array: calls that may
  * overlap on the GPU race and must be serialised by the caller.
  * device_status (nullable, device u32) receives PBMOE_DEV_ERR_* bits; when it
  * is NULL the bits land in the shared array, which the next call clears, so

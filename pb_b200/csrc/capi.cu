@@ -180,7 +180,7 @@ int moe_check_config(const pbmoe_moe_config* c, char* msg, size_t len) {
 MoeWsSizes moe_ws_sizes(uint32_t T, uint32_t E, uint32_t K, uint32_t H, uint32_t I) {
     MoeWsSizes s{};
     const size_t R = size_t(T) * K + T;
-    const size_t gmax = size_t(T) * K + 1;
+    const size_t gmax = size_t(T) * K + T;  // routed groups of at most 8 routes + the shared expert's
     size_t* b = s.bytes;
     b[0] = 0;                    // status lives in the context
     b[1] = 8;                    // ticket[2]
@@ -634,18 +634,23 @@ int moe_layer_impl(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_moe_we
     a.expert_count = e_count;
     a.ep = ep;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // Batches above 8 tokens run as consecutive chunks of 8 through the
-    // pipelined expert kernels when those take the layout: every token's
-    // routing, combine and norm are its own, so the chunks compute exactly
-    // what the 8-token layer computes for those tokens. (Not with phase events,
-    // which time one launch, nor with expert parallelism, whose exchange
-    // buffers hold one launch's tokens.)
+    // Batches above 32 tokens run as consecutive chunks of 32 through the
+    // pipelined expert kernels when those take the layout (chunks of 8 when
+    // only the 8-token form does): every token's routing, combine and norm
+    // are its own, so the chunks compute exactly what one launch computes for
+    // those tokens. (Not with phase events, which time one launch, nor with
+    // expert parallelism, whose exchange buffers hold one launch's tokens.)
     uint32_t chunk = tokens;
     if (tokens > 8 && !ep && !a.phase_events) {
         MoeLaunch probe = a;
-        probe.tokens = 8;
         if (a.in_norm_w) probe.x_dtype = PBMOE_BF16;  // the experts read the normalised bf16 rows
-        if (pbmoe::moe_pipe_supported(probe)) chunk = 8;
+        probe.tokens = tokens < 32 ? tokens : 32;
+        if (pbmoe::moe_pipe_supported(probe)) {
+            chunk = 32;
+        } else {
+            probe.tokens = 8;
+            if (pbmoe::moe_pipe_supported(probe)) chunk = 8;
+        }
     }
     const size_t xs = x_dtype == PBMOE_BF16 ? 2 : 4, os = out_dtype == PBMOE_BF16 ? 2 : 4;
     for (uint32_t c0 = 0; c0 < tokens; c0 += chunk) {

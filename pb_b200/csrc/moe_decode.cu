@@ -312,9 +312,13 @@ __device__ __noinline__ void plan_warp(uint32_t T, uint32_t K, uint32_t E, uint3
 }
 
 // The same plan by the whole CTA, for any number of routes: per-expert counts
-// and two block scans, ranks inside each expert from __match_any_sync.
+// and two block scans, ranks inside each expert from __match_any_sync. With
+// max_group = m > 0 an expert's routes (and the shared expert's T) form
+// ceil(count / m) consecutive groups of at most m routes each, in the same
+// grouped positions: the pipelined expert kernels take at most 8 routes per
+// group as their MMA's N operand.
 __device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint32_t e_lo, uint32_t e_hi,
-                                        bool has_shared, const MoeWs& ws, uint32_t* smem) {
+                                        bool has_shared, uint32_t max_group, const MoeWs& ws, uint32_t* smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t* cnt = smem;             // [E] counts -> starts
     uint32_t* gidx = cnt + E;         // [E] used flags -> group index
@@ -333,7 +337,8 @@ __device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint
         if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e], 1u);
     }
     __syncthreads();
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) gidx[e] = cnt[e] ? 1u : 0u;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x)
+        gidx[e] = max_group ? (cnt[e] + max_group - 1) / max_group : (cnt[e] ? 1u : 0u);
     __syncthreads();
     const uint32_t U = block_exclusive_scan(gidx, E, tmp);
     const uint32_t RL = block_exclusive_scan(cnt, E, tmp);  // cnt[e] = start of expert e; RL local routes
@@ -354,8 +359,9 @@ __device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint
         }
     }
     __syncthreads();
-    const uint32_t shared_groups = has_shared ? 1u : 0u;
-    const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared group
+    const uint32_t mg = max_group ? max_group : 0xffffffffu;
+    const uint32_t shared_groups = !has_shared ? 0u : max_group ? (T + max_group - 1) / max_group : 1u;
+    const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared groups
     for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
         const uint32_t e = ids[r];
         if (e < e_lo || e >= e_hi) continue;
@@ -363,12 +369,13 @@ __device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint
         const uint32_t pos = routed_base + cnt[e] + rank;
         ws.group_routes[pos] = r;
         ws.group_tokens[pos] = r / K;
-        if (rank == 0) {
-            // exclusive-scan property: the group's size is the next start minus this one
-            const uint32_t g = shared_groups + gidx[e];
+        if (rank % mg == 0) {
+            // exclusive-scan property: the expert's size is the next start minus this one
+            const uint32_t total = (e + 1 < E ? cnt[e + 1] : RL) - cnt[e];
+            const uint32_t g = shared_groups + gidx[e] + rank / mg;
             ws.group_expert[g] = e - e_lo;
-            ws.group_start[g] = routed_base + cnt[e];
-            ws.group_count[g] = (e + 1 < E ? cnt[e + 1] : RL) - cnt[e];
+            ws.group_start[g] = pos;
+            ws.group_count[g] = min(total - rank, mg);
         }
     }
     if (has_shared) {
@@ -376,10 +383,10 @@ __device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint
             ws.group_routes[t] = R + t;
             ws.group_tokens[t] = t;
         }
-        if (threadIdx.x == 0) {
-            ws.group_expert[0] = E;
-            ws.group_start[0] = 0;
-            ws.group_count[0] = T;
+        for (uint32_t j = threadIdx.x; j < shared_groups; j += blockDim.x) {
+            ws.group_expert[j] = E;
+            ws.group_start[j] = j * mg;
+            ws.group_count[j] = min(T - j * mg, mg);
         }
     }
     if (threadIdx.x == 0) *ws.num_groups = U + shared_groups;
@@ -391,7 +398,7 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
                   uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
                   const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
                   uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps,
-                  const float* __restrict__ router_bias, MoeWs ws) {
+                  const float* __restrict__ router_bias, uint32_t max_group, MoeWs ws) {
     extern __shared__ __align__(128) unsigned char rt_smem[];
     __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
     __shared__ __align__(8) uint64_t nbar;  // the norm weights
@@ -673,10 +680,10 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
 
     // group plan; shared memory reuses the staging area
     uint32_t* plan_smem = reinterpret_cast<uint32_t*>(rt_smem);
-    if (T * K <= kRtWarpPlanRoutes) {
+    if (T * K <= kRtWarpPlanRoutes && max_group == 0) {
         if (warp == 0) plan_warp(T, K, E, e_lo, e_hi, has_shared != 0, ws, plan_smem);
     } else {
-        plan_block(T, K, E, e_lo, e_hi, has_shared != 0, ws, plan_smem);
+        plan_block(T, K, E, e_lo, e_hi, has_shared != 0, max_group, ws, plan_smem);
     }
     if (threadIdx.x == 0) {
         ws.ticket[0] = 0;  // ready for the next launch
@@ -1111,6 +1118,18 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         return a.phase_events ? cudaEventRecord(static_cast<cudaEvent_t>(a.phase_events[i]), s) : cudaSuccess;
     };
     const bool pdl = a.phase_events == nullptr;
+    // the experts' input: x itself, or the router's normalised rows
+    MoeLaunch ex = a;
+    if (a.in_norm_w) {
+        ex.x = ws.xn;
+        ex.x_dtype = PBMOE_BF16;
+    }
+    const bool mx = a.layout.mxfp4 != 0;
+    const bool mma = !mx && moe_mma_supported(a.layout);
+    const bool pipe = mma && moe_pipe_supported(ex);
+    // the pipelined kernels take at most 8 routes per group: larger batches
+    // split each expert's routes into groups of 8
+    uint32_t max_group = pipe && T > 8 ? 8u : 0u;
     if ((err = mark(0)) != cudaSuccess) return err;
     // 1. router + routing + plan
     {
@@ -1133,7 +1152,7 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         void* args[] = {(void*)&x,    (void*)&T,     (void*)&H,  (void*)&E,  (void*)&K,
                         (void*)&norm, (void*)&scale, (void*)&rw, (void*)&sg, (void*)&has_shared,
                         (void*)&e_lo, (void*)&e_hi,  (void*)&ep_epoch, (void*)&inw, (void*)&ineps, (void*)&rbias,
-                        (void*)&ws};
+                        (void*)&max_group, (void*)&ws};
         if ((err = moe_launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRtThreads), smem, s, args,
                               a.pdl && pdl)) != cudaSuccess)
             return err;
@@ -1143,15 +1162,6 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     MoeLayoutDev L = a.layout;
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
-    // the experts' input: x itself, or the router's normalised rows
-    MoeLaunch ex = a;
-    if (a.in_norm_w) {
-        ex.x = ws.xn;
-        ex.x_dtype = PBMOE_BF16;
-    }
-    const bool mx = a.layout.mxfp4 != 0;
-    const bool mma = !mx && moe_mma_supported(a.layout);
-    const bool pipe = mma && moe_pipe_supported(ex);
     // 2. gate/up/SwiGLU
     if (mx) {
         if ((err = moe_up_mxfp4_launch(ex, gmax, s, pdl)) != cudaSuccess) return err;

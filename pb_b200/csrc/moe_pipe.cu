@@ -1,5 +1,5 @@
 // moe_pipe.cu — persistent, asynchronously pipelined MoE expert kernels for
-// decode batches of at most 8 tokens (group-64 Q4 experts, hidden 2048,
+// decode batches of at most 32 tokens (group-64 Q4 experts, hidden 2048,
 // intermediate 512: the expert shape of every configuration the runtime
 // ships; other shapes use the non-pipelined kernels of moe_mma.cu).
 //
@@ -28,17 +28,22 @@
 //       half-rows + their scales/biases. The 16 rows are the M operand of the
 //       mma and the batch's tokens the N operand (q4_mma_rows16); the tokens
 //       stay resident in shared memory (staged before the programmatic-
-//       dependent-launch wait, as they do not depend on the router). 8 compute
+//       dependent-launch wait, as they do not depend on the router). Batches
+//       above 8 tokens keep all 32 token rows and gather the N operand from
+//       the item's group, which the router's plan caps at 8 routes (an
+//       expert's routes and the shared expert's tokens split into groups of
+//       8, consecutive in the plan, so their weights stream together). 8 compute
 //       warps = 8 K-slices of each step; SwiGLU (silu(g)*u,
 //       shaders.metal:1699-1708) is written as bf16 hi/lo pair slots +
 //       per-8 partial sums (MoeWs::h_perm), the down kernel's input.
 //   moe_down_pipe_kernel  item = (group, 64 down rows): warp w takes the
 //       16-row block w%4 (the mma's M operand; the group's routes are N) over
 //       K-half w/4, and the two halves are summed through shared memory.
-//       Weight stages hold only weights: the routed activations of
-//       the (at most two) groups of the CTA's run are copied once into their
-//       own buffers after the programmatic-dependent-launch wait, while the
-//       first weight stages are requested before it.
+//       Weight stages hold only weights: the routed activations of each
+//       group of the CTA's run are copied once into one of two buffers (the
+//       first two after the programmatic-dependent-launch wait, while the
+//       first weight stages are requested before it; a later group's once the
+//       compute warps have left the group that held its buffer).
 
 #include "kernels.h"
 #include "pipe.cuh"
@@ -54,15 +59,20 @@ constexpr int kUpThreads = (kWarps + 2) * 32;     // + producer + epilogue
 constexpr int kDownThreads = (kWarps + 1) * 32;   // + producer
 constexpr int kRedBufs = 2;
 
-// Stage counts: bf16 activations run two CTAs per SM (3 stages each);
-// f32 activations keep a 16-row token tile and run one CTA per SM.
+// Stage counts: bf16 activations of at most 8 tokens run two CTAs per SM
+// (3 stages each); f32 activations keep a 16-row token tile and run one CTA
+// per SM; batches of 9..32 bf16 tokens (kGather) keep all 32 token rows
+// resident and run one CTA per SM.
 constexpr int kUpStagesBf16 = 3;
 constexpr int kUpStagesF32 = 5;
+constexpr int kUpStagesGather = 3;
 constexpr int kDownStages = 3;
-template <typename XT>
+constexpr uint32_t kPipeMaxTokens = 32;  // tokens of one launch (8 without kGather)
+template <typename XT, bool kGather>
 struct UpCfg {
-    static constexpr int kStages = sizeof(XT) == 4 ? kUpStagesF32 : kUpStagesBf16;
-    static constexpr int kCtasPerSm = sizeof(XT) == 4 ? 1 : 2;
+    static constexpr int kStages = kGather ? kUpStagesGather : sizeof(XT) == 4 ? kUpStagesF32 : kUpStagesBf16;
+    static constexpr int kCtasPerSm = kGather || sizeof(XT) == 4 ? 1 : 2;
+    static constexpr uint32_t kTileRows = kGather ? kPipeMaxTokens : sizeof(XT) == 4 ? 16 : 8;
 };
 
 // Named barrier ids (0 is __syncthreads).
@@ -72,6 +82,7 @@ __device__ __forceinline__ int bar_red(int p) { return 7 + p; }    // 7, 8 (up)
 __device__ __forceinline__ int bar_free(int p) { return 9 + p; }   // 9, 10 (up)
 __device__ __forceinline__ int bar_pair(int rb) { return 5 + rb; }       // 5..8 (down)
 __device__ __forceinline__ int bar_pair_free(int rb) { return 9 + rb; }  // 9..12 (down)
+__device__ __forceinline__ int bar_act_free(int hb) { return 13 + hb; }  // 13, 14 (down)
 
 static int device_sm_count() {
     static int cached[64] = {0};
@@ -145,12 +156,16 @@ __host__ __device__ constexpr UpStage up_stage(uint32_t H) {
             (32 * (H / 4 + 32) + 4 * 16 * (H / 64 + 16) + 127) / 128 * 128};
 }
 
-__host__ __device__ inline size_t up_pipe_smem(uint32_t H, bool lo, uint32_t cap_g, uint32_t cap_r) {
+__host__ __device__ inline size_t up_pipe_smem(uint32_t H, int stages, uint32_t tile_rows, uint32_t cap_g,
+                                              uint32_t cap_r) {
     const UpStage L = up_stage(H);
-    const int stages = lo ? kUpStagesF32 : kUpStagesBf16;
     // stages, token tile, partial-sum buffers, flags, mbarriers, plan
-    return size_t(stages) * L.bytes + act_tile_bytes(H, lo ? 16 : 8) + size_t(kRedBufs) * kWarps * 256 * 4 + 16 +
+    return size_t(stages) * L.bytes + act_tile_bytes(H, tile_rows) + size_t(kRedBufs) * kWarps * 256 * 4 + 16 +
            stages * 8 + plan_smem_bytes(cap_g, cap_r);
+}
+template <typename XT, bool kGather>
+inline size_t up_pipe_smem_for(uint32_t H, uint32_t cap_g, uint32_t cap_r) {
+    return up_pipe_smem(H, UpCfg<XT, kGather>::kStages, UpCfg<XT, kGather>::kTileRows, cap_g, cap_r);
 }
 
 struct DownStage {
@@ -185,13 +200,19 @@ __host__ __device__ inline size_t down_pipe_smem(uint32_t I, uint32_t cap_g, uin
 }
 
 // ---------------------------------------------------------------- up
-template <typename XT, uint32_t H, uint32_t I>
-__global__ void __launch_bounds__(kUpThreads, UpCfg<XT>::kCtasPerSm)
+// kGather (batches of 9..32 bf16 tokens): the tile holds every token of the
+// batch and an item's N operand is its group's (at most 8) tokens, gathered
+// by row index from the tile; without it the N operand is the tile's 8 rows,
+// i.e. every token of the batch, and the epilogue picks the group's columns.
+template <typename XT, uint32_t H, uint32_t I, bool kGather>
+__global__ void __launch_bounds__(kUpThreads, (UpCfg<XT, kGather>::kCtasPerSm))
 moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8_t* __restrict__ experts,
                    const uint8_t* __restrict__ shared_slot, MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g,
                    uint32_t cap_r, int x_from_router) {
+    using Cfg = UpCfg<XT, kGather>;
     constexpr bool kLo = sizeof(XT) == 4;
-    constexpr int S = UpCfg<XT>::kStages;
+    static_assert(!(kGather && kLo), "gathered token rows are bf16");
+    constexpr int S = Cfg::kStages;
     constexpr UpStage SL = up_stage(H);
     constexpr uint32_t kTiles = I / 16;          // 16-row tiles per expert
     constexpr uint32_t kTiles8 = I / 8;          // 8-row tiles of the h_perm layout
@@ -200,9 +221,9 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     static_assert(kGpw == 2, "two groups per warp per step");
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char* stages = smem_raw;
-    const ActTile tile = act_tile_at(stages + S * SL.bytes, H, kLo ? 16 : 8);
-    // partial sums: [kRedBufs][8 warps][gate | up][16 rows][8 tokens]
-    float* red = reinterpret_cast<float*>(stages + S * SL.bytes + act_tile_bytes(H, kLo ? 16 : 8));
+    const ActTile tile = act_tile_at(stages + S * SL.bytes, H, Cfg::kTileRows);
+    // partial sums: [kRedBufs][8 warps][gate | up][16 rows][8 columns]
+    float* red = reinterpret_cast<float*>(stages + S * SL.bytes + act_tile_bytes(H, Cfg::kTileRows));
     uint32_t* flags = reinterpret_cast<uint32_t*>(red + kRedBufs * kWarps * 256);  // [0] failure
     uint64_t* bar = reinterpret_cast<uint64_t*>(flags + 4);
     const PlanSmem pl = plan_at(bar + S, cap_g, cap_r);
@@ -220,10 +241,19 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     // are read only after the wait.
     auto stage_tokens = [&]() {
         if (warp < kWarps) {
-            if constexpr (kLo)
+            if constexpr (kLo) {
                 stage_act_mma<XT>(x, H, nullptr, static_cast<int>(T), H, tile, kBarStage, kComputeThreads);
-            else
+            } else if constexpr (kGather) {
+                for (uint32_t t0 = 0; t0 < T; t0 += 8) {  // 8-row blocks of the tile
+                    ActTile sub = tile;
+                    sub.act += static_cast<size_t>(t0) * tile.stride;
+                    sub.gsum += static_cast<size_t>(t0) * tile.groups;
+                    stage_act_rows8_tok<XT>(x + static_cast<size_t>(t0) * H, H, static_cast<int>(min(8u, T - t0)), H,
+                                            sub, kBarStage, kComputeThreads);
+                }
+            } else {
                 stage_act_rows8_tok<XT>(x, H, static_cast<int>(T), H, tile, kBarStage, kComputeThreads);
+            }
         }
     };
     if (!x_from_router) stage_tokens();
@@ -300,7 +330,7 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
                 const uint32_t start = pl.start[gi], n = pl.count[gi];
                 const bool active = q < n;
                 const uint32_t tok = active ? pl.token[start + q] : 0u;
-                const float* rb = red + p * kWarps * 256 + c * 8 + tok;
+                const float* rb = red + p * kWarps * 256 + c * 8 + (kGather ? q : tok);
                 float gs[4] = {0.f, 0.f, 0.f, 0.f}, us[4] = {0.f, 0.f, 0.f, 0.f};  // rows c, c+4, c+8, c+12
 #pragma unroll
                 for (int w = 0; w < kWarps; ++w) {
@@ -345,6 +375,11 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
 
     // compute warps: warp w takes groups 2w, 2w+1 of each half
     const int g = lane >> 2, t = lane & 3;
+    // tile rows of the lane's B-operand column g and of its output columns
+    // 2t, 2t+1 (their activation sums): the columns themselves, or with
+    // kGather the tokens of the item's group (columns past the group repeat
+    // its last token; the epilogue drops them)
+    uint32_t brow = static_cast<uint32_t>(g), xr0 = 2u * t, xr1 = 2u * t + 1u;
     float ag[4], au[4];
     for (uint32_t u = 0; u < steps; ++u) {
         const int s = static_cast<int>(u % S);
@@ -352,6 +387,13 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
         if (half == 0) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) ag[i] = au[i] = 0.f;
+            if constexpr (kGather) {
+                const uint32_t gi = (k0 + j) / kTiles;
+                const uint32_t p0 = pl.start[gi], n = pl.count[gi], last = n ? n - 1 : 0u;
+                brow = min(pl.token[p0 + min(static_cast<uint32_t>(g), last)], Cfg::kTileRows - 1);
+                xr0 = min(pl.token[p0 + min(2u * t, last)], Cfg::kTileRows - 1);
+                xr1 = min(pl.token[p0 + min(2u * t + 1u, last)], Cfg::kTileRows - 1);
+            }
         }
         if (!pipe_failed(flags)) {
             if (mbar_wait_bounded(&bar[s], (u / S) & 1u, kPipeWaitNs)) {
@@ -371,14 +413,14 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
                 for (uint32_t gl = 0; gl < kGpw; ++gl) {
                     const uint32_t grp = half * kHalfGroups + gl0 + gl;  // group index along H
                     const uint32_t wd = grp * 8 + 2 * t;
-                    const uint4 xb[2] = {tile.act[g * tile.stride + wd], tile.act[g * tile.stride + wd + 1]};
+                    const uint4 xb[2] = {tile.act[brow * tile.stride + wd], tile.act[brow * tile.stride + wd + 1]};
                     uint4 xl[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
                     if (kLo) {
                         xl[0] = tile.act[(g + 8) * tile.stride + wd];
                         xl[1] = tile.act[(g + 8) * tile.stride + wd + 1];
                     }
-                    const float X0 = tile.gsum[(2 * t) * tile.groups + grp];
-                    const float X1 = tile.gsum[(2 * t + 1) * tile.groups + grp];
+                    const float X0 = tile.gsum[xr0 * tile.groups + grp];
+                    const float X1 = tile.gsum[xr1 * tile.groups + grp];
                     const uint32_t wo = (gl0 + gl) * 32 + 8 * t;
                     const uint2 gg = *reinterpret_cast<const uint2*>(st + SL.gate + g * SL.rs + wo);
                     const uint2 gh = *reinterpret_cast<const uint2*>(st + SL.gate + (g + 8) * SL.rs + wo);
@@ -441,7 +483,7 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
         return;
     }
     const uint32_t my_items = k1 - k0;
-    const uint32_t g_first = k0 / tiles;  // a run spans at most two groups (host-checked)
+    const uint32_t g_first = k0 / tiles, g_last = (k1 - 1) / tiles;  // the run's groups
     if (threadIdx.x == 0) {
         for (int s = 0; s < S + 2; ++s) mbar_init(&bar[s], 32);  // the producer's lanes
         flags[0] = 0;
@@ -476,7 +518,7 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
         // ... and, once per group of the run, the group's routed activations:
         // hi and lo bf16 rows of h (pair order) and the per-8 partial sums
         auto issue_act = [&](uint32_t gi, int hb) {
-            const uint32_t start = pl.start[gi], n = pl.count[gi];
+            const uint32_t start = pl.start[gi], n = min(pl.count[gi], 8u);
             unsigned char* ab = abuf + hb * AL.bytes;
             const ActTile tile = act_tile_at(ab + AL.act, I, 16);
             for (uint32_t p = 0; p < n; ++p) {
@@ -493,11 +535,20 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
         for (int j = 0; j < S && static_cast<uint32_t>(j) < my_items; ++j) issue_weights(k0 + j, j);
         pdl_wait();  // h_perm comes from the up kernel
         issue_act(g_first, 0);
-        if ((k1 - 1) / tiles != g_first) issue_act(g_first + 1, 1);
+        if (g_last != g_first) issue_act(g_first + 1, 1);
         for (uint32_t j = 0; j + S < my_items; ++j) {
             const int s = static_cast<int>(j % S);
             named_sync(bar_empty(s), kHandshake);  // every compute warp has released item j's stage
-            if (!pipe_failed(flags)) issue_weights(k0 + j + S, s);
+            const uint32_t k = k0 + j + S;
+            if (k % tiles == 0 && k / tiles >= g_first + 2) {
+                // the first item of the run's third or later group m: its
+                // activations go into the buffer of group m - 2, which the
+                // compute warps left when they entered group m - 1
+                const int hb = static_cast<int>((k / tiles - g_first) & 1u);
+                named_sync(bar_act_free(hb), kHandshake);
+                if (!pipe_failed(flags)) issue_act(k / tiles, hb);
+            }
+            if (!pipe_failed(flags)) issue_weights(k, s);
         }
         cp_async_wait_all();  // no copy of this CTA outlives it
         return;
@@ -516,9 +567,12 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
         const uint32_t k = k0 + j;
         const uint32_t gi = k / tiles, r0 = (k % tiles) * 64;
         bool ok = !pipe_failed(flags);
-        if (ok && gi != cur_group) {
-            const int hb = static_cast<int>(gi - g_first);
-            ok = hb <= 1 && mbar_wait_bounded(&bar[S + hb], 0, kPipeWaitNs);
+        if (gi != cur_group) {
+            // group m of the run lives in activation buffer m % 2, its
+            // (m / 2)-th fill
+            const uint32_t m = gi - g_first;
+            const int hb = static_cast<int>(m & 1u);
+            if (ok) ok = mbar_wait_bounded(&bar[S + hb], (m >> 1) & 1u, kPipeWaitNs);
             if (ok) {
                 unsigned char* ab = abuf + hb * AL.bytes;
                 tile = act_tile_at(ab + AL.act, I, 16);
@@ -532,8 +586,11 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
                     X0[i] = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
                     X1[i] = ((c0.x + c0.y) + (c0.z + c0.w)) + ((c1.x + c1.y) + (c1.z + c1.w));
                 }
-                cur_group = gi;
             }
+            // group m - 1's buffer is free for group m + 1 (made after the
+            // wait above, so after the producer's sync for group m)
+            if (m >= 1 && gi + 1 <= g_last) named_arrive(bar_act_free(static_cast<int>((m + 1) & 1u)), kHandshake);
+            cur_group = gi;
         }
         if (ok) ok = mbar_wait_bounded(&bar[s], (j / S) & 1u, kPipeWaitNs);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows (g, g+8) x routes (2t, 2t+1)
@@ -609,7 +666,10 @@ static cudaError_t launch_pipe(const void* fn, dim3 grid, int threads, size_t sm
 
 static void plan_caps(const MoeLaunch& a, uint32_t& cap_g, uint32_t& cap_r) {
     const uint32_t routed = a.tokens * a.top_k;
-    cap_g = (routed < a.num_experts ? routed : a.num_experts) + 1;
+    if (a.tokens <= 8)
+        cap_g = (routed < a.num_experts ? routed : a.num_experts) + 1;
+    else  // groups of at most 8 routes: at most one per route, plus the shared expert's
+        cap_g = routed + (a.tokens + 7) / 8;
     cap_r = routed + a.tokens;
 }
 
@@ -617,21 +677,26 @@ static uint32_t down_grid() { return 2u * static_cast<uint32_t>(device_sm_count(
 
 bool moe_pipe_supported(const MoeLaunch& a) {
     const MoeLayoutDev& L = a.layout;
-    if (!moe_mma_supported(L) || a.tokens > 8 || L.hidden != kPipeH || L.inter != kPipeI) return false;
+    if (!moe_mma_supported(L) || a.tokens > kPipeMaxTokens || L.hidden != kPipeH || L.inter != kPipeI) return false;
     for (int i = 0; i < 9; ++i)
         if (L.off[i] % 16) return false;
+    const bool gather = a.tokens > 8;
+    // gathered batches take bf16 token rows; the expert-parallel exchange
+    // keeps its launches at 8 tokens
+    if (gather && (a.x_dtype != PBMOE_BF16 || a.ep)) return false;
     uint32_t cg, cr;
     plan_caps(a, cg, cr);
-    // a down CTA's run of items must span at most two groups: at most `tiles` items
-    const uint32_t tiles = kPipeH / 64;
-    if ((cg * tiles + down_grid() - 1) / down_grid() > tiles) return false;
     const bool lo = a.x_dtype == PBMOE_F32;
-    // two CTAs per SM for the bf16 up kernel and the down kernel
-    return up_pipe_smem(L.hidden, lo, cg, cr) <= (lo ? 220u : 112u) * 1024 &&
-           down_pipe_smem(L.inter, cg, cr) <= 112u * 1024;
+    const size_t up = gather ? up_pipe_smem_for<uint16_t, true>(L.hidden, cg, cr)
+                      : lo   ? up_pipe_smem_for<float, false>(L.hidden, cg, cr)
+                             : up_pipe_smem_for<uint16_t, false>(L.hidden, cg, cr);
+    // one CTA per SM for the gathered and f32 up kernels, two for the 8-token
+    // bf16 one and the down kernel
+    return up <= (gather || lo ? 227u : 112u) * 1024 && down_pipe_smem(L.inter, cg, cr) <= 112u * 1024;
 }
 
-cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
+template <typename XT, bool kGather>
+static cudaError_t up_pipe_launch_t(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     MoeLayoutDev L = a.layout;
     MoeWs ws = a.ws;
     uint32_t E = a.num_experts, T = a.tokens;
@@ -640,20 +705,18 @@ cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
     int from_router = a.in_norm_w != nullptr;
-    if (a.x_dtype == PBMOE_BF16) {
-        const dim3 grid(device_sm_count() * UpCfg<uint16_t>::kCtasPerSm);
-        const uint16_t* x = static_cast<const uint16_t*>(a.x);
-        void* args[] = {(void*)&x,       (void*)&T,  (void*)&E,  (void*)&experts, (void*)&shared,
-                        (void*)&L,       (void*)&ws, (void*)&cg, (void*)&cr, (void*)&from_router};
-        return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<uint16_t, kPipeH, kPipeI>), grid,
-                           kUpThreads, up_pipe_smem(L.hidden, false, cg, cr), s, args, pdl);
-    }
-    const float* x = static_cast<const float*>(a.x);
-    const dim3 grid(device_sm_count() * UpCfg<float>::kCtasPerSm);
-    void* args[] = {(void*)&x, (void*)&T, (void*)&E, (void*)&experts, (void*)&shared,
-                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr, (void*)&from_router};
-    return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<float, kPipeH, kPipeI>), grid, kUpThreads,
-                       up_pipe_smem(L.hidden, true, cg, cr), s, args, pdl);
+    const XT* x = static_cast<const XT*>(a.x);
+    const dim3 grid(device_sm_count() * UpCfg<XT, kGather>::kCtasPerSm);
+    void* args[] = {(void*)&x, (void*)&T,  (void*)&E,  (void*)&experts, (void*)&shared,
+                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr,      (void*)&from_router};
+    return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<XT, kPipeH, kPipeI, kGather>), grid,
+                       kUpThreads, up_pipe_smem_for<XT, kGather>(L.hidden, cg, cr), s, args, pdl);
+}
+
+cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
+    if (a.x_dtype == PBMOE_BF16)
+        return a.tokens > 8 ? up_pipe_launch_t<uint16_t, true>(a, s, pdl) : up_pipe_launch_t<uint16_t, false>(a, s, pdl);
+    return up_pipe_launch_t<float, false>(a, s, pdl);
 }
 
 cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {

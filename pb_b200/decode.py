@@ -310,9 +310,10 @@ class DecodeStep:
     def launches_per_step(self):
         """CUDA kernels one step launches: the input norm; per layer 2 fused
         projection launches, 3 MLA kernels (the first also doing RoPE and the
-        cache append), the o_proj launch and 4 MoE kernels per 8-token chunk;
-        the head's 3 (plus a memset)."""
-        chunks = (self.B + 7) // 8
+        cache append), the o_proj launch and 4 MoE kernels per MoE launch
+        (one for up to 32 tokens, then one per 32-token chunk); the head's 3
+        (plus a memset)."""
+        chunks = 1 if self.B <= 8 else (self.B + 31) // 32
         return 1 + self.cfg.layers * (2 + 3 + 1 + 4 * chunks) + 3
 
     def unique_experts(self):

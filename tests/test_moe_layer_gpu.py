@@ -185,11 +185,58 @@ def config1_layer():
     return synth.MoeLayerWeights("cuda", seed=2024)
 
 
-@pytest.mark.parametrize("tokens", [1, 8, 32])
+@pytest.mark.parametrize("tokens", [1, 8, 20, 32, 40])
 def test_config1_layer(ctx, oracle, config1_layer, tokens):
     """Config 1: hidden 2048, 512 experts top-10, I=512, group 64, shared expert;
-    every token's route ids bit-exact, every output within 1e-2."""
+    every token's route ids bit-exact, every output within 1e-2. 20 and 32
+    tokens run as one launch of the gathered expert pipe (groups of at most 8
+    routes), 40 as a 32-token launch and an 8-token one."""
     _check_layer(ctx, oracle, config1_layer, tokens, top_k=10, seed=77 + tokens)
+
+
+def _check_layer_x(ctx, oracle, w, x, top_k):
+    r = _run_layer(ctx, w, x, x.shape[0], top_k)
+    assert r["status"] == 0
+    x_np = x.float().cpu().numpy()
+    ref_out, ref_ids, ref_w, ref_logits = _oracle_layer(oracle, w, x_np, top_k)
+    check_routing(oracle, r, ref_logits, ref_ids, ref_w, top_k, w.hidden, x_np, what=f"T={x.shape[0]}")
+    assert_close(r["out"].float().cpu().numpy(), ref_out, what="layer output")
+    return r
+
+
+def test_config1_repeated_tokens_split_groups(ctx, oracle, config1_layer):
+    """32 tokens, 27 of them the same row: those route to the same 10
+    experts, whose 27+ routes each (and the shared expert's 32) the plan
+    splits into groups of at most 8 for the gathered expert pipe."""
+    from pb_b200 import synth
+
+    g = synth.gen("cuda", 4242)
+    x = synth.normal_bf16((32, config1_layer.hidden), 1.0, g, "cuda")
+    x[6:] = x[5]
+    ids = _check_layer_x(ctx, oracle, config1_layer, x, 10)["ids"].cpu().numpy()
+    assert (ids[6:] == ids[5]).all()
+
+
+def test_config1_all_distinct_experts(ctx, oracle, config1_layer):
+    """32 tokens whose top-10 experts are all different (a router of unit
+    rows: logit e of a token is its column e, set high on 10 columns per
+    token): 320 single-route groups + 4 shared-expert groups, so some CTAs of
+    the down kernel walk three groups and reuse an activation buffer."""
+    import copy
+
+    import torch
+
+    from pb_b200 import synth
+
+    w = copy.copy(config1_layer)
+    w.router = torch.zeros_like(config1_layer.router)
+    w.router[torch.arange(w.num_experts), torch.arange(w.num_experts)] = 1.0
+    g = synth.gen("cuda", 777)
+    x = synth.normal_bf16((32, w.hidden), 1.0, g, "cuda")
+    for t in range(32):
+        x[t, 10 * t:10 * t + 10] = 8.0 + 0.25 * torch.arange(10, device="cuda")
+    ids = _check_layer_x(ctx, oracle, w, x, 10)["ids"].cpu().numpy()
+    assert len(set(ids.ravel().tolist())) == 320
 
 
 @pytest.mark.parametrize("tokens", [1, 8, 32])

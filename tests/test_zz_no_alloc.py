@@ -10,8 +10,8 @@ fixed device array inside the library. These tests call it through the C ABI:
   the same inputs, so its outputs must be bit-identical to the regular entry
   point's, on two calls in a row (the second call reuses the array the first
   one left behind);
-* 9 to 29 tokens run as one launch (pbmoe_moe_layer splits such batches into
-  8-token chunks), a different kernel path, checked against the CPU oracle;
+* 9 to 29 tokens run as one launch of the gathered expert pipe (as
+  pbmoe_moe_layer runs them), checked against the CPU oracle;
 * at config-1 shapes 29 tokens fit the fixed array and 30 are refused with a
   message instead of running.
 
