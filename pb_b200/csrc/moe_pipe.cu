@@ -10,9 +10,9 @@
 //                      `stages` ahead and does nothing else: a thread's
 //                      cp.async may stall at issue until the SM's request
 //                      queue has room, and only this warp ever waits there
-//   epilogue warp (1)  up kernel only: sums the compute warps' K-slice
-//                      partials and writes SwiGLU output, off the compute
-//                      warps' critical path
+//   epilogue warps (2) up kernel only: sum the compute warps' K-slice
+//                      partials and write SwiGLU output (one 8-row tile of
+//                      the item each), off the compute warps' critical path
 // Handshakes: a stage is full when its mbarrier has the producer's 32 lane
 // arrivals (cp.async completion, no pending-count increment); compute warps
 // release it with bar.arrive EMPTY(s), on which the producer bar.syncs before
@@ -54,8 +54,10 @@ namespace pbmoe {
 constexpr uint32_t kPipeH = 2048, kPipeI = 512;
 constexpr int kWarps = 8;  // compute warps
 constexpr int kComputeThreads = kWarps * 32;
-constexpr int kHandshake = kComputeThreads + 32;  // compute warps + producer (or + epilogue)
-constexpr int kUpThreads = (kWarps + 2) * 32;     // + producer + epilogue
+constexpr int kHandshake = kComputeThreads + 32;  // compute warps + producer
+constexpr int kEpiWarps = 2;                      // up kernel: one epilogue warp per 8-row tile of an item
+constexpr int kRedHandshake = kComputeThreads + 32 * kEpiWarps;  // compute warps + epilogue warps
+constexpr int kUpThreads = (kWarps + 1 + kEpiWarps) * 32;       // + producer + epilogue
 constexpr int kDownThreads = (kWarps + 1) * 32;   // + producer
 constexpr int kRedBufs = 2;
 
@@ -68,6 +70,7 @@ constexpr int kUpStagesF32 = 5;
 constexpr int kUpStagesGather = 3;
 constexpr int kDownStages = 3;
 constexpr uint32_t kPipeMaxTokens = 32;  // tokens of one launch (8 without kGather)
+
 template <typename XT, bool kGather>
 struct UpCfg {
     static constexpr int kStages = kGather ? kUpStagesGather : sizeof(XT) == 4 ? kUpStagesF32 : kUpStagesBf16;
@@ -314,140 +317,165 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     }
     if (x_from_router) stage_tokens();
 
-    if (warp == kWarps + 1) {
-        // epilogue: lane (q = lane/4, c = lane%4) finishes route q of the
-        // group (q < n <= 8) for rows c, c+4 (first 8-row tile of the item)
-        // and 8+c, 12+c (second): it sums the 8 K-slice partials of each row
-        // for gate and up, applies SwiGLU and writes pair word c of both
-        // 8-row tiles as bf16 hi and lo; the quad sums each tile's per-8 partial.
+    if (warp > kWarps) {
+        // epilogue warp ew = 0, 1 takes the item's 8-row tile ew: lane
+        // (q = lane/4, c = lane%4) finishes route q of the group (q < n <= 8)
+        // for rows 8ew+c and 8ew+c+4: it sums the 8 K-slice partials of each
+        // row for gate and up (slice order 0..7), applies SwiGLU and writes
+        // pair word c of the tile as bf16 hi and lo; the quad sums the tile's
+        // per-8 partial.
+        const uint32_t ew = static_cast<uint32_t>(warp - kWarps - 1);
         const uint32_t q = static_cast<uint32_t>(lane >> 2), c = static_cast<uint32_t>(lane & 3);
         for (uint32_t j = 0; j < my_items; ++j) {
             const int p = static_cast<int>(j % kRedBufs);
-            named_sync(bar_red(p), kHandshake);  // red[p] holds item j's partials
+            named_sync(bar_red(p), kRedHandshake);  // red[p] holds item j's partials
             if (!pipe_failed(flags)) {
                 const uint32_t k = k0 + j;
                 const uint32_t gi = k / kTiles, ti = k % kTiles;
                 const uint32_t start = pl.start[gi], n = pl.count[gi];
                 const bool active = q < n;
                 const uint32_t tok = active ? pl.token[start + q] : 0u;
-                const float* rb = red + p * kWarps * 256 + c * 8 + (kGather ? q : tok);
-                float gs[4] = {0.f, 0.f, 0.f, 0.f}, us[4] = {0.f, 0.f, 0.f, 0.f};  // rows c, c+4, c+8, c+12
+                const float* rb = red + p * kWarps * 256 + (8 * ew + c) * 8 + (kGather ? q : tok);
+                float gs[2] = {0.f, 0.f}, us[2] = {0.f, 0.f};  // rows 8ew+c, 8ew+c+4
 #pragma unroll
                 for (int w = 0; w < kWarps; ++w) {
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
+                    for (int r = 0; r < 2; ++r) {
                         gs[r] += rb[w * 256 + r * 32];
                         us[r] += rb[w * 256 + 128 + r * 32];
                     }
                 }
-                float h[4];
+                float h[2];
 #pragma unroll
-                for (int r = 0; r < 4; ++r) h[r] = gs[r] / (1.0f + expf(-gs[r])) * us[r];
-                float part0 = h[0] + h[1], part1 = h[2] + h[3];
-                part0 += __shfl_xor_sync(kFull, part0, 1);
-                part0 += __shfl_xor_sync(kFull, part0, 2);
-                part1 += __shfl_xor_sync(kFull, part1, 1);
-                part1 += __shfl_xor_sync(kFull, part1, 2);
+                for (int r = 0; r < 2; ++r) h[r] = gs[r] / (1.0f + expf(-gs[r])) * us[r];
+                float part = h[0] + h[1];
+                part += __shfl_xor_sync(kFull, part, 1);
+                part += __shfl_xor_sync(kFull, part, 2);
                 if (active) {
                     uint8_t* hr = ws.h_perm + static_cast<size_t>(pl.route[start + q]) * hps;
                     uint32_t* hw = reinterpret_cast<uint32_t*>(hr);
                     uint32_t* lw = reinterpret_cast<uint32_t*>(hr + kTiles8 * 16);
-#pragma unroll
-                    for (int bt = 0; bt < 2; ++bt) {
-                        const float a = h[2 * bt], bv = h[2 * bt + 1];
-                        const uint32_t hi = f2_to_bf16x2(a, bv);
-                        const uint32_t lo = f2_to_bf16x2(a - __uint_as_float(hi << 16), bv - __uint_as_float(hi & 0xffff0000u));
-                        hw[(2 * ti + bt) * 4 + c] = hi;
-                        lw[(2 * ti + bt) * 4 + c] = lo;
-                    }
-                    if (c == 0) {
-                        float* pp = reinterpret_cast<float*>(hr + 2 * kTiles8 * 16);
-                        pp[2 * ti] = part0;
-                        pp[2 * ti + 1] = part1;
-                    }
+                    const uint32_t hi = f2_to_bf16x2(h[0], h[1]);
+                    const uint32_t lo = f2_to_bf16x2(h[0] - __uint_as_float(hi << 16), h[1] - __uint_as_float(hi & 0xffff0000u));
+                    hw[(2 * ti + ew) * 4 + c] = hi;
+                    lw[(2 * ti + ew) * 4 + c] = lo;
+                    if (c == 0) reinterpret_cast<float*>(hr + 2 * kTiles8 * 16)[2 * ti + ew] = part;
                 }
             }
             __syncwarp();
-            if (j + kRedBufs < my_items) named_arrive(bar_free(p), kHandshake);  // red[p] may be rewritten
+            if (j + kRedBufs < my_items) named_arrive(bar_free(p), kRedHandshake);  // red[p] may be rewritten
         }
         return;
     }
 
     // compute warps: warp w takes groups 2w, 2w+1 of each half
     const int g = lane >> 2, t = lane & 3;
+    const uint32_t gl0 = warp * kGpw;  // first group of this warp within a half
     // tile rows of the lane's B-operand column g and of its output columns
     // 2t, 2t+1 (their activation sums): the columns themselves, or with
     // kGather the tokens of the item's group (columns past the group repeat
     // its last token; the epilogue drops them)
     uint32_t brow = static_cast<uint32_t>(g), xr0 = 2u * t, xr1 = 2u * t + 1u;
+    // bf16 activations: the B fragments and activation sums of the warp's
+    // groups (both halves) stay in registers while the item's tokens are
+    // unchanged (the whole run without kGather, the item's group with it):
+    // the shared-memory traffic of a step is then the weight stage alone.
+    constexpr bool kCacheX = !kLo;
+    uint4 xc[2][kGpw][2];
+    float xs[2][kGpw][2];
+    uint32_t cur_gi = 0xffffffffu;
     float ag[4], au[4];
-    for (uint32_t u = 0; u < steps; ++u) {
-        const int s = static_cast<int>(u % S);
-        const uint32_t half = u & 1u, j = u >> 1;
-        if (half == 0) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) ag[i] = au[i] = 0.f;
-            if constexpr (kGather) {
-                const uint32_t gi = (k0 + j) / kTiles;
-                const uint32_t p0 = pl.start[gi], n = pl.count[gi], last = n ? n - 1 : 0u;
-                brow = min(pl.token[p0 + min(static_cast<uint32_t>(g), last)], Cfg::kTileRows - 1);
-                xr0 = min(pl.token[p0 + min(2u * t, last)], Cfg::kTileRows - 1);
-                xr1 = min(pl.token[p0 + min(2u * t + 1u, last)], Cfg::kTileRows - 1);
-            }
-        }
-        if (!pipe_failed(flags)) {
-            if (mbar_wait_bounded(&bar[s], (u / S) & 1u, kPipeWaitNs)) {
-                const unsigned char* st = stages + s * SL.bytes;
-                const uint32_t gl0 = warp * kGpw;  // first group of this warp within the half
-                // scale / bias pairs of rows g and g+8 for groups gl0, gl0+1
-                const unsigned char* sc = st + SL.sc + gl0 * 2;
-                const uint32_t sgw = *reinterpret_cast<const uint32_t*>(sc + 0 * 16 * SL.srs + g * SL.srs);
-                const uint32_t shw = *reinterpret_cast<const uint32_t*>(sc + 0 * 16 * SL.srs + (g + 8) * SL.srs);
-                const uint32_t bgw = *reinterpret_cast<const uint32_t*>(sc + 1 * 16 * SL.srs + g * SL.srs);
-                const uint32_t bhw = *reinterpret_cast<const uint32_t*>(sc + 1 * 16 * SL.srs + (g + 8) * SL.srs);
-                const uint32_t sgu = *reinterpret_cast<const uint32_t*>(sc + 2 * 16 * SL.srs + g * SL.srs);
-                const uint32_t shu = *reinterpret_cast<const uint32_t*>(sc + 2 * 16 * SL.srs + (g + 8) * SL.srs);
-                const uint32_t bgu = *reinterpret_cast<const uint32_t*>(sc + 3 * 16 * SL.srs + g * SL.srs);
-                const uint32_t bhu = *reinterpret_cast<const uint32_t*>(sc + 3 * 16 * SL.srs + (g + 8) * SL.srs);
-#pragma unroll
-                for (uint32_t gl = 0; gl < kGpw; ++gl) {
-                    const uint32_t grp = half * kHalfGroups + gl0 + gl;  // group index along H
-                    const uint32_t wd = grp * 8 + 2 * t;
-                    const uint4 xb[2] = {tile.act[brow * tile.stride + wd], tile.act[brow * tile.stride + wd + 1]};
-                    uint4 xl[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-                    if (kLo) {
-                        xl[0] = tile.act[(g + 8) * tile.stride + wd];
-                        xl[1] = tile.act[(g + 8) * tile.stride + wd + 1];
-                    }
-                    const float X0 = tile.gsum[xr0 * tile.groups + grp];
-                    const float X1 = tile.gsum[xr1 * tile.groups + grp];
-                    const uint32_t wo = (gl0 + gl) * 32 + 8 * t;
-                    const uint2 gg = *reinterpret_cast<const uint2*>(st + SL.gate + g * SL.rs + wo);
-                    const uint2 gh = *reinterpret_cast<const uint2*>(st + SL.gate + (g + 8) * SL.rs + wo);
-                    const uint2 ug = *reinterpret_cast<const uint2*>(st + SL.up + g * SL.rs + wo);
-                    const uint2 uh = *reinterpret_cast<const uint2*>(st + SL.up + (g + 8) * SL.rs + wo);
-                    auto bf = [&](uint32_t wv) {
-                        return gl ? __uint_as_float(wv & 0xffff0000u) : __uint_as_float(wv << 16);
-                    };
-                    q4_mma_rows16<kLo>(gg, gh, xb, xl, bf(sgw), bf(shw), bf(bgw), bf(bhw), X0, X1, ag);
-                    q4_mma_rows16<kLo>(ug, uh, xb, xl, bf(sgu), bf(shu), bf(bgu), bf(bhu), X0, X1, au);
+    for (uint32_t j = 0; j < my_items; ++j) {
+        if constexpr (kCacheX) {
+            const uint32_t gi = kGather ? (k0 + j) / kTiles : 0u;
+            if (gi != cur_gi) {
+                cur_gi = gi;
+                if constexpr (kGather) {
+                    const uint32_t p0 = pl.start[gi], n = pl.count[gi], last = n ? n - 1 : 0u;
+                    brow = min(pl.token[p0 + min(static_cast<uint32_t>(g), last)], Cfg::kTileRows - 1);
+                    xr0 = min(pl.token[p0 + min(2u * t, last)], Cfg::kTileRows - 1);
+                    xr1 = min(pl.token[p0 + min(2u * t + 1u, last)], Cfg::kTileRows - 1);
                 }
-            } else if (lane == 0) {
-                atomicOr(&flags[0], 1u);
-                latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+#pragma unroll
+                for (uint32_t hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                    for (uint32_t gl = 0; gl < kGpw; ++gl) {
+                        const uint32_t grp = hf * kHalfGroups + gl0 + gl;
+                        const uint32_t wd = grp * 8 + 2 * t;
+                        xc[hf][gl][0] = tile.act[brow * tile.stride + wd];
+                        xc[hf][gl][1] = tile.act[brow * tile.stride + wd + 1];
+                        xs[hf][gl][0] = tile.gsum[xr0 * tile.groups + grp];
+                        xs[hf][gl][1] = tile.gsum[xr1 * tile.groups + grp];
+                    }
+                }
             }
         }
-        if (u + S < steps) named_arrive(bar_empty(s), kHandshake);  // stage s released
-        if (half == 1) {
-            const int p = static_cast<int>(j % kRedBufs);
-            if (j >= kRedBufs) named_sync(bar_free(p), kHandshake);  // the epilogue is done with red[p]
-            float* rw = red + (p * kWarps + warp) * 256;
-            *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(ag[0], ag[1]);
-            *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(ag[2], ag[3]);
-            *reinterpret_cast<float2*>(rw + 128 + g * 8 + 2 * t) = make_float2(au[0], au[1]);
-            *reinterpret_cast<float2*>(rw + 128 + (g + 8) * 8 + 2 * t) = make_float2(au[2], au[3]);
-            named_arrive(bar_red(p), kHandshake);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ag[i] = au[i] = 0.f;
+#pragma unroll
+        for (uint32_t half = 0; half < 2; ++half) {
+            const uint32_t u = 2 * j + half;
+            const int s = static_cast<int>(u % S);
+            if (!pipe_failed(flags)) {
+                if (mbar_wait_bounded(&bar[s], (u / S) & 1u, kPipeWaitNs)) {
+                    const unsigned char* st = stages + s * SL.bytes;
+                    // scale / bias pairs of rows g and g+8 for groups gl0, gl0+1
+                    const unsigned char* sc = st + SL.sc + gl0 * 2;
+                    const uint32_t sgw = *reinterpret_cast<const uint32_t*>(sc + 0 * 16 * SL.srs + g * SL.srs);
+                    const uint32_t shw = *reinterpret_cast<const uint32_t*>(sc + 0 * 16 * SL.srs + (g + 8) * SL.srs);
+                    const uint32_t bgw = *reinterpret_cast<const uint32_t*>(sc + 1 * 16 * SL.srs + g * SL.srs);
+                    const uint32_t bhw = *reinterpret_cast<const uint32_t*>(sc + 1 * 16 * SL.srs + (g + 8) * SL.srs);
+                    const uint32_t sgu = *reinterpret_cast<const uint32_t*>(sc + 2 * 16 * SL.srs + g * SL.srs);
+                    const uint32_t shu = *reinterpret_cast<const uint32_t*>(sc + 2 * 16 * SL.srs + (g + 8) * SL.srs);
+                    const uint32_t bgu = *reinterpret_cast<const uint32_t*>(sc + 3 * 16 * SL.srs + g * SL.srs);
+                    const uint32_t bhu = *reinterpret_cast<const uint32_t*>(sc + 3 * 16 * SL.srs + (g + 8) * SL.srs);
+#pragma unroll
+                    for (uint32_t gl = 0; gl < kGpw; ++gl) {
+                        const uint32_t grp = half * kHalfGroups + gl0 + gl;  // group index along H
+                        const uint32_t wd = grp * 8 + 2 * t;
+                        uint4 xb[2], xl[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                        float X0, X1;
+                        if constexpr (kCacheX) {
+                            xb[0] = xc[half][gl][0];
+                            xb[1] = xc[half][gl][1];
+                            X0 = xs[half][gl][0];
+                            X1 = xs[half][gl][1];
+                        } else {
+                            xb[0] = tile.act[brow * tile.stride + wd];
+                            xb[1] = tile.act[brow * tile.stride + wd + 1];
+                            if (kLo) {
+                                xl[0] = tile.act[(g + 8) * tile.stride + wd];
+                                xl[1] = tile.act[(g + 8) * tile.stride + wd + 1];
+                            }
+                            X0 = tile.gsum[xr0 * tile.groups + grp];
+                            X1 = tile.gsum[xr1 * tile.groups + grp];
+                        }
+                        const uint32_t wo = (gl0 + gl) * 32 + 8 * t;
+                        const uint2 gg = *reinterpret_cast<const uint2*>(st + SL.gate + g * SL.rs + wo);
+                        const uint2 gh = *reinterpret_cast<const uint2*>(st + SL.gate + (g + 8) * SL.rs + wo);
+                        const uint2 ug = *reinterpret_cast<const uint2*>(st + SL.up + g * SL.rs + wo);
+                        const uint2 uh = *reinterpret_cast<const uint2*>(st + SL.up + (g + 8) * SL.rs + wo);
+                        auto bf = [&](uint32_t wv) {
+                            return gl ? __uint_as_float(wv & 0xffff0000u) : __uint_as_float(wv << 16);
+                        };
+                        q4_mma_rows16<kLo>(gg, gh, xb, xl, bf(sgw), bf(shw), bf(bgw), bf(bhw), X0, X1, ag);
+                        q4_mma_rows16<kLo>(ug, uh, xb, xl, bf(sgu), bf(shu), bf(bgu), bf(bhu), X0, X1, au);
+                    }
+                } else if (lane == 0) {
+                    atomicOr(&flags[0], 1u);
+                    latch_status(ws.status, PBMOE_DEV_ERR_PIPE_TIMEOUT);
+                }
+            }
+            if (u + S < steps) named_arrive(bar_empty(s), kHandshake);  // stage s released
         }
+        const int p = static_cast<int>(j % kRedBufs);
+        if (j >= kRedBufs) named_sync(bar_free(p), kRedHandshake);  // the epilogue is done with red[p]
+        float* rw = red + (p * kWarps + warp) * 256;
+        *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(ag[0], ag[1]);
+        *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(ag[2], ag[3]);
+        *reinterpret_cast<float2*>(rw + 128 + g * 8 + 2 * t) = make_float2(au[0], au[1]);
+        *reinterpret_cast<float2*>(rw + 128 + (g + 8) * 8 + 2 * t) = make_float2(au[2], au[3]);
+        named_arrive(bar_red(p), kRedHandshake);
     }
 }
 
