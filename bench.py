@@ -565,31 +565,46 @@ def _emit(line):
     print(json.dumps(line), flush=True)
 
 
-def run_matvec(args):
-    """Config 0: y = W x for W Q4 [4096 x 2048] (group 64), x bf16 [1 x 2048],
-    y bf16; 64 distinct weight matrices cycled (303 MB > L2)."""
+QMV_R, QMV_C, QMV_G, QMV_N = 4096, 2048, 64, 64  # config 0, 64 distinct matrices cycled (303 MB > L2)
+QMV_BYTES = QMV_R * QMV_C // 2 + 2 * QMV_R * (QMV_C // QMV_G) * 2 + QMV_C * 2 + QMV_R * 2  # 4,730,880 per launch
+
+
+def qmatvec_rates(ctx, steps, warmup, seed=1):
+    """Config 0 on the device: y = W x for 64 distinct Q4 [4096 x 2048]
+    matrices cycled in one CUDA graph (ms per launch), and the same matrices
+    as one resident projection batch on the input (pbmoe_q4_matvec_batch,
+    resident_mmap_matvec_batch: 4 launches of 16)."""
     import torch
 
-    from pb_b200 import capi, synth
+    from pb_b200 import synth
 
-    R, Cc, G, NC = 4096, 2048, 64, 64
-    byts = R * Cc // 2 + 2 * R * (Cc // G) * 2 + Cc * 2 + R * 2  # 4,730,880
-    ctx = capi.Context(0)
-    g = synth.gen("cuda", 1)
+    R, Cc, G, NC = QMV_R, QMV_C, QMV_G, QMV_N
+    g = synth.gen("cuda", seed)
     mats = [synth.q4_matrix(R, Cc, G, g, "cuda") for _ in range(NC)]
     x = synth.normal_bf16((1, Cc), 1.0, g, "cuda")
     y = torch.empty(1, R, device="cuda", dtype=torch.bfloat16)
     s = torch.cuda.Stream()
     calls = [(lambda m=m: ctx.q4_matvec(m[0], m[1], m[2], R, Cc, G, x, y, stream=s)) for m in mats]
-    ms, steps, clocks = _graph_time(calls, s, args.steps, args.warmup)
-    gbs = byts / (ms / 1e3) / 1e9
-    # the same 64 matrices as one resident projection batch on the input
-    # (pbmoe_q4_matvec_batch, resident_mmap_matvec_batch): 4 launches of 16
+    ms, n, clocks = _graph_time(calls, s, steps, warmup)
     ys = [torch.empty(1, R, device="cuda", dtype=torch.bfloat16) for _ in range(NC)]
     spec = [(m[0], m[1], m[2], R, Cc, G) for m in mats]
-    bms, _, _ = _graph_time([lambda: ctx.q4_matvec_batch(spec, x, ys, stream=s)], s, max(8, args.steps // NC),
-                            args.warmup)
-    bgbs = NC * byts / (bms / 1e3) / 1e9
+    bms, _, _ = _graph_time([lambda: ctx.q4_matvec_batch(spec, x, ys, stream=s)], s, max(8, steps // NC), warmup)
+    return dict(ms=ms, steps=n, clocks=clocks, gbs=QMV_BYTES / (ms / 1e3) / 1e9, batch_ms=bms,
+                batch_gbs=NC * QMV_BYTES / (bms / 1e3) / 1e9, mats=mats, x=x, y=y, stream=s)
+
+
+def run_matvec(args):
+    """Config 0: y = W x for W Q4 [4096 x 2048] (group 64), x bf16 [1 x 2048],
+    y bf16; 64 distinct weight matrices cycled (303 MB > L2)."""
+    import torch
+
+    from pb_b200 import capi
+
+    R, Cc, G, NC, byts = QMV_R, QMV_C, QMV_G, QMV_N, QMV_BYTES
+    ctx = capi.Context(0)
+    q = qmatvec_rates(ctx, args.steps, args.warmup)
+    ms, steps, clocks, gbs, bms, bgbs = q["ms"], q["steps"], q["clocks"], q["gbs"], q["batch_ms"], q["batch_gbs"]
+    mats, x, y, s = q["mats"], q["x"], q["y"], q["stream"]
     hx = x.cpu().pin_memory()
     hy = torch.empty(1, R, dtype=torch.bfloat16).pin_memory()
     dx = torch.empty_like(x)
@@ -1305,6 +1320,19 @@ def run_step(args):
             "clocks": clock_summary,
             "cpu_baseline": cpu,
         }
+        if world == 1:
+            # the other half of the headline metric: config 0's qmatvec GB/s
+            # (the same figures as --workload matvec, after the step's timing)
+            q = qmatvec_rates(ctx, 640, 3)
+            line["qmatvec"] = {
+                "value": q["gbs"], "unit": "GB/s", "frac": q["gbs"] / peak, "ms_per_launch": q["ms"],
+                "launches": q["steps"], "config": "config 0: Q4 [4096x2048] group 64 x bf16 [1x2048] -> bf16, "
+                "64 distinct matrices cycled in one CUDA graph (303 MB > L2)",
+                "projection_batch": {"value": q["batch_gbs"], "unit": "GB/s", "frac": q["batch_gbs"] / peak,
+                                     "ms_per_batch": q["batch_ms"],
+                                     "note": "the 64 matrices on one input through pbmoe_q4_matvec_batch"},
+                "clocks": q["clocks"]}
+            del q
         print(json.dumps(line), flush=True)
     del graph
     ctx.close()

@@ -522,9 +522,14 @@ static cudaError_t q4_matvec_launch_t(const Q4MatvecArgs& a, cudaStream_t s) {
         visit(a.packed, a.scales, a.biases);
         if (a.packed2) visit(a.packed2, a.scales2, a.biases2);
     }
-    // one or two tokens: the CUDA-core kernel (more weight bytes in flight per
-    // warp, one wave of CTAs); larger batches: the tensor-core kernel
-    if (a.batch > 2 && a.group == kMmaGroup && a.cols % 256 == 0 && all_aligned &&
+    // plain calls of one or two tokens: the CUDA-core kernel (more weight
+    // bytes in flight per warp, one wave of CTAs; a matrix set streams
+    // through the persistent kernel); larger batches and the fused forms
+    // (input norm, residual, a second matrix): the tensor-core kernel, whose
+    // shorter instruction stream after the dependency wait wins on the
+    // latency-bound decode projections
+    const bool fused_single = a.norm_w || a.residual || a.packed2;
+    if ((a.batch > 2 || fused_single) && a.group == kMmaGroup && a.cols % 256 == 0 && all_aligned &&
         reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
         cudaError_t e = launch_mma<XT, YT>(a, s);
         if (e != cudaErrorNotSupported) return e;
