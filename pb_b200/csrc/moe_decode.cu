@@ -29,6 +29,7 @@
 #include "kernels.h"
 #include "pipe.cuh"
 #include "q4_rows.cuh"
+#include "plan.cuh"
 #include "routing.cuh"
 
 namespace pbmoe {
@@ -78,8 +79,9 @@ namespace cg = cooperative_groups;
 // exact slot order of routing_top_k_iter, math.rs:746-765), and build the
 // layer-major plan (unique experts ascending, routes in route order inside
 // each group, the shared expert as group 0): directly when NR is 1, else the
-// last of them (counted in ticket[1]). The plan CTA resets both counters for
-// the next launch.
+// last of them (counted in ticket[1]); with the pipelined expert kernels,
+// which build the plan themselves from the route ids (plan.cuh), there is no
+// plan here. The last routing CTA resets both counters for the next launch.
 constexpr int kRtRows = 8;
 constexpr int kRtThreads = 32 * kRtRows;
 constexpr uint32_t kRtTokPass = 32;
@@ -311,94 +313,13 @@ __device__ __noinline__ void plan_warp(uint32_t T, uint32_t K, uint32_t E, uint3
     if (lane == 0) *ws.num_groups = U + shared_groups;
 }
 
-// The same plan by the whole CTA, for any number of routes: per-expert counts
-// and two block scans, ranks inside each expert from __match_any_sync. With
-// max_group = m > 0 an expert's routes (and the shared expert's T) form
-// ceil(count / m) consecutive groups of at most m routes each, in the same
-// grouped positions: the pipelined expert kernels take at most 8 routes per
-// group as their MMA's N operand.
-__device__ __noinline__ void plan_block(uint32_t T, uint32_t K, uint32_t E, uint32_t e_lo, uint32_t e_hi,
-                                        bool has_shared, uint32_t max_group, const MoeWs& ws, uint32_t* smem) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t* cnt = smem;             // [E] counts -> starts
-    uint32_t* gidx = cnt + E;         // [E] used flags -> group index
-    uint32_t* run = gidx + E;         // [E] routes of each expert placed so far
-    uint32_t* ids = run + E;          // [T*K]
-    uint32_t* rnk = ids + T * K;      // [T*K] rank of each route inside its group
-    uint32_t* tmp = rnk + T * K;      // [32]
-    const uint32_t R = T * K;
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = run[e] = 0;
-    __syncthreads();
-    // only the experts of this rank's range [e_lo, e_hi) form groups (all of
-    // them on a single GPU); group_expert holds the slot index e - e_lo
-    for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
-        const uint32_t e = __ldcg(ws.route_ids + r);
-        ids[r] = e;
-        if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e], 1u);
-    }
-    __syncthreads();
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x)
-        gidx[e] = max_group ? (cnt[e] + max_group - 1) / max_group : (cnt[e] ? 1u : 0u);
-    __syncthreads();
-    const uint32_t U = block_exclusive_scan(gidx, E, tmp);
-    const uint32_t RL = block_exclusive_scan(cnt, E, tmp);  // cnt[e] = start of expert e; RL local routes
-    // rank of each route among the earlier routes of its expert: warp 0 walks
-    // the routes 32 at a time; lanes with the same expert find each other with
-    // __match_any_sync and a per-expert running count carries across chunks
-    if (warp == 0) {
-        for (uint32_t r0 = 0; r0 < R; r0 += 32) {
-            const uint32_t r = r0 + lane;
-            const uint32_t e = r < R ? ids[r] : 0xffffffffu;
-            const uint32_t peers = __match_any_sync(kFull, e);
-            const uint32_t below = peers & ((1u << lane) - 1u);
-            if (r < R && e < E) {
-                rnk[r] = run[e] + __popc(below);
-                if ((peers >> lane) == 1u) run[e] += __popc(peers);  // the group's highest lane
-            }
-            __syncwarp();
-        }
-    }
-    __syncthreads();
-    const uint32_t mg = max_group ? max_group : 0xffffffffu;
-    const uint32_t shared_groups = !has_shared ? 0u : max_group ? (T + max_group - 1) / max_group : 1u;
-    const uint32_t routed_base = has_shared ? T : 0u;  // grouped positions taken by the shared groups
-    for (uint32_t r = threadIdx.x; r < R; r += blockDim.x) {
-        const uint32_t e = ids[r];
-        if (e < e_lo || e >= e_hi) continue;
-        const uint32_t rank = rnk[r];
-        const uint32_t pos = routed_base + cnt[e] + rank;
-        ws.group_routes[pos] = r;
-        ws.group_tokens[pos] = r / K;
-        if (rank % mg == 0) {
-            // exclusive-scan property: the expert's size is the next start minus this one
-            const uint32_t total = (e + 1 < E ? cnt[e + 1] : RL) - cnt[e];
-            const uint32_t g = shared_groups + gidx[e] + rank / mg;
-            ws.group_expert[g] = e - e_lo;
-            ws.group_start[g] = pos;
-            ws.group_count[g] = min(total - rank, mg);
-        }
-    }
-    if (has_shared) {
-        for (uint32_t t = threadIdx.x; t < T; t += blockDim.x) {
-            ws.group_routes[t] = R + t;
-            ws.group_tokens[t] = t;
-        }
-        for (uint32_t j = threadIdx.x; j < shared_groups; j += blockDim.x) {
-            ws.group_expert[j] = E;
-            ws.group_start[j] = j * mg;
-            ws.group_count[j] = min(T - j * mg, mg);
-        }
-    }
-    if (threadIdx.x == 0) *ws.num_groups = U + shared_groups;
-}
-
 template <typename XT>
 __global__ void __launch_bounds__(kRtThreads)
 moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, uint32_t K,
                   uint32_t normalization, float routed_scale, const uint16_t* __restrict__ router_w,
                   const uint16_t* __restrict__ shared_gate_w, int has_shared, uint32_t e_lo, uint32_t e_hi,
                   uint32_t* ep_epoch, const float* __restrict__ in_norm_w, float in_eps,
-                  const float* __restrict__ router_bias, uint32_t max_group, MoeWs ws) {
+                  const float* __restrict__ router_bias, uint32_t max_group, uint32_t build_plan, MoeWs ws) {
     extern __shared__ __align__(128) unsigned char rt_smem[];
     __shared__ __align__(8) uint64_t bars[kRtMaxChunks];
     __shared__ __align__(8) uint64_t nbar;  // the norm weights
@@ -678,12 +599,17 @@ moe_router_kernel(const XT* __restrict__ x, uint32_t T, uint32_t H, uint32_t E, 
         }
     }
 
-    // group plan; shared memory reuses the staging area
+    // group plan (unless the pipelined expert kernels build their own from
+    // the route ids); shared memory reuses the staging area
     uint32_t* plan_smem = reinterpret_cast<uint32_t*>(rt_smem);
-    if (T * K <= kRtWarpPlanRoutes && max_group == 0) {
+    if (!build_plan) {
+    } else if (T * K <= kRtWarpPlanRoutes && max_group == 0) {
         if (warp == 0) plan_warp(T, K, E, e_lo, e_hi, has_shared != 0, ws, plan_smem);
     } else {
-        plan_block(T, K, E, e_lo, e_hi, has_shared != 0, max_group, ws, plan_smem);
+        plan_block(T, K, E, e_lo, e_hi, has_shared != 0, max_group, ws.route_ids,
+                   PlanOut{ws.group_expert, ws.group_start, ws.group_count, ws.group_tokens, ws.group_routes,
+                           ws.num_groups},
+                   plan_smem);
     }
     if (threadIdx.x == 0) {
         ws.ticket[0] = 0;  // ready for the next launch
@@ -1128,8 +1054,11 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
     const bool mma = !mx && moe_mma_supported(a.layout);
     const bool pipe = mma && moe_pipe_supported(ex);
     // the pipelined kernels take at most 8 routes per group: larger batches
-    // split each expert's routes into groups of 8
+    // split each expert's routes into groups of 8; they build the plan
+    // themselves from the route ids, the other expert kernels read the
+    // router's
     uint32_t max_group = pipe && T > 8 ? 8u : 0u;
+    uint32_t build_plan = pipe ? 0u : 1u;
     if ((err = mark(0)) != cudaSuccess) return err;
     // 1. router + routing + plan
     {
@@ -1152,7 +1081,7 @@ static cudaError_t moe_layer_launch_t(const MoeLaunch& a, cudaStream_t s) {
         void* args[] = {(void*)&x,    (void*)&T,     (void*)&H,  (void*)&E,  (void*)&K,
                         (void*)&norm, (void*)&scale, (void*)&rw, (void*)&sg, (void*)&has_shared,
                         (void*)&e_lo, (void*)&e_hi,  (void*)&ep_epoch, (void*)&inw, (void*)&ineps, (void*)&rbias,
-                        (void*)&max_group, (void*)&ws};
+                        (void*)&max_group, (void*)&build_plan, (void*)&ws};
         if ((err = moe_launch_pdl(reinterpret_cast<const void*>(fn), grid, dim3(kRtThreads), smem, s, args,
                               a.pdl && pdl)) != cudaSuccess)
             return err;

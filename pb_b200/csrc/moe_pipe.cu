@@ -47,6 +47,7 @@
 
 #include "kernels.h"
 #include "pipe.cuh"
+#include "plan.cuh"
 #include "q4_mma.cuh"
 
 namespace pbmoe {
@@ -120,17 +121,30 @@ __device__ inline PlanSmem plan_at(void* base, uint32_t cap_g, uint32_t cap_r) {
     return {p, p + cap_g, p + 2 * cap_g, p + 3 * cap_g, p + 3 * cap_g + cap_r};
 }
 
-// All threads: copy the plan (ng groups, positions 0..npos) through L2.
-__device__ inline void load_plan(const MoeWs& ws, uint32_t ng, uint32_t npos, const PlanSmem& pl) {
-    for (uint32_t i = threadIdx.x; i < ng; i += blockDim.x) {
-        pl.expert[i] = __ldcg(ws.group_expert + i);
-        pl.start[i] = __ldcg(ws.group_start + i);
-        pl.count[i] = __ldcg(ws.group_count + i);
-    }
-    for (uint32_t i = threadIdx.x; i < npos; i += blockDim.x) {
-        pl.token[i] = __ldcg(ws.group_tokens + i);
-        pl.route[i] = __ldcg(ws.group_routes + i);
-    }
+// What a pipelined expert kernel needs to build the group plan itself from
+// the router's route ids (plan_rank, into its PlanSmem).
+struct PlanArgs {
+    uint32_t T, K, e_lo, e_hi, has_shared, max_group;
+};
+
+// All threads: the layer-major plan from ws.route_ids into pl, with `scratch`
+// (plan_scratch_bytes) as working space; returns the group count. Up to
+// kPlanRankRoutes routes the O(R)-per-thread ranking is the faster build,
+// above it the block scans (at 320 routes the ranking made the batch-32
+// decode step 0.9 ms slower).
+constexpr uint32_t kPlanRankRoutes = 128;
+__host__ __device__ inline size_t plan_scratch_bytes(uint32_t T, uint32_t K, uint32_t E) {
+    return 4 * (T * K <= kPlanRankRoutes ? plan_rank_scratch_words(T, K) : plan_block_scratch_words(T, K, E));
+}
+__device__ inline uint32_t build_plan(const PlanArgs& pa, uint32_t E, const MoeWs& ws, const PlanSmem& pl,
+                                      uint32_t cap_g, uint32_t* scratch, uint32_t* ng_smem) {
+    const PlanOut out{pl.expert, pl.start, pl.count, pl.token, pl.route, ng_smem};
+    if (pa.T * pa.K <= kPlanRankRoutes)
+        plan_rank(pa.T, pa.K, E, pa.e_lo, pa.e_hi, pa.has_shared != 0, pa.max_group, ws.route_ids, out, scratch);
+    else
+        plan_block(pa.T, pa.K, E, pa.e_lo, pa.e_hi, pa.has_shared != 0, pa.max_group, ws.route_ids, out, scratch);
+    __syncthreads();
+    return min(*ng_smem, cap_g);
 }
 
 // Contiguous run [k0, k1) of the `total` items for this CTA (sizes differ by
@@ -211,7 +225,7 @@ template <typename XT, uint32_t H, uint32_t I, bool kGather>
 __global__ void __launch_bounds__(kUpThreads, (UpCfg<XT, kGather>::kCtasPerSm))
 moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8_t* __restrict__ experts,
                    const uint8_t* __restrict__ shared_slot, MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g,
-                   uint32_t cap_r, int x_from_router) {
+                   uint32_t cap_r, int x_from_router, PlanArgs pa) {
     using Cfg = UpCfg<XT, kGather>;
     constexpr bool kLo = sizeof(XT) == 4;
     static_assert(!(kGather && kLo), "gathered token rows are bf16");
@@ -261,16 +275,16 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
     };
     if (!x_from_router) stage_tokens();
     pdl_wait();
-    // the plan first: the producer's first weight copies are then in flight
-    // while the compute warps stage tokens written by the router
-    const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
+    // the plan first, built from the route ids with the stage area as
+    // scratch: the producer's first weight copies are then in flight while
+    // the compute warps stage tokens written by the router
+    __shared__ uint32_t s_ng;
+    const uint32_t ng = build_plan(pa, E, ws, pl, cap_g, reinterpret_cast<uint32_t*>(stages), &s_ng);
     uint32_t k0, k1;
     item_run(ng * kTiles, k0, k1);
     if (k0 >= k1) return;
     const uint32_t my_items = k1 - k0;
     const uint32_t steps = 2 * my_items;
-    load_plan(ws, ng, cap_r, pl);
-    __syncthreads();
     // Every CTA of this grid is resident, so the down kernel may be scheduled
     // now: its CTAs take SMs as these exit and prefetch weights while the
     // rest of this grid finishes (it waits for all of it before reading h_perm).
@@ -483,7 +497,7 @@ moe_up_pipe_kernel(const XT* __restrict__ x, uint32_t T, uint32_t E, const uint8
 template <uint32_t H, uint32_t I>
 __global__ void __launch_bounds__(kDownThreads, 2)
 moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint8_t* __restrict__ shared_slot,
-                     MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g, uint32_t cap_r) {
+                     MoeLayoutDev Ld, MoeWs ws, uint32_t cap_g, uint32_t cap_r, PlanArgs pa) {
     constexpr int S = kDownStages;
     constexpr DownStage SL = down_stage(I);
     constexpr uint32_t tiles = H / 64;
@@ -500,10 +514,12 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const size_t hps = hperm_stride(I);
 
-    // The group plan was written by the router kernel, which completed before
-    // the up kernel passed its own wait; it is safe to read before this
-    // kernel's wait (through L2).
-    const uint32_t ng = min(__ldcg(ws.num_groups), cap_g);
+    // The route ids were written by the router kernel, which completed before
+    // the up kernel passed its own wait (and this kernel launched only after
+    // that): the plan is built from them before this kernel's wait, with the
+    // stage area as scratch.
+    __shared__ uint32_t s_ng;
+    const uint32_t ng = build_plan(pa, E, ws, pl, cap_g, reinterpret_cast<uint32_t*>(stages), &s_ng);
     uint32_t k0, k1;
     item_run(ng * tiles, k0, k1);
     if (k0 >= k1) {
@@ -517,7 +533,6 @@ moe_down_pipe_kernel(uint32_t E, const uint8_t* __restrict__ experts, const uint
         flags[0] = 0;
         fence_mbar_init();
     }
-    load_plan(ws, ng, cap_r, pl);
     __syncthreads();
 
     if (warp == kWarps) {
@@ -703,6 +718,17 @@ static void plan_caps(const MoeLaunch& a, uint32_t& cap_g, uint32_t& cap_r) {
 
 static uint32_t down_grid() { return 2u * static_cast<uint32_t>(device_sm_count()); }
 
+static PlanArgs plan_args(const MoeLaunch& a) {
+    PlanArgs p;
+    p.T = a.tokens;
+    p.K = a.top_k;
+    p.e_lo = a.expert_count ? a.expert_lo : 0u;
+    p.e_hi = a.expert_count ? a.expert_lo + a.expert_count : a.num_experts;
+    p.has_shared = a.shared_slot != nullptr;
+    p.max_group = a.tokens > 8 ? 8u : 0u;
+    return p;
+}
+
 bool moe_pipe_supported(const MoeLaunch& a) {
     const MoeLayoutDev& L = a.layout;
     if (!moe_mma_supported(L) || a.tokens > kPipeMaxTokens || L.hidden != kPipeH || L.inter != kPipeI) return false;
@@ -718,6 +744,11 @@ bool moe_pipe_supported(const MoeLaunch& a) {
     const size_t up = gather ? up_pipe_smem_for<uint16_t, true>(L.hidden, cg, cr)
                       : lo   ? up_pipe_smem_for<float, false>(L.hidden, cg, cr)
                              : up_pipe_smem_for<uint16_t, false>(L.hidden, cg, cr);
+    // the plan's scratch lives in the stage area of both kernels
+    const size_t scratch = plan_scratch_bytes(a.tokens, a.top_k, a.num_experts);
+    const int up_stages = gather ? kUpStagesGather : lo ? kUpStagesF32 : kUpStagesBf16;
+    if (scratch > size_t(up_stages) * up_stage(L.hidden).bytes || scratch > size_t(kDownStages) * down_stage(L.inter).bytes)
+        return false;
     // one CTA per SM for the gathered and f32 up kernels, two for the 8-token
     // bf16 one and the down kernel
     return up <= (gather || lo ? 227u : 112u) * 1024 && down_pipe_smem(L.inter, cg, cr) <= 112u * 1024;
@@ -733,10 +764,11 @@ static cudaError_t up_pipe_launch_t(const MoeLaunch& a, cudaStream_t s, bool pdl
     const uint8_t* experts = a.experts;
     const uint8_t* shared = a.shared_slot;
     int from_router = a.in_norm_w != nullptr;
+    PlanArgs pa = plan_args(a);
     const XT* x = static_cast<const XT*>(a.x);
     const dim3 grid(device_sm_count() * UpCfg<XT, kGather>::kCtasPerSm);
     void* args[] = {(void*)&x, (void*)&T,  (void*)&E,  (void*)&experts, (void*)&shared,
-                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr,      (void*)&from_router};
+                    (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr,      (void*)&from_router, (void*)&pa};
     return launch_pipe(reinterpret_cast<const void*>(moe_up_pipe_kernel<XT, kPipeH, kPipeI, kGather>), grid,
                        kUpThreads, up_pipe_smem_for<XT, kGather>(L.hidden, cg, cr), s, args, pdl);
 }
@@ -755,7 +787,8 @@ cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl) {
     const uint8_t* shared = a.shared_slot;
     uint32_t cg, cr;
     plan_caps(a, cg, cr);
-    void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr};
+    PlanArgs pa = plan_args(a);
+    void* args[] = {(void*)&E, (void*)&experts, (void*)&shared, (void*)&L, (void*)&ws, (void*)&cg, (void*)&cr, (void*)&pa};
     return launch_pipe(reinterpret_cast<const void*>(moe_down_pipe_kernel<kPipeH, kPipeI>), dim3(down_grid()),
                        kDownThreads, down_pipe_smem(L.inter, cg, cr), s, args, pdl);
 }
