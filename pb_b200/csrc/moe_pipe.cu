@@ -100,10 +100,11 @@ static int device_sm_count() {
     return cached[dev];
 }
 
-// The layer-major group plan (written by the router kernel) copied into
-// shared memory once per CTA, so that per-item lookups are shared-memory
-// loads instead of dependent L2 round trips. `cap_g` groups and `cap_r`
-// grouped positions fit (host-checked: T*K + 1 and T*K + T).
+// The layer-major group plan in shared memory, built by every CTA from the
+// router's route ids (build_plan below), so that per-item lookups are
+// shared-memory loads instead of dependent L2 round trips. `cap_g` groups and
+// `cap_r` grouped positions fit (plan_caps: min(T*K, E) + 1 groups, or T*K +
+// ceil(T/8) when groups are split at 8 routes; T*K + T positions).
 struct PlanSmem {
     uint32_t* expert;  // [cap_g]
     uint32_t* start;   // [cap_g]
