@@ -834,11 +834,13 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     __shared__ float piece_ss;
     __shared__ uint32_t missing;
     const uint32_t t = blockIdx.x;
-    pdl_wait();
-    // every CTA of this grid is resident: the next layer's first kernel may be
-    // scheduled now and prefetch its weights while the combine runs (it reads
-    // this kernel's outputs only after its own griddepcontrol.wait)
-    pdl_launch_dependents();
+    const uint32_t cb = blockIdx.y * piece, ce = min(H, cb + piece);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Before the dependency wait: the routes, their weights and the shared
+    // gate's logit (router outputs), the residual and the norm weights. This
+    // grid is launched only after the up kernel passed its own wait, i.e.
+    // after the router (and whatever wrote the residual before it)
+    // completed; only the expert outputs y come from the grids still running.
     if (threadIdx.x < K) {
         const uint32_t e = __ldcg(ws.route_ids + static_cast<size_t>(t) * K + threadIdx.x);
         wsh[threadIdx.x] = (e >= e_lo && e < e_hi) ? __ldcg(ws.route_w + static_cast<size_t>(t) * K + threadIdx.x)
@@ -847,11 +849,21 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     if (threadIdx.x == 0) missing = 0;
     float sw = 0.f;
     if (has_shared) sw = has_gate ? 1.0f / (1.0f + expf(-__ldcg(ws.shared_logit + t))) : 1.0f;
+    float4 res[kCombineVec], nwv[kCombineVec];
+#pragma unroll
+    for (int j = 0; j < kCombineVec; ++j) {
+        const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
+        res[j] = (c < ce && residual) ? load_act4<OT>(residual, static_cast<size_t>(t) * H + c) : zero;
+        nwv[j] = (c < ce && norm_w) ? *reinterpret_cast<const float4*>(norm_w + c) : zero;
+    }
+    pdl_wait();
+    // every CTA of this grid is resident: the next layer's first kernel may be
+    // scheduled now and prefetch its weights while the combine runs (it reads
+    // this kernel's outputs only after its own griddepcontrol.wait)
+    pdl_launch_dependents();
     __syncthreads();
     const float* yt = ws.y + static_cast<size_t>(t) * K * H;
     const float* ysh = ws.y + (static_cast<size_t>(T) * K + t) * H;
-    const uint32_t cb = blockIdx.y * piece, ce = min(H, cb + piece);
-    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 v[kCombineVec];
 #pragma unroll
     for (int j = 0; j < kCombineVec; ++j) {
@@ -928,7 +940,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     for (int j = 0; j < kCombineVec; ++j) {
         const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
         if (c < ce) {
-            float4 o = residual ? load_act4<OT>(residual, static_cast<size_t>(t) * H + c) : zero;
+            float4 o = res[j];
             add4(o, v[j]);
             store_act4<OT>(out, static_cast<size_t>(t) * H + c, o);
             ss += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
@@ -955,7 +967,7 @@ moe_combine_kernel(uint32_t T, uint32_t H, uint32_t K, int has_shared, int has_g
     for (int j = 0; j < kCombineVec; ++j) {
         const uint32_t c = cb + 4 * (threadIdx.x + j * blockDim.x);
         if (c < ce) {
-            const float4 nw = *reinterpret_cast<const float4*>(norm_w + c);
+            const float4 nw = nwv[j];
             store_act4<OT>(next_normed, static_cast<size_t>(t) * H + c,
                            make_float4(v[j].x * scale * nw.x, v[j].y * scale * nw.y, v[j].z * scale * nw.z,
                                        v[j].w * scale * nw.w));
