@@ -670,7 +670,9 @@ PBMOE_API int pbmoe_mla_rope_append(pbmoe_ctx* ctx, const pbmoe_mla_config* conf
  * pbmoe_mla_rope_append; c_kv_rows / k_rope_rows are its DEVICE arrays of
  * cache row pointers, args->c_kv / args->k_rope the HOST arrays of the same
  * caches), then the attention reads every sequence's args->seq_lens rows,
- * the appended one included. */
+ * the appended one included. A sequence's attended rows other than its own
+ * appended row must not be rows another sequence of the call appends (the
+ * attention may read them while the append runs). */
 PBMOE_API int pbmoe_mla_append_decode(pbmoe_ctx* ctx, const pbmoe_mla_config* config, const pbmoe_mla_args* args,
                                       const float* kv, const float* latent_norm_weight, float epsilon,
                                       const uint32_t* positions, uint16_t* const* c_kv_rows,

@@ -280,13 +280,17 @@ __global__ void __launch_bounds__(256) mla_absorb_kernel(const QT* __restrict__ 
 // order; warp w then owns tokens 8w .. 8w+7 for the online softmax and
 // context columns 128w .. 128w+127 for O += P C. Fragment loads run one step
 // ahead of the MMAs that use them.
+// fresh_pos (nullable): per sequence, the cache row the absorb launch of the
+// same call appends while this kernel may already run; every other attended
+// row was written before the call (the absorb launch passed its own
+// dependency wait before this grid launched), so a first tile without that
+// row is requested before this kernel's wait.
 __global__ void __launch_bounds__(kMlaThreads, kMlaCtasPerSm) mla_attn_kernel(const float* __restrict__ qp,
                                                                                MlaSeqs seqs, uint32_t split_tokens,
                                                                                uint32_t splits,
-                                                                               float* __restrict__ partial) {
+                                                                               float* __restrict__ partial,
+                                                                               const uint32_t* __restrict__ fresh_pos) {
     extern __shared__ __align__(128) unsigned char smem[];
-    pdl_wait();
-    pdl_launch_dependents();
     unsigned char* stage0 = smem;
     unsigned char* pbuf = stage0 + 2 * kStageBytes;
     float* wmax = reinterpret_cast<float*>(pbuf + kMlaHeads * kPRow);  // [warps][16]
@@ -299,6 +303,8 @@ __global__ void __launch_bounds__(kMlaThreads, kMlaCtasPerSm) mla_attn_kernel(co
     float* out = partial + (static_cast<size_t>(b) * splits + sp) * kMlaHeads * kMlaPartialFloats;
     const float NEG_INF = -__int_as_float(0x7f800000);
     if (t0 >= t1) {  // empty split: contributes nothing
+        pdl_wait();
+        pdl_launch_dependents();
         for (uint32_t i = threadIdx.x; i < kMlaHeads * kMlaPartialFloats; i += blockDim.x)
             out[i] = (i % kMlaPartialFloats == 0) ? NEG_INF : 0.f;
         return;
@@ -338,8 +344,19 @@ __global__ void __launch_bounds__(kMlaThreads, kMlaCtasPerSm) mla_attn_kernel(co
             }
         }
     };
-    issue_tile(0, 0);
-    cp_commit();
+    // the first tile before the wait unless it holds the row being appended
+    const uint32_t fresh = fresh_pos ? __ldg(fresh_pos + b) : 0xffffffffu;
+    const bool early = fresh < t0 || fresh >= min(t1, t0 + kMlaTile);
+    if (early) {
+        issue_tile(0, 0);
+        cp_commit();
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+    if (!early) {
+        issue_tile(0, 0);
+        cp_commit();
+    }
 
     // This warp's Q' (dims 144w .. 144w+143) as mma A fragments, bf16 hi and lo
     // (residue): for k-step kk the fragment holds Q'[g][16kk + 2t, +1],
@@ -732,8 +749,9 @@ cudaError_t mla_decode_launch(const MlaLaunch& a, cudaStream_t s) {
     if ((e = cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(kMlaSmem))) != cudaSuccess)
         return e;
+    const uint32_t* fresh = a.rope ? a.rope->positions : nullptr;
     if ((e = launch_pdl_kernel(mla_attn_kernel, dim3(a.splits, a.batch), dim3(kMlaThreads), kMlaSmem, s, a.qp,
-                               a.seqs, a.split_tokens, a.splits, a.partial)) != cudaSuccess)
+                               a.seqs, a.split_tokens, a.splits, a.partial, fresh)) != cudaSuccess)
         return e;
     if (a.splits > kOutMaxSplits) return cudaErrorInvalidValue;
     const dim3 og(kMlaHeads, a.batch);
