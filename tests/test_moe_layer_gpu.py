@@ -185,12 +185,14 @@ def config1_layer():
     return synth.MoeLayerWeights("cuda", seed=2024)
 
 
-@pytest.mark.parametrize("tokens", [1, 8, 20, 32, 40])
+@pytest.mark.parametrize("tokens", [1, 8, 9, 20, 32, 33, 40])
 def test_config1_layer(ctx, oracle, config1_layer, tokens):
     """Config 1: hidden 2048, 512 experts top-10, I=512, group 64, shared expert;
-    every token's route ids bit-exact, every output within 1e-2. 20 and 32
+    every token's route ids bit-exact, every output within 1e-2. 9 to 32
     tokens run as one launch of the gathered expert pipe (groups of at most 8
-    routes), 40 as a 32-token launch and an 8-token one."""
+    routes; up to 12 tokens the expert kernels build the group plan by
+    ranking, above by block scans), 33 and 40 as a 32-token launch and a
+    1- or 8-token one."""
     _check_layer(ctx, oracle, config1_layer, tokens, top_k=10, seed=77 + tokens)
 
 
