@@ -1347,9 +1347,9 @@ def run_step(args):
 # step, e.g. the MLA split partials, count here)
 STEP_NCU_TRAFFIC: dict = {
     "mla_decode": (2.218496 + 75.826176 + 2.808832 + 11.866368) * 1e6,  # absorb, attention (+ partials written), merge
-    "moe_router": 2.26e6,
-    "moe_gate_up": (73.21 + 2.15) * 1e6,
-    "moe_down": (36.80 + 0.13) * 1e6,
+    "moe_router": 2.25792e6,
+    "moe_gate_up": (73.243648 + 3.973632) * 1e6,
+    "moe_down": (36.826368 + 0.134144) * 1e6,
     "q_a+kv_a": 2.526464e6,
     "q_b": 2.74432e6,
 }
