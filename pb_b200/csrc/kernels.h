@@ -139,7 +139,7 @@ bool moe_mma_supported(const MoeLayoutDev& L);
 cudaError_t moe_up_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
 cudaError_t moe_down_mma_launch(const MoeLaunch& a, uint32_t gmax, cudaStream_t s, bool pdl);
 // Persistent, cp.async-pipelined expert kernels (moe_pipe.cu) for decode
-// batches of at most 8 tokens on moe_mma_supported layouts.
+// batches of at most 32 tokens (bf16 inputs above 8) on moe_mma_supported layouts.
 bool moe_pipe_supported(const MoeLaunch& a);
 cudaError_t moe_up_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
 cudaError_t moe_down_pipe_launch(const MoeLaunch& a, cudaStream_t s, bool pdl);
