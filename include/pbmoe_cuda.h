@@ -515,7 +515,10 @@ PBMOE_API int pbmoe_ep_moe_layer(pbmoe_ctx* ctx, const pbmoe_moe_config* config,
  * hands back the host output): x and residual are copied into device rows
  * owned by the context (sized by pbmoe_reserve), the layer runs, and out is
  * copied back, all ordered on `stream` (synchronise it before reading out;
- * pinned host memory makes the copies asynchronous). No next-layer norm. */
+ * pinned host memory makes the copies asynchronous). Page-locked residual
+ * and out buffers the device can address (cudaHostAlloc, cudaHostRegister;
+ * 16-byte aligned) are not copied: the layer's last kernel reads the
+ * residual and writes out in place. No next-layer norm. */
 PBMOE_API int pbmoe_moe_layer_host(pbmoe_ctx* ctx, const pbmoe_moe_config* config, const pbmoe_moe_weights* weights,
                                    const void* x, pbmoe_dtype x_dtype, const void* residual, void* out,
                                    pbmoe_dtype out_dtype, uint32_t tokens, void* stream);

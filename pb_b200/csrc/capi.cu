@@ -714,15 +714,35 @@ int pbmoe_moe_layer_host(pbmoe_ctx* ctx, const pbmoe_moe_config* c, const pbmoe_
     char* dres = dx + slot;
     char* dout = dres + slot;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Page-locked host rows that the device can address (cudaHostAlloc /
+    // cudaHostRegister memory) are used in place by the one kernel that
+    // touches each of them once per element: the combine kernel reads the
+    // residual (before its dependency wait) and stores the output. x is read
+    // by every router and expert CTA, so it is always copied in.
+    auto device_view = [](const void* p) -> void* {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+        return reinterpret_cast<uintptr_t>(at.devicePointer) % 16 == 0 ? at.devicePointer : nullptr;
+    };
+    const void* res_in_place = residual ? device_view(residual) : nullptr;
+    void* out_in_place = device_view(out);
     cudaError_t e = cudaMemcpyAsync(dx, x, size_t(tokens) * H * xs, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess && residual)
+    if (e == cudaSuccess && residual && !res_in_place)
         e = cudaMemcpyAsync(dres, residual, size_t(tokens) * H * os, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer (host rows) input copy");
-    const int rc = moe_layer_impl(ctx, c, w, dx, x_dtype, residual ? dres : nullptr, dout, out_dtype, tokens, nullptr,
-                                  nullptr, nullptr, stream, 0, 0, nullptr);
+    const void* res_dev = residual ? (res_in_place ? res_in_place : dres) : nullptr;
+    void* out_dev = out_in_place ? out_in_place : dout;
+    const int rc = moe_layer_impl(ctx, c, w, dx, x_dtype, res_dev, out_dev, out_dtype, tokens, nullptr, nullptr,
+                                  nullptr, stream, 0, 0, nullptr);
     if (rc != PBMOE_OK) return rc;
-    e = cudaMemcpyAsync(out, dout, size_t(tokens) * H * os, cudaMemcpyDeviceToHost, s);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer (host rows) output copy");
+    if (!out_in_place) {
+        e = cudaMemcpyAsync(out, dout, size_t(tokens) * H * os, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "moe layer (host rows) output copy");
+    }
     return PBMOE_OK;
 }
 

@@ -403,10 +403,12 @@ def test_moe_layer_rejects_bad_calls(ctx, small_layer):
     assert e.value.code == capi.PBMOE_ERR_UNSUPPORTED
 
 
-@pytest.mark.parametrize("tokens,out_f32", [(1, False), (8, True), (12, False)])
-def test_moe_layer_host_rows(ctx, config1_layer, tokens, out_f32):
-    """pbmoe_moe_layer_host (host x / residual / out, copies inside the call)
-    equals pbmoe_moe_layer on device rows, bit for bit."""
+@pytest.mark.parametrize("tokens,out_f32,pinned", [(1, False, True), (8, True, True), (12, False, True),
+                                                   (8, False, False)])
+def test_moe_layer_host_rows(ctx, config1_layer, tokens, out_f32, pinned):
+    """pbmoe_moe_layer_host (host x / residual / out) equals pbmoe_moe_layer on
+    device rows, bit for bit: with page-locked buffers the residual and the
+    output are used in place, with pageable ones everything is copied."""
     import torch
 
     from pb_b200 import capi, synth
@@ -419,8 +421,9 @@ def test_moe_layer_host_rows(ctx, config1_layer, tokens, out_f32):
     res = synth.normal_bf16((tokens, w.hidden), 1.0, synth.gen("cuda", 91), "cuda").to(dt)
     ref = torch.empty(tokens, w.hidden, device="cuda", dtype=dt)
     ctx.moe_layer(cfg, w.c_weights(), x, ref, tokens, residual=res)
-    hx, hres = x.cpu().pin_memory(), res.cpu().pin_memory()
-    hout = torch.empty(tokens, w.hidden, dtype=dt).pin_memory()
+    pin = (lambda t: t.pin_memory()) if pinned else (lambda t: t)
+    hx, hres = pin(x.cpu()), pin(res.cpu())
+    hout = pin(torch.full((tokens, w.hidden), float("nan"), dtype=dt))
     s = torch.cuda.current_stream()
     ctx.moe_layer_host(cfg, w.c_weights(), hx, hout, tokens, residual=hres, stream=s)
     s.synchronize()
