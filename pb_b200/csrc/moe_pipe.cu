@@ -17,7 +17,8 @@
 // arrivals (cp.async completion, no pending-count increment); compute warps
 // release it with bar.arrive EMPTY(s), on which the producer bar.syncs before
 // refilling it. Partial sums go through 2 rotating buffers (RED(p) arrive /
-// sync towards the epilogue warp, FREE(p) back). An arrival is made exactly
+// sync towards the epilogue warps, FREE(p) back; the down kernel's activation
+// buffers are handed back with ACT_FREE). An arrival is made exactly
 // when the matching sync will be made, and no role leaves its item loop
 // early: after a failure (a bounded wait expired, PBMOE_DEV_ERR_PIPE_TIMEOUT
 // latched) the roles keep the handshakes but skip waits, copies and math, so
