@@ -31,7 +31,7 @@
 //       stay resident in shared memory (staged before the programmatic-
 //       dependent-launch wait, as they do not depend on the router). Batches
 //       above 8 tokens keep all 32 token rows and gather the N operand from
-//       the item's group, which the router's plan caps at 8 routes (an
+//       the item's group, which the group plan caps at 8 routes (an
 //       expert's routes and the shared expert's tokens split into groups of
 //       8, consecutive in the plan, so their weights stream together). 8 compute
 //       warps = 8 K-slices of each step; SwiGLU (silu(g)*u,
